@@ -1,0 +1,404 @@
+// Python bindings of the PRA sm_100a kernels (torch tensors <-> raw launch blocks).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <vector>
+
+#include "kernels.h"
+
+namespace {
+
+inline cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check(cudaError_t e, const char* what) {
+  TORCH_CHECK(e == cudaSuccess, "pra_ops.", what, " failed: ", cudaGetErrorString(e));
+}
+
+void expect(const torch::Tensor& t, at::ScalarType dt, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.scalar_type() == dt, name, " has dtype ", t.scalar_type(), ", expected ", dt);
+}
+
+template <typename T>
+T* ptr(const torch::Tensor& t) {
+  return reinterpret_cast<T*>(t.data_ptr());
+}
+
+template <typename T>
+const T* optr(const c10::optional<torch::Tensor>& t) {
+  return (t.has_value() && t->defined() && t->numel() > 0) ? reinterpret_cast<const T*>(t->data_ptr()) : nullptr;
+}
+
+// ---------------------------------------------------------------- attention
+AttnParams attn_params(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, int64_t heads,
+                       int64_t kv_heads, const c10::optional<torch::Tensor>& mem_k,
+                       const c10::optional<torch::Tensor>& mem_v, const c10::optional<torch::Tensor>& mem_idx,
+                       const c10::optional<torch::Tensor>& mem_len, const c10::optional<torch::Tensor>& key_valid,
+                       double scale) {
+  TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && v.dim() == 3, "q/k/v must be [B, T, width] views");
+  TORCH_CHECK(q.stride(2) == 1 && k.stride(2) == 1 && v.stride(2) == 1, "q/k/v feature dim must be contiguous");
+  expect(q, at::kBFloat16, "q");
+  expect(k, at::kBFloat16, "k");
+  expect(v, at::kBFloat16, "v");
+  TORCH_CHECK(heads % kv_heads == 0, "heads must be a multiple of kv heads");
+  AttnParams p{};
+  p.B = q.size(0);
+  p.T = q.size(1);
+  p.H = heads;
+  p.Hkv = kv_heads;
+  p.q = ptr<const __nv_bfloat16>(q);
+  p.k = ptr<const __nv_bfloat16>(k);
+  p.v = ptr<const __nv_bfloat16>(v);
+  p.q_row = q.stride(1);
+  p.q_batch = q.stride(0);
+  p.k_row = k.stride(1);
+  p.k_batch = k.stride(0);
+  p.v_row = v.stride(1);
+  p.v_batch = v.stride(0);
+  p.scale = static_cast<float>(scale);
+  if (mem_idx.has_value() && mem_idx->numel() > 0) {
+    TORCH_CHECK(mem_k.has_value() && mem_v.has_value() && mem_len.has_value(), "memory needs k, v, idx and len");
+    expect(*mem_k, at::kBFloat16, "mem_k");
+    expect(*mem_v, at::kBFloat16, "mem_v");
+    expect(*mem_idx, at::kInt, "mem_idx");
+    expect(*mem_len, at::kInt, "mem_len");
+    TORCH_CHECK(mem_k->dim() == 2 && mem_k->stride(1) == 1 && mem_v->stride(1) == 1 &&
+                    mem_k->stride(0) == mem_v->stride(0),
+                "memory pools must be row-major [rows, width] with equal strides");
+    TORCH_CHECK(mem_idx->is_contiguous() && mem_idx->size(0) == p.B, "mem_idx must be [B, max]");
+    p.mem_k = ptr<const __nv_bfloat16>(*mem_k);
+    p.mem_v = ptr<const __nv_bfloat16>(*mem_v);
+    p.mem_row = mem_k->stride(0);
+    p.mem_idx = ptr<const int>(*mem_idx);
+    p.mem_len = ptr<const int>(*mem_len);
+    p.mem_max = mem_idx->size(1);
+  }
+  if (key_valid.has_value() && key_valid->numel() > 0) {
+    expect(*key_valid, at::kByte, "key_valid");
+    TORCH_CHECK(key_valid->is_contiguous() && key_valid->size(0) == p.B && key_valid->size(1) == p.T,
+                "key_valid must be [B, T]");
+    p.key_valid = ptr<const uint8_t>(*key_valid);
+  }
+  return p;
+}
+
+std::vector<torch::Tensor> attention_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, int64_t heads,
+                                         int64_t kv_heads, int64_t head_dim, c10::optional<torch::Tensor> mem_k,
+                                         c10::optional<torch::Tensor> mem_v, c10::optional<torch::Tensor> mem_idx,
+                                         c10::optional<torch::Tensor> mem_len, c10::optional<torch::Tensor> key_valid,
+                                         double scale) {
+  c10::cuda::CUDAGuard guard(q.device());
+  auto p = attn_params(q, k, v, heads, kv_heads, mem_k, mem_v, mem_idx, mem_len, key_valid, scale);
+  auto out = torch::empty({p.B, p.T, heads * head_dim}, q.options());
+  auto lse = torch::empty({p.B, heads, p.T}, q.options().dtype(at::kFloat));
+  p.o = ptr<__nv_bfloat16>(out);
+  p.o_row = out.stride(1);
+  p.o_batch = out.stride(0);
+  p.lse = ptr<float>(lse);
+  check(pra_attention_fwd(p, (int)head_dim, stream()), "attention_fwd");
+  return {out, lse};
+}
+
+std::vector<torch::Tensor> attention_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                         torch::Tensor out, torch::Tensor lse, int64_t heads, int64_t head_dim,
+                                         c10::optional<torch::Tensor> mem_k, c10::optional<torch::Tensor> mem_v,
+                                         c10::optional<torch::Tensor> mem_idx, c10::optional<torch::Tensor> mem_len,
+                                         c10::optional<torch::Tensor> key_valid, double scale) {
+  c10::cuda::CUDAGuard guard(q.device());
+  auto p = attn_params(q, k, v, heads, heads, mem_k, mem_v, mem_idx, mem_len, key_valid, scale);
+  expect(dout, at::kBFloat16, "dout");
+  TORCH_CHECK(dout.stride(2) == 1 && out.stride(2) == 1, "dout/out feature dim must be contiguous");
+  p.o = ptr<__nv_bfloat16>(out);
+  p.o_row = out.stride(1);
+  p.o_batch = out.stride(0);
+  p.lse = ptr<float>(lse);
+  p.dout = ptr<const __nv_bfloat16>(dout);
+  p.do_row = dout.stride(1);
+  p.do_batch = dout.stride(0);
+  auto delta = torch::empty({p.B, heads, p.T}, q.options().dtype(at::kFloat));
+  p.delta = ptr<float>(delta);
+  // dq, dk, dv packed as one [B, T, 3, H*D] buffer so the QKV weight gradient is a single GEMM.
+  auto dqkv = torch::empty({p.B, p.T, 3 * heads * head_dim}, q.options());
+  const int64_t w = heads * head_dim;
+  p.dq = ptr<__nv_bfloat16>(dqkv);
+  p.dk = p.dq + w;
+  p.dv = p.dq + 2 * w;
+  p.dq_row = p.dk_row = p.dv_row = dqkv.stride(1);
+  p.dq_batch = p.dk_batch = p.dv_batch = dqkv.stride(0);
+  check(pra_attention_bwd(p, (int)head_dim, stream()), "attention_bwd");
+  return {dqkv};
+}
+
+// ---------------------------------------------------------------- GEMM
+torch::Tensor& workspace(const torch::Tensor& like) {
+  static std::vector<torch::Tensor> per_device(16);
+  const int dev = like.get_device();
+  if (!per_device[dev].defined()) per_device[dev] = torch::empty({64 << 20}, like.options().dtype(at::kByte));
+  return per_device[dev];
+}
+
+void gemm(const std::string& kind, torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> C, torch::Tensor D,
+          c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> aux, double alpha, double beta,
+          c10::optional<torch::Tensor> alpha_ptr) {
+  c10::cuda::CUDAGuard guard(A.device());
+  expect(A, at::kBFloat16, "A");
+  expect(B, at::kBFloat16, "B");
+  expect(D, at::kBFloat16, "D");
+  TORCH_CHECK(A.is_contiguous() && B.is_contiguous() && D.is_contiguous(), "GEMM operands must be contiguous");
+  GemmArgs g{};
+  g.A = A.data_ptr();
+  g.B = B.data_ptr();
+  g.C = optr<void>(C);
+  g.D = D.data_ptr();
+  g.bias = optr<void>(bias);
+  g.aux = aux.has_value() ? aux->data_ptr() : nullptr;
+  g.alpha = (float)alpha;
+  g.beta = (float)beta;
+  g.alpha_ptr = optr<float>(alpha_ptr);
+  auto& ws = workspace(A);
+  g.workspace = ws.data_ptr();
+  g.workspace_bytes = ws.numel();
+  if (kind == "tn" || kind == "tn_gelu") {  // D[M,N] = A[M,K] B[N,K]^T
+    g.M = A.size(0); g.K = A.size(1); g.N = B.size(0);
+    TORCH_CHECK(B.size(1) == g.K && D.size(0) == g.M && D.size(1) == g.N, "tn shape mismatch");
+  } else if (kind == "nn" || kind == "nn_dgelu") {  // D[M,N] = A[M,K] B[K,N]
+    g.M = A.size(0); g.K = A.size(1); g.N = B.size(1);
+    TORCH_CHECK(B.size(0) == g.K && D.size(0) == g.M && D.size(1) == g.N, "nn shape mismatch");
+  } else if (kind == "wgrad") {  // D[M,N] = A[K,M]^T B[K,N]
+    g.K = A.size(0); g.M = A.size(1); g.N = B.size(1);
+    TORCH_CHECK(B.size(0) == g.K && D.size(0) == g.M && D.size(1) == g.N, "wgrad shape mismatch");
+  } else {
+    TORCH_CHECK(false, "unknown gemm kind ", kind);
+  }
+  if (C.has_value()) TORCH_CHECK(C->is_contiguous() && C->sizes() == D.sizes(), "C must match D");
+  if (g.beta != 0.f) TORCH_CHECK(g.C != nullptr, "beta != 0 needs C");
+  cudaError_t e;
+  if (kind == "tn") e = pra_gemm_tn_bias(g, stream());
+  else if (kind == "tn_gelu") e = pra_gemm_tn_bias_gelu(g, stream());
+  else if (kind == "nn") e = pra_gemm_nn(g, stream());
+  else if (kind == "nn_dgelu") e = pra_gemm_nn_dgelu(g, stream());
+  else e = pra_gemm_wgrad(g, stream());
+  check(e, kind.c_str());
+}
+
+// ---------------------------------------------------------------- norms
+std::vector<torch::Tensor> norm_fwd(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> b, double eps,
+                                    bool rms) {
+  c10::cuda::CUDAGuard guard(x.device());
+  expect(x, at::kBFloat16, "x");
+  expect(w, at::kBFloat16, "w");
+  TORCH_CHECK(x.is_contiguous(), "x must be contiguous");
+  const int D = x.size(-1);
+  const int M = x.numel() / D;
+  auto y = torch::empty_like(x);
+  auto mean = torch::empty({M}, x.options().dtype(at::kFloat));
+  auto rstd = torch::empty({M}, x.options().dtype(at::kFloat));
+  check(pra_norm_fwd(ptr<const __nv_bfloat16>(x), ptr<const __nv_bfloat16>(w), optr<__nv_bfloat16>(b),
+                     ptr<__nv_bfloat16>(y), ptr<float>(mean), ptr<float>(rstd), M, D, (float)eps, rms, stream()),
+        "norm_fwd");
+  return {y, mean, rstd};
+}
+
+std::vector<torch::Tensor> norm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor mean,
+                                    torch::Tensor rstd, c10::optional<torch::Tensor> dres, bool rms) {
+  c10::cuda::CUDAGuard guard(x.device());
+  expect(dy, at::kBFloat16, "dy");
+  TORCH_CHECK(dy.is_contiguous() && x.is_contiguous(), "norm_bwd inputs must be contiguous");
+  const int D = x.size(-1);
+  const int M = x.numel() / D;
+  auto dx = torch::empty_like(x);
+  const int parts = pra_norm_bwd_partials(M);
+  auto part = torch::empty({2, parts, D}, x.options().dtype(at::kFloat));
+  auto dw = torch::empty({D}, x.options());
+  auto db = torch::empty({D}, x.options());
+  check(pra_norm_bwd(ptr<const __nv_bfloat16>(dy), ptr<const __nv_bfloat16>(x), ptr<const __nv_bfloat16>(w),
+                     ptr<const float>(mean), ptr<const float>(rstd), optr<__nv_bfloat16>(dres), ptr<__nv_bfloat16>(dx),
+                     ptr<float>(part), ptr<float>(part) + (int64_t)parts * D, ptr<__nv_bfloat16>(dw),
+                     ptr<__nv_bfloat16>(db), M, D, rms, stream()),
+        "norm_bwd");
+  return {dx, dw, db};
+}
+
+torch::Tensor colsum(torch::Tensor g) {
+  c10::cuda::CUDAGuard guard(g.device());
+  expect(g, at::kBFloat16, "g");
+  TORCH_CHECK(g.is_contiguous(), "g must be contiguous");
+  const int N = g.size(-1);
+  const int M = g.numel() / N;
+  auto part = torch::empty({pra_colsum_partials(M), N}, g.options().dtype(at::kFloat));
+  auto out = torch::empty({N}, g.options());
+  check(pra_colsum(ptr<const __nv_bfloat16>(g), M, N, ptr<float>(part), ptr<__nv_bfloat16>(out), stream()), "colsum");
+  return out;
+}
+
+// ---------------------------------------------------------------- loss / optimizer
+std::vector<torch::Tensor> cross_entropy(torch::Tensor logits, torch::Tensor labels, int64_t vocab,
+                                         int64_t ignore_index) {
+  c10::cuda::CUDAGuard guard(logits.device());
+  expect(logits, at::kBFloat16, "logits");
+  expect(labels, at::kLong, "labels");
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "logits must be [M, ld] row-major");
+  const int64_t M = logits.size(0);
+  auto loss = torch::empty({M}, logits.options().dtype(at::kFloat));
+  auto valid = torch::empty({M}, logits.options().dtype(at::kFloat));
+  check(pra_cross_entropy(ptr<__nv_bfloat16>(logits), M, logits.stride(0), (int)vocab,
+                          ptr<const int64_t>(labels.contiguous()), (int)ignore_index, ptr<float>(loss),
+                          ptr<float>(valid), stream()),
+        "cross_entropy");
+  return {loss, valid};
+}
+
+std::vector<torch::Tensor> grad_norm(torch::Tensor grad, double max_norm) {
+  c10::cuda::CUDAGuard guard(grad.device());
+  TORCH_CHECK(grad.is_contiguous(), "grad must be contiguous");
+  auto part = torch::empty({pra_grad_norm_parts()}, grad.options().dtype(at::kFloat));
+  auto norm = torch::empty({1}, grad.options().dtype(at::kFloat));
+  auto coef = torch::empty({1}, grad.options().dtype(at::kFloat));
+  check(pra_grad_norm(grad.data_ptr(), grad.scalar_type() == at::kBFloat16, grad.numel(), (float)max_norm,
+                      ptr<float>(part), ptr<float>(norm), ptr<float>(coef), stream()),
+        "grad_norm");
+  return {norm, coef};
+}
+
+void adamw(torch::Tensor param, c10::optional<torch::Tensor> shadow, torch::Tensor grad, torch::Tensor m,
+           torch::Tensor v, double lr, double beta1, double beta2, double eps, double weight_decay, int64_t step,
+           c10::optional<torch::Tensor> coef, double grad_scale) {
+  c10::cuda::CUDAGuard guard(param.device());
+  expect(param, at::kFloat, "param");
+  TORCH_CHECK(param.is_contiguous() && grad.is_contiguous() && m.is_contiguous() && v.is_contiguous(),
+              "optimizer buffers must be contiguous");
+  TORCH_CHECK(grad.numel() == param.numel(), "grad size mismatch");
+  __nv_bfloat16* sh = nullptr;
+  if (shadow.has_value() && shadow->defined()) {
+    expect(*shadow, at::kBFloat16, "shadow");
+    TORCH_CHECK(shadow->numel() == param.numel() && shadow->is_contiguous(), "shadow size mismatch");
+    sh = ptr<__nv_bfloat16>(*shadow);
+  }
+  check(pra_adamw(ptr<float>(param), sh, grad.data_ptr(), grad.scalar_type() == at::kBFloat16, ptr<float>(m),
+                  ptr<float>(v), param.numel(), (float)lr, (float)beta1, (float)beta2, (float)eps,
+                  (float)weight_decay, (int)step, optr<float>(coef), (float)grad_scale, stream()),
+        "adamw");
+}
+
+// ---------------------------------------------------------------- gists
+std::vector<torch::Tensor> gist_mean(torch::Tensor pool_k, torch::Tensor pool_v, torch::Tensor start,
+                                     torch::Tensor len) {
+  c10::cuda::CUDAGuard guard(pool_k.device());
+  expect(pool_k, at::kBFloat16, "pool_k");
+  TORCH_CHECK(pool_k.stride(1) == 1 && pool_v.stride(0) == pool_k.stride(0), "pools must be row-major");
+  const int C = start.numel(), D = pool_k.size(1);
+  auto opts = pool_k.options().dtype(at::kFloat);
+  auto gk = torch::empty({C, D}, opts), gv = torch::empty({C, D}, opts), gn = torch::empty({C, D}, opts);
+  check(pra_gist_mean(ptr<const __nv_bfloat16>(pool_k), ptr<const __nv_bfloat16>(pool_v), pool_k.stride(0),
+                      ptr<const int>(start), ptr<const int>(len), C, D, ptr<float>(gk), ptr<float>(gv),
+                      ptr<float>(gn), stream()),
+        "gist_mean");
+  return {gk, gv, gn};
+}
+
+std::vector<torch::Tensor> gist_kmeans(torch::Tensor pool_k, torch::Tensor pool_v, torch::Tensor start,
+                                       torch::Tensor len, int64_t G, int64_t max_iters, double tol, bool normalize,
+                                       bool kmeanspp, bool farthest, torch::Tensor init_first, torch::Tensor init_idx,
+                                       torch::Tensor exp_draws, torch::Tensor exp_off) {
+  c10::cuda::CUDAGuard guard(pool_k.device());
+  expect(pool_k, at::kBFloat16, "pool_k");
+  const int C = start.numel(), D = pool_k.size(1);
+  auto fo = pool_k.options().dtype(at::kFloat);
+  auto io = pool_k.options().dtype(at::kInt);
+  auto gk = torch::zeros({C, G, D}, fo), gv = torch::zeros({C, G, D}, fo);
+  auto count = torch::empty({C}, io), occ = torch::zeros({C, G}, io), iters = torch::empty({C}, io),
+       status = torch::empty({C}, io);
+  check(pra_gist_kmeans(ptr<const __nv_bfloat16>(pool_k), ptr<const __nv_bfloat16>(pool_v), pool_k.stride(0),
+                        ptr<const int>(start), ptr<const int>(len), C, D, (int)G, (int)max_iters, (float)tol, normalize,
+                        kmeanspp, farthest, ptr<const int>(init_first), ptr<const int>(init_idx),
+                        ptr<const float>(exp_draws), ptr<const int64_t>(exp_off), ptr<float>(gk), ptr<float>(gv),
+                        ptr<int>(count), ptr<int>(occ), ptr<int>(iters), ptr<int>(status), stream()),
+        "gist_kmeans");
+  return {gk, gv, count, occ, iters, status};
+}
+
+// ---------------------------------------------------------------- routing
+std::vector<torch::Tensor> route(torch::Tensor query, torch::Tensor gists, torch::Tensor gist_count,
+                                 torch::Tensor row_pos_off, torch::Tensor row_ref_off, torch::Tensor ref_pos_off,
+                                 torch::Tensor pos_chunk, torch::Tensor pos_ref, torch::Tensor pos_rank,
+                                 torch::Tensor chunk_start,
+                                 torch::Tensor chunk_len, torch::Tensor chunk_pool_row, int64_t k_ref, int64_t k_chunk,
+                                 int64_t gist_agg, int64_t ref_agg, double threshold, int64_t budget, bool gist_only,
+                                 bool full_reference, bool deduplicate, int64_t max_sel, int64_t max_mem,
+                                 c10::optional<torch::Tensor> budget_rows) {
+  c10::cuda::CUDAGuard guard(query.device());
+  expect(query, at::kBFloat16, "query");
+  expect(gists, at::kFloat, "gists");
+  TORCH_CHECK(query.dim() == 2 && query.stride(1) == 1, "query must be [B, >=D] row-major");
+  TORCH_CHECK(gists.dim() == 3 && gists.is_contiguous(), "gists must be [C, G, D] contiguous");
+  RouteParams p{};
+  p.B = query.size(0);
+  p.D = gists.size(2);
+  p.G = gists.size(1);
+  p.query = ptr<const __nv_bfloat16>(query);
+  p.query_stride = query.stride(0);
+  p.gists = ptr<const float>(gists);
+  p.gist_count = ptr<const int>(gist_count);
+  p.row_pos_off = ptr<const int>(row_pos_off);
+  p.row_ref_off = ptr<const int>(row_ref_off);
+  p.ref_pos_off = ptr<const int>(ref_pos_off);
+  p.pos_chunk = ptr<const int>(pos_chunk);
+  p.pos_ref = ptr<const int>(pos_ref);
+  p.pos_rank = ptr<const int>(pos_rank);
+  p.chunk_start = ptr<const int>(chunk_start);
+  p.chunk_len = ptr<const int>(chunk_len);
+  p.chunk_pool_row = ptr<const int>(chunk_pool_row);
+  p.k_ref = k_ref;
+  p.k_chunk = k_chunk;
+  p.gist_agg = gist_agg;
+  p.ref_agg = ref_agg;
+  p.threshold = (float)threshold;
+  p.budget = budget;
+  p.budget_rows = optr<int>(budget_rows);
+  p.gist_only = gist_only;
+  p.full_reference = full_reference;
+  p.deduplicate = deduplicate;
+  p.max_sel = max_sel;
+  p.max_mem = max_mem;
+  auto io = query.options().dtype(at::kInt);
+  auto fo = query.options().dtype(at::kFloat);
+  auto mem_idx = torch::zeros({p.B, std::max<int64_t>(max_mem, 1)}, io);
+  auto ints = torch::zeros({8, p.B}, io);  // mem_len, sel_count, candidates, duplicates, status
+  auto sel_i = torch::full({4, p.B, std::max<int64_t>(max_sel, 1)}, -1, io);
+  auto sel_f = torch::zeros({3, p.B, std::max<int64_t>(max_sel, 1)}, fo);
+  p.mem_idx = ptr<int>(mem_idx);
+  p.mem_len = ptr<int>(ints);
+  p.sel_count = p.mem_len + p.B;
+  p.routing_candidates = p.mem_len + 2 * p.B;
+  p.duplicate_tokens = p.mem_len + 3 * p.B;
+  p.status = p.mem_len + 4 * p.B;
+  const int64_t s = (int64_t)p.B * std::max<int64_t>(max_sel, 1);
+  p.sel_chunk = ptr<int>(sel_i);
+  p.sel_ref_rank = p.sel_chunk + s;
+  p.sel_chunk_rank = p.sel_chunk + 2 * s;
+  p.sel_win_index = p.sel_chunk + 3 * s;
+  p.sel_ref_score = ptr<float>(sel_f);
+  p.sel_chunk_score = p.sel_ref_score + s;
+  p.sel_win_score = p.sel_ref_score + 2 * s;
+  check(pra_route(p, stream()), "route");
+  return {mem_idx, ints, sel_i, sel_f};
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "PRA sm_100a kernels";
+  m.def("attention_fwd", &attention_fwd);
+  m.def("attention_bwd", &attention_bwd);
+  m.def("gemm", &gemm);
+  m.def("norm_fwd", &norm_fwd);
+  m.def("norm_bwd", &norm_bwd);
+  m.def("colsum", &colsum);
+  m.def("cross_entropy", &cross_entropy);
+  m.def("grad_norm", &grad_norm);
+  m.def("adamw", &adamw);
+  m.def("gist_mean", &gist_mean);
+  m.def("gist_kmeans", &gist_kmeans);
+  m.def("route", &route);
+}

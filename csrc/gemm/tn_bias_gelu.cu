@@ -1,0 +1,16 @@
+// Z = A . B^T + bias (stored as aux), D = gelu(Z)   (MLP up-projection)
+#include "../gemm_impl.cuh"
+using namespace pra::gemm;
+using Op = cutlass::epilogue::fusion::LinCombPerColBiasEltActAux<cutlass::layout::RowMajor, cutlass::epilogue::thread::GELU,
+                                                                BF16, float, BF16, BF16, BF16, float>;
+using G = Gemm<cutlass::layout::RowMajor, cutlass::layout::ColumnMajor, BF16, Op>;
+
+cudaError_t pra_gemm_tn_bias_gelu(const GemmArgs& g, cudaStream_t st) {
+  typename G::Epilogue::FusionCallbacks::Arguments fusion{};
+  fusion.alpha = g.alpha;
+  fusion.beta = 0.f;
+  fusion.bias_ptr = static_cast<const BF16*>(g.bias);
+  fusion.aux_ptr = static_cast<BF16*>(g.aux);
+  fusion.dAux = cutlass::make_cute_packed_stride(typename decltype(fusion)::StrideAux{}, {g.M, g.N, 1});
+  return G::run(g.A, g.B, nullptr, g.D, g.M, g.N, g.K, fusion, g.workspace, g.workspace_bytes, st);
+}

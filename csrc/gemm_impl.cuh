@@ -1,0 +1,103 @@
+// bf16 GEMMs on the 5th-generation tensor cores, built from the CUTLASS sm100
+// collectives (tcgen05.mma issued by one thread per CTA pair, TMA-fed shared
+// memory stages, TMEM accumulators, fused epilogues).  Each exported variant is
+// instantiated in its own translation unit so they compile in parallel.
+//
+// Conventions (all packed, row-major unless noted):
+//   "tn"    D[M,N] = A[M,K] . B[N,K]^T            (forward: X W^T)
+//   "nn"    D[M,N] = A[M,K] . B[K,N]              (data gradient: dY W)
+//   "wgrad" D[M,N] = A[K,M]^T . B[K,N]            (weight gradient: dY^T X)
+#pragma once
+
+#include <cutlass/cutlass.h>
+#include <cute/tensor.hpp>
+#include <cutlass/epilogue/collective/collective_builder.hpp>
+#include <cutlass/epilogue/fusion/operations.hpp>
+#include <cutlass/epilogue/thread/activation.h>
+#include <cutlass/gemm/collective/collective_builder.hpp>
+#include <cutlass/gemm/device/gemm_universal_adapter.h>
+#include <cutlass/gemm/kernel/gemm_universal.hpp>
+#include <cutlass/util/packed_stride.hpp>
+
+#include "kernels.h"
+
+namespace pra {
+namespace gemm {
+
+using namespace cute;
+using BF16 = cutlass::bfloat16_t;
+
+// Exact derivative of the erf GELU: d/dz [z * Phi(z)] = Phi(z) + z * phi(z).
+template <typename T>
+struct GeluErfGrad {
+  static const bool kIsHeavy = true;
+  CUTLASS_HOST_DEVICE T operator()(T const& d_t, T const& z) const {
+    const float zf = float(z);
+    const float cdf = 0.5f * (1.f + erff(zf * 0.70710678118654752f));
+    const float pdf = 0.39894228040143268f * expf(-0.5f * zf * zf);
+    return T(float(d_t) * (cdf + zf * pdf));
+  }
+};
+
+template <typename T, int N>
+struct GeluErfGrad<cutlass::Array<T, N>> {
+  static const bool kIsHeavy = true;
+  CUTLASS_HOST_DEVICE cutlass::Array<T, N> operator()(cutlass::Array<T, N> const& d_t,
+                                                      cutlass::Array<T, N> const& z) const {
+    cutlass::Array<T, N> out;
+    GeluErfGrad<T> op;
+    CUTLASS_PRAGMA_UNROLL
+    for (int i = 0; i < N; ++i) out[i] = op(d_t[i], z[i]);
+    return out;
+  }
+};
+
+template <class LayoutA, class LayoutB, class ElementD, class FusionOp,
+          class TileShape = Shape<_256, _128, _64>, class ClusterShape = Shape<_2, _1, _1>>
+struct Gemm {
+  using LayoutD = cutlass::layout::RowMajor;
+  static constexpr int AlignAB = 8;
+  static constexpr int AlignD = 128 / cutlass::sizeof_bits<ElementD>::value;
+  using Epilogue = typename cutlass::epilogue::collective::CollectiveBuilder<
+      cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, TileShape, ClusterShape,
+      cutlass::epilogue::collective::EpilogueTileAuto, float, float, ElementD, LayoutD, AlignD, ElementD, LayoutD,
+      AlignD, cutlass::epilogue::collective::EpilogueScheduleAuto, FusionOp>::CollectiveOp;
+  using Mainloop = typename cutlass::gemm::collective::CollectiveBuilder<
+      cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, BF16, LayoutA, AlignAB, BF16, LayoutB, AlignAB, float,
+      TileShape, ClusterShape,
+      cutlass::gemm::collective::StageCountAutoCarveout<static_cast<int>(sizeof(typename Epilogue::SharedStorage))>,
+      cutlass::gemm::collective::KernelScheduleAuto>::CollectiveOp;
+  using Kernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, Mainloop, Epilogue>;
+  using Device = cutlass::gemm::device::GemmUniversalAdapter<Kernel>;
+  using StrideA = typename Kernel::StrideA;
+  using StrideB = typename Kernel::StrideB;
+  using StrideC = typename Kernel::StrideC;
+  using StrideD = typename Kernel::StrideD;
+
+  template <class FusionArgs>
+  static cudaError_t run(const void* A, const void* B, const void* C, void* D, int M, int N, int K,
+                         FusionArgs fusion, void* workspace, size_t workspace_bytes, cudaStream_t st) {
+    if (M == 0 || N == 0) return cudaSuccess;
+    typename Device::Arguments args{
+        cutlass::gemm::GemmUniversalMode::kGemm,
+        {M, N, K, 1},
+        {static_cast<const BF16*>(A), cutlass::make_cute_packed_stride(StrideA{}, {M, K, 1}),
+         static_cast<const BF16*>(B), cutlass::make_cute_packed_stride(StrideB{}, {N, K, 1})},
+        {fusion, static_cast<const ElementD*>(C), cutlass::make_cute_packed_stride(StrideC{}, {M, N, 1}),
+         static_cast<ElementD*>(D), cutlass::make_cute_packed_stride(StrideD{}, {M, N, 1})}};
+    Device op;
+    if (op.can_implement(args) != cutlass::Status::kSuccess) return cudaErrorNotSupported;
+    if (Device::get_workspace_size(args) > workspace_bytes) return cudaErrorMemoryAllocation;
+    if (op.initialize(args, workspace, st) != cutlass::Status::kSuccess) return cudaErrorLaunchFailure;
+    if (op.run(st) != cutlass::Status::kSuccess) return cudaErrorLaunchFailure;
+    return cudaGetLastError();
+  }
+
+  static size_t workspace(int M, int N, int K) {
+    typename Device::Arguments args{cutlass::gemm::GemmUniversalMode::kGemm, {M, N, K, 1}, {}, {}};
+    return Device::get_workspace_size(args);
+  }
+};
+
+}  // namespace gemm
+}  // namespace pra

@@ -1,0 +1,128 @@
+// Host-visible parameter blocks and launch entry points of the PRA kernels.
+// Pure C++ (no torch): shared by the .cu kernel files and the binding layer.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+// ---- ragged native-K/V attention (attention.cu) ---------------------------------
+struct AttnParams {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  __nv_bfloat16* o;
+  float* lse;                  // [B, H, T] natural-log LSE of the scaled scores
+  const __nv_bfloat16* mem_k;  // pool rows [tokens, Hkv * D]
+  const __nv_bfloat16* mem_v;
+  const int* mem_idx;          // [B, mem_max] pool row of each memory key
+  const int* mem_len;          // [B]
+  const uint8_t* key_valid;    // [B, T] or nullptr
+  int64_t q_row, q_batch, k_row, k_batch, v_row, v_batch, o_row, o_batch, mem_row;
+  int B, T, H, Hkv, mem_max;
+  float scale;
+  const __nv_bfloat16* dout;
+  int64_t do_row, do_batch;
+  float* delta;                // [B, H, T] workspace
+  __nv_bfloat16* dq;
+  __nv_bfloat16* dk;
+  __nv_bfloat16* dv;
+  int64_t dq_row, dq_batch, dk_row, dk_batch, dv_row, dv_batch;
+};
+
+cudaError_t pra_attention_fwd(const AttnParams& p, int head_dim, cudaStream_t stream);
+cudaError_t pra_attention_bwd(const AttnParams& p, int head_dim, cudaStream_t stream);
+
+// ---- GEMMs (gemm/*.cu, CUTLASS sm100 collectives) -------------------------------
+struct GemmArgs {
+  const void* A;
+  const void* B;
+  const void* C;      // beta * C source (may be null when beta == 0)
+  void* D;
+  const void* bias;   // per-column bias [N] (tn variants) or null
+  void* aux;          // pre-activation output (gelu fwd) / input (gelu bwd)
+  int M, N, K;
+  float alpha, beta;
+  const float* alpha_ptr;  // device scalar overriding alpha when non-null
+  void* workspace;
+  size_t workspace_bytes;
+};
+cudaError_t pra_gemm_tn_bias(const GemmArgs& g, cudaStream_t stream);
+cudaError_t pra_gemm_tn_bias_gelu(const GemmArgs& g, cudaStream_t stream);
+cudaError_t pra_gemm_nn(const GemmArgs& g, cudaStream_t stream);
+cudaError_t pra_gemm_nn_dgelu(const GemmArgs& g, cudaStream_t stream);
+cudaError_t pra_gemm_wgrad(const GemmArgs& g, cudaStream_t stream);
+
+// ---- norms (norm.cu) --------------------------------------------------------------
+cudaError_t pra_norm_fwd(const __nv_bfloat16* x, const __nv_bfloat16* w, const __nv_bfloat16* b, __nv_bfloat16* y,
+                         float* mean, float* rstd, int M, int D, float eps, bool rms, cudaStream_t stream);
+int pra_norm_bwd_partials(int M);
+cudaError_t pra_norm_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, const __nv_bfloat16* w, const float* mean,
+                         const float* rstd, const __nv_bfloat16* dres, __nv_bfloat16* dx, float* dw_part,
+                         float* db_part, __nv_bfloat16* dw, __nv_bfloat16* db, int M, int D, bool rms,
+                         cudaStream_t stream);
+int pra_colsum_partials(int M);
+cudaError_t pra_colsum(const __nv_bfloat16* g, int M, int N, float* part, __nv_bfloat16* out, cudaStream_t stream);
+
+// ---- loss / optimizer (loss_optim.cu) -----------------------------------------------
+cudaError_t pra_cross_entropy(__nv_bfloat16* logits, int64_t M, int64_t ld, int V, const int64_t* labels,
+                              int ignore_index, float* row_loss, float* row_valid, cudaStream_t stream);
+int pra_grad_norm_parts();
+cudaError_t pra_grad_norm(const void* grad, bool grad_bf16, int64_t n, float max_norm, float* part, float* norm_out,
+                          float* coef_out, cudaStream_t stream);
+cudaError_t pra_adamw(float* param, __nv_bfloat16* shadow, const void* grad, bool grad_bf16, float* m, float* v,
+                      int64_t n, float lr, float beta1, float beta2, float eps, float weight_decay, int step,
+                      const float* coef, float grad_scale, cudaStream_t stream);
+cudaError_t pra_cast_f32_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t stream);
+
+// ---- gists (gist.cu) ------------------------------------------------------------------
+cudaError_t pra_gist_mean(const __nv_bfloat16* pk, const __nv_bfloat16* pv, int64_t row_stride, const int* start,
+                          const int* len, int C, int D, float* gk, float* gv, float* gn, cudaStream_t stream);
+cudaError_t pra_gist_kmeans(const __nv_bfloat16* pk, const __nv_bfloat16* pv, int64_t row_stride, const int* start,
+                            const int* len, int C, int D, int G, int max_iters, float tol, bool normalize,
+                            bool kmeanspp, bool farthest, const int* init_first, const int* init_idx,
+                            const float* exp_draws, const int64_t* exp_off, float* gk, float* gv, int* count,
+                            int* occupancy, int* iterations, int* status, cudaStream_t stream);
+
+// ---- row-local routing + selection + materialisation plan (routing.cu) ----------------
+struct RouteParams {
+  int B, D, G;
+  const __nv_bfloat16* query;  // [B, >= D] routing queries
+  int64_t query_stride;
+  const float* gists;          // [C, G, D] L2-normalised
+  const int* gist_count;       // [C]
+  // Namespace of row b: positions [row_pos_off[b], row_pos_off[b+1]); position q names the
+  // global chunk pos_chunk[q], its URI pos_ref[q] (index among the row's URIs, which are
+  // sorted by URI string) and its lexical chunk-id rank pos_rank[q] within that URI.
+  // URI r (global slot, row_ref_off[b] <= r < row_ref_off[b+1]) owns positions
+  // [ref_pos_off[r], ref_pos_off[r+1]).
+  const int* row_pos_off;      // [B + 1]
+  const int* row_ref_off;      // [B + 1]
+  const int* ref_pos_off;      // [R + 1]
+  const int* pos_chunk;        // [P]
+  const int* pos_ref;          // [P]
+  const int* pos_rank;         // [P]
+  const int* chunk_start;      // [C] source token start
+  const int* chunk_len;        // [C] materialisable tokens
+  const int* chunk_pool_row;   // [C] first pool row of the chunk's K/V
+  int k_ref, k_chunk, gist_agg, ref_agg;  // aggregations: 0 max, 1 mean, 2 logsumexp
+  float threshold;
+  int budget;
+  const int* budget_rows;      // [B] per-row budgets, or null (scalar budget)
+  bool gist_only, full_reference, deduplicate;
+  int max_sel, max_mem;
+  int* mem_idx;                // [B, max_mem]
+  int* mem_len;                // [B]
+  int* sel_chunk;              // [B, max_sel] retained selections, selection order
+  int* sel_ref_rank;
+  int* sel_chunk_rank;
+  float* sel_ref_score;
+  float* sel_chunk_score;
+  int* sel_win_index;
+  float* sel_win_score;
+  int* sel_count;              // [B]
+  int* routing_candidates;     // [B]
+  int* duplicate_tokens;       // [B]
+  int* status;                 // [B] 0 ok, 1 namespace too large, 2 memory list truncated
+};
+cudaError_t pra_route(const RouteParams& p, cudaStream_t stream);

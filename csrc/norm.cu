@@ -1,0 +1,195 @@
+// LayerNorm / RMSNorm forward and backward on bf16 rows (fp32 statistics).
+//
+// Forward: y = (x - mean) * rstd * w (+ b)   [RMSNorm: mean = 0, rstd = 1/sqrt(mean(x^2)+eps)]
+// Backward: dx = rstd * (w*dy - mean(w*dy) - xhat * mean(w*dy*xhat)) (+ residual grad),
+//           dw/db accumulated per CTA into fp32 partials and reduced by a second kernel.
+#include "common.cuh"
+
+namespace pra {
+namespace norm {
+
+constexpr int NT = 256;
+constexpr int MAXV = 8;  // up to 8 bf16x2 pairs per thread: D <= 4096
+
+template <bool RMS>
+__global__ void __launch_bounds__(NT) fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                                                 const __nv_bfloat16* __restrict__ b, __nv_bfloat16* __restrict__ y,
+                                                 float* __restrict__ mean_out, float* __restrict__ rstd_out, int M,
+                                                 int D, float eps) {
+  __shared__ float scratch[32];
+  const int row = blockIdx.x;
+  if (row >= M) return;
+  const __nv_bfloat162* xr = reinterpret_cast<const __nv_bfloat162*>(x + (int64_t)row * D);
+  float2 vals[MAXV];
+  float s = 0.f, ss = 0.f;
+  int n = 0;
+  for (int i = threadIdx.x; i < D / 2; i += NT, ++n) {
+    vals[n] = __bfloat1622float2(xr[i]);
+    s += vals[n].x + vals[n].y;
+    ss += vals[n].x * vals[n].x + vals[n].y * vals[n].y;
+  }
+  float mean = 0.f, var;
+  if (RMS) {
+    var = block_sum(ss, scratch) / D;
+  } else {
+    mean = block_sum(s, scratch) / D;
+    float dev = 0.f;
+    for (int j = 0; j < n; ++j) {
+      const float a = vals[j].x - mean, c = vals[j].y - mean;
+      dev += a * a + c * c;
+    }
+    var = block_sum(dev, scratch) / D;
+  }
+  const float rstd = rsqrtf(var + eps);
+  const __nv_bfloat162* wr = reinterpret_cast<const __nv_bfloat162*>(w);
+  const __nv_bfloat162* br = reinterpret_cast<const __nv_bfloat162*>(b);
+  __nv_bfloat162* yr = reinterpret_cast<__nv_bfloat162*>(y + (int64_t)row * D);
+  n = 0;
+  for (int i = threadIdx.x; i < D / 2; i += NT, ++n) {
+    const float2 wv = __bfloat1622float2(wr[i]);
+    const float2 bv = b ? __bfloat1622float2(br[i]) : make_float2(0.f, 0.f);
+    yr[i] = __floats2bfloat162_rn((vals[n].x - mean) * rstd * wv.x + bv.x, (vals[n].y - mean) * rstd * wv.y + bv.y);
+  }
+  if (threadIdx.x == 0) {
+    if (mean_out) mean_out[row] = mean;
+    rstd_out[row] = rstd;
+  }
+}
+
+// Each CTA handles `rows_per_cta` rows; writes fp32 partial dw/db [gridDim.x, D].
+template <bool RMS>
+__global__ void __launch_bounds__(NT) bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                                                 const __nv_bfloat16* __restrict__ w, const float* __restrict__ mean_in,
+                                                 const float* __restrict__ rstd_in,
+                                                 const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx,
+                                                 float* __restrict__ dw_part, float* __restrict__ db_part, int M, int D,
+                                                 int rows_per_cta) {
+  __shared__ float scratch[32];
+  float2 accw[MAXV], accb[MAXV];
+#pragma unroll
+  for (int j = 0; j < MAXV; ++j) accw[j] = accb[j] = make_float2(0.f, 0.f);
+  const __nv_bfloat162* wr = reinterpret_cast<const __nv_bfloat162*>(w);
+  const int r0 = blockIdx.x * rows_per_cta;
+  const int r1 = min(r0 + rows_per_cta, M);
+  for (int row = r0; row < r1; ++row) {
+    const __nv_bfloat162* xr = reinterpret_cast<const __nv_bfloat162*>(x + (int64_t)row * D);
+    const __nv_bfloat162* gr = reinterpret_cast<const __nv_bfloat162*>(dy + (int64_t)row * D);
+    const float mean = RMS ? 0.f : mean_in[row];
+    const float rstd = rstd_in[row];
+    float2 xh[MAXV], wg[MAXV];
+    float s1 = 0.f, s2 = 0.f;
+    int n = 0;
+    for (int i = threadIdx.x; i < D / 2; i += NT, ++n) {
+      const float2 xv = __bfloat1622float2(xr[i]);
+      const float2 gv = __bfloat1622float2(gr[i]);
+      const float2 wv = __bfloat1622float2(wr[i]);
+      xh[n] = make_float2((xv.x - mean) * rstd, (xv.y - mean) * rstd);
+      wg[n] = make_float2(gv.x * wv.x, gv.y * wv.y);
+      s1 += wg[n].x + wg[n].y;
+      s2 += wg[n].x * xh[n].x + wg[n].y * xh[n].y;
+      accw[n].x += gv.x * xh[n].x;
+      accw[n].y += gv.y * xh[n].y;
+      accb[n].x += gv.x;
+      accb[n].y += gv.y;
+    }
+    const float m1 = RMS ? 0.f : block_sum(s1, scratch) / D;
+    const float m2 = block_sum(s2, scratch) / D;
+    __nv_bfloat162* out = reinterpret_cast<__nv_bfloat162*>(dx + (int64_t)row * D);
+    const __nv_bfloat162* rr = dres ? reinterpret_cast<const __nv_bfloat162*>(dres + (int64_t)row * D) : nullptr;
+    n = 0;
+    for (int i = threadIdx.x; i < D / 2; i += NT, ++n) {
+      float gx = rstd * (wg[n].x - m1 - xh[n].x * m2);
+      float gy = rstd * (wg[n].y - m1 - xh[n].y * m2);
+      if (rr) {
+        const float2 rv = __bfloat1622float2(rr[i]);
+        gx += rv.x;
+        gy += rv.y;
+      }
+      out[i] = __floats2bfloat162_rn(gx, gy);
+    }
+  }
+  int n = 0;
+  for (int i = threadIdx.x; i < D / 2; i += NT, ++n) {
+    dw_part[(int64_t)blockIdx.x * D + 2 * i] = accw[n].x;
+    dw_part[(int64_t)blockIdx.x * D + 2 * i + 1] = accw[n].y;
+    if (db_part) {
+      db_part[(int64_t)blockIdx.x * D + 2 * i] = accb[n].x;
+      db_part[(int64_t)blockIdx.x * D + 2 * i + 1] = accb[n].y;
+    }
+  }
+}
+
+// out[d] = sum_p part[p, d] (fp32 -> out dtype); one thread per column.
+template <typename T>
+__global__ void column_reduce_kernel(const float* __restrict__ part, int P, int D, T* __restrict__ out) {
+  const int d = blockIdx.x * blockDim.x + threadIdx.x;
+  if (d >= D) return;
+  float acc = 0.f;
+  for (int p = 0; p < P; ++p) acc += part[(int64_t)p * D + d];
+  out[d] = from_f32<T>(acc);
+}
+
+}  // namespace norm
+}  // namespace pra
+
+cudaError_t pra_norm_fwd(const __nv_bfloat16* x, const __nv_bfloat16* w, const __nv_bfloat16* b, __nv_bfloat16* y,
+                         float* mean, float* rstd, int M, int D, float eps, bool rms, cudaStream_t st) {
+  using namespace pra::norm;
+  if (D % 2 || D / 2 > NT * MAXV) return cudaErrorInvalidValue;
+  if (M == 0) return cudaSuccess;
+  if (rms) fwd_kernel<true><<<M, NT, 0, st>>>(x, w, nullptr, y, nullptr, rstd, M, D, eps);
+  else fwd_kernel<false><<<M, NT, 0, st>>>(x, w, b, y, mean, rstd, M, D, eps);
+  return cudaGetLastError();
+}
+
+int pra_norm_bwd_partials(int M) { return M == 0 ? 1 : (M + 15) / 16 > 592 ? 592 : (M + 15) / 16; }
+
+cudaError_t pra_norm_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, const __nv_bfloat16* w, const float* mean,
+                         const float* rstd, const __nv_bfloat16* dres, __nv_bfloat16* dx, float* dw_part,
+                         float* db_part, __nv_bfloat16* dw, __nv_bfloat16* db, int M, int D, bool rms,
+                         cudaStream_t st) {
+  using namespace pra::norm;
+  if (D % 2 || D / 2 > NT * MAXV) return cudaErrorInvalidValue;
+  const int parts = pra_norm_bwd_partials(M);
+  const int rows = M == 0 ? 0 : (M + parts - 1) / parts;
+  if (rms) bwd_kernel<true><<<parts, NT, 0, st>>>(dy, x, w, nullptr, rstd, dres, dx, dw_part, nullptr, M, D, rows);
+  else bwd_kernel<false><<<parts, NT, 0, st>>>(dy, x, w, mean, rstd, dres, dx, dw_part, db_part, M, D, rows);
+  PRA_RETURN_IF_ERROR(cudaGetLastError());
+  column_reduce_kernel<__nv_bfloat16><<<(D + 255) / 256, 256, 0, st>>>(dw_part, parts, D, dw);
+  if (!rms && db) column_reduce_kernel<__nv_bfloat16><<<(D + 255) / 256, 256, 0, st>>>(db_part, parts, D, db);
+  return cudaGetLastError();
+}
+
+// Column sums of a bf16 matrix [M, N] (bias gradients): two-stage, deterministic.
+namespace pra {
+namespace norm {
+__global__ void colsum_partial_kernel(const __nv_bfloat16* __restrict__ g, int M, int N, int rows_per_cta,
+                                      float* __restrict__ part) {
+  const int col2 = blockIdx.y * blockDim.x + threadIdx.x;  // bf16x2 column
+  if (col2 * 2 >= N) return;
+  const int r0 = blockIdx.x * rows_per_cta, r1 = min(r0 + rows_per_cta, M);
+  float ax = 0.f, ay = 0.f;
+  for (int r = r0; r < r1; ++r) {
+    const float2 v = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(g + (int64_t)r * N)[col2]);
+    ax += v.x;
+    ay += v.y;
+  }
+  part[(int64_t)blockIdx.x * N + 2 * col2] = ax;
+  part[(int64_t)blockIdx.x * N + 2 * col2 + 1] = ay;
+}
+}  // namespace norm
+}  // namespace pra
+
+int pra_colsum_partials(int M) { return M == 0 ? 1 : ((M + 63) / 64 > 256 ? 256 : (M + 63) / 64); }
+
+cudaError_t pra_colsum(const __nv_bfloat16* g, int M, int N, float* part, __nv_bfloat16* out, cudaStream_t st) {
+  using namespace pra::norm;
+  if (N % 2) return cudaErrorInvalidValue;
+  const int parts = pra_colsum_partials(M);
+  const int rows = M == 0 ? 0 : (M + parts - 1) / parts;
+  dim3 grid(parts, (N / 2 + 255) / 256);
+  colsum_partial_kernel<<<grid, 256, 0, st>>>(g, M, N, rows, part);
+  PRA_RETURN_IF_ERROR(cudaGetLastError());
+  column_reduce_kernel<__nv_bfloat16><<<(N + 255) / 256, 256, 0, st>>>(part, parts, N, out);
+  return cudaGetLastError();
+}

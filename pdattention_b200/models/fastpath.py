@@ -1,21 +1,783 @@
-"""Device execution path for TinyGPT-PRA (filled in by the sm_100a kernel layer)."""
+"""Device execution path of TinyGPT-PRA on B200 (bf16 sm_100a kernels).
+
+What changes relative to the object path (same semantics, different execution):
+
+* **Parameters** live in flat buffers: fp32 masters (the ``nn.Parameter``
+  storage, so ``state_dict`` keeps the reference layout), a bf16 compute copy,
+  a bf16 gradient buffer written directly by the weight-gradient GEMMs, and the
+  AdamW moments; one fused kernel clips and updates everything.
+* **Cache build** for a whole batch: every row's recursive build plan is traced
+  on the host (``plan_cache_builds``), entries are grouped into *waves* by their
+  visibility dependencies (an encode that reads memory runs after everything it
+  can see), and each wave encodes all its chunks of all rows in ONE batched
+  forward.  The QKV GEMM of every layer writes straight into a per-layer pool,
+  which IS the chunk K/V store (zero copy); gists (mean or k-means) are pooled
+  on the device from those rows.
+* **Routing + selection + materialisation** run in one kernel per layer
+  (``pra_ops.route``) against row-local namespaces, producing the memory key
+  list consumed by the ragged attention kernel -- no host round trip.
+
+Unsupported configurations (legacy cross-attention transport, reference-first
+or global-chunks search, summaries, trainable gists, grouped encoding, CPU
+residency, head widths other than 32/64/128) keep using the object path.
+"""
 
 from __future__ import annotations
 
+import math
+import time
+from dataclasses import dataclass, field
+
 import torch
 
-from .tiny import TinyPRAModel
+from ..chunking import partition_reference_tokens
+from ..memory.gists import kmeanspp_random_stream
+from ..memory.gists.strategies import local_generator
+from ..memory.services import plan_cache_builds
+from ..ops import _ext
+from ..ops.kernels import MemoryView, WeightSlot, attention, layer_norm, linear, lm_head_loss, lm_head_logits, mlp
+from .tiny import PRATransformerBlock, TinyPRAModel
+
+_AGG = {"max": 0, "mean": 1, "logsumexp": 2}
+_ALIGN = 8  # elements: every flat region starts 16-byte aligned (TMA and vector loads need 16)
+
+
+def unsupported_reason(cfg) -> str | None:
+    """Why a configuration must use the object path (``None`` when the device path applies)."""
+    head_dim = cfg.d_model // cfg.n_heads
+    checks = [
+        (cfg.n_vanilla_layers or cfg.n_mixed_layers, "vanilla/mixed blocks"),
+        (cfg.memory_transport != "native_kv", "cross_attention transport"),
+        (cfg.search_strategy != "hierarchical", f"search_strategy={cfg.search_strategy}"),
+        (cfg.routing_backend != "tensorized", "legacy routing backend"),
+        (cfg.use_summary, "summary routing"),
+        (cfg.cache_build_mode != "detached", "trainable gists"),
+        (cfg.reference_encoding_strategy != "independent", "grouped encoding"),
+        (cfg.encoding_chunking is not None, "bounded encoding"),
+        (cfg.kv_cache_residency != "gpu", "CPU-resident K/V"),
+        (cfg.gist_mode not in {"mean", "kmeans"}, f"gist_mode={cfg.gist_mode}"),
+        (cfg.reference_level_gist_mode is not None, "URI-level gists"),
+        (cfg.gists_per_chunk > 8, "more than 8 gists"),
+        (head_dim not in (32, 64, 128), f"head_dim={head_dim}"),
+        (cfg.dropout > 0, "dropout"),
+        (cfg.d_model % 8 or cfg.d_ff % 8, "widths not multiple of 8"),
+        (cfg.collect_routing_metrics or cfg.collect_rank_diagnostics, "full ranking diagnostics"),
+        (cfg.collect_detailed_timing, "host-timed diagnostics"),
+    ]
+    for bad, reason in checks:
+        if bad:
+            return reason
+    return None
+
+
+# ---------------------------------------------------------------------------
+# Flat parameters
+# ---------------------------------------------------------------------------
+
+def _round(n: int) -> int:
+    return (n + _ALIGN - 1) // _ALIGN * _ALIGN
+
+
+class FlatParams:
+    """fp32 master / bf16 compute / bf16 gradient / AdamW moment buffers in one layout."""
+
+    def __init__(self, model: TinyPRAModel, vocab_pad: int):
+        self.model = model
+        ordered = self._ordered(model)
+        offsets, cursor = {}, 0
+        for name, p in ordered:
+            offsets[name] = cursor
+            cursor += _round(p.numel())
+        head = model.head.weight
+        self.head_offset = offsets["head.weight"]
+        # the head's bf16 view is padded to vocab_pad rows of zeros (TMA-friendly logits width)
+        self.total = cursor + _round((vocab_pad - head.shape[0]) * head.shape[1])
+        dev = head.device
+        self.master = torch.zeros(self.total, device=dev, dtype=torch.float32)
+        self.shadow = torch.zeros(self.total, device=dev, dtype=torch.bfloat16)
+        self.grad = torch.zeros(self.total, device=dev, dtype=torch.bfloat16)
+        self.exp_avg = torch.zeros(self.total, device=dev, dtype=torch.float32)
+        self.exp_avg_sq = torch.zeros(self.total, device=dev, dtype=torch.float32)
+        self.offsets = offsets
+        self.params = dict(ordered)
+        for name, p in ordered:
+            view = self.master[offsets[name]: offsets[name] + p.numel()].view_as(p)
+            view.copy_(p.data)
+            p.data = view
+        self.vocab_pad = vocab_pad
+        self.refresh_shadow()
+
+    @staticmethod
+    def _ordered(model: TinyPRAModel) -> list[tuple[str, torch.nn.Parameter]]:
+        named = dict(model.named_parameters())
+        order = []
+        for i, block in enumerate(model.blocks):
+            pre = f"blocks.{i}."
+            for proj in ("q_proj", "k_proj", "v_proj"):
+                order.append(pre + f"attn.{proj}.weight")
+            for proj in ("q_proj", "k_proj", "v_proj"):
+                order.append(pre + f"attn.{proj}.bias")
+            order += [pre + "attn.o_proj.weight", pre + "attn.o_proj.bias", pre + "ln1.weight", pre + "ln1.bias",
+                      pre + "ln2.weight", pre + "ln2.bias", pre + "ff.0.weight", pre + "ff.0.bias",
+                      pre + "ff.2.weight", pre + "ff.2.bias"]
+        order += ["token_emb.weight", "pos_emb.weight", "ln.weight", "ln.bias"]
+        order += [n for n in named if n not in order and n != "head.weight"]
+        order.append("head.weight")
+        return [(n, named[n]) for n in order]
+
+    def refresh_shadow(self) -> None:
+        self.shadow.copy_(self.master)
+
+    def view(self, buffer: torch.Tensor, name: str, rows: int | None = None) -> torch.Tensor:
+        p = self.params[name]
+        if rows is None:
+            return buffer[self.offsets[name]: self.offsets[name] + p.numel()].view_as(p)
+        return buffer[self.offsets[name]: self.offsets[name] + rows * p.shape[1]].view(rows, p.shape[1])
+
+    def span(self, buffer: torch.Tensor, first: str, count: int, shape) -> torch.Tensor:
+        """A contiguous view covering ``count`` elements starting at parameter ``first``."""
+        start = self.offsets[first]
+        return buffer[start: start + count].view(*shape)
+
+    def slot(self, weight: str, bias: str | None = None) -> WeightSlot:
+        return WeightSlot(w=self.view(self.shadow, weight), b=self.view(self.shadow, bias) if bias else None,
+                          gw=self.view(self.grad, weight), gb=self.view(self.grad, bias) if bias else None)
+
+
+class FusedAdamW(torch.optim.Optimizer):
+    """AdamW over the flat buffers (one clip-norm reduction + one update kernel per step).
+
+    Parameter groups expose ``lr`` / ``betas`` / ``eps`` / ``weight_decay`` so the
+    stock ``LambdaLR`` warm-up and checkpoint round trips work unchanged.
+    """
+
+    def __init__(self, flat: FlatParams, lr: float, weight_decay: float, betas=(0.9, 0.999), eps: float = 1e-8,
+                 max_grad_norm: float = 1.0):
+        super().__init__(list(flat.params.values()), dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay))
+        self.flat = flat
+        self.max_grad_norm = max_grad_norm
+        self.step_count = 0
+        self.last_norm = None
+        self.grad_source = None  # set by the data-parallel engine to its reduced fp32 buffer
+
+    def zero_grad(self, set_to_none: bool = True) -> None:
+        for s in getattr(self.flat, "slots", ()):
+            s.fresh[0] = True
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        ext = _ext.require()
+        group = self.param_groups[0]
+        grads = self.grad_source if self.grad_source is not None else self.flat.grad
+        norm, coef = ext.grad_norm(grads, float(self.max_grad_norm))
+        self.step_count += 1
+        b1, b2 = group["betas"]
+        ext.adamw(self.flat.master, self.flat.shadow, grads, self.flat.exp_avg, self.flat.exp_avg_sq,
+                  float(group["lr"]), b1, b2, float(group["eps"]), float(group["weight_decay"]), self.step_count,
+                  coef, 1.0)
+        self.last_norm = norm
+        return None
+
+    def state_dict(self):
+        base = super().state_dict()
+        base["fused"] = {"step": self.step_count, "exp_avg": self.flat.exp_avg.cpu(),
+                         "exp_avg_sq": self.flat.exp_avg_sq.cpu()}
+        return base
+
+    def load_state_dict(self, state_dict):
+        fused = state_dict.get("fused")
+        if fused is not None:
+            self.step_count = int(fused["step"])
+            self.flat.exp_avg.copy_(fused["exp_avg"])
+            self.flat.exp_avg_sq.copy_(fused["exp_avg_sq"])
+        for group, saved in zip(self.param_groups, state_dict["param_groups"]):
+            for key in ("lr", "betas", "eps", "weight_decay", "initial_lr"):
+                if key in saved:
+                    group[key] = saved[key]
+
+
+# ---------------------------------------------------------------------------
+# Batched cache plan
+# ---------------------------------------------------------------------------
+
+@dataclass
+class ChunkRecord:
+    row: int
+    entry: int           # global entry index
+    uri: str
+    chunk_id: str
+    token_start: int
+    token_end: int
+    token_ids: tuple
+    seq: int = -1        # encode sequence (pool rows seq * L .. seq * L + len)
+    metadata: dict = field(default_factory=dict)
+
+
+@dataclass
+class EntryRecord:
+    row: int
+    uri: str
+    text: str
+    metadata: dict
+    use_memory: bool
+    visible: tuple        # global entry indices readable while this entry encodes
+    chunks: list = field(default_factory=list)  # global chunk indices
+    wave: int = 0
+
+
+class Namespace:
+    """Device arrays describing row-local routing namespaces (see ``RouteParams``)."""
+
+    def __init__(self, rows_entries: list[list[int]], entries: list[EntryRecord], chunks: list[ChunkRecord],
+                 device):
+        row_pos_off, row_ref_off, ref_pos_off = [0], [0], [0]
+        pos_chunk, pos_ref, pos_rank = [], [], []
+        for entry_ids in rows_entries:
+            by_uri = sorted(entry_ids, key=lambda e: entries[e].uri)
+            for local_ref, e in enumerate(by_uri):
+                ids = entries[e].chunks
+                rank = {c: i for i, c in enumerate(sorted(ids, key=lambda c: chunks[c].chunk_id))}
+                for c in ids:
+                    pos_chunk.append(c)
+                    pos_ref.append(local_ref)
+                    pos_rank.append(rank[c])
+                ref_pos_off.append(len(pos_chunk))
+            row_pos_off.append(len(pos_chunk))
+            row_ref_off.append(len(ref_pos_off) - 1)
+        as_int = lambda x: torch.tensor(x, dtype=torch.int32, device=device)  # noqa: E731
+        self.row_pos_off, self.row_ref_off, self.ref_pos_off = as_int(row_pos_off), as_int(row_ref_off), \
+            as_int(ref_pos_off)
+        self.pos_chunk, self.pos_ref, self.pos_rank = as_int(pos_chunk or [0]), as_int(pos_ref or [0]), \
+            as_int(pos_rank or [0])
+        self.rows_entries = rows_entries
+        self.empty = len(pos_chunk) == 0
+
+
+class BatchMemory:
+    """All rows' encoded references of one batch: pools, gists and chunk tables per layer."""
+
+    def __init__(self, runtime, entries, chunks, rows, seq_len, device):
+        cfg = runtime.cfg
+        self.entries, self.chunks, self.rows = entries, chunks, rows
+        self.seq_len = seq_len
+        n_seq = max(len(chunks), 1)
+        width = 3 * cfg.d_model
+        self.pools = [torch.empty((n_seq * seq_len, width), device=device, dtype=torch.bfloat16)
+                      for _ in range(cfg.n_layers)]
+        g = max(cfg.gists_per_chunk if cfg.gist_mode == "kmeans" else 1, 1)
+        self.G = g
+        self.gists = [torch.zeros((n_seq, g, cfg.d_model), device=device, dtype=torch.float32)
+                      for _ in range(cfg.n_layers)]
+        self.gist_k = [torch.zeros((n_seq, g, cfg.d_model), device=device, dtype=torch.float32)
+                       for _ in range(cfg.n_layers)]
+        self.gist_v = [torch.zeros((n_seq, g, cfg.d_model), device=device, dtype=torch.float32)
+                       for _ in range(cfg.n_layers)]
+        self.gist_count = [torch.zeros(n_seq, device=device, dtype=torch.int32) for _ in range(cfg.n_layers)]
+        as_int = lambda x: torch.tensor(x or [0], dtype=torch.int32, device=device)  # noqa: E731
+        self.chunk_start = as_int([c.token_start for c in chunks])
+        self.chunk_len = as_int([len(c.token_ids) for c in chunks])
+        self.chunk_pool_row = as_int([c.seq * seq_len for c in chunks])
+
+    def k_view(self, layer: int, d: int) -> torch.Tensor:
+        return self.pools[layer][:, d:2 * d]
+
+    def v_view(self, layer: int, d: int) -> torch.Tensor:
+        return self.pools[layer][:, 2 * d:]
+
+
+@dataclass
+class LayerRouting:
+    """Device outputs of one routing call (kept for deferred traces / metrics)."""
+
+    mem_idx: torch.Tensor
+    ints: torch.Tensor
+    sel_i: torch.Tensor
+    sel_f: torch.Tensor
+
+
+# ---------------------------------------------------------------------------
+# Runtime
+# ---------------------------------------------------------------------------
+
+class DeviceRuntime:
+    def __init__(self, model: TinyPRAModel):
+        self.model = model
+        self.cfg = model.cfg
+        cfg = self.cfg
+        self.device = model.head.weight.device
+        self.head_dim = cfg.d_model // cfg.n_heads
+        self.vocab_pad = (cfg.vocab_size + 127) // 128 * 128
+        self.flat = FlatParams(model, self.vocab_pad)
+        f = self.flat
+        d = cfg.d_model
+        self.layers = []
+        for i in range(cfg.n_layers):
+            pre = f"blocks.{i}."
+            qkv = WeightSlot(w=f.span(f.shadow, pre + "attn.q_proj.weight", 3 * d * d, (3 * d, d)),
+                             b=f.span(f.shadow, pre + "attn.q_proj.bias", 3 * d, (3 * d,)),
+                             gw=f.span(f.grad, pre + "attn.q_proj.weight", 3 * d * d, (3 * d, d)),
+                             gb=f.span(f.grad, pre + "attn.q_proj.bias", 3 * d, (3 * d,)))
+            self._check_contiguous(pre)
+            self.layers.append({
+                "ln1": f.slot(pre + "ln1.weight", pre + "ln1.bias"), "qkv": qkv,
+                "o": f.slot(pre + "attn.o_proj.weight", pre + "attn.o_proj.bias"),
+                "ln2": f.slot(pre + "ln2.weight", pre + "ln2.bias"),
+                "up": f.slot(pre + "ff.0.weight", pre + "ff.0.bias"),
+                "down": f.slot(pre + "ff.2.weight", pre + "ff.2.bias"),
+            })
+        self.ln_f = f.slot("ln.weight", "ln.bias")
+        head_rows = self.vocab_pad
+        self.head = WeightSlot(w=f.view(f.shadow, "head.weight", rows=head_rows),
+                               gw=f.view(f.grad, "head.weight", rows=head_rows))
+        f.slots = [s for layer in self.layers for s in layer.values()] + [self.ln_f, self.head]
+        self.tok_emb_w = f.view(f.shadow, "token_emb.weight")
+        self.pos_emb_w = f.view(f.shadow, "pos_emb.weight")
+        self.tok_emb_g = f.view(f.grad, "token_emb.weight")
+        self.pos_emb_g = f.view(f.grad, "pos_emb.weight")
+        self.anchor = torch.zeros(1, device=self.device, requires_grad=True)  # puts embeddings on the tape
+        self._kmeans_streams: dict[int, tuple] = {}
+        self.last_routing: dict[int, LayerRouting] = {}
+        self.last_memory: BatchMemory | None = None
+        self.last_namespace: Namespace | None = None
+
+    def _check_contiguous(self, pre: str) -> None:
+        f = self.flat
+        d = self.cfg.d_model
+        if (f.offsets[pre + "attn.k_proj.weight"] != f.offsets[pre + "attn.q_proj.weight"] + d * d
+                or f.offsets[pre + "attn.v_proj.bias"] != f.offsets[pre + "attn.q_proj.bias"] + 2 * d):
+            raise RuntimeError("q/k/v parameters must be adjacent in the flat layout (d_model*d_model % 64 != 0?)")
+
+    # -- embeddings -----------------------------------------------------------
+    def embed(self, ids: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
+        return _Embed.apply(ids, positions, self.anchor, self)
+
+    # -- one decoder pass ---------------------------------------------------------
+    def run_blocks(self, x: torch.Tensor, b: int, t: int, key_valid, routing, memory: BatchMemory | None,
+                   stop_after_kv: bool = False, pool_rows: slice | None = None, budget: int = 0,
+                   query_rows: torch.Tensor | None = None):
+        """Run the block stack on ``x`` ``[b*t, D]``.
+
+        ``routing`` is a ``Namespace`` (or ``None`` for no memory); with ``pool_rows``
+        the QKV of every layer is written into those rows of the layer pool (cache
+        build).  ``stop_after_kv`` skips the last block's attention and MLP.
+        """
+        cfg = self.cfg
+        d = cfg.d_model
+        for li, layer in enumerate(self.layers):
+            h = layer_norm(x, layer["ln1"])
+            if pool_rows is not None:
+                qkv = memory.pools[li][pool_rows]
+                _ext.require().gemm("tn", h, layer["qkv"].w, None, qkv, layer["qkv"].b, None, 1.0, 0.0, None)
+                if stop_after_kv and li == len(self.layers) - 1:
+                    return None
+            else:
+                qkv = linear(h, layer["qkv"])
+            qkv3 = qkv.view(b, t, 3 * d)
+            mem = None
+            if routing is not None and not routing.empty:
+                mem = self.route(li, qkv3, routing, memory, budget, query_rows)
+            a = attention(qkv3, cfg.n_heads, self.head_dim, mem, key_valid)
+            x = linear(a.view(b * t, d), layer["o"], residual=x)
+            x = mlp(layer_norm(x, layer["ln2"]), x, layer["up"], layer["down"])
+        return x
+
+    def route(self, li: int, qkv3: torch.Tensor, ns: Namespace, memory: BatchMemory, budget,
+              query_rows: torch.Tensor | None) -> MemoryView:
+        cfg = self.cfg
+        d = cfg.d_model
+        if query_rows is None:
+            query = qkv3[:, -1, :d]
+        else:
+            query = qkv3[torch.arange(qkv3.shape[0], device=qkv3.device), query_rows, :d]
+        max_sel = max(1, min(256, cfg.top_k_references * cfg.top_k_chunks_per_reference
+                             if cfg.detail_materialization != "full_reference" else 256))
+        budget_rows = budget if torch.is_tensor(budget) else None
+        scalar_budget = int(budget) if budget_rows is None else self.cfg.effective_model_max_context_tokens
+        max_mem = max(scalar_budget, 1)
+        gist_only = cfg.detail_materialization == "gist_only"
+        mem_idx, ints, sel_i, sel_f = _ext.require().route(
+            query, memory.gists[li], memory.gist_count[li], ns.row_pos_off, ns.row_ref_off, ns.ref_pos_off,
+            ns.pos_chunk, ns.pos_ref, ns.pos_rank, memory.chunk_start, memory.chunk_len, memory.chunk_pool_row,
+            min(cfg.top_k_references, 64), cfg.top_k_chunks_per_reference, _AGG[cfg.gist_score_aggregation],
+            _AGG[cfg.reference_score_aggregation], float(cfg.trigger_threshold), scalar_budget, gist_only,
+            cfg.detail_materialization == "full_reference", cfg.overlap_materialization == "deduplicate", max_sel,
+            max_mem, budget_rows)
+        self.last_routing[li] = LayerRouting(mem_idx, ints, sel_i, sel_f)
+        if gist_only:
+            gk = memory.gist_k[li].view(-1, d).bfloat16()
+            gv = memory.gist_v[li].view(-1, d).bfloat16()
+            return MemoryView(gk, gv, mem_idx, ints[0])
+        return MemoryView(memory.k_view(li, d), memory.v_view(li, d), mem_idx, ints[0])
+
+    # -- cache build ------------------------------------------------------------
+    def build_memory(self, metadata_rows: list[dict], tokenizer, resolver_config=None):
+        """Trace every row's recursive build, then encode all rows' chunks wave by wave."""
+        cfg = self.cfg
+        caches, builders = plan_cache_builds(self.model, tokenizer, metadata_rows, resolver_config=resolver_config)
+        entries: list[EntryRecord] = []
+        chunks: list[ChunkRecord] = []
+        rows: list[list[int]] = []
+        limit = cfg.effective_model_max_context_tokens
+        for row, builder in enumerate(builders):
+            index_of = {}
+            row_entries = []
+            for step in builder.plan:
+                ids = list(tokenizer.encode(step.text))
+                if len(ids) > limit:
+                    raise _Unsupported("reference longer than the native limit needs bounded encoding")
+                e = len(entries)
+                index_of[step.uri] = e
+                record = EntryRecord(row, step.uri, step.text, step.metadata, step.use_pra_memory,
+                                     tuple(index_of[u] for u in step.visible_uris if u in index_of))
+                for chunk in partition_reference_tokens(step.uri, ids, tokenizer, cfg, step.metadata,
+                                                        text=step.text, max_chunk_tokens=limit):
+                    ids_c = tuple(chunk.token_ids[:limit])
+                    record.chunks.append(len(chunks))
+                    chunks.append(ChunkRecord(row, e, step.uri, chunk.chunk_id, chunk.token_start,
+                                              min(chunk.token_start + len(ids_c), chunk.token_end), ids_c,
+                                              metadata=dict(chunk.metadata)))
+                record.wave = (1 + max((entries[v].wave for v in record.visible), default=-1)) if record.use_memory \
+                    else 0
+                entries.append(record)
+                row_entries.append(e)
+            rows.append(row_entries)
+        seq_len = max((len(c.token_ids) for c in chunks), default=1)
+        n_waves = max((e.wave for e in entries), default=-1) + 1
+        seq = 0
+        order = []
+        for wave in range(n_waves):
+            for e in entries:
+                if e.wave == wave:
+                    for c in e.chunks:
+                        chunks[c].seq = seq
+                        order.append(c)
+                        seq += 1
+        memory = BatchMemory(self, entries, chunks, rows, seq_len, self.device)
+        with torch.no_grad():
+            start = 0
+            for wave in range(n_waves):
+                wave_chunks = [c for c in order if entries[chunks[c].entry].wave == wave]
+                if not wave_chunks:
+                    continue
+                self._encode_wave(memory, wave_chunks, start)
+                start += len(wave_chunks)
+        self.last_memory = memory
+        return memory, caches, builders
+
+    def _encode_wave(self, memory: BatchMemory, wave_chunks: list[int], first_seq: int) -> None:
+        cfg = self.cfg
+        n = len(wave_chunks)
+        L = memory.seq_len
+        ids = torch.zeros((n, L), dtype=torch.long)
+        valid = torch.zeros((n, L), dtype=torch.uint8)
+        last = torch.zeros(n, dtype=torch.long)
+        for i, c in enumerate(wave_chunks):
+            toks = memory.chunks[c].token_ids
+            ids[i, : len(toks)] = torch.tensor(toks, dtype=torch.long)
+            valid[i, : len(toks)] = 1
+            last[i] = len(toks) - 1
+        ids, valid, last = (t.to(self.device, non_blocking=True) for t in (ids, valid, last))
+        positions = torch.arange(L, device=self.device).expand(n, L)
+        x = self.embed(ids, positions)
+        entries = memory.entries
+        needs_memory = any(entries[memory.chunks[c].entry].use_memory for c in wave_chunks)
+        namespace = None
+        if needs_memory:
+            rows_entries = [list(entries[memory.chunks[c].entry].visible)
+                            if entries[memory.chunks[c].entry].use_memory else [] for c in wave_chunks]
+            namespace = Namespace(rows_entries, entries, memory.chunks, self.device)
+        # each chunk is its own native call: its budget uses its own (unpadded) length
+        lengths = torch.tensor([len(memory.chunks[c].token_ids) for c in wave_chunks], dtype=torch.int32)
+        budget = cfg.effective_model_max_context_tokens - lengths - cfg.context_safety_reserve_tokens
+        if cfg.max_materialized_memory_tokens is not None:
+            budget = budget.clamp_max(cfg.max_materialized_memory_tokens)
+        budget = budget.clamp_min(0).to(self.device, non_blocking=True)
+        rows = slice(first_seq * L, (first_seq + n) * L)
+        self.run_blocks(x, n, L, valid, namespace, memory, stop_after_kv=True, pool_rows=rows, budget=budget,
+                        query_rows=last)
+        self._pool_gists(memory, wave_chunks)
+
+    def _pool_gists(self, memory: BatchMemory, wave_chunks: list[int]) -> None:
+        cfg = self.cfg
+        d = cfg.d_model
+        ext = _ext.require()
+        idx = torch.tensor(wave_chunks, dtype=torch.long, device=self.device)
+        start = memory.chunk_pool_row[idx].contiguous()
+        length = memory.chunk_len[idx].contiguous()
+        if cfg.gist_mode == "kmeans":
+            stream = self._kmeans_stream([len(memory.chunks[c].token_ids) for c in wave_chunks])
+        for li in range(cfg.n_layers):
+            pk, pv = memory.k_view(li, d), memory.v_view(li, d)
+            if cfg.gist_mode == "mean":
+                gk, gv, gn = ext.gist_mean(pk, pv, start, length)
+                memory.gist_k[li][idx, 0] = gk
+                memory.gist_v[li][idx, 0] = gv
+                memory.gists[li][idx, 0] = gn
+                memory.gist_count[li][idx] = 1
+            else:
+                G = memory.G
+                gk, gv, count, _occ, _it, status = ext.gist_kmeans(
+                    pk, pv, start, length, G, cfg.gist_kmeans_max_iters, float(cfg.gist_kmeans_tol),
+                    bool(cfg.gist_kmeans_normalize), cfg.gist_kmeans_init == "kmeans++",
+                    cfg.gist_kmeans_empty_cluster_policy == "farthest", *stream)
+                memory.gist_k[li][idx] = gk
+                memory.gist_v[li][idx] = gv
+                memory.gists[li][idx] = torch.nn.functional.normalize(gk, dim=-1, eps=1e-12)
+                memory.gist_count[li][idx] = count
+
+    def _kmeans_stream(self, lengths: list[int]):
+        """Per-chunk random-stream tables for the k-means kernel (cached per chunk length)."""
+        cfg = self.cfg
+        G = max(cfg.gists_per_chunk, 1)
+        firsts, offs, draws, idx_flat = [], [], [], []
+        cursor = 0
+        cache = {}
+        for n in lengths:
+            if n not in cache:
+                count = min(G, n)
+                if cfg.gist_kmeans_init == "kmeans++":
+                    first, exp = kmeanspp_random_stream(n, count, cfg.gist_kmeans_seed)
+                    cache[n] = (first, exp.flatten(), [])
+                else:
+                    perm = torch.randperm(n, generator=local_generator(cfg.gist_kmeans_seed))[:count]
+                    cache[n] = (0, torch.zeros(0), perm.tolist())
+            first, exp, perm = cache[n]
+            if cfg.gist_kmeans_init == "kmeans++":
+                firsts.append(first)
+                offs.append(cursor)
+                draws.append(exp)
+                cursor += exp.numel()
+            else:
+                firsts.append(len(idx_flat))
+                idx_flat.extend(perm)
+                offs.append(0)
+        dev = self.device
+        exp_all = torch.cat(draws) if draws else torch.zeros(1)
+        return (torch.tensor(firsts, dtype=torch.int32, device=dev),
+                torch.tensor(idx_flat or [0], dtype=torch.int32, device=dev), exp_all.float().to(dev),
+                torch.tensor(offs, dtype=torch.int64, device=dev))
+
+    # -- prompt forward + loss ----------------------------------------------------
+    def prompt_forward(self, input_ids, attention_mask, memory: BatchMemory | None, position_offset=0):
+        cfg = self.cfg
+        b, t = input_ids.shape
+        if torch.is_tensor(position_offset):
+            positions = position_offset.to(self.device).view(b, 1) + torch.arange(t, device=self.device)[None]
+        else:
+            positions = torch.arange(int(position_offset), int(position_offset) + t, device=self.device).expand(b, t)
+        if attention_mask is not None:
+            positions = positions.masked_fill(~attention_mask.bool(), 0)
+        x = self.embed(input_ids, positions)
+        valid = attention_mask.to(torch.uint8).contiguous() if attention_mask is not None else None
+        namespace = None
+        if memory is not None:
+            namespace = Namespace(memory.rows, memory.entries, memory.chunks, self.device)
+            self.last_namespace = namespace
+        budget = cfg.effective_model_max_context_tokens - t - cfg.context_safety_reserve_tokens
+        if budget < 0:
+            raise ValueError("Direct context and safety reserve exceed model_max_context_tokens.")
+        if cfg.max_materialized_memory_tokens is not None:
+            budget = min(budget, cfg.max_materialized_memory_tokens)
+        last = None
+        if attention_mask is not None:
+            pos = torch.arange(t, device=self.device).expand(b, t)
+            last = pos.masked_fill(~attention_mask.bool(), -1).max(dim=1).values
+        self.last_routing = {}
+        x = self.run_blocks(x, b, t, valid, namespace, memory, budget=budget, query_rows=last)
+        return layer_norm(x, self.ln_f)
+
+    def loss(self, hidden: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
+        return lm_head_loss(hidden, self.head, labels.reshape(-1).contiguous(), self.cfg.vocab_size, 0)
+
+    def logits(self, hidden: torch.Tensor, b: int, t: int) -> torch.Tensor:
+        return lm_head_logits(hidden, self.head)[:, : self.cfg.vocab_size].view(b, t, -1)
+
+
+class _Unsupported(RuntimeError):
+    pass
+
+
+class _Embed(torch.autograd.Function):
+    """x = token_emb[ids] + pos_emb[positions] (bf16); gradients land in the flat buffer."""
+
+    @staticmethod
+    def forward(ctx, ids, positions, anchor, rt: DeviceRuntime):
+        x = (rt.tok_emb_w[ids].float() + rt.pos_emb_w[positions].float()).bfloat16()
+        ctx.rt = rt
+        ctx.save_for_backward(ids, positions)
+        return x.view(-1, x.shape[-1])
+
+    @staticmethod
+    def backward(ctx, dx):
+        ids, positions = ctx.saved_tensors
+        rt = ctx.rt
+        d = dx.shape[-1]
+        g = dx.float().view(-1, d)
+        tok = torch.zeros(rt.tok_emb_g.shape, device=dx.device, dtype=torch.float32)
+        tok.index_add_(0, ids.reshape(-1), g)
+        pos = torch.zeros(rt.pos_emb_g.shape, device=dx.device, dtype=torch.float32)
+        pos.index_add_(0, positions.reshape(-1), g)
+        rt.tok_emb_g.copy_(tok)
+        rt.pos_emb_g.copy_(pos)
+        return None, None, None, None
+
+
+# ---------------------------------------------------------------------------
+# Model integration
+# ---------------------------------------------------------------------------
+
+def attach_device_runtime(model: TinyPRAModel) -> TinyPRAModel:
+    reason = unsupported_reason(model.cfg)
+    if reason is not None or not _ext.available():
+        return model
+    runtime = DeviceRuntime(model)
+    model._device_runtime = runtime
+    model.device_path_enabled = lambda: True
+    model.bf16_native = True
+
+    def build_optimizer(train_config):
+        return FusedAdamW(runtime.flat, train_config.learning_rate, train_config.weight_decay,
+                          max_grad_norm=train_config.max_grad_norm)
+
+    def optimizer_step_hook(optimizer, train_config):
+        if isinstance(optimizer, FusedAdamW):
+            optimizer.max_grad_norm = train_config.max_grad_norm
+            optimizer.step()
+            return float(optimizer.last_norm.item())
+        raise RuntimeError("device path expects the fused optimizer")
+
+    model.build_optimizer = build_optimizer
+    model.optimizer_step_hook = optimizer_step_hook
+    model.after_load_state = runtime.flat.refresh_shadow
+    original_load = model.load_state_dict
+
+    def load_state_dict(state, strict=True):
+        result = original_load(state, strict=strict)
+        runtime.flat.refresh_shadow()
+        return result
+
+    model.load_state_dict = load_state_dict
+    return model
 
 
 def prepare_model(cfg, device) -> TinyPRAModel:
-    """Build a model on ``device``; on CUDA it is wrapped for the bf16 device path."""
-    model = TinyPRAModel(cfg)
-    return model.to(device)
+    """A model on ``device``; on CUDA with a supported config it gets the device runtime."""
+    model = TinyPRAModel(cfg).to(device)
+    if str(device).startswith("cuda"):
+        if not _ext.available():
+            raise RuntimeError("CUDA device requested but the pra_ops extension is not built")
+        attach_device_runtime(model)
+    return model
 
 
-def device_batch_step(*args, **kwargs):
-    raise NotImplementedError
+def device_batch_step(model, batch, device, tokenizer, resolver_config, cache_config):
+    """Device version of the PRA batch step: batched cache build, one prompt forward, fused loss."""
+    rt: DeviceRuntime = model._device_runtime
+    metadata = batch["metadata"]
+    t0 = time.perf_counter()
+    try:
+        memory, caches, builders = rt.build_memory(metadata, tokenizer, resolver_config)
+    except _Unsupported:
+        model.device_path_enabled = lambda: False
+        from ..pra_train import _pra_batch_step
+
+        return _pra_batch_step(model, batch, device, tokenizer, resolver_config, cache_config)
+    build_s = time.perf_counter() - t0
+    ids = batch["input_ids"].to(device, non_blocking=True)
+    mask = batch["attention_mask"].to(device, non_blocking=True)
+    labels = batch["labels"].to(device, non_blocking=True)
+    hidden = rt.prompt_forward(ids, mask, memory if memory.chunks else None)
+    loss = rt.loss(hidden, labels)
+    tokens = int(batch["attention_mask"].sum())
+    b = ids.shape[0]
+    for cache, builder in zip(caches, builders):
+        cache.resolution_events = list(builder.events)
+        cache.dependencies = list(builder.dependencies)
+    metrics = {"cache_build_duration_seconds": build_s / max(b, 1), "cache_build_total_duration_seconds": build_s,
+               "logical_batch_size": float(b), "prompt_forward_calls": 1.0}
+    return loss, {"tokens": tokens, "examples": b, "batch": batch, "caches": caches, "metrics": metrics,
+                  "memory": memory, "hidden": hidden}
 
 
 def pra_attention_device(layer, x, attention_mask):
-    raise NotImplementedError
+    raise RuntimeError("per-layer device attention is driven by DeviceRuntime.run_blocks")
+
+
+# ---------------------------------------------------------------------------
+# Self-test of the routing kernel against the object path (used by the GPU tests)
+# ---------------------------------------------------------------------------
+
+def routing_selftest(device, seed: int = 0) -> None:
+    """Random namespaces routed on the device and through ``PRASimpleMemoryCache`` + budget."""
+    from ..config import PRAConfig
+    from ..memory.cache import (ChunkRoutingGist, LayerKV, LayerReferenceMemory, PRACacheEntry,
+                                PRASimpleMemoryCache, ReferenceChunkMemory)
+    from .attention import budget_selection
+
+    gen = torch.Generator().manual_seed(seed)
+    d, g_max = 64, 2
+    cfg = PRAConfig(d_model=d, n_heads=2, top_k_references=2, top_k_chunks_per_reference=3, trigger_threshold=-0.5,
+                    max_seq_len=400, gist_mode="kmeans", gists_per_chunk=g_max)
+    rows, entries, chunks = [], [], []
+    caches = []
+    for row in range(3):
+        cache = PRASimpleMemoryCache()
+        row_entries = []
+        for r in range(4 + row):
+            uri = f"mem://row{row}/doc{(r * 5) % 7}"
+            e = len(entries)
+            rec = EntryRecord(row, uri, "", {}, False, ())
+            entry = PRACacheEntry(uri=uri, text="")
+            mem = LayerReferenceMemory()
+            for c in range(1 + (r * 3 + row) % 12):
+                n = 10 + (c * 7) % 30
+                gist = torch.randn(1 + c % g_max, d, generator=gen)
+                ci = len(chunks)
+                chunks.append(ChunkRecord(row, e, uri, f"{uri}#chunk={c}", c * 40, c * 40 + n, tuple(range(n)),
+                                          seq=ci))
+                rec.chunks.append(ci)
+                kv = torch.zeros(1, 2, n, d // 2)
+                mem.chunks.append(ReferenceChunkMemory(f"{uri}#chunk={c}", uri, c * 40, c * 40 + n, LayerKV(kv, kv),
+                                                       ChunkRoutingGist(k=gist)))
+                chunks[ci].metadata["gist"] = gist
+            entry.layer_memory[0] = mem
+            cache.put(entry)
+            entries.append(rec)
+            row_entries.append(e)
+        caches.append(cache)
+        rows.append(row_entries)
+    seq_len = 64
+    ns = Namespace(rows, entries, chunks, device)
+    C = len(chunks)
+    gists = torch.zeros(C, g_max, d)
+    counts = torch.zeros(C, dtype=torch.int32)
+    for i, c in enumerate(chunks):
+        k = c.metadata["gist"]
+        gists[i, : k.shape[0]] = torch.nn.functional.normalize(k, dim=-1, eps=1e-12)
+        counts[i] = k.shape[0]
+    query = torch.randn(3, d, generator=gen)
+    t = 120
+    budget = cfg.effective_model_max_context_tokens - t
+    as_int = lambda x: torch.tensor(x, dtype=torch.int32, device=device)  # noqa: E731
+    mem_idx, ints, sel_i, sel_f = _ext.require().route(
+        query.bfloat16().to(device), gists.to(device), counts.to(device), ns.row_pos_off, ns.row_ref_off,
+        ns.ref_pos_off, ns.pos_chunk, ns.pos_ref, ns.pos_rank, as_int([c.token_start for c in chunks]),
+        as_int([len(c.token_ids) for c in chunks]), as_int([c.seq * seq_len for c in chunks]), cfg.top_k_references,
+        cfg.top_k_chunks_per_reference, 0, 0, float(cfg.trigger_threshold), budget, False, False, True, 16, budget)
+    mem_idx, ints, sel_i, sel_f = mem_idx.cpu(), ints.cpu(), sel_i.cpu(), sel_f.cpu()
+    q_bf = query.bfloat16().float()
+    for row in range(3):
+        hits = caches[row].search(q_bf[row:row + 1], 0, cfg)[0]
+        hits = [h for h in hits if h.chunk_score >= cfg.trigger_threshold]
+        kept, _ = budget_selection(hits, cfg, direct_tokens=t, routing_candidates=len(hits))
+        device_chunks = [chunks[int(c)].chunk_id for c in sel_i[0, row, : int(ints[1, row])]]
+        assert sorted(device_chunks) == sorted(h.chunk_id for h in kept), (row, device_chunks,
+                                                                           [h.chunk_id for h in kept])
+        expected_rows = []
+        for h in sorted(kept, key=lambda s: (s.reference_uri, s.token_start, s.chunk_id)):
+            ci = next(i for i, c in enumerate(chunks) if c.chunk_id == h.chunk_id and c.row == row)
+            expected_rows += [chunks[ci].seq * seq_len + j for j in range(len(chunks[ci].token_ids))]
+        got = mem_idx[row, : int(ints[0, row])].tolist()
+        assert got == expected_rows, (row, got[:10], expected_rows[:10])
+        for j, h in enumerate(sorted(kept, key=lambda s: (-s.chunk_score, s.reference_uri, s.chunk_id))):
+            assert math.isfinite(float(sel_f[1, row, j]))

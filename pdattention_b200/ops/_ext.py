@@ -1,0 +1,104 @@
+"""Build and load the in-tree sm_100a extension (``pra_ops``).
+
+``build()`` compiles every kernel translation unit for ``sm_100a`` with ninja
+(incremental, parallel) into ``pdattention_b200/ops/_build/`` and imports the
+result.  ``load()`` imports an already-built module without invoking the
+compiler, so a machine that received the built ``.so`` never recompiles.
+``require()`` is what the CUDA code paths call: it raises when the extension
+is missing instead of silently falling back to a slower path.
+"""
+
+from __future__ import annotations
+
+import importlib.machinery
+import importlib.util
+import os
+import sys
+import sysconfig
+from pathlib import Path
+
+NAME = "pra_ops"
+ROOT = Path(__file__).resolve().parents[2]
+CSRC = ROOT / "csrc"
+BUILD_DIR = Path(__file__).resolve().parent / "_build"
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+_SOURCES = ["bindings.cpp", "attention.cu", "norm.cu", "loss_optim.cu", "gist.cu", "routing.cu",
+            "gemm/tn_bias.cu", "gemm/tn_bias_gelu.cu", "gemm/nn.cu", "gemm/nn_dgelu.cu", "gemm/wgrad.cu"]
+
+_module = None
+
+
+def cutlass_include_dirs() -> list[str]:
+    """CUTLASS/CuTe header trees shipped inside site-packages (used with -I only)."""
+    site = Path(sysconfig.get_paths()["purelib"])
+    for base in (site / "flashinfer" / "data" / "cutlass", site / "tilelang" / "3rdparty" / "cutlass"):
+        if (base / "include" / "cutlass" / "cutlass.h").exists():
+            return [str(base / "include"), str(base / "tools" / "util" / "include")]
+    raise RuntimeError("CUTLASS headers not found (expected under flashinfer/data/cutlass)")
+
+
+def _so_path() -> Path | None:
+    suffix = importlib.machinery.EXTENSION_SUFFIXES
+    for candidate in BUILD_DIR.glob(f"{NAME}*.so"):
+        return candidate
+    del suffix
+    return None
+
+
+def build(verbose: bool = False):
+    """Compile (incrementally) and import the extension."""
+    global _module
+    from torch.utils import cpp_extension
+
+    BUILD_DIR.mkdir(parents=True, exist_ok=True)
+    os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0a")
+    os.environ.setdefault("MAX_JOBS", str(max(os.cpu_count() or 4, 4)))
+    cuda_flags = [*ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-DNDEBUG",
+                  "-diag-suppress", "20012,177,550", "-Xptxas", "-v" if verbose else "-O3"]
+    _module = cpp_extension.load(
+        name=NAME,
+        sources=[str(CSRC / s) for s in _SOURCES],
+        extra_include_paths=[str(CSRC), *cutlass_include_dirs()],
+        extra_cflags=["-O3", "-std=c++17"],
+        extra_cuda_cflags=cuda_flags,
+        extra_ldflags=["-lcuda"],
+        build_directory=str(BUILD_DIR),
+        verbose=verbose,
+    )
+    return _module
+
+
+def load():
+    """Import the built extension (no compilation); returns ``None`` when absent."""
+    global _module
+    if _module is not None:
+        return _module
+    if NAME in sys.modules:
+        _module = sys.modules[NAME]
+        return _module
+    so = _so_path()
+    if so is None:
+        return None
+    import torch  # noqa: F401  (the extension links against libtorch)
+
+    spec = importlib.util.spec_from_file_location(NAME, str(so))
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    sys.modules[NAME] = module
+    _module = module
+    return module
+
+
+def require():
+    """The extension, or a clear error: CUDA tensors never take a silent fallback."""
+    module = load()
+    if module is None:
+        raise RuntimeError(
+            "The pra_ops CUDA extension is not built. Run `python -c 'import __graft_entry__ as g; g.build()'` "
+            "(or pdattention_b200.ops._ext.build()) on a machine with nvcc before using CUDA tensors.")
+    return module
+
+
+def available() -> bool:
+    return load() is not None
