@@ -1,0 +1,341 @@
+"""TinyGPT-PRA training throughput (tokens/s) on one node, one rank per GPU.
+
+Workload (fixed per GPU, weak scaling): TinyGPT-PRA ~125M (12 PRA layers,
+d_model 768, 12 heads, native context 1024, GPT-2-size vocabulary 50257),
+bf16.  Each example's prompt holds 2 root references; each root names 1
+child, which names 6 leaves (16 references per example, depth-2 child-first
+recursion, 128 uniform-random tokens each), chunks of 64 tokens with 2 k-means
+gists per chunk; routing keeps 2 references x 2 chunks (256 memory tokens) next
+to a 768-token direct window.  Every step rebuilds every row's cache (the
+reference semantics), runs the routed forward, backward and AdamW.  Synthetic
+data, random-initialised weights.  Per-step working set (weights + activations)
+is far larger than the 126 MB L2, so no explicit flush is needed.
+
+``--impl reference`` runs the unmodified reference (installed in baseline/_ref)
+through its own batch step and optimizer code on the same data; with more than
+one rank its gradients are averaged with NCCL.
+
+Launch: ``python bench.py`` (1 GPU) or ``torchrun --nproc-per-node N bench.py --gpus N``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+PER_GPU_BATCH = 8
+VOCAB = 50257
+MODEL = dict(d_model=768, n_heads=12, n_layers=12, max_seq_len=1024, model_variant="td_pra", chunking_mode="fixed",
+             fixed_chunk_tokens=64, top_k_references=2, top_k_chunks_per_reference=2, gist_mode="kmeans",
+             gists_per_chunk=2, recursive_refs_enabled=True, recursive_max_depth=2, trigger_threshold=-1.0)
+# Written under the hierarchical stage name both frameworks' dataset registries know.
+STAGE = "stage1_hierarchical_synthetic"
+TREE = dict(roots=2, children=1, grandchildren=6, doc_tokens=128, prompt_tokens=767, vocab=VOCAB)
+
+
+def _env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = Path(tempfile.mkstemp(suffix=".csv")[1])
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.path.open("w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait(timeout=10)
+
+    def summary(self) -> dict:
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({name for r in rows for name, flag in zip(names, r[5:9]) if flag.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "samples": len(rows)}
+
+
+def _make_data(root: Path, examples: int, seed: int, tokenizer) -> None:
+    """Write the stage and register every reference handle it uses (fixes the vocabulary size)."""
+    from pdattention_b200.data.datasets import read_jsonl
+    from pdattention_b200.data.generators import generate_hierarchical_tokens
+
+    stage = generate_hierarchical_tokens(root / STAGE, examples=examples, seed=seed, **TREE)
+    for name in ("documents.jsonl", "questions.jsonl"):
+        for row in read_jsonl(stage / name):
+            tokenizer.encode(row.get("text") or row.get("prompt") or "")
+
+
+def _loader(module_cls, root: Path, tokenizer, rank: int, world: int):
+    kwargs = dict(batch_size=PER_GPU_BATCH, max_seq_len=MODEL["max_seq_len"], tokenizer=tokenizer, shuffle=False,
+                  pin_memory=torch.cuda.is_available())
+    if "rank" in module_cls.__init__.__code__.co_varnames:
+        kwargs.update(rank=rank, world_size=world)
+    return module_cls(STAGE, str(root), **kwargs).load()
+
+
+def _batches(dm, rank: int, world: int, count: int):
+    """``count`` batches of this rank's disjoint shard (cycled)."""
+    dataset = dm.dataset
+    per_rank = [dataset[i] for i in range(rank, len(dataset), world)]
+    out = []
+    i = 0
+    while len(out) < count:
+        rows = [per_rank[(i + j) % len(per_rank)] for j in range(PER_GPU_BATCH)]
+        batch = dm.collator(rows)
+        if torch.cuda.is_available():
+            for key in ("input_ids", "labels", "attention_mask"):
+                batch[key] = batch[key].pin_memory()
+        out.append(batch)
+        i += PER_GPU_BATCH
+    return out
+
+
+def _sync_all(world: int) -> None:
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier(device_ids=[torch.cuda.current_device()])
+        torch.cuda.synchronize()
+
+
+def _max(value: float, world: int) -> float:
+    if world <= 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run(impl: str, steps: int, warmup: int, gpus: int) -> dict:
+    rank, local, world = _env()
+    if gpus != world:
+        raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    from pdattention_b200.data import WordIdTokenizer
+
+    tmp = Path(tempfile.mkdtemp(prefix=f"pra_bench_{rank}_"))
+    total_steps = steps + warmup
+    tokenizer = WordIdTokenizer(VOCAB)
+    _make_data(tmp, examples=max(PER_GPU_BATCH * world * 2, 32), seed=0, tokenizer=tokenizer)
+    if impl == "reference":
+        step_fn, model_desc, counter = _reference_arm(tmp, tokenizer, rank, world)
+    else:
+        step_fn, model_desc, counter = _pra_arm(tmp, tokenizer, rank, world)
+    batches = step_fn.batches(total_steps)
+    tokens_per_step = [int(b["attention_mask"].sum()) for b in batches]
+
+    for i in range(warmup):
+        step_fn(batches[i])
+    _sync_all(world)
+    if counter is not None:
+        counter.reset()
+        counter.enabled = True
+    start_evt, end_evt = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h2d = d2h = 0
+    with ClockSampler(local) as clocks:
+        _sync_all(world)
+        wall0 = time.perf_counter()
+        start_evt.record()
+        for i in range(warmup, total_steps):
+            loss_host, moved, read = step_fn(batches[i])
+            h2d += moved
+            d2h += read
+        end_evt.record()
+        _sync_all(world)
+        wall = time.perf_counter() - wall0
+    if counter is not None:
+        counter.enabled = False
+    device_s = _max(start_evt.elapsed_time(end_evt) / 1000.0, world)
+    wall_s = _max(wall, world)
+    local_tokens = sum(tokens_per_step[warmup:])
+    total_tokens = local_tokens * world  # identical shards sizes on every rank
+    result = {
+        "metric": "PRA train tokens/s (TinyGPT-PRA ~125M, data parallel)",
+        "value": total_tokens / device_s,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": warmup,
+        "ms_per_step": 1000.0 * device_s / steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16" if impl != "reference" else "fp32",
+        "data": "synthetic (seeded uniform-random token ids, depth-2 recursive references), random-init weights",
+        "config": {"model": model_desc, "global_batch": PER_GPU_BATCH * world, "seq_len": MODEL["max_seq_len"],
+                   "direct_tokens_per_row": TREE["prompt_tokens"] + 1, "references_per_row": 16,
+                   "chunk_tokens": 64, "gists_per_chunk": 2, "parallelism": f"dp{world}",
+                   "l2": "per-step working set exceeds the 126 MB L2 (no flush)"},
+        "clocks": clocks.summary(),
+        "e2e": {"value": total_tokens / wall_s, "unit": "tokens/s", "h2d_bytes_per_step": h2d // max(steps, 1),
+                "d2h_bytes_per_step": d2h // max(steps, 1)},
+        "gpu_launches": (counter.launches if counter is not None else 0),
+        "last_loss": loss_host,
+    }
+    if impl == "reference":
+        result["impl"] = "reference"
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return result
+
+
+class _Step:
+    def __init__(self, fn, batch_source):
+        self.fn = fn
+        self.batches = batch_source
+
+    def __call__(self, batch):
+        return self.fn(batch)
+
+
+def _moved_bytes(batch) -> int:
+    return sum(batch[k].numel() * batch[k].element_size() for k in ("input_ids", "labels", "attention_mask"))
+
+
+def _pra_arm(root: Path, tokenizer, rank: int, world: int):
+    from pdattention_b200.config import PRAConfig, ResolverServiceConfig, TrainConfig
+    from pdattention_b200.data import PRADataModule
+    from pdattention_b200.models.fastpath import prepare_model
+    from pdattention_b200.ops._ext import launch_counter
+    from pdattention_b200.parallel.dp import attach_data_parallel
+    from pdattention_b200.pra_train import training_step
+
+    dm = _loader(PRADataModule, root, tokenizer, rank, world)
+    torch.manual_seed(0)
+    cfg = PRAConfig(vocab_size=tokenizer.vocab_size, device="cuda", **MODEL)
+    model = prepare_model(cfg, "cuda")
+    if getattr(model, "_device_runtime", None) is None:
+        raise RuntimeError("device path unavailable for the benchmark config")
+    model.train()
+    optimizer = model.build_optimizer(TrainConfig(device="cuda", learning_rate=3e-4))
+    attach_data_parallel(model, optimizer, world)
+    resolver = ResolverServiceConfig()
+
+    def step(batch):
+        dev_batch = dict(batch)
+        for key in ("input_ids", "labels", "attention_mask"):
+            dev_batch[key] = batch[key].to("cuda", non_blocking=True)
+        loss, _ = training_step(model, dev_batch, "cuda", tokenizer, optimizer, resolver_config=resolver)
+        value = float(loss.detach().float().item())
+        return value, _moved_bytes(batch), 4
+
+    params = sum(p.numel() for p in model.parameters())
+    return _Step(step, lambda n: _batches(dm, rank, world, n)), f"TinyGPT-PRA-{params / 1e6:.0f}M", launch_counter()
+
+
+def _reference_arm(root: Path, tokenizer, rank: int, world: int):
+    ref_root = REPO / "baseline" / "_ref"
+    if not (ref_root / "pra_torch").exists():
+        raise _Unavailable("reference not installed in baseline/_ref")
+    sys.path.append(str(ref_root))
+    from common.metrics import grad_norm as ref_grad_norm  # reference modules
+    from data.datamodules import PRADataModule as RefDataModule
+    from pra_torch.config import CacheServiceConfig, PRAConfig as RefConfig, ResolverServiceConfig
+    from pra_torch.model import TinyPRAModel as RefModel
+    from pra_torch.pra_train import _pra_batch_step as ref_batch_step
+
+    dm = _loader(RefDataModule, root, tokenizer, rank, world)
+    torch.manual_seed(0)
+    cfg = RefConfig(vocab_size=tokenizer.vocab_size, device="cuda", **MODEL)
+    model = RefModel(cfg).to("cuda").train()
+    optimizer = torch.optim.AdamW(model.parameters(), lr=3e-4, weight_decay=0.0)
+    resolver, cache = ResolverServiceConfig(), CacheServiceConfig()
+    params = [p for p in model.parameters()]
+
+    def step(batch):
+        optimizer.zero_grad(set_to_none=True)
+        loss, _ = ref_batch_step(model, batch, "cuda", tokenizer, resolver, cache)
+        loss.backward()
+        if world > 1:
+            import torch.distributed as dist
+
+            grads = [p.grad for p in params if p.grad is not None]
+            flat = torch.cat([g.reshape(-1) for g in grads])
+            dist.all_reduce(flat)
+            flat /= world
+            offset = 0
+            for g in grads:
+                g.copy_(flat[offset: offset + g.numel()].view_as(g))
+                offset += g.numel()
+        ref_grad_norm(model.parameters())
+        torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+        optimizer.step()
+        return float(loss.detach().cpu()), _moved_bytes(batch), 4
+
+    n = sum(p.numel() for p in model.parameters())
+    return _Step(step, lambda k: _batches(dm, rank, world, k)), f"TinyGPT-PRA-{n / 1e6:.0f}M (reference fp32)", None
+
+
+class _Unavailable(RuntimeError):
+    pass
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=10)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", choices=["pra", "reference"], default="pra")
+    args = parser.parse_args()
+    rank = _env()[0]
+    try:
+        result = run(args.impl, args.steps, max(args.warmup, 3), args.gpus)
+    except _Unavailable as exc:
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": str(exc)}))
+        return
+    if rank == 0:
+        print(json.dumps(result))
+
+
+if __name__ == "__main__":
+    main()

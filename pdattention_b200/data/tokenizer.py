@@ -74,6 +74,8 @@ class WordIdTokenizer:
     def __init__(self, base_vocab: int, reference_tokens: list[str] | None = None):
         self.base_vocab = int(base_vocab)
         self._refs: dict[str, int] = {}
+        self.stoi: dict[str, int] = {f"t{i}": i for i in range(self.base_vocab)}
+        self.itos: dict[int, str] = {i: f"t{i}" for i in range(self.base_vocab)}
         for token in reference_tokens or ["<REF_0>"]:
             self.register_reference_token(token)
 
@@ -81,20 +83,15 @@ class WordIdTokenizer:
         if not REF_TOKEN_PATTERN.fullmatch(token):
             raise ValueError(f"Invalid reference token: {token}")
         if token not in self._refs:
-            self._refs[token] = self.base_vocab + len(self._refs)
+            index = self.base_vocab + len(self._refs)
+            self._refs[token] = index
+            self.stoi[token] = index
+            self.itos[index] = token
         return self._refs[token]
 
     @property
     def vocab_size(self) -> int:
         return self.base_vocab + len(self._refs)
-
-    @property
-    def stoi(self) -> dict[str, int]:
-        return {**{f"t{i}": i for i in range(self.base_vocab)}, **self._refs}
-
-    @property
-    def itos(self) -> dict[int, str]:
-        return {v: k for k, v in self.stoi.items()}
 
     def encode(self, text: str) -> list[int]:
         out = []

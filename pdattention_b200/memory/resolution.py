@@ -69,6 +69,25 @@ def _fingerprint(value) -> str:
     return hashlib.sha256(json.dumps(value, sort_keys=True, default=str).encode("utf-8")).hexdigest()
 
 
+_VOCAB_FINGERPRINTS: dict[int, tuple[int, object, str]] = {}
+
+
+def tokenizer_fingerprint(tokenizer) -> str:
+    """sha256 of the vocabulary, memoised per tokenizer object and vocabulary size.
+
+    Hashing a large vocabulary on every resolve dominated cache-build time; the
+    value only changes when tokens are added, which changes the size.
+    """
+    stoi = getattr(tokenizer, "stoi", {})
+    key = id(tokenizer)
+    cached = _VOCAB_FINGERPRINTS.get(key)
+    if cached is not None and cached[0] == len(stoi) and cached[1] is tokenizer:
+        return cached[2]
+    value = _fingerprint(stoi)
+    _VOCAB_FINGERPRINTS[key] = (len(stoi), tokenizer, value)
+    return value
+
+
 _ROUTING_IDENTITY_KEYS = {
     "chunking_mode", "fixed_chunk_tokens", "fixed_chunk_overlap_tokens", "max_gists_per_reference", "use_summary",
     "summary_mode", "recursive_refs_enabled", "recursive_max_depth",
@@ -93,15 +112,20 @@ class RecursiveReferenceCacheBuilder:
         return ResolutionBudget(self.config.recursive_max_total_references, self.config.recursive_max_total_tokens)
 
     def _identity(self, resolved) -> dict:
-        routing = {k: v for k, v in asdict(self.config).items()
-                   if k.startswith(_ROUTING_IDENTITY_PREFIXES) or k in _ROUTING_IDENTITY_KEYS}
+        if getattr(self, "_static_identity", None) is None:
+            routing = {k: v for k, v in asdict(self.config).items()
+                       if k.startswith(_ROUTING_IDENTITY_PREFIXES) or k in _ROUTING_IDENTITY_KEYS}
+            self._static_identity = (
+                _fingerprint({"class": type(self.model).__name__, "d_model": self.config.d_model,
+                              "n_layers": self.config.n_layers, "n_heads": self.config.n_heads}),
+                _fingerprint(routing))
+        model_fp, routing_fp = self._static_identity
         return {
             "canonical_uri": resolved.uri,
             "content_fingerprint": _fingerprint({"text": resolved.text, "version": resolved.version}),
-            "model_fingerprint": _fingerprint({"class": type(self.model).__name__, "d_model": self.config.d_model,
-                                               "n_layers": self.config.n_layers, "n_heads": self.config.n_heads}),
-            "tokenizer_fingerprint": _fingerprint(getattr(self.tokenizer, "stoi", {})),
-            "routing_configuration_fingerprint": _fingerprint(routing),
+            "model_fingerprint": model_fp,
+            "tokenizer_fingerprint": tokenizer_fingerprint(self.tokenizer),
+            "routing_configuration_fingerprint": routing_fp,
         }
 
     def _missing(self, uri: str, depth: int, error: Exception):

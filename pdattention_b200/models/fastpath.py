@@ -159,6 +159,7 @@ class FusedAdamW(torch.optim.Optimizer):
         self.step_count = 0
         self.last_norm = None
         self.grad_source = None  # set by the data-parallel engine to its reduced fp32 buffer
+        self.grad_scale = 1.0    # 1/world when grad_source holds a sum over ranks
 
     def zero_grad(self, set_to_none: bool = True) -> None:
         for s in getattr(self.flat, "slots", ()):
@@ -169,12 +170,15 @@ class FusedAdamW(torch.optim.Optimizer):
         ext = _ext.require()
         group = self.param_groups[0]
         grads = self.grad_source if self.grad_source is not None else self.flat.grad
-        norm, coef = ext.grad_norm(grads, float(self.max_grad_norm))
+        # clip on the averaged gradient: ||sum / world|| = ||sum|| / world
+        norm, coef = ext.grad_norm(grads, float(self.max_grad_norm) / self.grad_scale)
         self.step_count += 1
         b1, b2 = group["betas"]
         ext.adamw(self.flat.master, self.flat.shadow, grads, self.flat.exp_avg, self.flat.exp_avg_sq,
                   float(group["lr"]), b1, b2, float(group["eps"]), float(group["weight_decay"]), self.step_count,
-                  coef, 1.0)
+                  coef, float(self.grad_scale))
+        if self.grad_scale != 1.0:
+            norm = norm * self.grad_scale
         self.last_norm = norm
         return None
 
@@ -763,7 +767,8 @@ def routing_selftest(device, seed: int = 0) -> None:
         query.bfloat16().to(device), gists.to(device), counts.to(device), ns.row_pos_off, ns.row_ref_off,
         ns.ref_pos_off, ns.pos_chunk, ns.pos_ref, ns.pos_rank, as_int([c.token_start for c in chunks]),
         as_int([len(c.token_ids) for c in chunks]), as_int([c.seq * seq_len for c in chunks]), cfg.top_k_references,
-        cfg.top_k_chunks_per_reference, 0, 0, float(cfg.trigger_threshold), budget, False, False, True, 16, budget)
+        cfg.top_k_chunks_per_reference, 0, 0, float(cfg.trigger_threshold), budget, False, False, True, 16, budget,
+        None)
     mem_idx, ints, sel_i, sel_f = mem_idx.cpu(), ints.cpu(), sel_i.cpu(), sel_f.cpu()
     q_bf = query.bfloat16().float()
     for row in range(3):

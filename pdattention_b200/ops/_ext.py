@@ -28,6 +28,41 @@ _SOURCES = ["bindings.cpp", "attention.cu", "norm.cu", "loss_optim.cu", "gist.cu
 
 _module = None
 
+# Kernels launched per extension call (used to report how many of this library's
+# kernels ran inside a timed region).
+KERNELS_PER_CALL = {"attention_fwd": 1, "attention_bwd": 3, "gemm": 1, "norm_fwd": 1, "norm_bwd": 3, "colsum": 2,
+                    "cross_entropy": 1, "grad_norm": 2, "adamw": 1, "gist_mean": 1, "gist_kmeans": 1, "route": 1}
+
+
+class LaunchCounter:
+    """Proxy around the extension that counts kernel launches while enabled."""
+
+    def __init__(self, module):
+        self._module = module
+        self.enabled = False
+        self.launches = 0
+        self.calls: dict[str, int] = {}
+
+    def __getattr__(self, name):
+        fn = getattr(self._module, name)
+        if not callable(fn):
+            return fn
+
+        def counted(*args, **kwargs):
+            if self.enabled:
+                self.launches += KERNELS_PER_CALL.get(name, 1)
+                self.calls[name] = self.calls.get(name, 0) + 1
+            return fn(*args, **kwargs)
+
+        return counted
+
+    def reset(self) -> None:
+        self.launches = 0
+        self.calls = {}
+
+
+_counter: LaunchCounter | None = None
+
 
 def cutlass_include_dirs() -> list[str]:
     """CUTLASS/CuTe header trees shipped inside site-packages (used with -I only)."""
@@ -92,12 +127,20 @@ def load():
 
 def require():
     """The extension, or a clear error: CUDA tensors never take a silent fallback."""
+    global _counter
+    if _counter is not None:
+        return _counter
     module = load()
     if module is None:
         raise RuntimeError(
             "The pra_ops CUDA extension is not built. Run `python -c 'import __graft_entry__ as g; g.build()'` "
             "(or pdattention_b200.ops._ext.build()) on a machine with nvcc before using CUDA tensors.")
-    return module
+    _counter = LaunchCounter(module)
+    return _counter
+
+
+def launch_counter() -> LaunchCounter:
+    return require()
 
 
 def available() -> bool:

@@ -412,4 +412,29 @@ def train_pra_model(*, cfg: PRAConfig, train_config: TrainConfig, datamodule, mo
                        batch_step=batch_step, eval_step=eval_step, state=state)
 
 
+def training_step(model, batch: dict, device: str, tokenizer, optimizer, *, resolver_config=None, cache_config=None,
+                  scheduler=None, max_grad_norm: float = 1.0) -> tuple[torch.Tensor, dict]:
+    """One optimizer step on one batch: cache build, routed forward, loss, backward, clip, update.
+
+    This is the unit the training engine repeats; it is public so drivers and
+    benchmarks run exactly the code path users get.  Returns ``(loss, info)``
+    with the loss still on the device (read it when needed).
+    """
+    resolver_config = ResolverServiceConfig.from_value(resolver_config)
+    cache_config = CacheServiceConfig.from_value(cache_config)
+    optimizer.zero_grad(set_to_none=True)
+    loss, info = _pra_batch_step(model, batch, device, tokenizer, resolver_config, cache_config)
+    loss.backward()
+    hook = getattr(model, "optimizer_step_hook", None)
+    if hook is not None:
+        hook(optimizer, type("Cfg", (), {"max_grad_norm": max_grad_norm})())
+    else:
+        if max_grad_norm:
+            torch.nn.utils.clip_grad_norm_(model.parameters(), max_grad_norm)
+        optimizer.step()
+    if scheduler is not None:
+        scheduler.step()
+    return loss, info
+
+
 from .ablation import evaluate_reference_ablation  # noqa: E402  (re-export, keeps the reference import path)
