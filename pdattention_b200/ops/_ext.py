@@ -24,7 +24,8 @@ BUILD_DIR = Path(__file__).resolve().parent / "_build"
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 _SOURCES = ["bindings.cpp", "attention.cu", "norm.cu", "loss_optim.cu", "gist.cu", "routing.cu",
-            "gemm/tn_bias.cu", "gemm/tn_bias_gelu.cu", "gemm/nn.cu", "gemm/nn_dgelu.cu", "gemm/wgrad.cu"]
+            "gemm/tn_bias.cu", "gemm/tn_bias_gelu.cu", "gemm/nn.cu", "gemm/nn_dgelu.cu", "gemm/wgrad.cu",
+            "colsum_noalloc.cu"]
 
 _module = None
 
