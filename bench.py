@@ -170,8 +170,11 @@ def run(impl: str, steps: int, warmup: int, gpus: int) -> dict:
     batches = step_fn.batches(total_steps)
     tokens_per_step = [int(b["attention_mask"].sum()) for b in batches]
 
+    def upcoming(i):
+        return batches[i + 1] if i + 1 < total_steps else None
+
     for i in range(warmup):
-        step_fn(batches[i])
+        step_fn(batches[i], upcoming(i))
     _sync_all(world)
     if counter is not None:
         counter.reset()
@@ -183,7 +186,7 @@ def run(impl: str, steps: int, warmup: int, gpus: int) -> dict:
         wall0 = time.perf_counter()
         start_evt.record()
         for i in range(warmup, total_steps):
-            loss_host, moved, read = step_fn(batches[i])
+            loss_host, moved, read = step_fn(batches[i], upcoming(i))
             h2d += moved
             d2h += read
         end_evt.record()
@@ -233,8 +236,8 @@ class _Step:
         self.fn = fn
         self.batches = batch_source
 
-    def __call__(self, batch):
-        return self.fn(batch)
+    def __call__(self, batch, next_batch=None):
+        return self.fn(batch, next_batch)
 
 
 def _moved_bytes(batch) -> int:
@@ -260,11 +263,12 @@ def _pra_arm(root: Path, tokenizer, rank: int, world: int):
     attach_data_parallel(model, optimizer, world)
     resolver = ResolverServiceConfig()
 
-    def step(batch):
+    def step(batch, next_batch=None):
         dev_batch = dict(batch)
         for key in ("input_ids", "labels", "attention_mask"):
             dev_batch[key] = batch[key].to("cuda", non_blocking=True)
-        loss, _ = training_step(model, dev_batch, "cuda", tokenizer, optimizer, resolver_config=resolver)
+        loss, _ = training_step(model, dev_batch, "cuda", tokenizer, optimizer, resolver_config=resolver,
+                                next_batch=next_batch)
         value = float(loss.detach().float().item())
         return value, _moved_bytes(batch), 4
 
@@ -291,7 +295,7 @@ def _reference_arm(root: Path, tokenizer, rank: int, world: int):
     resolver, cache = ResolverServiceConfig(), CacheServiceConfig()
     params = [p for p in model.parameters()]
 
-    def step(batch):
+    def step(batch, next_batch=None):
         optimizer.zero_grad(set_to_none=True)
         loss, _ = ref_batch_step(model, batch, "cuda", tokenizer, resolver, cache)
         loss.backward()

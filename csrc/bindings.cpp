@@ -282,40 +282,112 @@ void adamw(torch::Tensor param, c10::optional<torch::Tensor> shadow, torch::Tens
 }
 
 // ---------------------------------------------------------------- gists
+// pool_k / pool_v: [L, R, D] (or [R, D]) bf16 views with unit feature stride.
+GistArgs gist_args(const torch::Tensor& pool_k, const torch::Tensor& pool_v, const torch::Tensor& start,
+                   const torch::Tensor& len, const c10::optional<torch::Tensor>& dest, const torch::Tensor& gk,
+                   const torch::Tensor& gv, const torch::Tensor& gn, const torch::Tensor& count, int64_t nmax) {
+  expect(pool_k, at::kBFloat16, "pool_k");
+  expect(pool_v, at::kBFloat16, "pool_v");
+  expect(gk, at::kFloat, "gk");
+  expect(count, at::kInt, "count");
+  const bool layered = pool_k.dim() == 3;
+  TORCH_CHECK(pool_k.dim() == pool_v.dim() && (layered || pool_k.dim() == 2), "pools must be [L, R, D] or [R, D]");
+  const int r = layered ? 1 : 0;
+  TORCH_CHECK(pool_k.stride(r + 1) == 1 && pool_v.stride(r + 1) == 1 && pool_k.stride(r) == pool_v.stride(r) &&
+                  (!layered || pool_k.stride(0) == pool_v.stride(0)),
+              "pools must share row and layer strides");
+  TORCH_CHECK(gk.dim() == 4 && gk.is_contiguous() && gv.is_contiguous() && gn.is_contiguous() &&
+                  gv.sizes() == gk.sizes() && gn.sizes() == gk.sizes(),
+              "gist tables must be contiguous [L, S, G, D]");
+  TORCH_CHECK(count.dim() == 2 && count.is_contiguous() && count.size(0) == gk.size(0) && count.size(1) == gk.size(1),
+              "count must be [L, S]");
+  TORCH_CHECK(start.scalar_type() == at::kInt && len.scalar_type() == at::kInt, "start/len must be int32");
+  GistArgs a{};
+  a.pk = ptr<const __nv_bfloat16>(pool_k);
+  a.pv = ptr<const __nv_bfloat16>(pool_v);
+  a.row_stride = pool_k.stride(r);
+  a.layer_stride = layered ? pool_k.stride(0) : 0;
+  a.start = ptr<const int>(start);
+  a.len = ptr<const int>(len);
+  a.dest = optr<int>(dest);
+  a.C = start.numel();
+  a.D = pool_k.size(r + 1);
+  a.G = gk.size(2);
+  a.nmax = (int)nmax;
+  TORCH_CHECK(gk.size(3) == a.D, "gist width must equal the pool width");
+  TORCH_CHECK(gk.size(0) == (layered ? pool_k.size(0) : 1), "gist tables need one entry per pool layer");
+  a.gk = ptr<float>(gk);
+  a.gv = ptr<float>(gv);
+  a.gn = ptr<float>(gn);
+  a.out_layer_stride = gk.stride(0);
+  a.count = ptr<int>(count);
+  a.count_layer_stride = count.stride(0);
+  return a;
+}
+
+void gist_mean_into(torch::Tensor pool_k, torch::Tensor pool_v, torch::Tensor start, torch::Tensor len,
+                    c10::optional<torch::Tensor> dest, torch::Tensor gk, torch::Tensor gv, torch::Tensor gn,
+                    torch::Tensor count) {
+  c10::cuda::CUDAGuard guard(pool_k.device());
+  GistArgs a = gist_args(pool_k, pool_v, start, len, dest, gk, gv, gn, count, 1);
+  check(pra_gist_mean(a, gk.size(0), stream()), "gist_mean_into");
+}
+
+// Returns (iterations [L, C], status [L, C]).
+std::vector<torch::Tensor> gist_kmeans_into(torch::Tensor pool_k, torch::Tensor pool_v, torch::Tensor start,
+                                            torch::Tensor len, c10::optional<torch::Tensor> dest, torch::Tensor gk,
+                                            torch::Tensor gv, torch::Tensor gn, torch::Tensor count, int64_t nmax,
+                                            int64_t max_iters, double tol, bool normalize, bool kmeanspp,
+                                            bool farthest, torch::Tensor init_first, torch::Tensor init_idx,
+                                            torch::Tensor exp_draws, torch::Tensor exp_off,
+                                            c10::optional<torch::Tensor> occupancy) {
+  c10::cuda::CUDAGuard guard(pool_k.device());
+  GistArgs a = gist_args(pool_k, pool_v, start, len, dest, gk, gv, gn, count, nmax);
+  const int64_t L = gk.size(0);
+  auto io = pool_k.options().dtype(at::kInt);
+  auto iters = torch::empty({L, (int64_t)a.C}, io), status = torch::empty({L, (int64_t)a.C}, io);
+  a.max_iters = (int)max_iters;
+  a.tol = (float)tol;
+  a.normalize = normalize;
+  a.kmeanspp = kmeanspp;
+  a.farthest = farthest;
+  a.init_first = ptr<const int>(init_first);
+  a.init_idx = ptr<const int>(init_idx);
+  a.exp_draws = ptr<const float>(exp_draws);
+  TORCH_CHECK(exp_off.scalar_type() == at::kInt && init_first.scalar_type() == at::kInt, "k-means offsets must be int32");
+  a.exp_off = ptr<const int>(exp_off);
+  a.occupancy = occupancy.has_value() ? ptr<int>(*occupancy) : nullptr;
+  a.iterations = ptr<int>(iters);
+  a.status = ptr<int>(status);
+  check(pra_gist_kmeans(a, L, stream()), "gist_kmeans_into");
+  return {iters, status};
+}
+
+// Allocating single-layer forms: outputs are indexed by chunk.
 std::vector<torch::Tensor> gist_mean(torch::Tensor pool_k, torch::Tensor pool_v, torch::Tensor start,
                                      torch::Tensor len) {
-  c10::cuda::CUDAGuard guard(pool_k.device());
-  expect(pool_k, at::kBFloat16, "pool_k");
-  TORCH_CHECK(pool_k.stride(1) == 1 && pool_v.stride(0) == pool_k.stride(0), "pools must be row-major");
-  const int C = start.numel(), D = pool_k.size(1);
+  const int64_t C = start.numel(), D = pool_k.size(-1);
   auto opts = pool_k.options().dtype(at::kFloat);
-  auto gk = torch::empty({C, D}, opts), gv = torch::empty({C, D}, opts), gn = torch::empty({C, D}, opts);
-  check(pra_gist_mean(ptr<const __nv_bfloat16>(pool_k), ptr<const __nv_bfloat16>(pool_v), pool_k.stride(0),
-                      ptr<const int>(start), ptr<const int>(len), C, D, ptr<float>(gk), ptr<float>(gv),
-                      ptr<float>(gn), stream()),
-        "gist_mean");
-  return {gk, gv, gn};
+  auto gk = torch::empty({1, C, 1, D}, opts), gv = torch::empty({1, C, 1, D}, opts), gn = torch::empty({1, C, 1, D}, opts);
+  auto count = torch::empty({1, C}, pool_k.options().dtype(at::kInt));
+  gist_mean_into(pool_k, pool_v, start, len, c10::nullopt, gk, gv, gn, count);
+  return {gk.view({C, D}), gv.view({C, D}), gn.view({C, D})};
 }
 
 std::vector<torch::Tensor> gist_kmeans(torch::Tensor pool_k, torch::Tensor pool_v, torch::Tensor start,
                                        torch::Tensor len, int64_t G, int64_t max_iters, double tol, bool normalize,
                                        bool kmeanspp, bool farthest, torch::Tensor init_first, torch::Tensor init_idx,
                                        torch::Tensor exp_draws, torch::Tensor exp_off) {
-  c10::cuda::CUDAGuard guard(pool_k.device());
-  expect(pool_k, at::kBFloat16, "pool_k");
-  const int C = start.numel(), D = pool_k.size(1);
+  const int64_t C = start.numel(), D = pool_k.size(-1);
   auto fo = pool_k.options().dtype(at::kFloat);
   auto io = pool_k.options().dtype(at::kInt);
-  auto gk = torch::zeros({C, G, D}, fo), gv = torch::zeros({C, G, D}, fo);
-  auto count = torch::empty({C}, io), occ = torch::zeros({C, G}, io), iters = torch::empty({C}, io),
-       status = torch::empty({C}, io);
-  check(pra_gist_kmeans(ptr<const __nv_bfloat16>(pool_k), ptr<const __nv_bfloat16>(pool_v), pool_k.stride(0),
-                        ptr<const int>(start), ptr<const int>(len), C, D, (int)G, (int)max_iters, (float)tol, normalize,
-                        kmeanspp, farthest, ptr<const int>(init_first), ptr<const int>(init_idx),
-                        ptr<const float>(exp_draws), ptr<const int64_t>(exp_off), ptr<float>(gk), ptr<float>(gv),
-                        ptr<int>(count), ptr<int>(occ), ptr<int>(iters), ptr<int>(status), stream()),
-        "gist_kmeans");
-  return {gk, gv, count, occ, iters, status};
+  auto gk = torch::zeros({1, C, G, D}, fo), gv = torch::zeros({1, C, G, D}, fo), gn = torch::zeros({1, C, G, D}, fo);
+  auto count = torch::empty({1, C}, io), occ = torch::zeros({1, C, G}, io);
+  const int64_t nmax = C ? len.max().item<int>() : 1;
+  auto out = gist_kmeans_into(pool_k, pool_v, start, len, c10::nullopt, gk, gv, gn, count, std::max<int64_t>(nmax, 1),
+                              max_iters, tol, normalize, kmeanspp, farthest, init_first, init_idx, exp_draws, exp_off,
+                              occ);
+  return {gk[0], gv[0], count[0], occ[0], out[0][0], out[1][0]};
 }
 
 // ---------------------------------------------------------------- routing
@@ -363,10 +435,13 @@ std::vector<torch::Tensor> route(torch::Tensor query, torch::Tensor gists, torch
   p.max_mem = max_mem;
   auto io = query.options().dtype(at::kInt);
   auto fo = query.options().dtype(at::kFloat);
-  auto mem_idx = torch::zeros({p.B, std::max<int64_t>(max_mem, 1)}, io);
-  auto ints = torch::zeros({8, p.B}, io);  // mem_len, sel_count, candidates, duplicates, status
-  auto sel_i = torch::full({4, p.B, std::max<int64_t>(max_sel, 1)}, -1, io);
-  auto sel_f = torch::zeros({3, p.B, std::max<int64_t>(max_sel, 1)}, fo);
+  // the kernel writes every slot of ints and the trace tables; mem_idx is valid up to mem_len
+  auto mem_idx = torch::empty({p.B, std::max<int64_t>(max_mem, 1)}, io);
+  auto ints = torch::empty({5, p.B}, io);  // mem_len, sel_count, candidates, duplicates, status
+  auto sel_i = torch::empty({4, p.B, std::max<int64_t>(max_sel, 1)}, io);
+  auto sel_f = torch::empty({3, p.B, std::max<int64_t>(max_sel, 1)}, fo);
+  p.max_sel = std::max<int64_t>(max_sel, 1);
+  p.max_mem = std::max<int64_t>(max_mem, 1);
   p.mem_idx = ptr<int>(mem_idx);
   p.mem_len = ptr<int>(ints);
   p.sel_count = p.mem_len + p.B;
@@ -400,5 +475,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw", &adamw);
   m.def("gist_mean", &gist_mean);
   m.def("gist_kmeans", &gist_kmeans);
+  m.def("gist_mean_into", &gist_mean_into);
+  m.def("gist_kmeans_into", &gist_kmeans_into);
   m.def("route", &route);
 }

@@ -1,173 +1,300 @@
 // Chunk routing-gist construction on the device (cache build hot op).
 //
-// mean:   gist_k[c] = mean of the chunk's K rows, gist_v[c] = mean of its V rows,
-//         gist_n[c] = gist_k[c] / max(||gist_k[c]||, 1e-12)   (routing copy).
-// kmeans: one CTA per chunk: Lloyd in (optionally L2-normalised) key space,
-//         kmeans++ or sampled initialisation driven by a precomputed random
-//         stream (the draws a seeded CPU generator would make), farthest-point
-//         reseed of empty clusters, then key / value gists as the means of the
-//         original rows over the same assignments (occupied clusters only).
-// K/V rows live in a token pool [tokens, D] (bf16); chunk c owns rows
-// [start[c], start[c] + len[c]).
+// Both kernels run one CTA per (chunk, layer): grid (C, L).  Layer l's K/V
+// rows live in a token pool at pk + l * layer_stride (bf16, row stride
+// `row_stride`); chunk c owns rows [start[c], start[c] + len[c]).  Results are
+// written straight into the cache's per-layer gist tables at chunk slot
+// dest[c] (identity when dest is null):
+//   gk/gv/gn  [L, S, G, D] fp32   key gist, value gist, routing copy (gk / ||gk||)
+//   count     [L, S]       int    occupied gist slots of the chunk
+//
+// mean:   gk = mean of the chunk's K rows, gv = mean of its V rows, one slot.
+// kmeans: Lloyd in (optionally L2-normalised) key space with kmeans++ or sampled
+//         initialisation driven by a precomputed random stream (the draws a
+//         seeded CPU generator would make), farthest-point reseed of empty
+//         clusters, then key / value gists as the means of the original rows
+//         over the final assignment (occupied clusters only, in cluster order).
+//         The chunk's keys are staged once in shared memory (bf16) when they
+//         fit, so every Lloyd iteration reads on-chip data; each thread owns a
+//         4-column slice of the feature dimension and accumulates all clusters
+//         for it in registers (no atomics, no per-cluster passes).
+// Semantics follow pra_torch/gists/strategies.py (kmeans_gists) and
+// pra_torch/gists/common.py (assignment + paired means).
 #include "common.cuh"
 
 namespace pra {
 namespace gist {
 
 constexpr int NT = 256;
+constexpr int NWARPS = NT / 32;
+constexpr int MAXG = 8;
+constexpr int MAXN = 1024;
 constexpr float EPS = 1e-12f;
 
-__global__ void __launch_bounds__(NT) mean_kernel(const __nv_bfloat16* __restrict__ pk, const __nv_bfloat16* __restrict__ pv,
-                                                  int64_t row_stride, const int* __restrict__ start,
-                                                  const int* __restrict__ len, int D, float* __restrict__ gk,
-                                                  float* __restrict__ gv, float* __restrict__ gn) {
-  __shared__ float scratch[32];
-  const int c = blockIdx.x;
-  const int s = start[c], n = len[c];
-  const float inv_n = n > 0 ? 1.f / n : 0.f;
-  float sq = 0.f;
-  for (int d = threadIdx.x; d < D; d += NT) {
-    float ak = 0.f, av = 0.f;
-    for (int i = 0; i < n; ++i) {
-      ak += __bfloat162float(pk[(int64_t)(s + i) * row_stride + d]);
-      av += __bfloat162float(pv[(int64_t)(s + i) * row_stride + d]);
-    }
-    ak *= inv_n;
-    av *= inv_n;
-    gk[(int64_t)c * D + d] = ak;
-    gv[(int64_t)c * D + d] = av;
-    sq += ak * ak;
-  }
-  const float inv = 1.f / fmaxf(sqrtf(block_sum(sq, scratch)), EPS);
-  for (int d = threadIdx.x; d < D; d += NT) gn[(int64_t)c * D + d] = gk[(int64_t)c * D + d] * inv;
-}
-
-struct KMeansArgs {
-  const __nv_bfloat16* pk;
-  const __nv_bfloat16* pv;
-  int64_t row_stride;
-  const int* start;
-  const int* len;
-  int D, G, max_iters;
-  float tol;
-  bool normalize, kmeanspp, farthest;
-  const int* init_first;      // [C] kmeans++ first index, or offset into init_idx for sampled init
-  const int* init_idx;        // flat sampled indices
-  const float* exp_draws;     // flat Exp(1) draws
-  const int64_t* exp_off;     // [C] offset of this chunk's [G-1, N] draws
-  float* gk;                  // [C, G, D]
-  float* gv;                  // [C, G, D]
-  int* count;                 // [C] occupied clusters
-  int* occupancy;             // [C, G]
-  int* iterations;            // [C]
-  int* status;                // [C] 0 ok, 1 empty-cluster error
+struct Quad {
+  float x, y, z, w;
 };
 
-constexpr int MAXN = 1024;
-constexpr int MAXG = 8;
-
-// squared distance from (optionally normalised) point i to each of `nc` centres.
-__device__ void point_dists(const KMeansArgs& a, int s, int i, const float* inv_norm, const float* centers, int nc,
-                            float* out) {
-  const int lane = threadIdx.x & 31;
-  float acc[MAXG];
-#pragma unroll
-  for (int c = 0; c < MAXG; ++c) acc[c] = 0.f;
-  const float sc = a.normalize ? inv_norm[i] : 1.f;
-  for (int d = lane; d < a.D; d += 32) {
-    const float w = __bfloat162float(a.pk[(int64_t)(s + i) * a.row_stride + d]) * sc;
-#pragma unroll
-    for (int c = 0; c < MAXG; ++c) {
-      if (c < nc) {
-        const float diff = w - centers[c * a.D + d];
-        acc[c] += diff * diff;
-      }
-    }
-  }
-#pragma unroll
-  for (int c = 0; c < MAXG; ++c) {
-    if (c < nc) {
-      const float v = warp_sum(acc[c]);
-      if (lane == 0) out[c] = v;
-    }
-  }
+__device__ __forceinline__ Quad load_quad(const __nv_bfloat16* p) {
+  const uint2 raw = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+  return {a.x, a.y, b.x, b.y};
 }
 
-__global__ void __launch_bounds__(NT) kmeans_kernel(KMeansArgs a) {
-  extern __shared__ __align__(16) float sm[];
-  float* centers = sm;                       // [G, D]
-  float* next = centers + a.G * a.D;         // [G, D]
-  float* inv_norm = next + a.G * a.D;        // [MAXN]
-  float* dmin = inv_norm + MAXN;             // [MAXN]
-  float* dist = dmin + MAXN;                 // [MAXN, MAXG]
-  int* assign = reinterpret_cast<int*>(dist + MAXN * MAXG);  // [MAXN]
-  __shared__ int members[MAXG];
-  __shared__ int chosen[MAXG];
-  __shared__ float scratch[32];
-  __shared__ int pick;
+__device__ __forceinline__ int dest_of(const GistArgs& a, int c) { return a.dest ? a.dest[c] : c; }
 
-  const int c = blockIdx.x;
-  const int s = a.start[c], n = min(a.len[c], MAXN);
-  const int G = min(a.G, n);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = NT / 32;
-  const int D = a.D;
-  if (threadIdx.x == 0) a.status[c] = 0;
-  if (G == 0) {
-    if (threadIdx.x == 0) {
-      a.count[c] = 0;
-      a.iterations[c] = 0;
-    }
-    return;
-  }
-  // row norms of the keys (normalised working space)
-  for (int i = warp; i < n; i += nwarps) {
-    float acc = 0.f;
-    for (int d = lane; d < D; d += 32) {
-      const float v = __bfloat162float(a.pk[(int64_t)(s + i) * a.row_stride + d]);
-      acc += v * v;
-    }
-    acc = warp_sum(acc);
-    if (lane == 0) inv_norm[i] = 1.f / fmaxf(sqrtf(acc), EPS);
+// Sums v[0..G) over the block in place (all threads see the totals).  red holds NWARPS * MAXG floats.
+__device__ __forceinline__ void block_sum_vec(float* v, int G, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int q = 0; q < MAXG; ++q)
+    if (q < G) v[q] = warp_sum(v[q]);
+  __syncthreads();
+  if (lane == 0) {
+#pragma unroll
+    for (int q = 0; q < MAXG; ++q)
+      if (q < G) red[warp * MAXG + q] = v[q];
   }
   __syncthreads();
-  auto work = [&](int i, int d) {
-    const float v = __bfloat162float(a.pk[(int64_t)(s + i) * a.row_stride + d]);
-    return a.normalize ? v * inv_norm[i] : v;
+#pragma unroll
+  for (int q = 0; q < MAXG; ++q) {
+    if (q < G) {
+      float s = 0.f;
+      for (int w = 0; w < NWARPS; ++w) s += red[w * MAXG + q];
+      v[q] = s;
+    }
+  }
+  __syncthreads();
+}
+
+// Block argmax with the lowest index winning ties; returns the index (-1 if every value is -inf).
+__device__ __forceinline__ int block_argmax(float v, int i, float* rv, int* ri) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (ov > v || (ov == v && oi >= 0 && (i < 0 || oi < i))) {
+      v = ov;
+      i = oi;
+    }
+  }
+  __syncthreads();
+  if (lane == 0) {
+    rv[warp] = v;
+    ri[warp] = i;
+  }
+  __syncthreads();
+  float bv = rv[0];
+  int bi = ri[0];
+  for (int w = 1; w < NWARPS; ++w) {
+    if (rv[w] > bv || (rv[w] == bv && ri[w] >= 0 && (bi < 0 || ri[w] < bi))) {
+      bv = rv[w];
+      bi = ri[w];
+    }
+  }
+  __syncthreads();
+  return bi;
+}
+
+// ---------------------------------------------------------------- mean
+__global__ void __launch_bounds__(NT) mean_kernel(GistArgs a) {
+  __shared__ float red[NWARPS * MAXG];
+  const int c = blockIdx.x, layer = blockIdx.y;
+  const int s = a.start[c], n = a.len[c];
+  const int D = a.D, D4 = D / 4;
+  const __nv_bfloat16* pk = a.pk + layer * a.layer_stride + (int64_t)s * a.row_stride;
+  const __nv_bfloat16* pv = a.pv + layer * a.layer_stride + (int64_t)s * a.row_stride;
+  const int64_t out = layer * a.out_layer_stride + (int64_t)dest_of(a, c) * a.G * D;
+  const float inv_n = n > 0 ? 1.f / n : 0.f;
+  float sq[1] = {0.f};
+  for (int j = threadIdx.x; j < D4; j += NT) {
+    Quad k{0.f, 0.f, 0.f, 0.f}, v{0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int i = 0; i < n; ++i) {
+      const Quad kk = load_quad(pk + (int64_t)i * a.row_stride + 4 * j);
+      const Quad vv = load_quad(pv + (int64_t)i * a.row_stride + 4 * j);
+      k.x += kk.x; k.y += kk.y; k.z += kk.z; k.w += kk.w;
+      v.x += vv.x; v.y += vv.y; v.z += vv.z; v.w += vv.w;
+    }
+    k = {k.x * inv_n, k.y * inv_n, k.z * inv_n, k.w * inv_n};
+    v = {v.x * inv_n, v.y * inv_n, v.z * inv_n, v.w * inv_n};
+    *reinterpret_cast<float4*>(a.gk + out + 4 * j) = make_float4(k.x, k.y, k.z, k.w);
+    *reinterpret_cast<float4*>(a.gv + out + 4 * j) = make_float4(v.x, v.y, v.z, v.w);
+    sq[0] += k.x * k.x + k.y * k.y + k.z * k.z + k.w * k.w;
+  }
+  block_sum_vec(sq, 1, red);
+  const float inv = 1.f / fmaxf(sqrtf(sq[0]), EPS);
+  for (int j = threadIdx.x; j < D4; j += NT) {
+    const float4 k = *reinterpret_cast<const float4*>(a.gk + out + 4 * j);
+    *reinterpret_cast<float4*>(a.gn + out + 4 * j) = make_float4(k.x * inv, k.y * inv, k.z * inv, k.w * inv);
+  }
+  if (threadIdx.x == 0) a.count[layer * a.count_layer_stride + dest_of(a, c)] = n > 0 ? 1 : 0;
+}
+
+// ---------------------------------------------------------------- kmeans
+template <bool STAGED>
+__global__ void __launch_bounds__(NT) kmeans_kernel(GistArgs a) {
+  extern __shared__ __align__(16) float sm[];
+  const int D = a.D, D4 = D / 4, nmax = a.nmax;
+  float* centers = sm;                                    // [G, D]
+  float* inv_norm = centers + a.G * D;                    // [nmax]
+  float* dmin = inv_norm + nmax;                          // [nmax]
+  float* dist = dmin + nmax;                              // [nmax, MAXG]
+  int* assign = reinterpret_cast<int*>(dist + nmax * MAXG);  // [nmax]
+  __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(assign + nmax);  // [nmax, D] when STAGED
+  __shared__ int members[MAXG];
+  __shared__ int chosen[MAXG];
+  __shared__ int slot_of[MAXG];
+  __shared__ float red[NWARPS * MAXG];
+  __shared__ float rv[NWARPS];
+  __shared__ int ri[NWARPS];
+  __shared__ int pick;
+  __shared__ int stop;
+
+  const int c = blockIdx.x, layer = blockIdx.y;
+  const int s = a.start[c], n = min(a.len[c], nmax);
+  const int G = min(a.G, n);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int dst = dest_of(a, c);
+  const int64_t status_at = (int64_t)layer * a.C + c;
+  const __nv_bfloat16* gkey = a.pk + layer * a.layer_stride + (int64_t)s * a.row_stride;
+  const __nv_bfloat16* gval = a.pv + layer * a.layer_stride + (int64_t)s * a.row_stride;
+  const int64_t out = layer * a.out_layer_stride + (int64_t)dst * a.G * D;
+  if (threadIdx.x == 0) {
+    if (a.status) a.status[status_at] = a.len[c] > nmax ? 2 : 0;
+    a.count[layer * a.count_layer_stride + dst] = 0;
+    if (a.iterations) a.iterations[status_at] = 0;
+  }
+  if (G == 0) return;
+
+  // Keys: staged copy (row stride D) or the pool itself.
+  const __nv_bfloat16* keys = gkey;
+  int64_t kstride = a.row_stride;
+  if constexpr (STAGED) {
+    for (int e = threadIdx.x; e < n * D4; e += NT) {
+      const int i = e / D4, j = e - i * D4;
+      *reinterpret_cast<uint2*>(stage + (int64_t)i * D + 4 * j) =
+          *reinterpret_cast<const uint2*>(gkey + (int64_t)i * a.row_stride + 4 * j);
+    }
+    keys = stage;
+    kstride = D;
+    __syncthreads();
+  }
+  // Row norms (working space is the normalised keys when requested).
+  for (int i = warp; i < n; i += NWARPS) {
+    float acc = 0.f;
+    for (int j = lane; j < D4; j += 32) {
+      const Quad k = load_quad(keys + (int64_t)i * kstride + 4 * j);
+      acc += k.x * k.x + k.y * k.y + k.z * k.z + k.w * k.w;
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) inv_norm[i] = a.normalize ? 1.f / fmaxf(sqrtf(acc), EPS) : 1.f;
+  }
+  __syncthreads();
+
+  auto set_center = [&](int q, int i) {
+    for (int j = threadIdx.x; j < D4; j += NT) {
+      const Quad k = load_quad(keys + (int64_t)i * kstride + 4 * j);
+      const float sc = inv_norm[i];
+      *reinterpret_cast<float4*>(centers + q * D + 4 * j) = make_float4(k.x * sc, k.y * sc, k.z * sc, k.w * sc);
+    }
   };
+  // Squared distances from every point to centres [0, nc): warp per point.
+  auto distances = [&](int nc) {
+    for (int i = warp; i < n; i += NWARPS) {
+      float acc[MAXG];
+#pragma unroll
+      for (int q = 0; q < MAXG; ++q) acc[q] = 0.f;
+      const float sc = inv_norm[i];
+      for (int j = lane; j < D4; j += 32) {
+        const Quad k = load_quad(keys + (int64_t)i * kstride + 4 * j);
+        const float wx = k.x * sc, wy = k.y * sc, wz = k.z * sc, ww = k.w * sc;
+#pragma unroll
+        for (int q = 0; q < MAXG; ++q) {
+          if (q < nc) {
+            const float4 cc = *reinterpret_cast<const float4*>(centers + q * D + 4 * j);
+            const float dx = wx - cc.x, dy = wy - cc.y, dz = wz - cc.z, dw = ww - cc.w;
+            acc[q] += dx * dx + dy * dy + dz * dz + dw * dw;
+          }
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < MAXG; ++q) {
+        if (q < nc) {
+          const float v = warp_sum(acc[q]);
+          if (lane == 0) dist[i * MAXG + q] = v;
+        }
+      }
+    }
+    __syncthreads();
+  };
+  // Nearest centre per point (first minimum), member counts, farthest point.
+  auto assign_points = [&](bool want_far) {
+    if (threadIdx.x < MAXG) members[threadIdx.x] = 0;
+    __syncthreads();
+    float far_v = -INFINITY;
+    int far_i = -1;
+    for (int i = threadIdx.x; i < n; i += NT) {
+      int bi = 0;
+      float bd = dist[i * MAXG];
+      for (int q = 1; q < G; ++q)
+        if (dist[i * MAXG + q] < bd) {
+          bd = dist[i * MAXG + q];
+          bi = q;
+        }
+      assign[i] = bi;
+      dmin[i] = bd;
+      atomicAdd(&members[bi], 1);
+      if (bd > far_v) {
+        far_v = bd;
+        far_i = i;
+      }
+    }
+    if (want_far) {
+      const int far = block_argmax(far_v, far_i, rv, ri);
+      if (threadIdx.x == 0) pick = far < 0 ? 0 : far;
+    }
+    __syncthreads();
+  };
+
   // ---- initialisation ----
   if (a.kmeanspp) {
     if (threadIdx.x == 0) chosen[0] = a.init_first[c];
     __syncthreads();
-    for (int d = threadIdx.x; d < D; d += NT) centers[d] = work(chosen[0], d);
+    set_center(0, chosen[0]);
     __syncthreads();
     for (int j = 1; j < G; ++j) {
-      for (int i = warp; i < n; i += nwarps) {
-        point_dists(a, s, i, inv_norm, centers, j, dist + i * MAXG);
-      }
-      __syncthreads();
-      float part = 0.f;
+      distances(j);
+      float part[1] = {0.f};
       for (int i = threadIdx.x; i < n; i += NT) {
         float m = INFINITY;
-        for (int q = 0; q < j; ++q) m = fminf(m, dist[i * MAXG + q]);
         bool taken = false;
-        for (int q = 0; q < j; ++q) taken |= (chosen[q] == i);
+        for (int q = 0; q < j; ++q) {
+          m = fminf(m, dist[i * MAXG + q]);
+          taken |= (chosen[q] == i);
+        }
         dmin[i] = taken ? 0.f : m;
-        part += dmin[i];
+        part[0] += dmin[i];
       }
-      const float total = block_sum(part, scratch);
-      if (threadIdx.x == 0) {
-        int nxt = -1;
-        if (total > 0.f) {
-          const float* e = a.exp_draws + a.exp_off[c] + (int64_t)(j - 1) * n;
-          float best = -INFINITY;
-          for (int i = 0; i < n; ++i) {
-            const float q = (dmin[i] / total) / e[i];
-            if (q > best) {
-              best = q;
-              nxt = i;
-            }
+      block_sum_vec(part, 1, red);
+      const float total = part[0];
+      float best = -INFINITY;
+      int best_i = -1;
+      if (total > 0.f) {
+        const float* e = a.exp_draws + a.exp_off[c] + (int64_t)(j - 1) * n;
+        for (int i = threadIdx.x; i < n; i += NT) {
+          const float q = (dmin[i] / total) / e[i];
+          if (q > best) {
+            best = q;
+            best_i = i;
           }
         }
+      }
+      const int nxt0 = block_argmax(best, best_i, rv, ri);
+      if (threadIdx.x == 0) {
+        int nxt = nxt0;
         bool dup = nxt < 0;
         for (int q = 0; q < j && !dup; ++q) dup = (chosen[q] == nxt);
         if (dup) {
@@ -183,144 +310,197 @@ __global__ void __launch_bounds__(NT) kmeans_kernel(KMeansArgs a) {
         chosen[j] = nxt;
       }
       __syncthreads();
-      for (int d = threadIdx.x; d < D; d += NT) centers[j * D + d] = work(chosen[j], d);
+      set_center(j, chosen[j]);
       __syncthreads();
     }
   } else {
-    for (int j = 0; j < G; ++j)
-      for (int d = threadIdx.x; d < D; d += NT) centers[j * D + d] = work(a.init_idx[a.init_first[c] + j], d);
+    for (int q = 0; q < G; ++q) set_center(q, a.init_idx[a.init_first[c] + q]);
     __syncthreads();
   }
+
   // ---- Lloyd iterations ----
   int it = 0;
   for (it = 1; it <= a.max_iters; ++it) {
-    for (int i = warp; i < n; i += nwarps) point_dists(a, s, i, inv_norm, centers, G, dist + i * MAXG);
-    __syncthreads();
-    for (int i = threadIdx.x; i < n; i += NT) {
-      int bi = 0;
-      float bd = dist[i * MAXG];
-      for (int q = 1; q < G; ++q)
-        if (dist[i * MAXG + q] < bd) {
-          bd = dist[i * MAXG + q];
-          bi = q;
-        }
-      assign[i] = bi;
-      dmin[i] = bd;
-    }
-    if (threadIdx.x < MAXG) members[threadIdx.x] = 0;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      for (int i = 0; i < n; ++i) members[assign[i]]++;
-      int far = 0;
-      for (int i = 1; i < n; ++i)
-        if (dmin[i] > dmin[far]) far = i;
-      pick = far;
+    distances(G);
+    assign_points(true);
+    if (threadIdx.x == 0 && !a.farthest && a.status) {
       for (int q = 0; q < G; ++q)
-        if (members[q] == 0 && !a.farthest) a.status[c] = 1;
+        if (members[q] == 0) a.status[status_at] = 1;
     }
-    __syncthreads();
-    for (int q = 0; q < G; ++q) {
-      for (int d = threadIdx.x; d < D; d += NT) {
-        float v;
-        if (members[q] == 0) {
-          v = work(pick, d);
-        } else {
-          float acc = 0.f;
-          for (int i = 0; i < n; ++i)
-            if (assign[i] == q) acc += work(i, d);
-          v = acc / members[q];
+    // new centres: each thread owns 4 columns and accumulates every cluster
+    float shift[MAXG];
+#pragma unroll
+    for (int q = 0; q < MAXG; ++q) shift[q] = 0.f;
+    for (int j = threadIdx.x; j < D4; j += NT) {
+      float acc[MAXG][4];
+#pragma unroll
+      for (int q = 0; q < MAXG; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
+      for (int i = 0; i < n; ++i) {
+        const Quad k = load_quad(keys + (int64_t)i * kstride + 4 * j);
+        const float sc = inv_norm[i];
+        const int qi = assign[i];
+#pragma unroll
+        for (int q = 0; q < MAXG; ++q) {
+          if (q == qi) {
+            acc[q][0] += k.x * sc;
+            acc[q][1] += k.y * sc;
+            acc[q][2] += k.z * sc;
+            acc[q][3] += k.w * sc;
+          }
         }
-        next[q * D + d] = v;
+      }
+      const Quad fk = load_quad(keys + (int64_t)pick * kstride + 4 * j);
+      const float fsc = inv_norm[pick];
+#pragma unroll
+      for (int q = 0; q < MAXG; ++q) {
+        if (q < G) {
+          float4 nv;
+          if (members[q] == 0) {
+            nv = make_float4(fk.x * fsc, fk.y * fsc, fk.z * fsc, fk.w * fsc);
+          } else {
+            const float m = (float)members[q];
+            nv = make_float4(acc[q][0] / m, acc[q][1] / m, acc[q][2] / m, acc[q][3] / m);
+          }
+          float4* cp = reinterpret_cast<float4*>(centers + q * D + 4 * j);
+          const float4 old = *cp;
+          const float dx = nv.x - old.x, dy = nv.y - old.y, dz = nv.z - old.z, dw = nv.w - old.w;
+          shift[q] += dx * dx + dy * dy + dz * dz + dw * dw;
+          *cp = nv;
+        }
       }
     }
-    __syncthreads();
-    float shift = 0.f;
-    for (int q = 0; q < G; ++q) {
-      float part = 0.f;
-      for (int d = threadIdx.x; d < D; d += NT) {
-        const float df = next[q * D + d] - centers[q * D + d];
-        part += df * df;
-      }
-      shift = fmaxf(shift, sqrtf(block_sum(part, scratch)));
+    block_sum_vec(shift, G, red);
+    if (threadIdx.x == 0) {
+      float m = 0.f;
+      for (int q = 0; q < G; ++q) m = fmaxf(m, sqrtf(shift[q]));
+      stop = m <= a.tol;
     }
-    for (int i = threadIdx.x; i < G * D; i += NT) centers[i] = next[i];
     __syncthreads();
-    if (shift <= a.tol) break;
+    if (stop) break;
   }
   if (it > a.max_iters) it = a.max_iters;
-  // ---- final assignment and paired means over original rows ----
-  for (int i = warp; i < n; i += nwarps) point_dists(a, s, i, inv_norm, centers, G, dist + i * MAXG);
-  __syncthreads();
-  for (int i = threadIdx.x; i < n; i += NT) {
-    int bi = 0;
-    float bd = dist[i * MAXG];
-    for (int q = 1; q < G; ++q)
-      if (dist[i * MAXG + q] < bd) {
-        bd = dist[i * MAXG + q];
-        bi = q;
-      }
-    assign[i] = bi;
-  }
-  if (threadIdx.x < MAXG) members[threadIdx.x] = 0;
-  __syncthreads();
+
+  // ---- final assignment and paired means over the original rows ----
+  distances(G);
+  assign_points(false);
   if (threadIdx.x == 0) {
-    for (int i = 0; i < n; ++i) members[assign[i]]++;
     int slot = 0;
     for (int q = 0; q < G; ++q) {
-      chosen[q] = members[q] ? slot : -1;
-      if (members[q]) a.occupancy[c * a.G + slot++] = members[q];
+      slot_of[q] = members[q] ? slot : -1;
+      if (members[q] && a.occupancy) a.occupancy[status_at * a.G + slot] = members[q];
+      if (members[q]) ++slot;
     }
-    a.count[c] = slot;
-    a.iterations[c] = it;
+    a.count[layer * a.count_layer_stride + dst] = slot;
+    if (a.iterations) a.iterations[status_at] = it;
   }
   __syncthreads();
-  for (int q = 0; q < G; ++q) {
-    const int slot = chosen[q];
-    if (slot < 0) continue;
-    float part = 0.f;
-    for (int d = threadIdx.x; d < D; d += NT) {
-      float ak = 0.f, av = 0.f;
+  // keys (raw, not normalised) then values; each thread keeps its columns for the norms
+  float norm1[MAXG], norm2[MAXG];
+#pragma unroll
+  for (int q = 0; q < MAXG; ++q) norm1[q] = norm2[q] = 0.f;
+  for (int pass = 0; pass < 2; ++pass) {
+    const __nv_bfloat16* src = pass == 0 ? keys : gval;
+    const int64_t stride = pass == 0 ? kstride : a.row_stride;
+    float* dstp = pass == 0 ? a.gk : a.gv;
+    for (int j = threadIdx.x; j < D4; j += NT) {
+      float acc[MAXG][4];
+#pragma unroll
+      for (int q = 0; q < MAXG; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
       for (int i = 0; i < n; ++i) {
-        if (assign[i] != q) continue;
-        ak += __bfloat162float(a.pk[(int64_t)(s + i) * a.row_stride + d]);
-        av += __bfloat162float(a.pv[(int64_t)(s + i) * a.row_stride + d]);
+        const Quad k = load_quad(src + (int64_t)i * stride + 4 * j);
+        const int qi = assign[i];
+#pragma unroll
+        for (int q = 0; q < MAXG; ++q) {
+          if (q == qi) {
+            acc[q][0] += k.x;
+            acc[q][1] += k.y;
+            acc[q][2] += k.z;
+            acc[q][3] += k.w;
+          }
+        }
       }
-      ak /= members[q];
-      av /= members[q];
-      a.gk[((int64_t)c * a.G + slot) * D + d] = ak;
-      a.gv[((int64_t)c * a.G + slot) * D + d] = av;
-      part += ak * ak;
+#pragma unroll
+      for (int q = 0; q < MAXG; ++q) {
+        if (q < G && slot_of[q] >= 0) {
+          const float m = (float)members[q];
+          const float4 v = make_float4(acc[q][0] / m, acc[q][1] / m, acc[q][2] / m, acc[q][3] / m);
+          *reinterpret_cast<float4*>(dstp + out + (int64_t)slot_of[q] * D + 4 * j) = v;
+          if (pass == 0) norm1[q] += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+      }
     }
-    if (a.normalize) {
-      const float inv = 1.f / fmaxf(sqrtf(block_sum(part, scratch)), EPS);
-      for (int d = threadIdx.x; d < D; d += NT) a.gk[((int64_t)c * a.G + slot) * D + d] *= inv;
-    }
-    __syncthreads();
   }
+  // gk is L2-normalised when the working space is; gn = gk / ||gk|| is the routing copy.
+  block_sum_vec(norm1, G, red);
+  for (int j = threadIdx.x; j < D4; j += NT) {
+#pragma unroll
+    for (int q = 0; q < MAXG; ++q) {
+      if (q < G && slot_of[q] >= 0) {
+        float4* p = reinterpret_cast<float4*>(a.gk + out + (int64_t)slot_of[q] * D + 4 * j);
+        float4 v = *p;
+        if (a.normalize) {
+          const float inv = 1.f / fmaxf(sqrtf(norm1[q]), EPS);
+          v = make_float4(v.x * inv, v.y * inv, v.z * inv, v.w * inv);
+          *p = v;
+        }
+        norm2[q] += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      }
+    }
+  }
+  block_sum_vec(norm2, G, red);
+  for (int j = threadIdx.x; j < D4; j += NT) {
+#pragma unroll
+    for (int q = 0; q < MAXG; ++q) {
+      if (q < G && slot_of[q] >= 0) {
+        const int64_t o = out + (int64_t)slot_of[q] * D + 4 * j;
+        const float4 v = *reinterpret_cast<const float4*>(a.gk + o);
+        const float inv = 1.f / fmaxf(sqrtf(norm2[q]), EPS);
+        *reinterpret_cast<float4*>(a.gn + o) = make_float4(v.x * inv, v.y * inv, v.z * inv, v.w * inv);
+      }
+    }
+  }
+}
+
+size_t kmeans_fixed_smem(const GistArgs& a) {
+  return (size_t)a.G * a.D * sizeof(float) + (size_t)a.nmax * (2 * sizeof(float) + MAXG * sizeof(float) + sizeof(int));
 }
 
 }  // namespace gist
 }  // namespace pra
 
-cudaError_t pra_gist_mean(const __nv_bfloat16* pk, const __nv_bfloat16* pv, int64_t row_stride, const int* start,
-                          const int* len, int C, int D, float* gk, float* gv, float* gn, cudaStream_t st) {
-  if (C == 0) return cudaSuccess;
-  pra::gist::mean_kernel<<<C, pra::gist::NT, 0, st>>>(pk, pv, row_stride, start, len, D, gk, gv, gn);
+static cudaError_t check_gist_args(const GistArgs& a) {
+  if (a.D % 4 != 0 || a.row_stride % 4 != 0 || a.layer_stride % 4 != 0) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(a.pk) | reinterpret_cast<uintptr_t>(a.pv)) & 7) return cudaErrorInvalidValue;
+  if (reinterpret_cast<uintptr_t>(a.gk) & 15 || reinterpret_cast<uintptr_t>(a.gv) & 15 ||
+      reinterpret_cast<uintptr_t>(a.gn) & 15)
+    return cudaErrorInvalidValue;
+  return cudaSuccess;
+}
+
+cudaError_t pra_gist_mean(const GistArgs& a, int layers, cudaStream_t st) {
+  if (a.C == 0 || layers == 0) return cudaSuccess;
+  PRA_RETURN_IF_ERROR(check_gist_args(a));
+  pra::gist::mean_kernel<<<dim3(a.C, layers), pra::gist::NT, 0, st>>>(a);
   return cudaGetLastError();
 }
 
-cudaError_t pra_gist_kmeans(const __nv_bfloat16* pk, const __nv_bfloat16* pv, int64_t row_stride, const int* start,
-                            const int* len, int C, int D, int G, int max_iters, float tol, bool normalize,
-                            bool kmeanspp, bool farthest, const int* init_first, const int* init_idx,
-                            const float* exp_draws, const int64_t* exp_off, float* gk, float* gv, int* count,
-                            int* occupancy, int* iterations, int* status, cudaStream_t st) {
+cudaError_t pra_gist_kmeans(const GistArgs& a, int layers, cudaStream_t st) {
   using namespace pra::gist;
-  if (C == 0) return cudaSuccess;
-  if (G > MAXG) return cudaErrorInvalidValue;
-  KMeansArgs a{pk, pv, row_stride, start, len, D, G, max_iters, tol, normalize, kmeanspp, farthest, init_first,
-               init_idx, exp_draws, exp_off, gk, gv, count, occupancy, iterations, status};
-  const size_t smem = (size_t)(2 * G * D + 2 * MAXN + MAXN * MAXG) * sizeof(float) + MAXN * sizeof(int);
-  PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(kmeans_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  kmeans_kernel<<<C, NT, smem, st>>>(a);
+  if (a.C == 0 || layers == 0) return cudaSuccess;
+  if (a.G < 1 || a.G > MAXG || a.nmax < 1 || a.nmax > MAXN) return cudaErrorInvalidValue;
+  PRA_RETURN_IF_ERROR(check_gist_args(a));
+  const size_t fixed = kmeans_fixed_smem(a);
+  const size_t staged = fixed + (size_t)a.nmax * a.D * sizeof(__nv_bfloat16);
+  // Stage when two CTAs still fit on one SM (2 x 110 KB of the 228 KB per SM).
+  if (staged <= 110 * 1024) {
+    PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(kmeans_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)staged));
+    kmeans_kernel<true><<<dim3(a.C, layers), NT, staged, st>>>(a);
+  } else {
+    if (fixed > 200 * 1024) return cudaErrorInvalidValue;
+    PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(kmeans_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)fixed));
+    kmeans_kernel<false><<<dim3(a.C, layers), NT, fixed, st>>>(a);
+  }
   return cudaGetLastError();
 }

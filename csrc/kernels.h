@@ -76,13 +76,39 @@ cudaError_t pra_adamw(float* param, __nv_bfloat16* shadow, const void* grad, boo
 cudaError_t pra_cast_f32_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t stream);
 
 // ---- gists (gist.cu) ------------------------------------------------------------------
-cudaError_t pra_gist_mean(const __nv_bfloat16* pk, const __nv_bfloat16* pv, int64_t row_stride, const int* start,
-                          const int* len, int C, int D, float* gk, float* gv, float* gn, cudaStream_t stream);
-cudaError_t pra_gist_kmeans(const __nv_bfloat16* pk, const __nv_bfloat16* pv, int64_t row_stride, const int* start,
-                            const int* len, int C, int D, int G, int max_iters, float tol, bool normalize,
-                            bool kmeanspp, bool farthest, const int* init_first, const int* init_idx,
-                            const float* exp_draws, const int64_t* exp_off, float* gk, float* gv, int* count,
-                            int* occupancy, int* iterations, int* status, cudaStream_t stream);
+// One CTA per (chunk, layer).  Inputs: layer l's K/V rows at pk/pv + l * layer_stride
+// (bf16, row stride row_stride); chunk c owns rows [start[c], start[c] + len[c]).
+// Outputs land at chunk slot dest[c] (identity when null) of [L, S, G, D] fp32 tables
+// (out_layer_stride = S * G * D) and of count [L, S] (count_layer_stride = S).
+struct GistArgs {
+  const __nv_bfloat16* pk;
+  const __nv_bfloat16* pv;
+  int64_t row_stride, layer_stride;
+  const int* start;
+  const int* len;
+  const int* dest;
+  int C, D, G;
+  int nmax;                    // max chunk length in the launch (k-means scratch size)
+  float* gk;
+  float* gv;
+  float* gn;
+  int64_t out_layer_stride;
+  int* count;
+  int64_t count_layer_stride;
+  // k-means only
+  int max_iters;
+  float tol;
+  bool normalize, kmeanspp, farthest;
+  const int* init_first;       // [C] kmeans++ first index, or offset into init_idx for sampled init
+  const int* init_idx;         // flat sampled indices
+  const float* exp_draws;      // flat Exp(1) draws
+  const int* exp_off;          // [C] offset of this chunk's [G-1, len] draws
+  int* occupancy;              // [L, C, G] members per occupied slot (nullable)
+  int* iterations;             // [L, C] Lloyd iterations run (nullable)
+  int* status;                 // [L, C] 0 ok, 1 empty cluster under the error policy, 2 chunk too long (nullable)
+};
+cudaError_t pra_gist_mean(const GistArgs& args, int layers, cudaStream_t stream);
+cudaError_t pra_gist_kmeans(const GistArgs& args, int layers, cudaStream_t stream);
 
 // ---- row-local routing + selection + materialisation plan (routing.cu) ----------------
 struct RouteParams {

@@ -22,7 +22,7 @@ namespace route {
 constexpr int NT = 256;
 constexpr int MAX_ROW_CHUNKS = 8192;
 constexpr int MAX_ROW_REFS = 2048;
-constexpr int MAX_SEL = 256;
+constexpr int MAX_SEL = 256;  // must not exceed NT (one trace item per thread)
 constexpr float EPS = 1e-12f;
 
 __device__ __forceinline__ float reduce_set(const float* v, int n, int mode) {
@@ -50,27 +50,66 @@ __device__ __forceinline__ bool before(float s1, int r1, float s2, int r2) {
   return s1 > s2 || (s1 == s2 && r1 < r2);
 }
 
+// Exclusive prefix sum over the block of one int per thread (NT threads); returns the
+// thread's offset and writes the total to *total.
+__device__ __forceinline__ int block_exclusive_scan(int v, int* warp_tot, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  __syncthreads();
+  if (lane == 31) warp_tot[warp] = x;
+  __syncthreads();
+  int base = 0, all = 0;
+  for (int w = 0; w < NT / 32; ++w) {
+    if (w < warp) base += warp_tot[w];
+    all += warp_tot[w];
+  }
+  if (threadIdx.x == 0) *total = all;
+  __syncthreads();
+  return base + x - v;
+}
+
 __global__ void __launch_bounds__(NT) route_kernel(RouteParams p) {
   extern __shared__ __align__(16) float smem[];
   float* qn = smem;                                   // [D]
   float* cscore = qn + p.D;                           // [MAX_ROW_CHUNKS]
   float* wscore = cscore + MAX_ROW_CHUNKS;            // [MAX_ROW_CHUNKS]
   int* widx = reinterpret_cast<int*>(wscore + MAX_ROW_CHUNKS);  // [MAX_ROW_CHUNKS]
-  float* rscore = reinterpret_cast<float*>(widx + MAX_ROW_CHUNKS);  // [MAX_ROW_REFS]
+  int* crank = widx + MAX_ROW_CHUNKS;                 // [MAX_ROW_CHUNKS] lexical chunk rank (pos_rank)
+  float* rscore = reinterpret_cast<float*>(crank + MAX_ROW_CHUNKS);  // [MAX_ROW_REFS]
+  int* ref_taken = reinterpret_cast<int*>(rscore + MAX_ROW_REFS);    // [MAX_ROW_REFS]
   __shared__ float scratch[32];
-  __shared__ int sel_chunk[MAX_SEL], sel_rrank[MAX_SEL], sel_crank[MAX_SEL], sel_keep[MAX_SEL];
-  __shared__ float sel_rscore[MAX_SEL], sel_cscore[MAX_SEL];
-  __shared__ int top_ref[64];
-  __shared__ int n_sel;
+  __shared__ int warp_tot[NT / 32];
+  __shared__ float red_v[NT / 32];
+  __shared__ int red_i[NT / 32];
+  // per-selection item state (selection order)
+  __shared__ int it_pos[MAX_SEL], it_rrank[MAX_SEL], it_crank[MAX_SEL], it_keep[MAX_SEL];
+  __shared__ int it_ref[MAX_SEL], it_lex[MAX_SEL], it_chunk[MAX_SEL], it_start[MAX_SEL], it_len[MAX_SEL];
+  __shared__ float it_rscore[MAX_SEL], it_cscore[MAX_SEL];
+  __shared__ int by_budget[MAX_SEL], by_place[MAX_SEL], place_off[MAX_SEL], place_strip[MAX_SEL];
+  __shared__ int top_ref[64], ref_base[65], ref_first[64];
+  __shared__ int n_sel, n_kept, n_written, n_total;
 
   const int b = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = NT / 32;
   const int c0 = p.row_pos_off[b], c1 = p.row_pos_off[b + 1];
   const int r0 = p.row_ref_off[b], r1 = p.row_ref_off[b + 1];
   const int nc = c1 - c0, nr = r1 - r0;
+  // unused trace slots read as "no selection"
+  for (int i = threadIdx.x; i < p.max_sel; i += NT) {
+    const int64_t o = (int64_t)b * p.max_sel + i;
+    p.sel_chunk[o] = p.sel_ref_rank[o] = p.sel_chunk_rank[o] = p.sel_win_index[o] = -1;
+    p.sel_ref_score[o] = p.sel_chunk_score[o] = p.sel_win_score[o] = 0.f;
+  }
   if (threadIdx.x == 0) {
     p.mem_len[b] = 0;
     p.sel_count[b] = 0;
+    p.routing_candidates[b] = 0;
+    p.duplicate_tokens[b] = 0;
     p.status[b] = (nc > MAX_ROW_CHUNKS || nr > MAX_ROW_REFS) ? 1 : 0;
   }
   if (nc <= 0 || nr <= 0 || nc > MAX_ROW_CHUNKS || nr > MAX_ROW_REFS || p.k_ref <= 0 || p.k_chunk <= 0) return;
@@ -86,7 +125,8 @@ __global__ void __launch_bounds__(NT) route_kernel(RouteParams p) {
   for (int d = threadIdx.x; d < p.D; d += NT) qn[d] *= inv;
   __syncthreads();
 
-  // 2. chunk scores (warp per chunk)
+  // 2. chunk scores (warp per chunk, float4 gist reads)
+  const int D4 = p.D / 4;
   for (int i = warp; i < nc; i += nwarps) {
     const int c = p.pos_chunk[c0 + i];
     const int g_n = p.gist_count[c];
@@ -94,8 +134,11 @@ __global__ void __launch_bounds__(NT) route_kernel(RouteParams p) {
     for (int g = 0; g < p.G; ++g) {
       float acc = 0.f;
       if (g < g_n) {
-        const float* gv = p.gists + ((int64_t)c * p.G + g) * p.D;
-        for (int d = lane; d < p.D; d += 32) acc += qn[d] * gv[d];
+        const float4* gv = reinterpret_cast<const float4*>(p.gists + ((int64_t)c * p.G + g) * p.D);
+        for (int j = lane; j < D4; j += 32) {
+          const float4 x = gv[j];
+          acc += qn[4 * j] * x.x + qn[4 * j + 1] * x.y + qn[4 * j + 2] * x.z + qn[4 * j + 3] * x.w;
+        }
         acc = warp_sum(acc);
       }
       sc[g] = acc;
@@ -111,6 +154,7 @@ __global__ void __launch_bounds__(NT) route_kernel(RouteParams p) {
       cscore[i] = p.gist_agg == 0 ? ws : reduce_set(sc, g_n, p.gist_agg);
       wscore[i] = ws;
       widx[i] = wi;
+      crank[i] = p.pos_rank[c0 + i];
     }
   }
   __syncthreads();
@@ -118,150 +162,239 @@ __global__ void __launch_bounds__(NT) route_kernel(RouteParams p) {
   for (int r = threadIdx.x; r < nr; r += NT) {
     const int a = p.ref_pos_off[r0 + r] - c0, z = p.ref_pos_off[r0 + r + 1] - c0;
     rscore[r] = reduce_set(cscore + a, z - a, p.ref_agg);
+    ref_taken[r] = 0;
   }
   __syncthreads();
 
-  // 4. selection (single thread: k_ref * k_chunk items)
-  if (threadIdx.x == 0) {
-    const int kr = min(min(p.k_ref, nr), 64);
+  // 4a. top URIs under (-score, uri rank): rank counting when every ref has its own
+  // thread, otherwise repeated block argmax
+  const int kr = min(min(p.k_ref, nr), 64);
+  if (nr <= NT) {
+    if (threadIdx.x < nr) {
+      const int r = threadIdx.x;
+      int rank = 0;
+      for (int o = 0; o < nr; ++o) rank += before(rscore[o], o, rscore[r], r) ? 1 : 0;
+      if (rank < kr) top_ref[rank] = r;
+    }
+  } else {
     for (int j = 0; j < kr; ++j) {
-      int best = -1;
-      for (int r = 0; r < nr; ++r) {
-        bool used = false;
-        for (int q = 0; q < j; ++q) used |= (top_ref[q] == r);
-        if (used) continue;
-        if (best < 0 || before(rscore[r], r, rscore[best], best)) best = r;
+      float bv = -INFINITY;
+      int bi = -1;
+      for (int r = threadIdx.x; r < nr; r += NT)
+        if (!ref_taken[r] && (bi < 0 || before(rscore[r], r, bv, bi))) {
+          bv = rscore[r];
+          bi = r;
+        }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (oi >= 0 && (bi < 0 || before(ov, oi, bv, bi))) {
+          bv = ov;
+          bi = oi;
+        }
       }
-      top_ref[j] = best;
+      if (lane == 0) {
+        red_v[warp] = bv;
+        red_i[warp] = bi;
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        float v = red_v[0];
+        int i = red_i[0];
+        for (int w = 1; w < nwarps; ++w)
+          if (red_i[w] >= 0 && (i < 0 || before(red_v[w], red_i[w], v, i))) {
+            v = red_v[w];
+            i = red_i[w];
+          }
+        top_ref[j] = i;
+        ref_taken[i] = 1;
+      }
+      __syncthreads();
     }
-    int count = 0;
-    for (int j = 0; j < kr && count < MAX_SEL; ++j) {
+  }
+  __syncthreads();
+  // 4b. items per selected URI, their offsets, and each URI's best chunk
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int j = 0; j < kr; ++j) {
       const int r = top_ref[j];
-      const int a = p.ref_pos_off[r0 + r] - c0, z = p.ref_pos_off[r0 + r + 1] - c0;
-      if (p.full_reference) {
-        for (int i = a; i < z && count < MAX_SEL; ++i) {
-          sel_chunk[count] = i;
-          sel_rrank[count] = j + 1;
-          sel_crank[count] = i - a + 1;
-          sel_rscore[count] = rscore[r];
-          sel_cscore[count] = -INFINITY;  // filled below from the first routed hit
-          ++count;
+      const int len = p.ref_pos_off[r0 + r + 1] - p.ref_pos_off[r0 + r];
+      ref_base[j] = acc;
+      acc += p.full_reference ? len : min(p.k_chunk, len);
+    }
+    ref_base[kr] = acc;
+    n_sel = min(acc, MAX_SEL);
+  }
+  __syncthreads();
+  for (int j = warp; j < kr; j += nwarps) {
+    const int r = top_ref[j];
+    const int a = p.ref_pos_off[r0 + r] - c0, z = p.ref_pos_off[r0 + r + 1] - c0;
+    if (p.full_reference) {
+      // best chunk of the URI (its score is carried by every expanded chunk)
+      float bv = -INFINITY;
+      int bi = -1, br = 0;
+      for (int i = a + lane; i < z; i += 32)
+        if (bi < 0 || before(cscore[i], crank[i], bv, br)) {
+          bv = cscore[i];
+          bi = i;
+          br = crank[i];
         }
-        // the expanded chunks all carry the score of the URI's best routed chunk
-        int first = -1;
-        for (int i = a; i < z; ++i)
-          if (first < 0 || before(cscore[i], p.pos_rank[c0 + i], cscore[first], p.pos_rank[c0 + first])) first = i;
-        for (int q = count - (z - a); q < count; ++q) sel_cscore[q] = cscore[first];
-        continue;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        const int orr = __shfl_xor_sync(0xffffffffu, br, o);
+        if (oi >= 0 && (bi < 0 || before(ov, orr, bv, br))) {
+          bv = ov;
+          bi = oi;
+          br = orr;
+        }
       }
+      if (lane == 0) ref_first[j] = bi;
+      __syncwarp();
+      for (int i = a + lane; i < z; i += 32) {
+        const int q = ref_base[j] + (i - a);
+        if (q >= MAX_SEL) continue;
+        it_pos[q] = i;
+        it_rrank[q] = j + 1;
+        it_crank[q] = i - a + 1;
+        it_rscore[q] = rscore[r];
+        it_cscore[q] = cscore[bi];
+      }
+    } else {
       const int kc = min(p.k_chunk, z - a);
-      for (int t = 0; t < kc && count < MAX_SEL; ++t) {
-        int best = -1;
-        for (int i = a; i < z; ++i) {
-          bool used = false;
-          for (int q = count - t; q < count; ++q) used |= (sel_chunk[q] == i);
-          if (used) continue;
-          if (best < 0 || before(cscore[i], p.pos_rank[c0 + i], cscore[best], p.pos_rank[c0 + best])) best = i;
+      for (int i = a + lane; i < z; i += 32) {
+        int rank = 0;
+        for (int o = a; o < z; ++o) rank += before(cscore[o], crank[o], cscore[i], crank[i]) ? 1 : 0;
+        const int q = ref_base[j] + rank;
+        if (rank < kc && q < MAX_SEL) {
+          it_pos[q] = i;
+          it_rrank[q] = j + 1;
+          it_crank[q] = rank + 1;
+          it_rscore[q] = rscore[r];
+          it_cscore[q] = cscore[i];
         }
-        sel_chunk[count] = best;
-        sel_rrank[count] = j + 1;
-        sel_crank[count] = t + 1;
-        sel_rscore[count] = rscore[r];
-        sel_cscore[count] = cscore[best];
-        ++count;
       }
     }
-    // threshold
-    for (int q = 0; q < count; ++q) sel_keep[q] = sel_cscore[q] >= p.threshold ? 1 : 0;
-    // greedy budget in (-score, uri rank, chunk rank) order
+  }
+  __syncthreads();
+  const int count = n_sel;
+  // item attributes (threshold, namespace order, source span)
+  for (int q = threadIdx.x; q < count; q += NT) {
+    const int pos = c0 + it_pos[q];
+    const int c = p.pos_chunk[pos];
+    it_keep[q] = it_cscore[q] >= p.threshold ? 1 : 0;
+    it_ref[q] = p.pos_ref[pos];
+    it_lex[q] = crank[it_pos[q]];
+    it_chunk[q] = c;
+    it_start[q] = p.chunk_start[c];
+    it_len[q] = p.chunk_len[c];
+  }
+  __syncthreads();
+  // 4c. budget order (-score, uri, chunk rank, selection index) and materialisation order
+  // (uri, token start, chunk rank, selection index) among the threshold survivors
+  for (int q = threadIdx.x; q < count; q += NT) {
+    if (!it_keep[q]) continue;
+    int rb = 0, rp = 0;
+    for (int o = 0; o < count; ++o) {
+      if (!it_keep[o] || o == q) continue;
+      const bool ob = it_cscore[o] > it_cscore[q] ||
+                      (it_cscore[o] == it_cscore[q] &&
+                       (it_ref[o] < it_ref[q] ||
+                        (it_ref[o] == it_ref[q] && (it_lex[o] < it_lex[q] || (it_lex[o] == it_lex[q] && o < q)))));
+      const bool op = it_ref[o] < it_ref[q] ||
+                      (it_ref[o] == it_ref[q] &&
+                       (it_start[o] < it_start[q] ||
+                        (it_start[o] == it_start[q] && (it_lex[o] < it_lex[q] || (it_lex[o] == it_lex[q] && o < q)))));
+      rb += ob ? 1 : 0;
+      rp += op ? 1 : 0;
+    }
+    by_budget[rb] = q;
+    by_place[rp] = q;
+  }
+  __syncthreads();
+  // 4d. greedy whole-chunk budget (sequential by definition), then placement offsets
+  if (threadIdx.x == 0) {
+    int survivors = 0;
+    for (int q = 0; q < count; ++q) survivors += it_keep[q];
     int remaining = p.budget_rows ? p.budget_rows[b] : p.budget;
-    for (int pass = 0; pass < count; ++pass) {
-      int best = -1;
-      for (int q = 0; q < count; ++q) {
-        if (sel_keep[q] != 1) continue;
-        if (best < 0) {
-          best = q;
-          continue;
-        }
-        const int rq = p.pos_ref[c0 + sel_chunk[q]], rb = p.pos_ref[c0 + sel_chunk[best]];
-        const bool better = sel_cscore[q] > sel_cscore[best] ||
-                            (sel_cscore[q] == sel_cscore[best] &&
-                             (rq < rb || (rq == rb && p.pos_rank[c0 + sel_chunk[q]] < p.pos_rank[c0 + sel_chunk[best]])));
-        if (better) best = q;
-      }
-      if (best < 0) break;
-      const int cost = p.gist_only ? 1 : p.chunk_len[c0 + sel_chunk[best]];
+    for (int k = 0; k < survivors; ++k) {
+      const int q = by_budget[k];
+      const int cost = p.gist_only ? 1 : it_len[q];
       if (cost <= remaining) {
         remaining -= cost;
-        sel_keep[best] = 2;  // retained
+        it_keep[q] = 2;  // retained
       } else {
-        sel_keep[best] = 3;  // rejected by the budget
+        it_keep[q] = 3;  // rejected by the budget
       }
     }
-    // trace records (retained, in selection order)
-    int kept = 0;
-    for (int q = 0; q < count; ++q) {
-      if (sel_keep[q] != 2) continue;
-      const int c = p.pos_chunk[c0 + sel_chunk[q]];
-      const int64_t o = (int64_t)b * p.max_sel + kept;
-      if (kept < p.max_sel) {
-        p.sel_chunk[o] = c;
-        p.sel_ref_rank[o] = sel_rrank[q];
-        p.sel_chunk_rank[o] = sel_crank[q];
-        p.sel_ref_score[o] = sel_rscore[q];
-        p.sel_chunk_score[o] = sel_cscore[q];
-        p.sel_win_index[o] = widx[sel_chunk[q]];
-        p.sel_win_score[o] = wscore[sel_chunk[q]];
-      }
-      ++kept;
-    }
-    p.sel_count[b] = min(kept, p.max_sel);
-    p.routing_candidates[b] = count;
-    // materialisation order: (uri rank, token_start, chunk rank); strip covered overlap
-    int written = 0, duplicates = 0;
-    int last_ref = -1, covered = 0;
-    for (int pass = 0; pass < count; ++pass) {
-      int best = -1;
-      for (int q = 0; q < count; ++q) {
-        if (sel_keep[q] != 2) continue;
-        if (best < 0) {
-          best = q;
-          continue;
-        }
-        const int pq = c0 + sel_chunk[q], pb = c0 + sel_chunk[best];
-        const int cq = p.pos_chunk[pq], cb = p.pos_chunk[pb];
-        const int rq = p.pos_ref[pq], rb = p.pos_ref[pb];
-        const bool earlier = rq < rb || (rq == rb && (p.chunk_start[cq] < p.chunk_start[cb] ||
-                                                      (p.chunk_start[cq] == p.chunk_start[cb] &&
-                                                       p.pos_rank[pq] < p.pos_rank[pb])));
-        if (earlier) best = q;
-      }
-      if (best < 0) break;
-      sel_keep[best] = 4;
-      const int c = p.pos_chunk[c0 + sel_chunk[best]];
+    // materialisation walk over retained items: overlap already covered by the same URI is stripped
+    int written = 0, duplicates = 0, last_ref = -1, covered = 0, placed = 0;
+    for (int k = 0; k < survivors; ++k) {
+      const int q = by_place[k];
+      if (it_keep[q] != 2) continue;
+      by_place[placed++] = q;
       if (p.gist_only) {
-        if (written < p.max_mem) p.mem_idx[(int64_t)b * p.max_mem + written] = c * p.G + widx[sel_chunk[best]];
+        place_off[q] = written;
+        place_strip[q] = 0;
         ++written;
         continue;
       }
-      const int ref = p.pos_ref[c0 + sel_chunk[best]];
-      const int tstart = p.chunk_start[c], n = p.chunk_len[c];
-      int strip = 0;
-      const int end = (ref == last_ref) ? covered : tstart;
-      if (ref != last_ref) covered = tstart;
-      strip = min(max(end - tstart, 0), n);
+      const int tstart = it_start[q], n = it_len[q];
+      const int end = (it_ref[q] == last_ref) ? covered : tstart;
+      if (it_ref[q] != last_ref) covered = tstart;
+      int strip = min(max(end - tstart, 0), n);
       duplicates += strip;
       if (!p.deduplicate) strip = 0;
-      for (int t = strip; t < n; ++t) {
-        if (written < p.max_mem) p.mem_idx[(int64_t)b * p.max_mem + written] = p.chunk_pool_row[c] + t;
-        ++written;
-      }
+      place_off[q] = written;
+      place_strip[q] = strip;
+      written += n - strip;
       covered = max(end, tstart + n);
-      last_ref = ref;
+      last_ref = it_ref[q];
     }
+    n_kept = placed;
+    n_written = written;
+    p.routing_candidates[b] = count;
     p.mem_len[b] = min(written, p.max_mem);
     p.duplicate_tokens[b] = duplicates;
     if (written > p.max_mem) p.status[b] = 2;
+  }
+  __syncthreads();
+  // 4e. trace records: retained items in selection order
+  {
+    const int q = threadIdx.x;
+    const int flag = (q < count && it_keep[q] == 2) ? 1 : 0;
+    // count may exceed NT only when MAX_SEL > NT
+    int kept = block_exclusive_scan(flag, warp_tot, &n_total);
+    if (flag && kept < p.max_sel) {
+      const int64_t o = (int64_t)b * p.max_sel + kept;
+      const int i = it_pos[q];
+      p.sel_chunk[o] = it_chunk[q];
+      p.sel_ref_rank[o] = it_rrank[q];
+      p.sel_chunk_rank[o] = it_crank[q];
+      p.sel_ref_score[o] = it_rscore[q];
+      p.sel_chunk_score[o] = it_cscore[q];
+      p.sel_win_index[o] = widx[i];
+      p.sel_win_score[o] = wscore[i];
+    }
+    if (threadIdx.x == 0) p.sel_count[b] = min(n_total, p.max_sel);
+  }
+  // 4f. the memory key list, filled in parallel
+  const int kept_items = n_kept;
+  for (int k = warp; k < kept_items; k += nwarps) {
+    const int q = by_place[k];
+    const int c = it_chunk[q];
+    if (p.gist_only) {
+      if (lane == 0 && place_off[q] < p.max_mem)
+        p.mem_idx[(int64_t)b * p.max_mem + place_off[q]] = c * p.G + widx[it_pos[q]];
+      continue;
+    }
+    const int base_row = p.chunk_pool_row[c];
+    for (int t = place_strip[q] + lane; t < it_len[q]; t += 32) {
+      const int at = place_off[q] + t - place_strip[q];
+      if (at < p.max_mem) p.mem_idx[(int64_t)b * p.max_mem + at] = base_row + t;
+    }
   }
 }
 
@@ -272,8 +405,9 @@ cudaError_t pra_route(const RouteParams& p, cudaStream_t st) {
   using namespace pra::route;
   if (p.B == 0) return cudaSuccess;
   if (p.G > 8) return cudaErrorInvalidValue;
-  const size_t smem = (size_t)p.D * sizeof(float) + (size_t)MAX_ROW_CHUNKS * (2 * sizeof(float) + sizeof(int)) +
-                      (size_t)MAX_ROW_REFS * sizeof(float);
+  if (p.D % 4 != 0 || (reinterpret_cast<uintptr_t>(p.gists) & 15)) return cudaErrorInvalidValue;
+  const size_t smem = (size_t)p.D * sizeof(float) + (size_t)MAX_ROW_CHUNKS * (2 * sizeof(float) + 2 * sizeof(int)) +
+                      (size_t)MAX_ROW_REFS * (sizeof(float) + sizeof(int));
   PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   route_kernel<<<p.B, NT, smem, st>>>(p);
   return cudaGetLastError();

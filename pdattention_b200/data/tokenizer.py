@@ -94,19 +94,28 @@ class WordIdTokenizer:
         return self.base_vocab + len(self._refs)
 
     def encode(self, text: str) -> list[int]:
-        out = []
-        for word in text.split():
-            if word in self._refs or REF_TOKEN_PATTERN.fullmatch(word):
-                out.append(self.register_reference_token(word))
-            elif word.startswith("t") and word[1:].isdigit() and int(word[1:]) < self.base_vocab:
-                out.append(int(word[1:]))
-            else:
-                out.append(0)
+        get = self.stoi.get
+        words = text.split()
+        out = [get(word, -1) for word in words]
+        if -1 in out:  # unregistered reference handles, non-canonical or unknown words
+            for i, value in enumerate(out):
+                if value == -1:
+                    out[i] = self._encode_word(words[i])
         return out
 
+    def _encode_word(self, word: str) -> int:
+        if REF_TOKEN_PATTERN.fullmatch(word):
+            return self.register_reference_token(word)
+        if word.startswith("t") and word[1:].isdigit() and int(word[1:]) < self.base_vocab:
+            return int(word[1:])
+        return 0
+
     def decode(self, ids) -> str:
-        inverse = {v: k for k, v in self._refs.items()}
-        return " ".join(inverse.get(int(i), f"t{int(i)}") for i in ids)
+        itos = self.itos
+        try:
+            return " ".join([itos[i] for i in ids])
+        except (KeyError, TypeError):  # tensor elements, or ids above the registered range
+            return " ".join(itos.get(i) or f"t{i}" for i in map(int, ids))
 
 
 class BPETokenizer:

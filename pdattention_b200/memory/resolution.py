@@ -63,6 +63,7 @@ class BuildStep:
     use_pra_memory: bool
     visible_uris: tuple[str, ...]
     depth: int
+    token_ids: tuple[int, ...] | None = None  # the text's ids, tokenised once while planning
 
 
 def _fingerprint(value) -> str:
@@ -178,7 +179,8 @@ class RecursiveReferenceCacheBuilder:
         if existing is not None and hasattr(self.cache, "invalidate"):
             self.cache.invalidate(uri)
 
-        budget.consume(len(self.tokenizer.encode(resolved.text)))
+        token_ids = self.tokenizer.encode(resolved.text)
+        budget.consume(len(token_ids))
         if hasattr(self.cache, "begin_build") and not self.plan_only:
             self.cache.begin_build(uri)
         self.events.append(ResolutionEvent(uri, "building", depth, parent_uri=parent_uri))
@@ -207,7 +209,8 @@ class RecursiveReferenceCacheBuilder:
             if self.plan_only:
                 ready = [e.uri for e in self.cache.all_entries()] + self._planned_ready
                 visible = tuple(dict.fromkeys(ready)) if use_memory else ()
-                self.plan.append(BuildStep(uri, resolved.text, metadata, use_memory, visible, depth))
+                self.plan.append(BuildStep(uri, resolved.text, metadata, use_memory, visible, depth,
+                                           tuple(token_ids)))
                 self._planned_ready.append(uri)
                 self.events.append(ResolutionEvent(uri, "ready", depth, parent_uri=parent_uri))
                 return None

@@ -42,6 +42,26 @@ _AGG = {"max": 0, "mean": 1, "logsumexp": 2}
 _ALIGN = 8  # elements: every flat region starts 16-byte aligned (TMA and vector loads need 16)
 
 
+def _upload(device, *arrays, dtype=torch.int32) -> list[torch.Tensor]:
+    """Copy several host integer sequences to the device in ONE asynchronous copy.
+
+    The sequences are packed into a pinned staging buffer, so the copy neither
+    blocks the host nor synchronises the stream (a pageable ``torch.tensor(...,
+    device=cuda)`` does both); the returned tensors are views of one device
+    buffer.  Empty sequences come back as a one-element zero tensor.
+    """
+    import numpy as np
+
+    parts = [np.asarray(a if len(a) else [0], dtype=np.int64 if dtype == torch.int64 else np.int32).ravel()
+             for a in arrays]
+    sizes = [p.size for p in parts]
+    host = torch.from_numpy(np.concatenate(parts))
+    if torch.device(device).type == "cuda":
+        host = host.pin_memory()
+    dev = host.to(device, non_blocking=True)
+    return list(dev.split(sizes))
+
+
 def unsupported_reason(cfg) -> str | None:
     """Why a configuration must use the object path (``None`` when the device path applies)."""
     head_dim = cfg.d_model // cfg.n_heads
@@ -56,6 +76,8 @@ def unsupported_reason(cfg) -> str | None:
         (cfg.encoding_chunking is not None, "bounded encoding"),
         (cfg.kv_cache_residency != "gpu", "CPU-resident K/V"),
         (cfg.gist_mode not in {"mean", "kmeans"}, f"gist_mode={cfg.gist_mode}"),
+        (cfg.gist_mode == "kmeans" and cfg.gist_kmeans_empty_cluster_policy == "error",
+         "k-means error-on-empty-cluster policy"),
         (cfg.reference_level_gist_mode is not None, "URI-level gists"),
         (cfg.gists_per_chunk > 8, "more than 8 gists"),
         (head_dim not in (32, 64, 128), f"head_dim={head_dim}"),
@@ -248,11 +270,8 @@ class Namespace:
                 ref_pos_off.append(len(pos_chunk))
             row_pos_off.append(len(pos_chunk))
             row_ref_off.append(len(ref_pos_off) - 1)
-        as_int = lambda x: torch.tensor(x, dtype=torch.int32, device=device)  # noqa: E731
-        self.row_pos_off, self.row_ref_off, self.ref_pos_off = as_int(row_pos_off), as_int(row_ref_off), \
-            as_int(ref_pos_off)
-        self.pos_chunk, self.pos_ref, self.pos_rank = as_int(pos_chunk or [0]), as_int(pos_ref or [0]), \
-            as_int(pos_rank or [0])
+        (self.row_pos_off, self.row_ref_off, self.ref_pos_off, self.pos_chunk, self.pos_ref,
+         self.pos_rank) = _upload(device, row_pos_off, row_ref_off, ref_pos_off, pos_chunk, pos_ref, pos_rank)
         self.rows_entries = rows_entries
         self.empty = len(pos_chunk) == 0
 
@@ -266,27 +285,36 @@ class BatchMemory:
         self.seq_len = seq_len
         n_seq = max(len(chunks), 1)
         width = 3 * cfg.d_model
-        self.pools = [torch.empty((n_seq * seq_len, width), device=device, dtype=torch.bfloat16)
-                      for _ in range(cfg.n_layers)]
+        L = cfg.n_layers
+        # one allocation per table; per-layer views keep the indexing simple
+        self.pool = torch.empty((L, n_seq * seq_len, width), device=device, dtype=torch.bfloat16)
+        self.pools = list(self.pool.unbind(0))
         g = max(cfg.gists_per_chunk if cfg.gist_mode == "kmeans" else 1, 1)
         self.G = g
-        self.gists = [torch.zeros((n_seq, g, cfg.d_model), device=device, dtype=torch.float32)
-                      for _ in range(cfg.n_layers)]
-        self.gist_k = [torch.zeros((n_seq, g, cfg.d_model), device=device, dtype=torch.float32)
-                       for _ in range(cfg.n_layers)]
-        self.gist_v = [torch.zeros((n_seq, g, cfg.d_model), device=device, dtype=torch.float32)
-                       for _ in range(cfg.n_layers)]
-        self.gist_count = [torch.zeros(n_seq, device=device, dtype=torch.int32) for _ in range(cfg.n_layers)]
-        as_int = lambda x: torch.tensor(x or [0], dtype=torch.int32, device=device)  # noqa: E731
-        self.chunk_start = as_int([c.token_start for c in chunks])
-        self.chunk_len = as_int([len(c.token_ids) for c in chunks])
-        self.chunk_pool_row = as_int([c.seq * seq_len for c in chunks])
+        self.n_seq = n_seq
+        self.gist_tables = torch.zeros((3, L, n_seq, g, cfg.d_model), device=device, dtype=torch.float32)
+        self.gists_all, self.gist_k_all, self.gist_v_all = self.gist_tables.unbind(0)
+        self.gists = list(self.gists_all.unbind(0))
+        self.gist_k = list(self.gist_k_all.unbind(0))
+        self.gist_v = list(self.gist_v_all.unbind(0))
+        self.gist_count_all = torch.zeros((L, n_seq), device=device, dtype=torch.int32)
+        self.gist_count = list(self.gist_count_all.unbind(0))
+        self.chunk_start, self.chunk_len, self.chunk_pool_row = _upload(
+            device, [c.token_start for c in chunks], [len(c.token_ids) for c in chunks],
+            [c.seq * seq_len for c in chunks])
 
     def k_view(self, layer: int, d: int) -> torch.Tensor:
         return self.pools[layer][:, d:2 * d]
 
     def v_view(self, layer: int, d: int) -> torch.Tensor:
         return self.pools[layer][:, 2 * d:]
+
+    def k_all(self, d: int) -> torch.Tensor:
+        """[L, rows, d] view of every layer's keys."""
+        return self.pool[:, :, d:2 * d]
+
+    def v_all(self, d: int) -> torch.Tensor:
+        return self.pool[:, :, 2 * d:]
 
 
 @dataclass
@@ -297,6 +325,63 @@ class LayerRouting:
     ints: torch.Tensor
     sel_i: torch.Tensor
     sel_f: torch.Tensor
+
+
+@dataclass
+class BatchPlan:
+    """Host-side cache-build plan of one batch (see ``DeviceRuntime.plan_batch``)."""
+
+    metadata_rows: list
+    caches: list
+    builders: list
+    entries: list
+    chunks: list
+    rows: list
+    seq_len: int
+    waves: list
+
+
+class KMeansTables:
+    """Device copies of the seeded k-means initialisation draws, one block per chunk length.
+
+    The seeded CPU generator's draws depend only on (chunk length, gist count,
+    seed), so each distinct length is drawn once, appended to a device buffer and
+    shared by every chunk of that length; a wave then ships only two offsets per
+    chunk.  ``kmeans++`` blocks hold the first index and ``count - 1`` rows of
+    Exp(1) draws; ``sample`` blocks hold the sampled point indices.
+    """
+
+    def __init__(self, cfg, device):
+        self.cfg, self.device = cfg, device
+        self.blocks: dict[int, tuple[int, int]] = {}
+        self._draws: list[torch.Tensor] = []
+        self._idx: list[int] = []
+        self._draw_cursor = 0
+        self.draws = torch.zeros(1, device=device)
+        self.idx = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def lookup(self, lengths: list[int]) -> tuple[list[int], list[int]]:
+        cfg = self.cfg
+        new = [n for n in dict.fromkeys(lengths) if n not in self.blocks]
+        for n in new:
+            count = min(max(cfg.gists_per_chunk, 1), n)
+            if cfg.gist_kmeans_init == "kmeans++":
+                first, exp = kmeanspp_random_stream(n, count, cfg.gist_kmeans_seed)
+                self.blocks[n] = (int(first), self._draw_cursor)
+                self._draws.append(exp.flatten().float())
+                self._draw_cursor += exp.numel()
+            else:
+                perm = torch.randperm(n, generator=local_generator(cfg.gist_kmeans_seed))[:count]
+                self.blocks[n] = (len(self._idx), 0)
+                self._idx.extend(int(i) for i in perm)
+        if new:  # rare: a chunk length not seen before
+            if self._draws:
+                self.draws = torch.cat(self._draws).to(self.device)
+            if self._idx:
+                self.idx = torch.tensor(self._idx, dtype=torch.int32).to(self.device)
+        firsts = [self.blocks[n][0] for n in lengths]
+        offs = [self.blocks[n][1] for n in lengths]
+        return firsts, offs
 
 
 # ---------------------------------------------------------------------------
@@ -339,7 +424,10 @@ class DeviceRuntime:
         self.tok_emb_g = f.view(f.grad, "token_emb.weight")
         self.pos_emb_g = f.view(f.grad, "pos_emb.weight")
         self.anchor = torch.zeros(1, device=self.device, requires_grad=True)  # puts embeddings on the tape
-        self._kmeans_streams: dict[int, tuple] = {}
+        self.kmeans_tables = KMeansTables(cfg, self.device)
+        self._prefetched: BatchPlan | None = None
+        self._last_tokenizer = None
+        self._last_resolver = None
         self.last_routing: dict[int, LayerRouting] = {}
         self.last_memory: BatchMemory | None = None
         self.last_namespace: Namespace | None = None
@@ -414,8 +502,9 @@ class DeviceRuntime:
         return MemoryView(memory.k_view(li, d), memory.v_view(li, d), mem_idx, ints[0])
 
     # -- cache build ------------------------------------------------------------
-    def build_memory(self, metadata_rows: list[dict], tokenizer, resolver_config=None):
-        """Trace every row's recursive build, then encode all rows' chunks wave by wave."""
+    def plan_batch(self, metadata_rows: list[dict], tokenizer, resolver_config=None) -> "BatchPlan":
+        """Host half of the cache build: trace every row's recursive build, tokenise and
+        chunk each entry once, and order the entries into dependency waves."""
         cfg = self.cfg
         caches, builders = plan_cache_builds(self.model, tokenizer, metadata_rows, resolver_config=resolver_config)
         entries: list[EntryRecord] = []
@@ -426,7 +515,7 @@ class DeviceRuntime:
             index_of = {}
             row_entries = []
             for step in builder.plan:
-                ids = list(tokenizer.encode(step.text))
+                ids = list(step.token_ids) if step.token_ids is not None else list(tokenizer.encode(step.text))
                 if len(ids) > limit:
                     raise _Unsupported("reference longer than the native limit needs bounded encoding")
                 e = len(entries)
@@ -448,19 +537,47 @@ class DeviceRuntime:
         seq_len = max((len(c.token_ids) for c in chunks), default=1)
         n_waves = max((e.wave for e in entries), default=-1) + 1
         seq = 0
-        order = []
+        waves: list[list[int]] = []
         for wave in range(n_waves):
+            members = []
             for e in entries:
                 if e.wave == wave:
                     for c in e.chunks:
                         chunks[c].seq = seq
-                        order.append(c)
+                        members.append(c)
                         seq += 1
+            waves.append(members)
+        return BatchPlan(metadata_rows, caches, builders, entries, chunks, rows, seq_len, waves)
+
+    def prefetch(self, metadata_rows: list[dict], tokenizer=None, resolver_config=None) -> None:
+        """Plan the NEXT batch on the host while the device still runs the current one.
+
+        Planning needs no model state (only the tokenizer, resolver settings and the
+        rows' reference tables), so doing it ahead is exact; ``build_memory`` picks
+        the plan up when it is called with the same rows.
+        """
+        tokenizer = tokenizer or self._last_tokenizer
+        if tokenizer is None:
+            return
+        resolver_config = resolver_config if resolver_config is not None else self._last_resolver
+        try:
+            self._prefetched = self.plan_batch(metadata_rows, tokenizer, resolver_config)
+        except _Unsupported:
+            self._prefetched = None
+
+    def build_memory(self, metadata_rows: list[dict], tokenizer, resolver_config=None):
+        """Plan (or take the prefetched plan of) the batch, then encode all rows' chunks wave by wave."""
+        self._last_tokenizer, self._last_resolver = tokenizer, resolver_config
+        plan = self._prefetched
+        self._prefetched = None
+        if plan is None or plan.metadata_rows is not metadata_rows:
+            plan = self.plan_batch(metadata_rows, tokenizer, resolver_config)
+        caches, builders, entries, chunks, rows, seq_len = (plan.caches, plan.builders, plan.entries, plan.chunks,
+                                                            plan.rows, plan.seq_len)
         memory = BatchMemory(self, entries, chunks, rows, seq_len, self.device)
         with torch.no_grad():
             start = 0
-            for wave in range(n_waves):
-                wave_chunks = [c for c in order if entries[chunks[c].entry].wave == wave]
+            for wave_chunks in plan.waves:
                 if not wave_chunks:
                     continue
                 self._encode_wave(memory, wave_chunks, start)
@@ -472,15 +589,20 @@ class DeviceRuntime:
         cfg = self.cfg
         n = len(wave_chunks)
         L = memory.seq_len
-        ids = torch.zeros((n, L), dtype=torch.long)
-        valid = torch.zeros((n, L), dtype=torch.uint8)
-        last = torch.zeros(n, dtype=torch.long)
+        import numpy as np
+
+        lens = [len(memory.chunks[c].token_ids) for c in wave_chunks]
+        ids_host = np.zeros((n, L), dtype=np.int32)
         for i, c in enumerate(wave_chunks):
-            toks = memory.chunks[c].token_ids
-            ids[i, : len(toks)] = torch.tensor(toks, dtype=torch.long)
-            valid[i, : len(toks)] = 1
-            last[i] = len(toks) - 1
-        ids, valid, last = (t.to(self.device, non_blocking=True) for t in (ids, valid, last))
+            ids_host[i, : lens[i]] = memory.chunks[c].token_ids
+        # each chunk is its own native call: its budget uses its own (unpadded) length
+        limit = cfg.effective_model_max_context_tokens - cfg.context_safety_reserve_tokens
+        cap = cfg.max_materialized_memory_tokens
+        budgets = [max(0, min(limit - k, cap) if cap is not None else limit - k) for k in lens]
+        ids, lengths, budget = _upload(self.device, ids_host, lens, budgets)
+        ids = ids.view(n, L).long()
+        last = (lengths - 1).long()
+        valid = (torch.arange(L, device=self.device)[None, :] < lengths[:, None]).to(torch.uint8)
         positions = torch.arange(L, device=self.device).expand(n, L)
         x = self.embed(ids, positions)
         entries = memory.entries
@@ -490,76 +612,31 @@ class DeviceRuntime:
             rows_entries = [list(entries[memory.chunks[c].entry].visible)
                             if entries[memory.chunks[c].entry].use_memory else [] for c in wave_chunks]
             namespace = Namespace(rows_entries, entries, memory.chunks, self.device)
-        # each chunk is its own native call: its budget uses its own (unpadded) length
-        lengths = torch.tensor([len(memory.chunks[c].token_ids) for c in wave_chunks], dtype=torch.int32)
-        budget = cfg.effective_model_max_context_tokens - lengths - cfg.context_safety_reserve_tokens
-        if cfg.max_materialized_memory_tokens is not None:
-            budget = budget.clamp_max(cfg.max_materialized_memory_tokens)
-        budget = budget.clamp_min(0).to(self.device, non_blocking=True)
         rows = slice(first_seq * L, (first_seq + n) * L)
         self.run_blocks(x, n, L, valid, namespace, memory, stop_after_kv=True, pool_rows=rows, budget=budget,
                         query_rows=last)
         self._pool_gists(memory, wave_chunks)
 
     def _pool_gists(self, memory: BatchMemory, wave_chunks: list[int]) -> None:
+        """One launch builds the wave's gists for every layer, written in place into the cache tables."""
         cfg = self.cfg
         d = cfg.d_model
         ext = _ext.require()
-        idx = torch.tensor(wave_chunks, dtype=torch.long, device=self.device)
-        start = memory.chunk_pool_row[idx].contiguous()
-        length = memory.chunk_len[idx].contiguous()
-        if cfg.gist_mode == "kmeans":
-            stream = self._kmeans_stream([len(memory.chunks[c].token_ids) for c in wave_chunks])
-        for li in range(cfg.n_layers):
-            pk, pv = memory.k_view(li, d), memory.v_view(li, d)
-            if cfg.gist_mode == "mean":
-                gk, gv, gn = ext.gist_mean(pk, pv, start, length)
-                memory.gist_k[li][idx, 0] = gk
-                memory.gist_v[li][idx, 0] = gv
-                memory.gists[li][idx, 0] = gn
-                memory.gist_count[li][idx] = 1
-            else:
-                G = memory.G
-                gk, gv, count, _occ, _it, status = ext.gist_kmeans(
-                    pk, pv, start, length, G, cfg.gist_kmeans_max_iters, float(cfg.gist_kmeans_tol),
-                    bool(cfg.gist_kmeans_normalize), cfg.gist_kmeans_init == "kmeans++",
-                    cfg.gist_kmeans_empty_cluster_policy == "farthest", *stream)
-                memory.gist_k[li][idx] = gk
-                memory.gist_v[li][idx] = gv
-                memory.gists[li][idx] = torch.nn.functional.normalize(gk, dim=-1, eps=1e-12)
-                memory.gist_count[li][idx] = count
-
-    def _kmeans_stream(self, lengths: list[int]):
-        """Per-chunk random-stream tables for the k-means kernel (cached per chunk length)."""
-        cfg = self.cfg
-        G = max(cfg.gists_per_chunk, 1)
-        firsts, offs, draws, idx_flat = [], [], [], []
-        cursor = 0
-        cache = {}
-        for n in lengths:
-            if n not in cache:
-                count = min(G, n)
-                if cfg.gist_kmeans_init == "kmeans++":
-                    first, exp = kmeanspp_random_stream(n, count, cfg.gist_kmeans_seed)
-                    cache[n] = (first, exp.flatten(), [])
-                else:
-                    perm = torch.randperm(n, generator=local_generator(cfg.gist_kmeans_seed))[:count]
-                    cache[n] = (0, torch.zeros(0), perm.tolist())
-            first, exp, perm = cache[n]
-            if cfg.gist_kmeans_init == "kmeans++":
-                firsts.append(first)
-                offs.append(cursor)
-                draws.append(exp)
-                cursor += exp.numel()
-            else:
-                firsts.append(len(idx_flat))
-                idx_flat.extend(perm)
-                offs.append(0)
-        dev = self.device
-        exp_all = torch.cat(draws) if draws else torch.zeros(1)
-        return (torch.tensor(firsts, dtype=torch.int32, device=dev),
-                torch.tensor(idx_flat or [0], dtype=torch.int32, device=dev), exp_all.float().to(dev),
-                torch.tensor(offs, dtype=torch.int64, device=dev))
+        lengths = [len(memory.chunks[c].token_ids) for c in wave_chunks]
+        rows = [memory.chunks[c].seq * memory.seq_len for c in wave_chunks]
+        pk, pv = memory.k_all(d), memory.v_all(d)
+        if cfg.gist_mode == "mean":
+            start, length, dest = _upload(self.device, rows, lengths, wave_chunks)
+            ext.gist_mean_into(pk, pv, start, length, dest, memory.gist_k_all, memory.gist_v_all, memory.gists_all,
+                               memory.gist_count_all)
+            return
+        firsts, offs = self.kmeans_tables.lookup(lengths)
+        start, length, dest, first, off = _upload(self.device, rows, lengths, wave_chunks, firsts, offs)
+        ext.gist_kmeans_into(pk, pv, start, length, dest, memory.gist_k_all, memory.gist_v_all, memory.gists_all,
+                             memory.gist_count_all, max(lengths), cfg.gist_kmeans_max_iters,
+                             float(cfg.gist_kmeans_tol), bool(cfg.gist_kmeans_normalize),
+                             cfg.gist_kmeans_init == "kmeans++", cfg.gist_kmeans_empty_cluster_policy == "farthest",
+                             first, self.kmeans_tables.idx, self.kmeans_tables.draws, off, None)
 
     # -- prompt forward + loss ----------------------------------------------------
     def prompt_forward(self, input_ids, attention_mask, memory: BatchMemory | None, position_offset=0):
@@ -647,11 +724,16 @@ def attach_device_runtime(model: TinyPRAModel) -> TinyPRAModel:
         if isinstance(optimizer, FusedAdamW):
             optimizer.max_grad_norm = train_config.max_grad_norm
             optimizer.step()
-            return float(optimizer.last_norm.item())
+            return optimizer.last_norm  # 0-dim device tensor: read it only when it is logged
         raise RuntimeError("device path expects the fused optimizer")
+
+    def prefetch_batch(batch):
+        if isinstance(batch, dict) and "metadata" in batch:
+            runtime.prefetch(batch["metadata"])
 
     model.build_optimizer = build_optimizer
     model.optimizer_step_hook = optimizer_step_hook
+    model.prefetch_batch = prefetch_batch
     model.after_load_state = runtime.flat.refresh_shadow
     original_load = model.load_state_dict
 

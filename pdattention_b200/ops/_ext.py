@@ -32,7 +32,8 @@ _module = None
 # Kernels launched per extension call (used to report how many of this library's
 # kernels ran inside a timed region).
 KERNELS_PER_CALL = {"attention_fwd": 1, "attention_bwd": 3, "gemm": 1, "norm_fwd": 1, "norm_bwd": 3, "colsum": 2,
-                    "cross_entropy": 1, "grad_norm": 2, "adamw": 1, "gist_mean": 1, "gist_kmeans": 1, "route": 1}
+                    "cross_entropy": 1, "grad_norm": 2, "adamw": 1, "gist_mean": 1, "gist_kmeans": 1, "route": 1,
+                    "gist_mean_into": 1, "gist_kmeans_into": 1}
 
 
 class LaunchCounter:

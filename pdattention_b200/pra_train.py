@@ -413,12 +413,14 @@ def train_pra_model(*, cfg: PRAConfig, train_config: TrainConfig, datamodule, mo
 
 
 def training_step(model, batch: dict, device: str, tokenizer, optimizer, *, resolver_config=None, cache_config=None,
-                  scheduler=None, max_grad_norm: float = 1.0) -> tuple[torch.Tensor, dict]:
+                  scheduler=None, max_grad_norm: float = 1.0, next_batch: dict | None = None) -> tuple[torch.Tensor, dict]:
     """One optimizer step on one batch: cache build, routed forward, loss, backward, clip, update.
 
     This is the unit the training engine repeats; it is public so drivers and
     benchmarks run exactly the code path users get.  Returns ``(loss, info)``
-    with the loss still on the device (read it when needed).
+    with the loss still on the device (read it when needed).  With ``next_batch``
+    a device-path model plans that batch's cache build on the host while this
+    step's kernels run.
     """
     resolver_config = ResolverServiceConfig.from_value(resolver_config)
     cache_config = CacheServiceConfig.from_value(cache_config)
@@ -434,6 +436,9 @@ def training_step(model, batch: dict, device: str, tokenizer, optimizer, *, reso
         optimizer.step()
     if scheduler is not None:
         scheduler.step()
+    prefetch = getattr(model, "prefetch_batch", None)
+    if next_batch is not None and prefetch is not None:
+        prefetch(next_batch)
     return loss, info
 
 

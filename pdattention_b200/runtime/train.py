@@ -35,6 +35,9 @@ from .logging import build_logger
 from .metrics import DeviceTimer, RunningAverages, cuda_memory_allocated, grad_norm, perplexity
 
 
+_END = object()  # end-of-loader sentinel for the one-batch lookahead
+
+
 def _rank() -> int:
     if torch.distributed.is_available() and torch.distributed.is_initialized():
         return torch.distributed.get_rank()
@@ -278,7 +281,14 @@ def train_model(*, model, train_config, train_loader, val_loader=None, test_load
             pending = False
             return norm
 
-        for batch_idx, batch in enumerate(train_loader):
+        prefetch = getattr(model, "prefetch_batch", None)
+        iterator = iter(train_loader)
+        upcoming = next(iterator, _END)
+        batch_idx = -1
+        while upcoming is not _END:
+            batch = upcoming
+            batch_idx += 1
+            upcoming = next(iterator, _END)
             if sync_every_batch:
                 synchronize()
             timer = DeviceTimer(state.device)
@@ -297,6 +307,8 @@ def train_model(*, model, train_config, train_loader, val_loader=None, test_load
             pending = True
             did_step = (batch_idx + 1) % accum == 0
             norm = optimizer_step() if did_step else 0.0
+            if prefetch is not None and upcoming is not _END:
+                prefetch(upcoming)  # host planning of the next batch overlaps this step's kernels
             timer.stop()
             loss_value = float(loss.detach().float().cpu())  # the step's one host read
             if sync_every_batch:

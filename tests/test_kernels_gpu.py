@@ -226,7 +226,7 @@ def test_gist_mean_and_kmeans_match_strategies(ext):
     out = ext.gist_kmeans(pk, pv, start, length, 2, cfg.gist_kmeans_max_iters, cfg.gist_kmeans_tol, True, True, True,
                           torch.tensor(firsts, dtype=torch.int32, device="cuda"),
                           torch.zeros(1, dtype=torch.int32, device="cuda"), torch.cat(draws).cuda(),
-                          torch.tensor(offs, dtype=torch.int64, device="cuda"))
+                          torch.tensor(offs, dtype=torch.int32, device="cuda"))
     gk2, gv2, count = out[0], out[1], out[2]
     ctx = SimpleNamespace(level="chunk", token_ids=(), tokenizer=None, ref_end_token="", gru_pooler=None)
     for c, (s, n) in enumerate(zip(starts, lens)):
