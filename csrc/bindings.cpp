@@ -3,6 +3,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cmath>
 #include <vector>
 
 #include "kernels.h"
@@ -398,11 +399,12 @@ std::vector<torch::Tensor> route(torch::Tensor query, torch::Tensor gists, torch
                                  torch::Tensor chunk_len, torch::Tensor chunk_pool_row, int64_t k_ref, int64_t k_chunk,
                                  int64_t gist_agg, int64_t ref_agg, double threshold, int64_t budget, bool gist_only,
                                  bool full_reference, bool deduplicate, int64_t max_sel, int64_t max_mem,
-                                 c10::optional<torch::Tensor> budget_rows) {
+                                 c10::optional<torch::Tensor> budget_rows, c10::optional<torch::Tensor> query_rows) {
   c10::cuda::CUDAGuard guard(query.device());
   expect(query, at::kBFloat16, "query");
   expect(gists, at::kFloat, "gists");
-  TORCH_CHECK(query.dim() == 2 && query.stride(1) == 1, "query must be [B, >=D] row-major");
+  // query: [B, >=D] (one query per row) or [B, T, >=D] with query_rows [B] int32 picking the token
+  TORCH_CHECK((query.dim() == 2 || query.dim() == 3) && query.stride(-1) == 1, "query must be [B, (T,) >=D]");
   TORCH_CHECK(gists.dim() == 3 && gists.is_contiguous(), "gists must be [C, G, D] contiguous");
   RouteParams p{};
   p.B = query.size(0);
@@ -410,6 +412,12 @@ std::vector<torch::Tensor> route(torch::Tensor query, torch::Tensor gists, torch
   p.G = gists.size(1);
   p.query = ptr<const __nv_bfloat16>(query);
   p.query_stride = query.stride(0);
+  if (query.dim() == 3) {
+    TORCH_CHECK(query_rows.has_value() && query_rows->scalar_type() == at::kInt && query_rows->numel() == p.B,
+                "a [B, T, D] query needs int32 query_rows [B]");
+    p.query_row = ptr<const int>(*query_rows);
+    p.query_row_stride = query.stride(1);
+  }
   p.gists = ptr<const float>(gists);
   p.gist_count = ptr<const int>(gist_count);
   p.row_pos_off = ptr<const int>(row_pos_off);
@@ -462,6 +470,85 @@ std::vector<torch::Tensor> route(torch::Tensor query, torch::Tensor gists, torch
 
 }  // namespace
 
+// ---------------------------------------------------------------- native block-stack executor
+// Forward of a stack of pre-LN GPT blocks (LN -> QKV -> [route] -> attention -> O-proj + residual ->
+// LN -> up-GELU -> down + residual) driven entirely from C++: no Python, no autograd records,
+// one stream.  Used by the cache build (every layer's QKV lands in the K/V pool) and by
+// no-grad forwards.  weights holds 12 tensors per layer: ln1 w/b, qkv w/b, o w/b, ln2 w/b,
+// up w/b, down w/b (bf16).  ns (empty = no memory) holds the routing namespace: row_pos_off,
+// row_ref_off, ref_pos_off, pos_chunk, pos_ref, pos_rank, chunk_start, chunk_len,
+// chunk_pool_row; route_cfg = {k_ref, k_chunk, gist_agg, ref_agg, threshold, budget,
+// gist_only, full_reference, deduplicate, max_sel, max_mem}.
+// pool (optional) receives every layer's QKV rows; mem_pool is the [L, rows, 3D] pool the
+// routed memory keys are read from.
+// Returns {x, then per routed layer: mem_idx, ints, sel_i, sel_f}.
+std::vector<torch::Tensor> stack_forward(torch::Tensor x, int64_t B, int64_t T, std::vector<torch::Tensor> weights,
+                                         int64_t heads, int64_t head_dim, double eps,
+                                         c10::optional<torch::Tensor> key_valid, c10::optional<torch::Tensor> pool,
+                                         int64_t pool_row0, bool stop_after_kv, c10::optional<torch::Tensor> mem_pool,
+                                         std::vector<torch::Tensor> ns,
+                                         c10::optional<torch::Tensor> gists, c10::optional<torch::Tensor> gist_count,
+                                         c10::optional<torch::Tensor> gist_kv, c10::optional<torch::Tensor> budget_rows,
+                                         c10::optional<torch::Tensor> query_rows, std::vector<double> route_cfg) {
+  c10::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(weights.size() % 12 == 0, "stack_forward needs 12 weight tensors per layer");
+  const int64_t L = weights.size() / 12;
+  const int64_t D = heads * head_dim;
+  const int64_t M = B * T;
+  TORCH_CHECK(x.dim() == 2 && x.size(0) == M && x.size(1) == D && x.is_contiguous(), "x must be [B*T, D]");
+  const bool routed = !ns.empty();
+  if (routed) {
+    TORCH_CHECK(ns.size() == 9 && gists.has_value() && gist_count.has_value() && route_cfg.size() == 11,
+                "routing needs 9 namespace tensors, gists, gist_count and 11 settings");
+    TORCH_CHECK(mem_pool.has_value() || gist_kv.has_value(), "routing needs the memory K/V pool");
+  }
+  const bool gist_only = routed && route_cfg[6] != 0.0;
+  const double scale = 1.0 / std::sqrt((double)head_dim);
+  std::vector<torch::Tensor> out{x};
+  for (int64_t l = 0; l < L; ++l) {
+    const torch::Tensor* w = weights.data() + 12 * l;
+    auto h = norm_fwd(x, w[0], w[1], eps, false)[0];
+    torch::Tensor qkv = pool.has_value() ? pool->select(0, l).narrow(0, pool_row0, M)
+                                         : torch::empty({M, 3 * D}, x.options());
+    gemm("tn", h, w[2], c10::nullopt, qkv, w[3], c10::nullopt, 1.0, 0.0, c10::nullopt);
+    if (stop_after_kv && l == L - 1) break;
+    auto qkv3 = qkv.view({B, T, 3 * D});
+    c10::optional<torch::Tensor> mk, mv, mi, ml;
+    if (routed) {
+      auto r = route(qkv3.narrow(2, 0, D), gists->select(0, l), gist_count->select(0, l), ns[0], ns[1], ns[2], ns[3],
+                     ns[4], ns[5], ns[6], ns[7], ns[8], (int64_t)route_cfg[0], (int64_t)route_cfg[1],
+                     (int64_t)route_cfg[2], (int64_t)route_cfg[3], route_cfg[4], (int64_t)route_cfg[5], gist_only,
+                     route_cfg[7] != 0.0, route_cfg[8] != 0.0, (int64_t)route_cfg[9], (int64_t)route_cfg[10],
+                     budget_rows, query_rows.has_value() ? query_rows : c10::optional<torch::Tensor>(
+                                                               torch::full({B}, (int)(T - 1), x.options().dtype(at::kInt))));
+      if (gist_only) {
+        mk = gist_kv->select(0, 0).select(0, l);
+        mv = gist_kv->select(0, 1).select(0, l);
+      } else {
+        auto layer_pool = mem_pool->select(0, l);
+        mk = layer_pool.narrow(1, D, D);
+        mv = layer_pool.narrow(1, 2 * D, D);
+      }
+      mi = r[0];
+      ml = r[1].select(0, 0);
+      out.insert(out.end(), r.begin(), r.end());
+    }
+    auto a = attention_fwd(qkv3.narrow(2, 0, D), qkv3.narrow(2, D, D), qkv3.narrow(2, 2 * D, D), heads, heads,
+                           head_dim, mk, mv, mi, ml, key_valid, scale)[0];
+    auto x1 = torch::empty_like(x);
+    gemm("tn", a.view({M, D}), w[4], x, x1, w[5], c10::nullopt, 1.0, 1.0, c10::nullopt);
+    auto h2 = norm_fwd(x1, w[6], w[7], eps, false)[0];
+    const int64_t F = w[8].size(0);
+    auto z = torch::empty({M, F}, x.options()), u = torch::empty({M, F}, x.options());
+    gemm("tn_gelu", h2, w[8], c10::nullopt, u, w[9], z, 1.0, 0.0, c10::nullopt);
+    auto x2 = torch::empty_like(x);
+    gemm("tn", u, w[10], x1, x2, w[11], c10::nullopt, 1.0, 1.0, c10::nullopt);
+    x = x2;
+  }
+  out[0] = x;
+  return out;
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "PRA sm_100a kernels";
   m.def("attention_fwd", &attention_fwd);
@@ -478,4 +565,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gist_mean_into", &gist_mean_into);
   m.def("gist_kmeans_into", &gist_kmeans_into);
   m.def("route", &route);
+  m.def("stack_forward", &stack_forward);
 }

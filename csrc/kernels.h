@@ -113,8 +113,10 @@ cudaError_t pra_gist_kmeans(const GistArgs& args, int layers, cudaStream_t strea
 // ---- row-local routing + selection + materialisation plan (routing.cu) ----------------
 struct RouteParams {
   int B, D, G;
-  const __nv_bfloat16* query;  // [B, >= D] routing queries
+  const __nv_bfloat16* query;  // row b's query: query + b * query_stride (+ query_row[b] * query_row_stride)
   int64_t query_stride;
+  const int* query_row;        // [B] token row of each query inside its sequence, or null
+  int64_t query_row_stride;
   const float* gists;          // [C, G, D] L2-normalised
   const int* gist_count;       // [C]
   // Namespace of row b: positions [row_pos_off[b], row_pos_off[b+1]); position q names the

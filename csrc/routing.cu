@@ -115,9 +115,11 @@ __global__ void __launch_bounds__(NT) route_kernel(RouteParams p) {
   if (nc <= 0 || nr <= 0 || nc > MAX_ROW_CHUNKS || nr > MAX_ROW_REFS || p.k_ref <= 0 || p.k_chunk <= 0) return;
 
   // 1. normalised query
+  const __nv_bfloat16* qrow =
+      p.query + (int64_t)b * p.query_stride + (p.query_row ? (int64_t)p.query_row[b] * p.query_row_stride : 0);
   float sq = 0.f;
   for (int d = threadIdx.x; d < p.D; d += NT) {
-    const float v = __bfloat162float(p.query[(int64_t)b * p.query_stride + d]);
+    const float v = __bfloat162float(qrow[d]);
     qn[d] = v;
     sq += v * v;
   }

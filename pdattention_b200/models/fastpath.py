@@ -455,6 +455,11 @@ class DeviceRuntime:
         """
         cfg = self.cfg
         d = cfg.d_model
+        if query_rows is not None:
+            query_rows = query_rows.to(torch.int32)
+        if not torch.is_grad_enabled():
+            return self._run_blocks_native(x, b, t, key_valid, routing, memory, stop_after_kv, pool_rows, budget,
+                                           query_rows)
         for li, layer in enumerate(self.layers):
             h = layer_norm(x, layer["ln1"])
             if pool_rows is not None:
@@ -473,27 +478,73 @@ class DeviceRuntime:
             x = mlp(layer_norm(x, layer["ln2"]), x, layer["up"], layer["down"])
         return x
 
+    def _route_settings(self, budget) -> tuple[list[float], torch.Tensor | None]:
+        """(route_cfg list of the native executor / route binding, per-row budget tensor or None)."""
+        cfg = self.cfg
+        max_sel = max(1, min(256, cfg.top_k_references * cfg.top_k_chunks_per_reference
+                             if cfg.detail_materialization != "full_reference" else 256))
+        budget_rows = budget if torch.is_tensor(budget) else None
+        scalar_budget = int(budget) if budget_rows is None else cfg.effective_model_max_context_tokens
+        settings = [min(cfg.top_k_references, 64), cfg.top_k_chunks_per_reference, _AGG[cfg.gist_score_aggregation],
+                    _AGG[cfg.reference_score_aggregation], float(cfg.trigger_threshold), scalar_budget,
+                    float(cfg.detail_materialization == "gist_only"),
+                    float(cfg.detail_materialization == "full_reference"),
+                    float(cfg.overlap_materialization == "deduplicate"), max_sel, max(scalar_budget, 1)]
+        return settings, budget_rows
+
+    def _stack_weights(self) -> list[torch.Tensor]:
+        if getattr(self, "_stack_weight_list", None) is None:
+            out = []
+            for layer in self.layers:
+                for name in ("ln1", "qkv", "o", "ln2", "up", "down"):
+                    out += [layer[name].w, layer[name].b]
+            self._stack_weight_list = out
+        return self._stack_weight_list
+
+    def _run_blocks_native(self, x, b, t, key_valid, routing, memory, stop_after_kv, pool_rows, budget, query_rows):
+        """The whole block stack in one native call (no autograd): cache build and no-grad forwards."""
+        cfg = self.cfg
+        d = cfg.d_model
+        ext = _ext.require()
+        routed = routing is not None and not routing.empty
+        ns, gists, counts, gist_kv, budget_rows, settings = [], None, None, None, None, []
+        if routed:
+            ns = [routing.row_pos_off, routing.row_ref_off, routing.ref_pos_off, routing.pos_chunk, routing.pos_ref,
+                  routing.pos_rank, memory.chunk_start, memory.chunk_len, memory.chunk_pool_row]
+            gists, counts = memory.gists_all, memory.gist_count_all
+            settings, budget_rows = self._route_settings(budget)
+            if cfg.detail_materialization == "gist_only":
+                gist_kv = torch.stack([memory.gist_k_all, memory.gist_v_all]).view(
+                    2, cfg.n_layers, -1, d).bfloat16()
+        pool = memory.pool if pool_rows is not None else None
+        row0 = pool_rows.start if pool_rows is not None else 0
+        out = ext.stack_forward(x.contiguous(), b, t, self._stack_weights(), cfg.n_heads, self.head_dim, 1e-5,
+                                key_valid, pool, row0, stop_after_kv, memory.pool if routed else None, ns, gists,
+                                counts, gist_kv, budget_rows,
+                                query_rows, settings)
+        n_layers = cfg.n_layers
+        per_layer = 7 + (1 if routed else 0)
+        _ext.add_launches("stack_forward", n_layers * per_layer - (per_layer - 2 if stop_after_kv else 0))
+        if routed:
+            for li in range(n_layers - (1 if stop_after_kv else 0)):
+                mem_idx, ints, sel_i, sel_f = out[1 + 4 * li: 5 + 4 * li]
+                self.last_routing[li] = LayerRouting(mem_idx, ints, sel_i, sel_f)
+        return None if stop_after_kv else out[0]
+
     def route(self, li: int, qkv3: torch.Tensor, ns: Namespace, memory: BatchMemory, budget,
               query_rows: torch.Tensor | None) -> MemoryView:
         cfg = self.cfg
         d = cfg.d_model
+        settings, budget_rows = self._route_settings(budget)
+        gist_only = bool(settings[6])
         if query_rows is None:
-            query = qkv3[:, -1, :d]
-        else:
-            query = qkv3[torch.arange(qkv3.shape[0], device=qkv3.device), query_rows, :d]
-        max_sel = max(1, min(256, cfg.top_k_references * cfg.top_k_chunks_per_reference
-                             if cfg.detail_materialization != "full_reference" else 256))
-        budget_rows = budget if torch.is_tensor(budget) else None
-        scalar_budget = int(budget) if budget_rows is None else self.cfg.effective_model_max_context_tokens
-        max_mem = max(scalar_budget, 1)
-        gist_only = cfg.detail_materialization == "gist_only"
+            query_rows = torch.full((qkv3.shape[0],), qkv3.shape[1] - 1, dtype=torch.int32, device=qkv3.device)
         mem_idx, ints, sel_i, sel_f = _ext.require().route(
-            query, memory.gists[li], memory.gist_count[li], ns.row_pos_off, ns.row_ref_off, ns.ref_pos_off,
+            qkv3[:, :, :d], memory.gists[li], memory.gist_count[li], ns.row_pos_off, ns.row_ref_off, ns.ref_pos_off,
             ns.pos_chunk, ns.pos_ref, ns.pos_rank, memory.chunk_start, memory.chunk_len, memory.chunk_pool_row,
-            min(cfg.top_k_references, 64), cfg.top_k_chunks_per_reference, _AGG[cfg.gist_score_aggregation],
-            _AGG[cfg.reference_score_aggregation], float(cfg.trigger_threshold), scalar_budget, gist_only,
-            cfg.detail_materialization == "full_reference", cfg.overlap_materialization == "deduplicate", max_sel,
-            max_mem, budget_rows)
+            int(settings[0]), int(settings[1]), int(settings[2]), int(settings[3]), settings[4], int(settings[5]),
+            gist_only, bool(settings[7]), bool(settings[8]), int(settings[9]), int(settings[10]), budget_rows,
+            query_rows)
         self.last_routing[li] = LayerRouting(mem_idx, ints, sel_i, sel_f)
         if gist_only:
             gk = memory.gist_k[li].view(-1, d).bfloat16()
@@ -601,7 +652,7 @@ class DeviceRuntime:
         budgets = [max(0, min(limit - k, cap) if cap is not None else limit - k) for k in lens]
         ids, lengths, budget = _upload(self.device, ids_host, lens, budgets)
         ids = ids.view(n, L).long()
-        last = (lengths - 1).long()
+        last = lengths - 1
         valid = (torch.arange(L, device=self.device)[None, :] < lengths[:, None]).to(torch.uint8)
         positions = torch.arange(L, device=self.device).expand(n, L)
         x = self.embed(ids, positions)
@@ -850,7 +901,7 @@ def routing_selftest(device, seed: int = 0) -> None:
         ns.ref_pos_off, ns.pos_chunk, ns.pos_ref, ns.pos_rank, as_int([c.token_start for c in chunks]),
         as_int([len(c.token_ids) for c in chunks]), as_int([c.seq * seq_len for c in chunks]), cfg.top_k_references,
         cfg.top_k_chunks_per_reference, 0, 0, float(cfg.trigger_threshold), budget, False, False, True, 16, budget,
-        None)
+        None, None)
     mem_idx, ints, sel_i, sel_f = mem_idx.cpu(), ints.cpu(), sel_i.cpu(), sel_f.cpu()
     q_bf = query.bfloat16().float()
     for row in range(3):

@@ -33,7 +33,8 @@ _module = None
 # kernels ran inside a timed region).
 KERNELS_PER_CALL = {"attention_fwd": 1, "attention_bwd": 3, "gemm": 1, "norm_fwd": 1, "norm_bwd": 3, "colsum": 2,
                     "cross_entropy": 1, "grad_norm": 2, "adamw": 1, "gist_mean": 1, "gist_kmeans": 1, "route": 1,
-                    "gist_mean_into": 1, "gist_kmeans_into": 1}
+                    "gist_mean_into": 1, "gist_kmeans_into": 1,
+                    "stack_forward": 0}  # stack_forward: counted per layer by its caller
 
 
 class LaunchCounter:
@@ -64,6 +65,13 @@ class LaunchCounter:
 
 
 _counter: LaunchCounter | None = None
+
+
+def add_launches(name: str, count: int) -> None:
+    """Record ``count`` kernel launches made inside one native call (e.g. the block-stack executor)."""
+    if _counter is not None and _counter.enabled:
+        _counter.launches += count
+        _counter.calls[name] = _counter.calls.get(name, 0) + 1
 
 
 def cutlass_include_dirs() -> list[str]:

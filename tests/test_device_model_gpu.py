@@ -72,3 +72,28 @@ def test_checkpoint_roundtrip_keeps_reference_layout(cuda, tmp_path):
     attach_device_runtime(other)
     other.load_state_dict(state)
     assert torch.equal(other._device_runtime.flat.shadow, model._device_runtime.flat.shadow)
+
+
+def test_native_stack_executor_matches_autograd_path(cuda, tmp_path):
+    """The C++ block-stack executor (no-grad forwards, cache build) equals the autograd path."""
+    torch.manual_seed(3)
+    tok, batch = tiny_batch(Path(tmp_path))
+    model = TinyPRAModel(tiny_config(tok.vocab_size)).to(cuda)
+    attach_device_runtime(model)
+    rt = model._device_runtime
+    memory, _, _ = rt.build_memory(batch["metadata"], tok, ResolverServiceConfig())
+    ids = batch["input_ids"].to(cuda)
+    mask = batch["attention_mask"].to(cuda)
+    with torch.enable_grad():
+        ref = rt.prompt_forward(ids, mask, memory).float()
+        ref_routing = {k: v.mem_idx.clone() for k, v in rt.last_routing.items()}
+        ref_lens = {k: v.ints[0].clone() for k, v in rt.last_routing.items()}
+    with torch.no_grad():
+        got = rt.prompt_forward(ids, mask, memory).float()
+    assert set(rt.last_routing) == set(ref_routing)
+    for li, routing in rt.last_routing.items():
+        assert torch.equal(routing.ints[0], ref_lens[li])
+        for row in range(ids.shape[0]):
+            n = int(ref_lens[li][row])
+            assert torch.equal(routing.mem_idx[row, :n], ref_routing[li][row, :n])
+    assert torch.allclose(got, ref, atol=2e-2, rtol=2e-2), (got - ref).abs().max()
