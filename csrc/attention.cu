@@ -94,17 +94,28 @@ __device__ __forceinline__ KeyBlock key_block(int i, int n_mem_blocks) {
   return i < n_mem_blocks ? KeyBlock{true, i * BN} : KeyBlock{false, (i - n_mem_blocks) * BN};
 }
 
-__device__ __forceinline__ bool key_visible(const Params& p, int b, const KeyBlock& kb, int key_off, int query,
-                                            int mem_len) {
+// svalid: the block's key-padding mask staged in shared memory (null without a mask).
+__device__ __forceinline__ bool key_visible(const Params& p, const KeyBlock& kb, int key_off, int query, int mem_len,
+                                            const uint8_t* svalid) {
   const int key = kb.start + key_off;
   if (kb.memory) return key < mem_len;
   if (key >= p.T || key > query) return false;
-  return p.key_valid == nullptr || p.key_valid[(int64_t)b * p.T + key] != 0;
+  return svalid == nullptr || svalid[key_off] != 0;
+}
+
+// True when every key of the block is visible to every query row >= q0 (no masking needed).
+__device__ __forceinline__ bool block_unmasked(const Params& p, const KeyBlock& kb, int q0, int mem_len) {
+  if (kb.memory) return kb.start + BN <= mem_len;
+  return p.key_valid == nullptr && kb.start + BN - 1 <= q0 && kb.start + BN <= p.T;
 }
 
 template <int D>
-__device__ __forceinline__ void load_keys(const Params& p, __nv_bfloat16* sk, __nv_bfloat16* sv, int b, int kvh,
-                                          const KeyBlock& kb, int mem_len) {
+__device__ __forceinline__ void load_keys(const Params& p, __nv_bfloat16* sk, __nv_bfloat16* sv, uint8_t* svalid,
+                                          int b, int kvh, const KeyBlock& kb, int mem_len) {
+  if (!kb.memory && p.key_valid != nullptr && threadIdx.x < BN) {
+    const int t = kb.start + threadIdx.x;
+    svalid[threadIdx.x] = t < p.T ? p.key_valid[(int64_t)b * p.T + t] : 0;
+  }
   if (kb.memory) {
     const int* idx = p.mem_idx + (int64_t)b * p.mem_max;
     load_tile<D>(sk, p.mem_k, [&](int r) -> const __nv_bfloat16* {
@@ -134,8 +145,11 @@ __global__ void __launch_bounds__(NT) fwd_kernel(Params p) {
   __nv_bfloat16* sq = reinterpret_cast<__nv_bfloat16*>(smem_raw);
   __nv_bfloat16* sk = sq + BM * LD;   // [2][BN][LD]
   __nv_bfloat16* sv = sk + 2 * BN * LD;
+  uint8_t* svalid = reinterpret_cast<uint8_t*>(sv + 2 * BN * LD);  // [2][BN]
 
-  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  // grid (H * B, query blocks): the longest (last, causal) query blocks are scheduled first
+  const int h = blockIdx.x % p.H, b = blockIdx.x / p.H;
+  const int qb = gridDim.y - 1 - blockIdx.y;
   const int kvh = h / (p.H / p.Hkv);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = qb * BM;
@@ -149,7 +163,7 @@ __global__ void __launch_bounds__(NT) fwd_kernel(Params p) {
     const int t = q0 + r;
     return t < p.T ? p.q + b * p.q_batch + t * p.q_row + h * D : nullptr;
   });
-  load_keys<D>(p, sk, sv, b, kvh, key_block(0, n_mem), mem_len);
+  load_keys<D>(p, sk, sv, svalid, b, kvh, key_block(0, n_mem), mem_len);
   cp_async_commit();
 
   float o_acc[D / 8][4];
@@ -162,8 +176,8 @@ __global__ void __launch_bounds__(NT) fwd_kernel(Params p) {
   for (int it = 0; it < n_blocks; ++it) {
     const int buf = it & 1;
     if (it + 1 < n_blocks) {
-      load_keys<D>(p, sk + (buf ^ 1) * BN * LD, sv + (buf ^ 1) * BN * LD, b, kvh, key_block(it + 1, n_mem),
-                   mem_len);
+      load_keys<D>(p, sk + (buf ^ 1) * BN * LD, sv + (buf ^ 1) * BN * LD, svalid + (buf ^ 1) * BN, b, kvh,
+                   key_block(it + 1, n_mem), mem_len);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
@@ -176,13 +190,15 @@ __global__ void __launch_bounds__(NT) fwd_kernel(Params p) {
     for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
     mma_abt<D>(s, sq + warp * 16 * LD, sk + buf * BN * LD);
     float mx[2] = {-INFINITY, -INFINITY};
+    const bool unmasked = block_unmasked(p, kb, q0, mem_len);
+    const uint8_t* valid = p.key_valid ? svalid + buf * BN : nullptr;
 #pragma unroll
     for (int nb = 0; nb < 8; ++nb) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int q = row_a + (e >> 1) * 8;
         const int key_off = nb * 8 + (lane & 3) * 2 + (e & 1);
-        if (!key_visible(p, b, kb, key_off, q, mem_len)) s[nb][e] = -INFINITY;
+        if (!unmasked && !key_visible(p, kb, key_off, q, mem_len, valid)) s[nb][e] = -INFINITY;
         mx[e >> 1] = fmaxf(mx[e >> 1], s[nb][e]);
       }
     }
@@ -269,8 +285,11 @@ __global__ void __launch_bounds__(NT) bwd_dq_kernel(Params p) {
   __nv_bfloat16* sdo = sq + BM * LD;
   __nv_bfloat16* sk = sdo + BM * LD;  // [2][BN][LD]
   __nv_bfloat16* sv = sk + 2 * BN * LD;
+  uint8_t* svalid = reinterpret_cast<uint8_t*>(sv + 2 * BN * LD);  // [2][BN]
 
-  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  // grid (H * B, query blocks): the longest (last, causal) query blocks are scheduled first
+  const int h = blockIdx.x % p.H, b = blockIdx.x / p.H;
+  const int qb = gridDim.y - 1 - blockIdx.y;
   const int kvh = h / (p.H / p.Hkv);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = qb * BM;
@@ -286,7 +305,7 @@ __global__ void __launch_bounds__(NT) bwd_dq_kernel(Params p) {
     const int t = q0 + r;
     return t < p.T ? p.dout + b * p.do_batch + t * p.do_row + h * D : nullptr;
   });
-  load_keys<D>(p, sk, sv, b, kvh, key_block(0, n_mem), mem_len);
+  load_keys<D>(p, sk, sv, svalid, b, kvh, key_block(0, n_mem), mem_len);
   cp_async_commit();
 
   const int row_a = q0 + warp * 16 + (lane >> 2);
@@ -306,8 +325,8 @@ __global__ void __launch_bounds__(NT) bwd_dq_kernel(Params p) {
   for (int it = 0; it < n_blocks; ++it) {
     const int buf = it & 1;
     if (it + 1 < n_blocks) {
-      load_keys<D>(p, sk + (buf ^ 1) * BN * LD, sv + (buf ^ 1) * BN * LD, b, kvh, key_block(it + 1, n_mem),
-                   mem_len);
+      load_keys<D>(p, sk + (buf ^ 1) * BN * LD, sv + (buf ^ 1) * BN * LD, svalid + (buf ^ 1) * BN, b, kvh,
+                   key_block(it + 1, n_mem), mem_len);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
@@ -323,6 +342,8 @@ __global__ void __launch_bounds__(NT) bwd_dq_kernel(Params p) {
     }
     mma_abt<D>(s, sq + warp * 16 * LD, sk + buf * BN * LD);
     mma_abt<D>(dp, sdo + warp * 16 * LD, sv + buf * BN * LD);
+    const bool unmasked = block_unmasked(p, kb, q0, mem_len);
+    const uint8_t* valid = p.key_valid ? svalid + buf * BN : nullptr;
 #pragma unroll
     for (int nb = 0; nb < 8; ++nb) {
 #pragma unroll
@@ -330,7 +351,7 @@ __global__ void __launch_bounds__(NT) bwd_dq_kernel(Params p) {
         const int r = e >> 1;
         const int q = row_a + r * 8;
         const int key_off = nb * 8 + (lane & 3) * 2 + (e & 1);
-        const bool vis = key_visible(p, b, kb, key_off, q, mem_len) && lse2[r] != -INFINITY;
+        const bool vis = (unmasked || key_visible(p, kb, key_off, q, mem_len, valid)) && lse2[r] != -INFINITY;
         const float pr = vis ? exp2f(s[nb][e] * sl2 - lse2[r]) : 0.f;
         s[nb][e] = pr * (dp[nb][e] - dlt[r]);  // dS (unscaled)
       }
@@ -365,7 +386,9 @@ __global__ void __launch_bounds__(NT) bwd_dkdv_kernel(Params p) {
   float* s_lse = reinterpret_cast<float*>(sdo + 2 * BM * LD);  // [2][BM]
   float* s_dlt = s_lse + 2 * BM;
 
-  const int kblk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  // grid (H * B, key blocks): the first key blocks (seen by the most queries) are scheduled first
+  const int h = blockIdx.x % p.H, b = blockIdx.x / p.H;
+  const int kblk = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int k0 = kblk * BN;
   const int n_q = (p.T + BM - 1) / BM;
@@ -471,9 +494,9 @@ __global__ void __launch_bounds__(NT) bwd_dkdv_kernel(Params p) {
 template <int D>
 cudaError_t launch_fwd(const Params& p, cudaStream_t st) {
   constexpr int LD = Smem<D>::LD;
-  const size_t smem = (size_t)(BM + 4 * BN) * LD * sizeof(__nv_bfloat16);
+  const size_t smem = (size_t)(BM + 4 * BN) * LD * sizeof(__nv_bfloat16) + 2 * BN;
   PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  dim3 grid((p.T + BM - 1) / BM, p.H, p.B);
+  dim3 grid(p.H * p.B, (p.T + BM - 1) / BM);
   fwd_kernel<D><<<grid, NT, smem, st>>>(p);
   return cudaGetLastError();
 }
@@ -487,16 +510,16 @@ cudaError_t launch_bwd(const Params& p, cudaStream_t st) {
     PRA_RETURN_IF_ERROR(cudaGetLastError());
   }
   {
-    const size_t smem = (size_t)(2 * BM + 4 * BN) * LD * sizeof(__nv_bfloat16);
+    const size_t smem = (size_t)(2 * BM + 4 * BN) * LD * sizeof(__nv_bfloat16) + 2 * BN;
     PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    dim3 grid((p.T + BM - 1) / BM, p.H, p.B);
+    dim3 grid(p.H * p.B, (p.T + BM - 1) / BM);
     bwd_dq_kernel<D><<<grid, NT, smem, st>>>(p);
     PRA_RETURN_IF_ERROR(cudaGetLastError());
   }
   {
     const size_t smem = (size_t)(2 * BN + 4 * BM) * LD * sizeof(__nv_bfloat16) + 4 * BM * sizeof(float);
     PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(bwd_dkdv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    dim3 grid((p.T + BN - 1) / BN, p.H, p.B);
+    dim3 grid(p.H * p.B, (p.T + BN - 1) / BN);
     bwd_dkdv_kernel<D><<<grid, NT, smem, st>>>(p);
     return cudaGetLastError();
   }

@@ -328,6 +328,17 @@ class LayerRouting:
 
 
 @dataclass
+class RowPlan:
+    """Host-side plan of one row (row-local entry / chunk numbering)."""
+
+    item: dict
+    cache: object
+    builder: object
+    entries: list
+    chunks: list
+
+
+@dataclass
 class BatchPlan:
     """Host-side cache-build plan of one batch (see ``DeviceRuntime.plan_batch``)."""
 
@@ -425,7 +436,8 @@ class DeviceRuntime:
         self.pos_emb_g = f.view(f.grad, "pos_emb.weight")
         self.anchor = torch.zeros(1, device=self.device, requires_grad=True)  # puts embeddings on the tape
         self.kmeans_tables = KMeansTables(cfg, self.device)
-        self._prefetched: BatchPlan | None = None
+        self._prefetched_rows: tuple | None = None  # (metadata rows, {row: RowPlan})
+        self.upcoming: list | None = None  # next batch's rows, planned in slices during this step
         self._last_tokenizer = None
         self._last_resolver = None
         self.last_routing: dict[int, LayerRouting] = {}
@@ -553,38 +565,63 @@ class DeviceRuntime:
         return MemoryView(memory.k_view(li, d), memory.v_view(li, d), mem_idx, ints[0])
 
     # -- cache build ------------------------------------------------------------
-    def plan_batch(self, metadata_rows: list[dict], tokenizer, resolver_config=None) -> "BatchPlan":
-        """Host half of the cache build: trace every row's recursive build, tokenise and
-        chunk each entry once, and order the entries into dependency waves."""
+    def plan_row(self, item: dict, tokenizer, resolver_config=None) -> "RowPlan":
+        """Host planning of one row: trace its recursive build, tokenise and chunk each entry once.
+
+        Entry and chunk indices in the result are row-local; ``plan_batch`` renumbers them.
+        """
         cfg = self.cfg
-        caches, builders = plan_cache_builds(self.model, tokenizer, metadata_rows, resolver_config=resolver_config)
+        (cache,), (builder,) = plan_cache_builds(self.model, tokenizer, [item], resolver_config=resolver_config)
+        entries: list[EntryRecord] = []
+        chunks: list[ChunkRecord] = []
+        limit = cfg.effective_model_max_context_tokens
+        index_of = {}
+        for step in builder.plan:
+            ids = list(step.token_ids) if step.token_ids is not None else list(tokenizer.encode(step.text))
+            if len(ids) > limit:
+                raise _Unsupported("reference longer than the native limit needs bounded encoding")
+            e = len(entries)
+            index_of[step.uri] = e
+            record = EntryRecord(0, step.uri, step.text, step.metadata, step.use_pra_memory,
+                                 tuple(index_of[u] for u in step.visible_uris if u in index_of))
+            for chunk in partition_reference_tokens(step.uri, ids, tokenizer, cfg, step.metadata,
+                                                    text=step.text, max_chunk_tokens=limit):
+                ids_c = tuple(chunk.token_ids[:limit])
+                record.chunks.append(len(chunks))
+                chunks.append(ChunkRecord(0, e, step.uri, chunk.chunk_id, chunk.token_start,
+                                          min(chunk.token_start + len(ids_c), chunk.token_end), ids_c,
+                                          metadata=dict(chunk.metadata)))
+            record.wave = (1 + max((entries[v].wave for v in record.visible), default=-1)) if record.use_memory \
+                else 0
+            entries.append(record)
+        return RowPlan(item, cache, builder, entries, chunks)
+
+    def plan_batch(self, metadata_rows: list[dict], tokenizer, resolver_config=None,
+                   row_plans: dict | None = None) -> "BatchPlan":
+        """Host half of the cache build: every row's plan (taken from ``row_plans`` when
+        prefetched), renumbered into one batch and ordered into dependency waves."""
+        row_plans = row_plans or {}
+        caches, builders = [], []
         entries: list[EntryRecord] = []
         chunks: list[ChunkRecord] = []
         rows: list[list[int]] = []
-        limit = cfg.effective_model_max_context_tokens
-        for row, builder in enumerate(builders):
-            index_of = {}
-            row_entries = []
-            for step in builder.plan:
-                ids = list(step.token_ids) if step.token_ids is not None else list(tokenizer.encode(step.text))
-                if len(ids) > limit:
-                    raise _Unsupported("reference longer than the native limit needs bounded encoding")
-                e = len(entries)
-                index_of[step.uri] = e
-                record = EntryRecord(row, step.uri, step.text, step.metadata, step.use_pra_memory,
-                                     tuple(index_of[u] for u in step.visible_uris if u in index_of))
-                for chunk in partition_reference_tokens(step.uri, ids, tokenizer, cfg, step.metadata,
-                                                        text=step.text, max_chunk_tokens=limit):
-                    ids_c = tuple(chunk.token_ids[:limit])
-                    record.chunks.append(len(chunks))
-                    chunks.append(ChunkRecord(row, e, step.uri, chunk.chunk_id, chunk.token_start,
-                                              min(chunk.token_start + len(ids_c), chunk.token_end), ids_c,
-                                              metadata=dict(chunk.metadata)))
-                record.wave = (1 + max((entries[v].wave for v in record.visible), default=-1)) if record.use_memory \
-                    else 0
-                entries.append(record)
-                row_entries.append(e)
-            rows.append(row_entries)
+        for row, item in enumerate(metadata_rows):
+            plan = row_plans.get(row)
+            if plan is None or plan.item is not item:
+                plan = self.plan_row(item, tokenizer, resolver_config)
+            e0, c0 = len(entries), len(chunks)
+            for record in plan.entries:
+                record.row = row
+                record.visible = tuple(v + e0 for v in record.visible)
+                record.chunks = [c + c0 for c in record.chunks]
+            for chunk in plan.chunks:
+                chunk.row = row
+                chunk.entry += e0
+            entries.extend(plan.entries)
+            chunks.extend(plan.chunks)
+            rows.append(list(range(e0, len(entries))))
+            caches.append(plan.cache)
+            builders.append(plan.builder)
         seq_len = max((len(c.token_ids) for c in chunks), default=1)
         n_waves = max((e.wave for e in entries), default=-1) + 1
         seq = 0
@@ -600,29 +637,39 @@ class DeviceRuntime:
             waves.append(members)
         return BatchPlan(metadata_rows, caches, builders, entries, chunks, rows, seq_len, waves)
 
-    def prefetch(self, metadata_rows: list[dict], tokenizer=None, resolver_config=None) -> None:
-        """Plan the NEXT batch on the host while the device still runs the current one.
+    def prefetch(self, metadata_rows: list[dict], tokenizer=None, resolver_config=None, part: int = 0,
+                 parts: int = 1) -> None:
+        """Plan rows of the NEXT batch on the host while the device runs the current one.
 
         Planning needs no model state (only the tokenizer, resolver settings and the
-        rows' reference tables), so doing it ahead is exact; ``build_memory`` picks
-        the plan up when it is called with the same rows.
+        rows' reference tables), so doing it ahead is exact.  ``part``/``parts``
+        plan a slice of the rows, so the work can be spread over several points of
+        the current step; ``build_memory`` picks the plans up (and plans whatever is
+        missing) when it is called with the same rows.
         """
         tokenizer = tokenizer or self._last_tokenizer
         if tokenizer is None:
             return
         resolver_config = resolver_config if resolver_config is not None else self._last_resolver
-        try:
-            self._prefetched = self.plan_batch(metadata_rows, tokenizer, resolver_config)
-        except _Unsupported:
-            self._prefetched = None
+        if self._prefetched_rows is None or self._prefetched_rows[0] is not metadata_rows:
+            self._prefetched_rows = (metadata_rows, {})
+        done = self._prefetched_rows[1]
+        n = len(metadata_rows)
+        for row in range(part * n // parts, (part + 1) * n // parts):
+            if row not in done:
+                try:
+                    done[row] = self.plan_row(metadata_rows[row], tokenizer, resolver_config)
+                except _Unsupported:
+                    return
 
     def build_memory(self, metadata_rows: list[dict], tokenizer, resolver_config=None):
         """Plan (or take the prefetched plan of) the batch, then encode all rows' chunks wave by wave."""
         self._last_tokenizer, self._last_resolver = tokenizer, resolver_config
-        plan = self._prefetched
-        self._prefetched = None
-        if plan is None or plan.metadata_rows is not metadata_rows:
-            plan = self.plan_batch(metadata_rows, tokenizer, resolver_config)
+        ready = {}
+        if self._prefetched_rows is not None and self._prefetched_rows[0] is metadata_rows:
+            ready = self._prefetched_rows[1]
+        self._prefetched_rows = None
+        plan = self.plan_batch(metadata_rows, tokenizer, resolver_config, ready)
         caches, builders, entries, chunks, rows, seq_len = (plan.caches, plan.builders, plan.entries, plan.chunks,
                                                             plan.rows, plan.seq_len)
         memory = BatchMemory(self, entries, chunks, rows, seq_len, self.device)
@@ -778,13 +825,18 @@ def attach_device_runtime(model: TinyPRAModel) -> TinyPRAModel:
             return optimizer.last_norm  # 0-dim device tensor: read it only when it is logged
         raise RuntimeError("device path expects the fused optimizer")
 
+    def announce_batch(batch):
+        runtime.upcoming = batch["metadata"] if isinstance(batch, dict) and "metadata" in batch else None
+
     def prefetch_batch(batch):
         if isinstance(batch, dict) and "metadata" in batch:
-            runtime.prefetch(batch["metadata"])
+            runtime.prefetch(batch["metadata"], part=1, parts=2)  # second half; build_memory plans the rest
+            runtime.upcoming = None
 
     model.build_optimizer = build_optimizer
     model.optimizer_step_hook = optimizer_step_hook
     model.prefetch_batch = prefetch_batch
+    model.announce_batch = announce_batch
     model.after_load_state = runtime.flat.refresh_shadow
     original_load = model.load_state_dict
 
@@ -825,6 +877,8 @@ def device_batch_step(model, batch, device, tokenizer, resolver_config, cache_co
     labels = batch["labels"].to(device, non_blocking=True)
     hidden = rt.prompt_forward(ids, mask, memory if memory.chunks else None)
     loss = rt.loss(hidden, labels)
+    if rt.upcoming is not None:  # first half of the next batch's host planning overlaps this forward
+        rt.prefetch(rt.upcoming, part=0, parts=2)
     tokens = int(batch["attention_mask"].sum())
     b = ids.shape[0]
     for cache, builder in zip(caches, builders):

@@ -100,7 +100,7 @@ def build(verbose: bool = False):
     os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0a")
     os.environ.setdefault("MAX_JOBS", str(max(os.cpu_count() or 4, 4)))
     cuda_flags = [*ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-DNDEBUG",
-                  "-diag-suppress", "20012,177,550", "-Xptxas", "-v" if verbose else "-O3"]
+                  "-diag-suppress", "20012,177,550", "-DCUTLASS_ENABLE_DIRECT_CUDA_DRIVER_CALL=1", "-Xptxas", "-v" if verbose else "-O3"]
     _module = cpp_extension.load(
         name=NAME,
         sources=[str(CSRC / s) for s in _SOURCES],

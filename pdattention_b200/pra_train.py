@@ -425,6 +425,9 @@ def training_step(model, batch: dict, device: str, tokenizer, optimizer, *, reso
     resolver_config = ResolverServiceConfig.from_value(resolver_config)
     cache_config = CacheServiceConfig.from_value(cache_config)
     optimizer.zero_grad(set_to_none=True)
+    announce = getattr(model, "announce_batch", None)
+    if next_batch is not None and announce is not None:
+        announce(next_batch)
     loss, info = _pra_batch_step(model, batch, device, tokenizer, resolver_config, cache_config)
     loss.backward()
     hook = getattr(model, "optimizer_step_hook", None)

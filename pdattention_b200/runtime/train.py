@@ -296,6 +296,9 @@ def train_model(*, model, train_config, train_loader, val_loader=None, test_load
             wall0 = time.perf_counter()
             state.batch_step += 1
             batches += 1
+            announce = getattr(model, "announce_batch", None)
+            if announce is not None and upcoming is not _END:
+                announce(upcoming)
             amp = torch.amp.autocast("cuda") if state.scaler is not None else nullcontext()
             with amp:
                 loss, batch_metrics = batch_step(model, batch, state.device)
