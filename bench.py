@@ -155,7 +155,7 @@ def run(impl: str, steps: int, warmup: int, gpus: int) -> dict:
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     from pdattention_b200.data import WordIdTokenizer
 
@@ -214,6 +214,8 @@ def run(impl: str, steps: int, warmup: int, gpus: int) -> dict:
         "config": {"model": model_desc, "global_batch": PER_GPU_BATCH * world, "seq_len": MODEL["max_seq_len"],
                    "direct_tokens_per_row": TREE["prompt_tokens"] + 1, "references_per_row": 16,
                    "chunk_tokens": 64, "gists_per_chunk": 2, "parallelism": f"dp{world}",
+                   "dp_reduction": ("fused peer-memory all-reduce kernel" if impl != "reference" and world > 1
+                                    else "nccl all-reduce" if world > 1 else "none"),
                    "l2": "per-step working set exceeds the 126 MB L2 (no flush)"},
         "clocks": clocks.summary(),
         "e2e": {"value": total_tokens / wall_s, "unit": "tokens/s", "h2d_bytes_per_step": h2d // max(steps, 1),
@@ -223,6 +225,7 @@ def run(impl: str, steps: int, warmup: int, gpus: int) -> dict:
     }
     if impl == "reference":
         result["impl"] = "reference"
+    step_fn.close()
     if world > 1:
         import torch.distributed as dist
 
@@ -232,9 +235,10 @@ def run(impl: str, steps: int, warmup: int, gpus: int) -> dict:
 
 
 class _Step:
-    def __init__(self, fn, batch_source):
+    def __init__(self, fn, batch_source, close=None):
         self.fn = fn
         self.batches = batch_source
+        self.close = close or (lambda: None)
 
     def __call__(self, batch, next_batch=None):
         return self.fn(batch, next_batch)
@@ -260,7 +264,7 @@ def _pra_arm(root: Path, tokenizer, rank: int, world: int):
         raise RuntimeError("device path unavailable for the benchmark config")
     model.train()
     optimizer = model.build_optimizer(TrainConfig(device="cuda", learning_rate=3e-4))
-    attach_data_parallel(model, optimizer, world)
+    reducer = attach_data_parallel(model, optimizer, world)
     resolver = ResolverServiceConfig()
 
     def step(batch, next_batch=None):
@@ -273,7 +277,14 @@ def _pra_arm(root: Path, tokenizer, rank: int, world: int):
         return value, _moved_bytes(batch), 4
 
     params = sum(p.numel() for p in model.parameters())
-    return _Step(step, lambda n: _batches(dm, rank, world, n)), f"TinyGPT-PRA-{params / 1e6:.0f}M", launch_counter()
+    def close():
+        if reducer is not None:
+            reducer.check()  # raises if a peer wait timed out during the run
+            if hasattr(reducer, "close"):
+                reducer.close()
+
+    return (_Step(step, lambda n: _batches(dm, rank, world, n), close), f"TinyGPT-PRA-{params / 1e6:.0f}M",
+            launch_counter())
 
 
 def _reference_arm(root: Path, tokenizer, rank: int, world: int):

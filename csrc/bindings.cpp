@@ -4,6 +4,7 @@
 #include <torch/extension.h>
 
 #include <cmath>
+#include <cstring>
 #include <vector>
 
 #include "kernels.h"
@@ -470,6 +471,66 @@ std::vector<torch::Tensor> route(torch::Tensor query, torch::Tensor gists, torch
 
 }  // namespace
 
+// ---------------------------------------------------------------- peer buffers (CUDA IPC)
+// A dedicated cudaMalloc allocation (zeroed) that other processes on the node can map;
+// plain peer loads and stores only (no multicast object is ever created).
+py::tuple ipc_alloc(int64_t nbytes, int64_t device) {
+  c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  void* p = nullptr;
+  check(cudaMalloc(&p, (size_t)nbytes), "ipc_alloc (cudaMalloc)");
+  check(cudaMemset(p, 0, (size_t)nbytes), "ipc_alloc (cudaMemset)");
+  cudaIpcMemHandle_t h;
+  check(cudaIpcGetMemHandle(&h, p), "ipc_alloc (cudaIpcGetMemHandle)");
+  auto t = torch::from_blob(p, {nbytes}, [](void* q) { cudaFree(q); },
+                            torch::TensorOptions().dtype(torch::kUInt8).device(torch::kCUDA, device));
+  return py::make_tuple(t, py::bytes(reinterpret_cast<const char*>(&h), sizeof(h)));
+}
+
+int64_t ipc_open(py::bytes handle, int64_t device) {
+  c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  const std::string raw = handle;
+  TORCH_CHECK(raw.size() == sizeof(cudaIpcMemHandle_t), "bad IPC handle size");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, raw.data(), sizeof(h));
+  void* p = nullptr;
+  check(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "ipc_open");
+  return reinterpret_cast<int64_t>(p);
+}
+
+void ipc_close(int64_t address, int64_t device) {
+  c10::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  check(cudaIpcCloseMemHandle(reinterpret_cast<void*>(address)), "ipc_close");
+}
+
+// ---------------------------------------------------------------- data-parallel reduction
+// src/dst/sig: device addresses (ints) of every rank's gradient, output and signal buffers.
+void dp_allreduce(std::vector<int64_t> src, std::vector<int64_t> dst, std::vector<int64_t> sig, int64_t rank,
+                  int64_t offset, int64_t count, double scale, int64_t epoch, int64_t max_spins,
+                  torch::Tensor error) {
+  const int world = src.size();
+  TORCH_CHECK(world >= 1 && world <= DP_MAX_RANKS && dst.size() == src.size() && sig.size() == src.size(),
+              "dp_allreduce needs one src/dst/sig address per rank (at most ", DP_MAX_RANKS, ")");
+  TORCH_CHECK(error.scalar_type() == at::kInt && error.is_cuda(), "error must be an int32 CUDA tensor");
+  c10::cuda::CUDAGuard guard(error.device());
+  DpArgs a{};
+  for (int p = 0; p < world; ++p) {
+    a.src[p] = reinterpret_cast<const __nv_bfloat16*>(src[p]);
+    a.dst[p] = reinterpret_cast<float*>(dst[p]);
+    a.sig[p] = reinterpret_cast<uint32_t*>(sig[p]);
+  }
+  a.rank = rank;
+  a.world = world;
+  a.offset = offset;
+  a.count = count;
+  a.scale = (float)scale;
+  a.epoch = (uint32_t)epoch;
+  a.max_spins = max_spins;
+  a.error = ptr<int>(error);
+  check(pra_dp_allreduce(a, stream()), "dp_allreduce");
+}
+
+int64_t dp_signal_words(int64_t world) { return 2LL * pra_dp_allreduce_blocks() * world; }
+
 // ---------------------------------------------------------------- native block-stack executor
 // Forward of a stack of pre-LN GPT blocks (LN -> QKV -> [route] -> attention -> O-proj + residual ->
 // LN -> up-GELU -> down + residual) driven entirely from C++: no Python, no autograd records,
@@ -566,4 +627,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gist_kmeans_into", &gist_kmeans_into);
   m.def("route", &route);
   m.def("stack_forward", &stack_forward);
+  m.def("dp_allreduce", &dp_allreduce);
+  m.def("ipc_alloc", &ipc_alloc);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
+  m.def("dp_signal_words", &dp_signal_words);
 }

@@ -52,21 +52,23 @@ struct GeluErfGrad<cutlass::Array<T, N>> {
   }
 };
 
-template <class LayoutA, class LayoutB, class ElementD, class FusionOp,
-          class TileShape = Shape<_256, _128, _64>, class ClusterShape = Shape<_2, _1, _1>>
+// One-SM tcgen05 tiles, cluster of one CTA: every CTA issues its own TMA loads (the
+// library is also used by multi-GPU runs, which must not issue cluster-shared loads).
+template <class LayoutA, class LayoutB, class ElementD, class FusionOp, class TileShape = Shape<_128, _256, _64>>
 struct Gemm {
+  using ClusterShape = Shape<_1, _1, _1>;
   using LayoutD = cutlass::layout::RowMajor;
   static constexpr int AlignAB = 8;
   static constexpr int AlignD = 128 / cutlass::sizeof_bits<ElementD>::value;
   using Epilogue = typename cutlass::epilogue::collective::CollectiveBuilder<
       cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, TileShape, ClusterShape,
       cutlass::epilogue::collective::EpilogueTileAuto, float, float, ElementD, LayoutD, AlignD, ElementD, LayoutD,
-      AlignD, cutlass::epilogue::collective::EpilogueScheduleAuto, FusionOp>::CollectiveOp;
+      AlignD, cutlass::epilogue::TmaWarpSpecialized1Sm, FusionOp>::CollectiveOp;
   using Mainloop = typename cutlass::gemm::collective::CollectiveBuilder<
       cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, BF16, LayoutA, AlignAB, BF16, LayoutB, AlignAB, float,
       TileShape, ClusterShape,
       cutlass::gemm::collective::StageCountAutoCarveout<static_cast<int>(sizeof(typename Epilogue::SharedStorage))>,
-      cutlass::gemm::collective::KernelScheduleAuto>::CollectiveOp;
+      cutlass::gemm::KernelTmaWarpSpecialized1SmSm100>::CollectiveOp;
   using Kernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, Mainloop, Epilogue>;
   using Device = cutlass::gemm::device::GemmUniversalAdapter<Kernel>;
   using StrideA = typename Kernel::StrideA;

@@ -154,3 +154,19 @@ struct RouteParams {
   int* status;                 // [B] 0 ok, 1 namespace too large, 2 memory list truncated
 };
 cudaError_t pra_route(const RouteParams& p, cudaStream_t stream);
+
+// ---- data-parallel gradient all-reduce over peer memory (dp_reduce.cu) -----------------
+constexpr int DP_MAX_RANKS = 8;
+struct DpArgs {
+  const __nv_bfloat16* src[DP_MAX_RANKS];  // every rank's bf16 gradient buffer (symmetric memory)
+  float* dst[DP_MAX_RANKS];                // every rank's fp32 reduced buffer (symmetric memory)
+  uint32_t* sig[DP_MAX_RANKS];             // every rank's signal area: [2][blocks][world] uint32, zeroed once
+  int rank, world;
+  int64_t offset, count;                   // element range reduced by this launch (multiples of 8)
+  float scale;                             // applied to the sum (1/world gives the average)
+  uint32_t epoch;                          // strictly increasing per launch (signals compare >=)
+  long long max_spins;                     // poll limit of every wait
+  int* error;                              // local flag: 1 + phase of a timed-out wait
+};
+int pra_dp_allreduce_blocks();
+cudaError_t pra_dp_allreduce(const DpArgs& args, cudaStream_t stream);

@@ -150,6 +150,19 @@ class FlatParams:
     def refresh_shadow(self) -> None:
         self.shadow.copy_(self.master)
 
+    def rehome_grad(self, new: torch.Tensor, views: list[torch.Tensor]) -> None:
+        """Move the gradient buffer into ``new`` (e.g. symmetric memory) without
+        rebuilding anything: every view in ``views`` (slot gradients, embedding
+        gradients) is re-pointed in place at the same offset of ``new``."""
+        old = self.grad
+        assert new.numel() == old.numel() and new.dtype == old.dtype and new.is_contiguous()
+        new.copy_(old)
+        base = old.storage_offset()
+        storage = new.untyped_storage()
+        for v in views:
+            v.set_(storage, new.storage_offset() + v.storage_offset() - base, v.size(), v.stride())
+        self.grad = new
+
     def view(self, buffer: torch.Tensor, name: str, rows: int | None = None) -> torch.Tensor:
         p = self.params[name]
         if rows is None:
@@ -443,6 +456,11 @@ class DeviceRuntime:
         self.last_routing: dict[int, LayerRouting] = {}
         self.last_memory: BatchMemory | None = None
         self.last_namespace: Namespace | None = None
+
+    def grad_views(self) -> list[torch.Tensor]:
+        """Every tensor that aliases the flat gradient buffer."""
+        views = [t for slot in self.flat.slots for t in (slot.gw, slot.gb) if t is not None]
+        return views + [self.tok_emb_g, self.pos_emb_g]
 
     def _check_contiguous(self, pre: str) -> None:
         f = self.flat

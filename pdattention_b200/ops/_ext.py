@@ -25,7 +25,7 @@ ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 _SOURCES = ["bindings.cpp", "attention.cu", "norm.cu", "loss_optim.cu", "gist.cu", "routing.cu",
             "gemm/tn_bias.cu", "gemm/tn_bias_gelu.cu", "gemm/nn.cu", "gemm/nn_dgelu.cu", "gemm/wgrad.cu",
-            "colsum_noalloc.cu"]
+            "colsum_noalloc.cu", "dp_reduce.cu", "driver_shim.cu"]
 
 _module = None
 
@@ -34,7 +34,8 @@ _module = None
 KERNELS_PER_CALL = {"attention_fwd": 1, "attention_bwd": 3, "gemm": 1, "norm_fwd": 1, "norm_bwd": 3, "colsum": 2,
                     "cross_entropy": 1, "grad_norm": 2, "adamw": 1, "gist_mean": 1, "gist_kmeans": 1, "route": 1,
                     "gist_mean_into": 1, "gist_kmeans_into": 1,
-                    "stack_forward": 0}  # stack_forward: counted per layer by its caller
+                    "stack_forward": 0, "dp_allreduce": 1, "dp_signal_words": 0,
+                    "ipc_alloc": 0, "ipc_open": 0, "ipc_close": 0}  # stack_forward: counted per layer by its caller
 
 
 class LaunchCounter:
@@ -107,7 +108,6 @@ def build(verbose: bool = False):
         extra_include_paths=[str(CSRC), *cutlass_include_dirs()],
         extra_cflags=["-O3", "-std=c++17"],
         extra_cuda_cflags=cuda_flags,
-        extra_ldflags=["-lcuda"],
         build_directory=str(BUILD_DIR),
         verbose=verbose,
     )

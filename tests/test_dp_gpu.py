@@ -1,0 +1,116 @@
+"""Fused peer-memory data-parallel gradient reduction on 2 GPUs (skipped with fewer).
+
+The ranks are child processes, one per GPU, with NVLS off; the kernel uses plain
+peer loads and stores.  The timeout case makes a rank skip one reduction so the
+peer's bounded wait runs out: the kernel must return with an error status that the
+host reads, and the context must stay usable.
+"""
+
+import os
+import socket
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, queue) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    result = {"rank": rank}
+    try:
+        from pdattention_b200.config import TrainConfig
+        from pdattention_b200.models.fastpath import prepare_model
+        from pdattention_b200.parallel.dp import attach_data_parallel
+        from pdattention_b200.smoke import tiny_config
+
+        torch.manual_seed(0)
+        model = prepare_model(tiny_config(64), "cuda")
+        rt = model._device_runtime
+        opt = model.build_optimizer(TrainConfig(device="cuda", learning_rate=1e-3))
+        reducer = attach_data_parallel(model, opt, world, "peer")
+        grad = rt.flat.grad
+        # the slot views now alias the peer-visible buffer
+        gw = rt.layers[0]["qkv"].gw
+        result["aliased"] = grad.data_ptr() <= gw.data_ptr() < grad.data_ptr() + grad.numel() * 2
+        gen = torch.Generator(device="cuda").manual_seed(100 + rank)
+        grad.copy_(torch.randn(grad.shape, generator=gen, device="cuda").bfloat16())
+        out = reducer.reduce()
+        torch.cuda.synchronize()
+        reducer.check()
+        gathered = [torch.empty_like(grad) for _ in range(world)]
+        dist.all_gather(gathered, grad)
+        expected = gathered[0].float()
+        for t in gathered[1:]:
+            expected = expected + t.float()
+        expected = expected * (1.0 / world)
+        result["max_err"] = float((out - expected).abs().max())
+        # a second reduction reuses the signal area (epochs increase)
+        grad.mul_(2)
+        out = reducer.reduce()
+        torch.cuda.synchronize()
+        reducer.check()
+        result["max_err2"] = float((out - 2 * expected).abs().max())
+        # one optimizer step through the reducer keeps the replicas identical
+        opt.step()
+        checksum = rt.flat.master.double().sum().reshape(1)
+        sums = [torch.zeros_like(checksum) for _ in range(world)]
+        dist.all_gather(sums, checksum)
+        result["replicas_equal"] = all(float(s) == float(sums[0]) for s in sums)
+        dist.barrier()
+        # timeout: rank 1 skips one reduction; rank 0's bounded wait must run out
+        reducer.max_spins = 1 << 14
+        if rank == 0:
+            reducer.reduce()
+            torch.cuda.synchronize()
+            result["timeout_code"] = int(reducer.error.item())
+            reducer.error.zero_()
+            result["context_usable"] = bool(torch.ones(4, device="cuda").sum().item() == 4)
+        dist.barrier()
+        reducer.close()
+    except Exception as error:  # reported to the parent
+        result["error"] = repr(error)
+    finally:
+        queue.put(result)
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_peer_gradient_allreduce_two_gpus():
+    from pdattention_b200.ops import _ext
+
+    if not _ext.available():
+        pytest.skip("extension not built")
+    world = 2
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(world):
+        item = queue.get(timeout=300)
+        results[item["rank"]] = item
+    for p in procs:
+        p.join(timeout=60)
+    for rank, item in results.items():
+        assert "error" not in item, item
+        assert item["aliased"], item
+        assert item["max_err"] < 1e-5, item
+        assert item["max_err2"] < 1e-5, item
+        assert item["replicas_equal"], item
+    assert results[0]["timeout_code"] == 1, results[0]
+    assert results[0]["context_usable"]

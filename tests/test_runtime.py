@@ -121,3 +121,25 @@ def test_cli_commands(data_root, monkeypatch):
     assert out.exit_code == 0 and "PRA eval report (checkpoint)" in out.output
     out = runner.invoke(cli, ["train", "--model", "missing_profile"])
     assert out.exit_code != 0
+
+
+def test_flat_grad_rehome_keeps_views_aliased():
+    """Moving the flat gradient into another buffer re-points every slot view in place."""
+    from pdattention_b200.models.fastpath import FlatParams
+    from pdattention_b200.models.tiny import TinyPRAModel
+    from pdattention_b200.smoke import tiny_config
+
+    model = TinyPRAModel(tiny_config(64))
+    flat = FlatParams(model, 128)
+    flat.grad.copy_(torch.arange(flat.grad.numel()).to(torch.bfloat16))
+    views = [flat.view(flat.grad, "blocks.0.attn.o_proj.weight"), flat.view(flat.grad, "token_emb.weight")]
+    before = [v.clone() for v in views]
+    new = torch.zeros(flat.grad.numel() + 64, dtype=torch.bfloat16)[64:]
+    flat.rehome_grad(new, views)
+    assert flat.grad is new
+    for v, b in zip(views, before):
+        assert torch.equal(v, b)
+        assert new.data_ptr() <= v.data_ptr() < new.data_ptr() + new.numel() * 2
+    views[0].fill_(3)
+    start = flat.offsets["blocks.0.attn.o_proj.weight"]
+    assert float(new[start]) == 3.0
