@@ -146,7 +146,7 @@ void gemm(const std::string& kind, torch::Tensor A, torch::Tensor B, c10::option
   c10::cuda::CUDAGuard guard(A.device());
   expect(A, at::kBFloat16, "A");
   expect(B, at::kBFloat16, "B");
-  expect(D, at::kBFloat16, "D");
+  expect(D, kind == "tn_f32" ? at::kFloat : at::kBFloat16, "D");
   TORCH_CHECK(A.is_contiguous() && B.is_contiguous() && D.is_contiguous(), "GEMM operands must be contiguous");
   GemmArgs g{};
   g.A = A.data_ptr();
@@ -161,7 +161,7 @@ void gemm(const std::string& kind, torch::Tensor A, torch::Tensor B, c10::option
   auto& ws = workspace(A);
   g.workspace = ws.data_ptr();
   g.workspace_bytes = ws.numel();
-  if (kind == "tn" || kind == "tn_gelu") {  // D[M,N] = A[M,K] B[N,K]^T
+  if (kind == "tn" || kind == "tn_gelu" || kind == "tn_f32") {  // D[M,N] = A[M,K] B[N,K]^T
     g.M = A.size(0); g.K = A.size(1); g.N = B.size(0);
     TORCH_CHECK(B.size(1) == g.K && D.size(0) == g.M && D.size(1) == g.N, "tn shape mismatch");
   } else if (kind == "nn" || kind == "nn_dgelu") {  // D[M,N] = A[M,K] B[K,N]
@@ -177,6 +177,7 @@ void gemm(const std::string& kind, torch::Tensor A, torch::Tensor B, c10::option
   if (g.beta != 0.f) TORCH_CHECK(g.C != nullptr, "beta != 0 needs C");
   cudaError_t e;
   if (kind == "tn") e = pra_gemm_tn_bias(g, stream());
+  else if (kind == "tn_f32") e = pra_gemm_tn_f32(g, stream());
   else if (kind == "tn_gelu") e = pra_gemm_tn_bias_gelu(g, stream());
   else if (kind == "nn") e = pra_gemm_nn(g, stream());
   else if (kind == "nn_dgelu") e = pra_gemm_nn_dgelu(g, stream());
@@ -471,6 +472,143 @@ std::vector<torch::Tensor> route(torch::Tensor query, torch::Tensor gists, torch
 
 }  // namespace
 
+// ---------------------------------------------------------------- Llama-family ops
+// Rotary copy: rows of src (heads * head_dim, unit stride) to dst rows (dst_rows or identity).
+void rope_copy(torch::Tensor src, torch::Tensor dst, c10::optional<torch::Tensor> dst_rows,
+               c10::optional<torch::Tensor> pos, c10::optional<torch::Tensor> cos_t,
+               c10::optional<torch::Tensor> sin_t, int64_t heads, int64_t head_dim) {
+  c10::cuda::CUDAGuard guard(src.device());
+  expect(src, at::kBFloat16, "src");
+  expect(dst, at::kBFloat16, "dst");
+  TORCH_CHECK(src.dim() == 2 && dst.dim() == 2 && src.stride(1) == 1 && dst.stride(1) == 1, "rows must be 2-D");
+  TORCH_CHECK(src.size(1) >= heads * head_dim && dst.size(1) >= heads * head_dim, "row too short");
+  TORCH_CHECK(pos.has_value() == cos_t.has_value(), "positions need the cos/sin tables");
+  RopeCopyArgs a{};
+  a.src = ptr<const __nv_bfloat16>(src);
+  a.src_stride = src.stride(0);
+  a.dst = ptr<__nv_bfloat16>(dst);
+  a.dst_stride = dst.stride(0);
+  a.dst_rows = optr<int>(dst_rows);
+  a.pos = optr<int>(pos);
+  a.cos_t = optr<float>(cos_t);
+  a.sin_t = optr<float>(sin_t);
+  a.M = src.size(0);
+  a.heads = heads;
+  a.head_dim = head_dim;
+  check(pra_rope_copy(a, stream()), "rope_copy");
+}
+
+void silu_mul(torch::Tensor gate_up, torch::Tensor out) {
+  c10::cuda::CUDAGuard guard(gate_up.device());
+  expect(gate_up, at::kBFloat16, "gate_up");
+  TORCH_CHECK(gate_up.is_contiguous() && out.is_contiguous() && gate_up.size(1) == 2 * out.size(1),
+              "gate_up must be [M, 2F] and out [M, F]");
+  check(pra_silu_mul(ptr<const __nv_bfloat16>(gate_up), gate_up.size(0), out.size(1), ptr<__nv_bfloat16>(out),
+                     stream()),
+        "silu_mul");
+}
+
+// Split-K decode attention.  q [B, H*Dh]; memory pool k/v views [rows, >= Hkv*Dh] (row stride
+// shared); local caches [B, max_len, Hkv*Dh] views.  Returns {out [B, H*Dh]} and, with
+// export_partials, also the merged unnormalised (out, (max, sum)) fp32 partials.
+std::vector<torch::Tensor> decode_attention(torch::Tensor q, int64_t heads, int64_t kv_heads, int64_t head_dim,
+                                            c10::optional<torch::Tensor> mem_k, c10::optional<torch::Tensor> mem_v,
+                                            c10::optional<torch::Tensor> mem_idx,
+                                            c10::optional<torch::Tensor> mem_len,
+                                            c10::optional<torch::Tensor> loc_k, c10::optional<torch::Tensor> loc_v,
+                                            c10::optional<torch::Tensor> loc_len, int64_t max_keys,
+                                            int64_t split_keys, bool export_partials) {
+  c10::cuda::CUDAGuard guard(q.device());
+  expect(q, at::kBFloat16, "q");
+  TORCH_CHECK(q.dim() == 2 && q.stride(1) == 1 && q.size(1) == heads * head_dim, "q must be [B, H*Dh]");
+  DecodeAttnParams p{};
+  p.q = ptr<const __nv_bfloat16>(q);
+  p.q_row = q.stride(0);
+  p.B = q.size(0);
+  p.H = heads;
+  p.Hkv = kv_heads;
+  if (mem_idx.has_value() && mem_idx->numel() > 0) {
+    TORCH_CHECK(mem_k.has_value() && mem_v.has_value() && mem_len.has_value(), "memory needs k, v, idx and len");
+    TORCH_CHECK(mem_k->stride(-1) == 1 && mem_v->stride(0) == mem_k->stride(0), "memory pools share a row stride");
+    p.mem_k = ptr<const __nv_bfloat16>(*mem_k);
+    p.mem_v = ptr<const __nv_bfloat16>(*mem_v);
+    p.mem_row = mem_k->stride(0);
+    p.mem_idx = ptr<const int>(*mem_idx);
+    p.mem_max = mem_idx->size(1);
+    p.mem_len = ptr<const int>(*mem_len);
+  }
+  if (loc_k.has_value() && loc_k->numel() > 0) {
+    TORCH_CHECK(loc_k->dim() == 3 && loc_k->stride(2) == 1 && loc_v->strides() == loc_k->strides(),
+                "local caches must be [B, max_len, width] views with equal strides");
+    TORCH_CHECK(loc_len.has_value(), "local cache needs lengths");
+    p.loc_k = ptr<const __nv_bfloat16>(*loc_k);
+    p.loc_v = ptr<const __nv_bfloat16>(*loc_v);
+    p.loc_batch = loc_k->stride(0);
+    p.loc_row = loc_k->stride(1);
+    p.loc_len = ptr<const int>(*loc_len);
+  }
+  p.scale = 1.0f / std::sqrt((float)head_dim);
+  p.split_keys = split_keys;
+  p.n_split = std::max<int64_t>(1, (max_keys + split_keys - 1) / split_keys);
+  auto fo = q.options().dtype(at::kFloat);
+  auto part_o = torch::empty({p.B, heads, p.n_split, head_dim}, fo);
+  auto part_ml = torch::empty({p.B, heads, p.n_split, 2}, fo);
+  auto out = torch::empty({p.B, heads * head_dim}, q.options());
+  p.part_o = ptr<float>(part_o);
+  p.part_ml = ptr<float>(part_ml);
+  p.out = ptr<__nv_bfloat16>(out);
+  p.out_row = out.stride(0);
+  std::vector<torch::Tensor> result{out};
+  if (export_partials) {
+    auto eo = torch::empty({p.B, heads, head_dim}, fo), eml = torch::empty({p.B, heads, 2}, fo);
+    p.export_o = ptr<float>(eo);
+    p.export_ml = ptr<float>(eml);
+    result.push_back(eo);
+    result.push_back(eml);
+  }
+  check(pra_decode_attention(p, head_dim, stream()), "decode_attention");
+  return result;
+}
+
+// Exact top-k routing from approximate scores.  Returns {mem_idx [B, mem_max], mem_len [B],
+// selected chunk ids [B, k]}.
+std::vector<torch::Tensor> route_topk(torch::Tensor scores, torch::Tensor query, torch::Tensor gists,
+                                      torch::Tensor ns_start, torch::Tensor ns_end, torch::Tensor chunk_len,
+                                      torch::Tensor chunk_row0, int64_t k, int64_t k_cand, int64_t budget,
+                                      int64_t mem_max) {
+  c10::cuda::CUDAGuard guard(scores.device());
+  expect(scores, at::kFloat, "scores");
+  expect(query, at::kFloat, "query");
+  expect(gists, at::kFloat, "gists");
+  TORCH_CHECK(scores.dim() == 2 && scores.stride(1) == 1 && query.stride(-1) == 1 && gists.is_contiguous(),
+              "route_topk layouts");
+  RouteTopkArgs a{};
+  a.B = scores.size(0);
+  a.D = gists.size(-1);
+  a.scores = ptr<const float>(scores);
+  a.score_stride = scores.stride(0);
+  a.query = ptr<const float>(query);
+  a.query_stride = query.stride(0);
+  a.gists = ptr<const float>(gists);
+  a.ns_start = ptr<const int>(ns_start);
+  a.ns_end = ptr<const int>(ns_end);
+  a.chunk_len = ptr<const int>(chunk_len);
+  a.chunk_row0 = ptr<const int>(chunk_row0);
+  a.k = k;
+  a.k_cand = k_cand;
+  a.budget = budget;
+  auto io = scores.options().dtype(at::kInt);
+  auto mem_idx = torch::empty({a.B, std::max<int64_t>(mem_max, 1)}, io);
+  auto mem_len = torch::empty({a.B}, io);
+  auto sel = torch::empty({a.B, std::max<int64_t>(k, 1)}, io);
+  a.mem_idx = ptr<int>(mem_idx);
+  a.mem_max = std::max<int64_t>(mem_max, 1);
+  a.mem_len = ptr<int>(mem_len);
+  a.sel_out = ptr<int>(sel);
+  check(pra_route_topk(a, stream()), "route_topk");
+  return {mem_idx, mem_len, sel};
+}
+
 // ---------------------------------------------------------------- peer buffers (CUDA IPC)
 // A dedicated cudaMalloc allocation (zeroed) that other processes on the node can map;
 // plain peer loads and stores only (no multicast object is ever created).
@@ -628,6 +766,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("route", &route);
   m.def("stack_forward", &stack_forward);
   m.def("dp_allreduce", &dp_allreduce);
+  m.def("rope_copy", &rope_copy);
+  m.def("silu_mul", &silu_mul);
+  m.def("decode_attention", &decode_attention);
+  m.def("route_topk", &route_topk);
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", &ipc_close);

@@ -48,6 +48,7 @@ struct GemmArgs {
   size_t workspace_bytes;
 };
 cudaError_t pra_gemm_tn_bias(const GemmArgs& g, cudaStream_t stream);
+cudaError_t pra_gemm_tn_f32(const GemmArgs& g, cudaStream_t stream);  // fp32 D, no bias / C
 cudaError_t pra_gemm_tn_bias_gelu(const GemmArgs& g, cudaStream_t stream);
 cudaError_t pra_gemm_nn(const GemmArgs& g, cudaStream_t stream);
 cudaError_t pra_gemm_nn_dgelu(const GemmArgs& g, cudaStream_t stream);
@@ -170,3 +171,63 @@ struct DpArgs {
 };
 int pra_dp_allreduce_blocks();
 cudaError_t pra_dp_allreduce(const DpArgs& args, cudaStream_t stream);
+
+// ---- Llama-family engine (llama.cu) ------------------------------------------------------
+struct RopeCopyArgs {
+  const __nv_bfloat16* src;    // row m at src + m * src_stride (heads * head_dim values)
+  int64_t src_stride;
+  __nv_bfloat16* dst;          // row dst_rows[m] (or m) at dst + row * dst_stride; may alias src
+  int64_t dst_stride;
+  const int* dst_rows;         // [M] or null
+  const int* pos;              // [M] rotary positions, or null (plain copy)
+  const float* cos_t;          // [max_pos, head_dim / 2] (null: plain copy)
+  const float* sin_t;
+  int M, heads, head_dim;
+};
+cudaError_t pra_rope_copy(const RopeCopyArgs& args, cudaStream_t stream);
+cudaError_t pra_silu_mul(const __nv_bfloat16* gate_up, int64_t M, int F, __nv_bfloat16* out, cudaStream_t stream);
+
+struct DecodeAttnParams {
+  const __nv_bfloat16* q;      // [B, H * Dh] post-rotary queries of the decoded tokens
+  int64_t q_row;
+  int B, H, Hkv;
+  const __nv_bfloat16* mem_k;  // memory pool rows (kv head h at column h * Dh)
+  const __nv_bfloat16* mem_v;
+  int64_t mem_row;
+  const int* mem_idx;          // [B, mem_max]
+  int mem_max;
+  const int* mem_len;          // [B] or null
+  const __nv_bfloat16* loc_k;  // local cache: row t of batch b at b * loc_batch + t * loc_row
+  const __nv_bfloat16* loc_v;
+  int64_t loc_row, loc_batch;
+  const int* loc_len;          // [B] or null
+  float scale;
+  int split_keys, n_split;     // keys per split (multiple of 64), number of splits
+  float* part_o;               // [B, H, n_split, Dh] workspace
+  float* part_ml;              // [B, H, n_split, 2] workspace
+  __nv_bfloat16* out;          // [B, H * Dh] normalised output, or null
+  int64_t out_row;
+  float* export_o;             // [B, H, Dh] merged unnormalised output, or null
+  float* export_ml;            // [B, H, 2] merged (max, sum), or null
+};
+cudaError_t pra_decode_attention(const DecodeAttnParams& p, int head_dim, cudaStream_t stream);
+
+struct RouteTopkArgs {
+  int B, D;
+  const float* scores;         // [B, score_stride] approximate cosine scores (tensor-core GEMM)
+  int64_t score_stride;
+  const float* query;          // [B, query_stride] routing queries (fp32, unnormalised)
+  int64_t query_stride;
+  const float* gists;          // [C, D] L2-normalised fp32 gists (exact rescoring)
+  const int* ns_start;         // [B] namespace of row b: chunks [ns_start, ns_end)
+  const int* ns_end;
+  const int* chunk_len;        // [C]
+  const int* chunk_row0;       // [C] memory pool row of the chunk's first token
+  int k, k_cand;               // selected chunks (<= 64), approximate candidates (<= 512)
+  int budget;                  // token budget per row (< 0: none)
+  int* mem_idx;                // [B, mem_max]
+  int mem_max;
+  int* mem_len;                // [B]
+  int* sel_out;                // [B, k] selected chunk ids in chunk order (-1 pad), or null
+};
+cudaError_t pra_route_topk(const RouteTopkArgs& args, cudaStream_t stream);

@@ -1,0 +1,458 @@
+// Hot ops of the PRA Llama-family engine (Llama 3 / Mistral / Qwen2) on sm_100a.
+//
+//  * rope_copy      rotary positions (HF rotate_half layout, fp32 cos/sin tables built in
+//                   fp64 on the host) applied while copying head rows to a destination row
+//                   (in place for queries, into the KV cache / chunk pool for keys); with a
+//                   null position table it is a plain row copy (values).
+//  * silu_mul       SwiGLU activation over a fused [gate | up] GEMM output.
+//  * decode attention: split-K flash decoding for grouped-query heads.  One CTA per
+//                   (row, kv head, key split) computes the unnormalised partial
+//                   (max, sum, out) of the group's query heads over its keys; keys are
+//                   [selected memory rows (gathered through a row list) ; local cache
+//                   rows], all visible to the token being decoded.  A second kernel
+//                   merges the splits (and optionally exports the merged partial for a
+//                   cross-GPU combine).
+//  * route_topk     exact top-k routing per row: radix-select of the candidates from
+//                   tensor-core scores, fp32 cosine rescoring of the candidates, ties by
+//                   chunk id, greedy token budget, and the memory row list in chunk order.
+#include "common.cuh"
+
+namespace pra {
+namespace llama {
+
+// ---------------------------------------------------------------- rope / copy
+__global__ void rope_copy_kernel(RopeCopyArgs a) {
+  const int m = blockIdx.x;
+  const int half = a.head_dim / 2;
+  const int pairs = a.heads * half;
+  const __nv_bfloat16* src = a.src + (int64_t)m * a.src_stride;
+  const int64_t drow = a.dst_rows ? a.dst_rows[m] : m;
+  __nv_bfloat16* dst = a.dst + drow * a.dst_stride;
+  const int pos = a.pos ? a.pos[m] : 0;
+  for (int e = blockIdx.y * blockDim.x + threadIdx.x; e < pairs; e += gridDim.y * blockDim.x) {
+    const int h = e / half, i = e - h * half;
+    const int c0 = h * a.head_dim + i, c1 = c0 + half;
+    const float x0 = __bfloat162float(src[c0]), x1 = __bfloat162float(src[c1]);
+    if (a.cos_t == nullptr) {
+      dst[c0] = src[c0];
+      dst[c1] = src[c1];
+    } else {
+      const float c = a.cos_t[(int64_t)pos * half + i], s = a.sin_t[(int64_t)pos * half + i];
+      dst[c0] = __float2bfloat16(x0 * c - x1 * s);
+      dst[c1] = __float2bfloat16(x1 * c + x0 * s);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- swiglu
+__global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int64_t M, int F, __nv_bfloat16* __restrict__ out) {
+  const int64_t pairs = M * (F / 2);
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < pairs; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = e / (F / 2);
+    const int j = 2 * (int)(e - m * (F / 2));
+    const float2 g = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(gu + m * 2 * F + j));
+    const float2 u = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(gu + m * 2 * F + F + j));
+    const float a = g.x / (1.f + __expf(-g.x)) * u.x;
+    const float b = g.y / (1.f + __expf(-g.y)) * u.y;
+    *reinterpret_cast<__nv_bfloat162*>(out + m * F + j) = __floats2bfloat162_rn(a, b);
+  }
+}
+
+// ---------------------------------------------------------------- decode attention
+constexpr int DT = 128;   // threads (4 warps, 16 keys each per block of 64)
+constexpr int DBN = 64;   // keys per block
+constexpr float LOG2E = 1.4426950408889634f;
+
+template <int D>
+struct DSmem {
+  static constexpr int LD = D + 8;
+};
+
+template <int D>
+__global__ void __launch_bounds__(DT) decode_kernel(DecodeAttnParams p) {
+  constexpr int LD = DSmem<D>::LD;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __nv_bfloat16* sq = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [16][LD]
+  __nv_bfloat16* sk = sq + 16 * LD;                                 // [2][DBN][LD]
+  __nv_bfloat16* sv = sk + 2 * DBN * LD;                            // [2][DBN][LD]
+  float* red = reinterpret_cast<float*>(sv + 2 * DBN * LD);         // [4][16][D + 2]
+
+  const int G = p.H / p.Hkv;
+  const int b = blockIdx.x / p.Hkv, kvh = blockIdx.x % p.Hkv;
+  const int split = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mem_len = p.mem_len ? p.mem_len[b] : 0;
+  const int total = mem_len + (p.loc_len ? p.loc_len[b] : 0);
+  const int k0 = split * p.split_keys, k1 = min(total, k0 + p.split_keys);
+  const int64_t part = ((int64_t)b * p.H + kvh * G) * p.n_split + split;  // first head of the group
+
+  // queries of the group (rows >= G are zero)
+  for (int c = threadIdx.x; c < 16 * (D / 8); c += DT) {
+    const int r = c / (D / 8), col = (c % (D / 8)) * 8;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < G) v = *reinterpret_cast<const uint4*>(p.q + (int64_t)b * p.q_row + (kvh * G + r) * D + col);
+    *reinterpret_cast<uint4*>(sq + r * LD + col) = v;
+  }
+  auto key_addr = [&](int j, bool value) -> const __nv_bfloat16* {
+    if (j < mem_len) {
+      const int row = p.mem_idx[(int64_t)b * p.mem_max + j];
+      return (value ? p.mem_v : p.mem_k) + (int64_t)row * p.mem_row + kvh * D;
+    }
+    const int t = j - mem_len;
+    return (value ? p.loc_v : p.loc_k) + (int64_t)b * p.loc_batch + (int64_t)t * p.loc_row + kvh * D;
+  };
+  auto load_block = [&](int start, int buf) {
+    for (int c = threadIdx.x; c < DBN * (D / 8); c += DT) {
+      const int r = c / (D / 8), col = (c % (D / 8)) * 8;
+      const int j = start + r;
+      const bool ok = j < k1;
+      cp_async16(sk + (buf * DBN + r) * LD + col, ok ? key_addr(j, false) + col : p.q, ok);
+      cp_async16(sv + (buf * DBN + r) * LD + col, ok ? key_addr(j, true) + col : p.q, ok);
+    }
+    cp_async_commit();
+  };
+
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  const float sl2 = p.scale * LOG2E;
+  const int n_blocks = k1 > k0 ? (k1 - k0 + DBN - 1) / DBN : 0;
+  if (n_blocks > 0) load_block(k0, 0);
+  __syncthreads();
+  for (int it = 0; it < n_blocks; ++it) {
+    const int buf = it & 1;
+    if (it + 1 < n_blocks) {
+      load_block(k0 + (it + 1) * DBN, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    // S = Q[16 x D] . K[16 keys of this warp]^T
+    float s[2][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+    const __nv_bfloat16* kb = sk + (buf * DBN + warp * 16) * LD;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t a[4], bb[4];
+      ldmatrix_x4(a, smem_u32(sq + (lane & 15) * LD + kk * 16 + (lane >> 4) * 8));
+      const int row = ((lane >> 4) & 1) * 8 + (lane & 7);
+      ldmatrix_x4(bb, smem_u32(kb + row * LD + kk * 16 + ((lane >> 3) & 1) * 8));
+      mma_bf16_16816(s[0], a, bb);
+      mma_bf16_16816(s[1], a, bb + 2);
+    }
+    const int key_base = k0 + it * DBN + warp * 16;
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = key_base + nb * 8 + (lane & 3) * 2 + (e & 1);
+        if (key >= k1) s[nb][e] = -INFINITY;
+        mx[e >> 1] = fmaxf(mx[e >> 1], s[nb][e]);
+      }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+      const float m_new = fmaxf(m_run[r], mx[r]);
+      const float corr = (m_new == -INFINITY) ? 1.f : exp2f((m_run[r] - m_new) * sl2);
+      m_run[r] = m_new;
+      l_run[r] *= corr;
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) {
+        o[i][2 * r] *= corr;
+        o[i][2 * r + 1] *= corr;
+      }
+    }
+#pragma unroll
+    for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = e >> 1;
+        const float v = (m_run[r] == -INFINITY) ? 0.f : exp2f((s[nb][e] - m_run[r]) * sl2);
+        s[nb][e] = v;
+        l_run[r] += v;
+      }
+    // O += P[16 x 16] . V[16 keys x D]
+    uint32_t a[4];
+    a[0] = pack_bf16(s[0][0], s[0][1]);
+    a[1] = pack_bf16(s[0][2], s[0][3]);
+    a[2] = pack_bf16(s[1][0], s[1][1]);
+    a[3] = pack_bf16(s[1][2], s[1][3]);
+    const __nv_bfloat16* vb = sv + (buf * DBN + warp * 16) * LD;
+#pragma unroll
+    for (int np = 0; np < D / 16; ++np) {
+      uint32_t bb[4];
+      const int mm = lane >> 3;
+      const int row = (mm & 1) * 8 + (lane & 7);
+      ldmatrix_x4_trans(bb, smem_u32(vb + row * LD + np * 16 + (mm >> 1) * 8));
+      mma_bf16_16816(o[2 * np], a, bb);
+      mma_bf16_16816(o[2 * np + 1], a, bb + 2);
+    }
+    __syncthreads();
+  }
+  // merge the four warps' partials (rows: lane >> 2 and + 8)
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 1);
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 2);
+  }
+  constexpr int RS = D + 2;  // per (warp, row): o[D], m, l
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int row = (lane >> 2) + 8 * r;
+    float* dst = red + (warp * 16 + row) * RS;
+#pragma unroll
+    for (int nb = 0; nb < D / 8; ++nb) {
+      const int col = nb * 8 + (lane & 3) * 2;
+      dst[col] = o[nb][2 * r];
+      dst[col + 1] = o[nb][2 * r + 1];
+    }
+    if ((lane & 3) == 0) {
+      dst[D] = m_run[r];
+      dst[D + 1] = l_run[r];
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * D; e += DT) {
+    const int row = e / D, col = e % D;
+    float M = -INFINITY;
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, red[(w * 16 + row) * RS + D]);
+    float acc = 0.f, L = 0.f;
+    for (int w = 0; w < 4; ++w) {
+      const float* src = red + (w * 16 + row) * RS;
+      const float f = (src[D] == -INFINITY) ? 0.f : exp2f((src[D] - M) * sl2);
+      acc += src[col] * f;
+      L += src[D + 1] * f;
+    }
+    const int64_t at = part + (int64_t)row * p.n_split;
+    p.part_o[at * D + col] = acc;
+    if (col == 0) {
+      p.part_ml[at * 2] = M == -INFINITY ? -INFINITY : M * p.scale;  // natural-log units
+      p.part_ml[at * 2 + 1] = L;
+    }
+  }
+}
+
+// Merge the splits of each (row, head): out = sum_s o_s e^{m_s - M} / sum_s l_s e^{m_s - M}.
+// With export_ml the merged (M, L) and unnormalised out are also written (cross-GPU combine).
+__global__ void decode_merge_kernel(DecodeAttnParams p, int D) {
+  const int bh = blockIdx.x;
+  const int b = bh / p.H, h = bh % p.H;
+  const int64_t base = (int64_t)bh * p.n_split;
+  float M = -INFINITY;
+  for (int s = 0; s < p.n_split; ++s) M = fmaxf(M, p.part_ml[(base + s) * 2]);
+  float L = 0.f;
+  for (int s = 0; s < p.n_split; ++s) {
+    const float m = p.part_ml[(base + s) * 2];
+    L += m == -INFINITY ? 0.f : p.part_ml[(base + s) * 2 + 1] * __expf(m - M);
+  }
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < p.n_split; ++s) {
+      const float m = p.part_ml[(base + s) * 2];
+      if (m != -INFINITY) acc += p.part_o[(base + s) * D + d] * __expf(m - M);
+    }
+    if (p.out) p.out[(int64_t)b * p.out_row + h * D + d] = __float2bfloat16(L > 0.f ? acc / L : 0.f);
+    if (p.export_o) p.export_o[(int64_t)bh * D + d] = acc;
+  }
+  if (threadIdx.x == 0 && p.export_ml) {
+    p.export_ml[bh * 2] = M;
+    p.export_ml[bh * 2 + 1] = L;
+  }
+}
+
+// ---------------------------------------------------------------- routing top-k
+constexpr int RT = 1024;
+constexpr int MAX_CAND = 512;
+
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t prefix, prefix_mask;
+  __shared__ int need;
+  __shared__ int n_cand;
+  __shared__ int cand[MAX_CAND];
+  __shared__ float cscore[MAX_CAND];
+  __shared__ int picked[MAX_CAND];
+  __shared__ float red[32];
+  const int b = blockIdx.x;
+  const int c0 = a.ns_start[b], c1 = a.ns_end[b];
+  const int n = max(c1 - c0, 0);
+  const float* row = a.scores + (int64_t)b * a.score_stride;
+  const int kc = min(a.k_cand, min(n, MAX_CAND));
+  if (threadIdx.x == 0) {
+    prefix = 0;
+    prefix_mask = 0;
+    need = kc;
+    n_cand = 0;
+  }
+  __syncthreads();
+  // 1. radix select (MSB first, 8-bit digits): the kc-th largest approximate score
+  for (int shift = 24; shift >= 0 && kc > 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += RT) hist[i] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += RT) {
+      const uint32_t key = order_key(row[c0 + i]);
+      if ((key & prefix_mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int remaining = need;
+      int digit = 255;
+      for (; digit > 0; --digit) {
+        if ((int)hist[digit] >= remaining) break;
+        remaining -= hist[digit];
+      }
+      prefix |= (uint32_t)digit << shift;
+      prefix_mask |= 255u << shift;
+      need = remaining;
+    }
+    __syncthreads();
+  }
+  // 2. candidates: every chunk strictly above the threshold, then ties at it (lowest ids first)
+  const uint32_t thr = prefix;
+  for (int i = threadIdx.x; i < n && kc > 0; i += RT) {
+    if (order_key(row[c0 + i]) > thr) {
+      const int slot = atomicAdd(&n_cand, 1);
+      if (slot < MAX_CAND) cand[slot] = c0 + i;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && kc > 0) {
+    int cnt = min(n_cand, MAX_CAND);
+    for (int i = 0; i < n && cnt < kc; ++i)
+      if (order_key(row[c0 + i]) == thr) cand[cnt++] = c0 + i;
+    n_cand = cnt;
+  }
+  __syncthreads();
+  const int nc = n_cand;
+  // 3. exact fp32 cosine of the candidates (warp per candidate)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float sq = 0.f;
+  for (int d = threadIdx.x; d < a.D; d += RT) {
+    const float v = a.query[(int64_t)b * a.query_stride + d];
+    sq += v * v;
+  }
+  sq = warp_sum(sq);
+  if (lane == 0) red[warp] = sq;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < RT / 32; ++w) t += red[w];
+    red[0] = 1.f / fmaxf(sqrtf(t), 1e-12f);
+  }
+  __syncthreads();
+  const float qinv = red[0];
+  for (int i = warp; i < nc; i += RT / 32) {
+    const float* g = a.gists + (int64_t)cand[i] * a.D;
+    const float* q = a.query + (int64_t)b * a.query_stride;
+    float acc = 0.f;
+    for (int d = lane; d < a.D; d += 32) acc += q[d] * g[d];
+    acc = warp_sum(acc);
+    if (lane == 0) cscore[i] = acc * qinv;
+  }
+  __syncthreads();
+  // 4. top-k by (-score, chunk id), greedy budget in that order, then chunk order
+  const int k = min(a.k, nc);
+  for (int i = threadIdx.x; i < nc; i += RT) {
+    int rank = 0;
+    for (int j = 0; j < nc; ++j)
+      rank += (cscore[j] > cscore[i] || (cscore[j] == cscore[i] && cand[j] < cand[i])) ? 1 : 0;
+    picked[i] = rank;  // rank among candidates
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // order[r] = candidate index of rank r (ranks are unique)
+    int order[64];
+    const int kk = min(k, 64);
+    for (int i = 0; i < nc; ++i)
+      if (picked[i] < kk) order[picked[i]] = i;
+    int used = 0, chosen = 0;
+    int sel[64];
+    for (int r = 0; r < kk; ++r) {
+      const int c = cand[order[r]];
+      const int len = a.chunk_len[c];
+      if (a.budget >= 0 && used + len > a.budget) continue;
+      used += len;
+      sel[chosen++] = c;
+    }
+    // chunk order (insertion sort, k <= 64)
+    for (int i = 1; i < chosen; ++i) {
+      const int v = sel[i];
+      int j = i - 1;
+      while (j >= 0 && sel[j] > v) {
+        sel[j + 1] = sel[j];
+        --j;
+      }
+      sel[j + 1] = v;
+    }
+    int written = 0;
+    for (int i = 0; i < chosen; ++i) {
+      const int c = sel[i];
+      if (a.sel_out) a.sel_out[(int64_t)b * a.k + i] = c;
+      for (int t = 0; t < a.chunk_len[c] && written < a.mem_max; ++t)
+        a.mem_idx[(int64_t)b * a.mem_max + written++] = a.chunk_row0[c] + t;
+    }
+    for (int i = chosen; i < a.k && a.sel_out; ++i) a.sel_out[(int64_t)b * a.k + i] = -1;
+    a.mem_len[b] = written;
+  }
+}
+
+}  // namespace llama
+}  // namespace pra
+
+cudaError_t pra_rope_copy(const RopeCopyArgs& a, cudaStream_t st) {
+  if (a.M == 0) return cudaSuccess;
+  const int pairs = a.heads * (a.head_dim / 2);
+  const int threads = 256;
+  dim3 grid(a.M, (pairs + threads - 1) / threads);
+  pra::llama::rope_copy_kernel<<<grid, threads, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t pra_silu_mul(const __nv_bfloat16* gate_up, int64_t M, int F, __nv_bfloat16* out, cudaStream_t st) {
+  if (M == 0) return cudaSuccess;
+  if (F % 2) return cudaErrorInvalidValue;
+  const int64_t pairs = M * (F / 2);
+  const int64_t want = (pairs + 255) / 256;
+  const int blocks = (int)(want < 148 * 16 ? want : 148 * 16);
+  pra::llama::silu_mul_kernel<<<blocks, 256, 0, st>>>(gate_up, M, F, out);
+  return cudaGetLastError();
+}
+
+template <int D>
+static cudaError_t launch_decode(DecodeAttnParams p, cudaStream_t st) {
+  using namespace pra::llama;
+  constexpr int LD = DSmem<D>::LD;
+  const size_t smem = (size_t)(16 + 4 * DBN) * LD * sizeof(__nv_bfloat16) + 4 * 16 * (D + 2) * sizeof(float);
+  PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  decode_kernel<D><<<dim3(p.B * p.Hkv, p.n_split), DT, smem, st>>>(p);
+  PRA_RETURN_IF_ERROR(cudaGetLastError());
+  decode_merge_kernel<<<p.B * p.H, 128, 0, st>>>(p, D);
+  return cudaGetLastError();
+}
+
+cudaError_t pra_decode_attention(const DecodeAttnParams& p, int head_dim, cudaStream_t st) {
+  if (p.B == 0) return cudaSuccess;
+  if (p.H % p.Hkv || p.H / p.Hkv > 16 || p.split_keys % pra::llama::DBN) return cudaErrorInvalidValue;
+  switch (head_dim) {
+    case 64: return launch_decode<64>(p, st);
+    case 128: return launch_decode<128>(p, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t pra_route_topk(const RouteTopkArgs& a, cudaStream_t st) {
+  if (a.B == 0) return cudaSuccess;
+  if (a.k > 64 || a.k_cand > pra::llama::MAX_CAND) return cudaErrorInvalidValue;
+  pra::llama::route_topk_kernel<<<a.B, pra::llama::RT, 0, st>>>(a);
+  return cudaGetLastError();
+}

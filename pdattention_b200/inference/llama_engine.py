@@ -1,0 +1,382 @@
+"""Device inference engine for the PRA Llama-family models (prefill + decode on sm_100a kernels).
+
+Layout on one GPU (tensor parallelism shards the head / column dimensions, see
+``pdattention_b200.parallel.tp``):
+
+* weights (bf16): per layer a fused ``[q | k | v]`` projection (+ Qwen2 biases), the
+  output projection, a fused ``[gate | up]`` projection and the down projection;
+* chunk memory (``ChunkMemory``): per layer one pool ``[rows, 2 * kv_dim]`` holding the
+  post-rotary keys and the values of every reference token (chunk c owns rows
+  ``row0[c] .. row0[c] + len[c]``), plus the routing gists (mean pre-rotary key per
+  chunk) in fp32 (exact rescoring) and bf16 (tensor-core scoring);
+* local KV cache: per layer ``[2, B, max_len, kv_dim]`` for the direct window and the
+  generated tokens.
+
+Per layer and step: RMSNorm -> QKV GEMM -> routing (tensor-core scores + exact
+top-k) -> rotary copy of q in place and of k/v into the cache -> attention over
+[selected memory ; local causal] -> O GEMM with the residual fused -> RMSNorm ->
+gate/up GEMM -> SwiGLU -> down GEMM with the residual fused.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from ..models.llama import PRALlamaConfig, PRALlamaReference
+from ..ops import _ext
+
+
+# ---------------------------------------------------------------------------
+# Weights
+# ---------------------------------------------------------------------------
+
+@dataclass
+class LayerWeights:
+    ln_in: torch.Tensor
+    qkv: torch.Tensor          # [q_dim + 2 kv_dim (local shard), d]
+    qkv_bias: torch.Tensor | None
+    o: torch.Tensor            # [d, q_dim (local shard)]
+    ln_post: torch.Tensor
+    gate_up: torch.Tensor      # [2 F (local shard), d]
+    down: torch.Tensor         # [d, F (local shard)]
+
+
+class LlamaWeights:
+    """bf16 device weights (optionally one tensor-parallel shard)."""
+
+    def __init__(self, cfg: PRALlamaConfig, layers: list[LayerWeights], embed: torch.Tensor, norm: torch.Tensor,
+                 head: torch.Tensor, tp_rank: int = 0, tp_size: int = 1):
+        self.cfg, self.layers, self.embed, self.norm, self.head = cfg, layers, embed, norm, head
+        self.tp_rank, self.tp_size = tp_rank, tp_size
+
+    @staticmethod
+    def _shard_rows(t: torch.Tensor, rank: int, size: int) -> torch.Tensor:
+        n = t.shape[0] // size
+        return t[rank * n:(rank + 1) * n]
+
+    @classmethod
+    def from_reference(cls, model: PRALlamaReference, device, tp_rank: int = 0, tp_size: int = 1) -> "LlamaWeights":
+        cfg = model.cfg
+        if cfg.num_key_value_heads % tp_size or cfg.intermediate_size % tp_size:
+            raise ValueError("tensor-parallel size must divide the KV heads and the MLP width")
+        dev = torch.device(device)
+        bf = lambda t: t.detach().to(dev, torch.bfloat16).contiguous()  # noqa: E731
+        rows = cls._shard_rows
+        layers = []
+        for layer in model.model.layers:
+            a, m = layer.self_attn, layer.mlp
+            q = rows(a.q_proj.weight, tp_rank, tp_size)
+            k = rows(a.k_proj.weight, tp_rank, tp_size)
+            v = rows(a.v_proj.weight, tp_rank, tp_size)
+            bias = None
+            if cfg.attention_bias:
+                bias = bf(torch.cat([rows(a.q_proj.bias, tp_rank, tp_size), rows(a.k_proj.bias, tp_rank, tp_size),
+                                     rows(a.v_proj.bias, tp_rank, tp_size)]))
+            o = a.o_proj.weight.t().contiguous()
+            layers.append(LayerWeights(
+                ln_in=bf(layer.input_layernorm.weight), qkv=bf(torch.cat([q, k, v])), qkv_bias=bias,
+                o=bf(rows(o, tp_rank, tp_size).t()), ln_post=bf(layer.post_attention_layernorm.weight),
+                gate_up=bf(torch.cat([rows(m.gate_proj.weight, tp_rank, tp_size),
+                                      rows(m.up_proj.weight, tp_rank, tp_size)])),
+                down=bf(rows(m.down_proj.weight.t().contiguous(), tp_rank, tp_size).t())))
+        head = model.head_weight()
+        return cls(cfg, layers, bf(model.model.embed_tokens.weight), bf(model.model.norm.weight), bf(head),
+                   tp_rank, tp_size)
+
+    @classmethod
+    def random(cls, cfg: PRALlamaConfig, device, seed: int = 0, std: float = 0.02, tp_rank: int = 0,
+               tp_size: int = 1) -> "LlamaWeights":
+        """Random-init weights generated directly on the device (8B-class models)."""
+        dev = torch.device(device)
+        gen = torch.Generator(device=dev).manual_seed(seed + 1000 * tp_rank)
+
+        def rand(*shape):
+            return (torch.randn(*shape, generator=gen, device=dev, dtype=torch.float32) * std).to(torch.bfloat16)
+
+        d, f = cfg.hidden_size, cfg.intermediate_size // tp_size
+        qd, kd = cfg.q_dim // tp_size, cfg.kv_dim // tp_size
+        ones = lambda: torch.ones(d, device=dev, dtype=torch.bfloat16)  # noqa: E731
+        layers = [LayerWeights(ln_in=ones(), qkv=rand(qd + 2 * kd, d),
+                               qkv_bias=rand(qd + 2 * kd) if cfg.attention_bias else None, o=rand(d, qd),
+                               ln_post=ones(), gate_up=rand(2 * f, d), down=rand(d, f))
+                  for _ in range(cfg.num_hidden_layers)]
+        gen_shared = torch.Generator(device=dev).manual_seed(seed)  # embeddings / head replicated
+        embed = (torch.randn(cfg.vocab_size, d, generator=gen_shared, device=dev) * std).to(torch.bfloat16)
+        head = embed if cfg.tie_word_embeddings else \
+            (torch.randn(cfg.vocab_size, d, generator=gen_shared, device=dev) * std).to(torch.bfloat16)
+        return cls(cfg, layers, embed, ones(), head, tp_rank, tp_size)
+
+
+# ---------------------------------------------------------------------------
+# Chunk memory
+# ---------------------------------------------------------------------------
+
+class ChunkMemory:
+    """Per-layer chunk K/V pools and routing gists on the device."""
+
+    def __init__(self, cfg: PRALlamaConfig, n_chunks: int, kv_dim: int, device, chunk_tokens: int | None = None,
+                 gist_dim: int | None = None):
+        self.cfg = cfg
+        self.C = n_chunks
+        self.C_pad = (n_chunks + 7) // 8 * 8  # score rows stay 32-byte aligned for the scoring GEMM
+        self.tc = chunk_tokens or cfg.chunk_tokens
+        self.kv_dim = kv_dim                  # K/V width held here (this rank's KV heads)
+        self.gist_dim = gist_dim or kv_dim    # routing width (every KV head: gists are replicated)
+        L = cfg.num_hidden_layers
+        dev = torch.device(device)
+        self.pool = torch.empty((L, n_chunks * self.tc, 2 * kv_dim), device=dev, dtype=torch.bfloat16)
+        # gist tables [3, L, C, 1, gist_dim]: routing copy (normalised), key mean, value mean (unused)
+        self.tables = torch.zeros((3, L, self.C_pad, 1, self.gist_dim), device=dev, dtype=torch.float32)
+        self.gn, self.gk, self.gv = self.tables.unbind(0)
+        self.gn_bf16 = torch.zeros((L, self.C_pad, self.gist_dim), device=dev, dtype=torch.bfloat16)
+        self.count = torch.zeros((L, self.C_pad), device=dev, dtype=torch.int32)
+        self.chunk_len = torch.zeros(self.C_pad, device=dev, dtype=torch.int32)
+        self.chunk_row0 = (torch.arange(self.C_pad, device=dev, dtype=torch.int32) * self.tc)
+
+    def k(self, layer: int) -> torch.Tensor:
+        return self.pool[layer][:, : self.kv_dim]
+
+    def v(self, layer: int) -> torch.Tensor:
+        return self.pool[layer][:, self.kv_dim:]
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.pool, self.tables, self.gn_bf16))
+
+
+# ---------------------------------------------------------------------------
+# Engine
+# ---------------------------------------------------------------------------
+
+class PRALlamaEngine:
+    """Batched prefill / decode of a PRA Llama-family model on one GPU (or one TP shard)."""
+
+    def __init__(self, weights: LlamaWeights, device, tp=None, decode_split_keys: int = 512, k_cand_factor: int = 4):
+        self.w = weights
+        self.cfg = weights.cfg
+        self.device = torch.device(device)
+        self.tp = tp  # tensor-parallel communicator (None: one GPU)
+        cfg = self.cfg
+        self.tp_size = weights.tp_size
+        self.heads = cfg.num_attention_heads // self.tp_size
+        self.kv_heads = cfg.num_key_value_heads // self.tp_size
+        self.q_dim = self.heads * cfg.head_dim
+        self.kv_dim = self.kv_heads * cfg.head_dim
+        self.split_keys = decode_split_keys
+        self.k_cand_factor = k_cand_factor
+        self.ext = _ext.require()
+        self._rope_cache: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
+        self.memory: ChunkMemory | None = None
+        self.cache: torch.Tensor | None = None
+        self.cache_len: torch.Tensor | None = None
+        self.namespace: tuple[torch.Tensor, torch.Tensor] | None = None
+        self.last_selection: dict[int, torch.Tensor] = {}
+
+    # -- helpers ----------------------------------------------------------------
+    def rope_tables(self, max_pos: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """fp32 cos/sin ``[max_pos, Dh/2]`` computed in fp64 (cached, grown on demand)."""
+        have = max(self._rope_cache) if self._rope_cache else 0
+        if have < max_pos:
+            cfg = self.cfg
+            n = max(max_pos, 2 * have)
+            half = cfg.head_dim // 2
+            inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, half, dtype=torch.float64) / half))
+            ang = torch.arange(n, dtype=torch.float64)[:, None] * inv[None]
+            self._rope_cache = {n: (ang.cos().float().to(self.device), ang.sin().float().to(self.device))}
+        return next(iter(self._rope_cache.values()))
+
+    def _norm(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        return self.ext.norm_fwd(x, w, None, self.cfg.rms_norm_eps, True)[0]
+
+    def _gemm(self, x, w, bias=None, residual=None) -> torch.Tensor:
+        out = torch.empty((x.shape[0], w.shape[0]), device=x.device, dtype=torch.bfloat16)
+        self.ext.gemm("tn", x, w, residual, out, bias, None, 1.0, 1.0 if residual is not None else 0.0, None)
+        return out
+
+    def _row_parallel(self, x, w, residual) -> torch.Tensor:
+        """out = residual + x @ w^T, summed over tensor-parallel ranks."""
+        if self.tp is None:
+            return self._gemm(x, w, residual=residual)
+        return self.tp.gemm_allreduce(x, w, residual)
+
+    def _mlp(self, lw: LayerWeights, x: torch.Tensor) -> torch.Tensor:
+        h = self._norm(x, lw.ln_post)
+        gu = self._gemm(h, lw.gate_up)
+        act = torch.empty((x.shape[0], gu.shape[1] // 2), device=x.device, dtype=torch.bfloat16)
+        self.ext.silu_mul(gu, act)
+        return self._row_parallel(act, lw.down, x)
+
+    def _embed(self, ids: torch.Tensor) -> torch.Tensor:
+        return self.w.embed[ids.reshape(-1)].contiguous()
+
+    def _route(self, layer: int, q_rows: torch.Tensor, rows: int):
+        """Routing query (group mean of the pre-rotary query) -> memory row lists."""
+        cfg, mem = self.cfg, self.memory
+        g = cfg.group
+        rq = q_rows.float().view(rows, self.kv_heads, g, cfg.head_dim).mean(2).reshape(rows, self.kv_dim)
+        if self.tp is not None:
+            rq = self.tp.all_gather_columns(rq)  # full kv_dim routing query on every rank
+        rqn = torch.nn.functional.normalize(rq, dim=-1, eps=1e-12).to(torch.bfloat16)
+        scores = torch.empty((rows, mem.C_pad), device=self.device, dtype=torch.float32)
+        self.ext.gemm("tn_f32", rqn, mem.gn_bf16[layer], None, scores, None, None, 1.0, 0.0, None)
+        k = cfg.top_k_chunks
+        budget = cfg.memory_budget_tokens if cfg.memory_budget_tokens is not None else -1
+        mem_max = cfg.memory_tokens_per_row
+        start, end = self.namespace
+        gn = mem.gn[layer].view(mem.C_pad, -1)
+        mem_idx, mem_len, sel = self.ext.route_topk(scores, rq, gn, start, end, mem.chunk_len, mem.chunk_row0, k,
+                                                    min(max(k * self.k_cand_factor, k), 512), budget, mem_max)
+        self.last_selection[layer] = sel
+        return mem_idx, mem_len
+
+    # -- memory build -----------------------------------------------------------------
+    @torch.no_grad()
+    def build_memory(self, chunks: torch.Tensor, lengths: torch.Tensor, batch_chunks: int = 256) -> ChunkMemory:
+        """Encode ``chunks`` ``[C, Tc]`` (each its own sequence from position 0) into a
+        ``ChunkMemory`` (for tensor parallelism: this rank's KV heads of every chunk)."""
+        cfg = self.cfg
+        C, tc = chunks.shape
+        mem = ChunkMemory(cfg, C, self.kv_dim, self.device, tc, gist_dim=cfg.kv_dim)
+        mem.chunk_len[:C].copy_(lengths.to(self.device, torch.int32))
+        cos, sin = self.rope_tables(tc)
+        for c0 in range(0, C, batch_chunks):
+            c1 = min(C, c0 + batch_chunks)
+            self._encode_chunk_batch(mem, chunks[c0:c1].to(self.device), mem.chunk_len[c0:c1], c0, cos, sin)
+        if self.tp is not None:  # gists are computed per KV-head slice; every rank gets all of them
+            self.tp.gather_gists(mem)
+        # bf16 routing copy for the tensor-core scoring GEMM
+        mem.gn_bf16.copy_(mem.gn.view(cfg.num_hidden_layers, mem.C_pad, -1))
+        self.memory = mem
+        return mem
+
+    def _encode_chunk_batch(self, mem: ChunkMemory, ids, lengths, c0, cos, sin):
+        cfg, ext = self.cfg, self.ext
+        n, tc = ids.shape
+        M = n * tc
+        pos = torch.arange(tc, device=self.device, dtype=torch.int32).repeat(n)
+        rows = (torch.arange(M, device=self.device, dtype=torch.int32) + c0 * tc)
+        valid = (torch.arange(tc, device=self.device)[None] < lengths[:, None]).to(torch.uint8).contiguous()
+        dest = torch.arange(c0, c0 + n, device=self.device, dtype=torch.int32)
+        starts = rows.view(n, tc)[:, 0].contiguous()
+        x = self._embed(ids)
+        qd, kd = self.q_dim, self.kv_dim
+        for li, lw in enumerate(self.w.layers):
+            h = self._norm(x, lw.ln_in)
+            qkv = self._gemm(h, lw.qkv, lw.qkv_bias)
+            # gist: mean pre-rotary key of each chunk
+            k_pre = qkv[:, qd: qd + kd]
+            pool = mem.pool[li]
+            gk, gv, gn = (mem.gk[li: li + 1], mem.gv[li: li + 1], mem.gn[li: li + 1]) if self.tp is None else \
+                self.tp.local_gist_tables(mem, li)
+            ext.gist_mean_into(k_pre, qkv[:, qd + kd: qd + 2 * kd], starts - c0 * tc, lengths, dest, gk, gv, gn,
+                               mem.count[li: li + 1])
+            ext.rope_copy(k_pre, pool[:, :kd], rows, pos, cos, sin, self.kv_heads, cfg.head_dim)
+            ext.rope_copy(qkv[:, qd + kd:], pool[:, kd:], rows, None, None, None, self.kv_heads, cfg.head_dim)
+            ext.rope_copy(qkv[:, :qd], qkv[:, :qd], None, pos, cos, sin, self.heads, cfg.head_dim)
+            if li == len(self.w.layers) - 1:
+                break  # the last layer's output is never read
+            kv = pool[c0 * tc: c0 * tc + M].view(n, tc, 2 * kd)
+            a = ext.attention_fwd(qkv.view(n, tc, -1)[:, :, :qd], kv[:, :, :kd], kv[:, :, kd:], self.heads,
+                                  self.kv_heads, cfg.head_dim, None, None, None, None, valid,
+                                  1.0 / math.sqrt(cfg.head_dim))[0]
+            x = self._row_parallel(a.view(M, qd), lw.o, x)
+            x = self._mlp(lw, x)
+
+    # -- prefill / decode ---------------------------------------------------------------
+    def set_namespace(self, start: torch.Tensor, end: torch.Tensor) -> None:
+        """Row b may read chunks ``[start[b], end[b])`` of the memory."""
+        self.namespace = (start.to(self.device, torch.int32).contiguous(), end.to(self.device, torch.int32).contiguous())
+
+    @torch.no_grad()
+    def prefill(self, ids: torch.Tensor, lengths: torch.Tensor, max_new_tokens: int) -> torch.Tensor:
+        """Left-aligned prompts ``ids`` ``[B, T]`` with ``lengths``: fills the local caches and
+        returns the logits of each row's last prompt token ``[B, V]``."""
+        cfg, ext = self.cfg, self.ext
+        B, T = ids.shape
+        ids = ids.to(self.device)
+        lengths = lengths.to(self.device, torch.int32)
+        max_len = T + max_new_tokens
+        L = cfg.num_hidden_layers
+        qd, kd = self.q_dim, self.kv_dim
+        self.cache = torch.zeros((L, 2, B, max_len, kd), device=self.device, dtype=torch.bfloat16)
+        self.cache_len = lengths.clone()
+        self.max_len = max_len
+        cos, sin = self.rope_tables(max_len)
+        M = B * T
+        pos = torch.arange(T, device=self.device, dtype=torch.int32).repeat(B)
+        rows = (torch.arange(B, device=self.device, dtype=torch.int32)[:, None] * max_len
+                + torch.arange(T, device=self.device, dtype=torch.int32)[None]).reshape(-1)
+        valid = (torch.arange(T, device=self.device)[None] < lengths[:, None]).to(torch.uint8).contiguous()
+        last = (torch.arange(B, device=self.device) * T + lengths.long() - 1)
+        x = self._embed(ids)
+        use_memory = self.memory is not None and self.namespace is not None and cfg.top_k_chunks > 0
+        for li, lw in enumerate(self.w.layers):
+            h = self._norm(x, lw.ln_in)
+            qkv = self._gemm(h, lw.qkv, lw.qkv_bias)
+            mem_args = (None, None, None, None)
+            if use_memory and cfg.is_pra_layer(li):
+                mem_idx, mem_len = self._route(li, qkv[last, :qd], B)
+                mem_args = (self.memory.k(li), self.memory.v(li), mem_idx, mem_len)
+            kc = self.cache[li, 0].view(B * max_len, kd)
+            vc = self.cache[li, 1].view(B * max_len, kd)
+            ext.rope_copy(qkv[:, qd: qd + kd], kc, rows, pos, cos, sin, self.kv_heads, cfg.head_dim)
+            ext.rope_copy(qkv[:, qd + kd:], vc, rows, None, None, None, self.kv_heads, cfg.head_dim)
+            ext.rope_copy(qkv[:, :qd], qkv[:, :qd], None, pos, cos, sin, self.heads, cfg.head_dim)
+            a = ext.attention_fwd(qkv.view(B, T, -1)[:, :, :qd], self.cache[li, 0][:, :T], self.cache[li, 1][:, :T],
+                                  self.heads, self.kv_heads, cfg.head_dim, *mem_args, valid,
+                                  1.0 / math.sqrt(cfg.head_dim))[0]
+            x = self._row_parallel(a.view(M, qd), lw.o, x)
+            x = self._mlp(lw, x)
+        return self._logits(x[last])
+
+    def _logits(self, x_last: torch.Tensor) -> torch.Tensor:
+        h = self._norm(x_last.contiguous(), self.w.norm)
+        return self._gemm(h, self.w.head)
+
+    @torch.no_grad()
+    def decode_step(self, token_ids: torch.Tensor) -> torch.Tensor:
+        """One token per row at position ``cache_len[b]``; returns logits ``[B, V]``."""
+        cfg, ext = self.cfg, self.ext
+        B = token_ids.shape[0]
+        qd, kd = self.q_dim, self.kv_dim
+        cos, sin = self.rope_tables(self.max_len)
+        pos = self.cache_len
+        rows = torch.arange(B, device=self.device, dtype=torch.int32) * self.max_len + pos
+        new_len = pos + 1
+        x = self._embed(token_ids.to(self.device))
+        use_memory = self.memory is not None and self.namespace is not None and cfg.top_k_chunks > 0
+        max_keys = cfg.memory_tokens_per_row + self.max_len
+        for li, lw in enumerate(self.w.layers):
+            h = self._norm(x, lw.ln_in)
+            qkv = self._gemm(h, lw.qkv, lw.qkv_bias)
+            mem_args = (None, None, None, None)
+            if use_memory and cfg.is_pra_layer(li):
+                mem_idx, mem_len = self._route(li, qkv[:, :qd], B)
+                mem_args = (self.memory.k(li), self.memory.v(li), mem_idx, mem_len)
+            kc = self.cache[li, 0].view(B * self.max_len, kd)
+            vc = self.cache[li, 1].view(B * self.max_len, kd)
+            ext.rope_copy(qkv[:, qd: qd + kd], kc, rows, pos, cos, sin, self.kv_heads, cfg.head_dim)
+            ext.rope_copy(qkv[:, qd + kd:], vc, rows, None, None, None, self.kv_heads, cfg.head_dim)
+            q = torch.empty((B, qd), device=self.device, dtype=torch.bfloat16)
+            ext.rope_copy(qkv[:, :qd], q, None, pos, cos, sin, self.heads, cfg.head_dim)
+            a = ext.decode_attention(q, self.heads, self.kv_heads, cfg.head_dim, *mem_args, self.cache[li, 0],
+                                     self.cache[li, 1], new_len, max_keys, self.split_keys, False)[0]
+            x = self._row_parallel(a, lw.o, x)
+            x = self._mlp(lw, x)
+        self.cache_len = new_len
+        return self._logits(x)
+
+    @torch.no_grad()
+    def generate(self, ids: torch.Tensor, lengths: torch.Tensor, max_new_tokens: int) -> torch.Tensor:
+        """Greedy decoding: ``[B, max_new_tokens]`` new token ids."""
+        logits = self.prefill(ids, lengths, max_new_tokens)
+        out = []
+        tok = logits.float().argmax(-1)
+        for _ in range(max_new_tokens):
+            out.append(tok)
+            if len(out) == max_new_tokens:
+                break
+            tok = self.decode_step(tok).float().argmax(-1)
+        return torch.stack(out, dim=1)

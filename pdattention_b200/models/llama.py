@@ -376,6 +376,70 @@ class PRALlamaReference(nn.Module):
         return (logits, selections) if return_selection else logits
 
 
+@torch.no_grad()
+def reference_step(model: PRALlamaReference, ids: torch.Tensor, cache: list, memory: LlamaChunkMemory | None,
+                   namespace: list[int] | None):
+    """Incremental fp32 step of ONE row: ``ids`` ``[T]`` continue the sequence whose per-layer
+    post-rotary K/V are in ``cache`` (list of ``[k, v]`` ``[t, Hkv, Dh]``, extended in place).
+    Routing uses the last new token; returns (logits ``[T, V]``, selections per PRA layer)."""
+    cfg = model.cfg
+    t0 = cache[0][0].shape[0] if cache and cache[0][0] is not None else 0
+    T = ids.shape[0]
+    pos = torch.arange(t0, t0 + T, device=ids.device)[None]
+    cos, sin = rope_tables(cfg, pos)
+    x = model.model.embed_tokens(ids[None]).float()
+    picks = []
+    scale = 1.0 / math.sqrt(cfg.head_dim)
+    for li, layer in enumerate(model.model.layers):
+        q, k, v = model._qkv(layer, x)
+        keys_mem = vals_mem = None
+        if memory is not None and namespace and cfg.is_pra_layer(li) and cfg.top_k_chunks > 0:
+            rq = q[0, -1].view(cfg.num_key_value_heads, cfg.group, cfg.head_dim).mean(1).reshape(1, -1)
+            sel = select_chunks(cfg, rq, memory.gist[li], [namespace])[0]
+            picks.append(sel)
+            if sel:
+                keys_mem = torch.cat([memory.k[li][c, : int(memory.length[c])] for c in sel])
+                vals_mem = torch.cat([memory.v[li][c, : int(memory.length[c])] for c in sel])
+        qr, kr = apply_rope(q, cos, sin)[0], apply_rope(k, cos, sin)[0]
+        if cache[li][0] is None:
+            cache[li] = [kr, v[0]]
+        else:
+            cache[li] = [torch.cat([cache[li][0], kr]), torch.cat([cache[li][1], v[0]])]
+        lk, lv = cache[li]
+        n_loc = lk.shape[0]
+        causal = torch.arange(n_loc, device=ids.device)[None, :] <= (t0 + torch.arange(T, device=ids.device))[:, None]
+        if keys_mem is not None:
+            keys, vals = torch.cat([keys_mem, lk]), torch.cat([vals_mem, lv])
+            mask = torch.cat([torch.ones(T, keys_mem.shape[0], dtype=torch.bool, device=ids.device), causal], 1)
+        else:
+            keys, vals, mask = lk, lv, causal
+        g = cfg.group
+        s = torch.einsum("thd,khd->htk", qr, keys.repeat_interleave(g, 1)) * scale
+        p = torch.softmax(s.masked_fill(~mask[None], float("-inf")), dim=-1)
+        a = torch.einsum("htk,khd->thd", p, vals.repeat_interleave(g, 1))[None]
+        x = model._finish_layer(layer, x, a)
+    logits = (model.model.norm(x) @ model.head_weight().t())[0]
+    return logits, picks
+
+
+@torch.no_grad()
+def reference_generate(model: PRALlamaReference, ids: torch.Tensor, length: int, memory, namespace,
+                       max_new_tokens: int):
+    """Greedy fp32 decoding of one row: prefill (routing with the last prompt token), then one
+    token per step (routing with that token).  Returns (new ids, prefill logits of the last
+    prompt token, selections of every step)."""
+    cache = [[None, None] for _ in range(model.cfg.num_hidden_layers)]
+    logits, picks = reference_step(model, ids[:length], cache, memory, namespace)
+    first = logits[-1]
+    steps = [picks]
+    out = [int(first.argmax())]
+    for _ in range(max_new_tokens - 1):
+        logits, picks = reference_step(model, torch.tensor([out[-1]], device=ids.device), cache, memory, namespace)
+        steps.append(picks)
+        out.append(int(logits[-1].argmax()))
+    return out, first, steps
+
+
 def hf_config(cfg: PRALlamaConfig):
     """The matching Hugging Face config object (for loading weights / parity tests)."""
     import transformers

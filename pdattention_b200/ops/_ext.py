@@ -23,8 +23,8 @@ CSRC = ROOT / "csrc"
 BUILD_DIR = Path(__file__).resolve().parent / "_build"
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
-_SOURCES = ["bindings.cpp", "attention.cu", "norm.cu", "loss_optim.cu", "gist.cu", "routing.cu",
-            "gemm/tn_bias.cu", "gemm/tn_bias_gelu.cu", "gemm/nn.cu", "gemm/nn_dgelu.cu", "gemm/wgrad.cu",
+_SOURCES = ["bindings.cpp", "attention.cu", "norm.cu", "loss_optim.cu", "gist.cu", "routing.cu", "llama.cu",
+            "gemm/tn_bias.cu", "gemm/tn_bias_gelu.cu", "gemm/nn.cu", "gemm/nn_dgelu.cu", "gemm/wgrad.cu", "gemm/tn_f32.cu",
             "colsum_noalloc.cu", "dp_reduce.cu", "driver_shim.cu"]
 
 _module = None
@@ -35,7 +35,8 @@ KERNELS_PER_CALL = {"attention_fwd": 1, "attention_bwd": 3, "gemm": 1, "norm_fwd
                     "cross_entropy": 1, "grad_norm": 2, "adamw": 1, "gist_mean": 1, "gist_kmeans": 1, "route": 1,
                     "gist_mean_into": 1, "gist_kmeans_into": 1,
                     "stack_forward": 0, "dp_allreduce": 1, "dp_signal_words": 0,
-                    "ipc_alloc": 0, "ipc_open": 0, "ipc_close": 0}  # stack_forward: counted per layer by its caller
+                    "ipc_alloc": 0, "ipc_open": 0, "ipc_close": 0,
+                    "rope_copy": 1, "silu_mul": 1, "decode_attention": 2, "route_topk": 1}  # stack_forward: counted per layer by its caller
 
 
 class LaunchCounter:

@@ -82,3 +82,16 @@ def test_config_presets_and_parameter_counts():
     assert abs(qwen2_7b().parameter_count() / 1e9 - 7.62) < 0.05
     with pytest.raises(ValueError):
         PRALlamaConfig(num_attention_heads=6, num_key_value_heads=4)
+
+
+def test_incremental_reference_matches_full_forward_without_memory():
+    from pdattention_b200.models.llama import reference_step
+
+    cfg = tiny_llama()
+    model = PRALlamaReference(cfg).eval()
+    ids = torch.randint(0, cfg.vocab_size, (9,))
+    full = model(ids[None])[0]
+    cache = [[None, None] for _ in range(cfg.num_hidden_layers)]
+    a, _ = reference_step(model, ids[:6], cache, None, None)
+    b, _ = reference_step(model, ids[6:], cache, None, None)
+    assert torch.allclose(torch.cat([a, b]), full, atol=1e-5)

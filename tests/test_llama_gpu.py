@@ -1,0 +1,171 @@
+"""PRA Llama-family kernels and engine on the GPU against fp32 PyTorch / the fp32 oracle."""
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ext():
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA device required")
+    from pdattention_b200.ops import _ext
+
+    return _ext.require()
+
+
+def test_rope_copy_and_silu_mul(ext):
+    from pdattention_b200.models.llama import apply_rope, rope_tables, tiny_llama
+
+    cfg = tiny_llama(head_dim=64)
+    torch.manual_seed(0)
+    M, H = 37, 3
+    x = torch.randn(M, H * 64, device="cuda").bfloat16()
+    pos = torch.randint(0, 500, (M,), device="cuda", dtype=torch.int32)
+    half = 32
+    inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, half, dtype=torch.float64) / half))
+    ang = torch.arange(600, dtype=torch.float64)[:, None] * inv[None]
+    cos_t, sin_t = ang.cos().float().cuda(), ang.sin().float().cuda()
+    out = torch.empty(2 * M, H * 64, device="cuda").bfloat16()
+    rows = (torch.arange(M, device="cuda", dtype=torch.int32) * 2 + 1)
+    ext.rope_copy(x, out, rows, pos, cos_t, sin_t, H, 64)
+    c, s = rope_tables(cfg, pos[None].cpu().long())
+    ref = apply_rope(x.float().cpu().view(1, M, H, 64), c, s).view(M, H * 64)
+    assert torch.allclose(out[1::2].float().cpu(), ref, atol=2e-2, rtol=2e-2)
+    gu = torch.randn(M, 2 * 96, device="cuda").bfloat16()
+    act = torch.empty(M, 96, device="cuda").bfloat16()
+    ext.silu_mul(gu, act)
+    g, u = gu.float()[:, :96], gu.float()[:, 96:]
+    assert torch.allclose(act.float(), F.silu(g) * u, atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("head_dim", [64, 128])
+def test_decode_attention_matches_softmax(ext, head_dim):
+    torch.manual_seed(1)
+    B, H, Hkv, max_len = 3, 8, 2, 300
+    q = torch.randn(B, H * head_dim, device="cuda").bfloat16()
+    pool = torch.randn(500, 2 * Hkv * head_dim, device="cuda").bfloat16()
+    mk, mv = pool[:, : Hkv * head_dim], pool[:, Hkv * head_dim:]
+    mem_len = torch.tensor([70, 0, 130], device="cuda", dtype=torch.int32)
+    mem_idx = torch.randint(0, 500, (B, 130), device="cuda", dtype=torch.int32)
+    cache = torch.randn(2, B, max_len, Hkv * head_dim, device="cuda").bfloat16()
+    loc_len = torch.tensor([5, 300, 129], device="cuda", dtype=torch.int32)
+    out, eo, eml = ext.decode_attention(q, H, Hkv, head_dim, mk, mv, mem_idx, mem_len, cache[0], cache[1], loc_len,
+                                        130 + max_len, 128, True)
+    g = H // Hkv
+    for b in range(B):
+        n_m, n_l = int(mem_len[b]), int(loc_len[b])
+        keys = torch.cat([mk[mem_idx[b, :n_m].long()], cache[0, b, :n_l]]).float().view(-1, Hkv, head_dim)
+        vals = torch.cat([mv[mem_idx[b, :n_m].long()], cache[1, b, :n_l]]).float().view(-1, Hkv, head_dim)
+        qb = q[b].float().view(H, head_dim)
+        s = torch.einsum("hd,khd->hk", qb, keys.repeat_interleave(g, 1)) / math.sqrt(head_dim)
+        ref = torch.einsum("hk,khd->hd", torch.softmax(s, -1), vals.repeat_interleave(g, 1)).reshape(-1)
+        assert torch.allclose(out[b].float(), ref, atol=2e-2, rtol=2e-2), (b, (out[b].float() - ref).abs().max())
+        lse = torch.logsumexp(s, -1)
+        got = eml[b, :, 0] + torch.log(eml[b, :, 1])
+        assert torch.allclose(got, lse, atol=1e-2)
+
+
+def test_route_topk_exact_with_ties(ext):
+    torch.manual_seed(2)
+    B, C, D, k = 4, 1000, 64, 16
+    gists = F.normalize(torch.randn(C + 8, D, device="cuda"), dim=-1)
+    gists[10] = gists[3]  # exact tie: lower id must win
+    query = torch.randn(B, D, device="cuda")
+    query[0] = gists[3] * 2
+    approx = (F.normalize(query, dim=-1).bfloat16().float() @ gists.bfloat16().float().t()).contiguous()
+    start = torch.tensor([0, 0, 100, 990], device="cuda", dtype=torch.int32)
+    end = torch.tensor([C, 500, 900, C], device="cuda", dtype=torch.int32)
+    clen = torch.full((C + 8,), 8, device="cuda", dtype=torch.int32)
+    clen[::7] = 5
+    row0 = torch.arange(C + 8, device="cuda", dtype=torch.int32) * 8
+    mem_idx, mem_len, sel = ext.route_topk(approx, query, gists, start, end, clen, row0, k, 64, -1, k * 8)
+    exact = F.normalize(query, dim=-1) @ gists.t()
+    for b in range(B):
+        ids = list(range(int(start[b]), int(end[b])))
+        order = sorted(ids, key=lambda c: (-float(exact[b, c]), c))[:k]
+        want = sorted(order)
+        got = [int(c) for c in sel[b] if int(c) >= 0]
+        assert got == want, (b, got, want)
+        rows = [int(row0[c]) + t for c in want for t in range(int(clen[c]))]
+        assert int(mem_len[b]) == len(rows)
+        assert mem_idx[b, : len(rows)].tolist() == rows
+    assert 3 in [int(c) for c in sel[0]] and 10 in [int(c) for c in sel[0]]
+    # a token budget keeps whole chunks greedily in score order
+    mem_idx, mem_len, sel = ext.route_topk(approx, query, gists, start, end, clen, row0, k, 64, 20, k * 8)
+    assert int(mem_len.max()) <= 20
+
+
+def _tiny_setup(seed=0):
+    from pdattention_b200.models.llama import PRALlamaReference, tiny_llama
+
+    torch.manual_seed(seed)
+    cfg = tiny_llama(head_dim=64, hidden_size=128, num_attention_heads=4, num_key_value_heads=2, chunk_tokens=16,
+                     top_k_chunks=3)
+    model = PRALlamaReference(cfg).eval()
+    model.reset_parameters(seed=seed, std=0.08)
+    C = 12
+    chunks = torch.randint(0, cfg.vocab_size, (C, 16))
+    lengths = torch.tensor([16, 16, 11, 16, 16, 9, 16, 16, 16, 13, 16, 16])
+    return cfg, model, chunks, lengths
+
+
+def test_engine_memory_build_matches_oracle(ext):
+    from pdattention_b200.inference.llama_engine import LlamaWeights, PRALlamaEngine
+
+    cfg, model, chunks, lengths = _tiny_setup()
+    ref = model.encode_chunks(chunks, lengths)
+    engine = PRALlamaEngine(LlamaWeights.from_reference(model, "cuda"), "cuda")
+    mem = engine.build_memory(chunks, lengths, batch_chunks=5)
+    for li in range(cfg.num_hidden_layers):
+        for c in range(chunks.shape[0]):
+            n = int(lengths[c])
+            k = mem.k(li)[c * 16: c * 16 + n].float().cpu()
+            assert torch.allclose(k, ref.k[li][c, :n].reshape(n, -1), atol=5e-2, rtol=5e-2), (li, c)
+            v = mem.v(li)[c * 16: c * 16 + n].float().cpu()
+            assert torch.allclose(v, ref.v[li][c, :n].reshape(n, -1), atol=5e-2, rtol=5e-2), (li, c)
+        gref = F.normalize(ref.gist[li], dim=-1)
+        assert torch.allclose(mem.gn[li][: chunks.shape[0], 0].cpu(), gref, atol=2e-2)
+
+
+def test_engine_prefill_and_decode_match_oracle(ext):
+    from pdattention_b200.inference.llama_engine import LlamaWeights, PRALlamaEngine
+    from pdattention_b200.models.llama import reference_step
+
+    cfg, model, chunks, lengths = _tiny_setup(1)
+    ref_mem = model.encode_chunks(chunks, lengths)
+    engine = PRALlamaEngine(LlamaWeights.from_reference(model, "cuda"), "cuda", decode_split_keys=64)
+    engine.build_memory(chunks, lengths)
+    spans = [(0, 12), (0, 6), (4, 12)]
+    engine.set_namespace(torch.tensor([s for s, _ in spans]), torch.tensor([e for _, e in spans]))
+    B, T = 3, 20
+    plen = torch.tensor([20, 13, 7])
+    ids = torch.randint(0, cfg.vocab_size, (B, T))
+    logits = engine.prefill(ids, plen, max_new_tokens=4).float().cpu()
+    sel0 = {li: s.cpu() for li, s in engine.last_selection.items()}
+    caches = [[[None, None] for _ in range(cfg.num_hidden_layers)] for _ in range(B)]
+    agree = total = 0
+    for b in range(B):
+        ns = list(range(*spans[b]))
+        ref_logits, picks = reference_step(model, ids[b, : int(plen[b])], caches[b], ref_mem, ns)
+        ref = ref_logits[-1]
+        cos = F.cosine_similarity(logits[b], ref, dim=0)
+        assert cos > 0.995, (b, float(cos))
+        for li, p in enumerate(picks):
+            got = [int(c) for c in sel0[li][b] if int(c) >= 0]
+            agree += len(set(got) & set(p))
+            total += len(p)
+        assert [int(c) for c in sel0[0][b] if int(c) >= 0] == picks[0]
+    assert agree >= 0.9 * total
+    # teacher-forced decode steps
+    for step in range(3):
+        tok = torch.randint(0, cfg.vocab_size, (B,))
+        got = engine.decode_step(tok).float().cpu()
+        for b in range(B):
+            ref_logits, _ = reference_step(model, tok[b: b + 1], caches[b], ref_mem, list(range(*spans[b])))
+            cos = F.cosine_similarity(got[b], ref_logits[-1], dim=0)
+            assert cos > 0.99, (step, b, float(cos))
