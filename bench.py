@@ -330,6 +330,70 @@ def _reference_arm(root: Path, tokenizer, rank: int, world: int):
     return _Step(step, lambda k: _batches(dm, rank, world, k)), f"TinyGPT-PRA-{n / 1e6:.0f}M (reference fp32)", None
 
 
+def run_decode(impl: str, steps: int, warmup: int, gpus: int, memory_tokens: int | None, batch: int) -> dict:
+    """PRA decode on a Llama-3-8B-architecture model (random weights) with a shared chunk memory."""
+    if impl == "reference":
+        return {"impl": "reference", "unavailable": "the reference has no Llama-family PRA model, no tensor "
+                                                   "parallelism and no decode path for 8B models"}
+    rank, local, world = _env()
+    if gpus != world:
+        raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    tp = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        from pdattention_b200.parallel.tp import TensorParallel
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        tp = TensorParallel()
+    from pdattention_b200.inference.decode_bench import run_decode_benchmark
+    from pdattention_b200.ops._ext import launch_counter
+
+    tokens = memory_tokens or (1 << 20 if world > 1 else 1 << 18)
+    refs = 32
+    counter = launch_counter()
+    clocks = ClockSampler(local)
+    out = run_decode_benchmark(batch=batch, refs=refs, ref_tokens=tokens // refs, steps=steps, warmup=warmup, tp=tp,
+                               clocks=clocks, counter=counter)
+    result = {
+        "metric": "PRA decode tokens/s (Llama-3-8B architecture, sharded chunk memory)",
+        "value": out["tokens_per_s"],
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": warmup,
+        "ms_per_step": out["tpot_p50_ms"],
+        "tpot_p50_ms": out["tpot_p50_ms"],
+        "tpot_p90_ms": out["tpot_p90_ms"],
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (uniform-random token ids for prompts and references), random-init weights",
+        "config": {"model": f"Llama-3-8B architecture ({out['params_b']:.2f}B params)", "global_batch": batch,
+                   "seq_len": out["prompt_tokens"], "memory_tokens": out["memory_tokens"],
+                   "chunk_tokens": out["chunk_tokens"], "gists_per_chunk": 1, "chunk_top_k": out["top_k_chunks"],
+                   "parallelism": f"tp{world}", "memory_gb_per_gpu": round(out["memory_gb_per_gpu"], 2),
+                   "build_tokens_per_s": out["build_tokens_per_s"], "prefill_tokens_per_s": out["prefill_tokens_per_s"],
+                   "l2": "per-step working set (weights, caches, memory) exceeds the 126 MB L2 (no flush)"},
+        "clocks": clocks.summary(),
+        "e2e": {"value": out["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": out["h2d_bytes_per_step"],
+                "d2h_bytes_per_step": out["d2h_bytes_per_step"]},
+        "gpu_launches": out["gpu_launches"],
+    }
+    if tp is not None:
+        tp.close()
+        import torch.distributed as dist
+
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return result
+
+
 class _Unavailable(RuntimeError):
     pass
 
@@ -340,8 +404,20 @@ def main() -> None:
     parser.add_argument("--steps", type=int, default=10)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["pra", "reference"], default="pra")
+    parser.add_argument("--workload", choices=["train", "decode"], default="train",
+                        help="train: TinyGPT-PRA data-parallel training (default); decode: PRA Llama-3-8B decode "
+                             "with a chunk memory (tensor parallel over the GPUs)")
+    parser.add_argument("--memory-tokens", type=int, default=None,
+                        help="decode: total memory tokens (default 1M; 256K on one GPU, whose HBM cannot hold the "
+                             "1M-token K/V of all 32 layers next to the weights and caches)")
+    parser.add_argument("--batch", type=int, default=64)
     args = parser.parse_args()
     rank = _env()[0]
+    if args.workload == "decode":
+        result = run_decode(args.impl, args.steps, max(args.warmup, 3), args.gpus, args.memory_tokens, args.batch)
+        if rank == 0:
+            print(json.dumps(result))
+        return
     try:
         result = run(args.impl, args.steps, max(args.warmup, 3), args.gpus)
     except _Unavailable as exc:

@@ -472,6 +472,58 @@ std::vector<torch::Tensor> route(torch::Tensor query, torch::Tensor gists, torch
 
 }  // namespace
 
+// ---------------------------------------------------------------- tensor-parallel collectives
+void tp_allreduce(std::vector<int64_t> parts, std::vector<int64_t> sigs, int64_t rank,
+                  c10::optional<torch::Tensor> residual, torch::Tensor out, int64_t epoch, int64_t max_spins,
+                  torch::Tensor error) {
+  c10::cuda::CUDAGuard guard(out.device());
+  const int world = parts.size();
+  TORCH_CHECK(world >= 1 && world <= TP_MAX_RANKS && (int)sigs.size() == world, "one part/signal per rank");
+  expect(out, at::kBFloat16, "out");
+  TORCH_CHECK(out.is_contiguous(), "out must be contiguous");
+  TpAllreduceArgs a{};
+  for (int p = 0; p < world; ++p) {
+    a.part[p] = reinterpret_cast<const __nv_bfloat16*>(parts[p]);
+    a.sig[p] = reinterpret_cast<uint32_t*>(sigs[p]);
+  }
+  if (residual.has_value()) {
+    TORCH_CHECK(residual->is_contiguous() && residual->numel() == out.numel(), "residual must match out");
+    a.residual = ptr<const __nv_bfloat16>(*residual);
+  }
+  a.out = ptr<__nv_bfloat16>(out);
+  a.rank = rank;
+  a.world = world;
+  a.n = out.numel();
+  a.epoch = (uint32_t)epoch;
+  a.max_spins = max_spins;
+  a.error = ptr<int>(error);
+  check(pra_tp_allreduce(a, stream()), "tp_allreduce");
+}
+
+void tp_allgather(torch::Tensor src, std::vector<int64_t> dsts, std::vector<int64_t> sigs, int64_t rank,
+                  int64_t epoch, int64_t max_spins, torch::Tensor error) {
+  c10::cuda::CUDAGuard guard(src.device());
+  const int world = dsts.size();
+  TORCH_CHECK(world >= 1 && world <= TP_MAX_RANKS && (int)sigs.size() == world, "one dst/signal per rank");
+  expect(src, at::kFloat, "src");
+  TORCH_CHECK(src.dim() == 2 && src.stride(1) == 1, "src must be [rows, cols] row-major");
+  TpAllgatherArgs a{};
+  a.src = ptr<const float>(src);
+  a.src_stride = src.stride(0);
+  for (int p = 0; p < world; ++p) {
+    a.dst[p] = reinterpret_cast<float*>(dsts[p]);
+    a.sig[p] = reinterpret_cast<uint32_t*>(sigs[p]);
+  }
+  a.rank = rank;
+  a.world = world;
+  a.rows = src.size(0);
+  a.cols = src.size(1);
+  a.epoch = (uint32_t)epoch;
+  a.max_spins = max_spins;
+  a.error = ptr<int>(error);
+  check(pra_tp_allgather(a, stream()), "tp_allgather");
+}
+
 // ---------------------------------------------------------------- Llama-family ops
 // Rotary copy: rows of src (heads * head_dim, unit stride) to dst rows (dst_rows or identity).
 void rope_copy(torch::Tensor src, torch::Tensor dst, c10::optional<torch::Tensor> dst_rows,
@@ -767,6 +819,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("stack_forward", &stack_forward);
   m.def("dp_allreduce", &dp_allreduce);
   m.def("rope_copy", &rope_copy);
+  m.def("tp_allreduce", &tp_allreduce);
+  m.def("tp_allgather", &tp_allgather);
+  m.def("tp_signal_words", [](int64_t world) { return (int64_t)TP_MAX_BLOCKS * world; });
   m.def("silu_mul", &silu_mul);
   m.def("decode_attention", &decode_attention);
   m.def("route_topk", &route_topk);

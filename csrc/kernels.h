@@ -231,3 +231,30 @@ struct RouteTopkArgs {
   int* sel_out;                // [B, k] selected chunk ids in chunk order (-1 pad), or null
 };
 cudaError_t pra_route_topk(const RouteTopkArgs& args, cudaStream_t stream);
+
+// ---- tensor-parallel collectives over peer memory (tp_comm.cu) -------------------------
+constexpr int TP_MAX_RANKS = 8;
+constexpr int TP_MAX_BLOCKS = 296;  // signal slots per rank: TP_MAX_BLOCKS * world
+struct TpAllreduceArgs {
+  const __nv_bfloat16* part[TP_MAX_RANKS];  // every rank's partial (peer addresses)
+  const __nv_bfloat16* residual;            // local [n] or null
+  __nv_bfloat16* out;                       // local [n]
+  uint32_t* sig[TP_MAX_RANKS];              // every rank's signal area
+  int rank, world;
+  int64_t n;                                // elements (multiple of 8)
+  uint32_t epoch;
+  long long max_spins;
+  int* error;
+};
+struct TpAllgatherArgs {
+  const float* src;                         // local [rows, src_stride]
+  int64_t src_stride;
+  float* dst[TP_MAX_RANKS];                 // every rank's [rows, world * cols] buffer
+  uint32_t* sig[TP_MAX_RANKS];
+  int rank, world, rows, cols;
+  uint32_t epoch;
+  long long max_spins;
+  int* error;
+};
+cudaError_t pra_tp_allreduce(const TpAllreduceArgs& args, cudaStream_t stream);
+cudaError_t pra_tp_allgather(const TpAllgatherArgs& args, cudaStream_t stream);

@@ -211,7 +211,7 @@ class PRALlamaEngine:
     def _embed(self, ids: torch.Tensor) -> torch.Tensor:
         return self.w.embed[ids.reshape(-1)].contiguous()
 
-    def _route(self, layer: int, q_rows: torch.Tensor, rows: int):
+    def _route(self, layer: int, q_rows: torch.Tensor, rows: int, namespace=None):
         """Routing query (group mean of the pre-rotary query) -> memory row lists."""
         cfg, mem = self.cfg, self.memory
         g = cfg.group
@@ -224,7 +224,7 @@ class PRALlamaEngine:
         k = cfg.top_k_chunks
         budget = cfg.memory_budget_tokens if cfg.memory_budget_tokens is not None else -1
         mem_max = cfg.memory_tokens_per_row
-        start, end = self.namespace
+        start, end = namespace if namespace is not None else self.namespace
         gn = mem.gn[layer].view(mem.C_pad, -1)
         mem_idx, mem_len, sel = self.ext.route_topk(scores, rq, gn, start, end, mem.chunk_len, mem.chunk_row0, k,
                                                     min(max(k * self.k_cand_factor, k), 512), budget, mem_max)
@@ -241,6 +241,8 @@ class PRALlamaEngine:
         mem = ChunkMemory(cfg, C, self.kv_dim, self.device, tc, gist_dim=cfg.kv_dim)
         mem.chunk_len[:C].copy_(lengths.to(self.device, torch.int32))
         cos, sin = self.rope_tables(tc)
+        if self.tp is not None:  # each row-parallel partial must fit the peer buffer
+            batch_chunks = max(1, min(batch_chunks, self.tp.max_partial // (tc * cfg.hidden_size)))
         for c0 in range(0, C, batch_chunks):
             c1 = min(C, c0 + batch_chunks)
             self._encode_chunk_batch(mem, chunks[c0:c1].to(self.device), mem.chunk_len[c0:c1], c0, cos, sin)
@@ -290,43 +292,57 @@ class PRALlamaEngine:
         self.namespace = (start.to(self.device, torch.int32).contiguous(), end.to(self.device, torch.int32).contiguous())
 
     @torch.no_grad()
-    def prefill(self, ids: torch.Tensor, lengths: torch.Tensor, max_new_tokens: int) -> torch.Tensor:
+    def prefill(self, ids: torch.Tensor, lengths: torch.Tensor, max_new_tokens: int,
+                row_batch: int | None = None) -> torch.Tensor:
         """Left-aligned prompts ``ids`` ``[B, T]`` with ``lengths``: fills the local caches and
-        returns the logits of each row's last prompt token ``[B, V]``."""
-        cfg, ext = self.cfg, self.ext
+        returns the logits of each row's last prompt token ``[B, V]``.  ``row_batch`` bounds
+        how many rows run through the layers at once (activation memory)."""
+        cfg = self.cfg
         B, T = ids.shape
         ids = ids.to(self.device)
         lengths = lengths.to(self.device, torch.int32)
         max_len = T + max_new_tokens
         L = cfg.num_hidden_layers
-        qd, kd = self.q_dim, self.kv_dim
-        self.cache = torch.zeros((L, 2, B, max_len, kd), device=self.device, dtype=torch.bfloat16)
+        self.cache = torch.zeros((L, 2, B, max_len, self.kv_dim), device=self.device, dtype=torch.bfloat16)
         self.cache_len = lengths.clone()
         self.max_len = max_len
+        step = row_batch or B
+        outs = [self._prefill_rows(ids[r: r + step], lengths[r: r + step], r) for r in range(0, B, step)]
+        return torch.cat(outs)
+
+    def _prefill_rows(self, ids, lengths, r0: int) -> torch.Tensor:
+        cfg, ext = self.cfg, self.ext
+        B, T = ids.shape
+        max_len = self.max_len
+        qd, kd = self.q_dim, self.kv_dim
         cos, sin = self.rope_tables(max_len)
         M = B * T
         pos = torch.arange(T, device=self.device, dtype=torch.int32).repeat(B)
-        rows = (torch.arange(B, device=self.device, dtype=torch.int32)[:, None] * max_len
+        rows = ((torch.arange(B, device=self.device, dtype=torch.int32)[:, None] + r0) * max_len
                 + torch.arange(T, device=self.device, dtype=torch.int32)[None]).reshape(-1)
         valid = (torch.arange(T, device=self.device)[None] < lengths[:, None]).to(torch.uint8).contiguous()
         last = (torch.arange(B, device=self.device) * T + lengths.long() - 1)
         x = self._embed(ids)
         use_memory = self.memory is not None and self.namespace is not None and cfg.top_k_chunks > 0
+        namespace = None
+        if use_memory:
+            namespace = (self.namespace[0][r0: r0 + B].contiguous(), self.namespace[1][r0: r0 + B].contiguous())
         for li, lw in enumerate(self.w.layers):
             h = self._norm(x, lw.ln_in)
             qkv = self._gemm(h, lw.qkv, lw.qkv_bias)
             mem_args = (None, None, None, None)
             if use_memory and cfg.is_pra_layer(li):
-                mem_idx, mem_len = self._route(li, qkv[last, :qd], B)
+                mem_idx, mem_len = self._route(li, qkv[last, :qd], B, namespace)
                 mem_args = (self.memory.k(li), self.memory.v(li), mem_idx, mem_len)
-            kc = self.cache[li, 0].view(B * max_len, kd)
-            vc = self.cache[li, 1].view(B * max_len, kd)
+            kc = self.cache[li, 0].view(-1, kd)
+            vc = self.cache[li, 1].view(-1, kd)
             ext.rope_copy(qkv[:, qd: qd + kd], kc, rows, pos, cos, sin, self.kv_heads, cfg.head_dim)
             ext.rope_copy(qkv[:, qd + kd:], vc, rows, None, None, None, self.kv_heads, cfg.head_dim)
             ext.rope_copy(qkv[:, :qd], qkv[:, :qd], None, pos, cos, sin, self.heads, cfg.head_dim)
-            a = ext.attention_fwd(qkv.view(B, T, -1)[:, :, :qd], self.cache[li, 0][:, :T], self.cache[li, 1][:, :T],
-                                  self.heads, self.kv_heads, cfg.head_dim, *mem_args, valid,
-                                  1.0 / math.sqrt(cfg.head_dim))[0]
+            k_rows = self.cache[li, 0][r0: r0 + B, :T]
+            v_rows = self.cache[li, 1][r0: r0 + B, :T]
+            a = ext.attention_fwd(qkv.view(B, T, -1)[:, :, :qd], k_rows, v_rows, self.heads, self.kv_heads,
+                                  cfg.head_dim, *mem_args, valid, 1.0 / math.sqrt(cfg.head_dim))[0]
             x = self._row_parallel(a.view(M, qd), lw.o, x)
             x = self._mlp(lw, x)
         return self._logits(x[last])

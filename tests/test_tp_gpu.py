@@ -1,0 +1,108 @@
+"""Tensor-parallel PRA Llama engine on 2 GPUs against the fp32 oracle (skipped with fewer GPUs).
+
+Child processes, one per GPU, NVLS off; the collectives are this library's kernels on
+plain peer loads / stores.  The last case makes one rank skip an all-reduce so the
+peer's bounded wait runs out and reports an error status.
+"""
+
+import os
+import socket
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, queue):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    result = {"rank": rank}
+    try:
+        from pdattention_b200.inference.llama_engine import LlamaWeights, PRALlamaEngine
+        from pdattention_b200.models.llama import PRALlamaReference, reference_step, tiny_llama
+        from pdattention_b200.parallel.tp import TensorParallel
+
+        torch.manual_seed(0)
+        cfg = tiny_llama(head_dim=64, hidden_size=128, num_attention_heads=4, num_key_value_heads=2,
+                         chunk_tokens=16, top_k_chunks=3)
+        model = PRALlamaReference(cfg).eval()
+        model.reset_parameters(seed=0, std=0.08)
+        chunks = torch.randint(0, cfg.vocab_size, (10, 16))
+        lengths = torch.tensor([16, 16, 11, 16, 16, 9, 16, 16, 16, 13])
+        tp = TensorParallel()
+        engine = PRALlamaEngine(LlamaWeights.from_reference(model, "cuda", rank, world), "cuda", tp=tp,
+                                decode_split_keys=64)
+        engine.build_memory(chunks, lengths, batch_chunks=4)
+        spans = [(0, 10), (3, 8)]
+        engine.set_namespace(torch.tensor([a for a, _ in spans]), torch.tensor([b for _, b in spans]))
+        ids = torch.randint(0, cfg.vocab_size, (2, 18))
+        plen = torch.tensor([18, 11])
+        logits = engine.prefill(ids, plen, 3).float().cpu()
+        ref_mem = model.encode_chunks(chunks, lengths)
+        caches = [[[None, None] for _ in range(cfg.num_hidden_layers)] for _ in range(2)]
+        cos = []
+        for b in range(2):
+            ref, _ = reference_step(model, ids[b, : int(plen[b])], caches[b], ref_mem, list(range(*spans[b])))
+            cos.append(float(F.cosine_similarity(logits[b], ref[-1], dim=0)))
+        for _ in range(2):
+            tok = torch.randint(0, cfg.vocab_size, (2,), generator=torch.Generator().manual_seed(7))
+            got = engine.decode_step(tok).float().cpu()
+            for b in range(2):
+                ref, _ = reference_step(model, tok[b: b + 1], caches[b], ref_mem, list(range(*spans[b])))
+                cos.append(float(F.cosine_similarity(got[b], ref[-1], dim=0)))
+        torch.cuda.synchronize()
+        tp.check()
+        result["cos"] = cos
+        # timeout: rank 1 skips one all-reduce; rank 0's wait must run out and report
+        dist.barrier()
+        tp.max_spins = 1 << 14
+        if rank == 0:
+            x = torch.randn(8, 64, device="cuda").bfloat16()
+            w = torch.randn(16, 64, device="cuda").bfloat16()
+            tp.gemm_allreduce(x, w, None)
+            torch.cuda.synchronize()
+            result["timeout_code"] = int(tp.error.item())
+            tp.error.zero_()
+        dist.barrier()
+        tp.buffers.close()
+    except Exception as error:
+        import traceback
+
+        result["error"] = traceback.format_exc()
+    finally:
+        queue.put(result)
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tensor_parallel_engine_two_gpus():
+    world = 2
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(world):
+        item = queue.get(timeout=300)
+        results[item["rank"]] = item
+    for p in procs:
+        p.join(timeout=60)
+    for rank, item in results.items():
+        assert "error" not in item, item["error"]
+        assert min(item["cos"]) > 0.99, item["cos"]
+    assert results[0]["timeout_code"] == 1
