@@ -54,7 +54,19 @@ struct GeluErfGrad<cutlass::Array<T, N>> {
 
 // One-SM tcgen05 tiles, cluster of one CTA: every CTA issues its own TMA loads (the
 // library is also used by multi-GPU runs, which must not issue cluster-shared loads).
-template <class LayoutA, class LayoutB, class ElementD, class FusionOp, class TileShape = Shape<_128, _256, _64>>
+inline int sm_count() {
+  static int cached[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 0;
+  if (cached[dev] == 0) cudaDeviceGetAttribute(&cached[dev], cudaDevAttrMultiProcessorCount, dev);
+  return cached[dev];
+}
+
+// Scheduler: void (persistent data-parallel tiles) or cutlass::gemm::StreamKScheduler (the
+// K loop of the remaining tiles is split across idle SMs: skinny decode GEMMs).
+template <class LayoutA, class LayoutB, class ElementD, class FusionOp, class TileShape = Shape<_128, _256, _64>,
+          class Scheduler = void>
 struct Gemm {
   using ClusterShape = Shape<_1, _1, _1>;
   using LayoutD = cutlass::layout::RowMajor;
@@ -69,7 +81,7 @@ struct Gemm {
       TileShape, ClusterShape,
       cutlass::gemm::collective::StageCountAutoCarveout<static_cast<int>(sizeof(typename Epilogue::SharedStorage))>,
       cutlass::gemm::KernelTmaWarpSpecialized1SmSm100>::CollectiveOp;
-  using Kernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, Mainloop, Epilogue>;
+  using Kernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, Mainloop, Epilogue, Scheduler>;
   using Device = cutlass::gemm::device::GemmUniversalAdapter<Kernel>;
   using StrideA = typename Kernel::StrideA;
   using StrideB = typename Kernel::StrideB;
@@ -87,6 +99,8 @@ struct Gemm {
          static_cast<const BF16*>(B), cutlass::make_cute_packed_stride(StrideB{}, {N, K, 1})},
         {fusion, static_cast<const ElementD*>(C), cutlass::make_cute_packed_stride(StrideC{}, {M, N, 1}),
          static_cast<ElementD*>(D), cutlass::make_cute_packed_stride(StrideD{}, {M, N, 1})}};
+    cudaGetDevice(&args.hw_info.device_id);
+    args.hw_info.sm_count = sm_count();
     Device op;
     if (op.can_implement(args) != cutlass::Status::kSuccess) return cudaErrorNotSupported;
     if (Device::get_workspace_size(args) > workspace_bytes) return cudaErrorMemoryAllocation;

@@ -61,6 +61,7 @@ __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int64_t M,
 // ---------------------------------------------------------------- decode attention
 constexpr int DT = 128;   // threads (4 warps, 16 keys each per block of 64)
 constexpr int DBN = 64;   // keys per block
+constexpr int DSTAGES = 3;  // cp.async pipeline depth (blocks in flight per CTA)
 constexpr float LOG2E = 1.4426950408889634f;
 
 template <int D>
@@ -73,9 +74,9 @@ __global__ void __launch_bounds__(DT) decode_kernel(DecodeAttnParams p) {
   constexpr int LD = DSmem<D>::LD;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __nv_bfloat16* sq = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [16][LD]
-  __nv_bfloat16* sk = sq + 16 * LD;                                 // [2][DBN][LD]
-  __nv_bfloat16* sv = sk + 2 * DBN * LD;                            // [2][DBN][LD]
-  float* red = reinterpret_cast<float*>(sv + 2 * DBN * LD);         // [4][16][D + 2]
+  __nv_bfloat16* sk = sq + 16 * LD;                                 // [STAGES][DBN][LD]
+  __nv_bfloat16* sv = sk + DSTAGES * DBN * LD;                      // [STAGES][DBN][LD]
+  float* red = reinterpret_cast<float*>(sk);                        // [4][16][D + 2], after the key loop
 
   const int G = p.H / p.Hkv;
   const int b = blockIdx.x / p.Hkv, kvh = blockIdx.x % p.Hkv;
@@ -118,17 +119,17 @@ __global__ void __launch_bounds__(DT) decode_kernel(DecodeAttnParams p) {
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
   const float sl2 = p.scale * LOG2E;
   const int n_blocks = k1 > k0 ? (k1 - k0 + DBN - 1) / DBN : 0;
-  if (n_blocks > 0) load_block(k0, 0);
-  __syncthreads();
+#pragma unroll
+  for (int st = 0; st < DSTAGES - 1; ++st) {
+    if (st < n_blocks) load_block(k0 + st * DBN, st);
+    else cp_async_commit();  // empty group keeps the wait counts uniform
+  }
   for (int it = 0; it < n_blocks; ++it) {
-    const int buf = it & 1;
-    if (it + 1 < n_blocks) {
-      load_block(k0 + (it + 1) * DBN, buf ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
+    const int buf = it % DSTAGES;
+    cp_async_wait<DSTAGES - 2>();
+    __syncthreads();  // block `it` landed; every warp is done with block it - 1
+    if (it + DSTAGES - 1 < n_blocks) load_block(k0 + (it + DSTAGES - 1) * DBN, (it + DSTAGES - 1) % DSTAGES);
+    else cp_async_commit();
     // S = Q[16 x D] . K[16 keys of this warp]^T
     float s[2][4];
 #pragma unroll
@@ -192,8 +193,9 @@ __global__ void __launch_bounds__(DT) decode_kernel(DecodeAttnParams p) {
       mma_bf16_16816(o[2 * np], a, bb);
       mma_bf16_16816(o[2 * np + 1], a, bb + 2);
     }
-    __syncthreads();
   }
+  cp_async_wait<0>();
+  __syncthreads();  // the staging area becomes the warp-merge buffer
   // merge the four warps' partials (rows: lane >> 2 and + 8)
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
@@ -274,6 +276,27 @@ __device__ __forceinline__ uint32_t order_key(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// Exclusive prefix sum of one int per thread over an RT-thread block; *total gets the sum.
+__device__ __forceinline__ int block_scan_int(int v, int* tmp, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  __syncthreads();
+  if (lane == 31) tmp[warp] = x;
+  __syncthreads();
+  int base = 0, all = 0;
+  for (int w = 0; w < RT / 32; ++w) {
+    if (w < warp) base += tmp[w];
+    all += tmp[w];
+  }
+  *total = all;
+  return base + x - v;
+}
+
 __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
   __shared__ uint32_t hist[256];
   __shared__ uint32_t prefix, prefix_mask;
@@ -283,6 +306,9 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
   __shared__ float cscore[MAX_CAND];
   __shared__ int picked[MAX_CAND];
   __shared__ float red[32];
+  __shared__ int scan_tmp[RT / 32];
+  __shared__ int sel_chunk[64], sel_off[65];
+  __shared__ int n_sel;
   const int b = blockIdx.x;
   const int c0 = a.ns_start[b], c1 = a.ns_end[b];
   const int n = max(c1 - c0, 0);
@@ -326,13 +352,23 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0 && kc > 0) {
-    int cnt = min(n_cand, MAX_CAND);
-    for (int i = 0; i < n && cnt < kc; ++i)
-      if (order_key(row[c0 + i]) == thr) cand[cnt++] = c0 + i;
-    n_cand = cnt;
+  {
+    // ties at the threshold, lowest chunk ids first: each thread scans a contiguous segment
+    const int above = min(n_cand, MAX_CAND);
+    const int seg = (n + RT - 1) / RT;
+    const int s0 = min(n, threadIdx.x * seg), s1 = min(n, s0 + seg);
+    int mine = 0;
+    for (int i = s0; i < s1 && kc > 0; ++i) mine += order_key(row[c0 + i]) == thr ? 1 : 0;
+    int total = 0;
+    const int before = block_scan_int(mine, scan_tmp, &total);
+    const int want = kc - above;
+    int slot = above + before;
+    for (int i = s0; i < s1 && kc > 0 && slot < above + want; ++i)
+      if (order_key(row[c0 + i]) == thr) cand[slot++] = c0 + i;
+    __syncthreads();
+    if (threadIdx.x == 0) n_cand = kc > 0 ? above + min(want, total) : 0;
+    __syncthreads();
   }
-  __syncthreads();
   const int nc = n_cand;
   // 3. exact fp32 cosine of the candidates (warp per candidate)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -396,13 +432,21 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
     }
     int written = 0;
     for (int i = 0; i < chosen; ++i) {
-      const int c = sel[i];
-      if (a.sel_out) a.sel_out[(int64_t)b * a.k + i] = c;
-      for (int t = 0; t < a.chunk_len[c] && written < a.mem_max; ++t)
-        a.mem_idx[(int64_t)b * a.mem_max + written++] = a.chunk_row0[c] + t;
+      sel_chunk[i] = sel[i];
+      sel_off[i] = written;
+      written += a.chunk_len[sel[i]];
     }
-    for (int i = chosen; i < a.k && a.sel_out; ++i) a.sel_out[(int64_t)b * a.k + i] = -1;
-    a.mem_len[b] = written;
+    sel_off[chosen] = written;
+    n_sel = chosen;
+    for (int i = 0; i < a.k && a.sel_out; ++i) a.sel_out[(int64_t)b * a.k + i] = i < chosen ? sel[i] : -1;
+    a.mem_len[b] = min(written, a.mem_max);
+  }
+  __syncthreads();
+  // the memory row list, written by all threads
+  for (int i = 0; i < n_sel; ++i) {
+    const int c = sel_chunk[i], base = sel_off[i], len = sel_off[i + 1] - base;
+    for (int t = threadIdx.x; t < len; t += RT)
+      if (base + t < a.mem_max) a.mem_idx[(int64_t)b * a.mem_max + base + t] = a.chunk_row0[c] + t;
   }
 }
 
@@ -432,7 +476,9 @@ template <int D>
 static cudaError_t launch_decode(DecodeAttnParams p, cudaStream_t st) {
   using namespace pra::llama;
   constexpr int LD = DSmem<D>::LD;
-  const size_t smem = (size_t)(16 + 4 * DBN) * LD * sizeof(__nv_bfloat16) + 4 * 16 * (D + 2) * sizeof(float);
+  static_assert(2 * DSTAGES * DBN * LD * sizeof(__nv_bfloat16) >= 4 * 16 * (D + 2) * sizeof(float),
+                "merge buffer must fit in the staging area");
+  const size_t smem = (size_t)(16 + 2 * DSTAGES * DBN) * LD * sizeof(__nv_bfloat16);
   PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   decode_kernel<D><<<dim3(p.B * p.Hkv, p.n_split), DT, smem, st>>>(p);
   PRA_RETURN_IF_ERROR(cudaGetLastError());
