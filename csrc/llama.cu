@@ -77,6 +77,7 @@ __global__ void __launch_bounds__(DT) decode_kernel(DecodeAttnParams p) {
   __nv_bfloat16* sk = sq + 16 * LD;                                 // [STAGES][DBN][LD]
   __nv_bfloat16* sv = sk + DSTAGES * DBN * LD;                      // [STAGES][DBN][LD]
   float* red = reinterpret_cast<float*>(sk);                        // [4][16][D + 2], after the key loop
+  int* srow = reinterpret_cast<int*>(sv + DSTAGES * DBN * LD);      // [split_keys] key row (>= 0: memory pool)
 
   const int G = p.H / p.Hkv;
   const int b = blockIdx.x / p.Hkv, kvh = blockIdx.x % p.Hkv;
@@ -94,13 +95,14 @@ __global__ void __launch_bounds__(DT) decode_kernel(DecodeAttnParams p) {
     if (r < G) v = *reinterpret_cast<const uint4*>(p.q + (int64_t)b * p.q_row + (kvh * G + r) * D + col);
     *reinterpret_cast<uint4*>(sq + r * LD + col) = v;
   }
+  // key rows of this split, resolved once: memory keys -> pool row, local keys -> -(t + 1)
+  for (int j = k0 + threadIdx.x; j < k1; j += DT)
+    srow[j - k0] = j < mem_len ? p.mem_idx[(int64_t)b * p.mem_max + j] : -(j - mem_len + 1);
+  __syncthreads();
   auto key_addr = [&](int j, bool value) -> const __nv_bfloat16* {
-    if (j < mem_len) {
-      const int row = p.mem_idx[(int64_t)b * p.mem_max + j];
-      return (value ? p.mem_v : p.mem_k) + (int64_t)row * p.mem_row + kvh * D;
-    }
-    const int t = j - mem_len;
-    return (value ? p.loc_v : p.loc_k) + (int64_t)b * p.loc_batch + (int64_t)t * p.loc_row + kvh * D;
+    const int r = srow[j - k0];
+    if (r >= 0) return (value ? p.mem_v : p.mem_k) + (int64_t)r * p.mem_row + kvh * D;
+    return (value ? p.loc_v : p.loc_k) + (int64_t)b * p.loc_batch + (int64_t)(-r - 1) * p.loc_row + kvh * D;
   };
   auto load_block = [&](int start, int buf) {
     for (int c = threadIdx.x; c < DBN * (D / 8); c += DT) {
@@ -478,7 +480,7 @@ static cudaError_t launch_decode(DecodeAttnParams p, cudaStream_t st) {
   constexpr int LD = DSmem<D>::LD;
   static_assert(2 * DSTAGES * DBN * LD * sizeof(__nv_bfloat16) >= 4 * 16 * (D + 2) * sizeof(float),
                 "merge buffer must fit in the staging area");
-  const size_t smem = (size_t)(16 + 2 * DSTAGES * DBN) * LD * sizeof(__nv_bfloat16);
+  const size_t smem = (size_t)(16 + 2 * DSTAGES * DBN) * LD * sizeof(__nv_bfloat16) + (size_t)p.split_keys * sizeof(int);
   PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   decode_kernel<D><<<dim3(p.B * p.Hkv, p.n_split), DT, smem, st>>>(p);
   PRA_RETURN_IF_ERROR(cudaGetLastError());
@@ -488,7 +490,8 @@ static cudaError_t launch_decode(DecodeAttnParams p, cudaStream_t st) {
 
 cudaError_t pra_decode_attention(const DecodeAttnParams& p, int head_dim, cudaStream_t st) {
   if (p.B == 0) return cudaSuccess;
-  if (p.H % p.Hkv || p.H / p.Hkv > 16 || p.split_keys % pra::llama::DBN) return cudaErrorInvalidValue;
+  if (p.H % p.Hkv || p.H / p.Hkv > 16 || p.split_keys % pra::llama::DBN || p.split_keys > 4096)
+    return cudaErrorInvalidValue;
   switch (head_dim) {
     case 64: return launch_decode<64>(p, st);
     case 128: return launch_decode<128>(p, st);
