@@ -293,7 +293,7 @@ class PRALlamaEngine:
 
     @torch.no_grad()
     def prefill(self, ids: torch.Tensor, lengths: torch.Tensor, max_new_tokens: int,
-                row_batch: int | None = None) -> torch.Tensor:
+                row_batch: int | None = None, position_offset: torch.Tensor | None = None) -> torch.Tensor:
         """Left-aligned prompts ``ids`` ``[B, T]`` with ``lengths``: fills the local caches and
         returns the logits of each row's last prompt token ``[B, V]``.  ``row_batch`` bounds
         how many rows run through the layers at once (activation memory)."""
@@ -306,6 +306,11 @@ class PRALlamaEngine:
         self.cache = torch.zeros((L, 2, B, max_len, self.kv_dim), device=self.device, dtype=torch.bfloat16)
         self.cache_len = lengths.clone()
         self.max_len = max_len
+        # rotary position of cache slot t of row b: offset[b] + t (a long prompt's direct
+        # tail continues the positions of its implicit head when they are natively legal)
+        self.pos_offset = (position_offset.to(self.device, torch.int32) if position_offset is not None
+                           else torch.zeros(B, device=self.device, dtype=torch.int32))
+        self._max_pos = int(self.pos_offset.max()) + max_len if B else max_len
         step = row_batch or B
         outs = [self._prefill_rows(ids[r: r + step], lengths[r: r + step], r) for r in range(0, B, step)]
         return torch.cat(outs)
@@ -315,9 +320,10 @@ class PRALlamaEngine:
         B, T = ids.shape
         max_len = self.max_len
         qd, kd = self.q_dim, self.kv_dim
-        cos, sin = self.rope_tables(max_len)
+        cos, sin = self.rope_tables(self._max_pos)
         M = B * T
-        pos = torch.arange(T, device=self.device, dtype=torch.int32).repeat(B)
+        pos = (torch.arange(T, device=self.device, dtype=torch.int32)[None]
+               + self.pos_offset[r0: r0 + B, None]).reshape(-1)
         rows = ((torch.arange(B, device=self.device, dtype=torch.int32)[:, None] + r0) * max_len
                 + torch.arange(T, device=self.device, dtype=torch.int32)[None]).reshape(-1)
         valid = (torch.arange(T, device=self.device)[None] < lengths[:, None]).to(torch.uint8).contiguous()
@@ -357,9 +363,9 @@ class PRALlamaEngine:
         cfg, ext = self.cfg, self.ext
         B = token_ids.shape[0]
         qd, kd = self.q_dim, self.kv_dim
-        cos, sin = self.rope_tables(self.max_len)
-        pos = self.cache_len
-        rows = torch.arange(B, device=self.device, dtype=torch.int32) * self.max_len + pos
+        cos, sin = self.rope_tables(self._max_pos)
+        pos = self.cache_len + self.pos_offset
+        rows = torch.arange(B, device=self.device, dtype=torch.int32) * self.max_len + self.cache_len
         new_len = pos + 1
         x = self._embed(token_ids.to(self.device))
         use_memory = self.memory is not None and self.namespace is not None and cfg.top_k_chunks > 0

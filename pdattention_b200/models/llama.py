@@ -378,14 +378,14 @@ class PRALlamaReference(nn.Module):
 
 @torch.no_grad()
 def reference_step(model: PRALlamaReference, ids: torch.Tensor, cache: list, memory: LlamaChunkMemory | None,
-                   namespace: list[int] | None):
+                   namespace: list[int] | None, position_offset: int = 0):
     """Incremental fp32 step of ONE row: ``ids`` ``[T]`` continue the sequence whose per-layer
     post-rotary K/V are in ``cache`` (list of ``[k, v]`` ``[t, Hkv, Dh]``, extended in place).
     Routing uses the last new token; returns (logits ``[T, V]``, selections per PRA layer)."""
     cfg = model.cfg
     t0 = cache[0][0].shape[0] if cache and cache[0][0] is not None else 0
     T = ids.shape[0]
-    pos = torch.arange(t0, t0 + T, device=ids.device)[None]
+    pos = torch.arange(t0, t0 + T, device=ids.device)[None] + int(position_offset)
     cos, sin = rope_tables(cfg, pos)
     x = model.model.embed_tokens(ids[None]).float()
     picks = []

@@ -95,3 +95,18 @@ def test_incremental_reference_matches_full_forward_without_memory():
     a, _ = reference_step(model, ids[:6], cache, None, None)
     b, _ = reference_step(model, ids[6:], cache, None, None)
     assert torch.allclose(torch.cat([a, b]), full, atol=1e-5)
+
+
+def test_long_prompt_plan_splits_head_and_tail():
+    from pdattention_b200.inference.long_prompt import plan_long_prompts
+
+    prompts = [list(range(1, 51)), list(range(100, 110))]
+    plan = plan_long_prompts(prompts, direct_window=12, chunk_tokens=16, max_positions=40)
+    assert plan.chunks.shape == (3, 16)  # row 0: 38 head tokens -> 16 + 16 + 6
+    assert plan.chunk_lengths.tolist() == [16, 16, 6]
+    assert plan.ns_start.tolist() == [0, 3] and plan.ns_end.tolist() == [3, 3]
+    assert plan.tails[0].tolist() == list(range(39, 51)) and plan.tail_lengths.tolist() == [12, 10]
+    assert plan.position_offset.tolist() == [0, 0]  # 50 > 40 native positions: the tail restarts at 0
+    plan = plan_long_prompts(prompts, direct_window=12, chunk_tokens=16, max_positions=64)
+    assert plan.position_offset.tolist() == [38, 0]
+    assert plan.chunk_ids[0] == "pra://implicit/prompt/head#chunk=0"

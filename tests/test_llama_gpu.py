@@ -169,3 +169,25 @@ def test_engine_prefill_and_decode_match_oracle(ext):
             ref_logits, _ = reference_step(model, tok[b: b + 1], caches[b], ref_mem, list(range(*spans[b])))
             cos = F.cosine_similarity(got[b], ref_logits[-1], dim=0)
             assert cos > 0.99, (step, b, float(cos))
+
+
+def test_long_prompt_implicit_head_matches_oracle(ext):
+    from pdattention_b200.inference.llama_engine import LlamaWeights, PRALlamaEngine
+    from pdattention_b200.inference.long_prompt import long_prompt_generate
+    from pdattention_b200.models.llama import reference_step
+
+    cfg, model, _, _ = _tiny_setup(2)
+    gen = torch.Generator().manual_seed(3)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=gen).tolist() for n in (70, 40, 20)]
+    engine = PRALlamaEngine(LlamaWeights.from_reference(model, "cuda"), "cuda", decode_split_keys=64)
+    tokens, plan, first = long_prompt_generate(engine, prompts, 3, direct_window=16)
+    assert tokens.shape == (3, 3)
+    assert plan.position_offset.tolist() == [54, 24, 4]
+    mem = model.encode_chunks(plan.chunks, plan.chunk_lengths)
+    for b in range(3):
+        cache = [[None, None] for _ in range(cfg.num_hidden_layers)]
+        ns = list(range(int(plan.ns_start[b]), int(plan.ns_end[b])))
+        tail = plan.tails[b, : int(plan.tail_lengths[b])]
+        ref, _ = reference_step(model, tail, cache, mem, ns, position_offset=int(plan.position_offset[b]))
+        cos = F.cosine_similarity(first[b].float().cpu(), ref[-1], dim=0)
+        assert cos > 0.995, (b, float(cos))
