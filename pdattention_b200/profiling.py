@@ -1,0 +1,122 @@
+"""Small, fixed workloads for kernel profiling (``ncu``) and per-step kernel tables.
+
+Every case runs a few warm-up steps and exits 0, so it can run first without a
+profiler and then under ``ncu`` on one GPU with the same arguments::
+
+    python -m pdattention_b200.profiling train-small       # TinyGPT-PRA steps, 2 rows
+    python -m pdattention_b200.profiling decode-small      # Llama-3-8B decode, 512 memory chunks
+    python -m pdattention_b200.profiling train-table       # torch.profiler kernel table of one step (8 rows)
+    python -m pdattention_b200.profiling decode-table      # kernel table of one decode step (64 rows)
+
+The ``*-small`` cases keep device memory to a few GB so full ``ncu`` captures of one
+launch end quickly.  Numbers printed under a profiler are not benchmark values.
+"""
+
+from __future__ import annotations
+
+import argparse
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+
+def _train_step_fn(rows: int):
+    root = Path(__file__).resolve().parents[1]
+    sys.path.insert(0, str(root))
+    import bench  # the benchmark's data and model set-up
+
+    bench.PER_GPU_BATCH = rows
+    from pdattention_b200.data import WordIdTokenizer
+
+    tmp = Path(tempfile.mkdtemp())
+    tok = WordIdTokenizer(bench.VOCAB)
+    bench._make_data(tmp, max(16, 4 * rows), 0, tok)
+    step, _, counter = bench._pra_arm(tmp, tok, 0, 1)
+    return step, counter
+
+
+def train_small(steps: int = 3) -> None:
+    step, _ = _train_step_fn(2)
+    batches = step.batches(steps)
+    for b in batches:
+        step(b)
+    torch.cuda.synchronize()
+    print("ok")
+
+
+def _decode_engine(memory_chunks: int, prompt: int, rows: int):
+    from .inference.llama_engine import LlamaWeights, PRALlamaEngine
+    from .models.llama import PRESETS
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = PRESETS["llama3-8b"](chunk_tokens=64, top_k_chunks=16, direct_window=prompt)
+    engine = PRALlamaEngine(LlamaWeights.random(cfg, dev), dev)
+    gen = torch.Generator().manual_seed(0)
+    engine.build_memory(torch.randint(0, cfg.vocab_size, (memory_chunks, 64), generator=gen),
+                        torch.full((memory_chunks,), 64, dtype=torch.int32))
+    engine.set_namespace(torch.zeros(rows, dtype=torch.int32), torch.full((rows,), memory_chunks, dtype=torch.int32))
+    logits = engine.prefill(torch.randint(0, cfg.vocab_size, (rows, prompt), generator=gen),
+                            torch.full((rows,), prompt, dtype=torch.int32), 16, row_batch=8)
+    return engine, logits.float().argmax(-1)
+
+
+def decode_small(steps: int = 3) -> None:
+    engine, tok = _decode_engine(512, 2048, 64)
+    for _ in range(steps):
+        tok = engine.decode_step(tok).float().argmax(-1)
+    torch.cuda.synchronize()
+    print("ok")
+
+
+def _table(fn, rows: int = 30) -> None:
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=rows, max_name_column_width=70))
+
+
+def train_table() -> None:
+    step, counter = _train_step_fn(8)
+    batches = step.batches(6)
+    for b in batches[:4]:
+        step(b)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    step(batches[4])
+    torch.cuda.synchronize()
+    print(f"step wall ms {1000 * (time.perf_counter() - t0):.2f}")
+    _table(lambda: step(batches[5]))
+
+
+def decode_table() -> None:
+    engine, tok = _decode_engine(1024, 4096, 64)
+    for _ in range(3):
+        tok = engine.decode_step(tok).float().argmax(-1)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(5):
+        tok = engine.decode_step(tok).float().argmax(-1)
+    torch.cuda.synchronize()
+    print(f"step wall ms {1000 * (time.perf_counter() - t0) / 5:.2f}")
+    _table(lambda: engine.decode_step(tok))
+
+
+CASES = {"train-small": train_small, "decode-small": decode_small, "train-table": train_table,
+         "decode-table": decode_table}
+
+
+def main(argv=None) -> None:
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("case", choices=sorted(CASES))
+    args = parser.parse_args(argv)
+    torch.cuda.set_device(0)
+    CASES[args.case]()
+
+
+if __name__ == "__main__":
+    main()
