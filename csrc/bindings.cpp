@@ -474,7 +474,7 @@ std::vector<torch::Tensor> route(torch::Tensor query, torch::Tensor gists, torch
 
 // ---------------------------------------------------------------- tensor-parallel collectives
 void tp_allreduce(std::vector<int64_t> parts, std::vector<int64_t> sigs, int64_t rank,
-                  c10::optional<torch::Tensor> residual, torch::Tensor out, int64_t epoch, int64_t max_spins,
+                  c10::optional<torch::Tensor> residual, torch::Tensor out, torch::Tensor epochs, int64_t max_spins,
                   torch::Tensor error) {
   c10::cuda::CUDAGuard guard(out.device());
   const int world = parts.size();
@@ -494,14 +494,15 @@ void tp_allreduce(std::vector<int64_t> parts, std::vector<int64_t> sigs, int64_t
   a.rank = rank;
   a.world = world;
   a.n = out.numel();
-  a.epoch = (uint32_t)epoch;
+  TORCH_CHECK(epochs.scalar_type() == at::kInt && epochs.numel() >= TP_MAX_BLOCKS, "epochs: int32 [TP_MAX_BLOCKS]");
+  a.epochs = reinterpret_cast<uint32_t*>(epochs.data_ptr());
   a.max_spins = max_spins;
   a.error = ptr<int>(error);
   check(pra_tp_allreduce(a, stream()), "tp_allreduce");
 }
 
 void tp_allgather(torch::Tensor src, std::vector<int64_t> dsts, std::vector<int64_t> sigs, int64_t rank,
-                  int64_t epoch, int64_t max_spins, torch::Tensor error) {
+                  torch::Tensor epochs, int64_t max_spins, torch::Tensor error) {
   c10::cuda::CUDAGuard guard(src.device());
   const int world = dsts.size();
   TORCH_CHECK(world >= 1 && world <= TP_MAX_RANKS && (int)sigs.size() == world, "one dst/signal per rank");
@@ -518,7 +519,8 @@ void tp_allgather(torch::Tensor src, std::vector<int64_t> dsts, std::vector<int6
   a.world = world;
   a.rows = src.size(0);
   a.cols = src.size(1);
-  a.epoch = (uint32_t)epoch;
+  TORCH_CHECK(epochs.scalar_type() == at::kInt && epochs.numel() >= TP_MAX_BLOCKS, "epochs: int32 [TP_MAX_BLOCKS]");
+  a.epochs = reinterpret_cast<uint32_t*>(epochs.data_ptr());
   a.max_spins = max_spins;
   a.error = ptr<int>(error);
   check(pra_tp_allgather(a, stream()), "tp_allgather");

@@ -243,7 +243,7 @@ struct TpAllreduceArgs {
   uint32_t* sig[TP_MAX_RANKS];              // every rank's signal area
   int rank, world;
   int64_t n;                                // elements (multiple of 8)
-  uint32_t epoch;
+  uint32_t* epochs;                         // local [TP_MAX_BLOCKS] per-CTA call counters (start at 0)
   long long max_spins;
   int* error;
 };
@@ -253,7 +253,7 @@ struct TpAllgatherArgs {
   float* dst[TP_MAX_RANKS];                 // every rank's [rows, world * cols] buffer
   uint32_t* sig[TP_MAX_RANKS];
   int rank, world, rows, cols;
-  uint32_t epoch;
+  uint32_t* epochs;                         // local [TP_MAX_BLOCKS] per-CTA call counters (start at 0)
   long long max_spins;
   int* error;
 };

@@ -20,10 +20,19 @@ __device__ __forceinline__ void signal_store(uint32_t* addr, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(addr), "r"(v) : "memory");
 }
 
-__device__ bool cta_barrier(uint32_t* const* sig, int rank, int world, uint32_t epoch, long long max_spins,
+// The epoch of each call comes from this CTA's own counter in local device memory (read,
+// incremented and written back by the CTA itself), so the collectives can be captured in a
+// CUDA graph and replayed: every rank launches identical grids, so CTA b's counters of all
+// ranks advance in lockstep.
+__device__ bool cta_barrier(uint32_t* const* sig, uint32_t* epochs, int rank, int world, long long max_spins,
                             int* error, int phase) {
   __shared__ int ok;
-  if (threadIdx.x == 0) ok = 1;
+  __shared__ uint32_t epoch;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    epoch = epochs[blockIdx.x] + 1;
+    epochs[blockIdx.x] = epoch;
+  }
   __syncthreads();
   const int slot = blockIdx.x * world;
   if (threadIdx.x < world) {
@@ -39,7 +48,7 @@ __device__ bool cta_barrier(uint32_t* const* sig, int rank, int world, uint32_t 
 }
 
 __global__ void __launch_bounds__(NT) allreduce_oneshot_kernel(TpAllreduceArgs a) {
-  if (!cta_barrier(a.sig, a.rank, a.world, a.epoch, a.max_spins, a.error, 0)) return;
+  if (!cta_barrier(a.sig, a.epochs, a.rank, a.world, a.max_spins, a.error, 0)) return;
   const int64_t vecs = a.n / 8;
   for (int64_t v = (int64_t)blockIdx.x * NT + threadIdx.x; v < vecs; v += (int64_t)gridDim.x * NT) {
     float acc[8];
@@ -82,7 +91,7 @@ __global__ void __launch_bounds__(NT) allgather_cols_kernel(TpAllgatherArgs a) {
     const int64_t at = r * (int64_t)a.cols * a.world + (int64_t)a.rank * a.cols + c;
     for (int p = 0; p < a.world; ++p) a.dst[p][at] = v;
   }
-  cta_barrier(a.sig, a.rank, a.world, a.epoch, a.max_spins, a.error, 1);
+  cta_barrier(a.sig, a.epochs, a.rank, a.world, a.max_spins, a.error, 1);
 }
 
 }  // namespace tp

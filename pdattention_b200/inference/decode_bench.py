@@ -27,7 +27,7 @@ from .llama_engine import LlamaWeights, PRALlamaEngine
 def run_decode_benchmark(*, model: str = "llama3-8b", batch: int = 64, prompt_tokens: int = 4096, refs: int = 32,
                          ref_tokens: int = 32768, chunk_tokens: int = 64, top_k_chunks: int = 16, steps: int = 16,
                          warmup: int = 3, tp=None, seed: int = 0, prefill_rows: int = 4,
-                         build_chunks: int = 512, clocks=None, counter=None) -> dict:
+                         build_chunks: int = 512, clocks=None, counter=None, graphs: bool = True) -> dict:
     rank = tp.rank if tp is not None else 0
     world = tp.world if tp is not None else 1
     device = torch.device("cuda", torch.cuda.current_device())
@@ -56,16 +56,21 @@ def run_decode_benchmark(*, model: str = "llama3-8b", batch: int = 64, prompt_to
     tok = logits.float().argmax(-1)
     host_tok.copy_(tok.cpu())
 
+    step_fn = engine.decode_step
+
     def one_step():
         ids = host_tok.to(device, non_blocking=True)
-        nxt = engine.decode_step(ids).float().argmax(-1)
+        nxt = step_fn(ids).float().argmax(-1)
         host_out.copy_(nxt, non_blocking=True)
         return nxt
 
-    for _ in range(warmup):
+    for i in range(warmup):
         one_step()
         torch.cuda.synchronize()
         host_tok.copy_(host_out)
+        if graphs and i == 0:  # capture after one eager step, replay for the rest
+            engine.capture_decode()
+            step_fn = engine.decode_step_graphed
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     if tp is not None:
         tp.barrier()
@@ -88,9 +93,11 @@ def run_decode_benchmark(*, model: str = "llama3-8b", batch: int = 64, prompt_to
     launches = None
     if counter is not None:
         counter.enabled = False
-        launches = counter.launches
+        launches = engine.graph_launches * steps if graphs else counter.launches
     if sampler is not None:
         sampler.__exit__(None, None, None)
+    if graphs:
+        engine.release_graph()
     per_step = [a.elapsed_time(b) for a, b in events]
     device_s = sum(per_step) / 1000.0
     if tp is not None:
@@ -118,4 +125,5 @@ def run_decode_benchmark(*, model: str = "llama3-8b", batch: int = 64, prompt_to
         "d2h_bytes_per_step": batch * 8,
         "memory_gb_per_gpu": engine.memory.nbytes() / 1e9,
         "gpu_launches": launches,
+        "cuda_graphs": graphs,
     }

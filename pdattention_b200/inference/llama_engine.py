@@ -366,7 +366,7 @@ class PRALlamaEngine:
         cos, sin = self.rope_tables(self._max_pos)
         pos = self.cache_len + self.pos_offset
         rows = torch.arange(B, device=self.device, dtype=torch.int32) * self.max_len + self.cache_len
-        new_len = pos + 1
+        new_len = self.cache_len + 1
         x = self._embed(token_ids.to(self.device))
         use_memory = self.memory is not None and self.namespace is not None and cfg.top_k_chunks > 0
         max_keys = cfg.memory_tokens_per_row + self.max_len
@@ -387,8 +387,42 @@ class PRALlamaEngine:
                                      self.cache[li, 1], new_len, max_keys, self.split_keys, False)[0]
             x = self._row_parallel(a, lw.o, x)
             x = self._mlp(lw, x)
-        self.cache_len = new_len
+        self.cache_len.copy_(new_len)  # in place: a captured step replays on the same tensors
         return self._logits(x)
+
+    # -- CUDA-graph decode ------------------------------------------------------------
+    def capture_decode(self) -> None:
+        """Capture one ``decode_step`` into a CUDA graph (after at least one eager step).
+
+        Replays run the whole step (32 layers of GEMMs, routing, attention and the
+        tensor-parallel collectives) as one graph launch; the collectives take their
+        epochs from device counters, so replays stay in lockstep across ranks."""
+        B = self.cache_len.shape[0]
+        self._graph_ids = torch.zeros(B, dtype=torch.long, device=self.device)
+        ar0 = self.tp.epoch_ar if self.tp is not None else 0
+        ag0 = self.tp.epoch_ag if self.tp is not None else 0
+        torch.cuda.synchronize(self.device)
+        graph = torch.cuda.CUDAGraph()
+        counter = _ext.launch_counter()
+        was, before = counter.enabled, counter.launches
+        counter.enabled = True  # count this library's kernels recorded in the graph
+        with torch.cuda.graph(graph):
+            self._graph_out = self.decode_step(self._graph_ids)
+        self.graph_launches = counter.launches - before
+        counter.launches, counter.enabled = before, was
+        if self.tp is not None and ((self.tp.epoch_ar - ar0) % 2 or (self.tp.epoch_ag - ag0) % 2):
+            raise RuntimeError("a captured step must use both halves of each double buffer equally often")
+        self._graph = graph
+
+    def decode_step_graphed(self, token_ids: torch.Tensor) -> torch.Tensor:
+        """``decode_step`` through the captured graph (returns the graph's static logits)."""
+        self._graph_ids.copy_(token_ids, non_blocking=True)
+        self._graph.replay()
+        return self._graph_out
+
+    def release_graph(self) -> None:
+        self._graph = None
+        self._graph_out = None
 
     @torch.no_grad()
     def generate(self, ids: torch.Tensor, lengths: torch.Tensor, max_new_tokens: int) -> torch.Tensor:

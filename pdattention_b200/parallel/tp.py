@@ -46,8 +46,10 @@ class TensorParallel:
         self.gather_addr = [self.buffers.addresses("gather0"), self.buffers.addresses("gather1")]
         self.sig_ar = self.buffers.addresses("sig_ar")
         self.sig_ag = self.buffers.addresses("sig_ag")
-        self.epoch_ar = 0
+        self.epoch_ar = 0  # host call counters: pick the double buffer half
         self.epoch_ag = 0
+        # per-CTA device call counters of the two collectives (graph-replay safe epochs)
+        self.dev_epochs = torch.zeros((2, int(ext.tp_signal_words(1))), dtype=torch.int32, device=self.device)
         self.max_spins = int(max_spins)
         self.error = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._gist_slices: dict[int, torch.Tensor] = {}
@@ -64,8 +66,8 @@ class TensorParallel:
         ext.gemm("tn", x, w, None, part, None, None, 1.0, 0.0, None)
         out = torch.empty((m, n), device=x.device, dtype=torch.bfloat16)
         self.epoch_ar += 1
-        ext.tp_allreduce(self.part_addr[half], self.sig_ar, self.rank, residual, out, self.epoch_ar, self.max_spins,
-                         self.error)
+        ext.tp_allreduce(self.part_addr[half], self.sig_ar, self.rank, residual, out, self.dev_epochs[0],
+                         self.max_spins, self.error)
         return out
 
     def all_gather_columns(self, x: torch.Tensor) -> torch.Tensor:
@@ -76,7 +78,7 @@ class TensorParallel:
         half = self.epoch_ag & 1
         self.epoch_ag += 1
         ext = _ext.require()
-        ext.tp_allgather(x.float().contiguous(), self.gather_addr[half], self.sig_ag, self.rank, self.epoch_ag,
+        ext.tp_allgather(x.float().contiguous(), self.gather_addr[half], self.sig_ag, self.rank, self.dev_epochs[1],
                          self.max_spins, self.error)
         return self.gathers[half][: rows * cols * self.world].view(rows, cols * self.world).clone()
 

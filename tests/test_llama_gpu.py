@@ -191,3 +191,29 @@ def test_long_prompt_implicit_head_matches_oracle(ext):
         ref, _ = reference_step(model, tail, cache, mem, ns, position_offset=int(plan.position_offset[b]))
         cos = F.cosine_similarity(first[b].float().cpu(), ref[-1], dim=0)
         assert cos > 0.995, (b, float(cos))
+
+
+def test_graphed_decode_matches_eager(ext):
+    from pdattention_b200.inference.llama_engine import LlamaWeights, PRALlamaEngine
+
+    cfg, model, chunks, lengths = _tiny_setup(4)
+    weights = LlamaWeights.from_reference(model, "cuda")
+    outs = []
+    for graphed in (False, True):
+        engine = PRALlamaEngine(weights, "cuda", decode_split_keys=64)
+        engine.build_memory(chunks, lengths)
+        engine.set_namespace(torch.zeros(2, dtype=torch.int32), torch.full((2,), 12, dtype=torch.int32))
+        tok = engine.prefill(torch.arange(24).view(2, 12) % cfg.vocab_size, torch.tensor([12, 9]), 6).float().argmax(-1)
+        tok = engine.decode_step(tok).float().argmax(-1)
+        step = engine.decode_step
+        if graphed:
+            engine.capture_decode()
+            step = engine.decode_step_graphed
+        seq = []
+        for _ in range(4):
+            logits = step(tok).float().clone()
+            seq.append(logits)
+            tok = logits.argmax(-1)
+        outs.append(torch.stack(seq))
+        assert engine.cache_len.tolist() == [12 + 5, 9 + 5]
+    assert torch.allclose(outs[0], outs[1], atol=1e-3), (outs[0] - outs[1]).abs().max()
