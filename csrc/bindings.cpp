@@ -629,7 +629,7 @@ std::vector<torch::Tensor> decode_attention(torch::Tensor q, int64_t heads, int6
 std::vector<torch::Tensor> route_topk(torch::Tensor scores, torch::Tensor query, torch::Tensor gists,
                                       torch::Tensor ns_start, torch::Tensor ns_end, torch::Tensor chunk_len,
                                       torch::Tensor chunk_row0, int64_t k, int64_t k_cand, int64_t budget,
-                                      int64_t mem_max) {
+                                      int64_t mem_max, bool local, int64_t id_offset) {
   c10::cuda::CUDAGuard guard(scores.device());
   expect(scores, at::kFloat, "scores");
   expect(query, at::kFloat, "query");
@@ -652,6 +652,15 @@ std::vector<torch::Tensor> route_topk(torch::Tensor scores, torch::Tensor query,
   a.k_cand = k_cand;
   a.budget = budget;
   auto io = scores.options().dtype(at::kInt);
+  if (local) {  // this rank's best k (exact scores, global ids) for a cross-GPU merge
+    auto cs = torch::empty({a.B, std::max<int64_t>(k, 1)}, scores.options());
+    auto ci = torch::empty({a.B, std::max<int64_t>(k, 1)}, io);
+    a.cand_score = ptr<float>(cs);
+    a.cand_id = ptr<int>(ci);
+    a.id_offset = id_offset;
+    check(pra_route_topk(a, stream()), "route_topk");
+    return {cs, ci};
+  }
   auto mem_idx = torch::empty({a.B, std::max<int64_t>(mem_max, 1)}, io);
   auto mem_len = torch::empty({a.B}, io);
   auto sel = torch::empty({a.B, std::max<int64_t>(k, 1)}, io);
@@ -660,6 +669,33 @@ std::vector<torch::Tensor> route_topk(torch::Tensor scores, torch::Tensor query,
   a.mem_len = ptr<int>(mem_len);
   a.sel_out = ptr<int>(sel);
   check(pra_route_topk(a, stream()), "route_topk");
+  return {mem_idx, mem_len, sel};
+}
+
+// Merge per-rank candidates ([B, world * 2k]: per rank k scores then k ids as int bits).
+std::vector<torch::Tensor> route_merge(torch::Tensor cands, int64_t world, int64_t k, int64_t budget,
+                                       torch::Tensor chunk_len, torch::Tensor chunk_row0, int64_t mem_max) {
+  c10::cuda::CUDAGuard guard(cands.device());
+  expect(cands, at::kFloat, "cands");
+  TORCH_CHECK(cands.dim() == 2 && cands.stride(1) == 1 && cands.size(1) == world * 2 * k, "cands [B, world*2k]");
+  RouteMergeArgs a{};
+  a.B = cands.size(0);
+  a.world = world;
+  a.k = k;
+  a.cands = ptr<const float>(cands);
+  a.row_stride = cands.stride(0);
+  a.budget = budget;
+  a.chunk_len = ptr<const int>(chunk_len);
+  a.chunk_row0 = ptr<const int>(chunk_row0);
+  auto io = cands.options().dtype(at::kInt);
+  auto mem_idx = torch::empty({a.B, std::max<int64_t>(mem_max, 1)}, io);
+  auto mem_len = torch::empty({a.B}, io);
+  auto sel = torch::empty({a.B, std::max<int64_t>(k, 1)}, io);
+  a.mem_idx = ptr<int>(mem_idx);
+  a.mem_max = std::max<int64_t>(mem_max, 1);
+  a.mem_len = ptr<int>(mem_len);
+  a.sel_out = ptr<int>(sel);
+  check(pra_route_merge(a, stream()), "route_merge");
   return {mem_idx, mem_len, sel};
 }
 
@@ -827,6 +863,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("silu_mul", &silu_mul);
   m.def("decode_attention", &decode_attention);
   m.def("route_topk", &route_topk);
+  m.def("route_merge", &route_merge);
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", &ipc_close);

@@ -230,8 +230,26 @@ struct RouteTopkArgs {
   int mem_max;
   int* mem_len;                // [B]
   int* sel_out;                // [B, k] selected chunk ids in chunk order (-1 pad), or null
+  float* cand_score;           // local mode: [B, k] best exact scores in rank order (no budget / rows)
+  int* cand_id;                // local mode: [B, k] their chunk ids + id_offset (-1 pad)
+  int id_offset;
 };
 cudaError_t pra_route_topk(const RouteTopkArgs& args, cudaStream_t stream);
+
+// Merge of the per-rank local top-k candidates (chunk-sharded routing across GPUs).
+struct RouteMergeArgs {
+  int B, world, k;
+  const float* cands;          // [B, row_stride]: per rank [k scores | k ids as int bits]
+  int64_t row_stride;
+  int budget;
+  const int* chunk_len;        // [C] (global chunk ids)
+  const int* chunk_row0;       // [C]
+  int* mem_idx;                // [B, mem_max]
+  int mem_max;
+  int* mem_len;                // [B]
+  int* sel_out;                // [B, k] or null
+};
+cudaError_t pra_route_merge(const RouteMergeArgs& args, cudaStream_t stream);
 
 // ---- tensor-parallel collectives over peer memory (tp_comm.cu) -------------------------
 constexpr int TP_MAX_RANKS = 8;

@@ -299,6 +299,77 @@ __device__ __forceinline__ int block_scan_int(int v, int* tmp, int* total) {
   return base + x - v;
 }
 
+// Ranks candidates by (-score, chunk id) and keeps the best k.  Local mode (cand_score set):
+// writes them in rank order (global ids = id + id_offset; -inf / -1 padding) and stops.
+// Otherwise applies the greedy token budget in rank order, sorts the kept chunks by id and
+// writes the selection and the memory row list (all threads of the CTA take part).
+__device__ void finish_selection(const float* cscore, const int* cand, int nc, int b, int k_req, int budget,
+                                 const int* chunk_len, const int* chunk_row0, int* mem_idx, int mem_max,
+                                 int* mem_len, int* sel_out, float* cand_score, int* cand_id, int id_offset,
+                                 int* picked, int* sel_chunk, int* sel_off, int* n_sel) {
+  const int k = min(k_req, nc);
+  for (int i = threadIdx.x; i < nc; i += blockDim.x) {
+    int rank = 0;
+    for (int j = 0; j < nc; ++j)
+      rank += (cscore[j] > cscore[i] || (cscore[j] == cscore[i] && cand[j] < cand[i])) ? 1 : 0;
+    picked[i] = rank;  // ranks are unique
+  }
+  __syncthreads();
+  if (cand_score != nullptr) {
+    for (int i = threadIdx.x; i < nc; i += blockDim.x) {
+      if (picked[i] < k) {
+        cand_score[(int64_t)b * k_req + picked[i]] = cscore[i];
+        cand_id[(int64_t)b * k_req + picked[i]] = cand[i] + id_offset;
+      }
+    }
+    for (int r = k + threadIdx.x; r < k_req; r += blockDim.x) {
+      cand_score[(int64_t)b * k_req + r] = -INFINITY;
+      cand_id[(int64_t)b * k_req + r] = -1;
+    }
+    return;
+  }
+  if (threadIdx.x == 0) {
+    int order[64];
+    const int kk = min(k, 64);
+    for (int i = 0; i < nc; ++i)
+      if (picked[i] < kk) order[picked[i]] = i;
+    int used = 0, chosen = 0;
+    int sel[64];
+    for (int r = 0; r < kk; ++r) {
+      const int c = cand[order[r]];
+      const int len = chunk_len[c];
+      if (budget >= 0 && used + len > budget) continue;
+      used += len;
+      sel[chosen++] = c;
+    }
+    for (int i = 1; i < chosen; ++i) {  // chunk order (insertion sort, k <= 64)
+      const int v = sel[i];
+      int j = i - 1;
+      while (j >= 0 && sel[j] > v) {
+        sel[j + 1] = sel[j];
+        --j;
+      }
+      sel[j + 1] = v;
+    }
+    int written = 0;
+    for (int i = 0; i < chosen; ++i) {
+      sel_chunk[i] = sel[i];
+      sel_off[i] = written;
+      written += chunk_len[sel[i]];
+    }
+    sel_off[chosen] = written;
+    *n_sel = chosen;
+    for (int i = 0; i < k_req && sel_out; ++i) sel_out[(int64_t)b * k_req + i] = i < chosen ? sel[i] : -1;
+    mem_len[b] = min(written, mem_max);
+  }
+  __syncthreads();
+  for (int i = 0; i < *n_sel; ++i) {  // the memory row list, written by all threads
+    const int c = sel_chunk[i], base = sel_off[i], len = sel_off[i + 1] - base;
+    for (int t = threadIdx.x; t < len; t += blockDim.x)
+      if (base + t < mem_max) mem_idx[(int64_t)b * mem_max + base + t] = chunk_row0[c] + t;
+  }
+}
+
 __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
   __shared__ uint32_t hist[256];
   __shared__ uint32_t prefix, prefix_mask;
@@ -327,9 +398,18 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
   for (int shift = 24; shift >= 0 && kc > 0; shift -= 8) {
     for (int i = threadIdx.x; i < 256; i += RT) hist[i] = 0;
     __syncthreads();
-    for (int i = threadIdx.x; i < n; i += RT) {
-      const uint32_t key = order_key(row[c0 + i]);
-      if ((key & prefix_mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    // warp-aggregated histogram: cosine scores share their top bits, so plain per-thread
+    // atomics would serialise on one or two bins
+    const int lane = threadIdx.x & 31;
+    for (int base = threadIdx.x - lane; base < n; base += RT) {
+      const int i = base + lane;
+      uint32_t digit = 256u;  // "no digit" for lanes past the end or outside the prefix
+      if (i < n) {
+        const uint32_t key = order_key(row[c0 + i]);
+        if ((key & prefix_mask) == prefix) digit = (key >> shift) & 255u;
+      }
+      const unsigned peers = __match_any_sync(0xffffffffu, digit);
+      if (digit < 256u && lane == __ffs(peers) - 1) atomicAdd(&hist[digit], (uint32_t)__popc(peers));
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -398,58 +478,40 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
     if (lane == 0) cscore[i] = acc * qinv;
   }
   __syncthreads();
-  // 4. top-k by (-score, chunk id), greedy budget in that order, then chunk order
-  const int k = min(a.k, nc);
-  for (int i = threadIdx.x; i < nc; i += RT) {
-    int rank = 0;
-    for (int j = 0; j < nc; ++j)
-      rank += (cscore[j] > cscore[i] || (cscore[j] == cscore[i] && cand[j] < cand[i])) ? 1 : 0;
-    picked[i] = rank;  // rank among candidates
-  }
+  // 4. top-k by (-score, chunk id) (+ greedy budget, chunk order and the row list)
+  finish_selection(cscore, cand, nc, b, a.k, a.budget, a.chunk_len, a.chunk_row0, a.mem_idx, a.mem_max, a.mem_len,
+                   a.sel_out, a.cand_score, a.cand_id, a.id_offset, picked, sel_chunk, sel_off, &n_sel);
+}
+
+// Cross-GPU merge of the per-rank candidates: row b holds world blocks of [k scores | k ids
+// (int bits)] (rank-major, as the column all-gather leaves them).
+__global__ void __launch_bounds__(256) route_merge_kernel(RouteMergeArgs a) {
+  __shared__ int cand[MAX_CAND];
+  __shared__ float cscore[MAX_CAND];
+  __shared__ int picked[MAX_CAND];
+  __shared__ int sel_chunk[64], sel_off[65];
+  __shared__ int n_sel;
+  __shared__ int nc_s;
+  const int b = blockIdx.x;
+  const float* row = a.cands + (int64_t)b * a.row_stride;
+  if (threadIdx.x == 0) nc_s = 0;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    // order[r] = candidate index of rank r (ranks are unique)
-    int order[64];
-    const int kk = min(k, 64);
-    for (int i = 0; i < nc; ++i)
-      if (picked[i] < kk) order[picked[i]] = i;
-    int used = 0, chosen = 0;
-    int sel[64];
-    for (int r = 0; r < kk; ++r) {
-      const int c = cand[order[r]];
-      const int len = a.chunk_len[c];
-      if (a.budget >= 0 && used + len > a.budget) continue;
-      used += len;
-      sel[chosen++] = c;
-    }
-    // chunk order (insertion sort, k <= 64)
-    for (int i = 1; i < chosen; ++i) {
-      const int v = sel[i];
-      int j = i - 1;
-      while (j >= 0 && sel[j] > v) {
-        sel[j + 1] = sel[j];
-        --j;
+  for (int i = threadIdx.x; i < a.world * a.k; i += blockDim.x) {
+    const int r = i / a.k, j = i % a.k;
+    const float sc = row[r * 2 * a.k + j];
+    const int id = __float_as_int(row[r * 2 * a.k + a.k + j]);
+    if (id >= 0) {
+      const int slot = atomicAdd(&nc_s, 1);
+      if (slot < MAX_CAND) {
+        cand[slot] = id;
+        cscore[slot] = sc;
       }
-      sel[j + 1] = v;
     }
-    int written = 0;
-    for (int i = 0; i < chosen; ++i) {
-      sel_chunk[i] = sel[i];
-      sel_off[i] = written;
-      written += a.chunk_len[sel[i]];
-    }
-    sel_off[chosen] = written;
-    n_sel = chosen;
-    for (int i = 0; i < a.k && a.sel_out; ++i) a.sel_out[(int64_t)b * a.k + i] = i < chosen ? sel[i] : -1;
-    a.mem_len[b] = min(written, a.mem_max);
   }
   __syncthreads();
-  // the memory row list, written by all threads
-  for (int i = 0; i < n_sel; ++i) {
-    const int c = sel_chunk[i], base = sel_off[i], len = sel_off[i + 1] - base;
-    for (int t = threadIdx.x; t < len; t += RT)
-      if (base + t < a.mem_max) a.mem_idx[(int64_t)b * a.mem_max + base + t] = a.chunk_row0[c] + t;
-  }
+  const int nc = min(nc_s, MAX_CAND);
+  finish_selection(cscore, cand, nc, b, a.k, a.budget, a.chunk_len, a.chunk_row0, a.mem_idx, a.mem_max, a.mem_len,
+                   a.sel_out, nullptr, nullptr, 0, picked, sel_chunk, sel_off, &n_sel);
 }
 
 }  // namespace llama
@@ -497,6 +559,13 @@ cudaError_t pra_decode_attention(const DecodeAttnParams& p, int head_dim, cudaSt
     case 128: return launch_decode<128>(p, st);
     default: return cudaErrorInvalidValue;
   }
+}
+
+cudaError_t pra_route_merge(const RouteMergeArgs& a, cudaStream_t st) {
+  if (a.B == 0) return cudaSuccess;
+  if (a.k > 64 || a.world * a.k > pra::llama::MAX_CAND) return cudaErrorInvalidValue;
+  pra::llama::route_merge_kernel<<<a.B, 256, 0, st>>>(a);
+  return cudaGetLastError();
 }
 
 cudaError_t pra_route_topk(const RouteTopkArgs& a, cudaStream_t st) {

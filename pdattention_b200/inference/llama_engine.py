@@ -153,7 +153,8 @@ class ChunkMemory:
 class PRALlamaEngine:
     """Batched prefill / decode of a PRA Llama-family model on one GPU (or one TP shard)."""
 
-    def __init__(self, weights: LlamaWeights, device, tp=None, decode_split_keys: int = 512, k_cand_factor: int = 4):
+    def __init__(self, weights: LlamaWeights, device, tp=None, decode_split_keys: int = 512, k_cand_factor: int = 4,
+                 shard_routing: bool = True):
         self.w = weights
         self.cfg = weights.cfg
         self.device = torch.device(device)
@@ -166,6 +167,7 @@ class PRALlamaEngine:
         self.kv_dim = self.kv_heads * cfg.head_dim
         self.split_keys = decode_split_keys
         self.k_cand_factor = k_cand_factor
+        self.shard_routing = shard_routing  # TP: score chunk slices per rank + cross-GPU top-k merge
         self.ext = _ext.require()
         self._rope_cache: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
         self.memory: ChunkMemory | None = None
@@ -219,17 +221,41 @@ class PRALlamaEngine:
         if self.tp is not None:
             rq = self.tp.all_gather_columns(rq)  # full kv_dim routing query on every rank
         rqn = torch.nn.functional.normalize(rq, dim=-1, eps=1e-12).to(torch.bfloat16)
-        scores = torch.empty((rows, mem.C_pad), device=self.device, dtype=torch.float32)
-        self.ext.gemm("tn_f32", rqn, mem.gn_bf16[layer], None, scores, None, None, 1.0, 0.0, None)
         k = cfg.top_k_chunks
+        k_cand = min(max(k * self.k_cand_factor, k), 512)
         budget = cfg.memory_budget_tokens if cfg.memory_budget_tokens is not None else -1
         mem_max = cfg.memory_tokens_per_row
         start, end = namespace if namespace is not None else self.namespace
         gn = mem.gn[layer].view(mem.C_pad, -1)
-        mem_idx, mem_len, sel = self.ext.route_topk(scores, rq, gn, start, end, mem.chunk_len, mem.chunk_row0, k,
-                                                    min(max(k * self.k_cand_factor, k), 512), budget, mem_max)
+        shards = self.tp.world if (self.tp is not None and self.shard_routing) else 1
+        if shards == 1:
+            scores = torch.empty((rows, mem.C_pad), device=self.device, dtype=torch.float32)
+            self.ext.gemm("tn_f32", rqn, mem.gn_bf16[layer], None, scores, None, None, 1.0, 0.0, None)
+            mem_idx, mem_len, sel = self.ext.route_topk(scores, rq, gn, start, end, mem.chunk_len, mem.chunk_row0, k,
+                                                        k_cand, budget, mem_max, False, 0)
+        else:
+            # chunk-sharded routing: this rank scores its slice of the chunks, keeps its exact
+            # local top-k, and the ranks' candidates are all-gathered and merged
+            c0, c1 = self._route_slice(mem)
+            width = c1 - c0
+            scores = torch.empty((rows, width), device=self.device, dtype=torch.float32)
+            self.ext.gemm("tn_f32", rqn, mem.gn_bf16[layer][c0:c1], None, scores, None, None, 1.0, 0.0, None)
+            lo = (start - c0).clamp(0, width).to(torch.int32)
+            hi = (end - c0).clamp(0, width).to(torch.int32)
+            cs, ci = self.ext.route_topk(scores, rq, gn[c0:c1], lo, hi, mem.chunk_len, mem.chunk_row0, k, k_cand, -1,
+                                         0, True, c0)
+            local = torch.cat([cs, ci.view(torch.float32)], dim=1)
+            merged = self.tp.all_gather_columns(local)
+            mem_idx, mem_len, sel = self.ext.route_merge(merged, self.tp.world, k, budget, mem.chunk_len,
+                                                         mem.chunk_row0, mem_max)
         self.last_selection[layer] = sel
         return mem_idx, mem_len
+
+    def _route_slice(self, mem) -> tuple[int, int]:
+        """This rank's chunk slice for sharded routing (8-aligned, covers the padded table)."""
+        per = (mem.C_pad // self.tp.world + 7) // 8 * 8
+        c0 = min(mem.C_pad, self.tp.rank * per)
+        return c0, min(mem.C_pad, c0 + per)
 
     # -- memory build -----------------------------------------------------------------
     @torch.no_grad()

@@ -27,7 +27,7 @@ from .peer import PeerBuffers
 
 class TensorParallel:
     def __init__(self, group=None, max_partial_elems: int = 64 << 20, max_gather_elems: int = 1 << 20,
-                 max_spins: int = 1 << 22):
+                 max_spins: int = 1 << 23):
         ext = _ext.require()
         self.group = group or dist.group.WORLD
         self.world = dist.get_world_size(self.group)

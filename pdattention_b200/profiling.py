@@ -7,6 +7,7 @@ profiler and then under ``ncu`` on one GPU with the same arguments::
     python -m pdattention_b200.profiling decode-small      # Llama-3-8B decode, 512 memory chunks
     python -m pdattention_b200.profiling train-table       # torch.profiler kernel table of one step (8 rows)
     python -m pdattention_b200.profiling decode-table      # kernel table of one decode step (64 rows)
+    torchrun --nproc-per-node N -m pdattention_b200.profiling decode-table-tp   # TP decode step table
 
 The ``*-small`` cases keep device memory to a few GB so full ``ncu`` captures of one
 launch end quickly.  Numbers printed under a profiler are not benchmark values.
@@ -106,15 +107,69 @@ def decode_table() -> None:
     _table(lambda: engine.decode_step(tok))
 
 
+def decode_table_tp(memory_chunks: int = 16384) -> None:
+    """Kernel table of one graph-replayed decode step on rank 0 of a tensor-parallel group
+    (run under ``torch.distributed.run``; 64 rows, 4096-token prompts, 1M-token memory)."""
+    import datetime
+    import os
+
+    import torch.distributed as dist
+
+    from .inference.llama_engine import LlamaWeights, PRALlamaEngine
+    from .models.llama import PRESETS
+    from .parallel.tp import TensorParallel
+
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    tp = TensorParallel()
+    dev = torch.device("cuda", local)
+    cfg = PRESETS["llama3-8b"](chunk_tokens=64, top_k_chunks=16, direct_window=4096)
+    engine = PRALlamaEngine(LlamaWeights.random(cfg, dev, tp_rank=tp.rank, tp_size=tp.world), dev, tp=tp)
+    gen = torch.Generator().manual_seed(0)
+    engine.build_memory(torch.randint(0, cfg.vocab_size, (memory_chunks, 64), generator=gen),
+                        torch.full((memory_chunks,), 64, dtype=torch.int32), batch_chunks=256)
+    rows = 64
+    engine.set_namespace(torch.zeros(rows, dtype=torch.int32), torch.full((rows,), memory_chunks, dtype=torch.int32))
+    tok = engine.prefill(torch.randint(0, cfg.vocab_size, (rows, 4096), generator=gen),
+                         torch.full((rows,), 4096, dtype=torch.int32), 16, row_batch=4).float().argmax(-1)
+    tok = engine.decode_step(tok).float().argmax(-1)
+    engine.capture_decode()
+    for _ in range(3):
+        tok = engine.decode_step_graphed(tok).float().argmax(-1)
+    tp.barrier()
+    t0 = time.perf_counter()
+    for _ in range(5):
+        tok = engine.decode_step_graphed(tok).float().argmax(-1)
+    torch.cuda.synchronize()
+    if tp.rank == 0:
+        print(f"step wall ms {1000 * (time.perf_counter() - t0) / 5:.2f}")
+    tp.barrier()
+    # every rank runs under the profiler (its start-up stalls the host), only rank 0 prints
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+        tp.barrier()
+        engine.decode_step_graphed(tok)
+        torch.cuda.synchronize()
+    if tp.rank == 0:
+        print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=40, max_name_column_width=70))
+    tp.barrier()
+    engine.release_graph()
+    tp.close()
+    dist.destroy_process_group()
+
+
 CASES = {"train-small": train_small, "decode-small": decode_small, "train-table": train_table,
-         "decode-table": decode_table}
+         "decode-table": decode_table, "decode-table-tp": decode_table_tp}
 
 
 def main(argv=None) -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("case", choices=sorted(CASES))
     args = parser.parse_args(argv)
-    torch.cuda.set_device(0)
+    if args.case != "decode-table-tp":
+        torch.cuda.set_device(0)
     CASES[args.case]()
 
 

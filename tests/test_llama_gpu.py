@@ -83,7 +83,7 @@ def test_route_topk_exact_with_ties(ext):
     clen = torch.full((C + 8,), 8, device="cuda", dtype=torch.int32)
     clen[::7] = 5
     row0 = torch.arange(C + 8, device="cuda", dtype=torch.int32) * 8
-    mem_idx, mem_len, sel = ext.route_topk(approx, query, gists, start, end, clen, row0, k, 64, -1, k * 8)
+    mem_idx, mem_len, sel = ext.route_topk(approx, query, gists, start, end, clen, row0, k, 64, -1, k * 8, False, 0)
     exact = F.normalize(query, dim=-1) @ gists.t()
     for b in range(B):
         ids = list(range(int(start[b]), int(end[b])))
@@ -96,7 +96,7 @@ def test_route_topk_exact_with_ties(ext):
         assert mem_idx[b, : len(rows)].tolist() == rows
     assert 3 in [int(c) for c in sel[0]] and 10 in [int(c) for c in sel[0]]
     # a token budget keeps whole chunks greedily in score order
-    mem_idx, mem_len, sel = ext.route_topk(approx, query, gists, start, end, clen, row0, k, 64, 20, k * 8)
+    mem_idx, mem_len, sel = ext.route_topk(approx, query, gists, start, end, clen, row0, k, 64, 20, k * 8, False, 0)
     assert int(mem_len.max()) <= 20
 
 
@@ -217,3 +217,32 @@ def test_graphed_decode_matches_eager(ext):
         outs.append(torch.stack(seq))
         assert engine.cache_len.tolist() == [12 + 5, 9 + 5]
     assert torch.allclose(outs[0], outs[1], atol=1e-3), (outs[0] - outs[1]).abs().max()
+
+
+def test_sharded_routing_merge_equals_unsharded(ext):
+    """Local top-k per chunk slice + merge of the slices' candidates == routing over all chunks."""
+    torch.manual_seed(5)
+    B, C, D, k = 6, 800, 128, 16
+    gists = F.normalize(torch.randn(C, D, device="cuda"), dim=-1)
+    query = torch.randn(B, D, device="cuda")
+    scores = (F.normalize(query, dim=-1).bfloat16().float() @ gists.bfloat16().float().t()).contiguous()
+    start = torch.tensor([0, 0, 50, 300, 0, 790], device="cuda", dtype=torch.int32)
+    end = torch.tensor([C, 200, 700, 420, C, C], device="cuda", dtype=torch.int32)
+    clen = torch.full((C,), 64, device="cuda", dtype=torch.int32)
+    row0 = torch.arange(C, device="cuda", dtype=torch.int32) * 64
+    want = ext.route_topk(scores, query, gists, start, end, clen, row0, k, 64, 640, k * 64, False, 0)
+    world, per = 4, C // 4
+    blocks = []
+    for r in range(world):
+        c0, c1 = r * per, (r + 1) * per
+        lo = (start - c0).clamp(0, per).to(torch.int32)
+        hi = (end - c0).clamp(0, per).to(torch.int32)
+        cs, ci = ext.route_topk(scores[:, c0:c1].contiguous(), query, gists[c0:c1].contiguous(), lo, hi, clen, row0, k,
+                                64, -1, 0, True, c0)
+        blocks.append(torch.cat([cs, ci.view(torch.float32)], dim=1))
+    got = ext.route_merge(torch.cat(blocks, dim=1).contiguous(), world, k, 640, clen, row0, k * 64)
+    assert torch.equal(got[1], want[1])
+    assert torch.equal(got[2], want[2])
+    for b in range(B):
+        n = int(want[1][b])
+        assert torch.equal(got[0][b, :n], want[0][b, :n])
