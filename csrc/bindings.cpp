@@ -699,6 +699,28 @@ std::vector<torch::Tensor> route_merge(torch::Tensor cands, int64_t world, int64
   return {mem_idx, mem_len, sel};
 }
 
+// ---------------------------------------------------------------- embeddings
+// ids int32 [M]; positions int32 [M] or null (position = m % period); tables bf16 [*, D].
+torch::Tensor embed_add(torch::Tensor ids, c10::optional<torch::Tensor> positions, int64_t period, torch::Tensor tok,
+                        torch::Tensor pos) {
+  c10::cuda::CUDAGuard guard(ids.device());
+  TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous(), "ids must be contiguous int32");
+  expect(tok, at::kBFloat16, "tok");
+  expect(pos, at::kBFloat16, "pos");
+  TORCH_CHECK(tok.is_contiguous() && pos.is_contiguous() && tok.size(1) == pos.size(1), "embedding tables");
+  if (positions.has_value()) {
+    TORCH_CHECK(positions->scalar_type() == at::kInt && positions->is_contiguous() &&
+                    positions->numel() == ids.numel(),
+                "positions must be int32 like ids");
+  }
+  const int64_t M = ids.numel(), D = tok.size(1);
+  auto out = torch::empty({M, D}, tok.options());
+  check(pra_embed_add(ptr<const int>(ids), optr<int>(positions), (int)period, ptr<const __nv_bfloat16>(tok),
+                      ptr<const __nv_bfloat16>(pos), M, D, ptr<__nv_bfloat16>(out), stream()),
+        "embed_add");
+  return out;
+}
+
 // ---------------------------------------------------------------- peer buffers (CUDA IPC)
 // A dedicated cudaMalloc allocation (zeroed) that other processes on the node can map;
 // plain peer loads and stores only (no multicast object is ever created).
@@ -864,6 +886,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_attention", &decode_attention);
   m.def("route_topk", &route_topk);
   m.def("route_merge", &route_merge);
+  m.def("embed_add", &embed_add);
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", &ipc_close);

@@ -277,3 +277,7 @@ struct TpAllgatherArgs {
 };
 cudaError_t pra_tp_allreduce(const TpAllreduceArgs& args, cudaStream_t stream);
 cudaError_t pra_tp_allgather(const TpAllgatherArgs& args, cudaStream_t stream);
+
+// ---- embeddings (embed.cu) ---------------------------------------------------------------
+cudaError_t pra_embed_add(const int* ids, const int* positions, int period, const __nv_bfloat16* tok,
+                          const __nv_bfloat16* pos, int64_t M, int D, __nv_bfloat16* out, cudaStream_t stream);

@@ -268,7 +268,20 @@ class Namespace:
     """Device arrays describing row-local routing namespaces (see ``RouteParams``)."""
 
     def __init__(self, rows_entries: list[list[int]], entries: list[EntryRecord], chunks: list[ChunkRecord],
-                 device):
+                 device, arrays: list[torch.Tensor] | None = None):
+        if arrays is None:
+            host = self.host_arrays(rows_entries, entries, chunks)
+            arrays = _upload(device, *host)
+            empty = len(host[3]) == 0
+        else:
+            empty = bool(getattr(arrays, "empty", False))
+        (self.row_pos_off, self.row_ref_off, self.ref_pos_off, self.pos_chunk, self.pos_ref,
+         self.pos_rank) = arrays
+        self.rows_entries = rows_entries
+        self.empty = empty
+
+    @staticmethod
+    def host_arrays(rows_entries, entries, chunks) -> list[list[int]]:
         row_pos_off, row_ref_off, ref_pos_off = [0], [0], [0]
         pos_chunk, pos_ref, pos_rank = [], [], []
         for entry_ids in rows_entries:
@@ -283,10 +296,7 @@ class Namespace:
                 ref_pos_off.append(len(pos_chunk))
             row_pos_off.append(len(pos_chunk))
             row_ref_off.append(len(ref_pos_off) - 1)
-        (self.row_pos_off, self.row_ref_off, self.ref_pos_off, self.pos_chunk, self.pos_ref,
-         self.pos_rank) = _upload(device, row_pos_off, row_ref_off, ref_pos_off, pos_chunk, pos_ref, pos_rank)
-        self.rows_entries = rows_entries
-        self.empty = len(pos_chunk) == 0
+        return [row_pos_off, row_ref_off, ref_pos_off, pos_chunk, pos_ref, pos_rank]
 
 
 class BatchMemory:
@@ -363,6 +373,8 @@ class BatchPlan:
     rows: list
     seq_len: int
     waves: list
+    wave_tables: list | None = None   # per wave: {name: (offset, count)} into ``packed``
+    packed: object | None = None      # every wave's int32 host tables in one array (one upload)
 
 
 class KMeansTables:
@@ -653,7 +665,71 @@ class DeviceRuntime:
                         members.append(c)
                         seq += 1
             waves.append(members)
-        return BatchPlan(metadata_rows, caches, builders, entries, chunks, rows, seq_len, waves)
+        plan = BatchPlan(metadata_rows, caches, builders, entries, chunks, rows, seq_len, waves)
+        self._wave_tables(plan)
+        return plan
+
+    def _wave_tables(self, plan: "BatchPlan") -> None:
+        """Every wave's host-side inputs (token ids, padding masks, budgets, routing
+        namespaces, gist inputs) packed into one int32 array, so the cache build ships them
+        to the device in a single pinned copy."""
+        import numpy as np
+
+        cfg = self.cfg
+        L = plan.seq_len
+        chunks, entries = plan.chunks, plan.entries
+        limit = cfg.effective_model_max_context_tokens - cfg.context_safety_reserve_tokens
+        cap = cfg.max_materialized_memory_tokens
+        parts, tables, cursor = [], [], 0
+
+        def put(table, name, values, dtype=np.int32):
+            nonlocal cursor
+            arr = np.asarray(values, dtype=dtype).ravel()
+            if dtype == np.uint8:  # bytes ride in int32 words
+                pad = (-arr.size) % 4
+                words = np.concatenate([arr, np.zeros(pad, np.uint8)]).view(np.int32)
+                table[name] = (cursor, int(words.size), int(arr.size))
+                parts.append(words)
+                cursor += words.size
+                return
+            if arr.size == 0:
+                arr = np.zeros(1, np.int32)
+            table[name] = (cursor, int(arr.size), int(arr.size))
+            parts.append(arr)
+            cursor += arr.size
+
+        for members in plan.waves:
+            t = {}
+            n = len(members)
+            lens = [len(chunks[c].token_ids) for c in members]
+            ids = np.zeros((n, L), dtype=np.int32)
+            for i, c in enumerate(members):
+                ids[i, : lens[i]] = chunks[c].token_ids
+            valid = (np.arange(L)[None, :] < np.asarray(lens)[:, None]).astype(np.uint8)
+            put(t, "ids", ids)
+            put(t, "valid", valid, np.uint8)
+            put(t, "lens", lens)
+            put(t, "last", [k - 1 for k in lens])
+            put(t, "budget", [max(0, min(limit - k, cap) if cap is not None else limit - k) for k in lens])
+            put(t, "gist_rows", [chunks[c].seq * L for c in members])
+            put(t, "dest", members)
+            if cfg.gist_mode == "kmeans":
+                firsts, offs = self.kmeans_tables.lookup(lens)
+                put(t, "km_first", firsts)
+                put(t, "km_off", offs)
+            rows_entries = None
+            if any(entries[chunks[c].entry].use_memory for c in members):
+                rows_entries = [list(entries[chunks[c].entry].visible) if entries[chunks[c].entry].use_memory else []
+                                for c in members]
+                host = Namespace.host_arrays(rows_entries, entries, chunks)
+                for name, arr in zip(("ns0", "ns1", "ns2", "ns3", "ns4", "ns5"), host):
+                    put(t, name, arr)
+                t["ns_empty"] = len(host[3]) == 0
+            t["rows_entries"] = rows_entries
+            t["n"], t["max_len"] = n, max(lens) if lens else 1
+            tables.append(t)
+        plan.wave_tables = tables
+        plan.packed = np.concatenate(parts) if parts else np.zeros(1, np.int32)
 
     def prefetch(self, metadata_rows: list[dict], tokenizer=None, resolver_config=None, part: int = 0,
                  parts: int = 1) -> None:
@@ -691,68 +767,58 @@ class DeviceRuntime:
         caches, builders, entries, chunks, rows, seq_len = (plan.caches, plan.builders, plan.entries, plan.chunks,
                                                             plan.rows, plan.seq_len)
         memory = BatchMemory(self, entries, chunks, rows, seq_len, self.device)
+        host = torch.from_numpy(plan.packed)
+        if self.device.type == "cuda":
+            host = host.pin_memory()
+        packed = host.to(self.device, non_blocking=True)
         with torch.no_grad():
             start = 0
-            for wave_chunks in plan.waves:
+            for wave_chunks, table in zip(plan.waves, plan.wave_tables):
                 if not wave_chunks:
                     continue
-                self._encode_wave(memory, wave_chunks, start)
+                self._encode_wave(memory, wave_chunks, start, table, packed)
                 start += len(wave_chunks)
         self.last_memory = memory
         return memory, caches, builders
 
-    def _encode_wave(self, memory: BatchMemory, wave_chunks: list[int], first_seq: int) -> None:
-        cfg = self.cfg
+    def _encode_wave(self, memory: BatchMemory, wave_chunks: list[int], first_seq: int, table: dict,
+                     packed: torch.Tensor) -> None:
+        def view(name, dtype=None):
+            off, words, count = table[name]
+            t = packed[off: off + words]
+            return t.view(torch.uint8)[:count] if dtype == torch.uint8 else t
+
         n = len(wave_chunks)
         L = memory.seq_len
-        import numpy as np
-
-        lens = [len(memory.chunks[c].token_ids) for c in wave_chunks]
-        ids_host = np.zeros((n, L), dtype=np.int32)
-        for i, c in enumerate(wave_chunks):
-            ids_host[i, : lens[i]] = memory.chunks[c].token_ids
-        # each chunk is its own native call: its budget uses its own (unpadded) length
-        limit = cfg.effective_model_max_context_tokens - cfg.context_safety_reserve_tokens
-        cap = cfg.max_materialized_memory_tokens
-        budgets = [max(0, min(limit - k, cap) if cap is not None else limit - k) for k in lens]
-        ids, lengths, budget = _upload(self.device, ids_host, lens, budgets)
-        ids = ids.view(n, L).long()
-        last = lengths - 1
-        valid = (torch.arange(L, device=self.device)[None, :] < lengths[:, None]).to(torch.uint8)
-        positions = torch.arange(L, device=self.device).expand(n, L)
-        x = self.embed(ids, positions)
-        entries = memory.entries
-        needs_memory = any(entries[memory.chunks[c].entry].use_memory for c in wave_chunks)
+        ext = _ext.require()
+        x = ext.embed_add(view("ids"), None, L, self.tok_emb_w, self.pos_emb_w)
+        valid = view("valid", torch.uint8).view(n, L)
         namespace = None
-        if needs_memory:
-            rows_entries = [list(entries[memory.chunks[c].entry].visible)
-                            if entries[memory.chunks[c].entry].use_memory else [] for c in wave_chunks]
-            namespace = Namespace(rows_entries, entries, memory.chunks, self.device)
+        if table["rows_entries"] is not None:
+            arrays = [view(name) for name in ("ns0", "ns1", "ns2", "ns3", "ns4", "ns5")]
+            namespace = Namespace(table["rows_entries"], memory.entries, memory.chunks, self.device, arrays)
+            namespace.empty = table["ns_empty"]
         rows = slice(first_seq * L, (first_seq + n) * L)
-        self.run_blocks(x, n, L, valid, namespace, memory, stop_after_kv=True, pool_rows=rows, budget=budget,
-                        query_rows=last)
-        self._pool_gists(memory, wave_chunks)
+        self.run_blocks(x, n, L, valid, namespace, memory, stop_after_kv=True, pool_rows=rows,
+                        budget=view("budget"), query_rows=view("last"))
+        self._pool_gists(memory, table, view)
 
-    def _pool_gists(self, memory: BatchMemory, wave_chunks: list[int]) -> None:
+    def _pool_gists(self, memory: BatchMemory, table: dict, view) -> None:
         """One launch builds the wave's gists for every layer, written in place into the cache tables."""
         cfg = self.cfg
         d = cfg.d_model
         ext = _ext.require()
-        lengths = [len(memory.chunks[c].token_ids) for c in wave_chunks]
-        rows = [memory.chunks[c].seq * memory.seq_len for c in wave_chunks]
         pk, pv = memory.k_all(d), memory.v_all(d)
+        start, length, dest = view("gist_rows"), view("lens"), view("dest")
         if cfg.gist_mode == "mean":
-            start, length, dest = _upload(self.device, rows, lengths, wave_chunks)
             ext.gist_mean_into(pk, pv, start, length, dest, memory.gist_k_all, memory.gist_v_all, memory.gists_all,
                                memory.gist_count_all)
             return
-        firsts, offs = self.kmeans_tables.lookup(lengths)
-        start, length, dest, first, off = _upload(self.device, rows, lengths, wave_chunks, firsts, offs)
         ext.gist_kmeans_into(pk, pv, start, length, dest, memory.gist_k_all, memory.gist_v_all, memory.gists_all,
-                             memory.gist_count_all, max(lengths), cfg.gist_kmeans_max_iters,
+                             memory.gist_count_all, table["max_len"], cfg.gist_kmeans_max_iters,
                              float(cfg.gist_kmeans_tol), bool(cfg.gist_kmeans_normalize),
                              cfg.gist_kmeans_init == "kmeans++", cfg.gist_kmeans_empty_cluster_policy == "farthest",
-                             first, self.kmeans_tables.idx, self.kmeans_tables.draws, off, None)
+                             view("km_first"), self.kmeans_tables.idx, self.kmeans_tables.draws, view("km_off"), None)
 
     # -- prompt forward + loss ----------------------------------------------------
     def prompt_forward(self, input_ids, attention_mask, memory: BatchMemory | None, position_offset=0):
