@@ -394,6 +394,44 @@ def run_decode(impl: str, steps: int, warmup: int, gpus: int, memory_tokens: int
     return result
 
 
+def run_memory_sweep(gpus: int, impl: str, steps: int, warmup: int):
+    """Routing + memory-attention sweep of one Qwen2-7B-shaped PRA layer, memory sharded by chunk
+    over the GPUs: 64K / 1M / 16M tokens x G in {1, 4} x chunk top-k in {4, 16, 64}.  One JSON
+    line per configuration and arm (``fused``: this library's kernels and peer-memory
+    collectives; ``baseline``: PyTorch operators and NCCL)."""
+    rank, local, world = _env()
+    if gpus != world:
+        raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    comm = group = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        from pdattention_b200.parallel.tp import TensorParallel
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        comm = TensorParallel(max_partial_elems=1 << 10, max_gather_elems=4 << 20)
+        group = dist.group.WORLD
+    from pdattention_b200.inference.memory_sweep import run_sweep
+
+    arms = ("baseline",) if impl == "reference" else ("fused", "baseline")
+    for result in run_sweep(iters=max(steps, 5), warmup=warmup, comm=comm, group=group, arms=arms):
+        result.update({"metric": "PRA layer routing + memory attention time (Qwen2-7B layer shapes)",
+                       "unit": "us", "higher_is_better": False, "dtype": "bf16",
+                       "data": "synthetic Gaussian K/V, chunk-sharded memory",
+                       "baseline_note": "baseline = PyTorch operators + NCCL for the same math"})
+        yield result
+    if comm is not None:
+        comm.close()
+        import torch.distributed as dist
+
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
 class _Unavailable(RuntimeError):
     pass
 
@@ -404,7 +442,7 @@ def main() -> None:
     parser.add_argument("--steps", type=int, default=10)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["pra", "reference"], default="pra")
-    parser.add_argument("--workload", choices=["train", "decode"], default="train",
+    parser.add_argument("--workload", choices=["train", "decode", "memory-sweep"], default="train",
                         help="train: TinyGPT-PRA data-parallel training (default); decode: PRA Llama-3-8B decode "
                              "with a chunk memory (tensor parallel over the GPUs)")
     parser.add_argument("--memory-tokens", type=int, default=None,
@@ -413,6 +451,11 @@ def main() -> None:
     parser.add_argument("--batch", type=int, default=64)
     args = parser.parse_args()
     rank = _env()[0]
+    if args.workload == "memory-sweep":
+        for line in run_memory_sweep(args.gpus, args.impl, args.steps, max(args.warmup, 3)):
+            if rank == 0:
+                print(json.dumps(line), flush=True)
+        return
     if args.workload == "decode":
         result = run_decode(args.impl, args.steps, max(args.warmup, 3), args.gpus, args.memory_tokens, args.batch)
         if rank == 0:

@@ -629,7 +629,7 @@ std::vector<torch::Tensor> decode_attention(torch::Tensor q, int64_t heads, int6
 std::vector<torch::Tensor> route_topk(torch::Tensor scores, torch::Tensor query, torch::Tensor gists,
                                       torch::Tensor ns_start, torch::Tensor ns_end, torch::Tensor chunk_len,
                                       torch::Tensor chunk_row0, int64_t k, int64_t k_cand, int64_t budget,
-                                      int64_t mem_max, bool local, int64_t id_offset) {
+                                      int64_t mem_max, bool local, int64_t id_offset, int64_t gists_per_chunk) {
   c10::cuda::CUDAGuard guard(scores.device());
   expect(scores, at::kFloat, "scores");
   expect(query, at::kFloat, "query");
@@ -639,6 +639,7 @@ std::vector<torch::Tensor> route_topk(torch::Tensor scores, torch::Tensor query,
   RouteTopkArgs a{};
   a.B = scores.size(0);
   a.D = gists.size(-1);
+  a.G = gists_per_chunk;
   a.scores = ptr<const float>(scores);
   a.score_stride = scores.stride(0);
   a.query = ptr<const float>(query);
@@ -697,6 +698,18 @@ std::vector<torch::Tensor> route_merge(torch::Tensor cands, int64_t world, int64
   a.sel_out = ptr<int>(sel);
   check(pra_route_merge(a, stream()), "route_merge");
   return {mem_idx, mem_len, sel};
+}
+
+// Combine gathered attention partials [B, world * H * (D + 2)] -> [B, H * D] bf16.
+torch::Tensor combine_partials(torch::Tensor parts, int64_t world, int64_t heads, int64_t head_dim) {
+  c10::cuda::CUDAGuard guard(parts.device());
+  expect(parts, at::kFloat, "parts");
+  TORCH_CHECK(parts.is_contiguous() && parts.size(-1) == world * heads * (head_dim + 2), "parts layout");
+  const int64_t B = parts.size(0);
+  auto out = torch::empty({B, heads * head_dim}, parts.options().dtype(at::kBFloat16));
+  check(pra_combine_partials(ptr<const float>(parts), B, world, heads, head_dim, ptr<__nv_bfloat16>(out), stream()),
+        "combine_partials");
+  return out;
 }
 
 // ---------------------------------------------------------------- embeddings
@@ -887,6 +900,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("route_topk", &route_topk);
   m.def("route_merge", &route_merge);
   m.def("embed_add", &embed_add);
+  m.def("combine_partials", &combine_partials);
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", &ipc_close);

@@ -215,6 +215,7 @@ cudaError_t pra_decode_attention(const DecodeAttnParams& p, int head_dim, cudaSt
 
 struct RouteTopkArgs {
   int B, D;
+  int G;                       // gists per chunk: scores / gists hold C * G rows, chunk score = max over G
   const float* scores;         // [B, score_stride] approximate cosine scores (tensor-core GEMM)
   int64_t score_stride;
   const float* query;          // [B, query_stride] routing queries (fp32, unnormalised)
@@ -250,6 +251,8 @@ struct RouteMergeArgs {
   int* sel_out;                // [B, k] or null
 };
 cudaError_t pra_route_merge(const RouteMergeArgs& args, cudaStream_t stream);
+cudaError_t pra_combine_partials(const float* parts, int B, int world, int H, int D, __nv_bfloat16* out,
+                                 cudaStream_t stream);
 
 // ---- tensor-parallel collectives over peer memory (tp_comm.cu) -------------------------
 constexpr int TP_MAX_RANKS = 8;

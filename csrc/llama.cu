@@ -351,11 +351,11 @@ __device__ void finish_selection(const float* cscore, const int* cand, int nc, i
       }
       sel[j + 1] = v;
     }
-    int written = 0;
+    int written = 0;  // chunks held elsewhere (row0 < 0) stay selected but add no rows here
     for (int i = 0; i < chosen; ++i) {
       sel_chunk[i] = sel[i];
       sel_off[i] = written;
-      written += chunk_len[sel[i]];
+      written += chunk_row0[sel[i]] >= 0 ? chunk_len[sel[i]] : 0;
     }
     sel_off[chosen] = written;
     *n_sel = chosen;
@@ -386,6 +386,14 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
   const int c0 = a.ns_start[b], c1 = a.ns_end[b];
   const int n = max(c1 - c0, 0);
   const float* row = a.scores + (int64_t)b * a.score_stride;
+  const int G = a.G > 0 ? a.G : 1;
+  // a chunk's score is the best of its G gists' scores (gist aggregation "max")
+  auto chunk_score = [&](int c) -> float {
+    if (G == 1) return row[c];
+    float m = row[(int64_t)c * G];
+    for (int g = 1; g < G; ++g) m = fmaxf(m, row[(int64_t)c * G + g]);
+    return m;
+  };
   const int kc = min(a.k_cand, min(n, MAX_CAND));
   if (threadIdx.x == 0) {
     prefix = 0;
@@ -405,7 +413,7 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
       const int i = base + lane;
       uint32_t digit = 256u;  // "no digit" for lanes past the end or outside the prefix
       if (i < n) {
-        const uint32_t key = order_key(row[c0 + i]);
+        const uint32_t key = order_key(chunk_score(c0 + i));
         if ((key & prefix_mask) == prefix) digit = (key >> shift) & 255u;
       }
       const unsigned peers = __match_any_sync(0xffffffffu, digit);
@@ -428,7 +436,7 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
   // 2. candidates: every chunk strictly above the threshold, then ties at it (lowest ids first)
   const uint32_t thr = prefix;
   for (int i = threadIdx.x; i < n && kc > 0; i += RT) {
-    if (order_key(row[c0 + i]) > thr) {
+    if (order_key(chunk_score(c0 + i)) > thr) {
       const int slot = atomicAdd(&n_cand, 1);
       if (slot < MAX_CAND) cand[slot] = c0 + i;
     }
@@ -440,13 +448,13 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
     const int seg = (n + RT - 1) / RT;
     const int s0 = min(n, threadIdx.x * seg), s1 = min(n, s0 + seg);
     int mine = 0;
-    for (int i = s0; i < s1 && kc > 0; ++i) mine += order_key(row[c0 + i]) == thr ? 1 : 0;
+    for (int i = s0; i < s1 && kc > 0; ++i) mine += order_key(chunk_score(c0 + i)) == thr ? 1 : 0;
     int total = 0;
     const int before = block_scan_int(mine, scan_tmp, &total);
     const int want = kc - above;
     int slot = above + before;
     for (int i = s0; i < s1 && kc > 0 && slot < above + want; ++i)
-      if (order_key(row[c0 + i]) == thr) cand[slot++] = c0 + i;
+      if (order_key(chunk_score(c0 + i)) == thr) cand[slot++] = c0 + i;
     __syncthreads();
     if (threadIdx.x == 0) n_cand = kc > 0 ? above + min(want, total) : 0;
     __syncthreads();
@@ -470,12 +478,15 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
   __syncthreads();
   const float qinv = red[0];
   for (int i = warp; i < nc; i += RT / 32) {
-    const float* g = a.gists + (int64_t)cand[i] * a.D;
     const float* q = a.query + (int64_t)b * a.query_stride;
-    float acc = 0.f;
-    for (int d = lane; d < a.D; d += 32) acc += q[d] * g[d];
-    acc = warp_sum(acc);
-    if (lane == 0) cscore[i] = acc * qinv;
+    float best = -INFINITY;
+    for (int gi = 0; gi < G; ++gi) {
+      const float* g = a.gists + ((int64_t)cand[i] * G + gi) * a.D;
+      float acc = 0.f;
+      for (int d = lane; d < a.D; d += 32) acc += q[d] * g[d];
+      best = fmaxf(best, warp_sum(acc));
+    }
+    if (lane == 0) cscore[i] = best * qinv;
   }
   __syncthreads();
   // 4. top-k by (-score, chunk id) (+ greedy budget, chunk order and the row list)
@@ -512,6 +523,30 @@ __global__ void __launch_bounds__(256) route_merge_kernel(RouteMergeArgs a) {
   const int nc = min(nc_s, MAX_CAND);
   finish_selection(cscore, cand, nc, b, a.k, a.budget, a.chunk_len, a.chunk_row0, a.mem_idx, a.mem_max, a.mem_len,
                    a.sel_out, nullptr, nullptr, 0, picked, sel_chunk, sel_off, &n_sel);
+}
+
+// Combine per-rank attention partials: parts [B, world, H, D + 2] (unnormalised out, max,
+// sum; max in natural-log units) -> out [B, H * D] bf16.
+__global__ void combine_partials_kernel(const float* __restrict__ parts, int world, int H, int D,
+                                        __nv_bfloat16* __restrict__ out) {
+  const int b = blockIdx.x / H, h = blockIdx.x % H;
+  const int64_t stride_r = (int64_t)H * (D + 2);
+  const float* base = parts + (int64_t)b * world * stride_r + (int64_t)h * (D + 2);
+  float M = -INFINITY;
+  for (int r = 0; r < world; ++r) M = fmaxf(M, base[r * stride_r + D]);
+  float L = 0.f;
+  for (int r = 0; r < world; ++r) {
+    const float m = base[r * stride_r + D];
+    if (m != -INFINITY) L += base[r * stride_r + D + 1] * __expf(m - M);
+  }
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f;
+    for (int r = 0; r < world; ++r) {
+      const float m = base[r * stride_r + D];
+      if (m != -INFINITY) acc += base[r * stride_r + d] * __expf(m - M);
+    }
+    out[(int64_t)b * H * D + h * D + d] = __float2bfloat16(L > 0.f ? acc / L : 0.f);
+  }
 }
 
 }  // namespace llama
@@ -559,6 +594,13 @@ cudaError_t pra_decode_attention(const DecodeAttnParams& p, int head_dim, cudaSt
     case 128: return launch_decode<128>(p, st);
     default: return cudaErrorInvalidValue;
   }
+}
+
+cudaError_t pra_combine_partials(const float* parts, int B, int world, int H, int D, __nv_bfloat16* out,
+                                 cudaStream_t st) {
+  if (B == 0) return cudaSuccess;
+  pra::llama::combine_partials_kernel<<<B * H, 128, 0, st>>>(parts, world, H, D, out);
+  return cudaGetLastError();
 }
 
 cudaError_t pra_route_merge(const RouteMergeArgs& a, cudaStream_t st) {

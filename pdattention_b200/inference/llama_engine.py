@@ -232,7 +232,7 @@ class PRALlamaEngine:
             scores = torch.empty((rows, mem.C_pad), device=self.device, dtype=torch.float32)
             self.ext.gemm("tn_f32", rqn, mem.gn_bf16[layer], None, scores, None, None, 1.0, 0.0, None)
             mem_idx, mem_len, sel = self.ext.route_topk(scores, rq, gn, start, end, mem.chunk_len, mem.chunk_row0, k,
-                                                        k_cand, budget, mem_max, False, 0)
+                                                        k_cand, budget, mem_max, False, 0, 1)
         else:
             # chunk-sharded routing: this rank scores its slice of the chunks, keeps its exact
             # local top-k, and the ranks' candidates are all-gathered and merged
@@ -243,7 +243,7 @@ class PRALlamaEngine:
             lo = (start - c0).clamp(0, width).to(torch.int32)
             hi = (end - c0).clamp(0, width).to(torch.int32)
             cs, ci = self.ext.route_topk(scores, rq, gn[c0:c1], lo, hi, mem.chunk_len, mem.chunk_row0, k, k_cand, -1,
-                                         0, True, c0)
+                                         0, True, c0, 1)
             local = torch.cat([cs, ci.view(torch.float32)], dim=1)
             merged = self.tp.all_gather_columns(local)
             mem_idx, mem_len, sel = self.ext.route_merge(merged, self.tp.world, k, budget, mem.chunk_len,

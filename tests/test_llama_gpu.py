@@ -83,7 +83,7 @@ def test_route_topk_exact_with_ties(ext):
     clen = torch.full((C + 8,), 8, device="cuda", dtype=torch.int32)
     clen[::7] = 5
     row0 = torch.arange(C + 8, device="cuda", dtype=torch.int32) * 8
-    mem_idx, mem_len, sel = ext.route_topk(approx, query, gists, start, end, clen, row0, k, 64, -1, k * 8, False, 0)
+    mem_idx, mem_len, sel = ext.route_topk(approx, query, gists, start, end, clen, row0, k, 64, -1, k * 8, False, 0, 1)
     exact = F.normalize(query, dim=-1) @ gists.t()
     for b in range(B):
         ids = list(range(int(start[b]), int(end[b])))
@@ -96,7 +96,7 @@ def test_route_topk_exact_with_ties(ext):
         assert mem_idx[b, : len(rows)].tolist() == rows
     assert 3 in [int(c) for c in sel[0]] and 10 in [int(c) for c in sel[0]]
     # a token budget keeps whole chunks greedily in score order
-    mem_idx, mem_len, sel = ext.route_topk(approx, query, gists, start, end, clen, row0, k, 64, 20, k * 8, False, 0)
+    mem_idx, mem_len, sel = ext.route_topk(approx, query, gists, start, end, clen, row0, k, 64, 20, k * 8, False, 0, 1)
     assert int(mem_len.max()) <= 20
 
 
@@ -230,7 +230,7 @@ def test_sharded_routing_merge_equals_unsharded(ext):
     end = torch.tensor([C, 200, 700, 420, C, C], device="cuda", dtype=torch.int32)
     clen = torch.full((C,), 64, device="cuda", dtype=torch.int32)
     row0 = torch.arange(C, device="cuda", dtype=torch.int32) * 64
-    want = ext.route_topk(scores, query, gists, start, end, clen, row0, k, 64, 640, k * 64, False, 0)
+    want = ext.route_topk(scores, query, gists, start, end, clen, row0, k, 64, 640, k * 64, False, 0, 1)
     world, per = 4, C // 4
     blocks = []
     for r in range(world):
@@ -238,7 +238,7 @@ def test_sharded_routing_merge_equals_unsharded(ext):
         lo = (start - c0).clamp(0, per).to(torch.int32)
         hi = (end - c0).clamp(0, per).to(torch.int32)
         cs, ci = ext.route_topk(scores[:, c0:c1].contiguous(), query, gists[c0:c1].contiguous(), lo, hi, clen, row0, k,
-                                64, -1, 0, True, c0)
+                                64, -1, 0, True, c0, 1)
         blocks.append(torch.cat([cs, ci.view(torch.float32)], dim=1))
     got = ext.route_merge(torch.cat(blocks, dim=1).contiguous(), world, k, 640, clen, row0, k * 64)
     assert torch.equal(got[1], want[1])
@@ -246,3 +246,17 @@ def test_sharded_routing_merge_equals_unsharded(ext):
     for b in range(B):
         n = int(want[1][b])
         assert torch.equal(got[0][b, :n], want[0][b, :n])
+
+
+def test_memory_sweep_fused_step_matches_torch_baseline(ext):
+    from pdattention_b200.inference.memory_sweep import (HEAD_DIM, HEADS, KV_DIM, ShardedLayerMemory,
+                                                         baseline_layer_step, fused_layer_step)
+
+    mem = ShardedLayerMemory(1 << 16, 4, "cuda", seed=1)
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    rq = torch.randn((8, KV_DIM), generator=gen, device="cuda")
+    q = torch.randn((8, HEADS * HEAD_DIM), generator=gen, device="cuda").bfloat16()
+    for k in (4, 16):
+        got = fused_layer_step(mem, rq, q, k).float()
+        want = baseline_layer_step(mem, rq, q, k).float()
+        assert torch.allclose(got, want, atol=3e-2, rtol=3e-2), (k, (got - want).abs().max())
