@@ -629,7 +629,8 @@ std::vector<torch::Tensor> decode_attention(torch::Tensor q, int64_t heads, int6
 std::vector<torch::Tensor> route_topk(torch::Tensor scores, torch::Tensor query, torch::Tensor gists,
                                       torch::Tensor ns_start, torch::Tensor ns_end, torch::Tensor chunk_len,
                                       torch::Tensor chunk_row0, int64_t k, int64_t k_cand, int64_t budget,
-                                      int64_t mem_max, bool local, int64_t id_offset, int64_t gists_per_chunk) {
+                                      int64_t mem_max, bool local, int64_t id_offset, int64_t gists_per_chunk,
+                                      int64_t segments) {
   c10::cuda::CUDAGuard guard(scores.device());
   expect(scores, at::kFloat, "scores");
   expect(query, at::kFloat, "query");
@@ -640,6 +641,8 @@ std::vector<torch::Tensor> route_topk(torch::Tensor scores, torch::Tensor query,
   a.B = scores.size(0);
   a.D = gists.size(-1);
   a.G = gists_per_chunk;
+  a.segments = std::max<int64_t>(segments, 1);
+  TORCH_CHECK(a.segments == 1 || local, "segmented selection writes local candidates (merge them afterwards)");
   a.scores = ptr<const float>(scores);
   a.score_stride = scores.stride(0);
   a.query = ptr<const float>(query);
@@ -653,9 +656,13 @@ std::vector<torch::Tensor> route_topk(torch::Tensor scores, torch::Tensor query,
   a.k_cand = k_cand;
   a.budget = budget;
   auto io = scores.options().dtype(at::kInt);
-  if (local) {  // this rank's best k (exact scores, global ids) for a cross-GPU merge
-    auto cs = torch::empty({a.B, std::max<int64_t>(k, 1)}, scores.options());
-    auto ci = torch::empty({a.B, std::max<int64_t>(k, 1)}, io);
+  if (local) {  // best k per (row, segment) (exact scores, global ids) for a merge
+    if (a.segments > 1) {
+      const int64_t width = scores.size(1) / std::max<int64_t>(gists_per_chunk, 1);
+      a.seg_len = (width + a.segments - 1) / a.segments;
+    }
+    auto cs = torch::empty({a.B * a.segments, std::max<int64_t>(k, 1)}, scores.options());
+    auto ci = torch::empty({a.B * a.segments, std::max<int64_t>(k, 1)}, io);
     a.cand_score = ptr<float>(cs);
     a.cand_id = ptr<int>(ci);
     a.id_offset = id_offset;
@@ -675,7 +682,8 @@ std::vector<torch::Tensor> route_topk(torch::Tensor scores, torch::Tensor query,
 
 // Merge per-rank candidates ([B, world * 2k]: per rank k scores then k ids as int bits).
 std::vector<torch::Tensor> route_merge(torch::Tensor cands, int64_t world, int64_t k, int64_t budget,
-                                       torch::Tensor chunk_len, torch::Tensor chunk_row0, int64_t mem_max) {
+                                       torch::Tensor chunk_len, torch::Tensor chunk_row0, int64_t mem_max,
+                                       bool local) {
   c10::cuda::CUDAGuard guard(cands.device());
   expect(cands, at::kFloat, "cands");
   TORCH_CHECK(cands.dim() == 2 && cands.stride(1) == 1 && cands.size(1) == world * 2 * k, "cands [B, world*2k]");
@@ -689,6 +697,14 @@ std::vector<torch::Tensor> route_merge(torch::Tensor cands, int64_t world, int64
   a.chunk_len = ptr<const int>(chunk_len);
   a.chunk_row0 = ptr<const int>(chunk_row0);
   auto io = cands.options().dtype(at::kInt);
+  if (local) {  // merged best k as candidates (for a further merge across GPUs)
+    auto cs = torch::empty({a.B, std::max<int64_t>(k, 1)}, cands.options());
+    auto ci = torch::empty({a.B, std::max<int64_t>(k, 1)}, io);
+    a.cand_score = ptr<float>(cs);
+    a.cand_id = ptr<int>(ci);
+    check(pra_route_merge(a, stream()), "route_merge");
+    return {cs, ci};
+  }
   auto mem_idx = torch::empty({a.B, std::max<int64_t>(mem_max, 1)}, io);
   auto mem_len = torch::empty({a.B}, io);
   auto sel = torch::empty({a.B, std::max<int64_t>(k, 1)}, io);

@@ -231,9 +231,10 @@ struct RouteTopkArgs {
   int mem_max;
   int* mem_len;                // [B]
   int* sel_out;                // [B, k] selected chunk ids in chunk order (-1 pad), or null
-  float* cand_score;           // local mode: [B, k] best exact scores in rank order (no budget / rows)
-  int* cand_id;                // local mode: [B, k] their chunk ids + id_offset (-1 pad)
+  float* cand_score;           // local mode: [B * segments, k] best exact scores in rank order (no budget / rows)
+  int* cand_id;                // local mode: their chunk ids + id_offset (-1 pad)
   int id_offset;
+  int segments, seg_len;       // > 1: each row's chunks are cut into slices of seg_len, one CTA each (local mode)
 };
 cudaError_t pra_route_topk(const RouteTopkArgs& args, cudaStream_t stream);
 
@@ -249,6 +250,8 @@ struct RouteMergeArgs {
   int mem_max;
   int* mem_len;                // [B]
   int* sel_out;                // [B, k] or null
+  float* cand_score;           // local mode: [B, k] merged best candidates instead of rows (or null)
+  int* cand_id;
 };
 cudaError_t pra_route_merge(const RouteMergeArgs& args, cudaStream_t stream);
 cudaError_t pra_combine_partials(const float* parts, int B, int world, int H, int D, __nv_bfloat16* out,

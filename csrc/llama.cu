@@ -382,10 +382,16 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
   __shared__ int scan_tmp[RT / 32];
   __shared__ int sel_chunk[64], sel_off[65];
   __shared__ int n_sel;
+  // CTA = (query row, segment): with several segments each CTA selects among one slice
+  // of the row's chunks and writes local candidates that a merge pass combines
+  const int S = a.segments > 0 ? a.segments : 1;
   const int b = blockIdx.x;
-  const int c0 = a.ns_start[b], c1 = a.ns_end[b];
+  const int qb = b / S, seg = b % S;
+  const int seg0 = S > 1 ? seg * a.seg_len : 0;
+  const int c0 = S > 1 ? max(a.ns_start[qb], seg0) : a.ns_start[qb];
+  const int c1 = S > 1 ? min(a.ns_end[qb], seg0 + a.seg_len) : a.ns_end[qb];
   const int n = max(c1 - c0, 0);
-  const float* row = a.scores + (int64_t)b * a.score_stride;
+  const float* row = a.scores + (int64_t)qb * a.score_stride;
   const int G = a.G > 0 ? a.G : 1;
   // a chunk's score is the best of its G gists' scores (gist aggregation "max")
   auto chunk_score = [&](int c) -> float {
@@ -420,16 +426,32 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
       if (digit < 256u && lane == __ffs(peers) - 1) atomicAdd(&hist[digit], (uint32_t)__popc(peers));
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      int remaining = need;
-      int digit = 255;
-      for (; digit > 0; --digit) {
-        if ((int)hist[digit] >= remaining) break;
-        remaining -= hist[digit];
+    if (threadIdx.x < 32) {
+      // warp 0 finds the digit holding the need-th largest: lane l owns bins 255-8l .. 248-8l
+      const int ln = threadIdx.x;
+      uint32_t mine = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mine += hist[255 - 8 * ln - j];
+      uint32_t incl = mine;  // inclusive prefix from the top bins down
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (ln >= o) incl += y;
       }
-      prefix |= (uint32_t)digit << shift;
-      prefix_mask |= 255u << shift;
-      need = remaining;
+      const int want = need;
+      const unsigned hit = __ballot_sync(0xffffffffu, (int)incl >= want);
+      const int owner = hit ? __ffs(hit) - 1 : 31;  // the top-down walk always ends by lane 31
+      if (ln == owner) {
+        int remaining = want - (int)(incl - mine);
+        int digit = 255 - 8 * ln;
+        for (int j = 0; j < 7; ++j, --digit) {
+          if ((int)hist[digit] >= remaining) break;
+          remaining -= hist[digit];
+        }
+        prefix |= (uint32_t)digit << shift;
+        prefix_mask |= 255u << shift;
+        need = remaining;
+      }
     }
     __syncthreads();
   }
@@ -464,7 +486,7 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float sq = 0.f;
   for (int d = threadIdx.x; d < a.D; d += RT) {
-    const float v = a.query[(int64_t)b * a.query_stride + d];
+    const float v = a.query[(int64_t)qb * a.query_stride + d];
     sq += v * v;
   }
   sq = warp_sum(sq);
@@ -478,7 +500,7 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
   __syncthreads();
   const float qinv = red[0];
   for (int i = warp; i < nc; i += RT / 32) {
-    const float* q = a.query + (int64_t)b * a.query_stride;
+    const float* q = a.query + (int64_t)qb * a.query_stride;
     float best = -INFINITY;
     for (int gi = 0; gi < G; ++gi) {
       const float* g = a.gists + ((int64_t)cand[i] * G + gi) * a.D;
@@ -522,7 +544,7 @@ __global__ void __launch_bounds__(256) route_merge_kernel(RouteMergeArgs a) {
   __syncthreads();
   const int nc = min(nc_s, MAX_CAND);
   finish_selection(cscore, cand, nc, b, a.k, a.budget, a.chunk_len, a.chunk_row0, a.mem_idx, a.mem_max, a.mem_len,
-                   a.sel_out, nullptr, nullptr, 0, picked, sel_chunk, sel_off, &n_sel);
+                   a.sel_out, a.cand_score, a.cand_id, 0, picked, sel_chunk, sel_off, &n_sel);
 }
 
 // Combine per-rank attention partials: parts [B, world, H, D + 2] (unnormalised out, max,
@@ -613,6 +635,8 @@ cudaError_t pra_route_merge(const RouteMergeArgs& a, cudaStream_t st) {
 cudaError_t pra_route_topk(const RouteTopkArgs& a, cudaStream_t st) {
   if (a.B == 0) return cudaSuccess;
   if (a.k > 64 || a.k_cand > pra::llama::MAX_CAND) return cudaErrorInvalidValue;
-  pra::llama::route_topk_kernel<<<a.B, pra::llama::RT, 0, st>>>(a);
+  const int S = a.segments > 0 ? a.segments : 1;
+  if (S > 1 && (a.cand_score == nullptr || a.seg_len <= 0)) return cudaErrorInvalidValue;  // segments need a merge
+  pra::llama::route_topk_kernel<<<a.B * S, pra::llama::RT, 0, st>>>(a);
   return cudaGetLastError();
 }

@@ -27,6 +27,7 @@ import torch
 
 from ..models.llama import PRALlamaConfig, PRALlamaReference
 from ..ops import _ext
+from .routing import select_chunks
 
 
 # ---------------------------------------------------------------------------
@@ -231,8 +232,8 @@ class PRALlamaEngine:
         if shards == 1:
             scores = torch.empty((rows, mem.C_pad), device=self.device, dtype=torch.float32)
             self.ext.gemm("tn_f32", rqn, mem.gn_bf16[layer], None, scores, None, None, 1.0, 0.0, None)
-            mem_idx, mem_len, sel = self.ext.route_topk(scores, rq, gn, start, end, mem.chunk_len, mem.chunk_row0, k,
-                                                        k_cand, budget, mem_max, False, 0, 1)
+            mem_idx, mem_len, sel = select_chunks(self.ext, scores, rq, gn, start, end, mem.chunk_len,
+                                                  mem.chunk_row0, k, k_cand, budget, mem_max)
         else:
             # chunk-sharded routing: this rank scores its slice of the chunks, keeps its exact
             # local top-k, and the ranks' candidates are all-gathered and merged
@@ -242,12 +243,10 @@ class PRALlamaEngine:
             self.ext.gemm("tn_f32", rqn, mem.gn_bf16[layer][c0:c1], None, scores, None, None, 1.0, 0.0, None)
             lo = (start - c0).clamp(0, width).to(torch.int32)
             hi = (end - c0).clamp(0, width).to(torch.int32)
-            cs, ci = self.ext.route_topk(scores, rq, gn[c0:c1], lo, hi, mem.chunk_len, mem.chunk_row0, k, k_cand, -1,
-                                         0, True, c0, 1)
-            local = torch.cat([cs, ci.view(torch.float32)], dim=1)
-            merged = self.tp.all_gather_columns(local)
-            mem_idx, mem_len, sel = self.ext.route_merge(merged, self.tp.world, k, budget, mem.chunk_len,
-                                                         mem.chunk_row0, mem_max)
+            mem_idx, mem_len, sel = select_chunks(self.ext, scores, rq, gn[c0:c1], lo, hi, mem.chunk_len,
+                                                  mem.chunk_row0, k, k_cand, budget, mem_max, id_offset=c0,
+                                                  comm=self.tp, global_len=mem.chunk_len,
+                                                  global_row0=mem.chunk_row0)
         self.last_selection[layer] = sel
         return mem_idx, mem_len
 

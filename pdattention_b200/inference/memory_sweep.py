@@ -30,6 +30,7 @@ import torch
 import torch.nn.functional as F
 
 from ..ops import _ext
+from .routing import select_chunks
 
 HEADS, KV_HEADS, HEAD_DIM = 28, 4, 128
 KV_DIM = KV_HEADS * HEAD_DIM
@@ -90,14 +91,10 @@ def fused_layer_step(mem: ShardedLayerMemory, rq: torch.Tensor, q: torch.Tensor,
     zeros = torch.zeros(rows, device=rq.device, dtype=torch.int32)
     ends = torch.full((rows,), mem.n, device=rq.device, dtype=torch.int32)
     k_cand = min(max(4 * k, k), 512)
-    if world == 1:
-        mem_idx, mem_len, _ = ext.route_topk(scores, rq, mem.gn, zeros, ends, mem.chunk_len, mem.local_row0, k, k_cand,
-                                             -1, k * CHUNK, False, 0, mem.G)
-    else:
-        cs, ci = ext.route_topk(scores, rq, mem.gn, zeros, ends, mem.chunk_len, mem.local_row0, k, k_cand, -1, 0,
-                                True, mem.c0, mem.G)
-        merged = comm.all_gather_columns(torch.cat([cs, ci.view(torch.float32)], dim=1))
-        mem_idx, mem_len, _ = ext.route_merge(merged, world, k, -1, mem.chunk_len, mem.chunk_row0, k * CHUNK)
+    mem_idx, mem_len, _ = select_chunks(ext, scores, rq, mem.gn, zeros, ends, mem.chunk_len, mem.local_row0, k,
+                                        k_cand, -1, k * CHUNK, gists_per_chunk=mem.G, id_offset=mem.c0,
+                                        comm=comm if world > 1 else None, global_len=mem.chunk_len,
+                                        global_row0=mem.chunk_row0)
     mark("routed")
     pool_k, pool_v = mem.pool[:, :KV_DIM], mem.pool[:, KV_DIM:]
     res = ext.decode_attention(q, HEADS, KV_HEADS, HEAD_DIM, pool_k, pool_v, mem_idx, mem_len, None, None, None,

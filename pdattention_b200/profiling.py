@@ -160,7 +160,22 @@ def decode_table_tp(memory_chunks: int = 16384) -> None:
     dist.destroy_process_group()
 
 
-CASES = {"train-small": train_small, "decode-small": decode_small, "train-table": train_table,
+def sweep_table(tokens: int = 1 << 24, gists: int = 1, k: int = 16) -> None:
+    """Kernel table of one fused layer step of the memory sweep (one GPU, 16M-token memory)."""
+    from .inference.memory_sweep import HEAD_DIM, HEADS, KV_DIM, ShardedLayerMemory, fused_layer_step
+
+    dev = torch.device("cuda", 0)
+    mem = ShardedLayerMemory(tokens, gists, dev)
+    gen = torch.Generator(device=dev).manual_seed(3)
+    rq = torch.randn((64, KV_DIM), generator=gen, device=dev)
+    q = torch.randn((64, HEADS * HEAD_DIM), generator=gen, device=dev).to(torch.bfloat16)
+    for _ in range(3):
+        fused_layer_step(mem, rq, q, k)
+    torch.cuda.synchronize()
+    _table(lambda: fused_layer_step(mem, rq, q, k), rows=15)
+
+
+CASES = {"sweep-table": sweep_table, "train-small": train_small, "decode-small": decode_small, "train-table": train_table,
          "decode-table": decode_table, "decode-table-tp": decode_table_tp}
 
 

@@ -83,7 +83,7 @@ def test_route_topk_exact_with_ties(ext):
     clen = torch.full((C + 8,), 8, device="cuda", dtype=torch.int32)
     clen[::7] = 5
     row0 = torch.arange(C + 8, device="cuda", dtype=torch.int32) * 8
-    mem_idx, mem_len, sel = ext.route_topk(approx, query, gists, start, end, clen, row0, k, 64, -1, k * 8, False, 0, 1)
+    mem_idx, mem_len, sel = ext.route_topk(approx, query, gists, start, end, clen, row0, k, 64, -1, k * 8, False, 0, 1, 1)
     exact = F.normalize(query, dim=-1) @ gists.t()
     for b in range(B):
         ids = list(range(int(start[b]), int(end[b])))
@@ -96,7 +96,7 @@ def test_route_topk_exact_with_ties(ext):
         assert mem_idx[b, : len(rows)].tolist() == rows
     assert 3 in [int(c) for c in sel[0]] and 10 in [int(c) for c in sel[0]]
     # a token budget keeps whole chunks greedily in score order
-    mem_idx, mem_len, sel = ext.route_topk(approx, query, gists, start, end, clen, row0, k, 64, 20, k * 8, False, 0, 1)
+    mem_idx, mem_len, sel = ext.route_topk(approx, query, gists, start, end, clen, row0, k, 64, 20, k * 8, False, 0, 1, 1)
     assert int(mem_len.max()) <= 20
 
 
@@ -230,7 +230,7 @@ def test_sharded_routing_merge_equals_unsharded(ext):
     end = torch.tensor([C, 200, 700, 420, C, C], device="cuda", dtype=torch.int32)
     clen = torch.full((C,), 64, device="cuda", dtype=torch.int32)
     row0 = torch.arange(C, device="cuda", dtype=torch.int32) * 64
-    want = ext.route_topk(scores, query, gists, start, end, clen, row0, k, 64, 640, k * 64, False, 0, 1)
+    want = ext.route_topk(scores, query, gists, start, end, clen, row0, k, 64, 640, k * 64, False, 0, 1, 1)
     world, per = 4, C // 4
     blocks = []
     for r in range(world):
@@ -238,9 +238,9 @@ def test_sharded_routing_merge_equals_unsharded(ext):
         lo = (start - c0).clamp(0, per).to(torch.int32)
         hi = (end - c0).clamp(0, per).to(torch.int32)
         cs, ci = ext.route_topk(scores[:, c0:c1].contiguous(), query, gists[c0:c1].contiguous(), lo, hi, clen, row0, k,
-                                64, -1, 0, True, c0, 1)
+                                64, -1, 0, True, c0, 1, 1)
         blocks.append(torch.cat([cs, ci.view(torch.float32)], dim=1))
-    got = ext.route_merge(torch.cat(blocks, dim=1).contiguous(), world, k, 640, clen, row0, k * 64)
+    got = ext.route_merge(torch.cat(blocks, dim=1).contiguous(), world, k, 640, clen, row0, k * 64, False)
     assert torch.equal(got[1], want[1])
     assert torch.equal(got[2], want[2])
     for b in range(B):
@@ -260,3 +260,25 @@ def test_memory_sweep_fused_step_matches_torch_baseline(ext):
         got = fused_layer_step(mem, rq, q, k).float()
         want = baseline_layer_step(mem, rq, q, k).float()
         assert torch.allclose(got, want, atol=3e-2, rtol=3e-2), (k, (got - want).abs().max())
+
+
+def test_segmented_selection_equals_single_pass(ext, monkeypatch):
+    """Rows cut into segments (one CTA each) + on-GPU merge == one CTA per row."""
+    from pdattention_b200.inference import routing
+
+    torch.manual_seed(6)
+    B, C, D, k = 5, 3000, 64, 8
+    for G in (1, 4):
+        gists = F.normalize(torch.randn(C * G, D, device="cuda"), dim=-1)
+        query = torch.randn(B, D, device="cuda")
+        scores = (F.normalize(query, dim=-1).bfloat16().float() @ gists.bfloat16().float().t()).contiguous()
+        start = torch.tensor([0, 100, 0, 2500, 7], device="cuda", dtype=torch.int32)
+        end = torch.tensor([C, 2900, 1000, C, 8], device="cuda", dtype=torch.int32)
+        clen = torch.full((C,), 16, device="cuda", dtype=torch.int32)
+        row0 = torch.arange(C, device="cuda", dtype=torch.int32) * 16
+        want = ext.route_topk(scores, query, gists, start, end, clen, row0, k, 32, 100, k * 16, False, 0, G, 1)
+        monkeypatch.setattr(routing, "SEGMENT", 256)
+        got = routing.select_chunks(ext, scores, query, gists, start, end, clen, row0, k, 32, 100, k * 16,
+                                    gists_per_chunk=G)
+        monkeypatch.setattr(routing, "SEGMENT", 8192)
+        assert torch.equal(got[1], want[1]) and torch.equal(got[2], want[2]), (G, got[2], want[2])
