@@ -272,6 +272,7 @@ __global__ void decode_merge_kernel(DecodeAttnParams p, int D) {
 // ---------------------------------------------------------------- routing top-k
 constexpr int RT = 1024;
 constexpr int MAX_CAND = 512;
+constexpr int STAGE_N = 8192;  // chunk scores of one segment staged in shared memory
 
 __device__ __forceinline__ uint32_t order_key(float f) {
   const uint32_t u = __float_as_uint(f);
@@ -380,6 +381,7 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
   __shared__ int picked[MAX_CAND];
   __shared__ float red[32];
   __shared__ int scan_tmp[RT / 32];
+  __shared__ float seg_scores[STAGE_N];
   __shared__ int sel_chunk[64], sel_off[65];
   __shared__ int n_sel;
   // CTA = (query row, segment): with several segments each CTA selects among one slice
@@ -400,6 +402,12 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
     for (int g = 1; g < G; ++g) m = fmaxf(m, row[(int64_t)c * G + g]);
     return m;
   };
+  // the segment's chunk scores are staged in shared memory once: every radix pass and the
+  // candidate scans then read on-chip data (rows longer than STAGE_N read global memory)
+  const bool staged = n <= STAGE_N;
+  if (staged)
+    for (int i = threadIdx.x; i < n; i += RT) seg_scores[i] = chunk_score(c0 + i);
+  auto score_at = [&](int i) -> float { return staged ? seg_scores[i] : chunk_score(c0 + i); };
   const int kc = min(a.k_cand, min(n, MAX_CAND));
   if (threadIdx.x == 0) {
     prefix = 0;
@@ -419,7 +427,7 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
       const int i = base + lane;
       uint32_t digit = 256u;  // "no digit" for lanes past the end or outside the prefix
       if (i < n) {
-        const uint32_t key = order_key(chunk_score(c0 + i));
+        const uint32_t key = order_key(score_at(i));
         if ((key & prefix_mask) == prefix) digit = (key >> shift) & 255u;
       }
       const unsigned peers = __match_any_sync(0xffffffffu, digit);
@@ -458,7 +466,7 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
   // 2. candidates: every chunk strictly above the threshold, then ties at it (lowest ids first)
   const uint32_t thr = prefix;
   for (int i = threadIdx.x; i < n && kc > 0; i += RT) {
-    if (order_key(chunk_score(c0 + i)) > thr) {
+    if (order_key(score_at(i)) > thr) {
       const int slot = atomicAdd(&n_cand, 1);
       if (slot < MAX_CAND) cand[slot] = c0 + i;
     }
@@ -470,13 +478,13 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
     const int seg = (n + RT - 1) / RT;
     const int s0 = min(n, threadIdx.x * seg), s1 = min(n, s0 + seg);
     int mine = 0;
-    for (int i = s0; i < s1 && kc > 0; ++i) mine += order_key(chunk_score(c0 + i)) == thr ? 1 : 0;
+    for (int i = s0; i < s1 && kc > 0; ++i) mine += order_key(score_at(i)) == thr ? 1 : 0;
     int total = 0;
     const int before = block_scan_int(mine, scan_tmp, &total);
     const int want = kc - above;
     int slot = above + before;
     for (int i = s0; i < s1 && kc > 0 && slot < above + want; ++i)
-      if (order_key(chunk_score(c0 + i)) == thr) cand[slot++] = c0 + i;
+      if (order_key(score_at(i)) == thr) cand[slot++] = c0 + i;
     __syncthreads();
     if (threadIdx.x == 0) n_cand = kc > 0 ? above + min(want, total) : 0;
     __syncthreads();
