@@ -143,3 +143,29 @@ def test_flat_grad_rehome_keeps_views_aliased():
     views[0].fill_(3)
     start = flat.offsets["blocks.0.attn.o_proj.weight"]
     assert float(new[start]) == 3.0
+
+
+def test_standalone_entry_points_train_and_eval(data_root):
+    """``python -m pdattention_b200.standalone train|eval`` with a YAML like the packaged one."""
+    import yaml
+
+    from pdattention_b200.standalone import build_trainer, main
+
+    cfg = {"model": {"d_model": 32, "n_heads": 4, "n_layers": 2},
+           "pra": {"pra_layer_ids": [0, 1], "trigger_threshold": 0.0},
+           "standalone": {"experiment_name": "sa", "output_dir": str(data_root / "out"), "device": "cpu",
+                          "epochs": 1, "batch_size": 2, "eval_every_steps": 2, "save_every_steps": 2,
+                          "log_every_steps": 1, "use_tensorboard": False, "save_metric_plots": False,
+                          "max_examples": 4, "max_seq_len": 64, "dataset_stage": "stage0_synthetic_memory",
+                          "data_dir": str(data_root / "data")}}
+    path = data_root / "sa.yml"
+    path.write_text(yaml.safe_dump(cfg))
+    trainer = build_trainer(str(path), model_name="default")
+    assert trainer.model.cfg.d_model == 32 and trainer.model.cfg.pra_layer_ids == (0, 1)
+    main(["train", "--config", str(path), "--model", "default"])
+    ckpt = data_root / "out" / "sa" / "checkpoints" / "latest.pt"
+    assert ckpt.exists()
+    traces = data_root / "sa_traces.jsonl"
+    main(["eval", "--config", str(path), "--model", "default", "--checkpoint", str(ckpt),
+          "--traces-jsonl", str(traces)])
+    assert traces.read_text().strip()
