@@ -394,6 +394,50 @@ def run_decode(impl: str, steps: int, warmup: int, gpus: int, memory_tokens: int
     return result
 
 
+def run_long_prompt(impl: str, steps: int, gpus: int, prompt_tokens: int | None) -> dict:
+    """Mistral-7B-architecture PRA model, batch 16: 128K-token prompts whose latest 4,096 tokens stay
+    direct and the rest become implicit-head chunks, then greedy decode (tensor parallel)."""
+    if impl == "reference":
+        return {"impl": "reference", "unavailable": "the reference has no Llama/Mistral-family PRA model, no "
+                                                   "tensor parallelism and no device path for 7B long prompts"}
+    rank, local, world = _env()
+    torch.cuda.set_device(local)
+    tp = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        from pdattention_b200.parallel.tp import TensorParallel
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        tp = TensorParallel()
+    from pdattention_b200.inference.long_prompt import run_long_prompt_benchmark
+
+    clocks = ClockSampler(local)
+    out = run_long_prompt_benchmark(prompt_tokens=prompt_tokens or (1 << 17 if world > 1 else 1 << 15),
+                                    new_tokens=max(steps, 16), tp=tp, clocks=clocks)
+    result = {"metric": "PRA long-prompt decode tokens/s (Mistral-7B architecture, implicit head)",
+              "value": out["decode_tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": out["decode_steps"],
+              "warmup": 1, "ms_per_step": out["tpot_p50_ms"], "higher_is_better": True, "scaling": "strong",
+              "vs_baseline": None, "dtype": "bf16",
+              "data": "synthetic (uniform-random prompt token ids), random-init weights",
+              "config": {k: out[k] for k in ("model", "batch", "prompt_tokens", "direct_window", "head_tokens",
+                                             "new_tokens", "memory_gb_per_gpu", "position_offset")},
+              "prefill_tokens_per_s": out["prefill_tokens_per_s"],
+              "head_build_tokens_per_s": out["head_build_tokens_per_s"],
+              "tail_prefill_tokens_per_s": out["tail_prefill_tokens_per_s"], "clocks": clocks.summary()}
+    result["config"]["parallelism"] = f"tp{world}"
+    if tp is not None:
+        tp.close()
+        import torch.distributed as dist
+
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return result
+
+
 def run_memory_sweep(gpus: int, impl: str, steps: int, warmup: int):
     """Routing + memory-attention sweep of one Qwen2-7B-shaped PRA layer, memory sharded by chunk
     over the GPUs: 64K / 1M / 16M tokens x G in {1, 4} x chunk top-k in {4, 16, 64}.  One JSON
@@ -442,15 +486,22 @@ def main() -> None:
     parser.add_argument("--steps", type=int, default=10)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["pra", "reference"], default="pra")
-    parser.add_argument("--workload", choices=["train", "decode", "memory-sweep"], default="train",
+    parser.add_argument("--workload", choices=["train", "decode", "memory-sweep", "long-prompt"], default="train",
                         help="train: TinyGPT-PRA data-parallel training (default); decode: PRA Llama-3-8B decode "
                              "with a chunk memory (tensor parallel over the GPUs)")
     parser.add_argument("--memory-tokens", type=int, default=None,
                         help="decode: total memory tokens (default 1M; 256K on one GPU, whose HBM cannot hold the "
                              "1M-token K/V of all 32 layers next to the weights and caches)")
     parser.add_argument("--batch", type=int, default=64)
+    parser.add_argument("--prompt-tokens", type=int, default=None,
+                        help="long-prompt: tokens per prompt (default 128K; 32K on one GPU)")
     args = parser.parse_args()
     rank = _env()[0]
+    if args.workload == "long-prompt":
+        result = run_long_prompt(args.impl, args.steps, args.gpus, args.prompt_tokens)
+        if rank == 0:
+            print(json.dumps(result))
+        return
     if args.workload == "memory-sweep":
         for line in run_memory_sweep(args.gpus, args.impl, args.steps, max(args.warmup, 3)):
             if rank == 0:

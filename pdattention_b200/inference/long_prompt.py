@@ -83,3 +83,74 @@ def long_prompt_generate(engine, prompts: list[list[int]], max_new_tokens: int, 
     for _ in range(max_new_tokens - 1):
         out.append(engine.decode_step(out[-1]).float().argmax(-1))
     return torch.stack(out, dim=1), plan, first
+
+
+def run_long_prompt_benchmark(*, model: str = "mistral-7b", batch: int = 16, prompt_tokens: int = 131072,
+                              direct_window: int = 4096, new_tokens: int = 256, tp=None, seed: int = 0,
+                              clocks=None) -> dict:
+    """Long-prompt workload: ``batch`` prompts of ``prompt_tokens`` uniform-random ids; the latest
+    ``direct_window`` tokens stay direct, the rest become each row's implicit head chunks
+    (64 tokens, one mean gist each).  Times the head build, the tail prefill and
+    ``new_tokens`` greedy decode steps (CUDA-graph replays after one eager step); device
+    time with CUDA events, max over ranks."""
+    import statistics
+    import time
+
+    from ..models.llama import PRESETS
+    from .llama_engine import LlamaWeights, PRALlamaEngine
+
+    rank = tp.rank if tp is not None else 0
+    world = tp.world if tp is not None else 1
+    device = torch.device("cuda", torch.cuda.current_device())
+    cfg = PRESETS[model](chunk_tokens=64, top_k_chunks=16, direct_window=direct_window)
+    engine = PRALlamaEngine(LlamaWeights.random(cfg, device, seed=seed, tp_rank=rank, tp_size=world), device, tp=tp)
+    gen = torch.Generator().manual_seed(seed + 1)
+    prompts = torch.randint(0, cfg.vocab_size, (batch, prompt_tokens), generator=gen).tolist()
+    plan = plan_long_prompts(prompts, direct_window, cfg.chunk_tokens, cfg.max_position_embeddings)
+
+    def timed(fn):
+        if tp is not None:
+            tp.barrier()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        out = fn()
+        end.record()
+        torch.cuda.synchronize()
+        ms = start.elapsed_time(end)
+        return out, (tp.max_scalar(ms) if tp is not None else ms)
+
+    _, build_ms = timed(lambda: engine.build_memory(plan.chunks, plan.chunk_lengths, batch_chunks=256))
+    engine.set_namespace(plan.ns_start, plan.ns_end)
+    first, prefill_ms = timed(lambda: engine.prefill(plan.tails, plan.tail_lengths, new_tokens + 1, row_batch=4,
+                                                     position_offset=plan.position_offset))
+    tok = first.float().argmax(-1)
+    tok = engine.decode_step(tok).float().argmax(-1)  # one eager step, then the captured graph
+    engine.capture_decode()
+    steps = []
+    if clocks is not None:
+        clocks.__enter__()
+    for _ in range(new_tokens - 1):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        tok = engine.decode_step_graphed(tok).float().argmax(-1)
+        e.record()
+        steps.append((s, e))
+    torch.cuda.synchronize()
+    if clocks is not None:
+        clocks.__exit__(None, None, None)
+    per_step = [a.elapsed_time(b) for a, b in steps]
+    if tp is not None:
+        per_step = [tp.max_scalar(x) for x in per_step]
+    engine.release_graph()
+    decode_s = sum(per_step) / 1000
+    head_tokens = int(plan.chunk_lengths.sum())
+    return {"prefill_tokens_per_s": batch * prompt_tokens / ((build_ms + prefill_ms) / 1000),
+            "head_build_tokens_per_s": head_tokens / (build_ms / 1000),
+            "tail_prefill_tokens_per_s": int(plan.tail_lengths.sum()) / (prefill_ms / 1000),
+            "decode_tokens_per_s": batch * len(per_step) / decode_s,
+            "tpot_p50_ms": statistics.median(per_step), "head_tokens": head_tokens,
+            "memory_gb_per_gpu": engine.memory.nbytes() / 1e9, "batch": batch, "prompt_tokens": prompt_tokens,
+            "direct_window": direct_window, "new_tokens": new_tokens, "tp": world, "model": model,
+            "params_b": cfg.parameter_count() / 1e9, "decode_steps": len(per_step),
+            "position_offset": int(plan.position_offset[0])}
