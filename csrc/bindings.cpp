@@ -176,7 +176,9 @@ void gemm(const std::string& kind, torch::Tensor A, torch::Tensor B, c10::option
   if (C.has_value()) TORCH_CHECK(C->is_contiguous() && C->sizes() == D.sizes(), "C must match D");
   if (g.beta != 0.f) TORCH_CHECK(g.C != nullptr, "beta != 0 needs C");
   cudaError_t e;
-  if (kind == "tn") e = g.M <= 128 ? pra_gemm_tn_bias_small(g, stream()) : pra_gemm_tn_bias(g, stream());
+  if (kind == "tn")
+    e = g.M <= 128 ? pra_gemm_tn_bias_small(g, stream())
+                   : (g.N <= 1024 ? pra_gemm_tn_bias_narrow(g, stream()) : pra_gemm_tn_bias(g, stream()));
   else if (kind == "tn_f32") e = pra_gemm_tn_f32(g, stream());
   else if (kind == "tn_gelu") e = pra_gemm_tn_bias_gelu(g, stream());
   else if (kind == "nn") e = pra_gemm_nn(g, stream());

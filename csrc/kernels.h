@@ -50,6 +50,7 @@ struct GemmArgs {
 cudaError_t pra_gemm_tn_bias(const GemmArgs& g, cudaStream_t stream);
 cudaError_t pra_gemm_tn_f32(const GemmArgs& g, cudaStream_t stream);  // fp32 D, no bias / C
 cudaError_t pra_gemm_tn_bias_small(const GemmArgs& g, cudaStream_t stream);  // M <= 128, stream-K
+cudaError_t pra_gemm_tn_bias_narrow(const GemmArgs& g, cudaStream_t stream);  // N <= 1024, 128x128 tiles
 cudaError_t pra_gemm_tn_bias_gelu(const GemmArgs& g, cudaStream_t stream);
 cudaError_t pra_gemm_nn(const GemmArgs& g, cudaStream_t stream);
 cudaError_t pra_gemm_nn_dgelu(const GemmArgs& g, cudaStream_t stream);
