@@ -56,6 +56,166 @@ __global__ void __launch_bounds__(NT) fwd_kernel(const __nv_bfloat16* __restrict
   }
 }
 
+// Warp-per-row variants for D <= 1024 (every TinyGPT width): 16-byte loads, shuffle-only
+// reductions, 8 rows per 256-thread CTA.  Lane l owns the 8-element chunks l, l + 32, ...
+constexpr int WCH = 4;  // chunks of 8 per lane: D <= 32 * 8 * WCH = 1024
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float* f) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 v = __bfloat1622float2(h[i]);
+    f[2 * i] = v.x;
+    f[2 * i + 1] = v.y;
+  }
+}
+
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float* f) {
+  uint4 raw;
+  uint32_t* r = reinterpret_cast<uint32_t*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) r[i] = pack_bf16(f[2 * i], f[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = raw;
+}
+
+template <bool RMS>
+__global__ void __launch_bounds__(256) fwd_warp_kernel(const __nv_bfloat16* __restrict__ x,
+                                                       const __nv_bfloat16* __restrict__ w,
+                                                       const __nv_bfloat16* __restrict__ b, __nv_bfloat16* __restrict__ y,
+                                                       float* __restrict__ mean_out, float* __restrict__ rstd_out,
+                                                       int M, int D, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const int C = D / 8;
+  const __nv_bfloat16* xr = x + (int64_t)row * D;
+  float v[WCH][8];
+  float s = 0.f, ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < WCH; ++j) {
+    const int c = lane + 32 * j;
+    if (c < C) {
+      load8(xr + 8 * c, v[j]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        s += v[j][e];
+        ss += v[j][e] * v[j][e];
+      }
+    }
+  }
+  float mean = 0.f, var;
+  if (RMS) {
+    var = warp_sum(ss) / D;
+  } else {
+    mean = warp_sum(s) / D;
+    float dev = 0.f;
+#pragma unroll
+    for (int j = 0; j < WCH; ++j)
+      if (lane + 32 * j < C)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dev += (v[j][e] - mean) * (v[j][e] - mean);
+    var = warp_sum(dev) / D;
+  }
+  const float rstd = rsqrtf(var + eps);
+#pragma unroll
+  for (int j = 0; j < WCH; ++j) {
+    const int c = lane + 32 * j;
+    if (c < C) {
+      float wv[8], bv[8], o[8];
+      load8(w + 8 * c, wv);
+      if (b) load8(b + 8 * c, bv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = (v[j][e] - mean) * rstd * wv[e] + (b ? bv[e] : 0.f);
+      store8(y + (int64_t)row * D + 8 * c, o);
+    }
+  }
+  if (lane == 0) {
+    if (mean_out) mean_out[row] = mean;
+    rstd_out[row] = rstd;
+  }
+}
+
+// Backward, warp per row; each warp keeps its columns' dw/db sums in registers, the CTA
+// combines its 8 warps in a fixed order (deterministic) and writes one partial row.
+template <bool RMS>
+__global__ void __launch_bounds__(256) bwd_warp_kernel(const __nv_bfloat16* __restrict__ dy,
+                                                       const __nv_bfloat16* __restrict__ x,
+                                                       const __nv_bfloat16* __restrict__ w,
+                                                       const float* __restrict__ mean_in,
+                                                       const float* __restrict__ rstd_in,
+                                                       const __nv_bfloat16* __restrict__ dres,
+                                                       __nv_bfloat16* __restrict__ dx, float* __restrict__ dw_part,
+                                                       float* __restrict__ db_part, int M, int D, int rows_per_cta) {
+  extern __shared__ float red[];  // [8][2][D]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int C = D / 8;
+  float aw[WCH][8], ab[WCH][8];
+#pragma unroll
+  for (int j = 0; j < WCH; ++j)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) aw[j][e] = ab[j][e] = 0.f;
+  const int r0 = blockIdx.x * rows_per_cta, r1 = min(r0 + rows_per_cta, M);
+  for (int row = r0 + warp; row < r1; row += 8) {
+    const float mean = RMS ? 0.f : mean_in[row];
+    const float rstd = rstd_in[row];
+    float xh[WCH][8], wg[WCH][8];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < WCH; ++j) {
+      const int c = lane + 32 * j;
+      if (c < C) {
+        float xv[8], gv[8], wv[8];
+        load8(x + (int64_t)row * D + 8 * c, xv);
+        load8(dy + (int64_t)row * D + 8 * c, gv);
+        load8(w + 8 * c, wv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          xh[j][e] = (xv[e] - mean) * rstd;
+          wg[j][e] = gv[e] * wv[e];
+          s1 += wg[j][e];
+          s2 += wg[j][e] * xh[j][e];
+          aw[j][e] += gv[e] * xh[j][e];
+          ab[j][e] += gv[e];
+        }
+      }
+    }
+    const float m1 = RMS ? 0.f : warp_sum(s1) / D;
+    const float m2 = warp_sum(s2) / D;
+#pragma unroll
+    for (int j = 0; j < WCH; ++j) {
+      const int c = lane + 32 * j;
+      if (c < C) {
+        float o[8], rv[8];
+        if (dres) load8(dres + (int64_t)row * D + 8 * c, rv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = rstd * (wg[j][e] - m1 - xh[j][e] * m2) + (dres ? rv[e] : 0.f);
+        store8(dx + (int64_t)row * D + 8 * c, o);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < WCH; ++j) {
+    const int c = lane + 32 * j;
+    if (c < C)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        red[(warp * 2) * D + 8 * c + e] = aw[j][e];
+        red[(warp * 2 + 1) * D + 8 * c + e] = ab[j][e];
+      }
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float sw = 0.f, sb = 0.f;
+    for (int q = 0; q < 8; ++q) {
+      sw += red[(q * 2) * D + d];
+      sb += red[(q * 2 + 1) * D + d];
+    }
+    dw_part[(int64_t)blockIdx.x * D + d] = sw;
+    if (db_part) db_part[(int64_t)blockIdx.x * D + d] = sb;
+  }
+}
+
 // Each CTA handles `rows_per_cta` rows; writes fp32 partial dw/db [gridDim.x, D].
 template <bool RMS>
 __global__ void __launch_bounds__(NT) bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
@@ -137,6 +297,12 @@ cudaError_t pra_norm_fwd(const __nv_bfloat16* x, const __nv_bfloat16* w, const _
   using namespace pra::norm;
   if (D % 2 || D / 2 > NT * MAXV) return cudaErrorInvalidValue;
   if (M == 0) return cudaSuccess;
+  if (D % 8 == 0 && D <= 32 * 8 * WCH) {
+    const int blocks = (M + 7) / 8;
+    if (rms) fwd_warp_kernel<true><<<blocks, 256, 0, st>>>(x, w, nullptr, y, nullptr, rstd, M, D, eps);
+    else fwd_warp_kernel<false><<<blocks, 256, 0, st>>>(x, w, b, y, mean, rstd, M, D, eps);
+    return cudaGetLastError();
+  }
   if (rms) fwd_kernel<true><<<M, NT, 0, st>>>(x, w, nullptr, y, nullptr, rstd, M, D, eps);
   else fwd_kernel<false><<<M, NT, 0, st>>>(x, w, b, y, mean, rstd, M, D, eps);
   return cudaGetLastError();
@@ -152,8 +318,22 @@ cudaError_t pra_norm_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, const 
   if (D % 2 || D / 2 > NT * MAXV) return cudaErrorInvalidValue;
   const int parts = pra_norm_bwd_partials(M);
   const int rows = M == 0 ? 0 : (M + parts - 1) / parts;
-  if (rms) bwd_kernel<true><<<parts, NT, 0, st>>>(dy, x, w, nullptr, rstd, dres, dx, dw_part, nullptr, M, D, rows);
-  else bwd_kernel<false><<<parts, NT, 0, st>>>(dy, x, w, mean, rstd, dres, dx, dw_part, db_part, M, D, rows);
+  if (D % 8 == 0 && D <= 32 * 8 * WCH) {
+    const size_t smem = (size_t)16 * D * sizeof(float);
+    if (rms) {
+      PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(bwd_warp_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)smem));
+      bwd_warp_kernel<true><<<parts, 256, smem, st>>>(dy, x, w, nullptr, rstd, dres, dx, dw_part, nullptr, M, D, rows);
+    } else {
+      PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(bwd_warp_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)smem));
+      bwd_warp_kernel<false><<<parts, 256, smem, st>>>(dy, x, w, mean, rstd, dres, dx, dw_part, db_part, M, D, rows);
+    }
+  } else if (rms) {
+    bwd_kernel<true><<<parts, NT, 0, st>>>(dy, x, w, nullptr, rstd, dres, dx, dw_part, nullptr, M, D, rows);
+  } else {
+    bwd_kernel<false><<<parts, NT, 0, st>>>(dy, x, w, mean, rstd, dres, dx, dw_part, db_part, M, D, rows);
+  }
   PRA_RETURN_IF_ERROR(cudaGetLastError());
   column_reduce_kernel<__nv_bfloat16><<<(D + 255) / 256, 256, 0, st>>>(dw_part, parts, D, dw);
   if (!rms && db) column_reduce_kernel<__nv_bfloat16><<<(D + 255) / 256, 256, 0, st>>>(db_part, parts, D, db);
