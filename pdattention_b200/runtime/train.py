@@ -105,11 +105,21 @@ def create_training_state(model, train_config, *, optimizer=None, scheduler=None
     seed_everything(train_config.seed)
     device = resolve_device(train_config.device)
     model.to(device)
+    broadcast_parameters(model)  # data parallel: every rank starts from rank 0's weights
+    sync = getattr(model, "after_load_state", None)
+    if sync is not None:
+        sync()
     build_optimizer = getattr(model, "build_optimizer", None)
     if optimizer is None:
         optimizer = (build_optimizer(train_config) if build_optimizer is not None else
                      torch.optim.AdamW(model.parameters(), lr=train_config.learning_rate,
                                        weight_decay=train_config.weight_decay))
+        world = torch.distributed.get_world_size() if (torch.distributed.is_available() and
+                                                       torch.distributed.is_initialized()) else 1
+        if world > 1 and getattr(model, "_device_runtime", None) is not None:
+            from ..parallel.dp import attach_data_parallel
+
+            attach_data_parallel(model, optimizer, world)  # fused peer-memory gradient average
     if scheduler is None:
         scheduler = torch.optim.lr_scheduler.LambdaLR(optimizer, warmup_lambda(train_config.warmup_steps))
     run_dir = Path(train_config.output_dir) / train_config.experiment_name
@@ -201,8 +211,40 @@ def _validation_checkpoint(state: TrainingState, metrics: dict, epoch: int) -> b
     return state.early_stopping.update(val_loss)
 
 
+def average_gradients(model) -> None:
+    """Data parallel: every rank's gradients become the mean over ranks (one flat all-reduce;
+    gloo on CPU, NCCL on GPU).  No-op outside a process group."""
+    if not (torch.distributed.is_available() and torch.distributed.is_initialized()):
+        return
+    world = torch.distributed.get_world_size()
+    if world <= 1:
+        return
+    grads = [p.grad for p in model.parameters() if p.grad is not None]
+    if not grads:
+        return
+    flat = torch.cat([g.reshape(-1).float() for g in grads])
+    torch.distributed.all_reduce(flat, op=torch.distributed.ReduceOp.SUM)
+    flat /= world
+    offset = 0
+    for g in grads:
+        g.copy_(flat[offset: offset + g.numel()].view_as(g))
+        offset += g.numel()
+
+
+def broadcast_parameters(model, src: int = 0) -> None:
+    """Start every data-parallel rank from rank ``src``'s parameters."""
+    if not (torch.distributed.is_available() and torch.distributed.is_initialized()):
+        return
+    if torch.distributed.get_world_size() <= 1:
+        return
+    with torch.no_grad():
+        for p in model.parameters():
+            torch.distributed.broadcast(p.data, src=src)
+
+
 def _stock_optimizer_step(state: TrainingState, model, train_config) -> float:
     optimizer = state.optimizer
+    average_gradients(model)
     if state.scaler is not None:
         state.scaler.unscale_(optimizer)
     norm = grad_norm(model.parameters())
