@@ -529,9 +529,19 @@ cudaError_t launch_bwd(const Params& p, cudaStream_t st) {
 }  // namespace pra
 
 // ---------------------------------------------------------------------------
+static int g_attn_tcgen05 = 1;
+void pra_attention_set_impl(int tcgen05) { g_attn_tcgen05 = tcgen05; }
+int pra_attention_get_impl() { return g_attn_tcgen05; }
+
 cudaError_t pra_attention_fwd(const AttnParams& p, int head_dim, cudaStream_t st) {
   using namespace pra::attn;
   if (p.B * p.T == 0) return cudaSuccess;
+  // The tcgen05 kernel works on 128-query tiles; sequences of <= 64 tokens (chunk encodes)
+  // keep the 64-query mma.sync tiles, which waste no rows there.
+  if (g_attn_tcgen05 && p.T > 64) {
+    const cudaError_t e = pra_attention_fwd_tc(p, head_dim, st);
+    if (e != cudaErrorNotSupported) return e;
+  }
   switch (head_dim) {
     case 32: return launch_fwd<32>(p, st);
     case 64: return launch_fwd<64>(p, st);

@@ -1,0 +1,419 @@
+// Ragged native-K/V attention forward on the 5th-generation tensor cores (tcgen05, TMEM).
+//
+// Same operation and outputs as the mma.sync forward in attention.cu: one softmax over
+//   [ selected memory keys (gathered from a token pool through mem_idx, fully visible) ;
+//     local keys (causal, optional key-padding mask) ]
+// writing O (bf16) and the natural-log LSE per query row.
+//
+// One CTA of 256 threads owns a tile of 128 queries of one (batch row, head); query row r is
+// TMEM lane r of both accumulators and is owned by two threads (warps w and w + 4 may both
+// access lanes 32 (w % 4) ... + 31), each taking half of the S and O columns:
+//   S = Q K^T    (M=128, N=BN, K=D)   -> TMEM columns [0, BN)
+//   O += P V     (M=128, N=D,  K=BN)  -> TMEM columns [BN, BN + D)
+// Thread 0 issues the MMAs and commits them to one mbarrier; all threads stage K/V with
+// cp.async (memory keys are gathered row by row, which a tiled TMA box cannot express),
+// read their half S row with tcgen05.ld, apply the mask and the online softmax in registers
+// (row maxima and sums combined with the partner thread through shared memory; paired fp32
+// FMAs/adds and 3-input max) and write their half P row (bf16, two per 32-bit column) back
+// into TMEM, where the second MMA takes it as its A operand:
+//   O += P V     (A = P from TMEM columns [BN + D, BN + D + BN / 2), B = V from shared memory)  O stays in TMEM for the
+// whole key loop: a row's running maximum is only raised (and its O row rescaled in TMEM)
+// when a block's maximum exceeds it by more than 2^8 in exp2 units, so P <= 256 and the
+// final O / l and LSE = m * scale + log(l) stay exact.
+//
+// Per iteration j: wait S_j (its commit also covers P V_{j-1}); prefetch K/V_{j+1} into the
+// other stage (freed by P V_{j-1}); softmax of S_j into P; wait for K_{j+1}; thread 0 issues
+// P V_j and S_{j+1} back to back.  Two CTAs share an SM (81 KB / 97 KB shared memory for
+// head dim 64 / 128, 256 TMEM columns each), so one CTA's softmax overlaps the other's MMAs.
+//
+// Every mbarrier wait is bounded (about two seconds of SM clock); a CTA that times out sets
+// *status, stops issuing MMAs, waits (bounded) for the ones in flight, frees its TMEM and
+// returns.
+//
+// Reference behaviour: native_kv_attention (src/pra_torch/memory_batching.py:216, called from
+// src/pra_torch/attention.py:443): memory keys before the causal local window, one softmax.
+#include "tcgen05.cuh"
+
+namespace pra {
+namespace attn_tc {
+
+constexpr int BM = 128;
+constexpr int NT = 256;  // two threads per query row: warps w and w + 4 share TMEM lanes 32 (w % 4) ...
+constexpr uint32_t TMEM_COLS = 256;
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float RESCALE_LOG2 = 8.f;
+constexpr long long WAIT_CYCLES = 4000000000LL;
+
+template <int D>
+struct Cfg {
+  static constexpr int BN = D == 64 ? 128 : 64;
+  static constexpr int HB = BN / 2;  // S columns per thread
+  static constexpr int HD = D / 2;   // O columns per thread
+  static constexpr int Q_BYTES = BM * D * 2;
+  static constexpr int KV_BYTES = BN * D * 2;  // one K or V tile
+  static constexpr int OFF_K = Q_BYTES;  // stage s: K at OFF_K + 2 s KV, V after it
+  static constexpr int OFF_RED = OFF_K + 4 * KV_BYTES;    // [2][BM] floats: partner exchange
+  static constexpr int OFF_VALID = OFF_RED + 2 * BM * 4;  // [2][BN] key-padding mask
+  static constexpr int OFF_BAR = OFF_VALID + 2 * BN;
+  static constexpr int SMEM = OFF_BAR + 16;
+  // TMEM columns: S fp32 [0, BN), O fp32 [BN, BN + D), P bf16 pairs [BN + D, BN + D + BN / 2)
+  static constexpr int O_COL = BN, P_COL = BN + D;
+  static_assert(P_COL + BN / 2 <= (int)TMEM_COLS, "accumulators exceed the TMEM allocation");
+  static_assert(OFF_BAR % 8 == 0, "mbarrier alignment");
+  static_assert(HB % 32 == 0 && HD % 32 == 0, "32-column TMEM accesses");
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float m;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
+  return m;
+}
+
+// (a.x * b.x + c.x, a.y * b.y + c.y) in one paired instruction.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n .reg .b64 a, b, c, d;\n mov.b64 a, {%2, %3};\n mov.b64 b, {%4, %5};\n mov.b64 c, {%6, %7};\n"
+      " fma.rn.f32x2 d, a, b, c;\n mov.b64 {%0, %1}, d;\n}\n"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n .reg .b64 a, b, d;\n mov.b64 a, {%2, %3};\n mov.b64 b, {%4, %5};\n add.f32x2 d, a, b;\n"
+      " mov.b64 {%0, %1}, d;\n}\n"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// Pair barrier of the two warps (w, w + 4) that own the same 32 query rows.
+__device__ __forceinline__ void pair_sync(int warp) {
+  switch (warp & 3) {  // immediate barrier ids 1..4 (barrier 0 is __syncthreads)
+    case 0: asm volatile("bar.sync 1, 64;\n" ::: "memory"); break;
+    case 1: asm volatile("bar.sync 2, 64;\n" ::: "memory"); break;
+    case 2: asm volatile("bar.sync 3, 64;\n" ::: "memory"); break;
+    default: asm volatile("bar.sync 4, 64;\n" ::: "memory"); break;
+  }
+}
+
+// Stage a block of BN keys: K and V rows into chunk-major core-matrix tiles (zeros past the
+// end), the key-padding mask for local blocks.  One source-row computation serves K and V.
+template <int D>
+__device__ __forceinline__ void load_block(const AttnParams& p, uint8_t* sk, uint8_t* sv, uint8_t* svalid, int b,
+                                           int kvh, bool memory, int start, int mem_len) {
+  constexpr int BN = Cfg<D>::BN, C = D / 8;
+  if (!memory && p.key_valid != nullptr && threadIdx.x < BN) {
+    const int t = start + threadIdx.x;
+    svalid[threadIdx.x] = t < p.T ? p.key_valid[(int64_t)b * p.T + t] : 0;
+  }
+  const int* idx = memory ? p.mem_idx + (int64_t)b * p.mem_max : nullptr;
+#pragma unroll
+  for (int it = 0; it < BN * C / NT; ++it) {
+    const int i = it * NT + threadIdx.x;
+    const int ri = i & 7, c = (i >> 3) % C, rg = i / (8 * C);
+    const int r = rg * 8 + ri;
+    const __nv_bfloat16* ks = p.k;
+    const __nv_bfloat16* vs = p.v;
+    bool ok;
+    if (memory) {
+      const int j = start + r;
+      ok = j < mem_len;
+      if (ok) {
+        const int64_t off = (int64_t)idx[j] * p.mem_row + kvh * D + c * 8;
+        ks = p.mem_k + off;
+        vs = p.mem_v + off;
+      }
+    } else {
+      const int t = start + r;
+      ok = t < p.T;
+      if (ok) {
+        ks = p.k + b * p.k_batch + (int64_t)t * p.k_row + kvh * D + c * 8;
+        vs = p.v + b * p.v_batch + (int64_t)t * p.v_row + kvh * D + c * 8;
+      }
+    }
+    const uint32_t o = tc::core_off(r, c, BN);
+    cp_async16(sk + o, ks, ok);
+    cp_async16(sv + o, vs, ok);
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(NT, 2) fwd_kernel(AttnParams p) {
+  using C = Cfg<D>;
+  constexpr int BN = C::BN, HB = C::HB, HD = C::HD;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* sq = smem;
+  float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
+  uint8_t* svalid = smem + C::OFF_VALID;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + 8);
+  int* s_abort = reinterpret_cast<int*>(smem + C::OFF_BAR + 12);
+  auto stage_k = [&](int s) { return smem + C::OFF_K + s * 2 * C::KV_BYTES; };
+  auto stage_v = [&](int s) { return smem + C::OFF_K + s * 2 * C::KV_BYTES + C::KV_BYTES; };
+
+  // grid (H * B, query tiles): the longest (last, causal) query tiles are scheduled first
+  const int h = blockIdx.x % p.H, b = blockIdx.x / p.H;
+  const int qb = gridDim.y - 1 - blockIdx.y;
+  const int kvh = h / (p.H / p.Hkv);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int row = tid & (BM - 1), half = tid >> 7;
+  const int q0 = qb * BM;
+  const int mem_len = p.mem_len ? p.mem_len[b] : 0;
+  const int n_mem = (mem_len + BN - 1) / BN;
+  const int q_last = min(q0 + BM, p.T) - 1;
+  const int n_blocks = n_mem + q_last / BN + 1;
+
+  if (warp == 0) {
+    tc::alloc(s_tmem, TMEM_COLS);
+    tc::relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    *s_abort = 0;
+    tc::fence_mbarrier_init();
+  }
+#pragma unroll
+  for (int it = 0; it < BM * (D / 8) / NT; ++it) {
+    const int i = it * NT + tid;
+    const int ri = i & 7, c = (i >> 3) % (D / 8), rg = i / D;
+    const int r = rg * 8 + ri, t = q0 + r;
+    const bool ok = t < p.T;
+    cp_async16(sq + tc::core_off(r, c, BM), ok ? p.q + b * p.q_batch + (int64_t)t * p.q_row + h * D + c * 8 : p.q,
+               ok);
+  }
+  load_block<D>(p, stage_k(0), stage_v(0), svalid, b, kvh, n_mem > 0, 0, mem_len);
+  cp_async_commit();
+  cp_async_wait<0>();
+  fence_proxy_async_smem();
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+
+  const uint32_t tmem = *s_tmem;
+  const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
+  const uint32_t t_s = tmem + lane + half * HB;                // this thread's S columns
+  const uint32_t t_o = tmem + lane + C::O_COL + half * HD;     // this thread's O columns
+  const uint32_t t_p = tmem + lane + C::P_COL + half * HB / 2;  // this thread's P columns
+  constexpr uint32_t ID_S = tc::idesc_bf16(BM, BN, false);
+  constexpr uint32_t ID_O = tc::idesc_bf16(BM, D, true);
+  constexpr uint32_t Q_LBO = (BM / 8) * 128, KV_LBO = (BN / 8) * 128;
+  const uint32_t q_addr = smem_u32(sq);
+
+  // S = Q K^T: A = Q (K-major over D), B = K tile (K-major over D); 16 features per MMA.
+  auto issue_s = [&](int s) {
+    const uint32_t k_addr = smem_u32(stage_k(s));
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk)
+      tc::mma_bf16(tmem, tc::smem_desc(q_addr + kk * 2 * Q_LBO, Q_LBO, 128),
+                   tc::smem_desc(k_addr + kk * 2 * KV_LBO, KV_LBO, 128), ID_S, kk > 0);
+  };
+  // O (+)= P V: A = P in TMEM (8 columns per 16 keys), B = V tile (MN-major: D contiguous).
+  auto issue_o = [&](int s, bool acc) {
+    const uint32_t v_addr = smem_u32(stage_v(s));
+#pragma unroll
+    for (int kk = 0; kk < BN / 16; ++kk)
+      tc::mma_bf16_ts(tmem + C::O_COL, tmem + C::P_COL + kk * 8, tc::smem_desc(v_addr + kk * 2 * 128, 128, KV_LBO),
+                      ID_O, (acc || kk > 0) ? 1u : 0u);
+  };
+
+  if (tid == 0) {
+    issue_s(0);
+    tc::commit(bar);
+  }
+
+  const float sl2 = p.scale * LOG2E;
+  const int q = q0 + row;
+  float m_run = -INFINITY, l_run = 0.f;  // l_run: this thread's columns only
+  bool aborted = false;
+
+  for (int j = 0; j < n_blocks; ++j) {
+    const int s = j & 1;
+    if (!tc::mbar_wait_cycles(bar, (uint32_t)(j & 1), WAIT_CYCLES)) *s_abort = 1;
+    const bool memory = j < n_mem;
+    const int start = memory ? j * BN : (j - n_mem) * BN;
+    if (j + 1 < n_blocks) {
+      const bool mem_next = j + 1 < n_mem;
+      load_block<D>(p, stage_k(s ^ 1), stage_v(s ^ 1), svalid + (s ^ 1) * BN, b, kvh, mem_next,
+                    mem_next ? (j + 1) * BN : (j + 1 - n_mem) * BN, mem_len);
+      cp_async_commit();
+    }
+
+    // visible keys of this thread's columns: [0, lim) (and the padding mask for local blocks)
+    const int col0 = half * HB;
+    int lim;
+    const uint8_t* valid = nullptr;
+    if (memory) {
+      lim = mem_len - start - col0;
+    } else {
+      lim = min(p.T, q + 1) - start - col0;
+      if (p.key_valid != nullptr) valid = svalid + s * BN + col0;
+    }
+    const bool masked = lim < HB || valid != nullptr;
+    // S columns [c0, c0 + 32) of this thread, masked keys at -inf (read twice from TMEM: once
+    // for the row maximum, once for the exponentials, which keeps 32 scores live at a time)
+    auto load_s = [&](int c0, float (&sv)[32]) {
+      uint32_t r[32];
+      tc::ld32(t_s + c0, r);
+      if (!masked) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sv[i] = __uint_as_float(r[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int c = c0 + i;
+          const bool vis = c < lim && (valid == nullptr || valid[c] != 0);
+          sv[i] = vis ? __uint_as_float(r[i]) : -INFINITY;
+        }
+      }
+    };
+    float mx = -INFINITY;
+#pragma unroll
+    for (int c0 = 0; c0 < HB; c0 += 32) {
+      float sv[32];
+      load_s(c0, sv);
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) mx = max3(mx, sv[i], sv[i + 1]);
+    }
+    red[half * BM + row] = mx;
+    pair_sync(warp);
+    mx = fmaxf(mx, red[(half ^ 1) * BM + row]);
+
+    // running maximum, raised lazily; O rows rescaled in TMEM when it moves
+    float corr = 1.f;
+    bool rescale = false;
+    if (mx > m_run) {
+      if (m_run == -INFINITY) {
+        m_run = mx;  // nothing accumulated yet: l = 0 and the row of O is zero (or not yet written)
+      } else if ((mx - m_run) * sl2 > RESCALE_LOG2) {
+        corr = ex2((m_run - mx) * sl2);
+        l_run *= corr;
+        m_run = mx;
+        rescale = true;
+      }
+    }
+    if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+      for (int c0 = 0; c0 < HD; c0 += 32) {
+        uint32_t r[32];
+        tc::ld32(t_o + c0, r);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
+        tc::st32(t_o + c0, r);
+      }
+    }
+    const float ms = m_run == -INFINITY ? 0.f : m_run * sl2;
+    const float2 sl2x2 = make_float2(sl2, sl2), nms = make_float2(-ms, -ms);
+    float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int c0 = 0; c0 < HB; c0 += 32) {
+      float sv[32];
+      load_s(c0, sv);
+      uint32_t w[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float2 x = fma2(make_float2(sv[2 * i], sv[2 * i + 1]), sl2x2, nms);
+        x.x = ex2(x.x);
+        x.y = ex2(x.y);
+        acc = add2(acc, x);
+        w[i] = pack_bf16(x.x, x.y);
+      }
+      tc::st16(t_p + c0 / 2, w);
+    }
+    l_run += acc.x + acc.y;
+
+    if (j + 1 < n_blocks) cp_async_wait<0>();
+    fence_proxy_async_smem();  // cp.async data -> the tensor core's (async proxy) reads
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    if (*s_abort) {
+      aborted = true;
+      break;
+    }
+    if (tid == 0) {
+      issue_o(s, j > 0);
+      if (j + 1 < n_blocks) issue_s(s ^ 1);
+      tc::commit(bar);
+    }
+  }
+
+  if (!aborted) {
+    if (!tc::mbar_wait_cycles(bar, (uint32_t)(n_blocks & 1), WAIT_CYCLES)) aborted = true;
+  }
+  aborted = __syncthreads_or(aborted);  // uniform: the epilogue's TMEM loads are warp-collective
+  red[half * BM + row] = l_run;
+  pair_sync(warp);
+  const float l_tot = l_run + red[(half ^ 1) * BM + row];
+  if (!aborted) {
+    const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+    __nv_bfloat16* dst = p.o + b * p.o_batch + (int64_t)q * p.o_row + h * D + half * HD;
+#pragma unroll
+    for (int c0 = 0; c0 < HD; c0 += 32) {
+      uint32_t r[32];
+      tc::ld32(t_o + c0, r);
+      if (q < p.T) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 w;
+          w.x = pack_bf16(__uint_as_float(r[i + 0]) * inv, __uint_as_float(r[i + 1]) * inv);
+          w.y = pack_bf16(__uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
+          w.z = pack_bf16(__uint_as_float(r[i + 4]) * inv, __uint_as_float(r[i + 5]) * inv);
+          w.w = pack_bf16(__uint_as_float(r[i + 6]) * inv, __uint_as_float(r[i + 7]) * inv);
+          *reinterpret_cast<uint4*>(dst + c0 + i) = w;
+        }
+      }
+    }
+    if (q < p.T && half == 0)
+      p.lse[((int64_t)b * p.H + h) * p.T + q] = l_tot > 0.f ? m_run * p.scale + logf(l_tot) : -INFINITY;
+  } else {
+    // Stop: record the failure, give the MMAs in flight a bounded time to finish, free TMEM.
+    if (tid == 0 && p.status != nullptr) atomicExch(p.status, 1);
+    cp_async_wait<0>();
+    tc::mbar_wait_cycles(bar, (uint32_t)(n_blocks & 1), WAIT_CYCLES);
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after();
+    tc::dealloc(tmem, TMEM_COLS);
+  }
+}
+
+template <int D>
+cudaError_t launch(const AttnParams& p, cudaStream_t st) {
+  constexpr int smem = Cfg<D>::SMEM;
+  PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  dim3 grid(p.H * p.B, (p.T + BM - 1) / BM);
+  fwd_kernel<D><<<grid, NT, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace attn_tc
+}  // namespace pra
+
+// The tcgen05 forward takes head dims 64 and 128 with 16-byte aligned rows; returns
+// cudaErrorNotSupported for anything else so the caller can use the mma.sync kernel.
+cudaError_t pra_attention_fwd_tc(const AttnParams& p, int head_dim, cudaStream_t st) {
+  using namespace pra::attn_tc;
+  auto aligned = [](const void* ptr, int64_t a, int64_t b_) {
+    return (reinterpret_cast<uintptr_t>(ptr) % 16) == 0 && a % 8 == 0 && b_ % 8 == 0;
+  };
+  if (!aligned(p.q, p.q_row, p.q_batch) || !aligned(p.k, p.k_row, p.k_batch) || !aligned(p.v, p.v_row, p.v_batch) ||
+      !aligned(p.o, p.o_row, p.o_batch))
+    return cudaErrorNotSupported;
+  if (p.mem_idx != nullptr && (!aligned(p.mem_k, p.mem_row, 0) || !aligned(p.mem_v, p.mem_row, 0)))
+    return cudaErrorNotSupported;
+  switch (head_dim) {
+    case 64: return launch<64>(p, st);
+    case 128: return launch<128>(p, st);
+    default: return cudaErrorNotSupported;
+  }
+}

@@ -5,6 +5,7 @@
 
 #include <cmath>
 #include <cstring>
+#include <map>
 #include <vector>
 
 #include "kernels.h"
@@ -33,6 +34,15 @@ const T* optr(const c10::optional<torch::Tensor>& t) {
 }
 
 // ---------------------------------------------------------------- attention
+// Per-device status word of the attention kernels (1 after a kernel gave up on a bounded
+// wait); allocated on first use and never freed (it outlives the interpreter's tensors).
+torch::Tensor& attention_status_buffer(const torch::Device& dev) {
+  static auto* bufs = new std::map<int, torch::Tensor>();
+  auto& t = (*bufs)[dev.index()];
+  if (!t.defined()) t = torch::zeros({1}, torch::TensorOptions().dtype(at::kInt).device(dev));
+  return t;
+}
+
 AttnParams attn_params(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, int64_t heads,
                        int64_t kv_heads, const c10::optional<torch::Tensor>& mem_k,
                        const c10::optional<torch::Tensor>& mem_v, const c10::optional<torch::Tensor>& mem_idx,
@@ -45,6 +55,7 @@ AttnParams attn_params(const torch::Tensor& q, const torch::Tensor& k, const tor
   expect(v, at::kBFloat16, "v");
   TORCH_CHECK(heads % kv_heads == 0, "heads must be a multiple of kv heads");
   AttnParams p{};
+  p.status = ptr<int>(attention_status_buffer(q.device()));
   p.B = q.size(0);
   p.T = q.size(1);
   p.H = heads;
@@ -894,6 +905,12 @@ std::vector<torch::Tensor> stack_forward(torch::Tensor x, int64_t B, int64_t T, 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "PRA sm_100a kernels";
   m.def("attention_fwd", &attention_fwd);
+  m.def("attention_status", [](int64_t device) { return attention_status_buffer(torch::Device(torch::kCUDA, device)); });
+  m.def("set_attention_impl", [](const std::string& impl) {
+    TORCH_CHECK(impl == "tcgen05" || impl == "mma", "attention impl must be 'tcgen05' or 'mma'");
+    pra_attention_set_impl(impl == "tcgen05" ? 1 : 0);
+  });
+  m.def("attention_impl", []() { return std::string(pra_attention_get_impl() ? "tcgen05" : "mma"); });
   m.def("attention_bwd", &attention_bwd);
   m.def("gemm", &gemm);
   m.def("norm_fwd", &norm_fwd);

@@ -28,9 +28,15 @@ struct AttnParams {
   __nv_bfloat16* dk;
   __nv_bfloat16* dv;
   int64_t dq_row, dq_batch, dk_row, dk_batch, dv_row, dv_batch;
+  int* status;                 // optional: set to 1 by a kernel that gave up on a bounded wait
 };
 
 cudaError_t pra_attention_fwd(const AttnParams& p, int head_dim, cudaStream_t stream);
+// tcgen05 forward (head dims 64/128, 16-byte aligned rows); cudaErrorNotSupported otherwise.
+cudaError_t pra_attention_fwd_tc(const AttnParams& p, int head_dim, cudaStream_t stream);
+// Forward implementation: 1 = tcgen05 where supported (default), 0 = mma.sync everywhere.
+void pra_attention_set_impl(int tcgen05);
+int pra_attention_get_impl();
 cudaError_t pra_attention_bwd(const AttnParams& p, int head_dim, cudaStream_t stream);
 
 // ---- GEMMs (gemm/*.cu, CUTLASS sm100 collectives) -------------------------------

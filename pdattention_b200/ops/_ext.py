@@ -23,7 +23,7 @@ CSRC = ROOT / "csrc"
 BUILD_DIR = Path(__file__).resolve().parent / "_build"
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
-_SOURCES = ["bindings.cpp", "attention.cu", "norm.cu", "loss_optim.cu", "gist.cu", "routing.cu", "llama.cu",
+_SOURCES = ["bindings.cpp", "attention.cu", "attention_tc.cu", "norm.cu", "loss_optim.cu", "gist.cu", "routing.cu", "llama.cu",
             "gemm/tn_bias.cu", "gemm/tn_bias_gelu.cu", "gemm/nn.cu", "gemm/nn_dgelu.cu", "gemm/wgrad.cu", "gemm/tn_f32.cu", "gemm/tn_bias_small.cu", "gemm/tn_bias_narrow.cu",
             "colsum_noalloc.cu", "dp_reduce.cu", "tp_comm.cu", "embed.cu", "driver_shim.cu"]
 
@@ -37,7 +37,7 @@ KERNELS_PER_CALL = {"attention_fwd": 1, "attention_bwd": 3, "gemm": 1, "norm_fwd
                     "stack_forward": 0, "dp_allreduce": 1, "dp_signal_words": 0,
                     "ipc_alloc": 0, "ipc_open": 0, "ipc_close": 0,
                     "rope_copy": 1, "silu_mul": 1, "decode_attention": 2, "route_topk": 1,
-                    "tp_allreduce": 1, "tp_allgather": 1, "tp_signal_words": 0, "route_merge": 1, "embed_add": 1, "combine_partials": 1}  # stack_forward: counted per layer by its caller
+                    "tp_allreduce": 1, "tp_allgather": 1, "tp_signal_words": 0, "route_merge": 1, "embed_add": 1, "combine_partials": 1, "attention_status": 0, "set_attention_impl": 0, "attention_impl": 0}  # stack_forward: counted per layer by its caller
 
 
 class LaunchCounter:
@@ -147,6 +147,9 @@ def require():
         raise RuntimeError(
             "The pra_ops CUDA extension is not built. Run `python -c 'import __graft_entry__ as g; g.build()'` "
             "(or pdattention_b200.ops._ext.build()) on a machine with nvcc before using CUDA tensors.")
+    impl = os.environ.get("PRA_ATTENTION_IMPL")
+    if impl:  # "tcgen05" (default) or "mma": which forward attention kernel runs
+        module.set_attention_impl(impl)
     _counter = LaunchCounter(module)
     return _counter
 

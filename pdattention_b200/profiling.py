@@ -7,6 +7,7 @@ profiler and then under ``ncu`` on one GPU with the same arguments::
     python -m pdattention_b200.profiling decode-small      # Llama-3-8B decode, 512 memory chunks
     python -m pdattention_b200.profiling train-table       # torch.profiler kernel table of one step (8 rows)
     python -m pdattention_b200.profiling decode-table      # kernel table of one decode step (64 rows)
+    python -m pdattention_b200.profiling attention-fwd     # forward attention kernels, tcgen05 vs mma.sync
     torchrun --nproc-per-node N -m pdattention_b200.profiling decode-table-tp   # TP decode step table
 
 The ``*-small`` cases keep device memory to a few GB so full ``ncu`` captures of one
@@ -160,6 +161,54 @@ def decode_table_tp(memory_chunks: int = 16384) -> None:
     dist.destroy_process_group()
 
 
+def attention_fwd(iters: int = 20) -> None:
+    """Device time of the forward attention kernels (tcgen05 and mma.sync) on the shapes the
+    training step and the Llama prefill run: CUDA events around ``iters`` back-to-back
+    launches, median of five such batches."""
+    import math
+    import statistics
+
+    from .ops._ext import require
+
+    ext = require()
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    shapes = [  # name, B, T, H, Hkv, D, memory keys per row
+        ("tinygpt prompt", 8, 1024, 12, 12, 64, 1024),
+        ("tinygpt chunk encode", 128, 64, 12, 12, 64, 256),
+        ("llama prefill 4k", 1, 4096, 32, 8, 128, 1024),
+        ("llama chunk encode", 64, 64, 32, 8, 128, 0),
+    ]
+    print(f"{'shape':24s} {'impl':8s} {'us':>9s} {'TFLOP/s':>8s}")
+    for name, B, T, H, Hkv, D, M in shapes:
+        q = torch.randn((B, T, H * D), generator=gen, device=dev).bfloat16()
+        k = torch.randn((B, T, Hkv * D), generator=gen, device=dev).bfloat16()
+        v = torch.randn((B, T, Hkv * D), generator=gen, device=dev).bfloat16()
+        pool = torch.randn((max(M, 1) * 4, 2 * Hkv * D), generator=gen, device=dev).bfloat16()
+        idx = torch.randint(0, pool.shape[0], (B, max(M, 1)), generator=gen, device=dev, dtype=torch.int32)
+        mlen = torch.full((B,), M, device=dev, dtype=torch.int32)
+        keys = B * H * (M * T + T * (T + 1) / 2)
+        flops = 4.0 * D * keys
+        for impl in ("tcgen05", "mma"):
+            ext.set_attention_impl(impl)
+            call = lambda: ext.attention_fwd(q, k, v, H, Hkv, D, pool[:, :Hkv * D], pool[:, Hkv * D:], idx, mlen,
+                                             None, 1.0 / math.sqrt(D))
+            for _ in range(3):
+                call()
+            times = []
+            for _ in range(5):  # five batches of `iters` back-to-back launches
+                a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                for _ in range(iters):
+                    call()
+                b_.record()
+                b_.synchronize()
+                times.append(a.elapsed_time(b_) * 1000 / iters)
+            us = statistics.median(times)
+            print(f"{name:24s} {impl:8s} {us:9.1f} {flops / us / 1e6:8.1f}")
+    ext.set_attention_impl("tcgen05")
+
+
 def sweep_table(tokens: int = 1 << 24, gists: int = 1, k: int = 16) -> None:
     """Kernel table of one fused layer step of the memory sweep (one GPU, 16M-token memory)."""
     from .inference.memory_sweep import HEAD_DIM, HEADS, KV_DIM, ShardedLayerMemory, fused_layer_step
@@ -175,7 +224,7 @@ def sweep_table(tokens: int = 1 << 24, gists: int = 1, k: int = 16) -> None:
     _table(lambda: fused_layer_step(mem, rq, q, k), rows=15)
 
 
-CASES = {"sweep-table": sweep_table, "train-small": train_small, "decode-small": decode_small, "train-table": train_table,
+CASES = {"attention-fwd": attention_fwd, "sweep-table": sweep_table, "train-small": train_small, "decode-small": decode_small, "train-table": train_table,
          "decode-table": decode_table, "decode-table-tp": decode_table_tp}
 
 

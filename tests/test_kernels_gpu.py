@@ -242,3 +242,61 @@ def test_route_kernel_matches_object_search(ext):
     from pdattention_b200.models.fastpath import routing_selftest
 
     routing_selftest(torch.device("cuda"))
+
+
+def _gqa_reference(q, k, v, mem_k, mem_v, key_valid, scale, kv_heads):
+    """fp32 restatement with grouped KV heads: q [B,T,H,D], k/v [B,T,Hkv,D], memory per row."""
+    h = q.shape[2]
+    rep = h // kv_heads
+    expand = (lambda x: x.repeat_interleave(rep, dim=-2) if x is not None else None)
+    mk = [expand(m) for m in mem_k] if mem_k is not None else None
+    mv = [expand(m) for m in mem_v] if mem_v is not None else None
+    return _attention_reference(q, expand(k), expand(v), mk, mv, key_valid, scale)
+
+
+@pytest.mark.parametrize("head_dim", [64, 128])
+@pytest.mark.parametrize("t,lens,logit_scale", [(300, [260, 513], 1.0), (300, [0, 129], 6.0), (1, [64, 0], 1.0),
+                                                (1024, [0, 0], 3.0)])
+def test_attention_fwd_tcgen05(ext, head_dim, t, lens, logit_scale):
+    """The tcgen05 forward against fp32 PyTorch and the mma.sync forward: GQA (8 heads over 2),
+    memory blocks gathered from a pool, padding masks, and logits large enough that the lazily
+    raised running maximum rescales O in TMEM."""
+    b, h, hkv = 2, 8, 2
+    d, dk = h * head_dim, hkv * head_dim
+    q = _bf(b, t, d, seed=11)
+    k = _bf(b, t, dk, seed=12)
+    v = _bf(b, t, dk, seed=13)
+    key_valid = torch.ones(b, t, dtype=torch.uint8, device="cuda")
+    if t > 10:
+        key_valid[0, t // 3: t // 2] = 0
+    pool = _bf(1200, 2 * dk, seed=14)
+    g = torch.Generator(device="cuda").manual_seed(15)
+    idx = torch.zeros(b, max(max(lens), 1), dtype=torch.int32, device="cuda")
+    rows = []
+    for r, n in enumerate(lens):
+        sel = torch.randperm(1200, device="cuda", generator=g)[:n].int()
+        idx[r, :n] = sel
+        rows.append(sel.long())
+    mem_len = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    scale = logit_scale / math.sqrt(head_dim)
+    status = ext.attention_status(0)
+    status.zero_()
+    outs = {}
+    for impl in ("tcgen05", "mma"):
+        ext.set_attention_impl(impl)
+        outs[impl] = ext.attention_fwd(q, k, v, h, hkv, head_dim, pool[:, :dk], pool[:, dk:], idx, mem_len,
+                                       key_valid, scale)
+    ext.set_attention_impl("tcgen05")
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    mk = [pool[r_, :dk].view(-1, hkv, head_dim) for r_ in rows]
+    mv = [pool[r_, dk:].view(-1, hkv, head_dim) for r_ in rows]
+    ref = _gqa_reference(q.view(b, t, h, head_dim), k.view(b, t, hkv, head_dim), v.view(b, t, hkv, head_dim),
+                         mk, mv, key_valid, scale, hkv)
+    out_tc, lse_tc = outs["tcgen05"]
+    out_mma, lse_mma = outs["mma"]
+    _close(out_tc.view(b, t, h, head_dim), ref, 2e-2)
+    _close(out_tc, out_mma, 2e-2)
+    finite = torch.isfinite(lse_mma)
+    assert torch.equal(finite, torch.isfinite(lse_tc))
+    assert (lse_tc[finite] - lse_mma[finite]).abs().max().item() < 1e-2 * max(1.0, lse_mma[finite].abs().max().item())
