@@ -509,7 +509,11 @@ cudaError_t launch_bwd(const Params& p, cudaStream_t st) {
     delta_kernel<D><<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(p);
     PRA_RETURN_IF_ERROR(cudaGetLastError());
   }
-  {
+  cudaError_t tc_dq = cudaErrorNotSupported;
+  if (pra_attention_get_impl() && p.T > 64) tc_dq = pra_attention_bwd_dq_tc(p, D, st);
+  if (tc_dq != cudaErrorNotSupported) {
+    PRA_RETURN_IF_ERROR(tc_dq);
+  } else {
     const size_t smem = (size_t)(2 * BM + 4 * BN) * LD * sizeof(__nv_bfloat16) + 2 * BN;
     PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     dim3 grid(p.H * p.B, (p.T + BM - 1) / BM);

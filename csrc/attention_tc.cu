@@ -104,30 +104,61 @@ __device__ __forceinline__ void pair_sync(int warp) {
   }
 }
 
-// Stage a block of BN keys: K and V rows into chunk-major core-matrix tiles (zeros past the
-// end), the key-padding mask for local blocks.  One source-row computation serves K and V.
-template <int D>
-__device__ __forceinline__ void load_block(const AttnParams& p, uint8_t* sk, uint8_t* sv, uint8_t* svalid, int b,
-                                           int kvh, bool memory, int start, int mem_len) {
-  constexpr int BN = Cfg<D>::BN, C = D / 8;
-  if (!memory && p.key_valid != nullptr && threadIdx.x < BN) {
-    const int t = start + threadIdx.x;
-    svalid[threadIdx.x] = t < p.T ? p.key_valid[(int64_t)b * p.T + t] : 0;
-  }
-  const int* idx = memory ? p.mem_idx + (int64_t)b * p.mem_max : nullptr;
-#pragma unroll
-  for (int it = 0; it < BN * C / NT; ++it) {
+// Rows of a block staged by this thread: with i = it * NT + tid, row (i / (8 * C)) * 8 + i % 8
+// for it = 0 .. ROWS - 1 (C = D / 8 sixteen-byte chunks per row); the same rows for K and V.
+template <int D, int BN>
+struct Rows {
+  static constexpr int C = D / 8;
+  static constexpr int ROWS = BN * C / NT;
+  static __device__ __forceinline__ int row(int it) {
     const int i = it * NT + threadIdx.x;
-    const int ri = i & 7, c = (i >> 3) % C, rg = i / (8 * C);
-    const int r = rg * 8 + ri;
+    return (i / (8 * C)) * 8 + (i & 7);
+  }
+  static __device__ __forceinline__ int chunk() { return (threadIdx.x >> 3) % C; }
+};
+
+// What the loads of one key block need from global memory before they can be issued: the
+// pool row of each of this thread's memory keys (-1 past the end) and the padding mask byte
+// of key threadIdx.x for local blocks.  Fetched one block ahead so the latency is hidden.
+template <int D, int BN>
+struct BlockMeta {
+  int pool_row[Rows<D, BN>::ROWS];
+  uint8_t valid;
+};
+
+template <int D, int BN>
+__device__ __forceinline__ void fetch_meta(const AttnParams& p, BlockMeta<D, BN>& m, int b, bool memory, int start,
+                                           int mem_len) {
+  if (memory) {
+    const int* idx = p.mem_idx + (int64_t)b * p.mem_max;
+#pragma unroll
+    for (int it = 0; it < Rows<D, BN>::ROWS; ++it) {
+      const int j = start + Rows<D, BN>::row(it);
+      m.pool_row[it] = j < mem_len ? __ldg(idx + j) : -1;
+    }
+  } else if (p.key_valid != nullptr && threadIdx.x < BN) {
+    const int t = start + threadIdx.x;
+    m.valid = t < p.T ? __ldg(p.key_valid + (int64_t)b * p.T + t) : 0;
+  }
+}
+
+// Stage a block of BN keys: K and V rows into chunk-major core-matrix tiles (zeros past the
+// end), the key-padding mask for local blocks.
+template <int D, int BN>
+__device__ __forceinline__ void load_block(const AttnParams& p, const BlockMeta<D, BN>& m, uint8_t* sk, uint8_t* sv,
+                                           uint8_t* svalid, int b, int kvh, bool memory, int start) {
+  if (!memory && p.key_valid != nullptr && threadIdx.x < BN) svalid[threadIdx.x] = m.valid;
+  const int c = Rows<D, BN>::chunk();
+#pragma unroll
+  for (int it = 0; it < Rows<D, BN>::ROWS; ++it) {
+    const int r = Rows<D, BN>::row(it);
     const __nv_bfloat16* ks = p.k;
     const __nv_bfloat16* vs = p.v;
     bool ok;
     if (memory) {
-      const int j = start + r;
-      ok = j < mem_len;
+      ok = m.pool_row[it] >= 0;
       if (ok) {
-        const int64_t off = (int64_t)idx[j] * p.mem_row + kvh * D + c * 8;
+        const int64_t off = (int64_t)m.pool_row[it] * p.mem_row + kvh * D + c * 8;
         ks = p.mem_k + off;
         vs = p.mem_v + off;
       }
@@ -142,6 +173,20 @@ __device__ __forceinline__ void load_block(const AttnParams& p, uint8_t* sk, uin
     const uint32_t o = tc::core_off(r, c, BN);
     cp_async16(sk + o, ks, ok);
     cp_async16(sv + o, vs, ok);
+  }
+}
+
+// Stage BM query rows (t = q0 .. q0 + BM - 1 of head h) of `src` into a chunk-major tile.
+template <int D>
+__device__ __forceinline__ void load_query_rows(uint8_t* tile, const __nv_bfloat16* src, int64_t row_stride,
+                                                int64_t batch_stride, int b, int h, int q0, int T) {
+#pragma unroll
+  for (int it = 0; it < BM * (D / 8) / NT; ++it) {
+    const int i = it * NT + threadIdx.x;
+    const int c = (i >> 3) % (D / 8), r = (i / D) * 8 + (i & 7), t = q0 + r;
+    const bool ok = t < T;
+    cp_async16(tile + tc::core_off(r, c, BM), ok ? src + b * batch_stride + (int64_t)t * row_stride + h * D + c * 8 : src,
+               ok);
   }
 }
 
@@ -180,17 +225,13 @@ __global__ void __launch_bounds__(NT, 2) fwd_kernel(AttnParams p) {
     *s_abort = 0;
     tc::fence_mbarrier_init();
   }
-#pragma unroll
-  for (int it = 0; it < BM * (D / 8) / NT; ++it) {
-    const int i = it * NT + tid;
-    const int ri = i & 7, c = (i >> 3) % (D / 8), rg = i / D;
-    const int r = rg * 8 + ri, t = q0 + r;
-    const bool ok = t < p.T;
-    cp_async16(sq + tc::core_off(r, c, BM), ok ? p.q + b * p.q_batch + (int64_t)t * p.q_row + h * D + c * 8 : p.q,
-               ok);
-  }
-  load_block<D>(p, stage_k(0), stage_v(0), svalid, b, kvh, n_mem > 0, 0, mem_len);
+  load_query_rows<D>(sq, p.q, p.q_row, p.q_batch, b, h, q0, p.T);
+  auto block_start = [&](int j) { return j < n_mem ? j * BN : (j - n_mem) * BN; };
+  BlockMeta<D, BN> meta;
+  fetch_meta<D, BN>(p, meta, b, n_mem > 0, 0, mem_len);
+  load_block<D, BN>(p, meta, stage_k(0), stage_v(0), svalid, b, kvh, n_mem > 0, 0);
   cp_async_commit();
+  if (n_blocks > 1) fetch_meta<D, BN>(p, meta, b, 1 < n_mem, block_start(1), mem_len);
   cp_async_wait<0>();
   fence_proxy_async_smem();
   tc::fence_before();
@@ -238,12 +279,12 @@ __global__ void __launch_bounds__(NT, 2) fwd_kernel(AttnParams p) {
     const int s = j & 1;
     if (!tc::mbar_wait_cycles(bar, (uint32_t)(j & 1), WAIT_CYCLES)) *s_abort = 1;
     const bool memory = j < n_mem;
-    const int start = memory ? j * BN : (j - n_mem) * BN;
+    const int start = block_start(j);
     if (j + 1 < n_blocks) {
-      const bool mem_next = j + 1 < n_mem;
-      load_block<D>(p, stage_k(s ^ 1), stage_v(s ^ 1), svalid + (s ^ 1) * BN, b, kvh, mem_next,
-                    mem_next ? (j + 1) * BN : (j + 1 - n_mem) * BN, mem_len);
+      load_block<D, BN>(p, meta, stage_k(s ^ 1), stage_v(s ^ 1), svalid + (s ^ 1) * BN, b, kvh, j + 1 < n_mem,
+                    block_start(j + 1));
       cp_async_commit();
+      if (j + 2 < n_blocks) fetch_meta<D, BN>(p, meta, b, j + 2 < n_mem, block_start(j + 2), mem_len);
     }
 
     // visible keys of this thread's columns: [0, lim) (and the padding mask for local blocks)
@@ -257,30 +298,30 @@ __global__ void __launch_bounds__(NT, 2) fwd_kernel(AttnParams p) {
       if (p.key_valid != nullptr) valid = svalid + s * BN + col0;
     }
     const bool masked = lim < HB || valid != nullptr;
-    // S columns [c0, c0 + 32) of this thread, masked keys at -inf (read twice from TMEM: once
-    // for the row maximum, once for the exponentials, which keeps 32 scores live at a time)
-    auto load_s = [&](int c0, float (&sv)[32]) {
-      uint32_t r[32];
-      tc::ld32(t_s + c0, r);
+    // This thread's HB S columns (HB = 32 or 64, one TMEM load), masked keys at -inf.  S is
+    // read twice from TMEM: here for the row maximum, below (32 columns at a time) for the
+    // exponentials.
+    auto load_s = [&](float (&sv)[HB]) {
+      uint32_t r[HB];
+      if constexpr (HB == 64) tc::ld64(t_s, r);
+      else tc::ld32(t_s, r);
       if (!masked) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) sv[i] = __uint_as_float(r[i]);
+        for (int i = 0; i < HB; ++i) sv[i] = __uint_as_float(r[i]);
       } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int c = c0 + i;
-          const bool vis = c < lim && (valid == nullptr || valid[c] != 0);
+        for (int i = 0; i < HB; ++i) {
+          const bool vis = i < lim && (valid == nullptr || valid[i] != 0);
           sv[i] = vis ? __uint_as_float(r[i]) : -INFINITY;
         }
       }
     };
     float mx = -INFINITY;
+    {
+      float sv[HB];
+      load_s(sv);
 #pragma unroll
-    for (int c0 = 0; c0 < HB; c0 += 32) {
-      float sv[32];
-      load_s(c0, sv);
-#pragma unroll
-      for (int i = 0; i < 32; i += 2) mx = max3(mx, sv[i], sv[i + 1]);
+      for (int i = 0; i < HB; i += 2) mx = max3(mx, sv[i], sv[i + 1]);
     }
     red[half * BM + row] = mx;
     pair_sync(warp);
@@ -314,12 +355,18 @@ __global__ void __launch_bounds__(NT, 2) fwd_kernel(AttnParams p) {
     float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
     for (int c0 = 0; c0 < HB; c0 += 32) {
-      float sv[32];
-      load_s(c0, sv);
+      uint32_t r[32];
+      tc::ld32(t_s + c0, r);
       uint32_t w[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        float2 x = fma2(make_float2(sv[2 * i], sv[2 * i + 1]), sl2x2, nms);
+        float2 sv = make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+        if (masked) {
+          const int c = c0 + 2 * i;
+          if (!(c < lim && (valid == nullptr || valid[c] != 0))) sv.x = -INFINITY;
+          if (!(c + 1 < lim && (valid == nullptr || valid[c + 1] != 0))) sv.y = -INFINITY;
+        }
+        float2 x = fma2(sv, sl2x2, nms);
         x.x = ex2(x.x);
         x.y = ex2(x.y);
         acc = add2(acc, x);
@@ -387,6 +434,200 @@ __global__ void __launch_bounds__(NT, 2) fwd_kernel(AttnParams p) {
   }
 }
 
+// ---- backward: dQ -------------------------------------------------------------------------
+// dQ of a 128-query tile over every key block it sees, head dim 64, blocks of 64 keys:
+//   S  = Q K^T  -> TMEM [0, 64)       dP = dO V^T -> TMEM [64, 128)
+//   dS = P (dP - delta) with P = exp2(S scale log2e - lse log2e), bf16 pairs -> TMEM [192, 224)
+//   dQ += dS K  (A = dS from TMEM, B = K tile MN-major) -> TMEM [128, 192)
+// Two threads per query row (32 S/dP columns each), the same staging, prefetch and bounded
+// waits as the forward.  dQ = scale * (dS K).
+struct DqCfg {
+  static constexpr int D = 64, BN = 64, HB = 32;
+  static constexpr int Q_BYTES = BM * D * 2, KV_BYTES = BN * D * 2;
+  static constexpr int OFF_DO = Q_BYTES, OFF_K = 2 * Q_BYTES;  // stage s: K at OFF_K + 2 s KV, V after it
+  static constexpr int OFF_VALID = OFF_K + 4 * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_VALID + 2 * BN;
+  static constexpr int SMEM = OFF_BAR + 16;
+  static constexpr int S_COL = 0, DP_COL = 64, DQ_COL = 128, DS_COL = 192;
+};
+
+__global__ void __launch_bounds__(NT, 2) bwd_dq_kernel(AttnParams p) {
+  using C = DqCfg;
+  constexpr int D = C::D, BN = C::BN, HB = C::HB;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* sq = smem;
+  uint8_t* sdo = smem + C::OFF_DO;
+  uint8_t* svalid = smem + C::OFF_VALID;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + 8);
+  int* s_abort = reinterpret_cast<int*>(smem + C::OFF_BAR + 12);
+  auto stage_k = [&](int s) { return smem + C::OFF_K + s * 2 * C::KV_BYTES; };
+  auto stage_v = [&](int s) { return smem + C::OFF_K + s * 2 * C::KV_BYTES + C::KV_BYTES; };
+
+  const int h = blockIdx.x % p.H, b = blockIdx.x / p.H;
+  const int qb = gridDim.y - 1 - blockIdx.y;
+  const int kvh = h / (p.H / p.Hkv);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int row = tid & (BM - 1), half = tid >> 7;
+  const int q0 = qb * BM;
+  const int mem_len = p.mem_len ? p.mem_len[b] : 0;
+  const int n_mem = (mem_len + BN - 1) / BN;
+  const int q_last = min(q0 + BM, p.T) - 1;
+  const int n_blocks = n_mem + q_last / BN + 1;
+
+  if (warp == 0) {
+    tc::alloc(s_tmem, TMEM_COLS);
+    tc::relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    *s_abort = 0;
+    tc::fence_mbarrier_init();
+  }
+  load_query_rows<D>(sq, p.q, p.q_row, p.q_batch, b, h, q0, p.T);
+  load_query_rows<D>(sdo, p.dout, p.do_row, p.do_batch, b, h, q0, p.T);
+  auto block_start = [&](int j) { return j < n_mem ? j * BN : (j - n_mem) * BN; };
+  BlockMeta<D, BN> meta;
+  fetch_meta<D, BN>(p, meta, b, n_mem > 0, 0, mem_len);
+  load_block<D, BN>(p, meta, stage_k(0), stage_v(0), svalid, b, kvh, n_mem > 0, 0);
+  cp_async_commit();
+  if (n_blocks > 1) fetch_meta<D, BN>(p, meta, b, 1 < n_mem, block_start(1), mem_len);
+  const int q = q0 + row;
+  const int64_t at = ((int64_t)b * p.H + h) * p.T + q;
+  const float lse2 = q < p.T ? p.lse[at] * LOG2E : -INFINITY;
+  const float dlt = q < p.T ? p.delta[at] : 0.f;
+  cp_async_wait<0>();
+  fence_proxy_async_smem();
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+
+  const uint32_t tmem = *s_tmem;
+  const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
+  constexpr uint32_t ID_S = tc::idesc_bf16(BM, BN, false);
+  constexpr uint32_t ID_DQ = tc::idesc_bf16(BM, D, true);
+  constexpr uint32_t Q_LBO = (BM / 8) * 128, KV_LBO = (BN / 8) * 128;
+  const uint32_t q_addr = smem_u32(sq), do_addr = smem_u32(sdo);
+
+  // S = Q K^T and dP = dO V^T for the block in stage s (both operands K-major over D).
+  auto issue_s_dp = [&](int s) {
+    const uint32_t k_addr = smem_u32(stage_k(s)), v_addr = smem_u32(stage_v(s));
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk)
+      tc::mma_bf16(tmem + C::S_COL, tc::smem_desc(q_addr + kk * 2 * Q_LBO, Q_LBO, 128),
+                   tc::smem_desc(k_addr + kk * 2 * KV_LBO, KV_LBO, 128), ID_S, kk > 0);
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk)
+      tc::mma_bf16(tmem + C::DP_COL, tc::smem_desc(do_addr + kk * 2 * Q_LBO, Q_LBO, 128),
+                   tc::smem_desc(v_addr + kk * 2 * KV_LBO, KV_LBO, 128), ID_S, kk > 0);
+  };
+  // dQ (+)= dS K: A = dS in TMEM (8 columns per 16 keys), B = K tile MN-major (D contiguous).
+  auto issue_dq = [&](int s, bool acc) {
+    const uint32_t k_addr = smem_u32(stage_k(s));
+#pragma unroll
+    for (int kk = 0; kk < BN / 16; ++kk)
+      tc::mma_bf16_ts(tmem + C::DQ_COL, tmem + C::DS_COL + kk * 8, tc::smem_desc(k_addr + kk * 2 * 128, 128, KV_LBO),
+                      ID_DQ, (acc || kk > 0) ? 1u : 0u);
+  };
+
+  if (tid == 0) {
+    issue_s_dp(0);
+    tc::commit(bar);
+  }
+
+  const float sl2 = p.scale * LOG2E;
+  const float2 sl2x2 = make_float2(sl2, sl2), nlse = make_float2(-lse2, -lse2), ndlt = make_float2(-dlt, -dlt);
+  const bool row_live = lse2 != -INFINITY;
+  bool aborted = false;
+  for (int j = 0; j < n_blocks; ++j) {
+    const int s = j & 1;
+    if (!tc::mbar_wait_cycles(bar, (uint32_t)(j & 1), WAIT_CYCLES)) *s_abort = 1;
+    const bool memory = j < n_mem;
+    const int start = block_start(j);
+    if (j + 1 < n_blocks) {
+      load_block<D, BN>(p, meta, stage_k(s ^ 1), stage_v(s ^ 1), svalid + (s ^ 1) * BN, b, kvh, j + 1 < n_mem,
+                        block_start(j + 1));
+      cp_async_commit();
+      if (j + 2 < n_blocks) fetch_meta<D, BN>(p, meta, b, j + 2 < n_mem, block_start(j + 2), mem_len);
+    }
+    const int col0 = half * HB;
+    int lim;
+    const uint8_t* valid = nullptr;
+    if (memory) {
+      lim = mem_len - start - col0;
+    } else {
+      lim = min(p.T, q + 1) - start - col0;
+      if (p.key_valid != nullptr) valid = svalid + s * BN + col0;
+    }
+    const bool masked = lim < HB || valid != nullptr || !row_live;
+    uint32_t rs[32], rdp[32];
+    tc::ld32(tmem + lane + C::S_COL + col0, rs);
+    tc::ld32(tmem + lane + C::DP_COL + col0, rdp);
+    uint32_t w[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float2 sv = make_float2(__uint_as_float(rs[2 * i]), __uint_as_float(rs[2 * i + 1]));
+      if (masked) {
+        const int c = 2 * i;
+        if (!(row_live && c < lim && (valid == nullptr || valid[c] != 0))) sv.x = -INFINITY;
+        if (!(row_live && c + 1 < lim && (valid == nullptr || valid[c + 1] != 0))) sv.y = -INFINITY;
+      }
+      float2 pr = fma2(sv, sl2x2, nlse);
+      pr.x = ex2(pr.x);
+      pr.y = ex2(pr.y);
+      const float2 g = add2(make_float2(__uint_as_float(rdp[2 * i]), __uint_as_float(rdp[2 * i + 1])), ndlt);
+      w[i] = pack_bf16(pr.x * g.x, pr.y * g.y);
+    }
+    tc::st16(tmem + lane + C::DS_COL + half * (HB / 2), w);
+
+    if (j + 1 < n_blocks) cp_async_wait<0>();
+    fence_proxy_async_smem();
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    if (*s_abort) {
+      aborted = true;
+      break;
+    }
+    if (tid == 0) {
+      issue_dq(s, j > 0);
+      if (j + 1 < n_blocks) issue_s_dp(s ^ 1);
+      tc::commit(bar);
+    }
+  }
+
+  if (!aborted) {
+    if (!tc::mbar_wait_cycles(bar, (uint32_t)(n_blocks & 1), WAIT_CYCLES)) aborted = true;
+  }
+  aborted = __syncthreads_or(aborted);
+  if (!aborted) {
+    uint32_t r[32];
+    tc::ld32(tmem + lane + C::DQ_COL + half * 32, r);
+    if (q < p.T) {
+      __nv_bfloat16* dst = p.dq + b * p.dq_batch + (int64_t)q * p.dq_row + h * D + half * 32;
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        uint4 v;
+        v.x = pack_bf16(__uint_as_float(r[i + 0]) * p.scale, __uint_as_float(r[i + 1]) * p.scale);
+        v.y = pack_bf16(__uint_as_float(r[i + 2]) * p.scale, __uint_as_float(r[i + 3]) * p.scale);
+        v.z = pack_bf16(__uint_as_float(r[i + 4]) * p.scale, __uint_as_float(r[i + 5]) * p.scale);
+        v.w = pack_bf16(__uint_as_float(r[i + 6]) * p.scale, __uint_as_float(r[i + 7]) * p.scale);
+        *reinterpret_cast<uint4*>(dst + i) = v;
+      }
+    }
+  } else {
+    if (tid == 0 && p.status != nullptr) atomicExch(p.status, 1);
+    cp_async_wait<0>();
+    tc::mbar_wait_cycles(bar, (uint32_t)(n_blocks & 1), WAIT_CYCLES);
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after();
+    tc::dealloc(tmem, TMEM_COLS);
+  }
+}
+
 template <int D>
 cudaError_t launch(const AttnParams& p, cudaStream_t st) {
   constexpr int smem = Cfg<D>::SMEM;
@@ -398,6 +639,26 @@ cudaError_t launch(const AttnParams& p, cudaStream_t st) {
 
 }  // namespace attn_tc
 }  // namespace pra
+
+// dQ of the backward on tcgen05 (head dim 64, 16-byte aligned rows); cudaErrorNotSupported
+// otherwise.  Needs p.delta (sum_d dO * O per row) computed first.
+cudaError_t pra_attention_bwd_dq_tc(const AttnParams& p, int head_dim, cudaStream_t st) {
+  using namespace pra::attn_tc;
+  auto aligned = [](const void* ptr, int64_t a, int64_t b_) {
+    return (reinterpret_cast<uintptr_t>(ptr) % 16) == 0 && a % 8 == 0 && b_ % 8 == 0;
+  };
+  if (head_dim != 64 || !aligned(p.q, p.q_row, p.q_batch) || !aligned(p.k, p.k_row, p.k_batch) ||
+      !aligned(p.v, p.v_row, p.v_batch) || !aligned(p.dout, p.do_row, p.do_batch) ||
+      !aligned(p.dq, p.dq_row, p.dq_batch))
+    return cudaErrorNotSupported;
+  if (p.mem_idx != nullptr && (!aligned(p.mem_k, p.mem_row, 0) || !aligned(p.mem_v, p.mem_row, 0)))
+    return cudaErrorNotSupported;
+  constexpr int smem = DqCfg::SMEM;
+  PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  dim3 grid(p.H * p.B, (p.T + BM - 1) / BM);
+  bwd_dq_kernel<<<grid, NT, smem, st>>>(p);
+  return cudaGetLastError();
+}
 
 // The tcgen05 forward takes head dims 64 and 128 with 16-byte aligned rows; returns
 // cudaErrorNotSupported for anything else so the caller can use the mma.sync kernel.

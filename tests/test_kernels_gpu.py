@@ -300,3 +300,48 @@ def test_attention_fwd_tcgen05(ext, head_dim, t, lens, logit_scale):
     finite = torch.isfinite(lse_mma)
     assert torch.equal(finite, torch.isfinite(lse_tc))
     assert (lse_tc[finite] - lse_mma[finite]).abs().max().item() < 1e-2 * max(1.0, lse_mma[finite].abs().max().item())
+
+
+@pytest.mark.parametrize("t,lens,logit_scale", [(300, [260, 513], 1.0), (1024, [0, 64], 4.0)])
+def test_attention_bwd_dq_tcgen05(ext, t, lens, logit_scale):
+    """dQ from the tcgen05 backward against fp32 autograd and the mma.sync backward (head dim 64,
+    memory keys, padding mask); dK/dV must not depend on the dQ kernel choice."""
+    b, h, hd = 2, 4, 64
+    d = h * hd
+    qkv = _bf(b, t, 3 * d, seed=21)
+    q, k, v = qkv[..., :d], qkv[..., d:2 * d], qkv[..., 2 * d:]
+    key_valid = torch.ones(b, t, dtype=torch.uint8, device="cuda")
+    key_valid[1, t // 4: t // 3] = 0
+    pool = _bf(1200, 2 * d, seed=22)
+    g = torch.Generator(device="cuda").manual_seed(23)
+    idx = torch.zeros(b, max(lens), dtype=torch.int32, device="cuda")
+    rows = []
+    for r, n in enumerate(lens):
+        sel = torch.randperm(1200, device="cuda", generator=g)[:n].int()
+        idx[r, :n] = sel
+        rows.append(sel.long())
+    mem_len = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    scale = logit_scale / math.sqrt(hd)
+    out, lse = ext.attention_fwd(q, k, v, h, h, hd, pool[:, :d], pool[:, d:], idx, mem_len, key_valid, scale)
+    dout = _bf(b, t, d, seed=24)
+    status = ext.attention_status(0)
+    status.zero_()
+    grads = {}
+    for impl in ("tcgen05", "mma"):
+        ext.set_attention_impl(impl)
+        (grads[impl],) = ext.attention_bwd(dout, q, k, v, out, lse, h, hd, pool[:, :d], pool[:, d:], idx, mem_len,
+                                           key_valid, scale)
+    ext.set_attention_impl("tcgen05")
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    g_tc = grads["tcgen05"].view(b, t, 3, h, hd)
+    g_mma = grads["mma"].view(b, t, 3, h, hd)
+    _close(g_tc[:, :, 0], g_mma[:, :, 0], 2e-2)
+    assert torch.equal(g_tc[:, :, 1:], g_mma[:, :, 1:])
+    qf = q.float().view(b, t, h, hd).requires_grad_(True)
+    mk = [pool[r_, :d].view(-1, h, hd) for r_ in rows]
+    mv = [pool[r_, d:].view(-1, h, hd) for r_ in rows]
+    ref = _attention_reference(qf, k.float().view(b, t, h, hd), v.float().view(b, t, h, hd), mk, mv, key_valid,
+                               scale)
+    ref.backward(dout.float().view(b, t, h, hd))
+    _close(g_tc[:, :, 0], qf.grad, 3e-2)
