@@ -520,6 +520,10 @@ cudaError_t launch_bwd(const Params& p, cudaStream_t st) {
     bwd_dq_kernel<D><<<grid, NT, smem, st>>>(p);
     PRA_RETURN_IF_ERROR(cudaGetLastError());
   }
+  if (pra_attention_get_impl() && p.T > 64) {
+    const cudaError_t e = pra_attention_bwd_dkdv_tc(p, D, st);
+    if (e != cudaErrorNotSupported) return e;
+  }
   {
     const size_t smem = (size_t)(2 * BN + 4 * BM) * LD * sizeof(__nv_bfloat16) + 4 * BM * sizeof(float);
     PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(bwd_dkdv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

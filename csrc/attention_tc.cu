@@ -628,6 +628,217 @@ __global__ void __launch_bounds__(NT, 2) bwd_dq_kernel(AttnParams p) {
   }
 }
 
+// ---- backward: dK, dV of the local keys ---------------------------------------------------
+// One CTA owns 128 local keys of one (batch row, head) (TMEM lane = key) and walks the query
+// blocks of 32 that can see them (causal), head dim 64, MHA:
+//   S^T = K Q^T, dP^T = V dO^T        -> TMEM buffer x = block parity: [64 x, 64 x + 32), [64 x + 32, 64 x + 64)
+//   P^T = exp2(S^T scale log2e - lse log2e), dS^T = P^T (dP^T - delta), written as bf16 pairs
+//         over the first half of each thread's own S^T / dP^T columns
+//   dV += P^T dO, dK += dS^T Q         -> TMEM [128, 192), [192, 256)
+// The two S^T / dP^T buffers alternate, so the next block's MMAs never write columns that the
+// previous block's dV / dK MMAs read (tcgen05 MMAs into different accumulators are not
+// ordered); a buffer is reused two blocks later, after the commit that covers those reads.
+// Two threads per key row (16 query columns each); lse and delta of a block staged in shared
+// memory.  dK = scale * (dS^T Q).
+struct DkvCfg {
+  static constexpr int D = 64, BK = 128, BQ = 32, HQ = 16;
+  static constexpr int KV_BYTES = BK * D * 2, QB_BYTES = BQ * D * 2;
+  static constexpr int OFF_V = KV_BYTES, OFF_Q = 2 * KV_BYTES;  // stage s: Q at OFF_Q + 2 s QB, dO after it
+  static constexpr int OFF_LSE = OFF_Q + 4 * QB_BYTES;           // [2][BQ] lse * log2e, then [2][BQ] delta
+  static constexpr int OFF_BAR = OFF_LSE + 4 * BQ * 4;
+  static constexpr int SMEM = OFF_BAR + 16;
+  static constexpr int DV_COL = 128, DK_COL = 192;
+};
+
+__global__ void __launch_bounds__(NT, 2) bwd_dkdv_kernel(AttnParams p) {
+  using C = DkvCfg;
+  constexpr int D = C::D, BK = C::BK, BQ = C::BQ, HQ = C::HQ;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* sk = smem;
+  uint8_t* sv = smem + C::OFF_V;
+  float* s_lse = reinterpret_cast<float*>(smem + C::OFF_LSE);
+  float* s_dlt = s_lse + 2 * BQ;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + 8);
+  int* s_abort = reinterpret_cast<int*>(smem + C::OFF_BAR + 12);
+  auto stage_q = [&](int s) { return smem + C::OFF_Q + s * 2 * C::QB_BYTES; };
+  auto stage_do = [&](int s) { return smem + C::OFF_Q + s * 2 * C::QB_BYTES + C::QB_BYTES; };
+
+  // grid (H * B, key tiles): the first key tiles (seen by the most queries) are scheduled first
+  const int h = blockIdx.x % p.H, b = blockIdx.x / p.H;
+  const int k0 = blockIdx.y * BK;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int row = tid & (BK - 1), half = tid >> 7;
+  const int first_q = k0 / BQ;
+  const int n_blocks = (p.T + BQ - 1) / BQ - first_q;
+
+  if (warp == 0) {
+    tc::alloc(s_tmem, TMEM_COLS);
+    tc::relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    *s_abort = 0;
+    tc::fence_mbarrier_init();
+  }
+  load_query_rows<D>(sk, p.k, p.k_row, p.k_batch, b, h, k0, p.T);  // 128 key rows, same tile shape as a query tile
+  load_query_rows<D>(sv, p.v, p.v_row, p.v_batch, b, h, k0, p.T);
+  // Q / dO rows of query block qi (32 rows x 8 chunks: one 16-byte chunk per thread each) and its lse / delta
+  auto load_qblock = [&](int qi, int s) {
+    const int qs = qi * BQ;
+    const int c = (tid >> 3) & 7, r = (tid >> 6) * 8 + (tid & 7), t = qs + r;
+    const bool ok = t < p.T;
+    const uint32_t o = tc::core_off(r, c, BQ);
+    cp_async16(stage_q(s) + o, ok ? p.q + b * p.q_batch + (int64_t)t * p.q_row + h * D + c * 8 : p.q, ok);
+    cp_async16(stage_do(s) + o, ok ? p.dout + b * p.do_batch + (int64_t)t * p.do_row + h * D + c * 8 : p.dout, ok);
+    if (tid < BQ) {
+      const int tq = qs + tid;
+      const int64_t at = ((int64_t)b * p.H + h) * p.T + tq;
+      s_lse[s * BQ + tid] = tq < p.T ? p.lse[at] * LOG2E : -INFINITY;
+      s_dlt[s * BQ + tid] = tq < p.T ? p.delta[at] : 0.f;
+    }
+  };
+  load_qblock(first_q, 0);
+  cp_async_commit();
+  const int key = k0 + row;
+  const bool key_ok = key < p.T && (p.key_valid == nullptr || p.key_valid[(int64_t)b * p.T + key] != 0);
+  cp_async_wait<0>();
+  fence_proxy_async_smem();
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+
+  const uint32_t tmem = *s_tmem;
+  const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
+  constexpr uint32_t ID_ST = tc::idesc_bf16(BK, BQ, false);
+  constexpr uint32_t ID_G = tc::idesc_bf16(BK, D, true);
+  constexpr uint32_t K_LBO = (BK / 8) * 128, QB_LBO = (BQ / 8) * 128;
+  const uint32_t k_addr = smem_u32(sk), v_addr = smem_u32(sv);
+  auto st_col = [&](int x) { return (uint32_t)(64 * x); };
+  auto dpt_col = [&](int x) { return (uint32_t)(64 * x + 32); };
+
+  // S^T = K Q^T and dP^T = V dO^T for the query block in stage s (all operands K-major over D).
+  auto issue_st = [&](int s, int x) {
+    const uint32_t q_addr = smem_u32(stage_q(s)), do_addr = smem_u32(stage_do(s));
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk)
+      tc::mma_bf16(tmem + st_col(x), tc::smem_desc(k_addr + kk * 2 * K_LBO, K_LBO, 128),
+                   tc::smem_desc(q_addr + kk * 2 * QB_LBO, QB_LBO, 128), ID_ST, kk > 0);
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk)
+      tc::mma_bf16(tmem + dpt_col(x), tc::smem_desc(v_addr + kk * 2 * K_LBO, K_LBO, 128),
+                   tc::smem_desc(do_addr + kk * 2 * QB_LBO, QB_LBO, 128), ID_ST, kk > 0);
+  };
+  // dV += P^T dO, dK += dS^T Q: A from TMEM (query columns 16 kk .. 16 kk + 15 packed at column
+  // 16 kk of the thread pair's buffer), B = dO / Q stage MN-major (D contiguous).
+  auto issue_grad = [&](int s, int x, bool acc) {
+    const uint32_t q_addr = smem_u32(stage_q(s)), do_addr = smem_u32(stage_do(s));
+#pragma unroll
+    for (int kk = 0; kk < BQ / 16; ++kk)
+      tc::mma_bf16_ts(tmem + C::DV_COL, tmem + st_col(x) + kk * 16,
+                      tc::smem_desc(do_addr + kk * 2 * 128, 128, QB_LBO), ID_G, (acc || kk > 0) ? 1u : 0u);
+#pragma unroll
+    for (int kk = 0; kk < BQ / 16; ++kk)
+      tc::mma_bf16_ts(tmem + C::DK_COL, tmem + dpt_col(x) + kk * 16,
+                      tc::smem_desc(q_addr + kk * 2 * 128, 128, QB_LBO), ID_G, (acc || kk > 0) ? 1u : 0u);
+  };
+
+  if (tid == 0) {
+    issue_st(0, 0);
+    tc::commit(bar);
+  }
+
+  const float sl2 = p.scale * LOG2E;
+  const float2 sl2x2 = make_float2(sl2, sl2);
+  bool aborted = false;
+  for (int j = 0; j < n_blocks; ++j) {
+    const int s = j & 1, x = j & 1;
+    const int qs = (first_q + j) * BQ;
+    if (!tc::mbar_wait_cycles(bar, (uint32_t)(j & 1), WAIT_CYCLES)) *s_abort = 1;
+    if (j + 1 < n_blocks) {
+      load_qblock(first_q + j + 1, s ^ 1);
+      cp_async_commit();
+    }
+    const int c0 = half * HQ;  // this thread's query columns c0 .. c0 + 15
+    uint32_t rs[16], rdp[16];
+    tc::ld16(tmem + lane + st_col(x) + c0, rs);
+    tc::ld16(tmem + lane + dpt_col(x) + c0, rdp);
+    const float* lse_b = s_lse + s * BQ + c0;
+    const float* dlt_b = s_dlt + s * BQ + c0;
+    uint32_t wp[8], wd[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int c = 2 * i;
+      const int qa = qs + c0 + c;
+      const bool va = key_ok && qa < p.T && key <= qa && lse_b[c] != -INFINITY;
+      const bool vb = key_ok && qa + 1 < p.T && key <= qa + 1 && lse_b[c + 1] != -INFINITY;
+      float2 sv = make_float2(va ? __uint_as_float(rs[c]) : -INFINITY, vb ? __uint_as_float(rs[c + 1]) : -INFINITY);
+      float2 pr = fma2(sv, sl2x2, make_float2(va ? -lse_b[c] : 0.f, vb ? -lse_b[c + 1] : 0.f));
+      pr.x = ex2(pr.x);
+      pr.y = ex2(pr.y);
+      const float2 g = add2(make_float2(__uint_as_float(rdp[c]), __uint_as_float(rdp[c + 1])),
+                            make_float2(-dlt_b[c], -dlt_b[c + 1]));
+      wp[i] = pack_bf16(pr.x, pr.y);
+      wd[i] = pack_bf16(pr.x * g.x, pr.y * g.y);
+    }
+    tc::st8(tmem + lane + st_col(x) + c0, wp);
+    tc::st8(tmem + lane + dpt_col(x) + c0, wd);
+
+    if (j + 1 < n_blocks) cp_async_wait<0>();
+    fence_proxy_async_smem();
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    if (*s_abort) {
+      aborted = true;
+      break;
+    }
+    if (tid == 0) {
+      issue_grad(s, x, j > 0);
+      if (j + 1 < n_blocks) issue_st(s ^ 1, x ^ 1);
+      tc::commit(bar);
+    }
+  }
+
+  if (!aborted) {
+    if (!tc::mbar_wait_cycles(bar, (uint32_t)(n_blocks & 1), WAIT_CYCLES)) aborted = true;
+  }
+  aborted = __syncthreads_or(aborted);
+  if (!aborted) {
+    uint32_t rv[32], rk[32];
+    tc::ld32(tmem + lane + C::DV_COL + half * 32, rv);
+    tc::ld32(tmem + lane + C::DK_COL + half * 32, rk);
+    if (key < p.T) {
+      __nv_bfloat16* vd = p.dv + b * p.dv_batch + (int64_t)key * p.dv_row + h * D + half * 32;
+      __nv_bfloat16* kd = p.dk + b * p.dk_batch + (int64_t)key * p.dk_row + h * D + half * 32;
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        uint4 a, c;
+        a.x = pack_bf16(__uint_as_float(rv[i + 0]), __uint_as_float(rv[i + 1]));
+        a.y = pack_bf16(__uint_as_float(rv[i + 2]), __uint_as_float(rv[i + 3]));
+        a.z = pack_bf16(__uint_as_float(rv[i + 4]), __uint_as_float(rv[i + 5]));
+        a.w = pack_bf16(__uint_as_float(rv[i + 6]), __uint_as_float(rv[i + 7]));
+        c.x = pack_bf16(__uint_as_float(rk[i + 0]) * p.scale, __uint_as_float(rk[i + 1]) * p.scale);
+        c.y = pack_bf16(__uint_as_float(rk[i + 2]) * p.scale, __uint_as_float(rk[i + 3]) * p.scale);
+        c.z = pack_bf16(__uint_as_float(rk[i + 4]) * p.scale, __uint_as_float(rk[i + 5]) * p.scale);
+        c.w = pack_bf16(__uint_as_float(rk[i + 6]) * p.scale, __uint_as_float(rk[i + 7]) * p.scale);
+        *reinterpret_cast<uint4*>(vd + i) = a;
+        *reinterpret_cast<uint4*>(kd + i) = c;
+      }
+    }
+  } else {
+    if (tid == 0 && p.status != nullptr) atomicExch(p.status, 1);
+    cp_async_wait<0>();
+    tc::mbar_wait_cycles(bar, (uint32_t)(n_blocks & 1), WAIT_CYCLES);
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after();
+    tc::dealloc(tmem, TMEM_COLS);
+  }
+}
+
 template <int D>
 cudaError_t launch(const AttnParams& p, cudaStream_t st) {
   constexpr int smem = Cfg<D>::SMEM;
@@ -657,6 +868,24 @@ cudaError_t pra_attention_bwd_dq_tc(const AttnParams& p, int head_dim, cudaStrea
   PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   dim3 grid(p.H * p.B, (p.T + BM - 1) / BM);
   bwd_dq_kernel<<<grid, NT, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+// dK / dV of the local keys on tcgen05 (head dim 64, MHA, 16-byte aligned rows);
+// cudaErrorNotSupported otherwise.  Needs p.delta.
+cudaError_t pra_attention_bwd_dkdv_tc(const AttnParams& p, int head_dim, cudaStream_t st) {
+  using namespace pra::attn_tc;
+  auto aligned = [](const void* ptr, int64_t a, int64_t b_) {
+    return (reinterpret_cast<uintptr_t>(ptr) % 16) == 0 && a % 8 == 0 && b_ % 8 == 0;
+  };
+  if (head_dim != 64 || p.H != p.Hkv || !aligned(p.q, p.q_row, p.q_batch) || !aligned(p.k, p.k_row, p.k_batch) ||
+      !aligned(p.v, p.v_row, p.v_batch) || !aligned(p.dout, p.do_row, p.do_batch) ||
+      !aligned(p.dk, p.dk_row, p.dk_batch) || !aligned(p.dv, p.dv_row, p.dv_batch))
+    return cudaErrorNotSupported;
+  constexpr int smem = DkvCfg::SMEM;
+  PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  dim3 grid(p.H * p.B, (p.T + DkvCfg::BK - 1) / DkvCfg::BK);
+  bwd_dkdv_kernel<<<grid, NT, smem, st>>>(p);
   return cudaGetLastError();
 }
 

@@ -36,6 +36,8 @@ cudaError_t pra_attention_fwd(const AttnParams& p, int head_dim, cudaStream_t st
 cudaError_t pra_attention_fwd_tc(const AttnParams& p, int head_dim, cudaStream_t stream);
 // dQ of the backward on tcgen05 (head dim 64); cudaErrorNotSupported otherwise.
 cudaError_t pra_attention_bwd_dq_tc(const AttnParams& p, int head_dim, cudaStream_t stream);
+// dK / dV of the local keys on tcgen05 (head dim 64, MHA); cudaErrorNotSupported otherwise.
+cudaError_t pra_attention_bwd_dkdv_tc(const AttnParams& p, int head_dim, cudaStream_t stream);
 // Forward implementation: 1 = tcgen05 where supported (default), 0 = mma.sync everywhere.
 void pra_attention_set_impl(int tcgen05);
 int pra_attention_get_impl();

@@ -122,6 +122,22 @@ __device__ __forceinline__ void st16(uint32_t taddr, const uint32_t (&r)[16]) {
                : "memory");
 }
 
+// Warp-wide: thread i reads 16 consecutive 32-bit columns of TMEM lane (lane base + i).
+__device__ __forceinline__ void ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n"
+               "tcgen05.wait::ld.sync.aligned;\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+               : "r"(taddr));
+}
+
+// Warp-wide: thread i writes 8 consecutive 32-bit columns of TMEM lane (lane base + i),
+// waiting for the store to complete.
+__device__ __forceinline__ void st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};\n"
+               "tcgen05.wait::st.sync.aligned;\n" ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+
 // Bounded wait on an mbarrier phase: false once `max_cycles` SM clock cycles have passed.
 __device__ __forceinline__ bool mbar_wait_cycles(uint64_t* bar, uint32_t parity, long long max_cycles) {
   const long long t0 = clock64();
