@@ -185,10 +185,15 @@ def run(impl: str, steps: int, warmup: int, gpus: int) -> dict:
         _sync_all(world)
         wall0 = time.perf_counter()
         start_evt.record()
+        host_s = 0.0
         for i in range(warmup, total_steps):
+            t_host = time.perf_counter()
             loss_host, moved, read = step_fn(batches[i], upcoming(i))
+            host_s += time.perf_counter() - t_host
             h2d += moved
             d2h += read
+        if step_fn.flush is not None:
+            loss_host = step_fn.flush()
         end_evt.record()
         _sync_all(world)
         wall = time.perf_counter() - wall0
@@ -221,6 +226,7 @@ def run(impl: str, steps: int, warmup: int, gpus: int) -> dict:
         "e2e": {"value": total_tokens / wall_s, "unit": "tokens/s", "h2d_bytes_per_step": h2d // max(steps, 1),
                 "d2h_bytes_per_step": d2h // max(steps, 1)},
         "gpu_launches": (counter.launches if counter is not None else 0),
+        "host_ms_per_step": 1000.0 * _max(host_s, world) / steps,  # time inside the step call on the host
         "last_loss": loss_host,
     }
     if impl == "reference":
@@ -235,10 +241,11 @@ def run(impl: str, steps: int, warmup: int, gpus: int) -> dict:
 
 
 class _Step:
-    def __init__(self, fn, batch_source, close=None):
+    def __init__(self, fn, batch_source, close=None, flush=None):
         self.fn = fn
         self.batches = batch_source
         self.close = close or (lambda: None)
+        self.flush = flush  # returns the last step's host-read result, if reads lag one step
 
     def __call__(self, batch, next_batch=None):
         return self.fn(batch, next_batch)
@@ -266,6 +273,19 @@ def _pra_arm(root: Path, tokenizer, rank: int, world: int):
     optimizer = model.build_optimizer(TrainConfig(device="cuda", learning_rate=3e-4))
     reducer = attach_data_parallel(model, optimizer, world)
     resolver = ResolverServiceConfig()
+    # The loss of step i is copied to pinned host memory on the stream and read after step
+    # i + 1 has been queued, so the host never waits for the GPU between steps.
+    host_loss = [torch.zeros((), dtype=torch.float32).pin_memory() for _ in range(2)]
+    done = [torch.cuda.Event(), torch.cuda.Event()]
+    pending = {"slot": None, "value": float("nan")}
+
+    def read_pending():
+        slot = pending["slot"]
+        if slot is not None:
+            done[slot].synchronize()
+            pending["value"] = float(host_loss[slot])
+            pending["slot"] = None
+        return pending["value"]
 
     def step(batch, next_batch=None):
         dev_batch = dict(batch)
@@ -273,8 +293,13 @@ def _pra_arm(root: Path, tokenizer, rank: int, world: int):
             dev_batch[key] = batch[key].to("cuda", non_blocking=True)
         loss, _ = training_step(model, dev_batch, "cuda", tokenizer, optimizer, resolver_config=resolver,
                                 next_batch=next_batch)
-        value = float(loss.detach().float().item())
-        return value, _moved_bytes(batch), 4
+        previous = read_pending()
+        slot = 0 if pending.get("last", 1) == 1 else 1
+        pending["last"] = slot
+        host_loss[slot].copy_(loss.detach().float(), non_blocking=True)
+        done[slot].record()
+        pending["slot"] = slot
+        return previous, _moved_bytes(batch), 4
 
     params = sum(p.numel() for p in model.parameters())
     def close():
@@ -283,8 +308,8 @@ def _pra_arm(root: Path, tokenizer, rank: int, world: int):
             if hasattr(reducer, "close"):
                 reducer.close()
 
-    return (_Step(step, lambda n: _batches(dm, rank, world, n), close), f"TinyGPT-PRA-{params / 1e6:.0f}M",
-            launch_counter())
+    return (_Step(step, lambda n: _batches(dm, rank, world, n), close, read_pending),
+            f"TinyGPT-PRA-{params / 1e6:.0f}M", launch_counter())
 
 
 def _reference_arm(root: Path, tokenizer, rank: int, world: int):

@@ -902,6 +902,184 @@ std::vector<torch::Tensor> stack_forward(torch::Tensor x, int64_t B, int64_t T, 
   return out;
 }
 
+// ---------------------------------------------------------------- block stack with gradients
+// The same per-layer math as stack_forward (pre-norm blocks: LN -> QKV -> [route] -> attention
+// -> O + residual -> LN -> GELU MLP + residual), keeping what the backward needs, so one
+// autograd node covers the whole stack instead of six per layer.
+constexpr int kSavedPerLayer = 15;  // x, mean1, rstd1, h, qkv, a, lse, x1, mean2, rstd2, h2, z, u, mem_idx, mem_len
+
+// Returns {x_out, [4 routing tensors per layer when routed], kSavedPerLayer tensors per layer}.
+std::vector<torch::Tensor> stack_train_forward(torch::Tensor x, int64_t B, int64_t T, std::vector<torch::Tensor> weights,
+                                               int64_t heads, int64_t head_dim, double eps,
+                                               c10::optional<torch::Tensor> key_valid,
+                                               c10::optional<torch::Tensor> mem_pool, std::vector<torch::Tensor> ns,
+                                               c10::optional<torch::Tensor> gists,
+                                               c10::optional<torch::Tensor> gist_count,
+                                               c10::optional<torch::Tensor> gist_kv,
+                                               c10::optional<torch::Tensor> budget_rows,
+                                               c10::optional<torch::Tensor> query_rows, std::vector<double> route_cfg) {
+  c10::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(weights.size() % 12 == 0, "stack_train_forward needs 12 weight tensors per layer");
+  const int64_t L = weights.size() / 12;
+  const int64_t D = heads * head_dim;
+  const int64_t M = B * T;
+  TORCH_CHECK(x.dim() == 2 && x.size(0) == M && x.size(1) == D && x.is_contiguous(), "x must be [B*T, D]");
+  const bool routed = !ns.empty();
+  if (routed) {
+    TORCH_CHECK(ns.size() == 9 && gists.has_value() && gist_count.has_value() && route_cfg.size() == 11,
+                "routing needs 9 namespace tensors, gists, gist_count and 11 settings");
+    TORCH_CHECK(mem_pool.has_value() || gist_kv.has_value(), "routing needs the memory K/V pool");
+  }
+  const bool gist_only = routed && route_cfg[6] != 0.0;
+  const double scale = 1.0 / std::sqrt((double)head_dim);
+  auto none = torch::empty({0}, x.options().dtype(at::kInt));
+  auto last_rows = query_rows.has_value()
+                       ? *query_rows
+                       : torch::full({B}, (int)(T - 1), x.options().dtype(at::kInt));
+  std::vector<torch::Tensor> routing, saved;
+  saved.reserve(L * kSavedPerLayer);
+  for (int64_t l = 0; l < L; ++l) {
+    const torch::Tensor* w = weights.data() + 12 * l;
+    auto n1 = norm_fwd(x, w[0], w[1], eps, false);
+    auto qkv = torch::empty({M, 3 * D}, x.options());
+    gemm("tn", n1[0], w[2], c10::nullopt, qkv, w[3], c10::nullopt, 1.0, 0.0, c10::nullopt);
+    auto qkv3 = qkv.view({B, T, 3 * D});
+    c10::optional<torch::Tensor> mk, mv, mi, ml;
+    torch::Tensor mi_s = none, ml_s = none;
+    if (routed) {
+      auto r = route(qkv3.narrow(2, 0, D), gists->select(0, l), gist_count->select(0, l), ns[0], ns[1], ns[2], ns[3],
+                     ns[4], ns[5], ns[6], ns[7], ns[8], (int64_t)route_cfg[0], (int64_t)route_cfg[1],
+                     (int64_t)route_cfg[2], (int64_t)route_cfg[3], route_cfg[4], (int64_t)route_cfg[5], gist_only,
+                     route_cfg[7] != 0.0, route_cfg[8] != 0.0, (int64_t)route_cfg[9], (int64_t)route_cfg[10],
+                     budget_rows, last_rows);
+      if (gist_only) {
+        mk = gist_kv->select(0, 0).select(0, l);
+        mv = gist_kv->select(0, 1).select(0, l);
+      } else {
+        auto layer_pool = mem_pool->select(0, l);
+        mk = layer_pool.narrow(1, D, D);
+        mv = layer_pool.narrow(1, 2 * D, D);
+      }
+      mi = r[0];
+      ml = r[1].select(0, 0);
+      mi_s = r[0];
+      ml_s = r[1].select(0, 0);
+      routing.insert(routing.end(), r.begin(), r.end());
+    }
+    auto att = attention_fwd(qkv3.narrow(2, 0, D), qkv3.narrow(2, D, D), qkv3.narrow(2, 2 * D, D), heads, heads,
+                             head_dim, mk, mv, mi, ml, key_valid, scale);
+    auto a = att[0];
+    auto x1 = torch::empty_like(x);
+    gemm("tn", a.view({M, D}), w[4], x, x1, w[5], c10::nullopt, 1.0, 1.0, c10::nullopt);
+    auto n2 = norm_fwd(x1, w[6], w[7], eps, false);
+    const int64_t F = w[8].size(0);
+    auto z = torch::empty({M, F}, x.options()), u = torch::empty({M, F}, x.options());
+    gemm("tn_gelu", n2[0], w[8], c10::nullopt, u, w[9], z, 1.0, 0.0, c10::nullopt);
+    auto x2 = torch::empty_like(x);
+    gemm("tn", u, w[10], x1, x2, w[11], c10::nullopt, 1.0, 1.0, c10::nullopt);
+    for (auto& t : {x, n1[1], n1[2], n1[0], qkv, a, att[1], x1, n2[1], n2[2], n2[0], z, u, mi_s, ml_s})
+      saved.push_back(t);
+    x = x2;
+  }
+  std::vector<torch::Tensor> out{x};
+  out.insert(out.end(), routing.begin(), routing.end());
+  out.insert(out.end(), saved.begin(), saved.end());
+  return out;
+}
+
+// g (+)= colsum(dy) into a bias-gradient view.
+static void bias_grad(const torch::Tensor& dy, torch::Tensor& gb, double beta) {
+  if (!gb.defined() || gb.numel() == 0) return;
+  auto s = colsum(dy);
+  if (beta == 0.0) gb.copy_(s);
+  else gb.add_(s);
+}
+
+// gw (+)= dy^T x, gb (+)= colsum(dy).
+static void weight_grad(const torch::Tensor& dy, const torch::Tensor& x, torch::Tensor& gw, torch::Tensor& gb,
+                        double beta) {
+  if (gw.defined() && gw.numel() > 0)
+    gemm("wgrad", dy, x, beta != 0.0 ? c10::optional<torch::Tensor>(gw) : c10::nullopt, gw, c10::nullopt,
+         c10::nullopt, 1.0, beta, c10::nullopt);
+  bias_grad(dy, gb, beta);
+}
+
+// LayerNorm backward with the residual gradient added (dx = LN'(dh) + dres); norm weight and
+// bias gradients written (beta = 0) or added (beta = 1) into their views.
+static torch::Tensor norm_grad(const torch::Tensor& dh, const torch::Tensor& x, const torch::Tensor& w,
+                               const torch::Tensor& mean, const torch::Tensor& rstd, const torch::Tensor& dres,
+                               torch::Tensor& gw, torch::Tensor& gb, double beta) {
+  auto r = norm_bwd(dh, x, w, mean, rstd, dres, false);
+  if (gw.defined() && gw.numel() > 0) {
+    if (beta == 0.0) gw.copy_(r[1]);
+    else gw.add_(r[1]);
+  }
+  if (gb.defined() && gb.numel() > 0) {
+    if (beta == 0.0) gb.copy_(r[2]);
+    else gb.add_(r[2]);
+  }
+  return r[0];
+}
+
+// Backward of stack_train_forward: dy of the stack output -> dx of its input; weight
+// gradients into `grads` (12 per layer, aligned with `weights`; undefined/empty = none).
+torch::Tensor stack_train_backward(torch::Tensor dy, int64_t B, int64_t T, std::vector<torch::Tensor> weights,
+                                   std::vector<torch::Tensor> grads, double beta, int64_t heads, int64_t head_dim,
+                                   c10::optional<torch::Tensor> key_valid, std::vector<torch::Tensor> saved,
+                                   c10::optional<torch::Tensor> mem_pool, c10::optional<torch::Tensor> gist_kv,
+                                   bool gist_only) {
+  c10::cuda::CUDAGuard guard(dy.device());
+  const int64_t L = weights.size() / 12;
+  TORCH_CHECK(grads.size() == weights.size() && (int64_t)saved.size() == L * kSavedPerLayer,
+              "stack_train_backward: grads / saved tensors do not match the stack");
+  const int64_t D = heads * head_dim;
+  const int64_t M = B * T;
+  const double scale = 1.0 / std::sqrt((double)head_dim);
+  dy = dy.contiguous();
+  for (int64_t l = L - 1; l >= 0; --l) {
+    const torch::Tensor* w = weights.data() + 12 * l;
+    torch::Tensor* g = grads.data() + 12 * l;
+    const torch::Tensor* s = saved.data() + kSavedPerLayer * l;
+    const auto &x = s[0], &mean1 = s[1], &rstd1 = s[2], &h = s[3], &qkv = s[4], &a = s[5], &lse = s[6], &x1 = s[7],
+               &mean2 = s[8], &rstd2 = s[9], &h2 = s[10], &z = s[11], &u = s[12], &mi = s[13], &ml = s[14];
+    // MLP: y = x1 + gelu(h2 W1^T + b1) W2^T + b2
+    auto dz = torch::empty_like(z);
+    gemm("nn_dgelu", dy, w[10], c10::nullopt, dz, c10::nullopt, z, 1.0, 0.0, c10::nullopt);
+    weight_grad(dy, u, g[10], g[11], beta);
+    auto dh2 = torch::empty_like(h2);
+    gemm("nn", dz, w[8], c10::nullopt, dh2, c10::nullopt, c10::nullopt, 1.0, 0.0, c10::nullopt);
+    weight_grad(dz, h2, g[8], g[9], beta);
+    auto dx1 = norm_grad(dh2, x1, w[6], mean2, rstd2, dy, g[6], g[7], beta);
+    // O projection: x1 = x + a W_o^T + b_o
+    auto da = torch::empty({M, D}, dy.options());
+    gemm("nn", dx1, w[4], c10::nullopt, da, c10::nullopt, c10::nullopt, 1.0, 0.0, c10::nullopt);
+    weight_grad(dx1, a.view({M, D}), g[4], g[5], beta);
+    // attention
+    auto qkv3 = qkv.view({B, T, 3 * D});
+    c10::optional<torch::Tensor> mk, mv, mio, mlo;
+    if (mi.numel() > 0) {
+      if (gist_only) {
+        mk = gist_kv->select(0, 0).select(0, l);
+        mv = gist_kv->select(0, 1).select(0, l);
+      } else {
+        auto layer_pool = mem_pool->select(0, l);
+        mk = layer_pool.narrow(1, D, D);
+        mv = layer_pool.narrow(1, 2 * D, D);
+      }
+      mio = mi;
+      mlo = ml;
+    }
+    auto dqkv = attention_bwd(da.view({B, T, D}), qkv3.narrow(2, 0, D), qkv3.narrow(2, D, D),
+                              qkv3.narrow(2, 2 * D, D), a, lse, heads, head_dim, mk, mv, mio, mlo, key_valid,
+                              scale)[0].view({M, 3 * D});
+    auto dh = torch::empty_like(h);
+    gemm("nn", dqkv, w[2], c10::nullopt, dh, c10::nullopt, c10::nullopt, 1.0, 0.0, c10::nullopt);
+    weight_grad(dqkv, h, g[2], g[3], beta);
+    dy = norm_grad(dh, x, w[0], mean1, rstd1, dx1, g[0], g[1], beta);
+  }
+  return dy;
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "PRA sm_100a kernels";
   m.def("attention_fwd", &attention_fwd);
@@ -925,6 +1103,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gist_kmeans_into", &gist_kmeans_into);
   m.def("route", &route);
   m.def("stack_forward", &stack_forward);
+  m.def("stack_train_forward", &stack_train_forward);
+  m.def("stack_train_backward", &stack_train_backward);
   m.def("dp_allreduce", &dp_allreduce);
   m.def("rope_copy", &rope_copy);
   m.def("tp_allreduce", &tp_allreduce);

@@ -25,6 +25,7 @@ residency, head widths other than 32/64/128) keep using the object path.
 from __future__ import annotations
 
 import math
+import os
 import time
 from dataclasses import dataclass, field
 
@@ -502,6 +503,8 @@ class DeviceRuntime:
         if not torch.is_grad_enabled():
             return self._run_blocks_native(x, b, t, key_valid, routing, memory, stop_after_kv, pool_rows, budget,
                                            query_rows)
+        if pool_rows is None and not stop_after_kv and _NATIVE_TRAIN_STACK:
+            return _TrainStack.apply(x, self, b, t, key_valid, routing, memory, budget, query_rows)
         for li, layer in enumerate(self.layers):
             h = layer_norm(x, layer["ln1"])
             if pool_rows is not None:
@@ -860,6 +863,67 @@ class _Unsupported(RuntimeError):
     pass
 
 
+# The prompt's block stack with gradients runs as ONE autograd node over the native
+# stack_train_forward / stack_train_backward (the same kernels in the same order as the
+# per-layer autograd functions); PRA_TRAIN_STACK=python selects the per-layer path.
+_NATIVE_TRAIN_STACK = os.environ.get("PRA_TRAIN_STACK", "native").lower() != "python"
+
+
+class _TrainStack(torch.autograd.Function):
+    """x [b*t, D] -> the block stack's output; weight gradients land in the flat buffer."""
+
+    @staticmethod
+    def forward(ctx, x, rt: "DeviceRuntime", b: int, t: int, key_valid, routing, memory, budget, query_rows):
+        cfg = rt.cfg
+        d = cfg.d_model
+        ext = _ext.require()
+        routed = routing is not None and not routing.empty
+        ns, gists, counts, gist_kv, budget_rows, settings = [], None, None, None, None, []
+        if routed:
+            ns = [routing.row_pos_off, routing.row_ref_off, routing.ref_pos_off, routing.pos_chunk, routing.pos_ref,
+                  routing.pos_rank, memory.chunk_start, memory.chunk_len, memory.chunk_pool_row]
+            gists, counts = memory.gists_all, memory.gist_count_all
+            settings, budget_rows = rt._route_settings(budget)
+            if cfg.detail_materialization == "gist_only":
+                gist_kv = torch.stack([memory.gist_k_all, memory.gist_v_all]).view(
+                    2, cfg.n_layers, -1, d).bfloat16()
+        mem_pool = memory.pool if routed else None
+        out = ext.stack_train_forward(x.contiguous(), b, t, rt._stack_weights(), cfg.n_heads, rt.head_dim, 1e-5,
+                                      key_valid, mem_pool, ns, gists, counts, gist_kv, budget_rows, query_rows,
+                                      settings)
+        n_layers = cfg.n_layers
+        _ext.add_launches("stack_train_forward", n_layers * (7 + (1 if routed else 0)))
+        pos = 1
+        if routed:
+            for li in range(n_layers):
+                mem_idx, ints, sel_i, sel_f = out[pos: pos + 4]
+                rt.last_routing[li] = LayerRouting(mem_idx, ints, sel_i, sel_f)
+                pos += 4
+        ctx.rt, ctx.b, ctx.t = rt, b, t
+        ctx.key_valid, ctx.mem_pool, ctx.gist_kv = key_valid, mem_pool, gist_kv
+        ctx.gist_only = bool(routed and settings[6])
+        ctx.saved = out[pos:]
+        return out[0]
+
+    @staticmethod
+    def backward(ctx, dy):
+        rt = ctx.rt
+        slots = [layer[name] for layer in rt.layers for name in ("ln1", "qkv", "o", "ln2", "up", "down")]
+        betas = {s.grad_beta() for s in slots}
+        if len(betas) != 1:
+            raise RuntimeError("block-stack gradients are partly accumulated: zero_grad between steps")
+        empty = torch.empty(0, device=dy.device, dtype=torch.bfloat16)
+        grads = []
+        for s in slots:
+            grads += [s.gw if s.gw is not None else empty, s.gb if s.gb is not None else empty]
+        dx = _ext.require().stack_train_backward(dy.contiguous(), ctx.b, ctx.t, rt._stack_weights(), grads,
+                                                 betas.pop(), rt.cfg.n_heads, rt.head_dim, ctx.key_valid, ctx.saved,
+                                                 ctx.mem_pool, ctx.gist_kv, ctx.gist_only)
+        ctx.saved = None
+        _ext.add_launches("stack_train_backward", 25 * rt.cfg.n_layers)
+        return dx, None, None, None, None, None, None, None, None
+
+
 class _Embed(torch.autograd.Function):
     """x = token_emb[ids] + pos_emb[positions] (bf16); gradients land in the flat buffer."""
 
@@ -963,7 +1027,9 @@ def device_batch_step(model, batch, device, tokenizer, resolver_config, cache_co
     loss = rt.loss(hidden, labels)
     if rt.upcoming is not None:  # first half of the next batch's host planning overlaps this forward
         rt.prefetch(rt.upcoming, part=0, parts=2)
-    tokens = int(batch["attention_mask"].sum())
+    # a device mask's token count stays on the device (read lazily, after the step's loss read)
+    am = batch["attention_mask"]
+    tokens = int(am.sum()) if am.device.type == "cpu" else am.sum()
     b = ids.shape[0]
     for cache, builder in zip(caches, builders):
         cache.resolution_events = list(builder.events)

@@ -34,10 +34,10 @@ _module = None
 KERNELS_PER_CALL = {"attention_fwd": 1, "attention_bwd": 3, "gemm": 1, "norm_fwd": 1, "norm_bwd": 3, "colsum": 2,
                     "cross_entropy": 1, "grad_norm": 2, "adamw": 1, "gist_mean": 1, "gist_kmeans": 1, "route": 1,
                     "gist_mean_into": 1, "gist_kmeans_into": 1,
-                    "stack_forward": 0, "dp_allreduce": 1, "dp_signal_words": 0,
+                    "stack_forward": 0, "stack_train_forward": 0, "stack_train_backward": 0, "dp_allreduce": 1, "dp_signal_words": 0,
                     "ipc_alloc": 0, "ipc_open": 0, "ipc_close": 0,
                     "rope_copy": 1, "silu_mul": 1, "decode_attention": 2, "route_topk": 1,
-                    "tp_allreduce": 1, "tp_allgather": 1, "tp_signal_words": 0, "route_merge": 1, "embed_add": 1, "combine_partials": 1, "attention_status": 0, "set_attention_impl": 0, "attention_impl": 0}  # stack_forward: counted per layer by its caller
+                    "tp_allreduce": 1, "tp_allgather": 1, "tp_signal_words": 0, "route_merge": 1, "embed_add": 1, "combine_partials": 1, "attention_status": 0, "set_attention_impl": 0, "attention_impl": 0}  # stack_*: counted per layer by their callers
 
 
 class LaunchCounter:

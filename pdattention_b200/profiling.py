@@ -73,13 +73,18 @@ def decode_small(steps: int = 3) -> None:
     print("ok")
 
 
-def _table(fn, rows: int = 30) -> None:
+def _table(fn, rows: int = 30, host_rows: int = 0) -> None:
+    """Kernel table (by CUDA time) of ``fn``; with ``host_rows`` also the host-side table (by
+    self CPU time: Python-level ops, launches and copies issued by the host)."""
     from torch.profiler import ProfilerActivity, profile
 
     with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
         fn()
         torch.cuda.synchronize()
-    print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=rows, max_name_column_width=70))
+    averages = prof.key_averages()
+    print(averages.table(sort_by="cuda_time_total", row_limit=rows, max_name_column_width=70))
+    if host_rows:
+        print(averages.table(sort_by="self_cpu_time_total", row_limit=host_rows, max_name_column_width=70))
 
 
 def train_table() -> None:
@@ -92,7 +97,7 @@ def train_table() -> None:
     step(batches[4])
     torch.cuda.synchronize()
     print(f"step wall ms {1000 * (time.perf_counter() - t0):.2f}")
-    _table(lambda: step(batches[5]))
+    _table(lambda: step(batches[5]), host_rows=25)
 
 
 def decode_table() -> None:

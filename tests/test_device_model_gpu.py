@@ -97,3 +97,33 @@ def test_native_stack_executor_matches_autograd_path(cuda, tmp_path):
             n = int(ref_lens[li][row])
             assert torch.equal(routing.mem_idx[row, :n], ref_routing[li][row, :n])
     assert torch.allclose(got, ref, atol=2e-2, rtol=2e-2), (got - ref).abs().max()
+
+
+def test_native_train_stack_matches_per_layer_autograd(cuda, tmp_path):
+    """One autograd node over the native block stack gives the per-layer autograd path's loss and
+    (up to the rounding of the fused residual-gradient add) its gradients."""
+    from pdattention_b200.models import fastpath
+
+    torch.manual_seed(4)
+    tok, batch = tiny_batch(Path(tmp_path))
+    model = TinyPRAModel(tiny_config(tok.vocab_size)).to(cuda)
+    attach_device_runtime(model)
+    opt = model.build_optimizer(TrainConfig(device="cuda", learning_rate=1e-3))
+    rt = model._device_runtime
+    results = {}
+    try:
+        for native in (True, False):
+            fastpath._NATIVE_TRAIN_STACK = native
+            opt.zero_grad()
+            loss, _ = _pra_batch_step(model, batch, "cuda", tok, ResolverServiceConfig(), None)
+            loss.backward()
+            lens = rt.last_routing[0].ints[0].clone()
+            results[native] = (loss.detach().clone(), rt.flat.grad.float().clone(), lens)
+    finally:
+        fastpath._NATIVE_TRAIN_STACK = True
+    assert torch.equal(results[True][0], results[False][0])
+    assert torch.equal(results[True][2], results[False][2]) and int(results[True][2].sum()) > 0
+    g_native, g_python = results[True][1], results[False][1]
+    assert torch.isfinite(g_native).all()
+    err = (g_native - g_python).abs().max().item()
+    assert err <= 2e-2 * g_python.abs().max().item(), err
