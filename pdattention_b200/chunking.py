@@ -228,6 +228,21 @@ def _cap_chunks(chunks, max_chunks, policy, all_ids, text, tokenizer):
     return [*keep, merged], dropped
 
 
+def _union_length(spans) -> int:
+    """Number of integer positions covered by half-open [start, end) spans."""
+    total, reach = 0, None
+    for start, end in sorted(spans):
+        if end <= start:
+            continue
+        if reach is None or start >= reach:
+            total += end - start
+            reach = end
+        elif end > reach:
+            total += end - reach
+            reach = end
+    return total
+
+
 def partition_source(uri: str, token_ids, tokenizer, chunking, metadata=None, *, text: str | None = None,
                      max_chunks: int | None = None, overflow_policy: str = "truncate",
                      max_chunk_tokens: int | None = None) -> list[ReferenceChunk]:
@@ -264,7 +279,7 @@ def partition_source(uri: str, token_ids, tokenizer, chunking, metadata=None, *,
     if dropped:
         chunks = [replace(c, metadata={**c.metadata, "discarded_chunk_count": dropped}) for c in chunks]
     encoded = sum(len(c.token_ids) for c in chunks)
-    covered = len({p for c in chunks for p in range(c.token_start, c.token_end)})
+    covered = _union_length((c.token_start, c.token_end) for c in chunks)
     provenance = {
         "chunk_overlap_fraction": policy.overlap_fraction,
         "resolved_chunk_overlap_tokens": policy.resolved_overlap_tokens(policy.chunk_tokens),

@@ -605,6 +605,9 @@ class DeviceRuntime:
         """
         cfg = self.cfg
         (cache,), (builder,) = plan_cache_builds(self.model, tokenizer, [item], resolver_config=resolver_config)
+        # chunk texts are not kept here (only token ids and positions), and fixed windows use the
+        # tokenizer only to decode those texts: skip the decode
+        chunk_tok = _IdsOnlyTokenizer(tokenizer) if cfg.chunking_mode == "fixed" else tokenizer
         entries: list[EntryRecord] = []
         chunks: list[ChunkRecord] = []
         limit = cfg.effective_model_max_context_tokens
@@ -617,7 +620,7 @@ class DeviceRuntime:
             index_of[step.uri] = e
             record = EntryRecord(0, step.uri, step.text, step.metadata, step.use_pra_memory,
                                  tuple(index_of[u] for u in step.visible_uris if u in index_of))
-            for chunk in partition_reference_tokens(step.uri, ids, tokenizer, cfg, step.metadata,
+            for chunk in partition_reference_tokens(step.uri, ids, chunk_tok, cfg, step.metadata,
                                                     text=step.text, max_chunk_tokens=limit):
                 ids_c = tuple(chunk.token_ids[:limit])
                 record.chunks.append(len(chunks))
@@ -861,6 +864,20 @@ class DeviceRuntime:
 
 class _Unsupported(RuntimeError):
     pass
+
+
+class _IdsOnlyTokenizer:
+    """A tokenizer whose ``decode`` returns an empty string (for partitions whose chunk texts
+    are discarded); everything else is the wrapped tokenizer's."""
+
+    def __init__(self, tokenizer):
+        self._tokenizer = tokenizer
+
+    def decode(self, ids) -> str:
+        return ""
+
+    def __getattr__(self, name):
+        return getattr(self._tokenizer, name)
 
 
 # The prompt's block stack with gradients runs as ONE autograd node over the native
