@@ -544,9 +544,9 @@ int pra_attention_get_impl() { return g_attn_tcgen05; }
 cudaError_t pra_attention_fwd(const AttnParams& p, int head_dim, cudaStream_t st) {
   using namespace pra::attn;
   if (p.B * p.T == 0) return cudaSuccess;
-  // The tcgen05 kernel works on 128-query tiles; sequences of <= 64 tokens (chunk encodes)
-  // keep the 64-query mma.sync tiles, which waste no rows there.
-  if (g_attn_tcgen05 && p.T > 64) {
+  // tcgen05: 128-query tiles, or two sequences per tile for <= 64 tokens at head dim 64; other
+  // short sequences keep the 64-query mma.sync tiles, which waste no rows there.
+  if (g_attn_tcgen05 && (p.T > 64 || head_dim == 64)) {
     const cudaError_t e = pra_attention_fwd_tc(p, head_dim, st);
     if (e != cudaErrorNotSupported) return e;
   }

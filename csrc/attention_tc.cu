@@ -839,6 +839,279 @@ __global__ void __launch_bounds__(NT, 2) bwd_dkdv_kernel(AttnParams p) {
   }
 }
 
+// ---- forward, two short sequences per tile -----------------------------------------------
+// Sequences of <= 64 tokens (chunk encodes), head dim 64: batch rows b0 = 2 blockIdx.y and
+// b0 + 1 share one 128-query tile (rows 0-63: b0, rows 64-127: b0 + 1).  Every key block holds
+// 64 keys of each sequence (K/V rows 0-63 / 64-127): memory blocks j = 0 .. n_mem - 1 take
+// memory keys 64 j .. 64 j + 63 of each row's own list, then one local block.  A query row
+// only sees its own sequence's 64 columns; the other half of its P row is zero (written once),
+// so the single S and P V MMAs per block serve both sequences.  Otherwise as fwd_kernel<64>.
+struct PackCfg {
+  static constexpr int D = 64, BN = 128, KB = 64, HB = 32;
+  static constexpr int Q_BYTES = BM * D * 2, KV_BYTES = BN * D * 2;
+  static constexpr int OFF_K = Q_BYTES;
+  static constexpr int OFF_RED = OFF_K + 4 * KV_BYTES;
+  static constexpr int OFF_VALID = OFF_RED + 2 * BM * 4;
+  static constexpr int OFF_BAR = OFF_VALID + 2 * BN;
+  static constexpr int SMEM = OFF_BAR + 16;
+  static constexpr int O_COL = BN, P_COL = BN + D;  // as Cfg<64>
+};
+
+__global__ void __launch_bounds__(NT, 2) fwd_packed_kernel(AttnParams p) {
+  using C = PackCfg;
+  constexpr int D = C::D, BN = C::BN, KB = C::KB, HB = C::HB;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* sq = smem;
+  float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
+  uint8_t* svalid = smem + C::OFF_VALID;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + 8);
+  int* s_abort = reinterpret_cast<int*>(smem + C::OFF_BAR + 12);
+  auto stage_k = [&](int s) { return smem + C::OFF_K + s * 2 * C::KV_BYTES; };
+  auto stage_v = [&](int s) { return smem + C::OFF_K + s * 2 * C::KV_BYTES + C::KV_BYTES; };
+
+  const int h = blockIdx.x;
+  const int b0 = 2 * blockIdx.y;
+  const int kvh = h / (p.H / p.Hkv);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int row = tid & (BM - 1), half = tid >> 7;
+  const int seq = row >> 6, t = row & 63;
+  const int b = b0 + seq;
+  const bool row_seq = b < p.B;  // the second sequence may not exist (odd B)
+  const int mlen0 = p.mem_len != nullptr ? p.mem_len[b0] : 0;
+  const int mlen1 = (p.mem_len != nullptr && b0 + 1 < p.B) ? p.mem_len[b0 + 1] : 0;
+  const int n_mem = (max(mlen0, mlen1) + KB - 1) / KB;
+  const int n_blocks = n_mem + 1;
+
+  if (warp == 0) {
+    tc::alloc(s_tmem, TMEM_COLS);
+    tc::relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    *s_abort = 0;
+    tc::fence_mbarrier_init();
+  }
+  // Q rows: tile row r -> (b0 + r / 64, token r % 64)
+#pragma unroll
+  for (int it = 0; it < BM * (D / 8) / NT; ++it) {
+    const int i = it * NT + tid;
+    const int c = (i >> 3) % (D / 8), r = (i / D) * 8 + (i & 7);
+    const int bb = b0 + (r >> 6), tt = r & 63;
+    const bool ok = bb < p.B && tt < p.T;
+    cp_async16(sq + tc::core_off(r, c, BM), ok ? p.q + bb * p.q_batch + (int64_t)tt * p.q_row + h * D + c * 8 : p.q,
+               ok);
+  }
+  // K/V block j: tile row r -> key (r % 64) of block j of sequence r / 64
+  auto load_block_packed = [&](int j, int s) {
+    const bool memory = j < n_mem;
+    uint8_t* sk = stage_k(s);
+    uint8_t* sv = stage_v(s);
+    if (!memory && p.key_valid != nullptr && tid < BN) {
+      const int bb = b0 + (tid >> 6), tt = tid & 63;
+      svalid[s * BN + tid] = (bb < p.B && tt < p.T) ? p.key_valid[(int64_t)bb * p.T + tt] : 0;
+    }
+    const int c = (tid >> 3) % (D / 8);
+#pragma unroll
+    for (int it = 0; it < BN * (D / 8) / NT; ++it) {
+      const int i = it * NT + tid;
+      const int r = (i / D) * 8 + (i & 7);
+      const int sq_ = r >> 6, kk = r & 63, bb = b0 + sq_;
+      const __nv_bfloat16* ks = p.k;
+      const __nv_bfloat16* vs = p.v;
+      bool ok = false;
+      if (bb < p.B) {
+        if (memory) {
+          const int jj = j * KB + kk;
+          ok = jj < (sq_ ? mlen1 : mlen0);
+          if (ok) {
+            const int64_t off = (int64_t)__ldg(p.mem_idx + (int64_t)bb * p.mem_max + jj) * p.mem_row + kvh * D + c * 8;
+            ks = p.mem_k + off;
+            vs = p.mem_v + off;
+          }
+        } else {
+          ok = kk < p.T;
+          if (ok) {
+            ks = p.k + bb * p.k_batch + (int64_t)kk * p.k_row + kvh * D + c * 8;
+            vs = p.v + bb * p.v_batch + (int64_t)kk * p.v_row + kvh * D + c * 8;
+          }
+        }
+      }
+      const uint32_t o = tc::core_off(r, c, BN);
+      cp_async16(sk + o, ks, ok);
+      cp_async16(sv + o, vs, ok);
+    }
+  };
+  load_block_packed(0, 0);
+  cp_async_commit();
+  cp_async_wait<0>();
+  fence_proxy_async_smem();
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+
+  const uint32_t tmem = *s_tmem;
+  const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
+  const int col0 = seq * KB + half * HB;  // this thread's 32 S columns (its own sequence's keys)
+  const uint32_t t_s = tmem + lane + col0;
+  const uint32_t t_o = tmem + lane + C::O_COL + half * (D / 2);
+  const uint32_t t_p = tmem + lane + C::P_COL + col0 / 2;
+  {
+    // the other sequence's half of this row's P stays zero for the whole loop
+    uint32_t z[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) z[i] = 0u;
+    tc::st16(tmem + lane + C::P_COL + ((1 - seq) * KB + half * HB) / 2, z);
+  }
+  constexpr uint32_t ID_S = tc::idesc_bf16(BM, BN, false);
+  constexpr uint32_t ID_O = tc::idesc_bf16(BM, D, true);
+  constexpr uint32_t Q_LBO = (BM / 8) * 128, KV_LBO = (BN / 8) * 128;
+  const uint32_t q_addr = smem_u32(sq);
+  auto issue_s = [&](int s) {
+    const uint32_t k_addr = smem_u32(stage_k(s));
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk)
+      tc::mma_bf16(tmem, tc::smem_desc(q_addr + kk * 2 * Q_LBO, Q_LBO, 128),
+                   tc::smem_desc(k_addr + kk * 2 * KV_LBO, KV_LBO, 128), ID_S, kk > 0);
+  };
+  auto issue_o = [&](int s, bool acc) {
+    const uint32_t v_addr = smem_u32(stage_v(s));
+#pragma unroll
+    for (int kk = 0; kk < BN / 16; ++kk)
+      tc::mma_bf16_ts(tmem + C::O_COL, tmem + C::P_COL + kk * 8, tc::smem_desc(v_addr + kk * 2 * 128, 128, KV_LBO),
+                      ID_O, (acc || kk > 0) ? 1u : 0u);
+  };
+  tc::fence_before();
+  __syncthreads();  // P zeros stored before the first P V MMA
+  tc::fence_after();
+  if (tid == 0) {
+    issue_s(0);
+    tc::commit(bar);
+  }
+
+  const float sl2 = p.scale * LOG2E;
+  float m_run = -INFINITY, l_run = 0.f;
+  bool aborted = false;
+  for (int j = 0; j < n_blocks; ++j) {
+    const int s = j & 1;
+    if (!tc::mbar_wait_cycles(bar, (uint32_t)(j & 1), WAIT_CYCLES)) *s_abort = 1;
+    const bool memory = j < n_mem;
+    if (j + 1 < n_blocks) {
+      load_block_packed(j + 1, s ^ 1);
+      cp_async_commit();
+    }
+    // visible keys among this thread's 32 columns (key index k = half * 32 + c in its sequence)
+    int lim;
+    const uint8_t* valid = nullptr;
+    if (!row_seq) {
+      lim = 0;
+    } else if (memory) {
+      lim = (seq ? mlen1 : mlen0) - j * KB - half * HB;
+    } else {
+      lim = min(p.T, t + 1) - half * HB;
+      if (p.key_valid != nullptr) valid = svalid + s * BN + col0;
+    }
+    const bool masked = lim < HB || valid != nullptr;
+    float mx = -INFINITY;
+    uint32_t r[32];
+    tc::ld32(t_s, r);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      if (masked && !(i < lim && (valid == nullptr || valid[i] != 0))) r[i] = __float_as_uint(-INFINITY);
+    }
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) mx = max3(mx, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+    red[half * BM + row] = mx;
+    pair_sync(warp);
+    mx = fmaxf(mx, red[(half ^ 1) * BM + row]);
+    float corr = 1.f;
+    bool rescale = false;
+    if (mx > m_run) {
+      if (m_run == -INFINITY) {
+        m_run = mx;
+      } else if ((mx - m_run) * sl2 > RESCALE_LOG2) {
+        corr = ex2((m_run - mx) * sl2);
+        l_run *= corr;
+        m_run = mx;
+        rescale = true;
+      }
+    }
+    if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+      uint32_t o[32];
+      tc::ld32(t_o, o);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
+      tc::st32(t_o, o);
+    }
+    const float ms = m_run == -INFINITY ? 0.f : m_run * sl2;
+    const float2 sl2x2 = make_float2(sl2, sl2), nms = make_float2(-ms, -ms);
+    float2 acc = make_float2(0.f, 0.f);
+    uint32_t w[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      float2 x = fma2(make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sl2x2, nms);
+      x.x = ex2(x.x);
+      x.y = ex2(x.y);
+      acc = add2(acc, x);
+      w[i] = pack_bf16(x.x, x.y);
+    }
+    tc::st16(t_p, w);
+    l_run += acc.x + acc.y;
+
+    if (j + 1 < n_blocks) cp_async_wait<0>();
+    fence_proxy_async_smem();
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    if (*s_abort) {
+      aborted = true;
+      break;
+    }
+    if (tid == 0) {
+      issue_o(s, j > 0);
+      if (j + 1 < n_blocks) issue_s(s ^ 1);
+      tc::commit(bar);
+    }
+  }
+
+  if (!aborted) {
+    if (!tc::mbar_wait_cycles(bar, (uint32_t)(n_blocks & 1), WAIT_CYCLES)) aborted = true;
+  }
+  aborted = __syncthreads_or(aborted);
+  red[half * BM + row] = l_run;
+  pair_sync(warp);
+  const float l_tot = l_run + red[(half ^ 1) * BM + row];
+  if (!aborted) {
+    const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+    uint32_t o[32];
+    tc::ld32(t_o, o);
+    if (row_seq && t < p.T) {
+      __nv_bfloat16* dst = p.o + b * p.o_batch + (int64_t)t * p.o_row + h * D + half * (D / 2);
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        uint4 v;
+        v.x = pack_bf16(__uint_as_float(o[i + 0]) * inv, __uint_as_float(o[i + 1]) * inv);
+        v.y = pack_bf16(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+        v.z = pack_bf16(__uint_as_float(o[i + 4]) * inv, __uint_as_float(o[i + 5]) * inv);
+        v.w = pack_bf16(__uint_as_float(o[i + 6]) * inv, __uint_as_float(o[i + 7]) * inv);
+        *reinterpret_cast<uint4*>(dst + i) = v;
+      }
+      if (half == 0)
+        p.lse[((int64_t)b * p.H + h) * p.T + t] = l_tot > 0.f ? m_run * p.scale + logf(l_tot) : -INFINITY;
+    }
+  } else {
+    if (tid == 0 && p.status != nullptr) atomicExch(p.status, 1);
+    cp_async_wait<0>();
+    tc::mbar_wait_cycles(bar, (uint32_t)(n_blocks & 1), WAIT_CYCLES);
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after();
+    tc::dealloc(tmem, TMEM_COLS);
+  }
+}
+
 template <int D>
 cudaError_t launch(const AttnParams& p, cudaStream_t st) {
   constexpr int smem = Cfg<D>::SMEM;
@@ -901,6 +1174,13 @@ cudaError_t pra_attention_fwd_tc(const AttnParams& p, int head_dim, cudaStream_t
     return cudaErrorNotSupported;
   if (p.mem_idx != nullptr && (!aligned(p.mem_k, p.mem_row, 0) || !aligned(p.mem_v, p.mem_row, 0)))
     return cudaErrorNotSupported;
+  if (head_dim == 64 && p.T <= 64) {  // two sequences per 128-query tile
+    constexpr int smem = PackCfg::SMEM;
+    PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(fwd_packed_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    dim3 grid(p.H, (p.B + 1) / 2);
+    fwd_packed_kernel<<<grid, NT, smem, st>>>(p);
+    return cudaGetLastError();
+  }
   switch (head_dim) {
     case 64: return launch<64>(p, st);
     case 128: return launch<128>(p, st);

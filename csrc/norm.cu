@@ -279,14 +279,28 @@ __global__ void __launch_bounds__(NT) bwd_kernel(const __nv_bfloat16* __restrict
   }
 }
 
-// out[d] = sum_p part[p, d] (fp32 -> out dtype); one thread per column.
+// out[d] = sum_p part[p, d] (fp32 -> out dtype).  A block of 256 threads takes 32 columns:
+// warp w sums partial rows w, w + 8, ... (one coalesced 128-byte row segment per load), then
+// the eight warp sums are added in a fixed order (deterministic).
 template <typename T>
-__global__ void column_reduce_kernel(const float* __restrict__ part, int P, int D, T* __restrict__ out) {
-  const int d = blockIdx.x * blockDim.x + threadIdx.x;
-  if (d >= D) return;
+__global__ void __launch_bounds__(256) column_reduce_kernel(const float* __restrict__ part, int P, int D,
+                                                            T* __restrict__ out) {
+  __shared__ float red[8][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int d = blockIdx.x * 32 + tx;
   float acc = 0.f;
-  for (int p = 0; p < P; ++p) acc += part[(int64_t)p * D + d];
-  out[d] = from_f32<T>(acc);
+  if (d < D) {
+#pragma unroll 4
+    for (int p = ty; p < P; p += 8) acc += part[(int64_t)p * D + d];
+  }
+  red[ty][tx] = acc;
+  __syncthreads();
+  if (ty == 0 && d < D) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += red[i][tx];
+    out[d] = from_f32<T>(s);
+  }
 }
 
 }  // namespace norm
@@ -335,8 +349,8 @@ cudaError_t pra_norm_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, const 
     bwd_kernel<false><<<parts, NT, 0, st>>>(dy, x, w, mean, rstd, dres, dx, dw_part, db_part, M, D, rows);
   }
   PRA_RETURN_IF_ERROR(cudaGetLastError());
-  column_reduce_kernel<__nv_bfloat16><<<(D + 255) / 256, 256, 0, st>>>(dw_part, parts, D, dw);
-  if (!rms && db) column_reduce_kernel<__nv_bfloat16><<<(D + 255) / 256, 256, 0, st>>>(db_part, parts, D, db);
+  column_reduce_kernel<__nv_bfloat16><<<(D + 31) / 32, 256, 0, st>>>(dw_part, parts, D, dw);
+  if (!rms && db) column_reduce_kernel<__nv_bfloat16><<<(D + 31) / 32, 256, 0, st>>>(db_part, parts, D, db);
   return cudaGetLastError();
 }
 
@@ -370,6 +384,6 @@ cudaError_t pra_colsum(const __nv_bfloat16* g, int M, int N, float* part, __nv_b
   dim3 grid(parts, (N / 2 + 255) / 256);
   colsum_partial_kernel<<<grid, 256, 0, st>>>(g, M, N, rows, part);
   PRA_RETURN_IF_ERROR(cudaGetLastError());
-  column_reduce_kernel<__nv_bfloat16><<<(N + 255) / 256, 256, 0, st>>>(part, parts, N, out);
+  column_reduce_kernel<__nv_bfloat16><<<(N + 31) / 32, 256, 0, st>>>(part, parts, N, out);
   return cudaGetLastError();
 }

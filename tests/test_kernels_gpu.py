@@ -256,7 +256,8 @@ def _gqa_reference(q, k, v, mem_k, mem_v, key_valid, scale, kv_heads):
 
 @pytest.mark.parametrize("head_dim", [64, 128])
 @pytest.mark.parametrize("t,lens,logit_scale", [(300, [260, 513], 1.0), (300, [0, 129], 6.0), (1, [64, 0], 1.0),
-                                                (1024, [0, 0], 3.0)])
+                                                (1024, [0, 0], 3.0), (64, [200, 0], 1.0), (37, [70, 129], 6.0),
+                                                (64, [1000, 3], 2.0)])
 def test_attention_fwd_tcgen05(ext, head_dim, t, lens, logit_scale):
     """The tcgen05 forward against fp32 PyTorch and the mma.sync forward: GQA (8 heads over 2),
     memory blocks gathered from a pool, padding masks, and logits large enough that the lazily
@@ -348,3 +349,33 @@ def test_attention_bwd_tcgen05(ext, t, lens, logit_scale):
     _close(g_tc[:, :, 0], qf.grad, 3e-2)
     _close(g_tc[:, :, 1], kf.grad, 3e-2)
     _close(g_tc[:, :, 2], vf.grad, 3e-2)
+
+
+def test_attention_fwd_packed_odd_batch(ext):
+    """Sequences of <= 64 tokens run two per tcgen05 tile; an odd batch leaves the last tile
+    half empty."""
+    b, t, h, hd = 3, 50, 4, 64
+    d = h * hd
+    q, k, v = _bf(b, t, d, seed=31), _bf(b, t, d, seed=32), _bf(b, t, d, seed=33)
+    key_valid = torch.ones(b, t, dtype=torch.uint8, device="cuda")
+    key_valid[2, 10:20] = 0
+    pool = _bf(300, 2 * d, seed=34)
+    lens = [65, 0, 130]
+    idx = torch.zeros(b, 130, dtype=torch.int32, device="cuda")
+    rows = []
+    for r, n in enumerate(lens):
+        sel = torch.randperm(300, device="cuda")[:n].int()
+        idx[r, :n] = sel
+        rows.append(sel.long())
+    mem_len = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    scale = 1.0 / math.sqrt(hd)
+    out, lse = ext.attention_fwd(q, k, v, h, h, hd, pool[:, :d], pool[:, d:], idx, mem_len, key_valid, scale)
+    mk = [pool[r_, :d].view(-1, h, hd) for r_ in rows]
+    mv = [pool[r_, d:].view(-1, h, hd) for r_ in rows]
+    ref = _attention_reference(q.view(b, t, h, hd), k.view(b, t, h, hd), v.view(b, t, h, hd), mk, mv, key_valid,
+                               scale)
+    _close(out.view(b, t, h, hd), ref, 2e-2)
+    ext.set_attention_impl("mma")
+    _, lse_mma = ext.attention_fwd(q, k, v, h, h, hd, pool[:, :d], pool[:, d:], idx, mem_len, key_valid, scale)
+    ext.set_attention_impl("tcgen05")
+    assert (lse - lse_mma).abs().max().item() < 1e-2
