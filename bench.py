@@ -145,6 +145,18 @@ def _max(value: float, world: int) -> float:
     return float(t.item())
 
 
+def _gather(value: float, world: int) -> list[float]:
+    """Every rank's value (rank order); collective, so every rank calls it."""
+    if world <= 1:
+        return [value]
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(x.item()) for x in out]
+
+
 def run(impl: str, steps: int, warmup: int, gpus: int) -> dict:
     rank, local, world = _env()
     if gpus != world:
@@ -199,7 +211,9 @@ def run(impl: str, steps: int, warmup: int, gpus: int) -> dict:
         wall = time.perf_counter() - wall0
     if counter is not None:
         counter.enabled = False
-    device_s = _max(start_evt.elapsed_time(end_evt) / 1000.0, world)
+    per_rank_device = _gather(start_evt.elapsed_time(end_evt) / 1000.0, world)
+    per_rank_host = _gather(host_s, world)
+    device_s = max(per_rank_device)
     wall_s = _max(wall, world)
     local_tokens = sum(tokens_per_step[warmup:])
     total_tokens = local_tokens * world  # identical shards sizes on every rank
@@ -226,7 +240,9 @@ def run(impl: str, steps: int, warmup: int, gpus: int) -> dict:
         "e2e": {"value": total_tokens / wall_s, "unit": "tokens/s", "h2d_bytes_per_step": h2d // max(steps, 1),
                 "d2h_bytes_per_step": d2h // max(steps, 1)},
         "gpu_launches": (counter.launches if counter is not None else 0),
-        "host_ms_per_step": 1000.0 * _max(host_s, world) / steps,  # time inside the step call on the host
+        "host_ms_per_step": 1000.0 * max(per_rank_host) / steps,  # time inside the step call on the host
+        "per_rank_ms_per_step": {"device": [round(1000.0 * v / steps, 3) for v in per_rank_device],
+                                 "host": [round(1000.0 * v / steps, 3) for v in per_rank_host]},
         "last_loss": loss_host,
     }
     if impl == "reference":

@@ -798,7 +798,7 @@ void ipc_close(int64_t address, int64_t device) {
 // src/dst/sig: device addresses (ints) of every rank's gradient, output and signal buffers.
 void dp_allreduce(std::vector<int64_t> src, std::vector<int64_t> dst, std::vector<int64_t> sig, int64_t rank,
                   int64_t offset, int64_t count, double scale, int64_t epoch, int64_t max_spins,
-                  torch::Tensor error) {
+                  torch::Tensor error, int64_t blocks) {
   const int world = src.size();
   TORCH_CHECK(world >= 1 && world <= DP_MAX_RANKS && dst.size() == src.size() && sig.size() == src.size(),
               "dp_allreduce needs one src/dst/sig address per rank (at most ", DP_MAX_RANKS, ")");
@@ -818,6 +818,7 @@ void dp_allreduce(std::vector<int64_t> src, std::vector<int64_t> dst, std::vecto
   a.epoch = (uint32_t)epoch;
   a.max_spins = max_spins;
   a.error = ptr<int>(error);
+  a.blocks = (int)blocks;
   check(pra_dp_allreduce(a, stream()), "dp_allreduce");
 }
 
@@ -1023,11 +1024,13 @@ static torch::Tensor norm_grad(const torch::Tensor& dh, const torch::Tensor& x, 
 
 // Backward of stack_train_forward: dy of the stack output -> dx of its input; weight
 // gradients into `grads` (12 per layer, aligned with `weights`; undefined/empty = none).
+// The lists may hold a contiguous run of layers starting at stack layer `layer0` (the
+// memory pool is indexed by stack layer), so a caller can act between layers.
 torch::Tensor stack_train_backward(torch::Tensor dy, int64_t B, int64_t T, std::vector<torch::Tensor> weights,
                                    std::vector<torch::Tensor> grads, double beta, int64_t heads, int64_t head_dim,
                                    c10::optional<torch::Tensor> key_valid, std::vector<torch::Tensor> saved,
                                    c10::optional<torch::Tensor> mem_pool, c10::optional<torch::Tensor> gist_kv,
-                                   bool gist_only) {
+                                   bool gist_only, int64_t layer0) {
   c10::cuda::CUDAGuard guard(dy.device());
   const int64_t L = weights.size() / 12;
   TORCH_CHECK(grads.size() == weights.size() && (int64_t)saved.size() == L * kSavedPerLayer,
@@ -1059,10 +1062,10 @@ torch::Tensor stack_train_backward(torch::Tensor dy, int64_t B, int64_t T, std::
     c10::optional<torch::Tensor> mk, mv, mio, mlo;
     if (mi.numel() > 0) {
       if (gist_only) {
-        mk = gist_kv->select(0, 0).select(0, l);
-        mv = gist_kv->select(0, 1).select(0, l);
+        mk = gist_kv->select(0, 0).select(0, layer0 + l);
+        mv = gist_kv->select(0, 1).select(0, layer0 + l);
       } else {
-        auto layer_pool = mem_pool->select(0, l);
+        auto layer_pool = mem_pool->select(0, layer0 + l);
         mk = layer_pool.narrow(1, D, D);
         mv = layer_pool.narrow(1, 2 * D, D);
       }

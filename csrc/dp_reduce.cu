@@ -89,6 +89,7 @@ cudaError_t pra_dp_allreduce(const DpArgs& a, cudaStream_t st) {
         a.sig[p] == nullptr)
       return cudaErrorInvalidValue;
   }
-  pra::dp::allreduce_kernel<<<pra_dp_allreduce_blocks(), pra::dp::NT, 0, st>>>(a);
+  const int blocks = a.blocks > 0 && a.blocks < pra_dp_allreduce_blocks() ? a.blocks : pra_dp_allreduce_blocks();
+  pra::dp::allreduce_kernel<<<blocks, pra::dp::NT, 0, st>>>(a);
   return cudaGetLastError();
 }

@@ -180,6 +180,8 @@ struct DpArgs {
   uint32_t epoch;                          // strictly increasing per launch (signals compare >=)
   long long max_spins;                     // poll limit of every wait
   int* error;                              // local flag: 1 + phase of a timed-out wait
+  int blocks;                              // CTAs of the launch (0: pra_dp_allreduce_blocks()); fewer
+                                           // leave SMs to kernels that run concurrently (backward)
 };
 int pra_dp_allreduce_blocks();
 cudaError_t pra_dp_allreduce(const DpArgs& args, cudaStream_t stream);

@@ -470,6 +470,8 @@ class DeviceRuntime:
         self.last_memory: BatchMemory | None = None
         self.last_namespace: Namespace | None = None
 
+    grad_hooks = None  # optional: before_stack() / after_layer(l) calls during the backward
+
     def grad_views(self) -> list[torch.Tensor]:
         """Every tensor that aliases the flat gradient buffer."""
         views = [t for slot in self.flat.slots for t in (slot.gw, slot.gb) if t is not None]
@@ -933,9 +935,25 @@ class _TrainStack(torch.autograd.Function):
         grads = []
         for s in slots:
             grads += [s.gw if s.gw is not None else empty, s.gb if s.gb is not None else empty]
-        dx = _ext.require().stack_train_backward(dy.contiguous(), ctx.b, ctx.t, rt._stack_weights(), grads,
-                                                 betas.pop(), rt.cfg.n_heads, rt.head_dim, ctx.key_valid, ctx.saved,
-                                                 ctx.mem_pool, ctx.gist_kv, ctx.gist_only)
+        beta = betas.pop()
+        ext = _ext.require()
+        weights, saved, n_layers = rt._stack_weights(), ctx.saved, rt.cfg.n_layers
+        hooks = rt.grad_hooks if beta == 0.0 else None  # (accumulating micro-batches: reduce at the step)
+        args = (rt.cfg.n_heads, rt.head_dim, ctx.key_valid)
+        if hooks is None:
+            dx = ext.stack_train_backward(dy.contiguous(), ctx.b, ctx.t, weights, grads, beta, *args, saved,
+                                          ctx.mem_pool, ctx.gist_kv, ctx.gist_only, 0)
+        else:
+            # layer by layer, so a layer's finished gradients can be reduced across ranks while the
+            # layers below it run their backward
+            hooks.before_stack()
+            dx = dy.contiguous()
+            for li in reversed(range(n_layers)):
+                dx = ext.stack_train_backward(dx, ctx.b, ctx.t, weights[12 * li: 12 * li + 12],
+                                              grads[12 * li: 12 * li + 12], beta, *args,
+                                              saved[15 * li: 15 * li + 15], ctx.mem_pool, ctx.gist_kv,
+                                              ctx.gist_only, li)
+                hooks.after_layer(li)
         ctx.saved = None
         _ext.add_launches("stack_train_backward", 25 * rt.cfg.n_layers)
         return dx, None, None, None, None, None, None, None, None

@@ -4,10 +4,12 @@ Every rank holds the flat bf16 gradient buffer written by the backward GEMMs.
 The reducer turns it into the fp32 *average* gradient the fused optimizer reads.
 
 * ``PeerGradientReducer`` (the default on CUDA): the gradient buffer lives in
-  symmetric memory and one kernel (``pra_ops.dp_allreduce``) reads every rank's
+  symmetric memory and a kernel (``pra_ops.dp_allreduce``) reads every rank's
   bf16 slice over NVLink, sums in fp32, applies 1/world and stores the result
   into every rank's fp32 buffer -- cast, scale, reduce-scatter and all-gather
-  fused, no staging copy and no NCCL call.
+  fused, no staging copy and no NCCL call.  The reduction overlaps the backward:
+  each block's gradient range is reduced on a side stream as soon as the block's
+  backward has written it.
 * ``NcclGradientReducer`` (the baseline, ``PRA_DP_BACKEND=nccl``): fp32 copy +
   NCCL all-reduce buckets, with the 1/world scale applied by the optimizer.
 
@@ -52,12 +54,38 @@ class NcclGradientReducer:
 GradientReducer = NcclGradientReducer  # backwards-compatible name
 
 
+def reduction_ranges(flat) -> tuple[list[tuple[int, int]], tuple[int, int]]:
+    """(per-layer (start, count) element ranges of the flat gradient, the LM head's range): each
+    block's parameters are contiguous in the flat layout, and so is the head (last, with its
+    padding rows)."""
+    offsets = flat.offsets
+    layers = []
+    i = 0
+    while f"blocks.{i}.attn.q_proj.weight" in offsets:
+        start = offsets[f"blocks.{i}.attn.q_proj.weight"]
+        end = offsets.get(f"blocks.{i + 1}.attn.q_proj.weight", offsets["token_emb.weight"])
+        layers.append((start, end - start))
+        i += 1
+    head = offsets["head.weight"]
+    return layers, (head, flat.total - head)
+
+
 class PeerGradientReducer:
-    """Fused peer-memory all-reduce of the flat gradient (one kernel per step)."""
+    """Fused peer-memory all-reduce of the flat gradient.
+
+    With ``overlap`` (``PRA_DP_OVERLAP=1``; off by default) the reduction is launched
+    in pieces during the backward on a communication stream: the LM head's gradient as soon as
+    the block stack's backward starts, and each block's gradient as soon as that block's
+    backward has written it (hooks called by the native training stack); the embeddings and
+    final norm, finished last, are reduced when the optimizer asks.  The overlapped launches
+    use ``overlap_blocks`` CTAs so the backward keeps most SMs.  Every rank launches the same
+    pieces in the same order.
+    """
 
     scale_in_optimizer = False
 
-    def __init__(self, runtime, group=None, max_spins: int = 1 << 22):
+    def __init__(self, runtime, group=None, max_spins: int = 1 << 22, overlap: bool | None = None,
+                 overlap_blocks: int = 64):
         from .peer import PeerBuffers
 
         ext = _ext.require()
@@ -78,12 +106,57 @@ class PeerGradientReducer:
         self.epoch = 0
         self.max_spins = int(max_spins)
         self.error = torch.zeros(1, dtype=torch.int32, device=flat.grad.device)
+        if overlap is None:
+            overlap = os.environ.get("PRA_DP_OVERLAP", "0") != "0"
+        self.overlap = bool(overlap) and self.world > 1
+        self.overlap_blocks = int(overlap_blocks)
+        self.layer_ranges, self.head_range = reduction_ranges(flat)
+        self.done: list[tuple[int, int]] = []  # ranges already launched this step
+        self.comm = torch.cuda.Stream(device=flat.grad.device) if self.overlap else None
+        if self.overlap:
+            runtime.grad_hooks = self
+
+    def _launch(self, start: int, count: int, blocks: int = 0) -> None:
+        self.epoch += 1
+        _ext.require().dp_allreduce(self.src, self.dst, self.sig, self.rank, start, count, 1.0 / self.world,
+                                    self.epoch, self.max_spins, self.error, blocks)
+
+    def _launch_async(self, rng: tuple[int, int]) -> None:
+        ready = torch.cuda.Event()
+        ready.record()  # after the kernels that wrote this range (current stream)
+        self.comm.wait_event(ready)
+        with torch.cuda.stream(self.comm):
+            self._launch(rng[0], rng[1], self.overlap_blocks)
+        self.done.append(rng)
+
+    # hooks called by the native training stack's backward
+    def before_stack(self) -> None:
+        self._launch_async(self.head_range)
+
+    def after_layer(self, layer: int) -> None:
+        self._launch_async(self.layer_ranges[layer])
 
     def reduce(self) -> torch.Tensor:
-        """Average of every rank's gradient, in this rank's fp32 buffer."""
-        self.epoch += 1
-        _ext.require().dp_allreduce(self.src, self.dst, self.sig, self.rank, 0, self.numel, 1.0 / self.world,
-                                    self.epoch, self.max_spins, self.error)
+        """Average of every rank's gradient, in this rank's fp32 buffer (ordered before the
+        caller's next kernels on the current stream)."""
+        if not self.done:
+            self._launch(0, self.numel)
+            return self.out
+        rest, cursor = [], 0
+        for start, count in sorted(self.done):
+            if start > cursor:
+                rest.append((cursor, start - cursor))
+            cursor = max(cursor, start + count)
+        if cursor < self.numel:
+            rest.append((cursor, self.numel - cursor))
+        ready = torch.cuda.Event()
+        ready.record()
+        self.comm.wait_event(ready)
+        with torch.cuda.stream(self.comm):
+            for start, count in rest:
+                self._launch(start, count)
+        torch.cuda.current_stream().wait_stream(self.comm)
+        self.done = []
         return self.out
 
     def check(self) -> None:
@@ -101,7 +174,8 @@ def _backend() -> str:
     return os.environ.get("PRA_DP_BACKEND", "peer").lower()
 
 
-def attach_data_parallel(model, optimizer, world_size: int, backend: str | None = None):
+def attach_data_parallel(model, optimizer, world_size: int, backend: str | None = None,
+                         overlap: bool | None = None):
     """Route the fused optimizer through the averaged gradient (no-op for one rank).
 
     ``backend``: ``"peer"`` (fused symmetric-memory kernel) or ``"nccl"``; default
@@ -112,7 +186,7 @@ def attach_data_parallel(model, optimizer, world_size: int, backend: str | None 
     runtime = model._device_runtime
     backend = (backend or _backend()).lower()
     if backend == "peer":
-        reducer = PeerGradientReducer(runtime)
+        reducer = PeerGradientReducer(runtime, overlap=overlap)
     elif backend == "nccl":
         reducer = NcclGradientReducer(runtime.flat, world_size)
     else:

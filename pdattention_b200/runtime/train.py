@@ -119,7 +119,10 @@ def create_training_state(model, train_config, *, optimizer=None, scheduler=None
         if world > 1 and getattr(model, "_device_runtime", None) is not None:
             from ..parallel.dp import attach_data_parallel
 
-            attach_data_parallel(model, optimizer, world)  # fused peer-memory gradient average
+            # fused peer-memory gradient average; overlapped with the backward unless micro-batches
+            # accumulate (a block's gradient is final only after the last micro-batch)
+            attach_data_parallel(model, optimizer, world,
+                                 overlap=False if int(train_config.grad_accum_steps) > 1 else None)
     if scheduler is None:
         scheduler = torch.optim.lr_scheduler.LambdaLR(optimizer, warmup_lambda(train_config.warmup_steps))
     run_dir = Path(train_config.output_dir) / train_config.experiment_name

@@ -36,11 +36,19 @@ def _worker(rank: int, world: int, port: int, queue) -> None:
         from pdattention_b200.parallel.dp import attach_data_parallel
         from pdattention_b200.smoke import tiny_config
 
+        import tempfile
+        from pathlib import Path
+
+        from pdattention_b200.config import ResolverServiceConfig
+        from pdattention_b200.pra_train import _pra_batch_step
+        from pdattention_b200.smoke import tiny_batch
+
+        tok, batch = tiny_batch(Path(tempfile.mkdtemp()))
         torch.manual_seed(0)
-        model = prepare_model(tiny_config(64), "cuda")
+        model = prepare_model(tiny_config(tok.vocab_size), "cuda")  # the batch's ids fit the vocabulary
         rt = model._device_runtime
         opt = model.build_optimizer(TrainConfig(device="cuda", learning_rate=1e-3))
-        reducer = attach_data_parallel(model, opt, world, "peer")
+        reducer = attach_data_parallel(model, opt, world, "peer", overlap=True)
         grad = rt.flat.grad
         # the slot views now alias the peer-visible buffer
         gw = rt.layers[0]["qkv"].gw
@@ -69,6 +77,30 @@ def _worker(rank: int, world: int, port: int, queue) -> None:
         sums = [torch.zeros_like(checksum) for _ in range(world)]
         dist.all_gather(sums, checksum)
         result["replicas_equal"] = all(float(s) == float(sums[0]) for s in sums)
+        # overlapped pieces (the hooks the native backward calls: head, blocks top-down, then
+        # the rest at the optimizer) give the same average
+        result["hooked"] = reducer.overlap and rt.grad_hooks is reducer
+        grad.copy_(torch.randn(grad.shape, generator=gen, device="cuda").bfloat16())
+        dist.all_gather(gathered, grad)
+        expected = sum(t.float() for t in gathered) * (1.0 / world)
+        reducer.before_stack()
+        for li in reversed(range(len(reducer.layer_ranges))):
+            reducer.after_layer(li)
+        out = reducer.reduce()
+        torch.cuda.synchronize()
+        reducer.check()
+        result["max_err3"] = float((out - expected).abs().max())
+        # a real step through the native training stack (the hooks fire during its backward)
+        opt.zero_grad()
+        loss, _ = _pra_batch_step(model, batch, "cuda", tok, ResolverServiceConfig(), None)
+        loss.backward()
+        result["pieces"] = len(reducer.done)
+        opt.step()
+        torch.cuda.synchronize()
+        reducer.check()
+        checksum = rt.flat.master.double().sum().reshape(1)
+        dist.all_gather(sums, checksum)
+        result["replicas_equal2"] = all(float(s) == float(sums[0]) for s in sums)
         dist.barrier()
         # timeout: rank 1 skips one reduction; rank 0's bounded wait must run out
         reducer.max_spins = 1 << 14
@@ -112,5 +144,9 @@ def test_peer_gradient_allreduce_two_gpus():
         assert item["max_err"] < 1e-5, item
         assert item["max_err2"] < 1e-5, item
         assert item["replicas_equal"], item
+        assert item["hooked"], item
+        assert item["max_err3"] < 1e-5, item
+        assert item["pieces"] == 1 + 2, item  # head + the tiny model's 2 blocks before the optimizer step
+        assert item["replicas_equal2"], item
     assert results[0]["timeout_code"] == 1, results[0]
     assert results[0]["context_usable"]
