@@ -44,21 +44,23 @@ __device__ __forceinline__ Quad load_quad(const __nv_bfloat16* p) {
 
 __device__ __forceinline__ int dest_of(const GistArgs& a, int c) { return a.dest ? a.dest[c] : c; }
 
-// Sums v[0..G) over the block in place (all threads see the totals).  red holds NWARPS * MAXG floats.
+// Sums v[0..G) (G <= MG) over the block in place (all threads see the totals).  red holds
+// NWARPS * MAXG floats.
+template <int MG = MAXG>
 __device__ __forceinline__ void block_sum_vec(float* v, int G, float* red) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
-  for (int q = 0; q < MAXG; ++q)
+  for (int q = 0; q < MG; ++q)
     if (q < G) v[q] = warp_sum(v[q]);
   __syncthreads();
   if (lane == 0) {
 #pragma unroll
-    for (int q = 0; q < MAXG; ++q)
+    for (int q = 0; q < MG; ++q)
       if (q < G) red[warp * MAXG + q] = v[q];
   }
   __syncthreads();
 #pragma unroll
-  for (int q = 0; q < MAXG; ++q) {
+  for (int q = 0; q < MG; ++q) {
     if (q < G) {
       float s = 0.f;
       for (int w = 0; w < NWARPS; ++w) s += red[w * MAXG + q];
@@ -134,7 +136,8 @@ __global__ void __launch_bounds__(NT) mean_kernel(GistArgs a) {
 }
 
 // ---------------------------------------------------------------- kmeans
-template <bool STAGED>
+// MG: compile-time bound on the number of centres (>= a.G); the per-point loops run over it.
+template <bool STAGED, int MG>
 __global__ void __launch_bounds__(NT) kmeans_kernel(GistArgs a) {
   extern __shared__ __align__(16) float sm[];
   const int D = a.D, D4 = D / 4, nmax = a.nmax;
@@ -204,15 +207,15 @@ __global__ void __launch_bounds__(NT) kmeans_kernel(GistArgs a) {
   // Squared distances from every point to centres [0, nc): warp per point.
   auto distances = [&](int nc) {
     for (int i = warp; i < n; i += NWARPS) {
-      float acc[MAXG];
+      float acc[MG];
 #pragma unroll
-      for (int q = 0; q < MAXG; ++q) acc[q] = 0.f;
+      for (int q = 0; q < MG; ++q) acc[q] = 0.f;
       const float sc = inv_norm[i];
       for (int j = lane; j < D4; j += 32) {
         const Quad k = load_quad(keys + (int64_t)i * kstride + 4 * j);
         const float wx = k.x * sc, wy = k.y * sc, wz = k.z * sc, ww = k.w * sc;
 #pragma unroll
-        for (int q = 0; q < MAXG; ++q) {
+        for (int q = 0; q < MG; ++q) {
           if (q < nc) {
             const float4 cc = *reinterpret_cast<const float4*>(centers + q * D + 4 * j);
             const float dx = wx - cc.x, dy = wy - cc.y, dz = wz - cc.z, dw = ww - cc.w;
@@ -221,7 +224,7 @@ __global__ void __launch_bounds__(NT) kmeans_kernel(GistArgs a) {
         }
       }
 #pragma unroll
-      for (int q = 0; q < MAXG; ++q) {
+      for (int q = 0; q < MG; ++q) {
         if (q < nc) {
           const float v = warp_sum(acc[q]);
           if (lane == 0) dist[i * MAXG + q] = v;
@@ -278,7 +281,7 @@ __global__ void __launch_bounds__(NT) kmeans_kernel(GistArgs a) {
         dmin[i] = taken ? 0.f : m;
         part[0] += dmin[i];
       }
-      block_sum_vec(part, 1, red);
+      block_sum_vec<1>(part, 1, red);
       const float total = part[0];
       float best = -INFINITY;
       int best_i = -1;
@@ -328,19 +331,19 @@ __global__ void __launch_bounds__(NT) kmeans_kernel(GistArgs a) {
         if (members[q] == 0) a.status[status_at] = 1;
     }
     // new centres: each thread owns 4 columns and accumulates every cluster
-    float shift[MAXG];
+    float shift[MG];
 #pragma unroll
-    for (int q = 0; q < MAXG; ++q) shift[q] = 0.f;
+    for (int q = 0; q < MG; ++q) shift[q] = 0.f;
     for (int j = threadIdx.x; j < D4; j += NT) {
-      float acc[MAXG][4];
+      float acc[MG][4];
 #pragma unroll
-      for (int q = 0; q < MAXG; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
+      for (int q = 0; q < MG; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
       for (int i = 0; i < n; ++i) {
         const Quad k = load_quad(keys + (int64_t)i * kstride + 4 * j);
         const float sc = inv_norm[i];
         const int qi = assign[i];
 #pragma unroll
-        for (int q = 0; q < MAXG; ++q) {
+        for (int q = 0; q < MG; ++q) {
           if (q == qi) {
             acc[q][0] += k.x * sc;
             acc[q][1] += k.y * sc;
@@ -352,7 +355,7 @@ __global__ void __launch_bounds__(NT) kmeans_kernel(GistArgs a) {
       const Quad fk = load_quad(keys + (int64_t)pick * kstride + 4 * j);
       const float fsc = inv_norm[pick];
 #pragma unroll
-      for (int q = 0; q < MAXG; ++q) {
+      for (int q = 0; q < MG; ++q) {
         if (q < G) {
           float4 nv;
           if (members[q] == 0) {
@@ -369,7 +372,7 @@ __global__ void __launch_bounds__(NT) kmeans_kernel(GistArgs a) {
         }
       }
     }
-    block_sum_vec(shift, G, red);
+    block_sum_vec<MG>(shift, G, red);
     if (threadIdx.x == 0) {
       float m = 0.f;
       for (int q = 0; q < G; ++q) m = fmaxf(m, sqrtf(shift[q]));
@@ -395,22 +398,22 @@ __global__ void __launch_bounds__(NT) kmeans_kernel(GistArgs a) {
   }
   __syncthreads();
   // keys (raw, not normalised) then values; each thread keeps its columns for the norms
-  float norm1[MAXG], norm2[MAXG];
+  float norm1[MG], norm2[MG];
 #pragma unroll
-  for (int q = 0; q < MAXG; ++q) norm1[q] = norm2[q] = 0.f;
+  for (int q = 0; q < MG; ++q) norm1[q] = norm2[q] = 0.f;
   for (int pass = 0; pass < 2; ++pass) {
     const __nv_bfloat16* src = pass == 0 ? keys : gval;
     const int64_t stride = pass == 0 ? kstride : a.row_stride;
     float* dstp = pass == 0 ? a.gk : a.gv;
     for (int j = threadIdx.x; j < D4; j += NT) {
-      float acc[MAXG][4];
+      float acc[MG][4];
 #pragma unroll
-      for (int q = 0; q < MAXG; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
+      for (int q = 0; q < MG; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
       for (int i = 0; i < n; ++i) {
         const Quad k = load_quad(src + (int64_t)i * stride + 4 * j);
         const int qi = assign[i];
 #pragma unroll
-        for (int q = 0; q < MAXG; ++q) {
+        for (int q = 0; q < MG; ++q) {
           if (q == qi) {
             acc[q][0] += k.x;
             acc[q][1] += k.y;
@@ -420,7 +423,7 @@ __global__ void __launch_bounds__(NT) kmeans_kernel(GistArgs a) {
         }
       }
 #pragma unroll
-      for (int q = 0; q < MAXG; ++q) {
+      for (int q = 0; q < MG; ++q) {
         if (q < G && slot_of[q] >= 0) {
           const float m = (float)members[q];
           const float4 v = make_float4(acc[q][0] / m, acc[q][1] / m, acc[q][2] / m, acc[q][3] / m);
@@ -431,10 +434,10 @@ __global__ void __launch_bounds__(NT) kmeans_kernel(GistArgs a) {
     }
   }
   // gk is L2-normalised when the working space is; gn = gk / ||gk|| is the routing copy.
-  block_sum_vec(norm1, G, red);
+  block_sum_vec<MG>(norm1, G, red);
   for (int j = threadIdx.x; j < D4; j += NT) {
 #pragma unroll
-    for (int q = 0; q < MAXG; ++q) {
+    for (int q = 0; q < MG; ++q) {
       if (q < G && slot_of[q] >= 0) {
         float4* p = reinterpret_cast<float4*>(a.gk + out + (int64_t)slot_of[q] * D + 4 * j);
         float4 v = *p;
@@ -447,10 +450,10 @@ __global__ void __launch_bounds__(NT) kmeans_kernel(GistArgs a) {
       }
     }
   }
-  block_sum_vec(norm2, G, red);
+  block_sum_vec<MG>(norm2, G, red);
   for (int j = threadIdx.x; j < D4; j += NT) {
 #pragma unroll
-    for (int q = 0; q < MAXG; ++q) {
+    for (int q = 0; q < MG; ++q) {
       if (q < G && slot_of[q] >= 0) {
         const int64_t o = out + (int64_t)slot_of[q] * D + 4 * j;
         const float4 v = *reinterpret_cast<const float4*>(a.gk + o);
@@ -492,15 +495,16 @@ cudaError_t pra_gist_kmeans(const GistArgs& a, int layers, cudaStream_t st) {
   const size_t fixed = kmeans_fixed_smem(a);
   const size_t staged = fixed + (size_t)a.nmax * a.D * sizeof(__nv_bfloat16);
   // Stage when two CTAs still fit on one SM (2 x 110 KB of the 228 KB per SM).
-  if (staged <= 110 * 1024) {
-    PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(kmeans_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)staged));
-    kmeans_kernel<true><<<dim3(a.C, layers), NT, staged, st>>>(a);
-  } else {
-    if (fixed > 200 * 1024) return cudaErrorInvalidValue;
-    PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(kmeans_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)fixed));
-    kmeans_kernel<false><<<dim3(a.C, layers), NT, fixed, st>>>(a);
-  }
+  const bool stage = staged <= 110 * 1024;
+  if (!stage && fixed > 200 * 1024) return cudaErrorInvalidValue;
+  const size_t smem = stage ? staged : fixed;
+  auto go = [&](auto kernel) -> cudaError_t {
+    PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kernel<<<dim3(a.C, layers), NT, smem, st>>>(a);
+    return cudaSuccess;
+  };
+  if (a.G <= 2) PRA_RETURN_IF_ERROR(stage ? go(kmeans_kernel<true, 2>) : go(kmeans_kernel<false, 2>));
+  else if (a.G <= 4) PRA_RETURN_IF_ERROR(stage ? go(kmeans_kernel<true, 4>) : go(kmeans_kernel<false, 4>));
+  else PRA_RETURN_IF_ERROR(stage ? go(kmeans_kernel<true, MAXG>) : go(kmeans_kernel<false, MAXG>));
   return cudaGetLastError();
 }
