@@ -183,7 +183,8 @@ def _bound_chunk_lengths(chunks, tokenizer, max_chunk_tokens):
     out: list[ReferenceChunk] = []
     for chunk in chunks:
         if len(chunk.token_ids) <= max_chunk_tokens:
-            out.append(replace(chunk, chunk_id=chunk_identity(chunk.source_uri, len(out))))
+            chunk_id = chunk_identity(chunk.source_uri, len(out))
+            out.append(chunk if chunk.chunk_id == chunk_id else replace(chunk, chunk_id=chunk_id))
             continue
         for offset in range(0, len(chunk.token_ids), max_chunk_tokens):
             ids = tuple(chunk.token_ids[offset: offset + max_chunk_tokens])
@@ -249,7 +250,7 @@ def partition_source(uri: str, token_ids, tokenizer, chunking, metadata=None, *,
     """Partition exact token ids with one policy (shared by encoding and routing)."""
     policy = ChunkingConfig.from_value(chunking)
     meta = dict(metadata or {})
-    ids = [int(t) for t in token_ids]
+    ids = list(map(int, token_ids))
     if not ids:
         return []
     text = tokenizer.decode(ids) if text is None else text

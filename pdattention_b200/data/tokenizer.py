@@ -94,12 +94,11 @@ class WordIdTokenizer:
         return self.base_vocab + len(self._refs)
 
     def encode(self, text: str) -> list[int]:
-        get = self.stoi.get
         words = text.split()
-        out = [get(word, -1) for word in words]
-        if -1 in out:  # unregistered reference handles, non-canonical or unknown words
+        out = list(map(self.stoi.get, words))  # one C-level pass; None marks a word not in stoi
+        if None in out:  # unregistered reference handles, non-canonical or unknown words
             for i, value in enumerate(out):
-                if value == -1:
+                if value is None:
                     out[i] = self._encode_word(words[i])
         return out
 
