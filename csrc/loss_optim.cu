@@ -47,6 +47,84 @@ __global__ void __launch_bounds__(NT) ce_kernel(__nv_bfloat16* __restrict__ logi
   }
 }
 
+// Same outputs as ce_kernel with the row read from global memory once: 16-byte loads stage
+// the row (ld bf16 values, ld % 8 == 0) in shared memory while each thread keeps an online
+// (max, sum of exp) pair; the pairs are merged across the block, then the gradient is written
+// from the staged copy.  Global traffic: one read and one write of the row.
+__device__ __forceinline__ void merge_max_sum(float& m, float& s, float m2, float s2) {
+  const float mn = fmaxf(m, m2);
+  if (mn == -INFINITY) return;
+  s = s * __expf(m - mn) + s2 * __expf(m2 - mn);
+  m = mn;
+}
+
+__global__ void __launch_bounds__(NT) ce_staged_kernel(__nv_bfloat16* __restrict__ logits, int64_t ld, int V,
+                                                       const int64_t* __restrict__ labels, int ignore_index,
+                                                       float* __restrict__ row_loss, float* __restrict__ row_valid) {
+  extern __shared__ __align__(16) __nv_bfloat16 srow[];
+  __shared__ float wm[NT / 32], ws[NT / 32];
+  const int64_t row = blockIdx.x;
+  __nv_bfloat16* lr = logits + row * ld;
+  const int64_t label = labels[row];
+  const bool valid = label != ignore_index && label >= 0 && label < V;
+  const int nvec = (int)(ld / 8);
+  float m = -INFINITY, s = 0.f;
+  for (int v = threadIdx.x; v < nvec; v += NT) {
+    const uint4 raw = reinterpret_cast<const uint4*>(lr)[v];
+    reinterpret_cast<uint4*>(srow)[v] = raw;
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    float x[8], mx = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      x[k] = v * 8 + k < V ? __bfloat162float(e[k]) : -INFINITY;
+      mx = fmaxf(mx, x[k]);
+    }
+    if (mx == -INFINITY) continue;
+    float add = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) add += __expf(x[k] - mx);
+    merge_max_sum(m, s, mx, add);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    merge_max_sum(m, s, m2, s2);
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    wm[warp] = m;
+    ws[warp] = s;
+  }
+  __syncthreads();  // also: the staged row is complete
+  m = wm[0];
+  s = ws[0];
+  for (int w = 1; w < NT / 32; ++w) merge_max_sum(m, s, wm[w], ws[w]);
+  const float lse = m + __logf(s);
+  const float target = valid ? __bfloat162float(srow[label]) : 0.f;
+  const float inv = 1.f / s;
+  for (int v = threadIdx.x; v < nvec; v += NT) {
+    const uint4 raw = reinterpret_cast<const uint4*>(srow)[v];
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    uint4 out;
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+    for (int k = 0; k < 8; k += 2) {
+      float g[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int i = v * 8 + k + u;
+        g[u] = (valid && i < V) ? __expf(__bfloat162float(e[k + u]) - m) * inv - (i == label ? 1.f : 0.f) : 0.f;
+      }
+      ow[k / 2] = pack_bf16(g[0], g[1]);
+    }
+    reinterpret_cast<uint4*>(lr)[v] = out;
+  }
+  if (threadIdx.x == 0) {
+    row_loss[row] = valid ? lse - target : 0.f;
+    row_valid[row] = valid ? 1.f : 0.f;
+  }
+}
+
 // Sum of squares of a flat gradient buffer into per-CTA partials.
 template <typename G>
 __global__ void sumsq_kernel(const G* __restrict__ g, int64_t n, float* __restrict__ part) {
@@ -105,6 +183,14 @@ __global__ void cast_kernel(const float* __restrict__ src, __nv_bfloat16* __rest
 cudaError_t pra_cross_entropy(__nv_bfloat16* logits, int64_t M, int64_t ld, int V, const int64_t* labels,
                               int ignore_index, float* row_loss, float* row_valid, cudaStream_t st) {
   if (M == 0) return cudaSuccess;
+  const size_t staged = (size_t)ld * sizeof(__nv_bfloat16);
+  if (ld % 8 == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0 && staged <= 200 * 1024) {
+    PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(pra::lo::ce_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)staged));
+    pra::lo::ce_staged_kernel<<<(unsigned)M, pra::lo::NT, staged, st>>>(logits, ld, V, labels, ignore_index, row_loss,
+                                                                         row_valid);
+    return cudaGetLastError();
+  }
   pra::lo::ce_kernel<<<(unsigned)M, pra::lo::NT, 0, st>>>(logits, ld, V, labels, ignore_index, row_loss, row_valid);
   return cudaGetLastError();
 }
