@@ -156,9 +156,31 @@ __global__ void __launch_bounds__(256) bwd_warp_kernel(const __nv_bfloat16* __re
 #pragma unroll
     for (int e = 0; e < 8; ++e) aw[j][e] = ab[j][e] = 0.f;
   const int r0 = blockIdx.x * rows_per_cta, r1 = min(r0 + rows_per_cta, M);
+  // x / dy of the warp's next row are loaded while the current row is reduced
+  uint4 xr[WCH], gr[WCH];
+  float mean_n = 0.f, rstd_n = 0.f;
+  auto fetch = [&](int row) {
+#pragma unroll
+    for (int j = 0; j < WCH; ++j) {
+      const int c = lane + 32 * j;
+      if (c < C) {
+        xr[j] = *reinterpret_cast<const uint4*>(x + (int64_t)row * D + 8 * c);
+        gr[j] = *reinterpret_cast<const uint4*>(dy + (int64_t)row * D + 8 * c);
+      }
+    }
+    mean_n = RMS ? 0.f : mean_in[row];
+    rstd_n = rstd_in[row];
+  };
+  if (r0 + warp < r1) fetch(r0 + warp);
   for (int row = r0 + warp; row < r1; row += 8) {
-    const float mean = RMS ? 0.f : mean_in[row];
-    const float rstd = rstd_in[row];
+    const float mean = mean_n, rstd = rstd_n;
+    uint4 xc[WCH], gc[WCH];
+#pragma unroll
+    for (int j = 0; j < WCH; ++j) {
+      xc[j] = xr[j];
+      gc[j] = gr[j];
+    }
+    if (row + 8 < r1) fetch(row + 8);
     float xh[WCH][8], wg[WCH][8];
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
@@ -166,8 +188,8 @@ __global__ void __launch_bounds__(256) bwd_warp_kernel(const __nv_bfloat16* __re
       const int c = lane + 32 * j;
       if (c < C) {
         float xv[8], gv[8], wv[8];
-        load8(x + (int64_t)row * D + 8 * c, xv);
-        load8(dy + (int64_t)row * D + 8 * c, gv);
+        load8(reinterpret_cast<const __nv_bfloat16*>(&xc[j]), xv);
+        load8(reinterpret_cast<const __nv_bfloat16*>(&gc[j]), gv);
         load8(w + 8 * c, wv);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
@@ -322,7 +344,7 @@ cudaError_t pra_norm_fwd(const __nv_bfloat16* x, const __nv_bfloat16* w, const _
   return cudaGetLastError();
 }
 
-int pra_norm_bwd_partials(int M) { return M == 0 ? 1 : (M + 15) / 16 > 592 ? 592 : (M + 15) / 16; }
+int pra_norm_bwd_partials(int M) { return M == 0 ? 1 : (M + 31) / 32 > 592 ? 592 : (M + 31) / 32; }
 
 cudaError_t pra_norm_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, const __nv_bfloat16* w, const float* mean,
                          const float* rstd, const __nv_bfloat16* dres, __nv_bfloat16* dx, float* dw_part,
