@@ -61,7 +61,7 @@ __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int64_t M,
 // ---------------------------------------------------------------- decode attention
 constexpr int DT = 128;   // threads (4 warps, 16 keys each per block of 64)
 constexpr int DBN = 64;   // keys per block
-constexpr int DSTAGES = 3;  // cp.async pipeline depth (blocks in flight per CTA)
+constexpr int DSTAGES = 2;  // cp.async pipeline depth (blocks in flight per CTA)
 constexpr float LOG2E = 1.4426950408889634f;
 
 template <int D>
