@@ -495,7 +495,7 @@ template <int D>
 cudaError_t launch_fwd(const Params& p, cudaStream_t st) {
   constexpr int LD = Smem<D>::LD;
   const size_t smem = (size_t)(BM + 4 * BN) * LD * sizeof(__nv_bfloat16) + 2 * BN;
-  PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(fwd_kernel<D>), (int)smem));
   dim3 grid(p.H * p.B, (p.T + BM - 1) / BM);
   fwd_kernel<D><<<grid, NT, smem, st>>>(p);
   return cudaGetLastError();
@@ -515,7 +515,7 @@ cudaError_t launch_bwd(const Params& p, cudaStream_t st) {
     PRA_RETURN_IF_ERROR(tc_dq);
   } else {
     const size_t smem = (size_t)(2 * BM + 4 * BN) * LD * sizeof(__nv_bfloat16) + 2 * BN;
-    PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(bwd_dq_kernel<D>), (int)smem));
     dim3 grid(p.H * p.B, (p.T + BM - 1) / BM);
     bwd_dq_kernel<D><<<grid, NT, smem, st>>>(p);
     PRA_RETURN_IF_ERROR(cudaGetLastError());
@@ -526,7 +526,7 @@ cudaError_t launch_bwd(const Params& p, cudaStream_t st) {
   }
   {
     const size_t smem = (size_t)(2 * BN + 4 * BM) * LD * sizeof(__nv_bfloat16) + 4 * BM * sizeof(float);
-    PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(bwd_dkdv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(bwd_dkdv_kernel<D>), (int)smem));
     dim3 grid(p.H * p.B, (p.T + BN - 1) / BN);
     bwd_dkdv_kernel<D><<<grid, NT, smem, st>>>(p);
     return cudaGetLastError();

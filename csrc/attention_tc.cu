@@ -1115,7 +1115,7 @@ __global__ void __launch_bounds__(NT, 2) fwd_packed_kernel(AttnParams p) {
 template <int D>
 cudaError_t launch(const AttnParams& p, cudaStream_t st) {
   constexpr int smem = Cfg<D>::SMEM;
-  PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(fwd_kernel<D>), smem));
   dim3 grid(p.H * p.B, (p.T + BM - 1) / BM);
   fwd_kernel<D><<<grid, NT, smem, st>>>(p);
   return cudaGetLastError();
@@ -1138,7 +1138,7 @@ cudaError_t pra_attention_bwd_dq_tc(const AttnParams& p, int head_dim, cudaStrea
   if (p.mem_idx != nullptr && (!aligned(p.mem_k, p.mem_row, 0) || !aligned(p.mem_v, p.mem_row, 0)))
     return cudaErrorNotSupported;
   constexpr int smem = DqCfg::SMEM;
-  PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(bwd_dq_kernel), smem));
   dim3 grid(p.H * p.B, (p.T + BM - 1) / BM);
   bwd_dq_kernel<<<grid, NT, smem, st>>>(p);
   return cudaGetLastError();
@@ -1156,7 +1156,7 @@ cudaError_t pra_attention_bwd_dkdv_tc(const AttnParams& p, int head_dim, cudaStr
       !aligned(p.dk, p.dk_row, p.dk_batch) || !aligned(p.dv, p.dv_row, p.dv_batch))
     return cudaErrorNotSupported;
   constexpr int smem = DkvCfg::SMEM;
-  PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(bwd_dkdv_kernel), smem));
   dim3 grid(p.H * p.B, (p.T + DkvCfg::BK - 1) / DkvCfg::BK);
   bwd_dkdv_kernel<<<grid, NT, smem, st>>>(p);
   return cudaGetLastError();
@@ -1176,7 +1176,7 @@ cudaError_t pra_attention_fwd_tc(const AttnParams& p, int head_dim, cudaStream_t
     return cudaErrorNotSupported;
   if (head_dim == 64 && p.T <= 64) {  // two sequences per 128-query tile
     constexpr int smem = PackCfg::SMEM;
-    PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(fwd_packed_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(fwd_packed_kernel), smem));
     dim3 grid(p.H, (p.B + 1) / 2);
     fwd_packed_kernel<<<grid, NT, smem, st>>>(p);
     return cudaGetLastError();

@@ -7,6 +7,10 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "kernels.h"
 
 // Launch helpers return the first CUDA error instead of throwing; the binding
@@ -20,6 +24,23 @@
 namespace pra {
 
 inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+// Raise a kernel's dynamic shared-memory limit to `bytes`, calling cudaFuncSetAttribute only
+// when this (kernel, device) pair has not been given at least that much yet: the attribute
+// lasts for the process, and setting it on every launch costs host time per launch.
+inline cudaError_t set_max_dynamic_smem(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static auto* granted = new std::map<std::pair<const void*, int>, int>();  // never freed
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  int& have = (*granted)[{kernel, dev}];
+  if (have >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) have = bytes;
+  return e;
+}
 
 // Explicit conversions (the build disables implicit bf16 <-> float conversions).
 __device__ __forceinline__ float to_f32(float v) { return v; }

@@ -9,6 +9,8 @@
 //   "wgrad" D[M,N] = A[K,M]^T . B[K,N]            (weight gradient: dY^T X)
 #pragma once
 
+#include <atomic>
+
 #include <cutlass/cutlass.h>
 #include <cute/tensor.hpp>
 #include <cutlass/epilogue/collective/collective_builder.hpp>
@@ -104,7 +106,19 @@ struct Gemm {
     Device op;
     if (op.can_implement(args) != cutlass::Status::kSuccess) return cudaErrorNotSupported;
     if (Device::get_workspace_size(args) > workspace_bytes) return cudaErrorMemoryAllocation;
-    if (op.initialize(args, workspace, st) != cutlass::Status::kSuccess) return cudaErrorLaunchFailure;
+    // The full initialize() also sets the kernel's shared-memory attribute, which lasts for the
+    // process: do it on the first call per device, then only the per-call parts (workspace
+    // set-up and kernel parameters).
+    static std::atomic<uint64_t> configured{0};
+    const uint64_t bit = 1ull << (args.hw_info.device_id & 63);
+    if (!(configured.load(std::memory_order_acquire) & bit)) {
+      if (op.initialize(args, workspace, st) != cutlass::Status::kSuccess) return cudaErrorLaunchFailure;
+      configured.fetch_or(bit, std::memory_order_acq_rel);
+    } else {
+      if (Kernel::initialize_workspace(args, workspace, st, nullptr) != cutlass::Status::kSuccess)
+        return cudaErrorLaunchFailure;
+      if (op.update(args, workspace) != cutlass::Status::kSuccess) return cudaErrorLaunchFailure;
+    }
     if (op.run(st) != cutlass::Status::kSuccess) return cudaErrorLaunchFailure;
     return cudaGetLastError();
   }

@@ -499,7 +499,7 @@ cudaError_t pra_gist_kmeans(const GistArgs& a, int layers, cudaStream_t st) {
   if (!stage && fixed > 200 * 1024) return cudaErrorInvalidValue;
   const size_t smem = stage ? staged : fixed;
   auto go = [&](auto kernel) -> cudaError_t {
-    PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(kernel), (int)smem));
     kernel<<<dim3(a.C, layers), NT, smem, st>>>(a);
     return cudaSuccess;
   };

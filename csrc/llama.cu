@@ -608,7 +608,7 @@ static cudaError_t launch_decode(DecodeAttnParams p, cudaStream_t st) {
   static_assert(2 * DSTAGES * DBN * LD * sizeof(__nv_bfloat16) >= 4 * 16 * (D + 2) * sizeof(float),
                 "merge buffer must fit in the staging area");
   const size_t smem = (size_t)(16 + 2 * DSTAGES * DBN) * LD * sizeof(__nv_bfloat16) + (size_t)p.split_keys * sizeof(int);
-  PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(decode_kernel<D>), (int)smem));
   decode_kernel<D><<<dim3(p.B * p.Hkv, p.n_split), DT, smem, st>>>(p);
   PRA_RETURN_IF_ERROR(cudaGetLastError());
   decode_merge_kernel<<<p.B * p.H, 128, 0, st>>>(p, D);

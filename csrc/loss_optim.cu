@@ -185,8 +185,7 @@ cudaError_t pra_cross_entropy(__nv_bfloat16* logits, int64_t M, int64_t ld, int 
   if (M == 0) return cudaSuccess;
   const size_t staged = (size_t)ld * sizeof(__nv_bfloat16);
   if (ld % 8 == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0 && staged <= 200 * 1024) {
-    PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(pra::lo::ce_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)staged));
+    PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(pra::lo::ce_staged_kernel), (int)staged));
     pra::lo::ce_staged_kernel<<<(unsigned)M, pra::lo::NT, staged, st>>>(logits, ld, V, labels, ignore_index, row_loss,
                                                                          row_valid);
     return cudaGetLastError();

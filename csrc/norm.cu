@@ -357,12 +357,10 @@ cudaError_t pra_norm_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, const 
   if (D % 8 == 0 && D <= 32 * 8 * WCH) {
     const size_t smem = (size_t)16 * D * sizeof(float);
     if (rms) {
-      PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(bwd_warp_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)smem));
+      PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(bwd_warp_kernel<true>), (int)smem));
       bwd_warp_kernel<true><<<parts, 256, smem, st>>>(dy, x, w, nullptr, rstd, dres, dx, dw_part, nullptr, M, D, rows);
     } else {
-      PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(bwd_warp_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)smem));
+      PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(bwd_warp_kernel<false>), (int)smem));
       bwd_warp_kernel<false><<<parts, 256, smem, st>>>(dy, x, w, mean, rstd, dres, dx, dw_part, db_part, M, D, rows);
     }
   } else if (rms) {

@@ -410,7 +410,7 @@ cudaError_t pra_route(const RouteParams& p, cudaStream_t st) {
   if (p.D % 4 != 0 || (reinterpret_cast<uintptr_t>(p.gists) & 15)) return cudaErrorInvalidValue;
   const size_t smem = (size_t)p.D * sizeof(float) + (size_t)MAX_ROW_CHUNKS * (2 * sizeof(float) + 2 * sizeof(int)) +
                       (size_t)MAX_ROW_REFS * (sizeof(float) + sizeof(int));
-  PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(route_kernel), (int)smem));
   route_kernel<<<p.B, NT, smem, st>>>(p);
   return cudaGetLastError();
 }
