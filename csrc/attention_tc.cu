@@ -13,13 +13,13 @@
 // Thread 0 issues the MMAs and commits them to one mbarrier; all threads stage K/V with
 // cp.async (memory keys are gathered row by row, which a tiled TMA box cannot express),
 // read their half S row with tcgen05.ld, apply the mask and the online softmax in registers
-// (row maxima and sums combined with the partner thread through shared memory; paired fp32
-// FMAs/adds and 3-input max) and write their half P row (bf16, two per 32-bit column) back
-// into TMEM, where the second MMA takes it as its A operand:
-//   O += P V     (A = P from TMEM columns [BN + D, BN + D + BN / 2), B = V from shared memory)  O stays in TMEM for the
-// whole key loop: a row's running maximum is only raised (and its O row rescaled in TMEM)
-// when a block's maximum exceeds it by more than 2^8 in exp2 units, so P <= 256 and the
-// final O / l and LSE = m * scale + log(l) stay exact.
+// (row maxima and sums combined with the partner thread through shared memory; 3-input max)
+// and write their half P row (bf16, two per 32-bit column) back into TMEM, where the second
+// MMA takes it as its A operand:
+//   O += P V     (A = P from TMEM columns [BN + D, BN + D + BN / 2), B = V from shared memory)
+// O stays in TMEM for the whole key loop: a row's running maximum is only raised (and its O
+// row rescaled in TMEM) when a block's maximum exceeds it by more than 2^8 in exp2 units, so
+// P <= 256 and the final O / l and LSE = m * scale + log(l) stay exact.
 //
 // Per iteration j: wait S_j (its commit also covers P V_{j-1}); prefetch K/V_{j+1} into the
 // other stage (freed by P V_{j-1}); softmax of S_j into P; wait for K_{j+1}; thread 0 issues
@@ -75,24 +75,12 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return m;
 }
 
-// (a.x * b.x + c.x, a.y * b.y + c.y) in one paired instruction.
+// (a.x * b.x + c.x, a.y * b.y + c.y).
 __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
-  float2 d;
-  asm("{\n .reg .b64 a, b, c, d;\n mov.b64 a, {%2, %3};\n mov.b64 b, {%4, %5};\n mov.b64 c, {%6, %7};\n"
-      " fma.rn.f32x2 d, a, b, c;\n mov.b64 {%0, %1}, d;\n}\n"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return d;
+  return make_float2(fmaf(a.x, b.x, c.x), fmaf(a.y, b.y, c.y));
 }
 
-__device__ __forceinline__ float2 add2(float2 a, float2 b) {
-  float2 d;
-  asm("{\n .reg .b64 a, b, d;\n mov.b64 a, {%2, %3};\n mov.b64 b, {%4, %5};\n add.f32x2 d, a, b;\n"
-      " mov.b64 {%0, %1}, d;\n}\n"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return d;
-}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); }
 
 // Pair barrier of the two warps (w, w + 4) that own the same 32 query rows.
 __device__ __forceinline__ void pair_sync(int warp) {
