@@ -169,3 +169,33 @@ def test_standalone_entry_points_train_and_eval(data_root):
     main(["eval", "--config", str(path), "--model", "default", "--checkpoint", str(ckpt),
           "--traces-jsonl", str(traces)])
     assert traces.read_text().strip()
+
+
+def test_reduction_ranges_tile_the_flat_gradient():
+    """The overlapped gradient reduction's pieces: one contiguous range per block holding
+    exactly that block's parameters, in layout order, and the LM head's range last; the
+    embeddings and final norm are what the optimizer-time reduction covers."""
+    from pdattention_b200.models import TinyPRAModel
+    from pdattention_b200.models.fastpath import FlatParams
+    from pdattention_b200.parallel.dp import reduction_ranges
+    from pdattention_b200.smoke import tiny_config
+
+    cfg = tiny_config(96)
+    cfg.device = "cpu"
+    model = TinyPRAModel(cfg)
+    flat = FlatParams(model, (cfg.vocab_size + 127) // 128 * 128)
+    layers, head = reduction_ranges(flat)
+    assert len(layers) == cfg.n_layers
+    for i, (start, count) in enumerate(layers):
+        assert start % 8 == 0 and count % 8 == 0 and count > 0
+        inside = [n for n, off in flat.offsets.items() if start <= off < start + count]
+        assert inside and all(n.startswith(f"blocks.{i}.") for n in inside)
+        assert {n for n in flat.offsets if n.startswith(f"blocks.{i}.")} == set(inside)
+        if i:
+            assert start == layers[i - 1][0] + layers[i - 1][1]
+    assert head == (flat.offsets["head.weight"], flat.total - flat.offsets["head.weight"])
+    covered = sum(c for _, c in layers) + head[1]
+    rest = [n for n, off in flat.offsets.items()
+            if not any(s <= off < s + c for s, c in layers + [head])]
+    assert set(rest) == {"token_emb.weight", "pos_emb.weight", "ln.weight", "ln.bias"}
+    assert covered < flat.total
