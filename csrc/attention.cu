@@ -257,6 +257,36 @@ __global__ void __launch_bounds__(NT) fwd_kernel(Params p) {
   }
 }
 
+// delta[b,h,t] = sum_d dO * O with 16-byte loads: D / 8 consecutive lanes cover one head
+// (D / 8 <= 32), so a warp covers 256 / D (b, t, h) rows; reduction within each lane group.
+template <int D>
+__global__ void delta_vec_kernel(Params p) {
+  constexpr int L = D / 8;  // lanes per (b, t, h) row
+  const int64_t gt = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t total = (int64_t)p.B * p.T * p.H;
+  const int64_t item = gt / L;
+  const int part = (int)(gt % L);
+  float acc = 0.f;
+  if (item < total) {
+    const int h = item % p.H, t = (item / p.H) % p.T, b = item / ((int64_t)p.H * p.T);
+    const uint4 ov = *reinterpret_cast<const uint4*>(p.o + b * p.o_batch + (int64_t)t * p.o_row + h * D + part * 8);
+    const uint4 gv = *reinterpret_cast<const uint4*>(p.dout + b * p.do_batch + (int64_t)t * p.do_row + h * D + part * 8);
+    const __nv_bfloat162* oh = reinterpret_cast<const __nv_bfloat162*>(&ov);
+    const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&gv);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 a = __bfloat1622float2(oh[k]), c = __bfloat1622float2(gh[k]);
+      acc += a.x * c.x + a.y * c.y;
+    }
+  }
+#pragma unroll
+  for (int o = L / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (item < total && part == 0) {
+    const int h = item % p.H, t = (item / p.H) % p.T, b = item / ((int64_t)p.H * p.T);
+    p.delta[((int64_t)b * p.H + h) * p.T + t] = acc;
+  }
+}
+
 // delta[b,h,t] = sum_d dO * O   (one warp per (b, t, h))
 template <int D>
 __global__ void delta_kernel(Params p) {
@@ -505,8 +535,12 @@ template <int D>
 cudaError_t launch_bwd(const Params& p, cudaStream_t st) {
   constexpr int LD = Smem<D>::LD;
   {
-    const int64_t warps = (int64_t)p.B * p.T * p.H;
-    delta_kernel<D><<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(p);
+    const int64_t rows = (int64_t)p.B * p.T * p.H;
+    const bool vec = D % 8 == 0 && D / 8 <= 32 && p.o_row % 8 == 0 && p.o_batch % 8 == 0 && p.do_row % 8 == 0 &&
+                     p.do_batch % 8 == 0 && (reinterpret_cast<uintptr_t>(p.o) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(p.dout) & 15) == 0;
+    if (vec) delta_vec_kernel<D><<<(unsigned)((rows * (D / 8) + 255) / 256), 256, 0, st>>>(p);
+    else delta_kernel<D><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(p);
     PRA_RETURN_IF_ERROR(cudaGetLastError());
   }
   cudaError_t tc_dq = cudaErrorNotSupported;

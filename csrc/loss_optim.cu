@@ -125,6 +125,25 @@ __global__ void __launch_bounds__(NT) ce_staged_kernel(__nv_bfloat16* __restrict
   }
 }
 
+// Sum of squares of a bf16 buffer into per-CTA partials with 16-byte loads (n % 8 == 0,
+// 16-byte aligned); same partial layout as sumsq_kernel.
+__global__ void sumsq_bf16x8_kernel(const __nv_bfloat16* __restrict__ g, int64_t n, float* __restrict__ part) {
+  __shared__ float scratch[32];
+  float acc = 0.f;
+  const int64_t nv = n / 8;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 raw = reinterpret_cast<const uint4*>(g)[i];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 v = __bfloat1622float2(h[k]);
+      acc += v.x * v.x + v.y * v.y;
+    }
+  }
+  acc = block_sum(acc, scratch);
+  if (threadIdx.x == 0) part[blockIdx.x] = acc;
+}
+
 // Sum of squares of a flat gradient buffer into per-CTA partials.
 template <typename G>
 __global__ void sumsq_kernel(const G* __restrict__ g, int64_t n, float* __restrict__ part) {
@@ -200,7 +219,11 @@ int pra_grad_norm_parts() { return kNormParts; }
 cudaError_t pra_grad_norm(const void* grad, bool grad_bf16, int64_t n, float max_norm, float* part, float* norm_out,
                           float* coef_out, cudaStream_t st) {
   if (grad_bf16)
-    pra::lo::sumsq_kernel<__nv_bfloat16><<<kNormParts, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(grad), n, part);
+    if (n % 8 == 0 && (reinterpret_cast<uintptr_t>(grad) & 15) == 0)
+      pra::lo::sumsq_bf16x8_kernel<<<kNormParts, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(grad), n, part);
+    else
+      pra::lo::sumsq_kernel<__nv_bfloat16><<<kNormParts, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(grad), n,
+                                                                      part);
   else
     pra::lo::sumsq_kernel<float><<<kNormParts, 256, 0, st>>>(static_cast<const float*>(grad), n, part);
   PRA_RETURN_IF_ERROR(cudaGetLastError());
