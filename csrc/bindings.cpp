@@ -988,9 +988,17 @@ std::vector<torch::Tensor> stack_train_forward(torch::Tensor x, int64_t B, int64
   return out;
 }
 
-// g (+)= colsum(dy) into a bias-gradient view.
+// g (+)= colsum(dy) into a bias-gradient view (written in place when not accumulating).
 static void bias_grad(const torch::Tensor& dy, torch::Tensor& gb, double beta) {
   if (!gb.defined() || gb.numel() == 0) return;
+  if (beta == 0.0 && gb.is_contiguous() && gb.scalar_type() == at::kBFloat16 && dy.is_contiguous()) {
+    const int N = dy.size(-1);
+    const int M = dy.numel() / N;
+    auto part = torch::empty({pra_colsum_partials(M), N}, dy.options().dtype(at::kFloat));
+    check(pra_colsum(ptr<const __nv_bfloat16>(dy), M, N, ptr<float>(part), ptr<__nv_bfloat16>(gb), stream()),
+          "colsum");
+    return;
+  }
   auto s = colsum(dy);
   if (beta == 0.0) gb.copy_(s);
   else gb.add_(s);
@@ -1010,6 +1018,22 @@ static void weight_grad(const torch::Tensor& dy, const torch::Tensor& x, torch::
 static torch::Tensor norm_grad(const torch::Tensor& dh, const torch::Tensor& x, const torch::Tensor& w,
                                const torch::Tensor& mean, const torch::Tensor& rstd, const torch::Tensor& dres,
                                torch::Tensor& gw, torch::Tensor& gb, double beta) {
+  const bool direct = beta == 0.0 && gw.defined() && gw.numel() > 0 && gw.is_contiguous() && gb.defined() &&
+                      gb.numel() > 0 && gb.is_contiguous() && dh.is_contiguous() && x.is_contiguous() &&
+                      dres.is_contiguous();
+  if (direct) {  // weight and bias gradients written straight into their views
+    const int D = x.size(-1);
+    const int M = x.numel() / D;
+    auto dx = torch::empty_like(x);
+    const int parts = pra_norm_bwd_partials(M);
+    auto part = torch::empty({2, parts, D}, x.options().dtype(at::kFloat));
+    check(pra_norm_bwd(ptr<const __nv_bfloat16>(dh), ptr<const __nv_bfloat16>(x), ptr<const __nv_bfloat16>(w),
+                       ptr<const float>(mean), ptr<const float>(rstd), ptr<const __nv_bfloat16>(dres),
+                       ptr<__nv_bfloat16>(dx), ptr<float>(part), ptr<float>(part) + (int64_t)parts * D,
+                       ptr<__nv_bfloat16>(gw), ptr<__nv_bfloat16>(gb), M, D, false, stream()),
+          "norm_bwd");
+    return dx;
+  }
   auto r = norm_bwd(dh, x, w, mean, rstd, dres, false);
   if (gw.defined() && gw.numel() > 0) {
     if (beta == 0.0) gw.copy_(r[1]);
