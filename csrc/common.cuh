@@ -157,20 +157,15 @@ __device__ __forceinline__ bool bounded_wait_geq(const volatile uint32_t* flag, 
 
 namespace pra {
 
-// ---- mbarrier + bulk (TMA-engine) copies, CTA scope, no multicast ----------------------
+// ---- mbarriers (CTA scope) and the generic -> async proxy fence ------------------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
 
-// Makes barrier initialisation (and earlier generic-proxy shared-memory writes) visible to
-// the async proxy that bulk copies complete through.
+// Makes earlier generic-proxy shared-memory writes (cp.async data, register stores) visible
+// to the async proxy (the tensor cores' operand reads).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait_parity(uint64_t* bar, uint32_t parity) {
@@ -181,23 +176,6 @@ __device__ __forceinline__ bool mbar_try_wait_parity(uint64_t* bar, uint32_t par
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
-}
-
-// Bounded wait for the barrier phase with the given parity; false after max_polls polls.
-__device__ __forceinline__ bool mbar_wait_parity_bounded(uint64_t* bar, uint32_t parity, long long max_polls) {
-  for (long long i = 0; i < max_polls; ++i)
-    if (mbar_try_wait_parity(bar, parity)) return true;
-  return false;
-}
-
-// Global -> this CTA's shared memory, `bytes` (multiple of 16, both addresses 16-byte
-// aligned), completion counted on `bar`.
-__device__ __forceinline__ void bulk_copy_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
-          smem_u32(smem_dst)),
-      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
 }
 
 }  // namespace pra

@@ -82,8 +82,6 @@ __device__ __forceinline__ void dealloc(uint32_t taddr, uint32_t ncols) {
 
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
-__device__ __forceinline__ void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
-__device__ __forceinline__ void wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
 
 __device__ __forceinline__ void fence_mbarrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
