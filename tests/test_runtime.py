@@ -199,3 +199,36 @@ def test_reduction_ranges_tile_the_flat_gradient():
             if not any(s <= off < s + c for s, c in layers + [head])]
     assert set(rest) == {"token_emb.weight", "pos_emb.weight", "ln.weight", "ln.bias"}
     assert covered < flat.total
+
+
+def test_planning_without_chunk_texts_keeps_plans():
+    """Row planning decodes no chunk texts for fixed windows (the device path keeps only token
+    ids and positions); the plans must equal those planned with the plain tokenizer."""
+    import tempfile
+    import types
+    from pathlib import Path
+
+    from pdattention_b200.config import ResolverServiceConfig
+    from pdattention_b200.models import TinyPRAModel
+    from pdattention_b200.models import fastpath
+    from pdattention_b200.smoke import tiny_batch, tiny_config
+
+    tok, batch = tiny_batch(Path(tempfile.mkdtemp()))
+    cfg = tiny_config(tok.vocab_size)
+    cfg.device = "cpu"
+    assert cfg.chunking_mode == "fixed"
+    model = TinyPRAModel(cfg)
+    ctx = types.SimpleNamespace(cfg=model.cfg, model=model)
+    resolver = ResolverServiceConfig()
+    for item in batch["metadata"]:
+        fast = fastpath.DeviceRuntime.plan_row(ctx, item, tok, resolver)
+        original = fastpath._IdsOnlyTokenizer
+        fastpath._IdsOnlyTokenizer = lambda t: t  # plain tokenizer: chunk texts decoded
+        try:
+            plain = fastpath.DeviceRuntime.plan_row(ctx, item, tok, resolver)
+        finally:
+            fastpath._IdsOnlyTokenizer = original
+        assert [(e.uri, e.wave, e.visible, e.chunks) for e in fast.entries] == \
+            [(e.uri, e.wave, e.visible, e.chunks) for e in plain.entries]
+        assert [(c.chunk_id, c.token_start, c.token_end, c.token_ids, c.metadata) for c in fast.chunks] == \
+            [(c.chunk_id, c.token_start, c.token_end, c.token_ids, c.metadata) for c in plain.chunks]
