@@ -10,6 +10,10 @@
 
 #include "kernels.h"
 
+// Native cache-build planner (planner.cpp).
+pybind11::object pra_plan_batch(const pybind11::list& rows, const pybind11::object& tokenizer,
+                                const pybind11::dict& cfg);
+
 namespace {
 
 inline cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
@@ -1143,6 +1147,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("route_merge", &route_merge);
   m.def("embed_add", &embed_add);
   m.def("combine_partials", &combine_partials);
+  m.def("plan_batch", &pra_plan_batch, "native cache-build planner (returns None when a batch needs the Python planner)");
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", &ipc_close);

@@ -77,6 +77,17 @@ cudaError_t pra_norm_bwd(const __nv_bfloat16* dy, const __nv_bfloat16* x, const 
 int pra_colsum_partials(int M);
 cudaError_t pra_colsum(const __nv_bfloat16* g, int M, int N, float* part, __nv_bfloat16* out, cudaStream_t stream);
 
+// ---- allocation-free column sums (colsum_noalloc.cu) ---------------------------------
+// Exported C symbols for callers that cannot allocate device memory where they call
+// (the contract, capacity and sharing rules are in colsum_noalloc.cu).  Return values
+// are cudaError_t codes.
+extern "C" {
+__attribute__((visibility("default"))) long long pra_colsum_noalloc_capacity();
+__attribute__((visibility("default"))) void pra_colsum_noalloc_reset();
+__attribute__((visibility("default"))) int pra_colsum_noalloc(const void* g, int M, int N, void* out,
+                                                              cudaStream_t stream);
+}
+
 // ---- loss / optimizer (loss_optim.cu) -----------------------------------------------
 cudaError_t pra_cross_entropy(__nv_bfloat16* logits, int64_t M, int64_t ld, int V, const int64_t* labels,
                               int ignore_index, float* row_loss, float* row_valid, cudaStream_t stream);

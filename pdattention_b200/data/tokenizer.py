@@ -93,6 +93,11 @@ class WordIdTokenizer:
     def vocab_size(self) -> int:
         return self.base_vocab + len(self._refs)
 
+    def native_word_ids(self) -> tuple[int, dict[str, int]]:
+        """(base vocabulary, registered reference tokens): what a native tokenizer needs to
+        encode exactly as ``encode`` does for texts whose reference tokens are registered."""
+        return self.base_vocab, dict(self._refs)
+
     def encode(self, text: str) -> list[int]:
         words = text.split()
         out = list(map(self.stoi.get, words))  # one C-level pass; None marks a word not in stoi

@@ -7,7 +7,9 @@ What changes relative to the object path (same semantics, different execution):
   a bf16 gradient buffer written directly by the weight-gradient GEMMs, and the
   AdamW moments; one fused kernel clips and updates everything.
 * **Cache build** for a whole batch: every row's recursive build plan is traced
-  on the host (``plan_cache_builds``), entries are grouped into *waves* by their
+  on the host by the native planner (``pra_ops.plan_batch``, ``csrc/planner.cpp``;
+  the Python planner ``plan_cache_builds`` is its oracle and fallback), entries
+  are grouped into *waves* by their
   visibility dependencies (an encode that reads memory runs after everything it
   can see), and each wave encodes all its chunks of all rows in ONE batched
   forward.  The QKV GEMM of every layer writes straight into a per-layer pool,
@@ -34,9 +36,11 @@ import torch
 from ..chunking import partition_reference_tokens
 from ..memory.gists import kmeanspp_random_stream
 from ..memory.gists.strategies import local_generator
+from ..config import ResolverServiceConfig
 from ..memory.services import plan_cache_builds
 from ..ops import _ext
 from ..ops.kernels import MemoryView, WeightSlot, attention, layer_norm, linear, lm_head_loss, lm_head_logits, mlp
+from .native_plan import NativeBatchPlan, native_config
 from .tiny import PRATransformerBlock, TinyPRAModel
 
 _AGG = {"max": 0, "mean": 1, "logsumexp": 2}
@@ -303,7 +307,7 @@ class Namespace:
 class BatchMemory:
     """All rows' encoded references of one batch: pools, gists and chunk tables per layer."""
 
-    def __init__(self, runtime, entries, chunks, rows, seq_len, device):
+    def __init__(self, runtime, entries, chunks, rows, seq_len, device, chunk_tables=None, prompt_ns=None):
         cfg = runtime.cfg
         self.entries, self.chunks, self.rows = entries, chunks, rows
         self.seq_len = seq_len
@@ -323,9 +327,11 @@ class BatchMemory:
         self.gist_v = list(self.gist_v_all.unbind(0))
         self.gist_count_all = torch.zeros((L, n_seq), device=device, dtype=torch.int32)
         self.gist_count = list(self.gist_count_all.unbind(0))
-        self.chunk_start, self.chunk_len, self.chunk_pool_row = _upload(
-            device, [c.token_start for c in chunks], [len(c.token_ids) for c in chunks],
-            [c.seq * seq_len for c in chunks])
+        if chunk_tables is None:
+            chunk_tables = _upload(device, [c.token_start for c in chunks], [len(c.token_ids) for c in chunks],
+                                   [c.seq * seq_len for c in chunks])
+        self.chunk_start, self.chunk_len, self.chunk_pool_row = chunk_tables
+        self.prompt_ns = prompt_ns  # (device arrays, empty) of the prompt's namespace, when planned natively
 
     def k_view(self, layer: int, d: int) -> torch.Tensor:
         return self.pools[layer][:, d:2 * d]
@@ -463,12 +469,24 @@ class DeviceRuntime:
         self.anchor = torch.zeros(1, device=self.device, requires_grad=True)  # puts embeddings on the tape
         self.kmeans_tables = KMeansTables(cfg, self.device)
         self._prefetched_rows: tuple | None = None  # (metadata rows, {row: RowPlan})
+        self._prefetched_native: tuple | None = None  # (metadata rows, NativeBatchPlan)
         self.upcoming: list | None = None  # next batch's rows, planned in slices during this step
         self._last_tokenizer = None
         self._last_resolver = None
         self.last_routing: dict[int, LayerRouting] = {}
         self.last_memory: BatchMemory | None = None
         self.last_namespace: Namespace | None = None
+
+    @classmethod
+    def for_planning(cls, model: TinyPRAModel, device="cpu") -> "DeviceRuntime":
+        """A runtime that only plans cache builds (no parameters, no device buffers): the
+        host half of the device path, usable without a GPU."""
+        rt = cls.__new__(cls)
+        rt.model, rt.cfg, rt.device = model, model.cfg, torch.device(device)
+        rt.kmeans_tables = KMeansTables(model.cfg, rt.device)
+        rt._prefetched_rows = rt._prefetched_native = None
+        rt.upcoming = rt._last_tokenizer = rt._last_resolver = None
+        return rt
 
     grad_hooks = None  # optional: before_stack() / after_layer(l) calls during the backward
 
@@ -634,6 +652,23 @@ class DeviceRuntime:
             entries.append(record)
         return RowPlan(item, cache, builder, entries, chunks)
 
+    def plan_native(self, metadata_rows: list[dict], tokenizer, resolver_config=None) -> NativeBatchPlan | None:
+        """The batch plan from the native planner, or ``None`` when it needs the Python planner."""
+        ext = _ext.load()
+        if ext is None or not hasattr(ext, "plan_batch"):
+            return None
+        settings = native_config(self.cfg, ResolverServiceConfig.from_value(resolver_config))
+        if settings is None:
+            return None
+        rows = list(metadata_rows)
+        out = ext.plan_batch(rows, tokenizer, settings)
+        if out is None:
+            return None
+        plan = NativeBatchPlan(out, rows, lambda r: self.plan_row(rows[r], tokenizer, resolver_config))
+        if self.cfg.gist_mode == "kmeans":
+            plan.fill_kmeans(self.kmeans_tables)
+        return plan
+
     def plan_batch(self, metadata_rows: list[dict], tokenizer, resolver_config=None,
                    row_plans: dict | None = None) -> "BatchPlan":
         """Host half of the cache build: every row's plan (taken from ``row_plans`` when
@@ -734,6 +769,7 @@ class DeviceRuntime:
                     put(t, name, arr)
                 t["ns_empty"] = len(host[3]) == 0
             t["rows_entries"] = rows_entries
+            t["has_ns"] = rows_entries is not None
             t["n"], t["max_len"] = n, max(lens) if lens else 1
             tables.append(t)
         plan.wave_tables = tables
@@ -753,6 +789,13 @@ class DeviceRuntime:
         if tokenizer is None:
             return
         resolver_config = resolver_config if resolver_config is not None else self._last_resolver
+        if _NATIVE_PLANNER:
+            if self._prefetched_native is not None and self._prefetched_native[0] is metadata_rows:
+                return
+            plan = self.plan_native(metadata_rows, tokenizer, resolver_config)
+            if plan is not None:
+                self._prefetched_native = (metadata_rows, plan)
+                return
         if self._prefetched_rows is None or self._prefetched_rows[0] is not metadata_rows:
             self._prefetched_rows = (metadata_rows, {})
         done = self._prefetched_rows[1]
@@ -767,18 +810,34 @@ class DeviceRuntime:
     def build_memory(self, metadata_rows: list[dict], tokenizer, resolver_config=None):
         """Plan (or take the prefetched plan of) the batch, then encode all rows' chunks wave by wave."""
         self._last_tokenizer, self._last_resolver = tokenizer, resolver_config
+        plan = None
+        if self._prefetched_native is not None and self._prefetched_native[0] is metadata_rows:
+            plan = self._prefetched_native[1]
+        self._prefetched_native = None
         ready = {}
         if self._prefetched_rows is not None and self._prefetched_rows[0] is metadata_rows:
             ready = self._prefetched_rows[1]
         self._prefetched_rows = None
-        plan = self.plan_batch(metadata_rows, tokenizer, resolver_config, ready)
+        if plan is None and _NATIVE_PLANNER and not ready:
+            plan = self.plan_native(metadata_rows, tokenizer, resolver_config)
+        if plan is None:
+            plan = self.plan_batch(metadata_rows, tokenizer, resolver_config, ready)
+            for cache, builder in zip(plan.caches, plan.builders):
+                cache.resolution_events = list(builder.events)
+                cache.dependencies = list(builder.dependencies)
         caches, builders, entries, chunks, rows, seq_len = (plan.caches, plan.builders, plan.entries, plan.chunks,
                                                             plan.rows, plan.seq_len)
-        memory = BatchMemory(self, entries, chunks, rows, seq_len, self.device)
         host = torch.from_numpy(plan.packed)
         if self.device.type == "cuda":
             host = host.pin_memory()
         packed = host.to(self.device, non_blocking=True)
+        chunk_tables = prompt_ns = None
+        if getattr(plan, "native", False):
+            pt = plan.prompt_table
+            view = lambda name: packed[pt[name][0]: pt[name][0] + pt[name][1]]  # noqa: E731
+            chunk_tables = (view("chunk_start"), view("chunk_len"), view("chunk_pool_row"))
+            prompt_ns = ([view(f"ns{i}") for i in range(6)], bool(pt["ns_empty"]))
+        memory = BatchMemory(self, entries, chunks, rows, seq_len, self.device, chunk_tables, prompt_ns)
         with torch.no_grad():
             start = 0
             for wave_chunks, table in zip(plan.waves, plan.wave_tables):
@@ -802,9 +861,9 @@ class DeviceRuntime:
         x = ext.embed_add(view("ids"), None, L, self.tok_emb_w, self.pos_emb_w)
         valid = view("valid", torch.uint8).view(n, L)
         namespace = None
-        if table["rows_entries"] is not None:
+        if table["has_ns"]:
             arrays = [view(name) for name in ("ns0", "ns1", "ns2", "ns3", "ns4", "ns5")]
-            namespace = Namespace(table["rows_entries"], memory.entries, memory.chunks, self.device, arrays)
+            namespace = Namespace(table.get("rows_entries"), memory.entries, memory.chunks, self.device, arrays)
             namespace.empty = table["ns_empty"]
         rows = slice(first_seq * L, (first_seq + n) * L)
         self.run_blocks(x, n, L, valid, namespace, memory, stop_after_kv=True, pool_rows=rows,
@@ -842,7 +901,11 @@ class DeviceRuntime:
         valid = attention_mask.to(torch.uint8).contiguous() if attention_mask is not None else None
         namespace = None
         if memory is not None:
-            namespace = Namespace(memory.rows, memory.entries, memory.chunks, self.device)
+            if memory.prompt_ns is not None:
+                namespace = Namespace(memory.rows, memory.entries, memory.chunks, self.device, memory.prompt_ns[0])
+                namespace.empty = memory.prompt_ns[1]
+            else:
+                namespace = Namespace(memory.rows, memory.entries, memory.chunks, self.device)
             self.last_namespace = namespace
         budget = cfg.effective_model_max_context_tokens - t - cfg.context_safety_reserve_tokens
         if budget < 0:
@@ -886,6 +949,8 @@ class _IdsOnlyTokenizer:
 # stack_train_forward / stack_train_backward (the same kernels in the same order as the
 # per-layer autograd functions); PRA_TRAIN_STACK=python selects the per-layer path.
 _NATIVE_TRAIN_STACK = os.environ.get("PRA_TRAIN_STACK", "native").lower() != "python"
+# The native cache-build planner (csrc/planner.cpp); PRA_PLANNER=python keeps the Python planner.
+_NATIVE_PLANNER = os.environ.get("PRA_PLANNER", "native").lower() != "python"
 
 
 class _TrainStack(torch.autograd.Function):
@@ -1066,9 +1131,6 @@ def device_batch_step(model, batch, device, tokenizer, resolver_config, cache_co
     am = batch["attention_mask"]
     tokens = int(am.sum()) if am.device.type == "cpu" else am.sum()
     b = ids.shape[0]
-    for cache, builder in zip(caches, builders):
-        cache.resolution_events = list(builder.events)
-        cache.dependencies = list(builder.dependencies)
     metrics = {"cache_build_duration_seconds": build_s / max(b, 1), "cache_build_total_duration_seconds": build_s,
                "logical_batch_size": float(b), "prompt_forward_calls": 1.0}
     return loss, {"tokens": tokens, "examples": b, "batch": batch, "caches": caches, "metrics": metrics,

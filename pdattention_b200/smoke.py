@@ -1,4 +1,9 @@
-"""A tiny end-to-end TinyGPT-PRA training step used by the smoke check and GPU tests."""
+"""A tiny end-to-end TinyGPT-PRA training step used by the smoke check and GPU tests.
+
+The model has head width 64 (d_model 128, 2 heads), so the step runs the
+tcgen05/TMEM attention kernels (forward, packed short-sequence forward, dQ and
+dK/dV) rather than the mma.sync ones kept for head width 32.
+"""
 
 from __future__ import annotations
 
@@ -15,7 +20,7 @@ from .pra_train import _pra_batch_step
 
 
 def tiny_config(vocab: int) -> PRAConfig:
-    return PRAConfig(vocab_size=vocab, d_model=128, n_heads=4, n_layers=2, max_seq_len=256, model_variant="td_pra",
+    return PRAConfig(vocab_size=vocab, d_model=128, n_heads=2, n_layers=2, max_seq_len=256, model_variant="td_pra",
                      chunking_mode="fixed", fixed_chunk_tokens=32, top_k_references=2, top_k_chunks_per_reference=2,
                      gist_mode="kmeans", gists_per_chunk=2, recursive_refs_enabled=True, trigger_threshold=-1.0,
                      device="cuda")

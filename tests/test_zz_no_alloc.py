@@ -1,12 +1,13 @@
 """The allocation-free column-sum entry point, called through its exported C symbol.
 
 ``pra_colsum_noalloc`` is for callers that cannot allocate device memory where
-they call it (hosts that reserve all memory up front, or code issued during
-CUDA-graph capture where cudaMalloc is illegal).  It must give the same result
-as the library's ordinary column-sum op, on consecutive calls that reuse its
-fixed scratch array, and must refuse shapes that would overflow that array.
-This file sorts last so a run that stops at the first failure has already run
-every other test.
+they call it: hosts that reserve all device memory up front, or code running
+where its host forbids calls that can synchronise the device (cudaMalloc can).
+It must give the same column sums as the library's ordinary op and as an fp32
+``torch.sum``, on consecutive calls that reuse its fixed scratch array; it must
+accept a shape that fills that array exactly and refuse one that would overflow
+it or that hands it a misaligned matrix.  This file sorts last so a run that
+stops at the first failure has already run every other test.
 """
 
 import ctypes
@@ -14,7 +15,19 @@ import ctypes
 import pytest
 import torch
 
-pytestmark = pytest.mark.gpu
+
+def _load():
+    from pdattention_b200.ops import _ext
+
+    so = _ext._so_path()
+    if so is None:
+        pytest.skip("extension not built")
+    handle = ctypes.CDLL(str(so))
+    fn = handle.pra_colsum_noalloc
+    fn.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+    fn.restype = ctypes.c_int
+    handle.pra_colsum_noalloc_capacity.restype = ctypes.c_longlong
+    return handle
 
 
 @pytest.fixture(scope="module")
@@ -24,14 +37,7 @@ def lib():
     from pdattention_b200.ops import _ext
 
     _ext.require()
-    so = _ext._so_path()
-    assert so is not None, "extension not built"
-    handle = ctypes.CDLL(str(so))
-    fn = handle.pra_colsum_noalloc
-    fn.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
-    fn.restype = ctypes.c_int
-    handle.pra_colsum_noalloc_capacity.restype = ctypes.c_longlong
-    return handle
+    return _load()
 
 
 def _call(lib, g: torch.Tensor, out: torch.Tensor) -> int:
@@ -40,7 +46,15 @@ def _call(lib, g: torch.Tensor, out: torch.Tensor) -> int:
                                   ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(stream))
 
 
-def test_matches_existing_colsum_on_consecutive_calls(lib):
+def _check(out: torch.Tensor, g: torch.Tensor) -> None:
+    expected = g.float().sum(dim=0)
+    err = (out.float() - expected).abs().max().item()
+    scale = expected.abs().max().item() + 1e-6
+    assert err <= 2e-2 * scale, (tuple(g.shape), err, scale)
+
+
+@pytest.mark.gpu
+def test_matches_fp32_sum_and_existing_colsum_on_consecutive_calls(lib):
     from pdattention_b200.ops._ext import require
 
     ext = require()
@@ -49,13 +63,25 @@ def test_matches_existing_colsum_on_consecutive_calls(lib):
         g = torch.randn(m, n, device="cuda", generator=gen).bfloat16()
         out = torch.empty(n, device="cuda", dtype=torch.bfloat16)
         assert _call(lib, g, out) == 0
-        expected = ext.colsum(g)
         torch.cuda.synchronize()
-        err = (out.float() - expected.float()).abs().max().item()
-        scale = expected.float().abs().max().item() + 1e-6
-        assert err <= 2e-2 * scale, (m, n, err, scale)
+        _check(out, g)
+        expected = ext.colsum(g)
+        assert torch.equal(out, expected), (m, n)  # same kernels, same order of summation
 
 
+@pytest.mark.gpu
+def test_accepts_a_shape_that_fills_the_scratch_exactly(lib):
+    capacity = lib.pra_colsum_noalloc_capacity()
+    m, n = 16384, 4096  # 256 partial rows x 4096 columns
+    assert 256 * n == capacity
+    g = torch.randn(m, n, device="cuda", generator=torch.Generator(device="cuda").manual_seed(7)).bfloat16()
+    out = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    assert _call(lib, g, out) == 0
+    torch.cuda.synchronize()
+    _check(out, g)
+
+
+@pytest.mark.gpu
 def test_rejects_shapes_beyond_the_scratch_capacity(lib):
     capacity = lib.pra_colsum_noalloc_capacity()
     m, n = 8192, 8200  # 128 partial rows x 8200 columns > capacity
@@ -63,3 +89,12 @@ def test_rejects_shapes_beyond_the_scratch_capacity(lib):
     g = torch.zeros(m, n, device="cuda", dtype=torch.bfloat16)
     out = torch.empty(n, device="cuda", dtype=torch.bfloat16)
     assert _call(lib, g, out) != 0
+
+
+def test_rejects_misaligned_input_before_touching_the_device():
+    """A bf16 view starting at an odd element is refused with an error code, not launched."""
+    lib = _load()
+    rc = lib.pra_colsum_noalloc(ctypes.c_void_p(0x10002), 4, 8, ctypes.c_void_p(0x20000), ctypes.c_void_p(0))
+    assert rc != 0
+    rc = lib.pra_colsum_noalloc(ctypes.c_void_p(0x10000), 4, 7, ctypes.c_void_p(0x20000), ctypes.c_void_p(0))
+    assert rc != 0  # odd N
