@@ -1,27 +1,32 @@
-"""Random flat memory-QA smoke examples (``src/pra_core/synthetic_memory.py``)."""
+"""Flat memory-QA smoke examples: one referenced note per example holding a code word.
+
+Each example's prompt asks for the code stored in its single reference; the
+reference's full text states the code among filler sentences and its summary
+only says that a code exists, so answering needs the memory, not the summary.
+Draws use the module-level ``random`` state (seed it for repeatable sets).
+"""
 
 import random
 
 from .datasets import DatasetExample
 from .references import ReferenceTable
 
-_COLOURS = ("red", "blue", "green", "yellow", "purple")
-_ANIMALS = ("otter", "falcon", "tiger", "whale", "lynx")
+_ADJECTIVES = ("amber", "cobalt", "jade", "scarlet", "violet", "silver")
+_NOUNS = ("heron", "badger", "comet", "maple", "harbor", "glacier")
 
 
 def make_synthetic_examples(n: int = 100) -> list[DatasetExample]:
     examples = []
     for i in range(n):
-        code = f"{random.choice(_COLOURS)}-{random.choice(_ANIMALS)}-{i}"
+        code = "-".join((random.choice(_ADJECTIVES), random.choice(_NOUNS), str(i)))
         uri = f"mem://doc{i}#summary"
-        body = (f"Document {i}. This document contains project notes. The secret code is {code}. "
-                f"The owner is team alpha. The rest of the document is filler text about systems and memory.")
-        summary = f"Document {i} summary: contains a secret code and project notes."
         table = ReferenceTable()
-        handle = table.register(uri, summary=summary)
+        handle = table.register(uri, summary=f"Note {i}: records an access code among general notes.")
+        text = (f"Note {i}. General notes about storage and scheduling follow. "
+                f"Access code: {code}. Maintained by the platform group. "
+                f"Further paragraphs discuss caches, queues and retries.")
         examples.append(DatasetExample(
-            id=f"synthetic_{i}", prompt=f"Question: what is the secret code in {handle.token}? Answer:",
-            target=f" {code}\n", refs={uri: body}, summaries={uri: summary}, reference_table=table,
-            expected_ref_ids=[handle.id],
-        ))
+            id=f"synthetic_{i}", prompt=f"Question: what is the access code in {handle.token}? Answer:",
+            target=f" {code}\n", refs={uri: text}, summaries={uri: handle.summary}, reference_table=table,
+            expected_ref_ids=[handle.id]))
     return examples

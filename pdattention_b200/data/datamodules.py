@@ -1,8 +1,16 @@
-"""Loader wrapper with the reference's 80/10/10 seeded split (``src/data/datamodules.py``).
+"""Stage data module: dataset, tokenizer, collator and train/val/test loaders.
 
-Adds rank-aware sharding for data-parallel training: with ``world_size > 1``
-each rank iterates a disjoint ``DistributedSampler`` shard of the train split.
+Public surface of ``src/data/datamodules.py:9-108`` (constructor arguments,
+``load`` / ``train_loader`` / ``val_loader`` / ``test_loader`` /
+``build_reference_tables``).  The split is the reference's seeded 80/10/10
+``random_split`` (so a seed selects the same examples in both frameworks); a
+character tokenizer, when none is given, is fitted to every question, answer,
+reference summary and reference text.  For data-parallel training
+(``world_size > 1``) the train loader iterates this rank's disjoint
+``DistributedSampler`` shard, reshuffled per epoch with ``sampler.set_epoch``.
 """
+
+from __future__ import annotations
 
 import torch
 from torch.utils.data import DataLoader, DistributedSampler, random_split
@@ -12,33 +20,55 @@ from .datasets import PRADataset, dataset_class_for_stage
 from .tokenizer import PRATokenizer
 
 
+def split_sizes(n: int) -> tuple[int, int, int] | None:
+    """(train, val, test) sizes of ``n`` examples, or ``None`` when every split is the whole set."""
+    if n < 3:
+        return None
+    val = max(1, int(n * 0.1))
+    train = max(1, int(n * 0.8))
+    test = n - train - val
+    return (train, val, test) if test > 0 else (n - val - 1, val, 1)
+
+
+def tokenizer_corpus(dataset) -> list[str]:
+    """Texts a fitted character vocabulary must cover."""
+    texts = []
+    for sample in dataset:
+        texts.append(f"{sample.question} {sample.answer}")
+        texts.extend(piece for ref in sample.references
+                     for piece in (ref.summary or "", str(ref.metadata.get("text", ""))))
+    return texts
+
+
 class PRADataModule:
     def __init__(self, dataset_stage: str, data_dir: str = "data", max_examples: int | None = None,
                  batch_size: int = 8, max_seq_len: int = 96, shuffle: bool = True, num_workers: int = 0,
                  pin_memory: bool = False, persistent_workers: bool = False, tokenizer=None, split_seed: int = 0,
                  rank: int = 0, world_size: int = 1):
-        self.dataset_stage = dataset_stage
-        self.data_dir = data_dir
-        self.max_examples = max_examples
-        self.batch_size = batch_size
-        self.max_seq_len = max_seq_len
-        self.shuffle = shuffle
-        self.num_workers = num_workers
-        self.pin_memory = pin_memory
-        self.persistent_workers = persistent_workers and num_workers > 0
+        self.dataset_stage, self.data_dir, self.max_examples = dataset_stage, data_dir, max_examples
+        self.batch_size, self.max_seq_len, self.shuffle = batch_size, max_seq_len, shuffle
+        self.num_workers, self.pin_memory = num_workers, pin_memory
+        self.persistent_workers = bool(persistent_workers and num_workers > 0)
         self.tokenizer = tokenizer
         self.split_seed = int(split_seed)
         self.rank, self.world_size = int(rank), int(world_size)
         self.dataset: PRADataset | None = None
-        self.train_dataset = self.val_dataset = self.test_dataset = None
         self.collator: PRACollator | None = None
+        self._splits: dict[str, object] = {}
+
+    # split datasets (None before load())
+    train_dataset = property(lambda self: self._splits.get("train"))
+    val_dataset = property(lambda self: self._splits.get("val"))
+    test_dataset = property(lambda self: self._splits.get("test"))
 
     def load(self):
         self.dataset = dataset_class_for_stage(self.dataset_stage)(self.data_dir, max_examples=self.max_examples)
-        if self.tokenizer is None:
-            self.tokenizer = PRATokenizer(self._corpus(self.dataset))
+        self.tokenizer = self.tokenizer or PRATokenizer(tokenizer_corpus(self.dataset))
         self.collator = PRACollator(self.tokenizer, max_seq_len=self.max_seq_len)
-        self.train_dataset, self.val_dataset, self.test_dataset = self._split(self.dataset, seed=self.split_seed)
+        sizes = split_sizes(len(self.dataset))
+        parts = ([self.dataset] * 3 if sizes is None else
+                 random_split(self.dataset, list(sizes), generator=torch.Generator().manual_seed(self.split_seed)))
+        self._splits = dict(zip(("train", "val", "test"), parts))
         return self
 
     def train_loader(self) -> DataLoader:
@@ -58,33 +88,18 @@ class PRADataModule:
     def _loader(self, dataset, shuffle: bool, shard: bool = False) -> DataLoader:
         if dataset is None:
             raise RuntimeError("PRADataModule.load() must be called before requesting loaders.")
-        sampler = None
-        if shard and self.world_size > 1:
-            sampler = DistributedSampler(dataset, num_replicas=self.world_size, rank=self.rank, shuffle=shuffle,
-                                         seed=self.split_seed)
-            shuffle = False
-        return DataLoader(dataset, batch_size=self.batch_size, shuffle=shuffle, sampler=sampler,
+        sampler = (DistributedSampler(dataset, num_replicas=self.world_size, rank=self.rank, shuffle=shuffle,
+                                      seed=self.split_seed) if shard and self.world_size > 1 else None)
+        return DataLoader(dataset, batch_size=self.batch_size, shuffle=shuffle and sampler is None, sampler=sampler,
                           num_workers=self.num_workers, pin_memory=self.pin_memory,
                           persistent_workers=self.persistent_workers, collate_fn=self.collator)
 
-    @staticmethod
-    def _corpus(dataset) -> list[str]:
-        texts = []
-        for sample in dataset:
-            texts.append(sample.question + " " + sample.answer)
-            for ref in sample.references:
-                texts.append(ref.summary or "")
-                texts.append(str(ref.metadata.get("text", "")))
-        return texts
+    # kept for callers of the reference's private helpers
+    _corpus = staticmethod(tokenizer_corpus)
 
     @staticmethod
     def _split(dataset, *, seed: int = 0):
-        n = len(dataset)
-        if n < 3:
+        sizes = split_sizes(len(dataset))
+        if sizes is None:
             return dataset, dataset, dataset
-        n_train, n_val = max(1, int(n * 0.8)), max(1, int(n * 0.1))
-        n_test = n - n_train - n_val
-        if n_test <= 0:
-            n_test = 1
-            n_train = n - n_val - n_test
-        return random_split(dataset, [n_train, n_val, n_test], generator=torch.Generator().manual_seed(seed))
+        return random_split(dataset, list(sizes), generator=torch.Generator().manual_seed(seed))
