@@ -838,7 +838,9 @@ int64_t dp_signal_words(int64_t world) { return 2LL * pra_dp_allreduce_blocks() 
 // chunk_pool_row; route_cfg = {k_ref, k_chunk, gist_agg, ref_agg, threshold, budget,
 // gist_only, full_reference, deduplicate, max_sel, max_mem}.
 // pool (optional) receives every layer's QKV rows; mem_pool is the [L, rows, 3D] pool the
-// routed memory keys are read from.
+// routed memory keys are read from.  after_qkv (a callable or None) runs after every layer's QKV
+// GEMM with the layer index: the cache build computes that layer's gists of every chunk there,
+// so one layer-synchronous pass serves chunks that route over each other's memory.
 // Returns {x, then per routed layer: mem_idx, ints, sel_i, sel_f}.
 std::vector<torch::Tensor> stack_forward(torch::Tensor x, int64_t B, int64_t T, std::vector<torch::Tensor> weights,
                                          int64_t heads, int64_t head_dim, double eps,
@@ -847,9 +849,11 @@ std::vector<torch::Tensor> stack_forward(torch::Tensor x, int64_t B, int64_t T, 
                                          std::vector<torch::Tensor> ns,
                                          c10::optional<torch::Tensor> gists, c10::optional<torch::Tensor> gist_count,
                                          c10::optional<torch::Tensor> gist_kv, c10::optional<torch::Tensor> budget_rows,
-                                         c10::optional<torch::Tensor> query_rows, std::vector<double> route_cfg) {
+                                         c10::optional<torch::Tensor> query_rows, std::vector<double> route_cfg,
+                                         pybind11::object after_qkv) {
   c10::cuda::CUDAGuard guard(x.device());
   TORCH_CHECK(weights.size() % 12 == 0, "stack_forward needs 12 weight tensors per layer");
+  const bool hooked = !after_qkv.is_none();
   const int64_t L = weights.size() / 12;
   const int64_t D = heads * head_dim;
   const int64_t M = B * T;
@@ -869,6 +873,7 @@ std::vector<torch::Tensor> stack_forward(torch::Tensor x, int64_t B, int64_t T, 
     torch::Tensor qkv = pool.has_value() ? pool->select(0, l).narrow(0, pool_row0, M)
                                          : torch::empty({M, 3 * D}, x.options());
     gemm("tn", h, w[2], c10::nullopt, qkv, w[3], c10::nullopt, 1.0, 0.0, c10::nullopt);
+    if (hooked) after_qkv(l);  // e.g. this layer's gists of every chunk, before any routing reads them
     if (stop_after_kv && l == L - 1) break;
     auto qkv3 = qkv.view({B, T, 3 * D});
     c10::optional<torch::Tensor> mk, mv, mi, ml;

@@ -64,6 +64,7 @@ struct Config {
   int max_chunks = -1;  // -1: unlimited
   int overflow = 0;     // 0 truncate, 1 merge_tail, 2 error
   bool kmeans = false;
+  bool single_pass = false;  // one encode group over every chunk (layer-synchronous cache build)
 };
 
 // A resolved document of one row (shared by every URI that resolves to it).
@@ -522,6 +523,7 @@ py::object plan_batch_impl(const py::list& rows, const py::object& tokenizer, co
   cfg.max_chunks = c["max_chunks"].cast<int>();
   cfg.overflow = c["overflow"].cast<int>();
   cfg.kmeans = c["kmeans"].cast<bool>();
+  cfg.single_pass = c.contains("single_pass") && c["single_pass"].cast<bool>();
   if (cfg.chunk_size <= 0 || cfg.chunk_size - cfg.overlap <= 0 || cfg.max_children < 0) return py::none();
 
   Tokenizer tok;
@@ -605,6 +607,12 @@ py::object plan_batch_impl(const py::list& rows, const py::object& tokenizer, co
           chunks[ch].seq = seq++;
           waves[w].push_back(ch);
         }
+
+  if (cfg.single_pass && n_waves > 1) {  // every chunk in one group, in encode-sequence order
+    std::vector<int> all;
+    for (const auto& w : waves) all.insert(all.end(), w.begin(), w.end());
+    waves.assign(1, all);
+  }
 
   // 3. packed tables
   std::vector<std::vector<int>> rank_memo;

@@ -60,106 +60,108 @@ class PreparedPromptBatch:
 
 
 def prepare_prompt_for_pra(input_ids: Sequence[int] | torch.Tensor, config) -> PreparedPrompt:
-    ids = tuple(int(t) for t in input_ids)
+    """Split one prompt into its direct tail and (``implicit_reference`` mode) its implicit head."""
+    ids = tuple(map(int, input_ids))
     limit = int(config.effective_prompt_direct_tokens)
     mode = config.prompt_overflow_mode
-    if len(ids) <= limit:
+    overflow = len(ids) - limit
+    if overflow <= 0:
         return PreparedPrompt(ids, (), len(ids), limit, mode)
+    if mode not in ("error", "truncate", "implicit_reference"):
+        raise ValueError(f"Unsupported prompt_overflow_mode: {mode}")
     if mode == "error":
         raise ValueError(f"Prompt has {len(ids)} tokens, exceeding direct limit {limit}.")
-    if mode == "truncate":
-        return PreparedPrompt(ids[-limit:], (), len(ids), limit, "truncate")
-    if mode != "implicit_reference":
-        raise ValueError(f"Unsupported prompt_overflow_mode: {mode}")
-    return PreparedPrompt(ids[-limit:], ids[:-limit], len(ids), limit, "implicit_reference")
+    head = ids[:overflow] if mode == "implicit_reference" else ()
+    return PreparedPrompt(ids[overflow:], head, len(ids), limit, mode)
 
 
-def _valid_ids(values: torch.Tensor, mask: torch.Tensor | None) -> list[int]:
-    if mask is None:
-        return [int(v) for v in values]
-    return [int(v) for v, keep in zip(values, mask) if bool(keep)]
+def _row_tokens(values: torch.Tensor, mask: torch.Tensor | None, full) -> list[int]:
+    """A row's untruncated tokens from metadata when the collator kept them, else its valid ids."""
+    if full is not None:
+        return list(map(int, full))
+    keep = values if mask is None else values[mask.bool()]
+    return keep.tolist()
 
 
-def _source_rows(input_ids, attention_mask, labels, metadata):
-    ids_rows, label_rows = [], ([] if labels is not None else None)
-    for row in range(input_ids.shape[0]):
-        item = metadata[row] if metadata is not None else {}
-        mask = attention_mask[row] if attention_mask is not None else None
-        ids = item.get("full_input_ids")
-        ids_rows.append([int(v) for v in (ids if ids is not None else _valid_ids(input_ids[row], mask))])
-        if label_rows is not None:
-            lab = item.get("full_labels")
-            label_rows.append([int(v) for v in (lab if lab is not None else _valid_ids(labels[row], mask))])
-    return ids_rows, label_rows
-
-
-def _pad_rows(rows, *, value, device, dtype):
-    if not rows or any(not r for r in rows):
+def _right_pad(rows: list[list[int]], value: int, device, dtype) -> tuple[torch.Tensor, torch.Tensor]:
+    if not rows or min(map(len, rows)) == 0:
         raise ValueError("Prompt preparation requires at least one token per batch row.")
-    width = max(len(r) for r in rows)
-    out = torch.full((len(rows), width), value, dtype=dtype)
-    mask = torch.zeros((len(rows), width), dtype=torch.long)
-    for i, r in enumerate(rows):
-        out[i, : len(r)] = torch.tensor(r, dtype=dtype)
-        mask[i, : len(r)] = 1
-    return out.to(device), mask.to(device)
+    tensors = [torch.tensor(r, dtype=dtype) for r in rows]
+    padded = torch.nn.utils.rnn.pad_sequence(tensors, batch_first=True, padding_value=value)
+    lengths = torch.tensor([len(r) for r in rows])
+    mask = (torch.arange(padded.shape[1])[None, :] < lengths[:, None]).long()
+    return padded.to(device), mask.to(device)
 
 
 def head_metadata(row: int, split: PreparedPrompt, max_prompt_gists) -> dict:
+    """Metadata recorded on a row's implicit head entry."""
     return {"implicit": True, "source": "prompt", "kind": "head", "display_name": IMPLICIT_PROMPT_HEAD_NAME,
             "prompt_row": row, "prompt_total_tokens": split.total_tokens, "prompt_direct_tokens": len(split.direct_ids),
             "prompt_implicit_tokens": len(split.implicit_ids), "max_prompt_gists": max_prompt_gists}
 
 
+def _encode_heads(model, tokenizer, heads: list[tuple[int, PreparedPrompt]], device) -> dict:
+    """row -> encoded implicit-head entry (batched when the model can, else one row at a time)."""
+    if not heads:
+        return {}
+    batched = getattr(model, "encode_prompt_heads", None)
+    if batched is not None:
+        return batched(heads, tokenizer, device)
+    cfg = model.cfg
+    return {row: model.encode_reference_tokens_to_cache(
+                IMPLICIT_PROMPT_HEAD_URI, split.implicit_ids, tokenizer, device,
+                metadata=head_metadata(row, split, cfg.max_prompt_gists), max_chunks=cfg.max_prompt_gists,
+                use_configured_max_chunks=False, max_chunk_tokens=cfg.effective_model_max_context_tokens,
+                historical_encoding=cfg.prompt_position_mode == "historical")
+            for row, split in heads}
+
+
+def _head_sizes(entry) -> tuple[int, int]:
+    """(chunks, gists of the first encoded layer) of a head entry."""
+    if entry is None:
+        return 0, 0
+    gists = 0
+    if entry.layer_memory:
+        gists = sum(int(c.routing_gist.k.shape[0]) for c in entry.layer_memory[min(entry.layer_memory)].chunks)
+    return int(entry.metadata.get("chunk_count", 0)), gists
+
+
 def prepare_prompt_batch_for_pra(model, tokenizer, input_ids: torch.Tensor, *, attention_mask=None, labels=None,
                                  metadata: list[dict] | None = None, caches: list[PRAMemoryCache] | None = None,
                                  pad_token_id: int = 0) -> PreparedPromptBatch:
-    """Split every row, right-pad the direct tails and encode each row's implicit head."""
+    """Split every row, right-pad the direct tails (and their labels), and put each row's encoded
+    implicit head into that row's cache (replacing an earlier head)."""
     if input_ids.ndim != 2:
         raise ValueError(f"Expected input_ids [batch,tokens], got {tuple(input_ids.shape)}.")
     batch = int(input_ids.shape[0])
     if metadata is not None and len(metadata) != batch:
         raise ValueError("Prompt metadata must align with input batch rows.")
-    caches = caches if caches is not None else [PRASimpleMemoryCache() for _ in range(batch)]
+    caches = [PRASimpleMemoryCache() for _ in range(batch)] if caches is None else caches
     if len(caches) != batch:
         raise ValueError("Prompt caches must align with input batch rows.")
     cfg = model.cfg
-    src_ids, src_labels = _source_rows(input_ids, attention_mask, labels, metadata)
-    splits = [prepare_prompt_for_pra(row, cfg) for row in src_ids]
-    direct, mask = _pad_rows([list(s.direct_ids) for s in splits], value=pad_token_id, device=input_ids.device,
-                             dtype=input_ids.dtype)
+    items = metadata if metadata is not None else [{}] * batch
+    masks = attention_mask if attention_mask is not None else [None] * batch
+    token_rows = [_row_tokens(input_ids[r], masks[r], items[r].get("full_input_ids")) for r in range(batch)]
+    splits = [prepare_prompt_for_pra(row, cfg) for row in token_rows]
+    direct, mask = _right_pad([list(s.direct_ids) for s in splits], pad_token_id, input_ids.device, input_ids.dtype)
     padded_labels = None
-    if src_labels is not None:
-        tails = [row[-len(s.direct_ids):] for row, s in zip(src_labels, splits)]
-        padded_labels, _ = _pad_rows(tails, value=pad_token_id, device=labels.device, dtype=labels.dtype)
-    heads = [(row, split) for row, split in enumerate(splits) if split.implicit_ids]
+    if labels is not None:
+        label_rows = [_row_tokens(labels[r], masks[r], items[r].get("full_labels")) for r in range(batch)]
+        padded_labels, _ = _right_pad([row[-len(s.direct_ids):] for row, s in zip(label_rows, splits)],
+                                      pad_token_id, labels.device, labels.dtype)
     for cache in caches:
         if hasattr(cache, "invalidate"):
             cache.invalidate(IMPLICIT_PROMPT_HEAD_URI)
-    encode_many = getattr(model, "encode_prompt_heads", None)
-    entries = {}
-    if heads:
-        if encode_many is not None:
-            entries = encode_many([(row, split) for row, split in heads], tokenizer, input_ids.device)
-        else:
-            for row, split in heads:
-                entries[row] = model.encode_reference_tokens_to_cache(
-                    IMPLICIT_PROMPT_HEAD_URI, split.implicit_ids, tokenizer, input_ids.device,
-                    metadata=head_metadata(row, split, cfg.max_prompt_gists), max_chunks=cfg.max_prompt_gists,
-                    use_configured_max_chunks=False, max_chunk_tokens=cfg.effective_model_max_context_tokens,
-                    historical_encoding=(cfg.prompt_position_mode == "historical"))
+    entries = _encode_heads(model, tokenizer, [(r, s) for r, s in enumerate(splits) if s.implicit_ids],
+                            input_ids.device)
     stats = []
-    for row, (split, cache) in enumerate(zip(splits, caches)):
-        chunks = gists = 0
+    for row, split in enumerate(splits):
         entry = entries.get(row)
         if entry is not None:
-            cache.put(entry)
-            chunks = int(entry.metadata.get("chunk_count", 0))
-            if entry.layer_memory:
-                first = entry.layer_memory[min(entry.layer_memory)]
-                gists = sum(int(c.routing_gist.k.shape[0]) for c in first.chunks)
+            caches[row].put(entry)
         stats.append(PromptPreparationStats(split.total_tokens, len(split.direct_ids), len(split.implicit_ids),
-                                            chunks, gists))
+                                            *_head_sizes(entry)))
     offsets = torch.tensor([cfg.prompt_tail_position_offset(len(s.implicit_ids), len(s.direct_ids)) for s in splits],
                            dtype=torch.long, device=input_ids.device)
     return PreparedPromptBatch(direct, mask, padded_labels, offsets, caches, splits, stats)

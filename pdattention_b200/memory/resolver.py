@@ -1,8 +1,12 @@
-"""URI resolution boundary (``src/pra_torch/resolver.py:11-95``).
+"""URI resolution: the boundary between PRA routing and wherever content lives.
 
-A resolver maps a URI (or its anchor-free base) to content, a local
-``<REF_n>`` -> child URI table, anchors, metadata, version and summary, and
-raises ``KeyError`` for unknown URIs.
+``InMemoryResolver`` serves documents from dictionaries (the contract of
+``src/pra_torch/resolver.py:11-95``): a URI, or failing that its anchor-free
+base (``doc#section`` -> ``doc``), maps to its text, a local ``<REF_n>`` -> child
+URI table, anchors, metadata, version and summary; an unknown URI raises
+``KeyError``.  A document value is either plain text or a structured dict whose
+fields override the resolver-wide side tables (``summaries``,
+``reference_tables``, ``metadata``, ``versions``).
 """
 
 from __future__ import annotations
@@ -24,9 +28,11 @@ class ResolvedReference:
     summary: str | None = None
 
 
-class InMemoryResolver:
-    """Dictionary-backed resolver; values are strings or structured dicts."""
+def _optional_str(value) -> str | None:
+    return None if value is None else str(value)
 
+
+class InMemoryResolver:
     def __init__(self, documents: dict, summaries: dict[str, str] | None = None,
                  reference_tables: dict[str, dict[str, str]] | None = None, metadata: dict[str, dict] | None = None,
                  versions: dict[str, str] | None = None):
@@ -36,34 +42,37 @@ class InMemoryResolver:
         self.metadata = metadata or {}
         self.versions = versions or {}
 
-    def _lookup(self, uri: str):
-        value = self.documents.get(uri)
-        if value is None:
-            value = self.documents.get(split_uri_anchor(uri)[0])
-        if value is None:
-            raise KeyError(f"Reference URI is not available: {uri}")
-        return value
+    def _document(self, uri: str):
+        for key in dict.fromkeys((uri, split_uri_anchor(uri)[0])):
+            value = self.documents.get(key)
+            if value is not None:
+                return value
+        raise KeyError(f"Reference URI is not available: {uri}")
+
+    def _fields(self, uri: str, value) -> tuple:
+        """(text, table, anchors, metadata, version, summary) of a stored value; side tables are
+        keyed by the requested URI and fill whatever a structured value leaves out."""
+        side_table = self.reference_tables.get(uri) or {}
+        side_meta = self.metadata.get(uri, {})
+        if not isinstance(value, dict):
+            return (str(value), dict(side_table), {}, dict(side_meta), self.versions.get(uri),
+                    self.summaries.get(uri))
+        return (str(value.get("text", "")), dict(value.get("reference_table") or side_table),
+                dict(value.get("anchors") or {}), {**side_meta, **dict(value.get("metadata") or {})},
+                value.get("version", self.versions.get(uri)), value.get("summary", self.summaries.get(uri)))
 
     def resolve(self, uri: str, summary_only: bool = False) -> ResolvedReference:
-        value = self._lookup(uri)
-        if isinstance(value, dict):
-            text = str(value.get("text", ""))
-            table = dict(value.get("reference_table") or self.reference_tables.get(uri) or {})
-            anchors = dict(value.get("anchors") or {})
-            meta = {**self.metadata.get(uri, {}), **dict(value.get("metadata") or {})}
-            version = value.get("version", self.versions.get(uri))
-            summary = value.get("summary", self.summaries.get(uri))
-        else:
-            text, table, anchors = str(value), dict(self.reference_tables.get(uri) or {}), {}
-            meta, version, summary = dict(self.metadata.get(uri, {})), self.versions.get(uri), self.summaries.get(uri)
-        return ResolvedReference(
-            uri=uri, text=str(summary or "") if summary_only else text,
-            reference_table={str(k): str(v) for k, v in table.items()}, anchors=anchors, metadata=meta,
-            version=str(version) if version is not None else None,
-            summary=str(summary) if summary is not None else None)
+        """The document behind ``uri``; ``summary_only`` returns the summary as the text."""
+        text, table, anchors, metadata, version, summary = self._fields(uri, self._document(uri))
+        return ResolvedReference(uri=uri, text=str(summary or "") if summary_only else text,
+                                 reference_table={str(token): str(child) for token, child in table.items()},
+                                 anchors=anchors, metadata=metadata, version=_optional_str(version),
+                                 summary=_optional_str(summary))
 
     def resolve_handle(self, handle: ReferenceHandle, summary_only: bool = False) -> HandleResolvedReference:
+        """The handle-oriented view: children as unnumbered handles (id -1) in table order."""
         resolved = self.resolve(handle.uri, summary_only=summary_only)
-        children = [ReferenceHandle(id=-1, token=t, uri=u) for t, u in resolved.reference_table.items()]
-        return HandleResolvedReference(handle=handle, text=resolved.text, children=children,
-                                       metadata={**resolved.metadata, "version": resolved.version})
+        return HandleResolvedReference(
+            handle=handle, text=resolved.text,
+            children=[ReferenceHandle(id=-1, token=token, uri=child) for token, child in resolved.reference_table.items()],
+            metadata={**resolved.metadata, "version": resolved.version})

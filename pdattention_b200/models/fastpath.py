@@ -509,12 +509,14 @@ class DeviceRuntime:
     # -- one decoder pass ---------------------------------------------------------
     def run_blocks(self, x: torch.Tensor, b: int, t: int, key_valid, routing, memory: BatchMemory | None,
                    stop_after_kv: bool = False, pool_rows: slice | None = None, budget: int = 0,
-                   query_rows: torch.Tensor | None = None):
+                   query_rows: torch.Tensor | None = None, after_qkv=None):
         """Run the block stack on ``x`` ``[b*t, D]``.
 
         ``routing`` is a ``Namespace`` (or ``None`` for no memory); with ``pool_rows``
         the QKV of every layer is written into those rows of the layer pool (cache
         build).  ``stop_after_kv`` skips the last block's attention and MLP.
+        ``after_qkv(layer)`` runs after each layer's QKV projection (no-grad native
+        stack only): the layer-synchronous cache build computes that layer's gists there.
         """
         cfg = self.cfg
         d = cfg.d_model
@@ -522,7 +524,9 @@ class DeviceRuntime:
             query_rows = query_rows.to(torch.int32)
         if not torch.is_grad_enabled():
             return self._run_blocks_native(x, b, t, key_valid, routing, memory, stop_after_kv, pool_rows, budget,
-                                           query_rows)
+                                           query_rows, after_qkv)
+        if after_qkv is not None:
+            raise RuntimeError("per-layer hooks run only in the no-grad native stack")
         if pool_rows is None and not stop_after_kv and _NATIVE_TRAIN_STACK:
             return _TrainStack.apply(x, self, b, t, key_valid, routing, memory, budget, query_rows)
         for li, layer in enumerate(self.layers):
@@ -566,7 +570,8 @@ class DeviceRuntime:
             self._stack_weight_list = out
         return self._stack_weight_list
 
-    def _run_blocks_native(self, x, b, t, key_valid, routing, memory, stop_after_kv, pool_rows, budget, query_rows):
+    def _run_blocks_native(self, x, b, t, key_valid, routing, memory, stop_after_kv, pool_rows, budget, query_rows,
+                           after_qkv=None):
         """The whole block stack in one native call (no autograd): cache build and no-grad forwards."""
         cfg = self.cfg
         d = cfg.d_model
@@ -586,10 +591,11 @@ class DeviceRuntime:
         out = ext.stack_forward(x.contiguous(), b, t, self._stack_weights(), cfg.n_heads, self.head_dim, 1e-5,
                                 key_valid, pool, row0, stop_after_kv, memory.pool if routed else None, ns, gists,
                                 counts, gist_kv, budget_rows,
-                                query_rows, settings)
+                                query_rows, settings, after_qkv)
         n_layers = cfg.n_layers
         per_layer = 7 + (1 if routed else 0)
         _ext.add_launches("stack_forward", n_layers * per_layer - (per_layer - 2 if stop_after_kv else 0))
+        # (gist launches made by after_qkv go through the counted extension proxy)
         if routed:
             for li in range(n_layers - (1 if stop_after_kv else 0)):
                 mem_idx, ints, sel_i, sel_f = out[1 + 4 * li: 5 + 4 * li]
@@ -652,6 +658,17 @@ class DeviceRuntime:
             entries.append(record)
         return RowPlan(item, cache, builder, entries, chunks)
 
+    def _single_pass(self) -> bool:
+        """Whether the cache build runs as one layer-synchronous pass over every chunk.
+
+        A chunk's layer-l attention reads only layer-l keys, values and gists of the
+        entries it may see, and those depend only on layer l-1 states, so computing
+        each layer for every chunk at once gives the values of an entry-by-entry
+        build (what the dependency waves order).  Gist-only materialisation reads
+        the gists as attention keys and keeps the wave order.
+        """
+        return _LAYER_SYNC and self.cfg.detail_materialization != "gist_only"
+
     def plan_native(self, metadata_rows: list[dict], tokenizer, resolver_config=None) -> NativeBatchPlan | None:
         """The batch plan from the native planner, or ``None`` when it needs the Python planner."""
         ext = _ext.load()
@@ -660,6 +677,7 @@ class DeviceRuntime:
         settings = native_config(self.cfg, ResolverServiceConfig.from_value(resolver_config))
         if settings is None:
             return None
+        settings["single_pass"] = self._single_pass()
         rows = list(metadata_rows)
         out = ext.plan_batch(rows, tokenizer, settings)
         if out is None:
@@ -708,6 +726,8 @@ class DeviceRuntime:
                         members.append(c)
                         seq += 1
             waves.append(members)
+        if self._single_pass() and len(waves) > 1:  # one encode group, in encode-sequence order
+            waves = [[c for members in waves for c in members]]
         plan = BatchPlan(metadata_rows, caches, builders, entries, chunks, rows, seq_len, waves)
         self._wave_tables(plan)
         return plan
@@ -866,23 +886,30 @@ class DeviceRuntime:
             namespace = Namespace(table.get("rows_entries"), memory.entries, memory.chunks, self.device, arrays)
             namespace.empty = table["ns_empty"]
         rows = slice(first_seq * L, (first_seq + n) * L)
+        hook = None
+        if self._single_pass():  # every layer's gists right after its QKV: one pass serves all chunks
+            hook = lambda layer: self._pool_gists(memory, table, view, layer)  # noqa: E731
         self.run_blocks(x, n, L, valid, namespace, memory, stop_after_kv=True, pool_rows=rows,
-                        budget=view("budget"), query_rows=view("last"))
-        self._pool_gists(memory, table, view)
+                        budget=view("budget"), query_rows=view("last"), after_qkv=hook)
+        if hook is None:
+            self._pool_gists(memory, table, view)
 
-    def _pool_gists(self, memory: BatchMemory, table: dict, view) -> None:
-        """One launch builds the wave's gists for every layer, written in place into the cache tables."""
+    def _pool_gists(self, memory: BatchMemory, table: dict, view, layer: int | None = None) -> None:
+        """One launch builds the group's gists for every layer (or for ``layer`` only), written in
+        place into the cache tables."""
         cfg = self.cfg
         d = cfg.d_model
         ext = _ext.require()
         pk, pv = memory.k_all(d), memory.v_all(d)
+        gk, gv, gn, gc = memory.gist_k_all, memory.gist_v_all, memory.gists_all, memory.gist_count_all
+        if layer is not None:
+            sel = slice(layer, layer + 1)
+            pk, pv, gk, gv, gn, gc = pk[sel], pv[sel], gk[sel], gv[sel], gn[sel], gc[sel]
         start, length, dest = view("gist_rows"), view("lens"), view("dest")
         if cfg.gist_mode == "mean":
-            ext.gist_mean_into(pk, pv, start, length, dest, memory.gist_k_all, memory.gist_v_all, memory.gists_all,
-                               memory.gist_count_all)
+            ext.gist_mean_into(pk, pv, start, length, dest, gk, gv, gn, gc)
             return
-        ext.gist_kmeans_into(pk, pv, start, length, dest, memory.gist_k_all, memory.gist_v_all, memory.gists_all,
-                             memory.gist_count_all, table["max_len"], cfg.gist_kmeans_max_iters,
+        ext.gist_kmeans_into(pk, pv, start, length, dest, gk, gv, gn, gc, table["max_len"], cfg.gist_kmeans_max_iters,
                              float(cfg.gist_kmeans_tol), bool(cfg.gist_kmeans_normalize),
                              cfg.gist_kmeans_init == "kmeans++", cfg.gist_kmeans_empty_cluster_policy == "farthest",
                              view("km_first"), self.kmeans_tables.idx, self.kmeans_tables.draws, view("km_off"), None)
@@ -951,6 +978,8 @@ class _IdsOnlyTokenizer:
 _NATIVE_TRAIN_STACK = os.environ.get("PRA_TRAIN_STACK", "native").lower() != "python"
 # The native cache-build planner (csrc/planner.cpp); PRA_PLANNER=python keeps the Python planner.
 _NATIVE_PLANNER = os.environ.get("PRA_PLANNER", "native").lower() != "python"
+# Cache build as one layer-synchronous pass (default) or one full pass per dependency wave.
+_LAYER_SYNC = os.environ.get("PRA_CACHE_BUILD", "layer").lower() != "waves"
 
 
 class _TrainStack(torch.autograd.Function):

@@ -127,3 +127,60 @@ def test_native_train_stack_matches_per_layer_autograd(cuda, tmp_path):
     assert torch.isfinite(g_native).all()
     err = (g_native - g_python).abs().max().item()
     assert err <= 2e-2 * g_python.abs().max().item(), err
+
+
+def test_layer_synchronous_cache_build_matches_wave_build(cuda, tmp_path, monkeypatch):
+    """One pass over every chunk, layer by layer, gives the memory an entry-by-entry (wave) build gives."""
+    from pdattention_b200.models import fastpath
+
+    torch.manual_seed(5)
+    tok, batch = tiny_batch(Path(tmp_path))
+    model = TinyPRAModel(tiny_config(tok.vocab_size)).to(cuda)
+    attach_device_runtime(model)
+    rt = model._device_runtime
+    built = {}
+    for sync in (False, True):
+        monkeypatch.setattr(fastpath, "_LAYER_SYNC", sync)
+        with torch.no_grad():
+            memory, _, _ = rt.build_memory(batch["metadata"], tok, ResolverServiceConfig())
+        torch.cuda.synchronize()
+        built[sync] = (memory.pool.float().clone(), memory.gists_all.clone(), memory.gist_count_all.clone())
+    assert len(rt.plan_batch(batch["metadata"], tok).waves) == 1  # one encode group in layer-synchronous mode
+    (pool_a, gists_a, count_a), (pool_b, gists_b, count_b) = built[False], built[True]
+    assert torch.equal(count_a, count_b)
+    assert torch.allclose(pool_a, pool_b, atol=2e-2, rtol=2e-2), (pool_a - pool_b).abs().max()
+    assert torch.allclose(gists_a, gists_b, atol=2e-2, rtol=2e-2), (gists_a - gists_b).abs().max()
+
+
+def test_device_logits_and_selected_chunks_match_object_path(cuda, tmp_path):
+    """Model level: bf16 device logits against the fp32 object path (which equals the reference
+    oracle on CPU), and the chunk ids each layer selects for each row."""
+    torch.manual_seed(11)
+    tok, batch = tiny_batch(Path(tmp_path))
+    cfg = tiny_config(tok.vocab_size)
+    reference = TinyPRAModel(copy.deepcopy(cfg)).to(cuda).eval()
+    device_model = TinyPRAModel(copy.deepcopy(cfg)).to(cuda)
+    device_model.load_state_dict(reference.state_dict())
+    attach_device_runtime(device_model)
+    with torch.no_grad():
+        _, ref_out = _pra_batch_step(reference, batch, "cuda", tok, ResolverServiceConfig(), None)
+        _, dev_out = _pra_batch_step(device_model, batch, "cuda", tok, ResolverServiceConfig(), None)
+    rt = device_model._device_runtime
+    b, t = batch["input_ids"].shape
+    dev_logits = rt.logits(dev_out["hidden"], b, t).float()
+    ref_logits = ref_out["logits"].float()
+    valid = batch["attention_mask"].bool().to(cuda)
+    err = (dev_logits - ref_logits).abs()[valid]
+    assert err.max() <= 0.05 * ref_logits.abs()[valid].max(), err.max()
+    expected = reference.selected_chunks_by_layer()
+    memory = dev_out["memory"]
+    for layer, rows in expected.items():
+        routing = rt.last_routing[layer]
+        same = 0
+        for row in range(b):
+            count = int(routing.ints[1, row])
+            got = sorted(memory.chunks[int(c)].chunk_id for c in routing.sel_i[0, row, :count].tolist())
+            want = sorted(hit.chunk_id for hit in rows[row])
+            same += got == want
+        # layer 0 routes queries that differ from the fp32 ones only by bf16 rounding
+        assert same == b if layer == 0 else same >= 0.75 * b, (layer, same, b)

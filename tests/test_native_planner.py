@@ -143,7 +143,11 @@ def _compare(rt, rows, tok, resolver=None):
     {"recursive_cycle_policy": "link_only"},
     {"context_safety_reserve_tokens": 4, "max_materialized_memory_tokens": 50},
 ])
-def test_native_plan_equals_python_plan(over):
+@pytest.mark.parametrize("layer_sync", [True, False])
+def test_native_plan_equals_python_plan(over, layer_sync, monkeypatch):
+    from pdattention_b200.models import fastpath
+
+    monkeypatch.setattr(fastpath, "_LAYER_SYNC", layer_sync)
     cfg = _cfg(**over)
     rt = DeviceRuntime.for_planning(TinyPRAModel(cfg))
     tok = WordIdTokenizer(500, [f"<REF_{i}>" for i in range(1, 20)])
