@@ -372,10 +372,14 @@ def _reference_arm(root: Path, tokenizer, rank: int, world: int):
 
 
 def run_decode(impl: str, steps: int, warmup: int, gpus: int, memory_tokens: int | None, batch: int) -> dict:
-    """PRA decode on a Llama-3-8B-architecture model (random weights) with a shared chunk memory."""
+    """PRA decode on a Llama-3-8B-architecture model (random weights) with a shared chunk memory.
+
+    ``impl="reference"``: the reference has no Llama-family PRA model, no tensor parallelism
+    and no 8B decode path, so the comparison arm is ``baseline/torch_pra_decode.py``, the
+    reference's PRA decode semantics in plain PyTorch + cuBLAS + NCCL (it imports nothing
+    from this framework), on the same workload."""
     if impl == "reference":
-        return {"impl": "reference", "unavailable": "the reference has no Llama-family PRA model, no tensor "
-                                                   "parallelism and no decode path for 8B models"}
+        return _run_decode_torch_arm(steps, warmup, gpus, memory_tokens, batch)
     rank, local, world = _env()
     if gpus != world:
         raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={world}")
@@ -428,6 +432,50 @@ def run_decode(impl: str, steps: int, warmup: int, gpus: int, memory_tokens: int
     }
     if tp is not None:
         tp.close()
+        import torch.distributed as dist
+
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return result
+
+
+def _run_decode_torch_arm(steps: int, warmup: int, gpus: int, memory_tokens: int | None, batch: int) -> dict:
+    rank, local, world = _env()
+    if gpus != world:
+        raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    sys.path.insert(0, str(REPO / "baseline"))
+    import torch_pra_decode
+
+    tokens = memory_tokens or (1 << 20 if world > 1 else 1 << 18)
+    clocks = ClockSampler(local)
+    with clocks:
+        out = torch_pra_decode.run(batch=batch, memory_tokens=tokens, steps=steps, warmup=warmup)
+    result = {
+        "metric": "PRA decode tokens/s (Llama-3-8B architecture, sharded chunk memory)", "value": out["tokens_per_s"],
+        "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": out["tpot_p50_ms"],
+        "tpot_p50_ms": out["tpot_p50_ms"], "tpot_p90_ms": out["tpot_p90_ms"], "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (uniform-random token ids for prompts and references), random-init weights",
+        "config": {"model": "Llama-3-8B architecture", "global_batch": batch, "seq_len": out["prompt_tokens"],
+                   "memory_tokens": out["memory_tokens"], "chunk_tokens": 64, "gists_per_chunk": 1,
+                   "chunk_top_k": out["top_k_chunks"], "parallelism": f"tp{world}",
+                   "build_tokens_per_s": out["build_tokens_per_s"],
+                   "prefill_tokens_per_s": out["prefill_tokens_per_s"]},
+        "clocks": clocks.summary(),
+        "e2e": {"value": out["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": out["h2d_bytes_per_step"],
+                "d2h_bytes_per_step": out["d2h_bytes_per_step"]},
+        "gpu_launches": 0, "impl": "reference",
+        "reference_kind": "the reference's PRA decode semantics in plain PyTorch + cuBLAS + NCCL "
+                          "(baseline/torch_pra_decode.py); the reference itself has no Llama-family or TP path"}
+    if world > 1:
         import torch.distributed as dist
 
         dist.barrier(device_ids=[local])

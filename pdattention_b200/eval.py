@@ -1,10 +1,12 @@
-"""``pra eval``: compare no_refs / full_context / simple_rag / pra on the test split.
+"""``pra eval``: four prompt variants compared on the test split.
 
-Behaviour of ``src/pra_torch/eval.py``: a missing checkpoint falls back to a
-random-initialised model with a corpus-built character tokenizer; a checkpoint
-restores ``PRAConfig(**cfg)`` (device overridden) and a BPE or character
-tokenizer; every variant reports LM loss, containment accuracy of greedy
-generations, input-token cost and (for pra) reference / anchor / cache hits.
+Variants (``src/pra_torch/eval.py:128-138`` defines the same four): the question
+alone, the references' full texts prepended, their summaries prepended, and the
+question with the references in PRA memory.  Each reports the LM loss over the
+loader, the fraction of greedy generations containing the answer, the prompt's
+token cost, and for the memory variant the reference / anchor / cache hits.  A
+missing checkpoint gives a random-initialised model with a fitted character
+tokenizer.
 """
 
 from __future__ import annotations
@@ -27,15 +29,14 @@ CharTokenizer = PRATokenizer
 
 
 def build_training_corpus(examples) -> list[str]:
+    """Texts a fitted character vocabulary must cover (question samples or core examples)."""
     texts = []
     for ex in examples:
         if hasattr(ex, "question"):
-            texts.append(ex.question + " " + ex.answer)
-            for ref in ex.references:
-                texts += [ref.summary or "", str(ref.metadata.get("text", ""))]
+            texts.append(f"{ex.question} {ex.answer}")
+            texts.extend(piece for ref in ex.references for piece in (ref.summary or "", str(ref.metadata.get("text", ""))))
         else:
-            texts.append(ex.prompt + ex.target)
-            texts += list(ex.refs.values()) + list(ex.summaries.values())
+            texts.extend([ex.prompt + ex.target, *ex.refs.values(), *ex.summaries.values()])
     return texts
 
 
@@ -69,131 +70,162 @@ def load_model_and_tokenizer(ckpt_path: str, device: str, examples, *, max_seq_l
                              memory_transport: str = "native_kv", use_cross_attention_memory=None,
                              use_concat_memory=None, memory_alpha: float = 0.5, resolver_config=None,
                              cache_config=None, **routing_kwargs):
-    """Restore (or randomly initialise) a model and its tokenizer; returns ``(model, tokenizer, loaded)``."""
-    if not os.path.exists(ckpt_path):
-        tokenizer = CharTokenizer(build_training_corpus(examples))
-        cfg = PRAConfig(vocab_size=tokenizer.vocab_size, d_model=d_model, n_heads=n_heads, n_layers=n_layers,
-                        n_vanilla_layers=n_vanilla_layers, n_mixed_layers=n_mixed_layers, max_seq_len=max_seq_len,
-                        dropout=dropout, pra_layer_ids=tuple(pra_layer_ids), top_k_references=top_k_references,
-                        top_k_chunks_per_reference=top_k_chunks_per_reference, trigger_threshold=trigger_threshold,
-                        memory_transport=memory_transport, use_cross_attention_memory=use_cross_attention_memory,
-                        use_concat_memory=use_concat_memory, memory_alpha=memory_alpha, device=device,
-                        **routing_kwargs)
-        return TinyPRAModel(cfg).to(device), tokenizer, False
-    checkpoint = read_checkpoint(ckpt_path, map_location=device)
-    values = dict(checkpoint["cfg"])
-    values["device"] = device
-    cfg = PRAConfig(**values)
-    if checkpoint.get("tokenizer_type") == "BPETokenizer" and checkpoint.get("tokenizer_json"):
-        tokenizer = BPETokenizer.from_json(checkpoint["tokenizer_json"])
-    else:
-        tokenizer = CharTokenizer.from_vocab(checkpoint["stoi"])
-    model = TinyPRAModel(cfg).to(device)
-    model.load_state_dict(checkpoint["model"])
-    model.eval()
-    return model, tokenizer, True
+    """Restore (or randomly initialise) a model and its tokenizer; returns ``(model, tokenizer, loaded)``.
+
+    A checkpoint restores ``PRAConfig(**cfg)`` with ``device`` overridden and its BPE or character
+    tokenizer; without one, a character tokenizer is fitted to ``examples`` and the model is built
+    from the keyword arguments."""
+    if os.path.exists(ckpt_path):
+        checkpoint = read_checkpoint(ckpt_path, map_location=device)
+        cfg = PRAConfig(**{**dict(checkpoint["cfg"]), "device": device})
+        bpe = checkpoint.get("tokenizer_type") == "BPETokenizer" and checkpoint.get("tokenizer_json")
+        tokenizer = BPETokenizer.from_json(checkpoint["tokenizer_json"]) if bpe else \
+            CharTokenizer.from_vocab(checkpoint["stoi"])
+        model = TinyPRAModel(cfg).to(device)
+        model.load_state_dict(checkpoint["model"])
+        return model.eval(), tokenizer, True
+    tokenizer = CharTokenizer(build_training_corpus(examples))
+    cfg = PRAConfig(vocab_size=tokenizer.vocab_size, d_model=d_model, n_heads=n_heads, n_layers=n_layers,
+                    n_vanilla_layers=n_vanilla_layers, n_mixed_layers=n_mixed_layers, max_seq_len=max_seq_len,
+                    dropout=dropout, pra_layer_ids=tuple(pra_layer_ids), top_k_references=top_k_references,
+                    top_k_chunks_per_reference=top_k_chunks_per_reference, trigger_threshold=trigger_threshold,
+                    memory_transport=memory_transport, use_cross_attention_memory=use_cross_attention_memory,
+                    use_concat_memory=use_concat_memory, memory_alpha=memory_alpha, device=device, **routing_kwargs)
+    return TinyPRAModel(cfg).to(device), tokenizer, False
 
 
 def generate_greedy(model, tokenizer, prompt: str, device: str, max_new_tokens: int) -> str:
+    """Greedy continuation without memory (the prompt window slides at ``max_seq_len``)."""
     ids = torch.tensor([tokenizer.encode(prompt)], dtype=torch.long, device=device)
+    window = model.cfg.max_seq_len
     for _ in range(max_new_tokens):
-        logits = model(ids[:, -model.cfg.max_seq_len:], use_pra_memory=False)
-        ids = torch.cat([ids, logits[:, -1, :].argmax(dim=-1, keepdim=True)], dim=1)
+        nxt = model(ids[:, -window:], use_pra_memory=False)[:, -1].argmax(dim=-1, keepdim=True)
+        ids = torch.cat([ids, nxt], dim=1)
     return tokenizer.decode(ids[0])
 
 
 def generate_pra(model, tokenizer, prompt: str, device: str, max_new_tokens: int) -> str:
+    """Greedy continuation through the model's PRA memory (its attached cache)."""
     ids = torch.tensor([tokenizer.encode(prompt)], dtype=torch.long, device=device)
-    out = model.generate(ids, max_new_tokens=max_new_tokens, tokenizer=tokenizer, do_sample=False)
-    return tokenizer.decode(out[0])
+    return tokenizer.decode(model.generate(ids, max_new_tokens=max_new_tokens, tokenizer=tokenizer, do_sample=False)[0])
+
+
+# The four compared prompts: the question alone, every reference's full text in front of it,
+# the reference summaries in front of it (a retrieval-by-summary stand-in), and the question
+# alone with the references in PRA memory.
+def _prompt_set(question: str, texts: list[str], summaries: list[str]) -> dict:
+    return {"no_refs": question, "full_context": "Context:\n" + "\n".join(texts) + "\n\n" + question,
+            "simple_rag": "Retrieved summary:\n" + "\n".join(summaries) + "\n\n" + question, "pra": question}
 
 
 def baseline_prompts_from_metadata(item) -> dict:
-    refs, question = item["references"], item["question"]
-    docs = "\n".join(str(r.metadata.get("text", "")) for r in refs)
-    summaries = "\n".join(r.summary or "" for r in refs)
-    return {"no_refs": question, "full_context": f"Context:\n{docs}\n\n{question}",
-            "simple_rag": f"Retrieved summary:\n{summaries}\n\n{question}", "pra": question}
+    refs = item["references"]
+    return _prompt_set(item["question"], [str(r.metadata.get("text", "")) for r in refs],
+                       [r.summary or "" for r in refs])
 
 
 def baseline_prompts(ex) -> dict:
     if hasattr(ex, "references"):
         return baseline_prompts_from_metadata({"question": ex.question, "references": ex.references})
-    docs, summaries = "\n".join(ex.refs.values()), "\n".join(ex.summaries.values())
-    return {"no_refs": ex.prompt, "full_context": f"Context:\n{docs}\n\n{ex.prompt}",
-            "simple_rag": f"Retrieved summary:\n{summaries}\n\n{ex.prompt}", "pra": ex.prompt}
+    return _prompt_set(ex.prompt, list(ex.refs.values()), list(ex.summaries.values()))
 
 
 def generated_contains_target(output: str, prompt: str, target: str) -> bool:
     return target.strip() in output[len(prompt):]
 
 
+class _Tally:
+    """Running sums of one variant's evaluation."""
+
+    def __init__(self):
+        self.n = self.exact = self.ref_hits = self.anchor_hits = 0
+        self.input_tokens = self.full_tokens = self.resolved = self.retrieved = 0
+        self.losses: list[float] = []
+        self.sample = ""
+
+    def per_example(self, value) -> float:
+        return value / max(self.n, 1)
+
+
+def _memory_hits(cache, item) -> tuple[bool, bool]:
+    """(every expected reference is cached, an expected anchor appears in the cached texts or URIs)."""
+    expected = {r.uri for r in item["references"] if r.id in item["target_reference_ids"]}
+    ref_hit = not expected or bool(expected.intersection(cache.entries))
+    anchors = item.get("expected_anchors", [])
+    texts, uris = "\n".join(e.text for e in cache.all_entries()), " ".join(cache.entries)
+    return ref_hit, not anchors or any(a in texts or a in uris for a in anchors)
+
+
 def evaluate_variant(name, model, tokenizer, dataloader, device, max_new_tokens, *, resolver_config=None,
                      cache_config=None) -> EvalResult:
-    t0 = time.perf_counter()
-    exact = ref_hits = anchor_hits = cache_hits = cost = resolved = retrieved = full_cost = total = 0
-    loss_sum, loss_count, sample = 0.0, 0, ""
+    """LM loss over the loader and greedy-generation accuracy of one prompt variant."""
+    started = time.perf_counter()
+    with_memory = name == "pra"
+    tally = _Tally()
     for batch in dataloader:
         ids, labels = batch["input_ids"].to(device), batch["labels"].to(device)
-        if name == "pra":
+        if with_memory:
             cache = build_cache_from_metadata(model, tokenizer, batch["metadata"], device,
                                               resolver_config=resolver_config, cache_config=cache_config)
-            resolved += len(cache.entries)
-            retrieved += sum(len(tokenizer.encode(e.text)) for e in cache.all_entries())
+            tally.resolved += len(cache.entries)
+            tally.retrieved += sum(len(tokenizer.encode(e.text)) for e in cache.all_entries())
             logits = model(ids)
         else:
             model.clear_pra_cache()
             logits = model(ids, use_pra_memory=False)
-        loss_sum += float(F.cross_entropy(logits.view(-1, logits.size(-1)), labels.view(-1), ignore_index=0).detach().cpu())
-        loss_count += 1
+        tally.losses.append(float(F.cross_entropy(logits.flatten(0, 1), labels.flatten(), ignore_index=0).detach().cpu()))
         for item in batch["metadata"]:
             prompts = baseline_prompts_from_metadata(item)
-            prompt, target = prompts[name], item["answer"].strip()
-            cost += len(tokenizer.encode(prompt))
-            full_cost += len(tokenizer.encode(prompts["full_context"]))
-            if name == "pra":
-                expected = {r.uri for r in item["references"] if r.id in item["target_reference_ids"]}
-                if not expected or expected.intersection(model.pra_cache.entries):
-                    ref_hits += 1
-                    cache_hits += 1
-                anchors = item.get("expected_anchors", [])
-                text = "\n".join(e.text for e in model.pra_cache.all_entries())
-                if not anchors or any(a in text or a in " ".join(model.pra_cache.entries) for a in anchors):
-                    anchor_hits += 1
-                output = generate_pra(model, tokenizer, prompt, device, max_new_tokens)
-            else:
-                output = generate_greedy(model, tokenizer, prompt, device, max_new_tokens)
-            exact += int(generated_contains_target(output, prompt, target))
-            sample = output if total == 0 else sample
-            total += 1
-    n = max(total, 1)
-    pra = name == "pra"
-    return EvalResult(name, exact, total, cost / n, resolved / n, exact / n, ref_hits / n if pra else 0.0,
-                      anchor_hits / n if pra else 0.0, 0.0, retrieved / n, full_cost / n,
-                      loss_sum / max(loss_count, 1), cache_hits / n if pra else 0.0, time.perf_counter() - t0, sample)
+            prompt = prompts[name]
+            tally.input_tokens += len(tokenizer.encode(prompt))
+            tally.full_tokens += len(tokenizer.encode(prompts["full_context"]))
+            if with_memory:
+                ref_hit, anchor_hit = _memory_hits(model.pra_cache, item)
+                tally.ref_hits += ref_hit
+                tally.anchor_hits += anchor_hit
+            generate = generate_pra if with_memory else generate_greedy
+            output = generate(model, tokenizer, prompt, device, max_new_tokens)
+            tally.exact += generated_contains_target(output, prompt, item["answer"].strip())
+            tally.sample = tally.sample if tally.n else output
+            tally.n += 1
+    hit = (lambda v: tally.per_example(v)) if with_memory else (lambda v: 0.0)
+    return EvalResult(name, tally.exact, tally.n, tally.per_example(tally.input_tokens),
+                      tally.per_example(tally.resolved), tally.per_example(tally.exact), hit(tally.ref_hits),
+                      hit(tally.anchor_hits), 0.0, tally.per_example(tally.retrieved),
+                      tally.per_example(tally.full_tokens), sum(tally.losses) / max(len(tally.losses), 1),
+                      hit(tally.ref_hits), time.perf_counter() - started, tally.sample)
+
+
+_REPORT_HEADER = ("variant       loss     accuracy   input_tokens   resolved_refs   ref_hit   anchor_hit   cache_hit"
+                  "   latency")
 
 
 def print_report(results, loaded_checkpoint: bool) -> None:
     print(f"PRA eval report ({'checkpoint' if loaded_checkpoint else 'random initialization'})")
-    print("variant       loss     accuracy   input_tokens   resolved_refs   ref_hit   anchor_hit   cache_hit   latency")
+    print(_REPORT_HEADER)
     for r in results:
         print(f"{r.name:<13} {r.lm_loss:>6.3f} {r.accuracy:>7.2%} {r.avg_input_tokens:>14.1f} "
               f"{r.avg_resolved_refs:>15.1f} {r.expected_ref_hit:>8.2%} {r.expected_anchor_hit:>11.2%} "
               f"{r.cache_hit_ratio:>10.2%} {r.latency:>8.3f}s")
     print("\nSample PRA output:")
-    pra = next((r for r in results if r.name == "pra"), None)
-    if pra is not None:
-        print(pra.sample_output)
+    for r in results:
+        if r.name == "pra":
+            print(r.sample_output)
+            break
+
+
+VARIANTS = ("no_refs", "full_context", "simple_rag", "pra")
 
 
 def run_evaluation(*, ckpt: str, device: str, datamodule, max_new_tokens: int, max_seq_len: int = 96,
                    resolver_config=None, cache_config=None, **model_kwargs):
+    """Restore the model (or initialise one), rebuild the data module's collator for its tokenizer
+    and evaluate every variant on the test split."""
     model, tokenizer, loaded = load_model_and_tokenizer(ckpt, device, datamodule.dataset, max_seq_len=max_seq_len,
                                                         **model_kwargs)
     datamodule.tokenizer = tokenizer
     datamodule.collator = PRACollator(tokenizer, max_seq_len=max_seq_len)
     results = [evaluate_variant(name, model, tokenizer, datamodule.test_loader(), device, max_new_tokens,
-                                resolver_config=resolver_config, cache_config=cache_config)
-               for name in ("no_refs", "full_context", "simple_rag", "pra")]
+                                resolver_config=resolver_config, cache_config=cache_config) for name in VARIANTS]
     print_report(results, loaded)
     return results

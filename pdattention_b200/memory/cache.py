@@ -383,27 +383,145 @@ class PRAMemoryCache(ABC):
 def _selected(hit: _ChunkHit, reference_score, layer_id, ref_rank, chunk_rank,
               reference_hit: _ReferenceHit | None = None) -> SelectedChunk:
     meta = hit.entry.metadata
+    ref = reference_hit
     return SelectedChunk(
         entry=hit.entry, chunk=hit.chunk, reference_score=reference_score, chunk_score=hit.score,
         layer_id=layer_id, reference_rank=ref_rank, rank_within_reference=chunk_rank,
         winning_gist_index=hit.winning_gist_index, winning_gist_score=hit.winning_gist_score,
-        gist_count=hit.gist_count,
-        winning_reference_gist_index=reference_hit.winning_gist_index if reference_hit else None,
-        winning_reference_gist_score=reference_hit.winning_gist_score if reference_hit else None,
-        reference_gist_count=reference_hit.gist_count if reference_hit else 0,
+        gist_count=hit.gist_count, winning_reference_gist_index=ref.winning_gist_index if ref else None,
+        winning_reference_gist_score=ref.winning_gist_score if ref else None,
+        reference_gist_count=ref.gist_count if ref else 0,
         metadata={"routing_source": hit.routing_source, "reference_source": meta.get("source", "reference"),
                   "implicit_reference": bool(meta.get("implicit", False)),
-                  "reference_display_name": meta.get("display_name", hit.entry.uri)},
-    )
+                  "reference_display_name": meta.get("display_name", hit.entry.uri)})
+
+
+# ---------------------------------------------------------------------------
+# Scalar scoring (the oracle path) and the host-side strategies
+# ---------------------------------------------------------------------------
+
+def _augmented_gists(gist: ChunkRoutingGist, summary_k: torch.Tensor) -> torch.Tensor:
+    """``augment`` summary mode: every content gist moved towards the mean summary direction."""
+    boost = F.normalize(summary_k.mean(dim=0), dim=-1)
+    return F.normalize(F.normalize(gist.k, dim=-1) + boost.unsqueeze(0), dim=-1)
+
+
+def score_chunk(query: torch.Tensor, entry, chunk, config) -> _ChunkHit:
+    """One chunk's cosine routing score for one ``[D]`` query (content gists, optionally combined
+    with the chunk's summary gists as ``config.summary_mode`` says)."""
+    gist, agg = chunk.routing_gist, config.gist_score_aggregation
+    content = score_gist_set(query, gist.k, agg)
+    score, source = content.aggregate_score, "content"
+    if config.use_summary and gist.summary_k is not None:
+        summary_k = _as_rows(gist.summary_k)
+        mode = config.summary_mode
+        if mode == "replace":
+            score, source = score_gist_set(query, summary_k, agg).aggregate_score, "summary"
+        elif mode == "hybrid":
+            score, source = max(score, score_gist_set(query, summary_k, agg).aggregate_score), "hybrid"
+        elif mode == "augment":
+            score, source = score_gist_set(query, _augmented_gists(gist, summary_k), agg).aggregate_score, "augment"
+        else:
+            raise ValueError(f"Unsupported summary mode: {mode}")
+    winner = content.winning_index
+    win_score = None
+    if content.per_gist_scores is not None and winner is not None:
+        win_score = float(content.per_gist_scores[winner].cpu())
+    return _ChunkHit(entry, chunk, score, source, winner, win_score, int(gist.k.shape[0]))
+
+
+def _layer_chunks(entries, layer_id: int):
+    return [(e, c) for e in entries if layer_id in e.layer_memory for c in e.layer_memory[layer_id].chunks]
+
+
+def _by_reference(hits) -> dict[str, list[_ChunkHit]]:
+    grouped: dict[str, list[_ChunkHit]] = defaultdict(list)
+    for hit in hits:
+        grouped[hit.entry.uri].append(hit)
+    return grouped
+
+
+def _chunk_order(hits):
+    """Chunks best first; equal scores by chunk id (string order)."""
+    return sorted(hits, key=lambda h: (-h.score, h.chunk.chunk_id))
+
+
+def _reference_order(scores: dict[str, float]) -> list[str]:
+    """URIs best first; equal scores by URI."""
+    return sorted(scores, key=lambda u: (-scores[u], u))
+
+
+def _reference_scores(grouped, aggregation: str) -> dict[str, float]:
+    return {uri: _aggregate([h.score for h in hits], aggregation) for uri, hits in grouped.items()}
+
+
+def _hierarchical(hits, layer_id, config) -> list[SelectedChunk]:
+    """The top URIs by aggregated chunk score, then the top chunks inside each."""
+    grouped = _by_reference(hits)
+    scores = _reference_scores(grouped, config.reference_score_aggregation)
+    picked = []
+    for ref_rank, uri in enumerate(_reference_order(scores)[: config.top_k_references], start=1):
+        best = _chunk_order(grouped[uri])[: config.top_k_chunks_per_reference]
+        picked += [_selected(hit, scores[uri], layer_id, ref_rank, rank) for rank, hit in enumerate(best, start=1)]
+    return picked
+
+
+def _global_chunks(hits, layer_id, config) -> list[SelectedChunk]:
+    """One global chunk ranking, admitting a chunk while both its URI's chunk quota and the URI quota allow."""
+    scores = _reference_scores(_by_reference(hits), config.reference_score_aggregation)
+    admitted: dict[str, int] = {}  # uri -> chunks taken, in admission order
+    picked = []
+    for hit in sorted(hits, key=lambda h: (-h.score, h.entry.uri, h.chunk.chunk_id)):
+        uri = hit.entry.uri
+        taken = admitted.get(uri)
+        if taken is None:
+            if len(admitted) >= config.top_k_references:
+                continue
+            taken = admitted[uri] = 0
+        if taken >= config.top_k_chunks_per_reference:
+            continue
+        admitted[uri] = taken + 1
+        picked.append(_selected(hit, scores[uri], layer_id, list(admitted).index(uri) + 1, taken + 1))
+    return picked
+
+
+_HOST_STRATEGIES = {"hierarchical": _hierarchical, "global_chunks": _global_chunks}
+
+
+def _rankings(hits, config, *, reference_scores=None) -> list[dict]:
+    """Every URI and chunk with its rank and score (routing metrics and rank diagnostics)."""
+    grouped = _by_reference(hits)
+    scores = reference_scores if reference_scores is not None else \
+        _reference_scores(grouped, config.reference_score_aggregation)
+    table = []
+    for ref_rank, uri in enumerate(_reference_order(scores), start=1):
+        chunks = [{"chunk_id": h.chunk.chunk_id, "chunk_rank": rank, "chunk_score": float(h.score),
+                   "token_start": h.chunk.token_start, "token_end": h.chunk.token_end, "gist_count": h.gist_count,
+                   "winning_gist_index": h.winning_gist_index, "winning_gist_score": h.winning_gist_score}
+                  for rank, h in enumerate(_chunk_order(grouped.get(uri, [])), start=1)]
+        table.append({"reference_uri": uri, "reference_rank": ref_rank, "reference_score": float(scores[uri]),
+                      "chunks": chunks})
+    return table
+
+
+@dataclass
+class _Slot:
+    """One URI's lifecycle record: the state, the entry once ready, the failure once failed."""
+
+    state: CacheBuildState
+    entry: PRACacheEntry | None = None
+    failure: str | None = None
 
 
 class PRASimpleMemoryCache(PRAMemoryCache):
-    """In-process cache implementing the three routing strategies."""
+    """In-process cache: one lifecycle table, per-layer packed routing indexes, three strategies.
+
+    Only ``READY`` URIs are visible (``get``, ``all_entries``, routing); any change of the
+    table drops the packed indexes, which are rebuilt on the next search.
+    """
 
     def __init__(self):
-        self._entries: dict[str, PRACacheEntry] = {}
-        self._states: dict[str, CacheBuildState] = {}
-        self._failures: dict[str, str] = {}
+        self._slots: dict[str, _Slot] = {}
         self._last_rankings_by_layer: dict[int, list[list[dict]]] = {}
         self._indexes: dict[tuple, RoutingIndex] = {}
         self.resolution_events: list = []
@@ -413,60 +531,61 @@ class PRASimpleMemoryCache(PRAMemoryCache):
     def invalidate_routing_indexes(self) -> None:
         self._indexes.clear()
 
+    def _set(self, uri: str, slot: _Slot | None) -> None:
+        if slot is None:
+            self._slots.pop(uri, None)
+        else:
+            self._slots[uri] = slot
+        self.invalidate_routing_indexes()
+
+    def _ready(self):
+        return ((uri, slot.entry) for uri, slot in self._slots.items() if slot.state is CacheBuildState.READY)
+
     @property
     def entries(self) -> dict[str, PRACacheEntry]:
-        return self._entries
+        return dict(self._ready())
 
     def begin_build(self, uri: str) -> None:
-        self.invalidate_routing_indexes()
-        self._states[uri] = CacheBuildState.BUILDING
+        self._set(uri, _Slot(CacheBuildState.BUILDING))
 
     def mark_failed(self, uri: str, error: Exception | str) -> None:
-        self._entries.pop(uri, None)
-        self.invalidate_routing_indexes()
-        self._states[uri] = CacheBuildState.FAILED
-        self._failures[uri] = str(error)
-
-    def state(self, uri: str) -> CacheBuildState:
-        return self._states.get(uri, CacheBuildState.MISSING)
-
-    def failure(self, uri: str) -> str | None:
-        return self._failures.get(uri)
+        self._set(uri, _Slot(CacheBuildState.FAILED, failure=str(error)))
 
     def put(self, entry: PRACacheEntry) -> None:
-        self._entries[entry.uri] = entry
+        self._set(entry.uri, _Slot(CacheBuildState.READY, entry))
+
+    def invalidate(self, uri: str) -> None:
+        self._set(uri, None)
+
+    def clear(self) -> None:
+        self._slots.clear()
+        self._last_rankings_by_layer.clear()
         self.invalidate_routing_indexes()
-        self._states[entry.uri] = CacheBuildState.READY
-        self._failures.pop(entry.uri, None)
+
+    def state(self, uri: str) -> CacheBuildState:
+        slot = self._slots.get(uri)
+        return CacheBuildState.MISSING if slot is None else slot.state
+
+    def failure(self, uri: str) -> str | None:
+        slot = self._slots.get(uri)
+        return None if slot is None else slot.failure
 
     def get(self, uri: str) -> PRACacheEntry | None:
-        return self._entries.get(uri) if self.state(uri) == CacheBuildState.READY else None
+        slot = self._slots.get(uri)
+        return slot.entry if slot is not None and slot.state is CacheBuildState.READY else None
 
     def has(self, uri: str) -> bool:
         return self.get(uri) is not None
 
     def all_entries(self) -> list[PRACacheEntry]:
-        return [e for uri, e in self._entries.items() if self.state(uri) == CacheBuildState.READY]
-
-    def clear(self) -> None:
-        self._entries.clear()
-        self._states.clear()
-        self._failures.clear()
-        self._last_rankings_by_layer.clear()
-        self.invalidate_routing_indexes()
+        return [entry for _, entry in self._ready()]
 
     def is_empty(self) -> bool:
-        return not any(self.state(uri) == CacheBuildState.READY for uri in self._entries)
-
-    def invalidate(self, uri: str) -> None:
-        self._entries.pop(uri, None)
-        self.invalidate_routing_indexes()
-        self._states.pop(uri, None)
-        self._failures.pop(uri, None)
+        return next(self._ready(), None) is None
 
     def layer_counts(self, layer_id: int) -> dict[str, int]:
         entries = [e for e in self.all_entries() if layer_id in e.layer_memory]
-        chunks = [c for e in entries for c in e.layer_memory[layer_id].chunks]
+        chunks = [c for _, c in _layer_chunks(entries, layer_id)]
         ref_gists = [e.reference_gists_by_layer[layer_id] for e in entries if layer_id in e.reference_gists_by_layer]
         return {"references": len(entries), "chunks": len(chunks), "tokens": sum(c.token_count for c in chunks),
                 "chunk_gists": sum(int(c.routing_gist.k.shape[0]) for c in chunks),
@@ -478,11 +597,11 @@ class PRASimpleMemoryCache(PRAMemoryCache):
     # -- packed index --------------------------------------------------
     def routing_index(self, layer_id: int, query: torch.Tensor, *, reuse: bool = True) -> RoutingIndex | None:
         key = (int(layer_id), str(query.device), query.dtype)
-        if reuse and key in self._indexes:
-            return self._indexes[key]
-        index = build_routing_index(self.all_entries(), layer_id, query.device, query.dtype)
-        if reuse and index is not None:
-            self._indexes[key] = index
+        index = self._indexes.get(key) if reuse else None
+        if index is None:
+            index = build_routing_index(self.all_entries(), layer_id, query.device, query.dtype)
+            if reuse and index is not None:
+                self._indexes[key] = index
         return index
 
     def prepare_routing_index(self, layer_id: int, query: torch.Tensor, *, force_rebuild: bool = False) -> dict:
@@ -498,36 +617,12 @@ class PRASimpleMemoryCache(PRAMemoryCache):
         return {"reused": reused, "candidate_chunks": len(index.records),
                 "candidate_gists": int(index.gist_mask.sum().item()), "index_bytes": index.nbytes}
 
-    # -- scalar (oracle) scoring ---------------------------------------
-    @staticmethod
-    def _score_chunk(query: torch.Tensor, entry, chunk, config) -> _ChunkHit:
-        gist = chunk.routing_gist
-        content = score_gist_set(query, gist.k, config.gist_score_aggregation)
-        score, source = content.aggregate_score, "content"
-        if config.use_summary and gist.summary_k is not None:
-            summary_k = _as_rows(gist.summary_k)
-            summary = score_gist_set(query, summary_k, config.gist_score_aggregation)
-            if config.summary_mode == "replace":
-                score, source = summary.aggregate_score, "summary"
-            elif config.summary_mode == "hybrid":
-                score, source = max(score, summary.aggregate_score), "hybrid"
-            elif config.summary_mode == "augment":
-                boost = F.normalize(summary_k.mean(dim=0), dim=-1)
-                mixed = F.normalize(F.normalize(gist.k, dim=-1) + boost.unsqueeze(0), dim=-1)
-                score, source = score_gist_set(query, mixed, config.gist_score_aggregation).aggregate_score, "augment"
-            else:
-                raise ValueError(f"Unsupported summary mode: {config.summary_mode}")
-        win_score = None
-        if content.per_gist_scores is not None and content.winning_index is not None:
-            win_score = float(content.per_gist_scores[content.winning_index].cpu())
-        return _ChunkHit(entry, chunk, score, source, content.winning_index, win_score, int(gist.k.shape[0]))
+    # -- scoring ---------------------------------------------------------
+    _score_chunk = staticmethod(score_chunk)
 
     def _score_chunks(self, query, layer_id, config, *, entries=None) -> list[list[_ChunkHit]]:
-        records = [(e, c) for e in (entries if entries is not None else self.all_entries())
-                   if layer_id in e.layer_memory for c in e.layer_memory[layer_id].chunks]
-        if not records:
-            return [[] for _ in range(query.shape[0])]
-        return [[self._score_chunk(row, e, c, config) for e, c in records] for row in query]
+        records = _layer_chunks(self.all_entries() if entries is None else entries, layer_id)
+        return [[score_chunk(row, e, c, config) for e, c in records] for row in query]
 
     def _tensor_hits(self, query, layer_id, config) -> tuple:
         index = self.routing_index(layer_id, query, reuse=config.cache_build_mode == "detached")
@@ -542,6 +637,7 @@ class PRASimpleMemoryCache(PRAMemoryCache):
 
     @staticmethod
     def _fallback_reference_gists(entry: PRACacheEntry, layer_id: int, config):
+        """URI gists derived from the chunk gists (``mean`` or ``last``) when none were built."""
         memory = entry.layer_memory.get(layer_id)
         if memory is None or not memory.chunks:
             return None
@@ -550,19 +646,14 @@ class PRASimpleMemoryCache(PRAMemoryCache):
             raise ValueError("search_strategy='reference_first' requires reference_level_gist_mode.")
         if mode not in {"mean", "last"}:
             raise RuntimeError(f"Reference gists for mode {mode!r} must be created during cache construction.")
-        keys = torch.cat([c.routing_gist.k for c in memory.chunks], dim=0)
-        has_v = all(c.routing_gist.v is not None for c in memory.chunks)
-        values = torch.cat([c.routing_gist.v for c in memory.chunks], dim=0) if has_v else None
-        if mode == "mean":
-            gk = keys.mean(dim=0, keepdim=True)
-            gv = values.mean(dim=0, keepdim=True) if values is not None else None
-        else:
-            gk = keys[-1:].clone()
-            gv = values[-1:].clone() if values is not None else None
-        gists = ReferenceRoutingGists(k=gk, v=gv, mode=mode, metadata={
+        gists = [c.routing_gist for c in memory.chunks]
+        keys = torch.cat([g.k for g in gists], dim=0)
+        values = torch.cat([g.v for g in gists], dim=0) if all(g.v is not None for g in gists) else None
+        pick = (lambda t: t.mean(dim=0, keepdim=True)) if mode == "mean" else (lambda t: t[-1:].clone())
+        made = ReferenceRoutingGists(k=pick(keys), v=None if values is None else pick(values), mode=mode, metadata={
             "requested_gists": int(config.reference_gists_per_reference), "actual_gists": 1, "legacy_fallback": True})
-        entry.reference_gists_by_layer[layer_id] = gists
-        return gists
+        entry.reference_gists_by_layer[layer_id] = made
+        return made
 
     def _score_references(self, query, layer_id, config) -> list[_ReferenceHit]:
         if config.reference_level_gist_mode is None:
@@ -574,43 +665,14 @@ class PRASimpleMemoryCache(PRAMemoryCache):
             if gists is None:
                 continue
             s = score_gist_set(query, gists.k, config.reference_gist_score_aggregation)
-            win = (float(s.per_gist_scores[s.winning_index].cpu())
-                   if s.per_gist_scores is not None and s.winning_index is not None else None)
+            win = None
+            if s.per_gist_scores is not None and s.winning_index is not None:
+                win = float(s.per_gist_scores[s.winning_index].cpu())
             hits.append(_ReferenceHit(entry, s.aggregate_score, s.winning_index, win, int(gists.k.shape[0])))
         return hits
 
     # -- strategies ------------------------------------------------------
-    @staticmethod
-    def _serialize_rankings(hits, config, *, reference_scores=None) -> list[dict]:
-        grouped = defaultdict(list)
-        for hit in hits:
-            grouped[hit.entry.uri].append(hit)
-        if reference_scores is None:
-            reference_scores = {u: _aggregate([h.score for h in g], config.reference_score_aggregation)
-                                for u, g in grouped.items()}
-        out = []
-        for ref_rank, uri in enumerate(sorted(reference_scores, key=lambda u: (-reference_scores[u], u)), start=1):
-            ranked = sorted(grouped.get(uri, []), key=lambda h: (-h.score, h.chunk.chunk_id))
-            out.append({"reference_uri": uri, "reference_rank": ref_rank,
-                        "reference_score": float(reference_scores[uri]),
-                        "chunks": [{"chunk_id": h.chunk.chunk_id, "chunk_rank": r, "chunk_score": float(h.score),
-                                    "token_start": h.chunk.token_start, "token_end": h.chunk.token_end,
-                                    "gist_count": h.gist_count, "winning_gist_index": h.winning_gist_index,
-                                    "winning_gist_score": h.winning_gist_score}
-                                   for r, h in enumerate(ranked, start=1)]})
-        return out
-
-    def _hierarchical(self, hits, layer_id, config):
-        grouped = defaultdict(list)
-        for hit in hits:
-            grouped[hit.entry.uri].append(hit)
-        scores = {u: _aggregate([h.score for h in g], config.reference_score_aggregation) for u, g in grouped.items()}
-        chosen = sorted(scores, key=lambda u: (-scores[u], u))[: config.top_k_references]
-        out = []
-        for ref_rank, uri in enumerate(chosen, start=1):
-            ranked = sorted(grouped[uri], key=lambda h: (-h.score, h.chunk.chunk_id))[: config.top_k_chunks_per_reference]
-            out.extend(_selected(h, scores[uri], layer_id, ref_rank, r) for r, h in enumerate(ranked, start=1))
-        return out
+    _serialize_rankings = staticmethod(_rankings)
 
     def _hierarchical_from_tensors(self, hits_by_row, index: RoutingIndex, scores, layer_id, config):
         chunk_scores, win_index, win_score = scores
@@ -619,114 +681,82 @@ class PRASimpleMemoryCache(PRAMemoryCache):
                                   config.top_k_chunks_per_reference)
         if sel is None:
             return [[] for _ in range(chunk_scores.shape[0])]
-        host = [t.detach().cpu().tolist() for t in (sel.ref_index, sel.ref_score, sel.chunk_index, sel.chunk_score,
-                                                     sel.win_index, sel.win_score)]
-        ref_i, ref_s, chunk_i, chunk_s, win_i, win_s = host
+        ref_i, ref_s, chunk_i, chunk_s, win_i, win_s = (
+            t.detach().cpu().tolist() for t in (sel.ref_index, sel.ref_score, sel.chunk_index, sel.chunk_score,
+                                                sel.win_index, sel.win_score))
         k_chunk = sel.chunk_index.shape[-1]
-        out = []
+        rows = []
         for b in range(len(ref_i)):
-            order = sorted(range(len(ref_i[b])), key=lambda j: (-ref_s[b][j], index.reference_entries[ref_i[b][j]].uri))
+            refs = sorted(range(len(ref_i[b])), key=lambda j: (-ref_s[b][j], index.reference_entries[ref_i[b][j]].uri))
             row = []
-            for ref_rank, j in enumerate(order, start=1):
+            for ref_rank, j in enumerate(refs, start=1):
                 n_valid = min(k_chunk, len(index.ref_chunks_host[ref_i[b][j]]))
-                slots = sorted(range(n_valid), key=lambda s: (-chunk_s[b][j][s], index.records[chunk_i[b][j][s]][1].chunk_id))
-                for chunk_rank, s in enumerate(slots, start=1):
-                    c = chunk_i[b][j][s]
+                slots = sorted(range(n_valid),
+                               key=lambda s: (-chunk_s[b][j][s], index.records[chunk_i[b][j][s]][1].chunk_id))
+                for chunk_rank, slot in enumerate(slots, start=1):
+                    c = chunk_i[b][j][slot]
                     entry, chunk = index.records[c]
                     hit = hits_by_row[b][c] if hits_by_row is not None else _ChunkHit(
-                        entry, chunk, float(chunk_s[b][j][s]), "content", int(win_i[b][j][s]), float(win_s[b][j][s]),
-                        int(chunk.routing_gist.k.shape[0]))
+                        entry, chunk, float(chunk_s[b][j][slot]), "content", int(win_i[b][j][slot]),
+                        float(win_s[b][j][slot]), int(chunk.routing_gist.k.shape[0]))
                     row.append(_selected(hit, float(ref_s[b][j]), layer_id, ref_rank, chunk_rank))
-            out.append(row)
-        return out
+            rows.append(row)
+        return rows
 
-    def _reference_first(self, query, layer_id, config):
+    def _reference_first(self, query, layer_id, config) -> list[SelectedChunk]:
+        """Score the URI gists first, then only the chunks of the best URIs."""
         ref_hits = sorted(self._score_references(query, layer_id, config),
                           key=lambda h: (-h.score, h.entry.uri))[: config.top_k_references]
         if not ref_hits:
             return []
-        chunk_hits = self._score_chunks(query.unsqueeze(0), layer_id, config, entries=[h.entry for h in ref_hits])[0]
-        grouped = defaultdict(list)
-        for hit in chunk_hits:
-            grouped[hit.entry.uri].append(hit)
-        out = []
+        grouped = _by_reference(self._score_chunks(query.unsqueeze(0), layer_id, config,
+                                                   entries=[h.entry for h in ref_hits])[0])
+        picked = []
         for ref_rank, rh in enumerate(ref_hits, start=1):
-            ranked = sorted(grouped[rh.entry.uri], key=lambda h: (-h.score, h.chunk.chunk_id))
-            out.extend(_selected(h, rh.score, layer_id, ref_rank, r, rh)
-                       for r, h in enumerate(ranked[: config.top_k_chunks_per_reference], start=1))
-        return out
-
-    def _global_chunks(self, hits, layer_id, config):
-        by_uri = defaultdict(list)
-        for hit in hits:
-            by_uri[hit.entry.uri].append(hit.score)
-        ref_score = {u: _aggregate(s, config.reference_score_aggregation) for u, s in by_uri.items()}
-        out, uris, taken = [], [], defaultdict(int)
-        for hit in sorted(hits, key=lambda h: (-h.score, h.entry.uri, h.chunk.chunk_id)):
-            uri = hit.entry.uri
-            if taken[uri] >= config.top_k_chunks_per_reference:
-                continue
-            if uri not in uris:
-                if len(uris) >= config.top_k_references:
-                    continue
-                uris.append(uri)
-            taken[uri] += 1
-            out.append(_selected(hit, ref_score[uri], layer_id, uris.index(uri) + 1, taken[uri]))
-        return out
+            best = _chunk_order(grouped[rh.entry.uri])[: config.top_k_chunks_per_reference]
+            picked += [_selected(h, rh.score, layer_id, ref_rank, r, rh) for r, h in enumerate(best, start=1)]
+        return picked
 
     def search(self, query: torch.Tensor, layer_id: int, config: "PRAConfig") -> list[list[SelectedChunk]]:
         """Route ``[B,D]`` (or ``[D]``) queries with the configured strategy; rows never mix."""
         query = query.unsqueeze(0) if query.ndim == 1 else query
         if query.ndim != 2:
             raise ValueError(f"Expected query [batch,model] or [model], got {tuple(query.shape)}.")
-        batch = query.shape[0]
-        if config.top_k_references == 0 or config.top_k_chunks_per_reference == 0:
-            self._last_rankings_by_layer[layer_id] = [[] for _ in range(batch)]
-            return [[] for _ in range(batch)]
+        empty = [[] for _ in range(query.shape[0])]
         keep_rankings = bool(config.collect_routing_metrics or config.collect_rank_diagnostics)
-
-        if config.search_strategy == "reference_first":
+        strategy = config.search_strategy
+        rankings: list = empty
+        if config.top_k_references == 0 or config.top_k_chunks_per_reference == 0:
+            selected = empty
+        elif strategy == "reference_first":
             selected, rankings = [], []
             for row in query:
                 selected.append(self._reference_first(row, layer_id, config))
-                if keep_rankings:
-                    hits = self._score_chunks(row.unsqueeze(0), layer_id, config)[0]
-                    refs = {h.entry.uri: h.score for h in self._score_references(row, layer_id, config)}
-                    rankings.append(self._serialize_rankings(hits, config, reference_scores=refs))
-                else:
-                    rankings.append([])
-            self._last_rankings_by_layer[layer_id] = rankings
-            return selected
-
-        tensorized = config.routing_backend == "tensorized" and not config.use_summary
-        if tensorized and config.search_strategy == "hierarchical" and not keep_rankings:
-            index = self.routing_index(layer_id, query, reuse=config.cache_build_mode == "detached")
-            if index is None:
-                self._last_rankings_by_layer[layer_id] = [[] for _ in range(batch)]
-                return [[] for _ in range(batch)]
-            scores = score_index(query, index, config.gist_score_aggregation)
-            self._last_rankings_by_layer[layer_id] = [[] for _ in range(batch)]
-            return self._hierarchical_from_tensors(None, index, scores, layer_id, config)
-
-        if tensorized:
-            hits_by_row, index, scores = self._tensor_hits(query, layer_id, config)
-            if config.search_strategy == "hierarchical" and index is not None:
-                self._last_rankings_by_layer[layer_id] = (
-                    [self._serialize_rankings(h, config) for h in hits_by_row] if keep_rankings
-                    else [[] for _ in range(batch)])
-                return self._hierarchical_from_tensors(hits_by_row, index, scores, layer_id, config)
-        else:
-            hits_by_row = self._score_chunks(query, layer_id, config)
-
-        selected, rankings = [], []
-        for hits in hits_by_row:
-            rankings.append(self._serialize_rankings(hits, config) if keep_rankings else [])
-            if config.search_strategy == "hierarchical":
-                selected.append(self._hierarchical(hits, layer_id, config))
-            elif config.search_strategy == "global_chunks":
-                selected.append(self._global_chunks(hits, layer_id, config))
+                refs = {h.entry.uri: h.score for h in self._score_references(row, layer_id, config)} \
+                    if keep_rankings else None
+                rankings.append(_rankings(self._score_chunks(row.unsqueeze(0), layer_id, config)[0], config,
+                                          reference_scores=refs) if keep_rankings else [])
+        elif config.routing_backend == "tensorized" and not config.use_summary and strategy == "hierarchical":
+            if keep_rankings:  # rankings need every chunk's score on the host
+                hits_by_row, index, scores = self._tensor_hits(query, layer_id, config)
+                if index is not None:
+                    rankings = [_rankings(h, config) for h in hits_by_row]
             else:
-                raise ValueError(f"Unsupported search_strategy: {config.search_strategy}")
+                index = self.routing_index(layer_id, query, reuse=config.cache_build_mode == "detached")
+                hits_by_row, scores = None, None if index is None else score_index(
+                    query, index, config.gist_score_aggregation)
+            selected = empty if index is None else \
+                self._hierarchical_from_tensors(hits_by_row, index, scores, layer_id, config)
+        else:
+            if config.routing_backend == "tensorized" and not config.use_summary:
+                hits_by_row = self._tensor_hits(query, layer_id, config)[0]
+            else:
+                hits_by_row = self._score_chunks(query, layer_id, config)
+            choose = _HOST_STRATEGIES.get(strategy)
+            if choose is None:
+                raise ValueError(f"Unsupported search_strategy: {strategy}")
+            selected = [choose(hits, layer_id, config) for hits in hits_by_row]
+            rankings = [_rankings(hits, config) if keep_rankings else [] for hits in hits_by_row]
         self._last_rankings_by_layer[layer_id] = rankings
         return selected
 
