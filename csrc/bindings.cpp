@@ -543,6 +543,95 @@ void tp_allgather(torch::Tensor src, std::vector<int64_t> dsts, std::vector<int6
   check(pra_tp_allgather(a, stream()), "tp_allgather");
 }
 
+// ---------------------------------------------------------------- decode GEMM
+// Per-device split-K workspace and arrival counters (zero between calls: the finishing CTA of a
+// tile clears its part), allocated on first use and kept for the process.
+torch::Tensor& decode_gemm_state(const torch::Device& dev, bool counters) {
+  static auto* bufs = new std::map<std::pair<int, bool>, torch::Tensor>();
+  auto& t = (*bufs)[{dev.index(), counters}];
+  if (!t.defined()) {
+    auto opts = torch::TensorOptions().device(dev);
+    t = counters ? torch::zeros({DG_MAX_TILES}, opts.dtype(at::kInt))
+                 : torch::zeros({(int64_t)pra_decode_gemm_workspace_floats()}, opts.dtype(at::kFloat));
+  }
+  return t;
+}
+
+// out[M, N] (+ out2 for columns >= split_col) = x[M, K] w[N, K]^T (+ bias, + residual); with peer
+// addresses in recv / flags (one per rank) the result is summed over the ranks (row-parallel
+// projection) inside the same kernel.  splits <= 0 picks the K split from the SM count.
+void decode_gemm(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
+                 c10::optional<torch::Tensor> residual, torch::Tensor out, c10::optional<torch::Tensor> out2,
+                 int64_t split_col, int64_t splits, std::vector<int64_t> recv, std::vector<int64_t> flags, int64_t rank,
+                 c10::optional<torch::Tensor> epochs, int64_t max_spins, c10::optional<torch::Tensor> error) {
+  c10::cuda::CUDAGuard guard(x.device());
+  expect(x, at::kBFloat16, "x");
+  expect(w, at::kBFloat16, "w");
+  expect(out, at::kBFloat16, "out");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && w.dim() == 2 && w.is_contiguous() && w.size(1) == x.size(1),
+              "decode_gemm: x [M, K] (unit column stride) and w [N, K] contiguous");
+  TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1 && out.size(0) == x.size(0), "decode_gemm: out [M, >=cols]");
+  DecodeGemmArgs a{};
+  a.x = ptr<const __nv_bfloat16>(x);
+  a.ldx = x.stride(0);
+  a.w = ptr<const __nv_bfloat16>(w);
+  a.M = x.size(0);
+  a.N = w.size(0);
+  a.K = w.size(1);
+  a.out = ptr<__nv_bfloat16>(out);
+  a.ldo = out.stride(0);
+  a.bias = optr<__nv_bfloat16>(bias);
+  if (bias.has_value()) TORCH_CHECK(bias->numel() == a.N && bias->scalar_type() == at::kBFloat16, "bias [N] bf16");
+  if (residual.has_value()) {
+    expect(*residual, at::kBFloat16, "residual");
+    TORCH_CHECK(residual->dim() == 2 && residual->stride(0) == a.ldo && residual->stride(1) == 1 &&
+                    residual->size(0) == a.M, "residual must share out's row stride");
+    a.residual = ptr<const __nv_bfloat16>(*residual);
+  }
+  a.split_col = out2.has_value() ? (int)split_col : a.N;
+  if (out2.has_value()) {
+    expect(*out2, at::kBFloat16, "out2");
+    TORCH_CHECK(out2->dim() == 2 && out2->stride(1) == 1 && out2->size(0) == a.M && out2->size(1) >= a.N - split_col,
+                "out2 [M, >= N - split_col]");
+    a.out2 = ptr<__nv_bfloat16>(*out2);
+    a.ldo2 = out2->stride(0);
+  }
+  TORCH_CHECK(out.size(1) >= a.split_col, "out narrower than its columns");
+  const int tiles = (a.N + 127) / 128, nkb = a.K / 64;
+  static int sm_cache[64] = {};
+  int& sms = sm_cache[x.device().index() & 63];
+  if (sms == 0) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, x.device().index());
+  if (splits <= 0) {
+    // split K only while every split keeps >= 8 stages of 64 (shorter splits pay more in the
+    // workspace reduction than they gain in parallel weight streams)
+    splits = std::max(1, std::min(nkb / 8, sms / std::max(tiles, 1)));
+  }
+  a.splits = (int)splits;
+  a.workspace = ptr<float>(decode_gemm_state(x.device(), false));
+  a.counters = reinterpret_cast<uint32_t*>(decode_gemm_state(x.device(), true).data_ptr());
+  a.world = 1;
+  if (!recv.empty()) {
+    const int world = recv.size();
+    TORCH_CHECK(world <= TP_MAX_RANKS && (int)flags.size() == world && epochs.has_value() && error.has_value(),
+                "fused all-reduce needs one receive buffer and one flag area per rank, epochs and an error word");
+    TORCH_CHECK(!out2.has_value(), "the fused all-reduce writes one output");
+    TORCH_CHECK((int64_t)tiles * std::max<int64_t>(splits, 1) <= sms,
+                "fused all-reduce grids must fit on the SMs at once (tiles x splits <= SM count)");
+    TORCH_CHECK(out.is_contiguous() && out.size(1) == a.N, "fused all-reduce: out [M, N] contiguous");
+    a.world = world;
+    a.rank = rank;
+    for (int p = 0; p < world; ++p) {
+      a.recv[p] = reinterpret_cast<__nv_bfloat16*>(recv[p]);
+      a.flags[p] = reinterpret_cast<uint32_t*>(flags[p]);
+    }
+    TORCH_CHECK(epochs->scalar_type() == at::kInt && epochs->numel() >= DG_MAX_TILES, "epochs: int32 [DG_MAX_TILES]");
+    a.epochs = reinterpret_cast<uint32_t*>(epochs->data_ptr());
+    a.max_spins = max_spins;
+    a.error = ptr<int>(*error);
+  }
+  check(pra_decode_gemm(a, stream()), "decode_gemm");
+}
+
 // ---------------------------------------------------------------- Llama-family ops
 // Rotary copy: rows of src (heads * head_dim, unit stride) to dst rows (dst_rows or identity).
 void rope_copy(torch::Tensor src, torch::Tensor dst, c10::optional<torch::Tensor> dst_rows,
@@ -1152,6 +1241,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("route_merge", &route_merge);
   m.def("embed_add", &embed_add);
   m.def("combine_partials", &combine_partials);
+  m.def("decode_gemm", &decode_gemm);
+  m.def("decode_gemm_max_tiles", []() { return (int64_t)DG_MAX_TILES; });
   m.def("plan_batch", &pra_plan_batch, "native cache-build planner (returns None when a batch needs the Python planner)");
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_open", &ipc_open);

@@ -1,0 +1,380 @@
+// Decode GEMMs on the 5th-generation tensor cores, with the row-parallel all-reduce fused in.
+//
+// Decode multiplies few token rows (M <= 64) by large weights, so the weight stream is the
+// whole cost.  Each CTA owns 128 output features (one weight slab) and, with split-K, a range
+// of the reduction; the MMA is "swapped": A = the weight tile (128 features x 64 K, K-major),
+// B = the token rows (M x 64 K, K-major), so the fp32 accumulator in TMEM is D^T[feature][token]
+// with one TMEM lane per output feature.  Both operands stream through a 6-stage ring of 2-D
+// TMA tiles in the 128-byte swizzle layout (64 K elements per row): one thread issues the
+// copies against "full" mbarriers, one thread issues the MMAs and releases each stage through
+// its "empty" mbarrier (tcgen05.commit), so a CTA keeps up to six tiles in flight with two
+// instructions per tile instead of one 16-byte copy per thread per chunk.
+//
+// Epilogues (the accumulator is staged through shared memory as fp32 [token][feature] so every
+// global access is a 16-byte row chunk):
+//  * plain: + bias, + residual, bf16 store; columns >= split_col go to a second output (the
+//    routing query rows appended to a QKV weight land in their own buffer);
+//  * split-K: every split adds its fp32 partial into a workspace tile with vector reductions;
+//    the last split to arrive (per-tile counter) finishes the tile and clears the workspace;
+//  * fused all-reduce (tensor-parallel row-parallel projection, world > 1): the finishing CTA
+//    pushes its bf16 partial tile into every rank's receive buffer (plain NVLink peer stores),
+//    raises a per-tile flag on every rank with a release store, waits (bounded) for every
+//    rank's flag of the same tile, then adds the residual to the sum of all ranks' partials.
+//    Tile j of every rank meets tile j of every peer, so no grid-wide barrier is needed, and
+//    the per-tile call counters live in device memory (graph capture replays stay in step).
+//    Callers alternate two receive/flag halves between calls, so a rank that runs ahead
+//    never writes a half its peers may still be reading.
+#include <cuda.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tcgen05.cuh"
+
+namespace pra {
+namespace dg {
+
+constexpr int NT = 128;   // 4 warps: TMEM lanes 0..127 are the tile's 128 output features
+constexpr int BF = 128;   // output features per tile
+constexpr int BK = 64;    // reduction depth per stage: one 128-byte swizzle atom of bf16
+constexpr int MT = 64;    // token rows per tile (MMA N)
+constexpr int STAGES = 6;
+constexpr int A_BYTES = BF * BK * 2;  // 16 KB
+constexpr int B_BYTES = MT * BK * 2;  // 8 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int OFF_BAR = STAGES * STAGE_BYTES;
+constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;  // + barriers, + alignment slack for the 1024-byte swizzle atoms
+constexpr int TMEM_COLS = MT;
+constexpr long long WAIT_CYCLES = 4000000000LL;  // about two seconds at the boost clock
+static_assert(MT * BF * 4 <= OFF_BAR, "the fp32 epilogue tile reuses the stage memory");
+
+__device__ __forceinline__ void signal_store(uint32_t* addr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+__device__ __forceinline__ void expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// 2-D tile copy of this GPU's global memory into this CTA's shared memory, completing on `bar`
+// (no cluster, no multicast); x = the K element (a multiple of 64), y = the row.
+__device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Shared-memory descriptor of a K-major bf16 tile in the 128-byte swizzle layout TMA writes:
+// rows of 128 bytes (64 K elements) in 1024-byte atoms of 8 rows (SBO = 1024); the K offset
+// within the atom moves the start address by 32 bytes per 16 elements.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+  uint64_t d = (uint64_t)((addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;            // leading byte offset (unused by swizzled K-major layouts)
+  d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset: 8 rows x 128 bytes
+  d |= (uint64_t)1 << 46;            // descriptor version
+  d |= (uint64_t)2 << 61;            // 128-byte swizzle
+  return d;
+}
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ void staged8(const float* p, float (&v)[8]) {
+  const float4 lo = reinterpret_cast<const float4*>(p)[0], hi = reinterpret_cast<const float4*>(p)[1];
+  v[0] = lo.x, v[1] = lo.y, v[2] = lo.z, v[3] = lo.w, v[4] = hi.x, v[5] = hi.y, v[6] = hi.z, v[7] = hi.w;
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
+  uint4 out;
+  uint32_t* o = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
+  return out;
+}
+
+__global__ void __launch_bounds__(NT) decode_gemm_kernel(const __grid_constant__ CUtensorMap map_w,
+                                                          const __grid_constant__ CUtensorMap map_x, DecodeGemmArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  // the swizzle atoms need 1024-byte alignment
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* empty = full + STAGES;
+  uint64_t* done = empty + STAGES;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(done + 1);
+  uint32_t* s_epoch = s_tmem + 1;
+  int* s_flag = reinterpret_cast<int*>(s_tmem + 2);  // [0] a wait gave up, [1] last split, [2] peer wait gave up
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile = blockIdx.x, split = blockIdx.y;
+  const int n0 = tile * BF;
+  const int nkb = a.K / BK;
+  const int per = (nkb + a.splits - 1) / a.splits;
+  const int kb0 = split * per, kb1 = min(nkb, kb0 + per);
+  const int nk = kb1 - kb0;  // >= 1: the host sizes splits so every split has work
+
+  if (warp == 0) {
+    tc::alloc(s_tmem, TMEM_COLS);
+    tc::relinquish();
+  }
+  if (tid == 32) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    mbar_init(done, 1);
+    s_flag[0] = s_flag[1] = s_flag[2] = 0;
+    tc::fence_mbarrier_init();
+  }
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 0 && lane == 0) {  // TMA producer
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(&map_w) : "memory");
+    for (int kb = 0; kb < nk; ++kb) {
+      const int slot = kb % STAGES;
+      if (kb >= STAGES && !tc::mbar_wait_cycles(empty + slot, (uint32_t)((kb / STAGES - 1) & 1), WAIT_CYCLES)) {
+        s_flag[0] = 1;
+        break;
+      }
+      uint8_t* st = smem + slot * STAGE_BYTES;
+      expect_tx(full + slot, STAGE_BYTES);
+      tma_load(st, &map_w, (kb0 + kb) * BK, n0, full + slot);
+      tma_load(st + A_BYTES, &map_x, (kb0 + kb) * BK, 0, full + slot);
+    }
+  } else if (warp == 1 && lane == 0) {  // MMA issuer
+    constexpr uint32_t IDESC = tc::idesc_bf16(BF, MT, false);
+    for (int kb = 0; kb < nk; ++kb) {
+      const int slot = kb % STAGES;
+      if (!tc::mbar_wait_cycles(full + slot, (uint32_t)((kb / STAGES) & 1), WAIT_CYCLES)) {
+        s_flag[0] = 1;
+        break;
+      }
+      tc::fence_after();
+      const uint32_t a_addr = smem_u32(smem + slot * STAGE_BYTES), b_addr = a_addr + A_BYTES;
+#pragma unroll
+      for (int kk = 0; kk < BK / 16; ++kk)
+        tc::mma_bf16(tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), IDESC,
+                     (kb > 0 || kk > 0) ? 1u : 0u);
+      tc::commit(empty + slot);
+    }
+    tc::commit(done);
+  }
+  // everyone: the accumulator is complete once `done` fires
+  if (!tc::mbar_wait_cycles(done, 0, WAIT_CYCLES)) s_flag[0] = 1;
+  tc::fence_after();
+  __syncthreads();
+  const bool timed_out = s_flag[0] != 0;
+  float acc[MT];
+  if (!timed_out) {
+    uint32_t r[MT];
+    tc::ld64(tmem + ((uint32_t)(warp * 32) << 16), r);
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc[m] = __uint_as_float(r[m]);
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) tc::dealloc(tmem, TMEM_COLS);
+  if (timed_out) {
+    if (tid == 0 && a.error) atomicExch(a.error, 1);
+    return;
+  }
+  const int feat = tid;  // this thread's output feature within the tile (TMEM lane)
+
+  // ---- split-K: sum the splits' partials in the workspace; the last split finishes the tile
+  if (a.splits > 1) {
+    float* ws = a.workspace + ((int64_t)tile * BF + feat) * MT;
+#pragma unroll
+    for (int m = 0; m < MT; m += 4) red_add_v4(ws + m, acc[m], acc[m + 1], acc[m + 2], acc[m + 3]);
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_flag[1] = atomicAdd(a.counters + tile, 1u) == (uint32_t)(a.splits - 1);
+    __syncthreads();
+    if (!s_flag[1]) return;
+    __threadfence();
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int m = 0; m < MT; m += 4) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(ws + m));
+      acc[m] = v.x;
+      acc[m + 1] = v.y;
+      acc[m + 2] = v.z;
+      acc[m + 3] = v.w;
+      __stcg(reinterpret_cast<float4*>(ws + m), zero);  // the workspace starts at zero for the next call
+    }
+    if (tid == 0) a.counters[tile] = 0;
+  }
+
+  // ---- stage the fp32 tile as [token][feature] so every global access is a 16-byte row chunk
+  float* tile_s = reinterpret_cast<float*>(smem);
+#pragma unroll
+  for (int m = 0; m < MT; ++m) tile_s[m * BF + feat] = acc[m];
+  __syncthreads();
+  constexpr int CHUNKS = MT * (BF / 8);  // 8 features per chunk
+
+  if (a.world <= 1) {
+    for (int i = tid; i < CHUNKS; i += NT) {
+      const int m = i / (BF / 8), c = i % (BF / 8), n = n0 + c * 8;
+      if (m >= a.M || n >= a.N) continue;
+      float v[8];
+      staged8(tile_s + m * BF + c * 8, v);
+      if (a.bias) {
+        float b[8];
+        load8(a.bias + n, b);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] += b[j];
+      }
+      if (a.residual) {
+        float r[8];
+        load8(a.residual + (int64_t)m * a.ldo + n, r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] += r[j];
+      }
+      const bool second = a.out2 != nullptr && n >= a.split_col;
+      __nv_bfloat16* dst = second ? a.out2 + (int64_t)m * a.ldo2 + (n - a.split_col) : a.out + (int64_t)m * a.ldo + n;
+      *reinterpret_cast<uint4*>(dst) = pack8(v);
+    }
+    return;
+  }
+
+  // ---- fused all-reduce: push this rank's bf16 partial tile to every rank, flag, wait, reduce
+  if (tid == 0) {
+    const uint32_t e = a.epochs[tile] + 1;
+    a.epochs[tile] = e;
+    *s_epoch = e;
+  }
+  for (int i = tid; i < CHUNKS; i += NT) {
+    const int m = i / (BF / 8), c = i % (BF / 8), n = n0 + c * 8;
+    if (m >= a.M || n >= a.N) continue;
+    float v[8];
+    staged8(tile_s + m * BF + c * 8, v);
+    const uint4 packed = pack8(v);
+    const int64_t at = ((int64_t)a.rank * a.M + m) * a.N + n;
+    for (int p = 0; p < a.world; ++p) *reinterpret_cast<uint4*>(a.recv[p] + at) = packed;
+  }
+  __syncthreads();
+  const uint32_t epoch = *s_epoch;
+  if (tid < a.world) {
+    __threadfence_system();
+    signal_store(a.flags[tid] + (int64_t)tile * a.world + a.rank, epoch);
+  }
+  if (tid < a.world) {
+    if (!bounded_wait_geq(a.flags[a.rank] + (int64_t)tile * a.world + tid, epoch, a.max_spins)) {
+      s_flag[2] = 1;
+      atomicExch(a.error, 2);
+    }
+  }
+  __syncthreads();
+  if (s_flag[2]) return;
+  for (int i = tid; i < CHUNKS; i += NT) {
+    const int m = i / (BF / 8), c = i % (BF / 8), n = n0 + c * 8;
+    if (m >= a.M || n >= a.N) continue;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (a.residual) load8(a.residual + (int64_t)m * a.ldo + n, v);
+    if (a.bias) {
+      float b[8];
+      load8(a.bias + n, b);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] += b[j];
+    }
+    for (int p = 0; p < a.world; ++p) {  // rank order: every rank sums identically
+      float part[8];
+      load8(a.recv[a.rank] + ((int64_t)p * a.M + m) * a.N + n, part);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] += part[j];
+    }
+    *reinterpret_cast<uint4*>(a.out + (int64_t)m * a.ldo + n) = pack8(v);
+  }
+}
+
+}  // namespace dg
+}  // namespace pra
+
+namespace {
+
+// Tensor maps of [rows, cols] bf16 matrices (row stride ld elements) cut into 64-column x
+// `box_rows` boxes in the 128-byte swizzle layout; cached by (address, shape) because weights
+// are static and activation buffers repeat, and encoding costs microseconds of host time.
+struct MapKey {
+  const void* ptr;
+  int64_t cols, rows, ld, box_rows;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && cols == o.cols && rows == o.rows && ld == o.ld && box_rows == o.box_rows;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    return std::hash<const void*>()(k.ptr) ^ (size_t)(k.cols * 1000003 + k.rows * 7919 + k.ld * 31 + k.box_rows);
+  }
+};
+
+const CUtensorMap* tile_map(const void* ptr, int64_t cols, int64_t rows, int64_t ld, int box_rows) {
+  static std::mutex mutex;
+  static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+  const MapKey key{ptr, cols, rows, ld, box_rows};
+  std::lock_guard<std::mutex> lock(mutex);
+  auto it = cache.find(key);
+  if (it != cache.end()) return &it->second;
+  if (cache.size() > 4096) cache.clear();  // bounded: stale entries of freed buffers
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)pra::dg::BK, (cuuint32_t)box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  if (cuTensorMapEncodeTiled(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, elem,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return nullptr;
+  return &cache.emplace(key, map).first->second;
+}
+
+}  // namespace
+
+size_t pra_decode_gemm_workspace_floats() { return (size_t)DG_MAX_TILES * pra::dg::BF * pra::dg::MT; }
+
+cudaError_t pra_decode_gemm(const DecodeGemmArgs& a, cudaStream_t st) {
+  using namespace pra::dg;
+  if (a.M <= 0 || a.N <= 0) return cudaSuccess;
+  if (a.M > MT || a.K % BK || a.N % 8 || a.ldo % 8 || a.ldx % 8 || a.world > TP_MAX_RANKS) return cudaErrorInvalidValue;
+  if (a.out2 && (a.split_col % 8 || a.ldo2 % 8)) return cudaErrorInvalidValue;
+  const int tiles = (a.N + BF - 1) / BF;
+  if (tiles > DG_MAX_TILES) return cudaErrorInvalidValue;
+  const int nkb = a.K / BK;
+  int splits = a.splits < 1 ? 1 : (a.splits > nkb ? nkb : a.splits);
+  const int per = (nkb + splits - 1) / splits;
+  splits = (nkb + per - 1) / per;  // no empty split
+  if (splits > 1 && (a.workspace == nullptr || a.counters == nullptr)) return cudaErrorInvalidValue;
+  if (a.world > 1 && (a.epochs == nullptr || a.error == nullptr)) return cudaErrorInvalidValue;
+  static int configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(decode_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    configured[dev] = 1;
+  }
+  if ((reinterpret_cast<uintptr_t>(a.w) | reinterpret_cast<uintptr_t>(a.x)) & 15) return cudaErrorInvalidValue;
+  const CUtensorMap* map_w = tile_map(a.w, a.K, a.N, a.K, BF);
+  const CUtensorMap* map_x = tile_map(a.x, a.K, a.M, a.ldx, MT);
+  if (map_w == nullptr || map_x == nullptr) return cudaErrorInvalidValue;
+  DecodeGemmArgs b = a;
+  b.splits = splits;
+  decode_gemm_kernel<<<dim3(tiles, splits), NT, SMEM_BYTES, st>>>(*map_w, *map_x, b);
+  return cudaGetLastError();
+}

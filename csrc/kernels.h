@@ -311,3 +311,35 @@ cudaError_t pra_tp_allgather(const TpAllgatherArgs& args, cudaStream_t stream);
 // ---- embeddings (embed.cu) ---------------------------------------------------------------
 cudaError_t pra_embed_add(const int* ids, const int* positions, int period, const __nv_bfloat16* tok,
                           const __nv_bfloat16* pos, int64_t M, int D, __nv_bfloat16* out, cudaStream_t stream);
+
+// ---- decode GEMM (decode_gemm.cu) ---------------------------------------------------------
+// out[M, N] = x[M, K] . w[N, K]^T for few token rows (M <= 64): one CTA per 128 output features
+// (and K split), tcgen05 MMA with the weight tile as A (M = 128 features) and the token rows as
+// B, fp32 accumulator in TMEM.  Epilogue: bias, residual, bf16 store split over two outputs
+// (columns >= split_col go to out2), or, with world > 1, the fused all-reduce of a row-parallel
+// projection (every rank's bf16 partial tile pushed to every rank, per-tile flags, residual + sum).
+constexpr int DG_MAX_TILES = 1024;
+struct DecodeGemmArgs {
+  const __nv_bfloat16* x;  // [M, K] rows at stride ldx
+  int64_t ldx;
+  const __nv_bfloat16* w;  // [N, K] row-major
+  int M, N, K, splits;
+  const __nv_bfloat16* bias;      // [N] or null
+  const __nv_bfloat16* residual;  // [M, N] (row stride ldo) or null
+  __nv_bfloat16* out;             // columns [0, split_col): out[m * ldo + n]
+  int64_t ldo;
+  __nv_bfloat16* out2;            // columns [split_col, N): out2[m * ldo2 + n - split_col] (null: none)
+  int64_t ldo2;
+  int split_col;
+  float* workspace;               // split-K partial sums [tiles, 128, 64] (zero between calls)
+  uint32_t* counters;             // split-K arrivals [tiles] (zero between calls)
+  // fused all-reduce (world > 1)
+  int world, rank;
+  __nv_bfloat16* recv[TP_MAX_RANKS];  // every rank's receive half: [world][M][N]
+  uint32_t* flags[TP_MAX_RANKS];      // every rank's flag half: [DG_MAX_TILES][world]
+  uint32_t* epochs;                   // local per-tile call counters [DG_MAX_TILES]
+  long long max_spins;
+  int* error;                         // 1 + phase after a bounded wait gave up
+};
+size_t pra_decode_gemm_workspace_floats();
+cudaError_t pra_decode_gemm(const DecodeGemmArgs& a, cudaStream_t stream);

@@ -56,11 +56,11 @@ def run_decode_benchmark(*, model: str = "llama3-8b", batch: int = 64, prompt_to
     tok = logits.float().argmax(-1)
     host_tok.copy_(tok.cpu())
 
-    step_fn = engine.decode_step
+    step_fn = lambda ids: engine.decode_step(ids, sample=True)  # noqa: E731  greedy ids, vocabulary-parallel
 
     def one_step():
         ids = host_tok.to(device, non_blocking=True)
-        nxt = step_fn(ids).float().argmax(-1)
+        nxt = step_fn(ids)
         host_out.copy_(nxt, non_blocking=True)
         return nxt
 
@@ -69,7 +69,7 @@ def run_decode_benchmark(*, model: str = "llama3-8b", batch: int = 64, prompt_to
         torch.cuda.synchronize()
         host_tok.copy_(host_out)
         if graphs and i == 0:  # capture after one eager step, replay for the rest
-            engine.capture_decode()
+            engine.capture_decode(sample=True)
             step_fn = engine.decode_step_graphed
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     if tp is not None:

@@ -21,6 +21,7 @@ gate/up GEMM -> SwiGLU -> down GEMM with the residual fused.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import torch
@@ -28,6 +29,11 @@ import torch
 from ..models.llama import PRALlamaConfig, PRALlamaReference
 from ..ops import _ext
 from .routing import select_chunks
+
+# Decode projections on this library's decode GEMM (PRA_DECODE_GEMM=cutlass keeps the CUTLASS
+# stream-K GEMM and the separate all-reduce); rows per call it serves.
+_DECODE_GEMM = os.environ.get("PRA_DECODE_GEMM", "native").lower() != "cutlass"
+_DECODE_ROWS = 64
 
 
 # ---------------------------------------------------------------------------
@@ -43,6 +49,8 @@ class LayerWeights:
     ln_post: torch.Tensor
     gate_up: torch.Tensor      # [2 F (local shard), d]
     down: torch.Tensor         # [d, F (local shard)]
+    qkv_route: torch.Tensor | None = None       # [q | k | v | routing-query rows] (decode GEMM)
+    qkv_route_bias: torch.Tensor | None = None
 
 
 class LlamaWeights:
@@ -176,6 +184,54 @@ class PRALlamaEngine:
         self.cache_len: torch.Tensor | None = None
         self.namespace: tuple[torch.Tensor, torch.Tensor] | None = None
         self.last_selection: dict[int, torch.Tensor] = {}
+        # Vocabulary-parallel LM head: under tensor parallelism each rank holds rows
+        # [vocab_start, vocab_end) of the head and computes only that slice of the logits.
+        vocab = self.w.head.shape[0]
+        per = -(-vocab // self.tp_size)
+        per = -(-per // 8) * 8  # 16-byte aligned slices
+        rank = self.w.tp_rank
+        self.vocab_start = min(vocab, rank * per)
+        self.vocab_end = min(vocab, self.vocab_start + per)
+        self.head_local = self.w.head[self.vocab_start: self.vocab_end]
+        # Decode (<= 64 rows) runs its projections on this library's decode GEMM, the row-parallel
+        # ones fused with their all-reduce; each layer's QKV weight gains the routing-query rows.
+        self.native_decode = _DECODE_GEMM
+        self.route_dim = cfg.num_key_value_heads * cfg.head_dim
+        if self.native_decode:
+            self._attach_route_rows()
+
+    def _attach_route_rows(self) -> None:
+        """Append to every layer's ``[q | k | v]`` weight the routing-query rows: for each KV head,
+        the mean of its group's query rows (over ALL ranks' heads, gathered once here), so the
+        decode QKV GEMM also yields the full-width routing query (the KV-group mean of the
+        pre-rotary query) and routing needs no per-step gather.  ``lw.qkv`` becomes a view of the
+        first rows (no second copy of the projection)."""
+        cfg = self.cfg
+        g, dh = cfg.group, cfg.head_dim
+        qd, kd = self.q_dim, self.kv_dim
+
+        def group_mean(rows: torch.Tensor) -> torch.Tensor:  # [heads * dh, ...] -> [kv_heads * dh, ...]
+            return rows.float().unflatten(0, (self.kv_heads, g, dh)).mean(1).flatten(0, 1)
+
+        def gather(t: torch.Tensor) -> torch.Tensor:
+            if self.tp is None:
+                return t
+            import torch.distributed as dist
+
+            parts = [torch.empty_like(t) for _ in range(self.tp_size)]
+            dist.all_gather(parts, t.contiguous(), group=self.tp.group)
+            return torch.cat(parts)  # rank-major = KV-head order
+
+        for lw in self.w.layers:
+            route = gather(group_mean(lw.qkv[:qd]).to(torch.bfloat16))
+            fused = torch.cat([lw.qkv, route]).contiguous()
+            lw.qkv_route = fused
+            lw.qkv = fused[: qd + 2 * kd]
+            lw.qkv_route_bias = None
+            if lw.qkv_bias is not None:
+                rb = gather(group_mean(lw.qkv_bias[:qd]).to(torch.bfloat16))
+                lw.qkv_route_bias = torch.cat([lw.qkv_bias, rb]).contiguous()
+                lw.qkv_bias = lw.qkv_route_bias[: qd + 2 * kd]
 
     # -- helpers ----------------------------------------------------------------
     def rope_tables(self, max_pos: int) -> tuple[torch.Tensor, torch.Tensor]:
@@ -193,15 +249,24 @@ class PRALlamaEngine:
     def _norm(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         return self.ext.norm_fwd(x, w, None, self.cfg.rms_norm_eps, True)[0]
 
+    def _decode_rows(self, x) -> bool:
+        return self.native_decode and x.shape[0] <= _DECODE_ROWS
+
     def _gemm(self, x, w, bias=None, residual=None) -> torch.Tensor:
         out = torch.empty((x.shape[0], w.shape[0]), device=x.device, dtype=torch.bfloat16)
+        if self._decode_rows(x):
+            self.ext.decode_gemm(x, w, bias, residual, out, None, 0, 0, [], [], 0, None, 0, None)
+            return out
         self.ext.gemm("tn", x, w, residual, out, bias, None, 1.0, 1.0 if residual is not None else 0.0, None)
         return out
 
     def _row_parallel(self, x, w, residual) -> torch.Tensor:
-        """out = residual + x @ w^T, summed over tensor-parallel ranks."""
+        """out = residual + x @ w^T, summed over tensor-parallel ranks (decode rows: one fused
+        GEMM + all-reduce kernel)."""
         if self.tp is None:
             return self._gemm(x, w, residual=residual)
+        if self._decode_rows(x) and x.shape[0] <= self.tp.decode_rows and w.shape[0] <= self.tp.decode_width:
+            return self.tp.fused_gemm_allreduce(x, w, residual)
         return self.tp.gemm_allreduce(x, w, residual)
 
     def _mlp(self, lw: LayerWeights, x: torch.Tensor) -> torch.Tensor:
@@ -214,14 +279,23 @@ class PRALlamaEngine:
     def _embed(self, ids: torch.Tensor) -> torch.Tensor:
         return self.w.embed[ids.reshape(-1)].contiguous()
 
-    def _route(self, layer: int, q_rows: torch.Tensor, rows: int, namespace=None):
-        """Routing query (group mean of the pre-rotary query) -> memory row lists."""
+    def _route(self, layer: int, q_rows: torch.Tensor | None, rows: int, namespace=None,
+               route_query: torch.Tensor | None = None):
+        """Routing query (group mean of the pre-rotary query) -> memory row lists.
+
+        ``route_query`` is that query already at full width (bf16, from the decode QKV GEMM);
+        without it the mean is taken here from this rank's query heads and gathered.  Scores
+        against the normalised gists only rank the chunks (a query's norm is the same for all
+        of them); the candidates are rescored as exact fp32 cosines."""
         cfg, mem = self.cfg, self.memory
-        g = cfg.group
-        rq = q_rows.float().view(rows, self.kv_heads, g, cfg.head_dim).mean(2).reshape(rows, self.kv_dim)
-        if self.tp is not None:
-            rq = self.tp.all_gather_columns(rq)  # full kv_dim routing query on every rank
-        rqn = torch.nn.functional.normalize(rq, dim=-1, eps=1e-12).to(torch.bfloat16)
+        if route_query is not None:
+            rqn = route_query
+            rq = route_query.float()
+        else:
+            rq = q_rows.float().view(rows, self.kv_heads, cfg.group, cfg.head_dim).mean(2).reshape(rows, self.kv_dim)
+            if self.tp is not None:
+                rq = self.tp.all_gather_columns(rq)  # full kv_dim routing query on every rank
+            rqn = torch.nn.functional.normalize(rq, dim=-1, eps=1e-12).to(torch.bfloat16)
         k = cfg.top_k_chunks
         k_cand = min(max(k * self.k_cand_factor, k), 512)
         budget = cfg.memory_budget_tokens if cfg.memory_budget_tokens is not None else -1
@@ -378,13 +452,44 @@ class PRALlamaEngine:
             x = self._mlp(lw, x)
         return self._logits(x[last])
 
-    def _logits(self, x_last: torch.Tensor) -> torch.Tensor:
+    def _local_logits(self, x_last: torch.Tensor) -> torch.Tensor:
+        """This rank's vocabulary slice of the logits ``[B, vocab_end - vocab_start]``."""
         h = self._norm(x_last.contiguous(), self.w.norm)
-        return self._gemm(h, self.w.head)
+        return self._gemm(h, self.head_local)
+
+    def _logits(self, x_last: torch.Tensor) -> torch.Tensor:
+        """Full logits ``[B, V]`` (the slices of every rank gathered under tensor parallelism)."""
+        local = self._local_logits(x_last)
+        if self.tp is None:
+            return local
+        import torch.distributed as dist
+
+        width = -(-self.w.head.shape[0] // self.tp_size)
+        width = -(-width // 8) * 8
+        padded = torch.zeros((local.shape[0], width), device=local.device, dtype=local.dtype)
+        padded[:, : local.shape[1]] = local
+        parts = [torch.empty_like(padded) for _ in range(self.tp_size)]
+        dist.all_gather(parts, padded, group=self.tp.group)
+        return torch.cat(parts, dim=1)[:, : self.w.head.shape[0]]
+
+    def _greedy(self, x_last: torch.Tensor) -> torch.Tensor:
+        """Greedy next token ids ``[B]``: each rank's (max, index) over its vocabulary slice, merged
+        across ranks (ties go to the lowest index, as ``argmax`` over the full logits does)."""
+        local = self._local_logits(x_last)
+        best, idx = local.float().max(dim=-1)
+        if self.tp is None:
+            return idx
+        pair = torch.stack([best, (idx + self.vocab_start).float()], dim=1)  # ids < 2^24 are exact in fp32
+        every = self.tp.gather_small(pair).view(-1, self.tp_size, 2)
+        score, ids = every[..., 0], every[..., 1]
+        top = score.max(dim=1, keepdim=True).values
+        return torch.where(score == top, ids, torch.full_like(ids, float("inf"))).min(dim=1).values.long()
 
     @torch.no_grad()
-    def decode_step(self, token_ids: torch.Tensor) -> torch.Tensor:
-        """One token per row at position ``cache_len[b]``; returns logits ``[B, V]``."""
+    def decode_step(self, token_ids: torch.Tensor, sample: bool = False) -> torch.Tensor:
+        """One token per row at position ``cache_len[b]``; returns logits ``[B, V]``, or with
+        ``sample=True`` the greedy next token ids ``[B]`` (no full-vocabulary logits are formed
+        under tensor parallelism)."""
         cfg, ext = self.cfg, self.ext
         B = token_ids.shape[0]
         qd, kd = self.q_dim, self.kv_dim
@@ -397,10 +502,17 @@ class PRALlamaEngine:
         max_keys = cfg.memory_tokens_per_row + self.max_len
         for li, lw in enumerate(self.w.layers):
             h = self._norm(x, lw.ln_in)
-            qkv = self._gemm(h, lw.qkv, lw.qkv_bias)
+            rq = None
+            if self._decode_rows(h):  # one GEMM: q, k, v and the full-width routing query
+                qkv = torch.empty((B, qd + 2 * kd), device=self.device, dtype=torch.bfloat16)
+                rq = torch.empty((B, self.route_dim), device=self.device, dtype=torch.bfloat16)
+                ext.decode_gemm(h, lw.qkv_route, lw.qkv_route_bias, None, qkv, rq, qd + 2 * kd, 0, [], [], 0, None,
+                                0, None)
+            else:
+                qkv = self._gemm(h, lw.qkv, lw.qkv_bias)
             mem_args = (None, None, None, None)
             if use_memory and cfg.is_pra_layer(li):
-                mem_idx, mem_len = self._route(li, qkv[:, :qd], B)
+                mem_idx, mem_len = self._route(li, qkv[:, :qd], B, route_query=rq)
                 mem_args = (self.memory.k(li), self.memory.v(li), mem_idx, mem_len)
             kc = self.cache[li, 0].view(B * self.max_len, kd)
             vc = self.cache[li, 1].view(B * self.max_len, kd)
@@ -413,10 +525,10 @@ class PRALlamaEngine:
             x = self._row_parallel(a, lw.o, x)
             x = self._mlp(lw, x)
         self.cache_len.copy_(new_len)  # in place: a captured step replays on the same tensors
-        return self._logits(x)
+        return self._greedy(x) if sample else self._logits(x)
 
     # -- CUDA-graph decode ------------------------------------------------------------
-    def capture_decode(self) -> None:
+    def capture_decode(self, sample: bool = False) -> None:
         """Capture one ``decode_step`` into a CUDA graph (after at least one eager step).
 
         Replays run the whole step (32 layers of GEMMs, routing, attention and the
@@ -426,21 +538,24 @@ class PRALlamaEngine:
         self._graph_ids = torch.zeros(B, dtype=torch.long, device=self.device)
         ar0 = self.tp.epoch_ar if self.tp is not None else 0
         ag0 = self.tp.epoch_ag if self.tp is not None else 0
+        dg0 = self.tp.epoch_dg if self.tp is not None else 0
         torch.cuda.synchronize(self.device)
         graph = torch.cuda.CUDAGraph()
         counter = _ext.launch_counter()
         was, before = counter.enabled, counter.launches
         counter.enabled = True  # count this library's kernels recorded in the graph
         with torch.cuda.graph(graph):
-            self._graph_out = self.decode_step(self._graph_ids)
+            self._graph_out = self.decode_step(self._graph_ids, sample=sample)
         self.graph_launches = counter.launches - before
         counter.launches, counter.enabled = before, was
-        if self.tp is not None and ((self.tp.epoch_ar - ar0) % 2 or (self.tp.epoch_ag - ag0) % 2):
+        if self.tp is not None and ((self.tp.epoch_ar - ar0) % 2 or (self.tp.epoch_ag - ag0) % 2
+                                    or (self.tp.epoch_dg - dg0) % 2):
             raise RuntimeError("a captured step must use both halves of each double buffer equally often")
         self._graph = graph
 
     def decode_step_graphed(self, token_ids: torch.Tensor) -> torch.Tensor:
-        """``decode_step`` through the captured graph (returns the graph's static logits)."""
+        """``decode_step`` through the captured graph (returns the graph's static output: logits, or
+        next token ids when captured with ``sample=True``)."""
         self._graph_ids.copy_(token_ids, non_blocking=True)
         self._graph.replay()
         return self._graph_out
@@ -459,5 +574,5 @@ class PRALlamaEngine:
             out.append(tok)
             if len(out) == max_new_tokens:
                 break
-            tok = self.decode_step(tok).float().argmax(-1)
+            tok = self.decode_step(tok, sample=True)
         return torch.stack(out, dim=1)

@@ -81,7 +81,7 @@ def long_prompt_generate(engine, prompts: list[list[int]], max_new_tokens: int, 
                            position_offset=plan.position_offset)
     out = [first.float().argmax(-1)]
     for _ in range(max_new_tokens - 1):
-        out.append(engine.decode_step(out[-1]).float().argmax(-1))
+        out.append(engine.decode_step(out[-1], sample=True))
     return torch.stack(out, dim=1), plan, first
 
 
@@ -125,15 +125,15 @@ def run_long_prompt_benchmark(*, model: str = "mistral-7b", batch: int = 16, pro
     first, prefill_ms = timed(lambda: engine.prefill(plan.tails, plan.tail_lengths, new_tokens + 1, row_batch=4,
                                                      position_offset=plan.position_offset))
     tok = first.float().argmax(-1)
-    tok = engine.decode_step(tok).float().argmax(-1)  # one eager step, then the captured graph
-    engine.capture_decode()
+    tok = engine.decode_step(tok, sample=True)  # one eager step, then the captured graph
+    engine.capture_decode(sample=True)
     steps = []
     if clocks is not None:
         clocks.__enter__()
     for _ in range(new_tokens - 1):
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        tok = engine.decode_step_graphed(tok).float().argmax(-1)
+        tok = engine.decode_step_graphed(tok)
         e.record()
         steps.append((s, e))
     torch.cuda.synchronize()

@@ -68,7 +68,11 @@ def _upload(device, *arrays, dtype=torch.int32) -> list[torch.Tensor]:
 
 
 def unsupported_reason(cfg) -> str | None:
-    """Why a configuration must use the object path (``None`` when the device path applies)."""
+    """Why a configuration must use the object path (``None`` when the device path applies).
+
+    ``dropout`` is not a reason: a PRA block has no dropout (``src/pra_torch/model.py:56-87``;
+    only vanilla and mixed blocks apply it, and those are refused here), so the ``td_pra_*``
+    profiles, which set dropout 0.1, train on the device path unchanged."""
     head_dim = cfg.d_model // cfg.n_heads
     checks = [
         (cfg.n_vanilla_layers or cfg.n_mixed_layers, "vanilla/mixed blocks"),
@@ -86,7 +90,6 @@ def unsupported_reason(cfg) -> str | None:
         (cfg.reference_level_gist_mode is not None, "URI-level gists"),
         (cfg.gists_per_chunk > 8, "more than 8 gists"),
         (head_dim not in (32, 64, 128), f"head_dim={head_dim}"),
-        (cfg.dropout > 0, "dropout"),
         (cfg.d_model % 8 or cfg.d_ff % 8, "widths not multiple of 8"),
         (cfg.collect_routing_metrics or cfg.collect_rank_diagnostics, "full ranking diagnostics"),
         (cfg.collect_detailed_timing, "host-timed diagnostics"),

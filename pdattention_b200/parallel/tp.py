@@ -26,11 +26,14 @@ from .peer import PeerBuffers
 
 
 class TensorParallel:
+    SMALL_ELEMS = 1 << 16  # single-buffered gathers of a few values per row (greedy sampling)
+
     def __init__(self, group=None, max_partial_elems: int = 64 << 20, max_gather_elems: int = 1 << 20,
-                 max_spins: int = 1 << 23):
+                 max_spins: int = 1 << 23, decode_rows: int = 64, decode_width: int = 8192):
         ext = _ext.require()
         self.group = group or dist.group.WORLD
         self.world = dist.get_world_size(self.group)
+        tiles = int(ext.decode_gemm_max_tiles())
         self.rank = dist.get_rank(self.group)
         self.device = torch.device("cuda", torch.cuda.current_device())
         words = int(ext.tp_signal_words(self.world))
@@ -39,17 +42,31 @@ class TensorParallel:
         self.buffers = PeerBuffers({
             "part0": (max_partial_elems, torch.bfloat16), "part1": (max_partial_elems, torch.bfloat16),
             "gather0": (max_gather_elems, torch.float32), "gather1": (max_gather_elems, torch.float32),
-            "sig_ar": (words, torch.int32), "sig_ag": (words, torch.int32)}, self.group, self.device)
+            "small": (self.SMALL_ELEMS, torch.float32),
+            "dg_recv0": (self.world * decode_rows * decode_width, torch.bfloat16),
+            "dg_recv1": (self.world * decode_rows * decode_width, torch.bfloat16),
+            "dg_flag0": (tiles * self.world, torch.int32), "dg_flag1": (tiles * self.world, torch.int32),
+            "sig_ar": (words, torch.int32), "sig_ag": (words, torch.int32), "sig_small": (words, torch.int32)},
+            self.group, self.device)
         self.parts = [self.buffers.local("part0"), self.buffers.local("part1")]
         self.part_addr = [self.buffers.addresses("part0"), self.buffers.addresses("part1")]
         self.gathers = [self.buffers.local("gather0"), self.buffers.local("gather1")]
         self.gather_addr = [self.buffers.addresses("gather0"), self.buffers.addresses("gather1")]
         self.sig_ar = self.buffers.addresses("sig_ar")
         self.sig_ag = self.buffers.addresses("sig_ag")
+        self.small = self.buffers.local("small")
+        self.small_addr = self.buffers.addresses("small")
+        self.sig_small = self.buffers.addresses("sig_small")
+        # fused GEMM + all-reduce of decode rows: two receive / flag halves, alternated per call
+        self.decode_rows, self.decode_width = decode_rows, decode_width
+        self.dg_recv = [self.buffers.addresses("dg_recv0"), self.buffers.addresses("dg_recv1")]
+        self.dg_flags = [self.buffers.addresses("dg_flag0"), self.buffers.addresses("dg_flag1")]
+        self.dg_epochs = torch.zeros(tiles, dtype=torch.int32, device=self.device)
+        self.epoch_dg = 0
         self.epoch_ar = 0  # host call counters: pick the double buffer half
         self.epoch_ag = 0
         # per-CTA device call counters of the two collectives (graph-replay safe epochs)
-        self.dev_epochs = torch.zeros((2, int(ext.tp_signal_words(1))), dtype=torch.int32, device=self.device)
+        self.dev_epochs = torch.zeros((3, int(ext.tp_signal_words(1))), dtype=torch.int32, device=self.device)
         self.max_spins = int(max_spins)
         self.error = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._gist_slices: dict[int, torch.Tensor] = {}
@@ -70,6 +87,21 @@ class TensorParallel:
                          self.max_spins, self.error)
         return out
 
+    def fused_gemm_allreduce(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None,
+                             bias: torch.Tensor | None = None) -> torch.Tensor:
+        """``residual + sum_ranks x @ w^T`` for at most ``decode_rows`` rows in ONE kernel: each
+        128-feature tile's partial is pushed to every rank over NVLink as soon as it is computed
+        and summed where it lands (``decode_gemm``); the row-parallel projections of decode."""
+        m, n = x.shape[0], w.shape[0]
+        if m > self.decode_rows or n > self.decode_width:
+            raise ValueError("fused all-reduce sized for decode rows; use gemm_allreduce")
+        half = self.epoch_dg & 1
+        self.epoch_dg += 1
+        out = torch.empty((m, n), device=x.device, dtype=torch.bfloat16)
+        _ext.require().decode_gemm(x, w, bias, residual, out, None, 0, 0, self.dg_recv[half], self.dg_flags[half],
+                                   self.rank, self.dg_epochs, self.max_spins, self.error)
+        return out
+
     def all_gather_columns(self, x: torch.Tensor) -> torch.Tensor:
         """``[rows, cols]`` fp32 slices -> ``[rows, world * cols]`` (rank-major column blocks)."""
         rows, cols = x.shape
@@ -81,6 +113,20 @@ class TensorParallel:
         ext.tp_allgather(x.float().contiguous(), self.gather_addr[half], self.sig_ag, self.rank, self.dev_epochs[1],
                          self.max_spins, self.error)
         return self.gathers[half][: rows * cols * self.world].view(rows, cols * self.world).clone()
+
+    def gather_small(self, x: torch.Tensor) -> torch.Tensor:
+        """``[rows, cols]`` fp32 -> ``[rows, world * cols]`` through a single buffer.
+
+        For calls separated by other collectives of this communicator (e.g. one per decode
+        step, whose all-reduces keep the ranks in lockstep), so one buffer is enough and a
+        captured step's double-buffer parity is untouched.  Returns a view of the buffer,
+        valid until the next call."""
+        rows, cols = x.shape
+        if rows * cols * self.world > self.SMALL_ELEMS:
+            raise ValueError("gather larger than the small tensor-parallel buffer")
+        _ext.require().tp_allgather(x.float().contiguous(), self.small_addr, self.sig_small, self.rank,
+                                    self.dev_epochs[2], self.max_spins, self.error)
+        return self.small[: rows * cols * self.world].view(rows, cols * self.world)
 
     # -- memory build ---------------------------------------------------------------
     def local_gist_tables(self, mem, layer: int):

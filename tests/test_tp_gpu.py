@@ -66,6 +66,21 @@ def _worker(rank, world, port, queue):
         torch.cuda.synchronize()
         tp.check()
         result["cos"] = cos
+        # the fused decode GEMM + all-reduce against fp32 partials summed by NCCL
+        gen = torch.Generator(device="cuda").manual_seed(100 + rank)
+        errs = []
+        for m, n, k in ((64, 4096, 512), (5, 256, 1792), (33, 1024, 128)):
+            x = torch.randn(m, k, device="cuda", generator=gen).bfloat16()
+            w = (torch.randn(n, k, device="cuda", generator=gen) * 0.05).bfloat16()
+            res = torch.randn(m, n, device="cuda", generator=torch.Generator(device="cuda").manual_seed(9)).bfloat16()
+            got = tp.fused_gemm_allreduce(x, w, res).float()
+            want = x.float() @ w.float().t()
+            dist.all_reduce(want)
+            want += res.float()
+            errs.append(float((got - want).abs().max() / want.abs().max()))
+        torch.cuda.synchronize()
+        tp.check()
+        result["fused_err"] = errs
         # timeout: rank 1 skips one all-reduce; rank 0's wait must run out and report
         dist.barrier()
         tp.max_spins = 1 << 14
@@ -75,6 +90,14 @@ def _worker(rank, world, port, queue):
             tp.gemm_allreduce(x, w, None)
             torch.cuda.synchronize()
             result["timeout_code"] = int(tp.error.item())
+            tp.error.zero_()
+        dist.barrier()
+        if rank == 0:  # the fused kernel's per-tile wait runs out the same way
+            x = torch.randn(8, 64, device="cuda").bfloat16()
+            w = torch.randn(256, 64, device="cuda").bfloat16()
+            tp.fused_gemm_allreduce(x, w, None)
+            torch.cuda.synchronize()
+            result["fused_timeout_code"] = int(tp.error.item())
             tp.error.zero_()
         dist.barrier()
         tp.buffers.close()
@@ -105,4 +128,6 @@ def test_tensor_parallel_engine_two_gpus():
     for rank, item in results.items():
         assert "error" not in item, item["error"]
         assert min(item["cos"]) > 0.99, item["cos"]
+        assert max(item["fused_err"]) < 2e-2, item["fused_err"]
     assert results[0]["timeout_code"] == 1
+    assert results[0]["fused_timeout_code"] == 2
