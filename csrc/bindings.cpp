@@ -632,6 +632,64 @@ void decode_gemm(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> 
   check(pra_decode_gemm(a, stream()), "decode_gemm");
 }
 
+// Decode QKV projection with the rotary epilogue: one GEMM writes the rotated query rows, the
+// rotated keys and the values straight into their cache rows, and (columns >= v_end) the
+// routing query.
+void decode_qkv_rope(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias, torch::Tensor q_out,
+                     torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor cache_rows, torch::Tensor pos,
+                     torch::Tensor cos_t, torch::Tensor sin_t, int64_t head_dim, int64_t q_end, int64_t k_end,
+                     int64_t v_end, c10::optional<torch::Tensor> route_out) {
+  c10::cuda::CUDAGuard guard(x.device());
+  expect(x, at::kBFloat16, "x");
+  expect(w, at::kBFloat16, "w");
+  expect(q_out, at::kBFloat16, "q_out");
+  expect(k_cache, at::kBFloat16, "k_cache");
+  expect(v_cache, at::kBFloat16, "v_cache");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && w.is_contiguous() && w.size(1) == x.size(1), "x [M, K], w [N, K]");
+  TORCH_CHECK(cache_rows.scalar_type() == at::kInt && pos.scalar_type() == at::kInt &&
+                  cache_rows.numel() == x.size(0) && pos.numel() == x.size(0), "cache_rows / pos: int32 [M]");
+  TORCH_CHECK(cos_t.scalar_type() == at::kFloat && sin_t.scalar_type() == at::kFloat, "cos / sin tables: fp32");
+  TORCH_CHECK(k_cache.stride(-1) == 1 && v_cache.stride(-1) == 1 && k_cache.stride(0) == v_cache.stride(0),
+              "caches: row-major rows with one stride");
+  DecodeGemmArgs a{};
+  a.x = ptr<const __nv_bfloat16>(x);
+  a.ldx = x.stride(0);
+  a.w = ptr<const __nv_bfloat16>(w);
+  a.M = x.size(0);
+  a.N = w.size(0);
+  a.K = w.size(1);
+  a.bias = optr<__nv_bfloat16>(bias);
+  a.split_col = (int)v_end;
+  if (route_out.has_value()) {
+    expect(*route_out, at::kBFloat16, "route_out");
+    a.out2 = ptr<__nv_bfloat16>(*route_out);
+    a.ldo2 = route_out->stride(0);
+  }
+  a.pos = ptr<const int>(pos);
+  a.cos_t = ptr<const float>(cos_t);
+  a.sin_t = ptr<const float>(sin_t);
+  a.head_dim = (int)head_dim;
+  a.q_end = (int)q_end;
+  a.k_end = (int)k_end;
+  a.q_out = ptr<__nv_bfloat16>(q_out);
+  a.ldq = q_out.stride(0);
+  a.k_cache = ptr<__nv_bfloat16>(k_cache);
+  a.v_cache = ptr<__nv_bfloat16>(v_cache);
+  a.ld_cache = k_cache.stride(0);
+  a.cache_rows = ptr<const int>(cache_rows);
+  a.out = a.q_out;
+  a.ldo = a.ldq;
+  static int sm_cache[64] = {};
+  int& sms = sm_cache[x.device().index() & 63];
+  if (sms == 0) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, x.device().index());
+  const int tiles = (a.N + 127) / 128, nkb = a.K / 64;
+  a.splits = std::max(1, std::min(nkb / 8, sms / std::max(tiles, 1)));
+  a.workspace = ptr<float>(decode_gemm_state(x.device(), false));
+  a.counters = reinterpret_cast<uint32_t*>(decode_gemm_state(x.device(), true).data_ptr());
+  a.world = 1;
+  check(pra_decode_gemm(a, stream()), "decode_qkv_rope");
+}
+
 // ---------------------------------------------------------------- Llama-family ops
 // Rotary copy: rows of src (heads * head_dim, unit stride) to dst rows (dst_rows or identity).
 void rope_copy(torch::Tensor src, torch::Tensor dst, c10::optional<torch::Tensor> dst_rows,
@@ -1242,6 +1300,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_add", &embed_add);
   m.def("combine_partials", &combine_partials);
   m.def("decode_gemm", &decode_gemm);
+  m.def("decode_qkv_rope", &decode_qkv_rope);
   m.def("decode_gemm_max_tiles", []() { return (int64_t)DG_MAX_TILES; });
   m.def("plan_batch", &pra_plan_batch, "native cache-build planner (returns None when a batch needs the Python planner)");
   m.def("ipc_alloc", &ipc_alloc);

@@ -229,6 +229,43 @@ __global__ void __launch_bounds__(NT) decode_gemm_kernel(const __grid_constant__
   __syncthreads();
   constexpr int CHUNKS = MT * (BF / 8);  // 8 features per chunk
 
+  if (a.world <= 1 && a.pos != nullptr) {  // decode QKV: bias, rotary, scatter into q / caches / routing query
+    const int half = a.head_dim / 2;
+    for (int i = tid; i < CHUNKS; i += NT) {
+      const int m = i / (BF / 8), c = i % (BF / 8), n = n0 + c * 8;
+      if (m >= a.M || n >= a.N) continue;
+      float v[8];
+      staged8(tile_s + m * BF + c * 8, v);
+      float b[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (a.bias) load8(a.bias + n, b);
+      if (n < a.k_end) {  // query or key head: rotate pairs (i, i + half) of each head
+        const int p = a.pos[m];
+        float r[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int f = c * 8 + j, hi = (n + j) % a.head_dim;  // tile-local feature, index within its head
+          const bool first = hi < half;
+          const int partner = first ? f + half : f - half;
+          const float x = v[j] + b[j];
+          const float xp = tile_s[m * BF + partner] + (a.bias ? __bfloat162float(a.bias[n0 + partner]) : 0.f);
+          const int ii = first ? hi : hi - half;
+          const float cs = a.cos_t[(int64_t)p * half + ii], sn = a.sin_t[(int64_t)p * half + ii];
+          r[j] = first ? x * cs - xp * sn : x * cs + xp * sn;
+        }
+        __nv_bfloat16* dst = n < a.q_end ? a.q_out + (int64_t)m * a.ldq + n
+                                         : a.k_cache + (int64_t)a.cache_rows[m] * a.ld_cache + (n - a.q_end);
+        *reinterpret_cast<uint4*>(dst) = pack8(r);
+        continue;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] += b[j];
+      __nv_bfloat16* dst = n < a.split_col ? a.v_cache + (int64_t)a.cache_rows[m] * a.ld_cache + (n - a.k_end)
+                                           : a.out2 + (int64_t)m * a.ldo2 + (n - a.split_col);
+      *reinterpret_cast<uint4*>(dst) = pack8(v);
+    }
+    return;
+  }
+
   if (a.world <= 1) {
     for (int i = tid; i < CHUNKS; i += NT) {
       const int m = i / (BF / 8), c = i % (BF / 8), n = n0 + c * 8;
@@ -354,6 +391,10 @@ cudaError_t pra_decode_gemm(const DecodeGemmArgs& a, cudaStream_t st) {
   if (a.M <= 0 || a.N <= 0) return cudaSuccess;
   if (a.M > MT || a.K % BK || a.N % 8 || a.ldo % 8 || a.ldx % 8 || a.world > TP_MAX_RANKS) return cudaErrorInvalidValue;
   if (a.out2 && (a.split_col % 8 || a.ldo2 % 8)) return cudaErrorInvalidValue;
+  if (a.pos && (a.world > 1 || a.head_dim <= 0 || BF % a.head_dim || a.q_end % a.head_dim || a.k_end % a.head_dim ||
+                a.ldq % 8 || a.ld_cache % 8 || (a.split_col < a.N && a.out2 == nullptr) || !a.q_out || !a.k_cache ||
+                !a.v_cache || !a.cache_rows || !a.cos_t || !a.sin_t))
+    return cudaErrorInvalidValue;
   const int tiles = (a.N + BF - 1) / BF;
   if (tiles > DG_MAX_TILES) return cudaErrorInvalidValue;
   const int nkb = a.K / BK;

@@ -340,6 +340,20 @@ struct DecodeGemmArgs {
   uint32_t* epochs;                   // local per-tile call counters [DG_MAX_TILES]
   long long max_spins;
   int* error;                         // 1 + phase after a bounded wait gave up
+  // rotary decode-QKV epilogue (pos != null, world == 1): columns [0, q_end) are query heads
+  // (rotated into q_out), [q_end, k_end) key heads (rotated into k_cache row cache_rows[m]),
+  // [k_end, split_col) value heads (into v_cache row cache_rows[m]); columns >= split_col
+  // still go to out2.  Head boundaries are multiples of head_dim, which divides 128.
+  const int* pos;                     // [M] rotary position per row
+  const float* cos_t;                 // [max_pos, head_dim / 2]
+  const float* sin_t;
+  int head_dim, q_end, k_end;
+  __nv_bfloat16* q_out;
+  int64_t ldq;
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  int64_t ld_cache;
+  const int* cache_rows;              // [M]
 };
 size_t pra_decode_gemm_workspace_floats();
 cudaError_t pra_decode_gemm(const DecodeGemmArgs& a, cudaStream_t stream);

@@ -502,24 +502,24 @@ class PRALlamaEngine:
         max_keys = cfg.memory_tokens_per_row + self.max_len
         for li, lw in enumerate(self.w.layers):
             h = self._norm(x, lw.ln_in)
-            rq = None
-            if self._decode_rows(h):  # one GEMM: q, k, v and the full-width routing query
-                qkv = torch.empty((B, qd + 2 * kd), device=self.device, dtype=torch.bfloat16)
-                rq = torch.empty((B, self.route_dim), device=self.device, dtype=torch.bfloat16)
-                ext.decode_gemm(h, lw.qkv_route, lw.qkv_route_bias, None, qkv, rq, qd + 2 * kd, 0, [], [], 0, None,
-                                0, None)
-            else:
-                qkv = self._gemm(h, lw.qkv, lw.qkv_bias)
-            mem_args = (None, None, None, None)
-            if use_memory and cfg.is_pra_layer(li):
-                mem_idx, mem_len = self._route(li, qkv[:, :qd], B, route_query=rq)
-                mem_args = (self.memory.k(li), self.memory.v(li), mem_idx, mem_len)
             kc = self.cache[li, 0].view(B * self.max_len, kd)
             vc = self.cache[li, 1].view(B * self.max_len, kd)
-            ext.rope_copy(qkv[:, qd: qd + kd], kc, rows, pos, cos, sin, self.kv_heads, cfg.head_dim)
-            ext.rope_copy(qkv[:, qd + kd:], vc, rows, None, None, None, self.kv_heads, cfg.head_dim)
             q = torch.empty((B, qd), device=self.device, dtype=torch.bfloat16)
-            ext.rope_copy(qkv[:, :qd], q, None, pos, cos, sin, self.heads, cfg.head_dim)
+            rq = qkv = None
+            if self._decode_rows(h):
+                # one GEMM: rotated q, rotated k and v straight into their cache rows, routing query
+                rq = torch.empty((B, self.route_dim), device=self.device, dtype=torch.bfloat16)
+                ext.decode_qkv_rope(h, lw.qkv_route, lw.qkv_route_bias, q, kc, vc, rows, pos, cos, sin, cfg.head_dim,
+                                    qd, qd + kd, qd + 2 * kd, rq)
+            else:
+                qkv = self._gemm(h, lw.qkv, lw.qkv_bias)
+                ext.rope_copy(qkv[:, qd: qd + kd], kc, rows, pos, cos, sin, self.kv_heads, cfg.head_dim)
+                ext.rope_copy(qkv[:, qd + kd:], vc, rows, None, None, None, self.kv_heads, cfg.head_dim)
+                ext.rope_copy(qkv[:, :qd], q, None, pos, cos, sin, self.heads, cfg.head_dim)
+            mem_args = (None, None, None, None)
+            if use_memory and cfg.is_pra_layer(li):
+                mem_idx, mem_len = self._route(li, None if qkv is None else qkv[:, :qd], B, route_query=rq)
+                mem_args = (self.memory.k(li), self.memory.v(li), mem_idx, mem_len)
             a = ext.decode_attention(q, self.heads, self.kv_heads, cfg.head_dim, *mem_args, self.cache[li, 0],
                                      self.cache[li, 1], new_len, max_keys, self.split_keys, False)[0]
             x = self._row_parallel(a, lw.o, x)

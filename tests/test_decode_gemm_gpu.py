@@ -47,3 +47,41 @@ def test_two_outputs_and_strided_input(ext):
     scale = want.abs().max().item()
     assert (out.float() - want[:, :split]).abs().max().item() <= 2e-2 * scale
     assert (out2.float() - want[:, split:]).abs().max().item() <= 2e-2 * scale
+
+
+@pytest.mark.parametrize("head_dim,heads,kv_heads,bias", [(128, 4, 2, False), (64, 8, 4, True)])
+def test_rotary_qkv_epilogue_matches_gemm_then_rope(ext, head_dim, heads, kv_heads, bias):
+    """One decode GEMM writes rotated q, rotated k / plain v into their cache rows and the
+    routing-query columns, as the QKV GEMM followed by the rotary copies does."""
+    gen = torch.Generator(device="cuda").manual_seed(head_dim)
+    m, k = 24, 512
+    qd, kd, rd = heads * head_dim, kv_heads * head_dim, 256
+    n = qd + 2 * kd + rd
+    x = torch.randn(m, k, device="cuda", generator=gen).bfloat16()
+    w = (torch.randn(n, k, device="cuda", generator=gen) * 0.05).bfloat16()
+    b = torch.randn(n, device="cuda", generator=gen).bfloat16() if bias else None
+    half = head_dim // 2
+    inv = 1.0 / (10000.0 ** (torch.arange(half, dtype=torch.float64) / half))
+    ang = torch.arange(4096, dtype=torch.float64)[:, None] * inv[None]
+    cos, sin = ang.cos().float().cuda(), ang.sin().float().cuda()
+    pos = torch.randint(0, 4000, (m,), device="cuda", generator=gen, dtype=torch.int32)
+    rows = (torch.arange(m, device="cuda", dtype=torch.int32) * 7 + 3).int()
+    caches = [torch.zeros(m * 7 + 8, kd, device="cuda", dtype=torch.bfloat16) for _ in range(4)]
+    q_fused, q_ref = (torch.empty(m, qd, device="cuda", dtype=torch.bfloat16) for _ in range(2))
+    r_fused = torch.empty(m, rd, device="cuda", dtype=torch.bfloat16)
+    ext.decode_qkv_rope(x, w, b, q_fused, caches[0], caches[1], rows, pos, cos, sin, head_dim, qd, qd + kd,
+                        qd + 2 * kd, r_fused)
+    full = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    ext.gemm("tn", x, w, None, full, b, None, 1.0, 0.0, None)
+    ext.rope_copy(full[:, qd: qd + kd], caches[2], rows, pos, cos, sin, kv_heads, head_dim)
+    ext.rope_copy(full[:, qd + kd: qd + 2 * kd], caches[3], rows, None, None, None, kv_heads, head_dim)
+    ext.rope_copy(full[:, :qd], q_ref, None, pos, cos, sin, heads, head_dim)
+    torch.cuda.synchronize()
+
+    def close(a, r):
+        scale = r.float().abs().max().item() + 1e-6
+        return (a.float() - r.float()).abs().max().item() <= 2e-2 * scale
+
+    assert close(q_fused, q_ref)
+    assert close(caches[0], caches[2]) and close(caches[1], caches[3])
+    assert close(r_fused, full[:, qd + 2 * kd:])
