@@ -4,8 +4,9 @@ Same stage registry and sample construction as ``src/data/datasets.py:27-306``:
 a question row may restrict its references by ``reference_uris`` or
 ``reference_ids``; referenced documents with a ``reference_table`` carry the
 whole document map so recursive resolution can find children.  The stage
-generators here are this framework's own (``generators/``); WikiText-derived
-stages need the Hugging Face ``datasets`` package and network access.
+generators here are this framework's own (``generators/``,
+``native_kv_benchmarks``); WikiText, HotpotQA and QASPER stages read local
+copies of those corpora (no downloads).
 """
 
 from __future__ import annotations
@@ -160,19 +161,22 @@ GitHubRepositoryDataset = _stage_class("GitHubRepositoryDataset", "stage6_github
 WikiTextReferenceDataset = _stage_class("WikiTextReferenceDataset", "wikitext2_references",
                                         "generate_wikitext_reference_dataset", "WikiText parts as references.")
 WikiTextReferenceV2Dataset = _stage_class("WikiTextReferenceV2Dataset", "wikitext2_references_v2",
-                                          "generate_wikitext_reference_dataset", "Selection-labelled WikiText parts.")
+                                          "generate_wikitext_reference_dataset_v2", "Selection-labelled WikiText parts.")
 WikiTextNativeKVFixedTargetDataset = _stage_class("WikiTextNativeKVFixedTargetDataset",
                                                   "wikitext2_nativekv_fixed_target",
-                                                  "generate_wikitext_reference_dataset",
+                                                  "generate_wikitext_nativekv_fixed_target_dataset",
                                                   "WikiText history with a fixed tail and target.")
 SyntheticNativeKVFixedTargetDataset = _stage_class("SyntheticNativeKVFixedTargetDataset",
-                                                   "synthetic_nativekv_fixed_target", "generate_synthetic_native_kv",
+                                                   "synthetic_nativekv_fixed_target",
+                                                   "generate_synthetic_native_kv_dataset",
                                                    "Key/value retrieval with invariant target.")
 HotpotQANativeKVFixedTargetDataset = _stage_class("HotpotQANativeKVFixedTargetDataset",
-                                                  "hotpotqa_nativekv_fixed_target", "generate_wikitext_reference_dataset",
-                                                  "HotpotQA evidence (needs network).")
+                                                  "hotpotqa_nativekv_fixed_target",
+                                                  "generate_hotpotqa_native_kv_dataset",
+                                                  "Balanced HotpotQA yes/no evidence (local corpus file).")
 QASPERNativeKVFixedTargetDataset = _stage_class("QASPERNativeKVFixedTargetDataset", "qasper_nativekv_fixed_target",
-                                                "generate_wikitext_reference_dataset", "QASPER evidence (needs network).")
+                                                "generate_qasper_native_kv_dataset",
+                                                "QASPER evidence spans (local corpus archive).")
 # Synthetic benchmark stages of this framework.
 KeyValueQADataset = _stage_class("KeyValueQADataset", "synthetic_kv_qa", "generate_kv_qa",
                                  "Seeded uniform-random documents with embedded key:value pairs.")
@@ -195,11 +199,22 @@ def dataset_class_for_stage(stage: str):
         raise KeyError(f"Unknown dataset stage: {stage}") from None
 
 
-def load_wikitext_splits(dataset_name: str = "wikitext-2-raw-v1", *, cache_dir=None):
+def load_wikitext_splits(dataset_name: str = "wikitext-2-raw-v1", *, cache_dir=None, corpus_path=None):
+    """``{"train", "validation", "test"}`` rows of WikiText-2/103: from ``corpus_path`` (a
+    directory with the raw ``wiki.{train,valid,test}.raw`` files) or from the ``datasets``
+    package's cache.  Nothing is downloaded by this framework."""
     if dataset_name not in {"wikitext-2-raw-v1", "wikitext-103-raw-v1"}:
         raise ValueError(f"Unsupported WikiText dataset: {dataset_name}")
-    from datasets import load_dataset  # optional dependency
-
+    if corpus_path is not None:
+        root = Path(corpus_path)
+        names = {"train": "wiki.train.raw", "validation": "wiki.valid.raw", "test": "wiki.test.raw"}
+        return {split: [{"text": line} for line in (root / name).read_text(encoding="utf-8").splitlines()]
+                for split, name in names.items()}
+    try:
+        from datasets import load_dataset
+    except ImportError as exc:
+        raise RuntimeError("WikiText needs corpus_path= (local wiki.*.raw files) or the 'datasets' package "
+                           "with a cached copy") from exc
     return load_dataset("Salesforce/wikitext", dataset_name, cache_dir=str(cache_dir) if cache_dir else None)
 
 

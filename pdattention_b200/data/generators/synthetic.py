@@ -79,33 +79,3 @@ def generate_hierarchy(out_dir, n: int = 1, seed: int = 0) -> Path:
                           "answer": f"{minutes} minutes", "expected_ref_ids": [index],
                           "expected_anchors": ["Authentication"]})
     return _write_stage(out_dir, documents, references, questions)
-
-
-def generate_synthetic_native_kv(out_dir, n: int = 8, split_count: int = 4, seed: int = 0) -> Path:
-    """History split into ``split_count - 1`` references; the tail and target stay fixed."""
-    rng = random.Random(seed)
-    documents, references, questions = [], [], []
-    for example in range(n):
-        key, value = f"K{rng.randint(100, 999)}", f"V{rng.randint(100, 999)}"
-        history = [f"w{rng.randint(0, 50)}" for _ in range(48)]
-        history.insert(rng.randrange(len(history)), f"{key}:{value}")
-        parts = split_count - 1
-        cuts = [i * len(history) // parts for i in range(parts + 1)]
-        uris = []
-        for part in range(parts):
-            uri = f"synthetic://{example}/history-{part + 1}-of-{parts}"
-            uris.append(uri)
-            documents.append({"id": f"s{example}-{part}", "uri": uri, "text": " ".join(history[cuts[part]:cuts[part + 1]])})
-            references.append({"id": len(references) + 1, "token": f"<REF_{len(references) + 1}>", "uri": uri})
-        questions.append({"id": f"snkv-{example}", "prompt": f"value of {key}?", "answer": value,
-                          "reference_uris": uris, "expected_ref_ids": []})
-    return _write_stage(out_dir, documents, references, questions)
-
-
-def generate_wikitext_reference_dataset(*args, **kwargs):
-    """WikiText-derived stages need the Hugging Face ``datasets`` package and network access."""
-    try:
-        import datasets  # noqa: F401
-    except ImportError as exc:
-        raise RuntimeError("WikiText stages require the 'datasets' package and network access.") from exc
-    raise RuntimeError("WikiText stages require network access to download the corpus.")
