@@ -3,7 +3,10 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include <cmath>
+#include <cstdio>
 #include <cstring>
 #include <map>
 #include <vector>
@@ -729,6 +732,42 @@ void silu_mul(torch::Tensor gate_up, torch::Tensor out) {
 // Split-K decode attention.  q [B, H*Dh]; memory pool k/v views [rows, >= Hkv*Dh] (row stride
 // shared); local caches [B, max_len, Hkv*Dh] views.  Returns {out [B, H*Dh]} and, with
 // export_partials, also the merged unnormalised (out, (max, sum)) fp32 partials.
+// ---------------------------------------------------------------- bounds-checked variants
+// set_bounds_check(true) makes the gather and routing launches below run their checked
+// variants: the first out-of-range index is recorded in a per-device BoundsStatus and the
+// access is skipped.  Enable it before capturing a CUDA graph (the status word is allocated on
+// the first checked launch of each device).
+static bool g_bounds_check = false;
+static std::map<int, torch::Tensor> g_bounds_words;
+
+static BoundsStatus* bounds_word(const torch::Device& dev) {
+  if (!g_bounds_check) return nullptr;
+  auto it = g_bounds_words.find(dev.index());
+  if (it == g_bounds_words.end()) {
+    auto t = torch::zeros({(int64_t)sizeof(BoundsStatus)}, torch::dtype(torch::kUInt8).device(dev));
+    it = g_bounds_words.emplace(dev.index(), t).first;
+  }
+  return reinterpret_cast<BoundsStatus*>(it->second.data_ptr());
+}
+
+void set_bounds_check(bool on) { g_bounds_check = on; }
+bool bounds_check_enabled() { return g_bounds_check; }
+
+// {code, kernel check id, offending value, bound} of the first violation on `device` (zeros: clean).
+std::vector<int64_t> bounds_status(int64_t device) {
+  auto it = g_bounds_words.find((int)device);
+  if (it == g_bounds_words.end()) return {0, 0, 0, 0};
+  BoundsStatus h{};
+  auto host = it->second.cpu();
+  std::memcpy(&h, host.data_ptr(), sizeof h);
+  return {h.code, h.kernel, h.index, h.limit};
+}
+
+void bounds_reset(int64_t device) {
+  auto it = g_bounds_words.find((int)device);
+  if (it != g_bounds_words.end()) it->second.zero_();
+}
+
 std::vector<torch::Tensor> decode_attention(torch::Tensor q, int64_t heads, int64_t kv_heads, int64_t head_dim,
                                             c10::optional<torch::Tensor> mem_k, c10::optional<torch::Tensor> mem_v,
                                             c10::optional<torch::Tensor> mem_idx,
@@ -754,6 +793,7 @@ std::vector<torch::Tensor> decode_attention(torch::Tensor q, int64_t heads, int6
     p.mem_idx = ptr<const int>(*mem_idx);
     p.mem_max = mem_idx->size(1);
     p.mem_len = ptr<const int>(*mem_len);
+    p.mem_rows = mem_k->size(0);
   }
   if (loc_k.has_value() && loc_k->numel() > 0) {
     TORCH_CHECK(loc_k->dim() == 3 && loc_k->stride(2) == 1 && loc_v->strides() == loc_k->strides(),
@@ -764,7 +804,9 @@ std::vector<torch::Tensor> decode_attention(torch::Tensor q, int64_t heads, int6
     p.loc_batch = loc_k->stride(0);
     p.loc_row = loc_k->stride(1);
     p.loc_len = ptr<const int>(*loc_len);
+    p.loc_cap = loc_k->size(1);
   }
+  p.bounds = bounds_word(q.device());
   p.scale = 1.0f / std::sqrt((float)head_dim);
   p.split_keys = split_keys;
   p.n_split = std::max<int64_t>(1, (max_keys + split_keys - 1) / split_keys);
@@ -794,7 +836,7 @@ std::vector<torch::Tensor> route_topk(torch::Tensor scores, torch::Tensor query,
                                       torch::Tensor ns_start, torch::Tensor ns_end, torch::Tensor chunk_len,
                                       torch::Tensor chunk_row0, int64_t k, int64_t k_cand, int64_t budget,
                                       int64_t mem_max, bool local, int64_t id_offset, int64_t gists_per_chunk,
-                                      int64_t segments) {
+                                      int64_t segments, int64_t pool_rows) {
   c10::cuda::CUDAGuard guard(scores.device());
   expect(scores, at::kFloat, "scores");
   expect(query, at::kFloat, "query");
@@ -819,6 +861,9 @@ std::vector<torch::Tensor> route_topk(torch::Tensor scores, torch::Tensor query,
   a.k = k;
   a.k_cand = k_cand;
   a.budget = budget;
+  a.n_chunks = scores.size(1) / std::max<int64_t>(gists_per_chunk, 1);
+  a.pool_rows = pool_rows;
+  a.bounds = bounds_word(scores.device());
   auto io = scores.options().dtype(at::kInt);
   if (local) {  // best k per (row, segment) (exact scores, global ids) for a merge
     if (a.segments > 1) {
@@ -847,7 +892,7 @@ std::vector<torch::Tensor> route_topk(torch::Tensor scores, torch::Tensor query,
 // Merge per-rank candidates ([B, world * 2k]: per rank k scores then k ids as int bits).
 std::vector<torch::Tensor> route_merge(torch::Tensor cands, int64_t world, int64_t k, int64_t budget,
                                        torch::Tensor chunk_len, torch::Tensor chunk_row0, int64_t mem_max,
-                                       bool local) {
+                                       bool local, int64_t pool_rows) {
   c10::cuda::CUDAGuard guard(cands.device());
   expect(cands, at::kFloat, "cands");
   TORCH_CHECK(cands.dim() == 2 && cands.stride(1) == 1 && cands.size(1) == world * 2 * k, "cands [B, world*2k]");
@@ -860,6 +905,9 @@ std::vector<torch::Tensor> route_merge(torch::Tensor cands, int64_t world, int64
   a.budget = budget;
   a.chunk_len = ptr<const int>(chunk_len);
   a.chunk_row0 = ptr<const int>(chunk_row0);
+  a.n_chunks = chunk_len.numel();
+  a.pool_rows = pool_rows;
+  a.bounds = bounds_word(cands.device());
   auto io = cands.options().dtype(at::kInt);
   if (local) {  // merged best k as candidates (for a further merge across GPUs)
     auto cs = torch::empty({a.B, std::max<int64_t>(k, 1)}, cands.options());
@@ -975,6 +1023,21 @@ void dp_allreduce(std::vector<int64_t> src, std::vector<int64_t> dst, std::vecto
 
 int64_t dp_signal_words(int64_t world) { return 2LL * pra_dp_allreduce_blocks() * world; }
 
+// One NVTX range per layer of the block-stack executors ("pra.layer 3 fwd"): a profiler's
+// timeline shows which layer each kernel belongs to.  Without an attached tool NVTX calls are
+// no-op stubs.
+struct LayerRange {
+  LayerRange(int64_t layer, const char* what) {
+    char name[48];
+    std::snprintf(name, sizeof name, "pra.layer %lld %s", (long long)layer, what);
+    nvtxRangePushA(name);
+  }
+  ~LayerRange() { nvtxRangePop(); }
+  LayerRange(const LayerRange&) = delete;
+  LayerRange& operator=(const LayerRange&) = delete;
+};
+
+
 // ---------------------------------------------------------------- native block-stack executor
 // Forward of a stack of pre-LN GPT blocks (LN -> QKV -> [route] -> attention -> O-proj + residual ->
 // LN -> up-GELU -> down + residual) driven entirely from C++: no Python, no autograd records,
@@ -1015,6 +1078,7 @@ std::vector<torch::Tensor> stack_forward(torch::Tensor x, int64_t B, int64_t T, 
   const double scale = 1.0 / std::sqrt((double)head_dim);
   std::vector<torch::Tensor> out{x};
   for (int64_t l = 0; l < L; ++l) {
+    LayerRange range(l, "fwd");
     const torch::Tensor* w = weights.data() + 12 * l;
     auto h = norm_fwd(x, w[0], w[1], eps, false)[0];
     torch::Tensor qkv = pool.has_value() ? pool->select(0, l).narrow(0, pool_row0, M)
@@ -1096,6 +1160,7 @@ std::vector<torch::Tensor> stack_train_forward(torch::Tensor x, int64_t B, int64
   std::vector<torch::Tensor> routing, saved;
   saved.reserve(L * kSavedPerLayer);
   for (int64_t l = 0; l < L; ++l) {
+    LayerRange range(l, "train fwd");
     const torch::Tensor* w = weights.data() + 12 * l;
     auto n1 = norm_fwd(x, w[0], w[1], eps, false);
     auto qkv = torch::empty({M, 3 * D}, x.options());
@@ -1220,6 +1285,7 @@ torch::Tensor stack_train_backward(torch::Tensor dy, int64_t B, int64_t T, std::
   const double scale = 1.0 / std::sqrt((double)head_dim);
   dy = dy.contiguous();
   for (int64_t l = L - 1; l >= 0; --l) {
+    LayerRange range(l, "bwd");
     const torch::Tensor* w = weights.data() + 12 * l;
     torch::Tensor* g = grads.data() + 12 * l;
     const torch::Tensor* s = saved.data() + kSavedPerLayer * l;
@@ -1295,8 +1361,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_signal_words", [](int64_t world) { return (int64_t)TP_MAX_BLOCKS * world; });
   m.def("silu_mul", &silu_mul);
   m.def("decode_attention", &decode_attention);
-  m.def("route_topk", &route_topk);
-  m.def("route_merge", &route_merge);
+  m.def("route_topk", &route_topk, py::arg("scores"), py::arg("query"), py::arg("gists"), py::arg("ns_start"),
+        py::arg("ns_end"), py::arg("chunk_len"), py::arg("chunk_row0"), py::arg("k"), py::arg("k_cand"),
+        py::arg("budget"), py::arg("mem_max"), py::arg("local"), py::arg("id_offset"), py::arg("gists_per_chunk"),
+        py::arg("segments"), py::arg("pool_rows") = -1);
+  m.def("route_merge", &route_merge, py::arg("cands"), py::arg("world"), py::arg("k"), py::arg("budget"),
+        py::arg("chunk_len"), py::arg("chunk_row0"), py::arg("mem_max"), py::arg("local"),
+        py::arg("pool_rows") = -1);
+  m.def("set_bounds_check", &set_bounds_check);
+  m.def("bounds_check_enabled", &bounds_check_enabled);
+  m.def("bounds_status", &bounds_status);
+  m.def("bounds_reset", &bounds_reset);
   m.def("embed_add", &embed_add);
   m.def("combine_partials", &combine_partials);
   m.def("decode_gemm", &decode_gemm);

@@ -139,6 +139,16 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
 }
 
+// Records the first bounds violation of a checked kernel (later ones keep the first record).
+__device__ __forceinline__ void bounds_fail(BoundsStatus* s, int kernel, long long index, long long limit) {
+  if (atomicCAS(&s->code, 0, 1) == 0) {
+    s->kernel = kernel;
+    s->index = index;
+    s->limit = limit;
+    __threadfence();
+  }
+}
+
 // Bounded spin on a 32-bit flag in global (or peer) memory.  Returns true when
 // `*flag >= expected` was observed before `max_spins` polls; the caller records
 // a timeout status otherwise.  Every cross-agent wait in this library uses it.

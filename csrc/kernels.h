@@ -212,6 +212,24 @@ struct RopeCopyArgs {
 cudaError_t pra_rope_copy(const RopeCopyArgs& args, cudaStream_t stream);
 cudaError_t pra_silu_mul(const __nv_bfloat16* gate_up, int64_t M, int F, __nv_bfloat16* out, cudaStream_t stream);
 
+// Bounds-checked kernel variants (``set_bounds_check(true)``): a checked kernel records the
+// first out-of-range index it meets here and skips that access (the key is masked, the row is
+// not written); it never traps.  Checks cost a compare per index, so they are opt-in.
+struct BoundsStatus {
+  int code;         // 0: clean, 1: a violation was recorded
+  int kernel;       // which check (PRA_BOUNDS_* below)
+  long long index;  // the offending value
+  long long limit;  // the bound it broke
+};
+enum : int {
+  PRA_BOUNDS_DECODE_MEM_LEN = 1,   // decode: memory length > the row list's capacity
+  PRA_BOUNDS_DECODE_LOC_LEN = 2,   // decode: local length > the cache's capacity
+  PRA_BOUNDS_DECODE_MEM_ROW = 3,   // decode: memory row id outside the pool
+  PRA_BOUNDS_ROUTE_NAMESPACE = 4,  // routing: namespace range outside the chunk table
+  PRA_BOUNDS_ROUTE_POOL_ROW = 5,   // routing: a selected chunk's rows run past the pool
+  PRA_BOUNDS_ROUTE_CHUNK = 6,      // routing merge: candidate chunk id outside the chunk table
+};
+
 struct DecodeAttnParams {
   const __nv_bfloat16* q;      // [B, H * Dh] post-rotary queries of the decoded tokens
   int64_t q_row;
@@ -234,6 +252,9 @@ struct DecodeAttnParams {
   int64_t out_row;
   float* export_o;             // [B, H, Dh] merged unnormalised output, or null
   float* export_ml;            // [B, H, 2] merged (max, sum), or null
+  int64_t mem_rows;            // rows of the memory pool (bounds-checked variant)
+  int loc_cap;                 // local cache capacity per row (bounds-checked variant)
+  BoundsStatus* bounds;        // non-null: run the bounds-checked variant
 };
 cudaError_t pra_decode_attention(const DecodeAttnParams& p, int head_dim, cudaStream_t stream);
 
@@ -259,6 +280,9 @@ struct RouteTopkArgs {
   int* cand_id;                // local mode: their chunk ids + id_offset (-1 pad)
   int id_offset;
   int segments, seg_len;       // > 1: each row's chunks are cut into slices of seg_len, one CTA each (local mode)
+  int n_chunks;                // chunks in the table (bounds-checked variant)
+  int64_t pool_rows;           // rows of the memory pool (bounds-checked variant)
+  BoundsStatus* bounds;        // non-null: run the bounds-checked variant
 };
 cudaError_t pra_route_topk(const RouteTopkArgs& args, cudaStream_t stream);
 
@@ -276,6 +300,9 @@ struct RouteMergeArgs {
   int* sel_out;                // [B, k] or null
   float* cand_score;           // local mode: [B, k] merged best candidates instead of rows (or null)
   int* cand_id;
+  int n_chunks;                // chunks in the table (bounds-checked variant)
+  int64_t pool_rows;           // rows of the memory pool (bounds-checked variant)
+  BoundsStatus* bounds;        // non-null: run the bounds-checked variant
 };
 cudaError_t pra_route_merge(const RouteMergeArgs& args, cudaStream_t stream);
 cudaError_t pra_combine_partials(const float* parts, int B, int world, int H, int D, __nv_bfloat16* out,

@@ -15,6 +15,8 @@
 //  * route_topk     exact top-k routing per row: radix-select of the candidates from
 //                   tensor-core scores, fp32 cosine rescoring of the candidates, ties by
 //                   chunk id, greedy token budget, and the memory row list in chunk order.
+#include <climits>
+
 #include "common.cuh"
 
 namespace pra {
@@ -69,7 +71,9 @@ struct DSmem {
   static constexpr int LD = D + 8;
 };
 
-template <int D>
+constexpr int kBadRow = INT_MIN;  // checked variant: a key whose row failed its bounds check
+
+template <int D, bool CHECK>
 __global__ void __launch_bounds__(DT) decode_kernel(DecodeAttnParams p) {
   constexpr int LD = DSmem<D>::LD;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -83,8 +87,19 @@ __global__ void __launch_bounds__(DT) decode_kernel(DecodeAttnParams p) {
   const int b = blockIdx.x / p.Hkv, kvh = blockIdx.x % p.Hkv;
   const int split = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int mem_len = p.mem_len ? p.mem_len[b] : 0;
-  const int total = mem_len + (p.loc_len ? p.loc_len[b] : 0);
+  int mem_len = p.mem_len ? p.mem_len[b] : 0;
+  int loc_len = p.loc_len ? p.loc_len[b] : 0;
+  if constexpr (CHECK) {  // lengths past their buffers: record, then clamp (the extra keys are skipped)
+    if (mem_len < 0 || mem_len > p.mem_max) {
+      if (threadIdx.x == 0) bounds_fail(p.bounds, PRA_BOUNDS_DECODE_MEM_LEN, mem_len, p.mem_max);
+      mem_len = max(0, min(mem_len, p.mem_max));
+    }
+    if (loc_len < 0 || (p.loc_k != nullptr && loc_len > p.loc_cap)) {
+      if (threadIdx.x == 0) bounds_fail(p.bounds, PRA_BOUNDS_DECODE_LOC_LEN, loc_len, p.loc_cap);
+      loc_len = max(0, min(loc_len, p.loc_cap));
+    }
+  }
+  const int total = mem_len + loc_len;
   const int k0 = split * p.split_keys, k1 = min(total, k0 + p.split_keys);
   const int64_t part = ((int64_t)b * p.H + kvh * G) * p.n_split + split;  // first head of the group
 
@@ -96,8 +111,16 @@ __global__ void __launch_bounds__(DT) decode_kernel(DecodeAttnParams p) {
     *reinterpret_cast<uint4*>(sq + r * LD + col) = v;
   }
   // key rows of this split, resolved once: memory keys -> pool row, local keys -> -(t + 1)
-  for (int j = k0 + threadIdx.x; j < k1; j += DT)
-    srow[j - k0] = j < mem_len ? p.mem_idx[(int64_t)b * p.mem_max + j] : -(j - mem_len + 1);
+  for (int j = k0 + threadIdx.x; j < k1; j += DT) {
+    int r = j < mem_len ? p.mem_idx[(int64_t)b * p.mem_max + j] : -(j - mem_len + 1);
+    if constexpr (CHECK) {
+      if (j < mem_len && (r < 0 || r >= p.mem_rows)) {
+        bounds_fail(p.bounds, PRA_BOUNDS_DECODE_MEM_ROW, r, p.mem_rows);
+        r = kBadRow;  // never loaded, scored -inf
+      }
+    }
+    srow[j - k0] = r;
+  }
   __syncthreads();
   auto key_addr = [&](int j, bool value) -> const __nv_bfloat16* {
     const int r = srow[j - k0];
@@ -108,7 +131,7 @@ __global__ void __launch_bounds__(DT) decode_kernel(DecodeAttnParams p) {
     for (int c = threadIdx.x; c < DBN * (D / 8); c += DT) {
       const int r = c / (D / 8), col = (c % (D / 8)) * 8;
       const int j = start + r;
-      const bool ok = j < k1;
+      const bool ok = j < k1 && (!CHECK || srow[j - k0] != kBadRow);
       cp_async16(sk + (buf * DBN + r) * LD + col, ok ? key_addr(j, false) + col : p.q, ok);
       cp_async16(sv + (buf * DBN + r) * LD + col, ok ? key_addr(j, true) + col : p.q, ok);
     }
@@ -153,7 +176,7 @@ __global__ void __launch_bounds__(DT) decode_kernel(DecodeAttnParams p) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int key = key_base + nb * 8 + (lane & 3) * 2 + (e & 1);
-        if (key >= k1) s[nb][e] = -INFINITY;
+        if (key >= k1 || (CHECK && srow[key - k0] == kBadRow)) s[nb][e] = -INFINITY;
         mx[e >> 1] = fmaxf(mx[e >> 1], s[nb][e]);
       }
 #pragma unroll
@@ -304,10 +327,12 @@ __device__ __forceinline__ int block_scan_int(int v, int* tmp, int* total) {
 // writes them in rank order (global ids = id + id_offset; -inf / -1 padding) and stops.
 // Otherwise applies the greedy token budget in rank order, sorts the kept chunks by id and
 // writes the selection and the memory row list (all threads of the CTA take part).
+template <bool CHECK>
 __device__ void finish_selection(const float* cscore, const int* cand, int nc, int b, int k_req, int budget,
                                  const int* chunk_len, const int* chunk_row0, int* mem_idx, int mem_max,
                                  int* mem_len, int* sel_out, float* cand_score, int* cand_id, int id_offset,
-                                 int* picked, int* sel_chunk, int* sel_off, int* n_sel) {
+                                 int* picked, int* sel_chunk, int* sel_off, int* n_sel, int64_t pool_rows,
+                                 BoundsStatus* bounds) {
   const int k = min(k_req, nc);
   for (int i = threadIdx.x; i < nc; i += blockDim.x) {
     int rank = 0;
@@ -366,11 +391,21 @@ __device__ void finish_selection(const float* cscore, const int* cand, int nc, i
   __syncthreads();
   for (int i = 0; i < *n_sel; ++i) {  // the memory row list, written by all threads
     const int c = sel_chunk[i], base = sel_off[i], len = sel_off[i + 1] - base;
-    for (int t = threadIdx.x; t < len; t += blockDim.x)
-      if (base + t < mem_max) mem_idx[(int64_t)b * mem_max + base + t] = chunk_row0[c] + t;
+    for (int t = threadIdx.x; t < len; t += blockDim.x) {
+      if (base + t >= mem_max) continue;
+      int row = chunk_row0[c] + t;
+      if constexpr (CHECK) {
+        if (pool_rows >= 0 && (int64_t)row >= pool_rows) {  // the chunk's rows run past the pool: record, mark the key bad
+          bounds_fail(bounds, PRA_BOUNDS_ROUTE_POOL_ROW, row, pool_rows);
+          row = -1;
+        }
+      }
+      mem_idx[(int64_t)b * mem_max + base + t] = row;
+    }
   }
 }
 
+template <bool CHECK>
 __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
   __shared__ uint32_t hist[256];
   __shared__ uint32_t prefix, prefix_mask;
@@ -390,8 +425,15 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
   const int b = blockIdx.x;
   const int qb = b / S, seg = b % S;
   const int seg0 = S > 1 ? seg * a.seg_len : 0;
-  const int c0 = S > 1 ? max(a.ns_start[qb], seg0) : a.ns_start[qb];
-  const int c1 = S > 1 ? min(a.ns_end[qb], seg0 + a.seg_len) : a.ns_end[qb];
+  int c0 = S > 1 ? max(a.ns_start[qb], seg0) : a.ns_start[qb];
+  int c1 = S > 1 ? min(a.ns_end[qb], seg0 + a.seg_len) : a.ns_end[qb];
+  if constexpr (CHECK) {  // namespace outside the chunk table: record, then clamp it into the table
+    if (c1 > c0 && (c0 < 0 || c1 > a.n_chunks)) {
+      if (threadIdx.x == 0) bounds_fail(a.bounds, PRA_BOUNDS_ROUTE_NAMESPACE, c0 < 0 ? c0 : c1, a.n_chunks);
+      c0 = max(c0, 0);
+      c1 = min(c1, a.n_chunks);
+    }
+  }
   const int n = max(c1 - c0, 0);
   const float* row = a.scores + (int64_t)qb * a.score_stride;
   const int G = a.G > 0 ? a.G : 1;
@@ -520,12 +562,14 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
   }
   __syncthreads();
   // 4. top-k by (-score, chunk id) (+ greedy budget, chunk order and the row list)
-  finish_selection(cscore, cand, nc, b, a.k, a.budget, a.chunk_len, a.chunk_row0, a.mem_idx, a.mem_max, a.mem_len,
-                   a.sel_out, a.cand_score, a.cand_id, a.id_offset, picked, sel_chunk, sel_off, &n_sel);
+  finish_selection<CHECK>(cscore, cand, nc, b, a.k, a.budget, a.chunk_len, a.chunk_row0, a.mem_idx, a.mem_max,
+                          a.mem_len, a.sel_out, a.cand_score, a.cand_id, a.id_offset, picked, sel_chunk, sel_off,
+                          &n_sel, a.pool_rows, a.bounds);
 }
 
 // Cross-GPU merge of the per-rank candidates: row b holds world blocks of [k scores | k ids
 // (int bits)] (rank-major, as the column all-gather leaves them).
+template <bool CHECK>
 __global__ void __launch_bounds__(256) route_merge_kernel(RouteMergeArgs a) {
   __shared__ int cand[MAX_CAND];
   __shared__ float cscore[MAX_CAND];
@@ -541,6 +585,10 @@ __global__ void __launch_bounds__(256) route_merge_kernel(RouteMergeArgs a) {
     const int r = i / a.k, j = i % a.k;
     const float sc = row[r * 2 * a.k + j];
     const int id = __float_as_int(row[r * 2 * a.k + a.k + j]);
+    if (CHECK && id >= a.n_chunks) {  // a rank sent a chunk id outside the table: record, drop it
+      bounds_fail(a.bounds, PRA_BOUNDS_ROUTE_CHUNK, id, a.n_chunks);
+      continue;
+    }
     if (id >= 0) {
       const int slot = atomicAdd(&nc_s, 1);
       if (slot < MAX_CAND) {
@@ -551,8 +599,9 @@ __global__ void __launch_bounds__(256) route_merge_kernel(RouteMergeArgs a) {
   }
   __syncthreads();
   const int nc = min(nc_s, MAX_CAND);
-  finish_selection(cscore, cand, nc, b, a.k, a.budget, a.chunk_len, a.chunk_row0, a.mem_idx, a.mem_max, a.mem_len,
-                   a.sel_out, a.cand_score, a.cand_id, 0, picked, sel_chunk, sel_off, &n_sel);
+  finish_selection<CHECK>(cscore, cand, nc, b, a.k, a.budget, a.chunk_len, a.chunk_row0, a.mem_idx, a.mem_max,
+                          a.mem_len, a.sel_out, a.cand_score, a.cand_id, 0, picked, sel_chunk, sel_off, &n_sel,
+                          a.pool_rows, a.bounds);
 }
 
 // Combine per-rank attention partials: parts [B, world, H, D + 2] (unnormalised out, max,
@@ -608,8 +657,14 @@ static cudaError_t launch_decode(DecodeAttnParams p, cudaStream_t st) {
   static_assert(2 * DSTAGES * DBN * LD * sizeof(__nv_bfloat16) >= 4 * 16 * (D + 2) * sizeof(float),
                 "merge buffer must fit in the staging area");
   const size_t smem = (size_t)(16 + 2 * DSTAGES * DBN) * LD * sizeof(__nv_bfloat16) + (size_t)p.split_keys * sizeof(int);
-  PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(decode_kernel<D>), (int)smem));
-  decode_kernel<D><<<dim3(p.B * p.Hkv, p.n_split), DT, smem, st>>>(p);
+  const dim3 grid(p.B * p.Hkv, p.n_split);
+  if (p.bounds != nullptr) {
+    PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(decode_kernel<D, true>), (int)smem));
+    decode_kernel<D, true><<<grid, DT, smem, st>>>(p);
+  } else {
+    PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(decode_kernel<D, false>), (int)smem));
+    decode_kernel<D, false><<<grid, DT, smem, st>>>(p);
+  }
   PRA_RETURN_IF_ERROR(cudaGetLastError());
   decode_merge_kernel<<<p.B * p.H, 128, 0, st>>>(p, D);
   return cudaGetLastError();
@@ -636,7 +691,8 @@ cudaError_t pra_combine_partials(const float* parts, int B, int world, int H, in
 cudaError_t pra_route_merge(const RouteMergeArgs& a, cudaStream_t st) {
   if (a.B == 0) return cudaSuccess;
   if (a.k > 64 || a.world * a.k > pra::llama::MAX_CAND) return cudaErrorInvalidValue;
-  pra::llama::route_merge_kernel<<<a.B, 256, 0, st>>>(a);
+  if (a.bounds != nullptr) pra::llama::route_merge_kernel<true><<<a.B, 256, 0, st>>>(a);
+  else pra::llama::route_merge_kernel<false><<<a.B, 256, 0, st>>>(a);
   return cudaGetLastError();
 }
 
@@ -645,6 +701,7 @@ cudaError_t pra_route_topk(const RouteTopkArgs& a, cudaStream_t st) {
   if (a.k > 64 || a.k_cand > pra::llama::MAX_CAND) return cudaErrorInvalidValue;
   const int S = a.segments > 0 ? a.segments : 1;
   if (S > 1 && (a.cand_score == nullptr || a.seg_len <= 0)) return cudaErrorInvalidValue;  // segments need a merge
-  pra::llama::route_topk_kernel<<<a.B * S, pra::llama::RT, 0, st>>>(a);
+  if (a.bounds != nullptr) pra::llama::route_topk_kernel<true><<<a.B * S, pra::llama::RT, 0, st>>>(a);
+  else pra::llama::route_topk_kernel<false><<<a.B * S, pra::llama::RT, 0, st>>>(a);
   return cudaGetLastError();
 }

@@ -28,6 +28,7 @@ import torch
 
 from ..models.llama import PRALlamaConfig, PRALlamaReference
 from ..ops import _ext
+from ..tracing import traced
 from .routing import select_chunks
 
 # Decode projections on this library's decode GEMM (PRA_DECODE_GEMM=cutlass keeps the CUTLASS
@@ -307,7 +308,8 @@ class PRALlamaEngine:
             scores = torch.empty((rows, mem.C_pad), device=self.device, dtype=torch.float32)
             self.ext.gemm("tn_f32", rqn, mem.gn_bf16[layer], None, scores, None, None, 1.0, 0.0, None)
             mem_idx, mem_len, sel = select_chunks(self.ext, scores, rq, gn, start, end, mem.chunk_len,
-                                                  mem.chunk_row0, k, k_cand, budget, mem_max)
+                                                  mem.chunk_row0, k, k_cand, budget, mem_max,
+                                                  pool_rows=mem.pool.shape[1])
         else:
             # chunk-sharded routing: this rank scores its slice of the chunks, keeps its exact
             # local top-k, and the ranks' candidates are all-gathered and merged
@@ -320,7 +322,7 @@ class PRALlamaEngine:
             mem_idx, mem_len, sel = select_chunks(self.ext, scores, rq, gn[c0:c1], lo, hi, mem.chunk_len,
                                                   mem.chunk_row0, k, k_cand, budget, mem_max, id_offset=c0,
                                                   comm=self.tp, global_len=mem.chunk_len,
-                                                  global_row0=mem.chunk_row0)
+                                                  global_row0=mem.chunk_row0, pool_rows=mem.pool.shape[1])
         self.last_selection[layer] = sel
         return mem_idx, mem_len
 
@@ -332,6 +334,7 @@ class PRALlamaEngine:
 
     # -- memory build -----------------------------------------------------------------
     @torch.no_grad()
+    @traced("pra.llama.build_memory")
     def build_memory(self, chunks: torch.Tensor, lengths: torch.Tensor, batch_chunks: int = 256) -> ChunkMemory:
         """Encode ``chunks`` ``[C, Tc]`` (each its own sequence from position 0) into a
         ``ChunkMemory`` (for tensor parallelism: this rank's KV heads of every chunk)."""
@@ -391,6 +394,7 @@ class PRALlamaEngine:
         self.namespace = (start.to(self.device, torch.int32).contiguous(), end.to(self.device, torch.int32).contiguous())
 
     @torch.no_grad()
+    @traced("pra.llama.prefill")
     def prefill(self, ids: torch.Tensor, lengths: torch.Tensor, max_new_tokens: int,
                 row_batch: int | None = None, position_offset: torch.Tensor | None = None) -> torch.Tensor:
         """Left-aligned prompts ``ids`` ``[B, T]`` with ``lengths``: fills the local caches and
@@ -486,6 +490,7 @@ class PRALlamaEngine:
         return torch.where(score == top, ids, torch.full_like(ids, float("inf"))).min(dim=1).values.long()
 
     @torch.no_grad()
+    @traced("pra.llama.decode_step")
     def decode_step(self, token_ids: torch.Tensor, sample: bool = False) -> torch.Tensor:
         """One token per row at position ``cache_len[b]``; returns logits ``[B, V]``, or with
         ``sample=True`` the greedy next token ids ``[B]`` (no full-vocabulary logits are formed

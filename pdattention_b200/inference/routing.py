@@ -31,24 +31,26 @@ def segments_for(n_chunks: int, k: int) -> int:
 
 def select_chunks(ext, scores, query, gists, start, end, chunk_len, chunk_row0, k: int, k_cand: int, budget: int,
                   mem_max: int, *, gists_per_chunk: int = 1, id_offset: int = 0, comm=None,
-                  global_len=None, global_row0=None):
+                  global_len=None, global_row0=None, pool_rows: int = -1):
     """``(mem_idx, mem_len, selected ids)`` for every row.  ``scores`` ``[B, C_local * G]``;
     with ``comm`` the chunk ids are global (``id_offset`` = this rank's first chunk) and
-    ``global_len`` / ``global_row0`` describe every chunk (row0 < 0: held by another rank)."""
+    ``global_len`` / ``global_row0`` describe every chunk (row0 < 0: held by another rank).
+    ``pool_rows`` (the memory pool's row count) lets the bounds-checked kernels verify the row
+    lists they write."""
     G = gists_per_chunk
     n = scores.shape[1] // G
     S = segments_for(n, k)
     world = comm.world if comm is not None else 1
     if world == 1 and S == 1:
         return ext.route_topk(scores, query, gists, start, end, chunk_len, chunk_row0, k, k_cand, budget, mem_max,
-                              False, 0, G, 1)
+                              False, 0, G, 1, pool_rows)
     rows = query.shape[0]
     cs, ci = ext.route_topk(scores, query, gists, start, end, chunk_len, chunk_row0, k, k_cand, -1, 0, True,
                             id_offset, G, S)
     if S > 1:
         blocks = torch.cat([cs.view(rows, S, k), ci.view(torch.float32).view(rows, S, k)], dim=2).view(rows, -1)
         if world == 1:
-            return ext.route_merge(blocks, S, k, budget, chunk_len, chunk_row0, mem_max, False)
+            return ext.route_merge(blocks, S, k, budget, chunk_len, chunk_row0, mem_max, False, pool_rows)
         cs, ci = ext.route_merge(blocks, S, k, -1, chunk_len, chunk_row0, 0, True)
     merged = comm.all_gather_columns(torch.cat([cs, ci.view(torch.float32)], dim=1))
-    return ext.route_merge(merged, world, k, budget, global_len, global_row0, mem_max, False)
+    return ext.route_merge(merged, world, k, budget, global_len, global_row0, mem_max, False, pool_rows)

@@ -39,6 +39,7 @@ from ..memory.gists.strategies import local_generator
 from ..config import ResolverServiceConfig
 from ..memory.services import plan_cache_builds
 from ..ops import _ext
+from ..tracing import nvtx_range, traced
 from ..ops.kernels import MemoryView, WeightSlot, attention, layer_norm, linear, lm_head_loss, lm_head_logits, mlp
 from .native_plan import NativeBatchPlan, native_config
 from .tiny import PRATransformerBlock, TinyPRAModel
@@ -209,6 +210,7 @@ class FusedAdamW(torch.optim.Optimizer):
             s.fresh[0] = True
 
     @torch.no_grad()
+    @traced("pra.optimizer")
     def step(self, closure=None):
         ext = _ext.require()
         group = self.param_groups[0]
@@ -830,6 +832,7 @@ class DeviceRuntime:
                 except _Unsupported:
                     return
 
+    @traced("pra.cache_build")
     def build_memory(self, metadata_rows: list[dict], tokenizer, resolver_config=None):
         """Plan (or take the prefetched plan of) the batch, then encode all rows' chunks wave by wave."""
         self._last_tokenizer, self._last_resolver = tokenizer, resolver_config
@@ -918,6 +921,7 @@ class DeviceRuntime:
                              view("km_first"), self.kmeans_tables.idx, self.kmeans_tables.draws, view("km_off"), None)
 
     # -- prompt forward + loss ----------------------------------------------------
+    @traced("pra.prompt_forward")
     def prompt_forward(self, input_ids, attention_mask, memory: BatchMemory | None, position_offset=0):
         cfg = self.cfg
         b, t = input_ids.shape
@@ -950,6 +954,7 @@ class DeviceRuntime:
         x = self.run_blocks(x, b, t, valid, namespace, memory, budget=budget, query_rows=last)
         return layer_norm(x, self.ln_f)
 
+    @traced("pra.loss")
     def loss(self, hidden: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
         return lm_head_loss(hidden, self.head, labels.reshape(-1).contiguous(), self.cfg.vocab_size, 0)
 
@@ -1022,6 +1027,7 @@ class _TrainStack(torch.autograd.Function):
         return out[0]
 
     @staticmethod
+    @traced("pra.stack_backward")
     def backward(ctx, dy):
         rt = ctx.rt
         slots = [layer[name] for layer in rt.layers for name in ("ln1", "qkv", "o", "ln2", "up", "down")]
