@@ -995,18 +995,20 @@ void ipc_close(int64_t address, int64_t device) {
 
 // ---------------------------------------------------------------- data-parallel reduction
 // src/dst/sig: device addresses (ints) of every rank's gradient, output and signal buffers.
+// dst empty: the bf16 result goes back into every rank's src buffer (in place).
 void dp_allreduce(std::vector<int64_t> src, std::vector<int64_t> dst, std::vector<int64_t> sig, int64_t rank,
                   int64_t offset, int64_t count, double scale, int64_t epoch, int64_t max_spins,
                   torch::Tensor error, int64_t blocks) {
   const int world = src.size();
-  TORCH_CHECK(world >= 1 && world <= DP_MAX_RANKS && dst.size() == src.size() && sig.size() == src.size(),
+  const bool in_place = dst.empty();
+  TORCH_CHECK(world >= 1 && world <= DP_MAX_RANKS && (in_place || dst.size() == src.size()) && sig.size() == src.size(),
               "dp_allreduce needs one src/dst/sig address per rank (at most ", DP_MAX_RANKS, ")");
   TORCH_CHECK(error.scalar_type() == at::kInt && error.is_cuda(), "error must be an int32 CUDA tensor");
   c10::cuda::CUDAGuard guard(error.device());
   DpArgs a{};
   for (int p = 0; p < world; ++p) {
     a.src[p] = reinterpret_cast<const __nv_bfloat16*>(src[p]);
-    a.dst[p] = reinterpret_cast<float*>(dst[p]);
+    a.dst[p] = in_place ? nullptr : reinterpret_cast<float*>(dst[p]);
     a.sig[p] = reinterpret_cast<uint32_t*>(sig[p]);
   }
   a.rank = rank;
@@ -1018,6 +1020,7 @@ void dp_allreduce(std::vector<int64_t> src, std::vector<int64_t> dst, std::vecto
   a.max_spins = max_spins;
   a.error = ptr<int>(error);
   a.blocks = (int)blocks;
+  a.in_place_bf16 = in_place ? 1 : 0;
   check(pra_dp_allreduce(a, stream()), "dp_allreduce");
 }
 

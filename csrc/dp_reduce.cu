@@ -10,7 +10,11 @@
 //   2. reduce-scatter + all-gather in one pass: rank r owns the r-th slice of the
 //      range; for each 16-byte vector of its slice it loads the 8 bf16 values of every
 //      rank (ranks summed in a fixed order, so the result does not depend on the
-//      reducing rank), scales, and stores the fp32 vector into EVERY rank's output;
+//      reducing rank), scales, and stores the vector into EVERY rank's output: fp32 into
+//      dst, or (in_place_bf16) bf16 back into the gradient buffers themselves.  In place
+//      is race free: only the owner of a vector reads or writes it during the pass, and it
+//      loads every rank's value before it stores.  bf16 stores move 2 bytes per element
+//      and peer instead of 4;
 //   3. exit barrier: the same handshake again, so a rank's output is complete (and its
 //      gradient buffer no longer read) once its own launch has finished.
 // Each wait polls at most `max_spins` times; on a timeout the CTA records
@@ -65,6 +69,16 @@ __global__ void __launch_bounds__(NT) allreduce_kernel(DpArgs a) {
         acc[2 * i + 1] += f.y;
       }
     }
+    if (a.in_place_bf16) {
+      uint4 packed;
+      packed.x = pack_bf16(acc[0] * a.scale, acc[1] * a.scale);
+      packed.y = pack_bf16(acc[2] * a.scale, acc[3] * a.scale);
+      packed.z = pack_bf16(acc[4] * a.scale, acc[5] * a.scale);
+      packed.w = pack_bf16(acc[6] * a.scale, acc[7] * a.scale);
+      for (int p = 0; p < a.world; ++p)
+        reinterpret_cast<uint4*>(const_cast<__nv_bfloat16*>(a.src[p]))[base + v] = packed;
+      continue;
+    }
     const float4 lo = make_float4(acc[0] * a.scale, acc[1] * a.scale, acc[2] * a.scale, acc[3] * a.scale);
     const float4 hi = make_float4(acc[4] * a.scale, acc[5] * a.scale, acc[6] * a.scale, acc[7] * a.scale);
     for (int p = 0; p < a.world; ++p) {
@@ -79,14 +93,20 @@ __global__ void __launch_bounds__(NT) allreduce_kernel(DpArgs a) {
 }  // namespace dp
 }  // namespace pra
 
-int pra_dp_allreduce_blocks() { return 2 * 148; }
+int pra_dp_allreduce_blocks() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+    sms = 148;
+  return 2 * sms;
+}
 
 cudaError_t pra_dp_allreduce(const DpArgs& a, cudaStream_t st) {
   if (a.world < 1 || a.world > DP_MAX_RANKS || a.rank < 0 || a.rank >= a.world) return cudaErrorInvalidValue;
   if (a.offset % 8 != 0 || a.count % 8 != 0 || a.count < 0) return cudaErrorInvalidValue;
   for (int p = 0; p < a.world; ++p) {
-    if ((reinterpret_cast<uintptr_t>(a.src[p]) & 15) || (reinterpret_cast<uintptr_t>(a.dst[p]) & 15) ||
-        a.sig[p] == nullptr)
+    if ((reinterpret_cast<uintptr_t>(a.src[p]) & 15) || a.sig[p] == nullptr ||
+        (!a.in_place_bf16 && (a.dst[p] == nullptr || (reinterpret_cast<uintptr_t>(a.dst[p]) & 15))))
       return cudaErrorInvalidValue;
   }
   const int blocks = a.blocks > 0 && a.blocks < pra_dp_allreduce_blocks() ? a.blocks : pra_dp_allreduce_blocks();

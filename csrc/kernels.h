@@ -193,8 +193,10 @@ struct DpArgs {
   int* error;                              // local flag: 1 + phase of a timed-out wait
   int blocks;                              // CTAs of the launch (0: pra_dp_allreduce_blocks()); fewer
                                            // leave SMs to kernels that run concurrently (backward)
+  int in_place_bf16;                       // 1: store the bf16 result back into every rank's src buffer
+                                           // (dst unused): half the NVLink bytes of fp32 stores
 };
-int pra_dp_allreduce_blocks();
+int pra_dp_allreduce_blocks();  // 2 CTAs per SM of the current device
 cudaError_t pra_dp_allreduce(const DpArgs& args, cudaStream_t stream);
 
 // ---- Llama-family engine (llama.cu) ------------------------------------------------------

@@ -5,11 +5,15 @@ The reducer turns it into the fp32 *average* gradient the fused optimizer reads.
 
 * ``PeerGradientReducer`` (the default on CUDA): the gradient buffer lives in
   symmetric memory and a kernel (``pra_ops.dp_allreduce``) reads every rank's
-  bf16 slice over NVLink, sums in fp32, applies 1/world and stores the result
-  into every rank's fp32 buffer -- cast, scale, reduce-scatter and all-gather
-  fused, no staging copy and no NCCL call.  The reduction overlaps the backward:
-  each block's gradient range is reduced on a side stream as soon as the block's
-  backward has written it.
+  bf16 slice over NVLink, sums in fp32 (ranks in a fixed order), applies 1/world
+  and stores the average into every rank's buffer -- cast, scale,
+  reduce-scatter and all-gather fused, no staging copy and no NCCL call.  By
+  default the average is stored as bf16 back into the gradient buffers (2 bytes
+  per element and peer cross NVLink, as many as the gradients themselves);
+  ``PRA_DP_OUT=fp32`` stores an fp32 average into a separate buffer instead.
+  With ``PRA_DP_OVERLAP=1`` the reduction overlaps the backward: each block's
+  gradient range is reduced on a side stream as soon as the block's backward has
+  written it.
 * ``NcclGradientReducer`` (the baseline, ``PRA_DP_BACKEND=nccl``): fp32 copy +
   NCCL all-reduce buckets, with the 1/world scale applied by the optimizer.
 
@@ -85,7 +89,7 @@ class PeerGradientReducer:
     scale_in_optimizer = False
 
     def __init__(self, runtime, group=None, max_spins: int = 1 << 22, overlap: bool | None = None,
-                 overlap_blocks: int = 64):
+                 overlap_blocks: int = 64, out_dtype: str | None = None):
         from .peer import PeerBuffers
 
         ext = _ext.require()
@@ -97,12 +101,18 @@ class PeerGradientReducer:
             raise ValueError("the peer reducer spans one NVLink domain of at most 8 GPUs")
         n = flat.grad.numel()
         self.numel = n
-        self.buffers = PeerBuffers({"grad": (n, torch.bfloat16), "out": (n, torch.float32),
-                                    "signals": (int(ext.dp_signal_words(self.world)), torch.int32)},
-                                   group, flat.grad.device)
-        self.src, self.dst, self.sig = (self.buffers.addresses(k) for k in ("grad", "out", "signals"))
-        self.out = self.buffers.local("out")
+        out_dtype = (out_dtype or os.environ.get("PRA_DP_OUT", "bf16")).lower()
+        if out_dtype not in ("bf16", "fp32"):
+            raise ValueError(f"PRA_DP_OUT must be bf16 or fp32, not {out_dtype!r}")
+        self.in_place = out_dtype == "bf16"
+        spec = {"grad": (n, torch.bfloat16), "signals": (int(ext.dp_signal_words(self.world)), torch.int32)}
+        if not self.in_place:
+            spec["out"] = (n, torch.float32)
+        self.buffers = PeerBuffers(spec, group, flat.grad.device)
+        self.src, self.sig = self.buffers.addresses("grad"), self.buffers.addresses("signals")
+        self.dst = [] if self.in_place else self.buffers.addresses("out")  # [] = in place, bf16
         flat.rehome_grad(self.buffers.local("grad"), runtime.grad_views())
+        self.out = self.buffers.local("grad") if self.in_place else self.buffers.local("out")
         self.epoch = 0
         self.max_spins = int(max_spins)
         self.error = torch.zeros(1, dtype=torch.int32, device=flat.grad.device)
@@ -175,18 +185,19 @@ def _backend() -> str:
 
 
 def attach_data_parallel(model, optimizer, world_size: int, backend: str | None = None,
-                         overlap: bool | None = None):
+                         overlap: bool | None = None, out_dtype: str | None = None):
     """Route the fused optimizer through the averaged gradient (no-op for one rank).
 
     ``backend``: ``"peer"`` (fused symmetric-memory kernel) or ``"nccl"``; default
-    from ``PRA_DP_BACKEND`` (``peer``).
+    from ``PRA_DP_BACKEND`` (``peer``).  ``out_dtype`` (peer backend): ``"bf16"`` (average
+    written back in place, the default) or ``"fp32"`` (separate fp32 buffer).
     """
     if world_size <= 1:
         return None
     runtime = model._device_runtime
     backend = (backend or _backend()).lower()
     if backend == "peer":
-        reducer = PeerGradientReducer(runtime, overlap=overlap)
+        reducer = PeerGradientReducer(runtime, overlap=overlap, out_dtype=out_dtype)
     elif backend == "nccl":
         reducer = NcclGradientReducer(runtime.flat, world_size)
     else:

@@ -1,7 +1,9 @@
 """Fused peer-memory data-parallel gradient reduction on 2 GPUs (skipped with fewer).
 
 The ranks are child processes, one per GPU, with NVLS off; the kernel uses plain
-peer loads and stores.  The timeout case makes a rank skip one reduction so the
+peer loads and stores.  Both output modes run: the bf16 average written back in
+place into the gradient buffers (equal to the fp32 average of the same rank order
+rounded to bf16) and the fp32 average in a separate buffer.  The timeout case makes a rank skip one reduction so the
 peer's bounded wait runs out: the kernel must return with an error status that the
 host reads, and the context must stay usable.
 """
@@ -24,7 +26,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank: int, world: int, port: int, queue) -> None:
+def _worker(rank: int, world: int, port: int, queue, out_dtype: str = "bf16") -> None:
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
@@ -48,29 +50,30 @@ def _worker(rank: int, world: int, port: int, queue) -> None:
         model = prepare_model(tiny_config(tok.vocab_size), "cuda")  # the batch's ids fit the vocabulary
         rt = model._device_runtime
         opt = model.build_optimizer(TrainConfig(device="cuda", learning_rate=1e-3))
-        reducer = attach_data_parallel(model, opt, world, "peer", overlap=True)
+        reducer = attach_data_parallel(model, opt, world, "peer", overlap=True, out_dtype=out_dtype)
+        exact = (lambda t: t.bfloat16().float()) if out_dtype == "bf16" else (lambda t: t)  # noqa: E731
         grad = rt.flat.grad
         # the slot views now alias the peer-visible buffer
         gw = rt.layers[0]["qkv"].gw
         result["aliased"] = grad.data_ptr() <= gw.data_ptr() < grad.data_ptr() + grad.numel() * 2
         gen = torch.Generator(device="cuda").manual_seed(100 + rank)
         grad.copy_(torch.randn(grad.shape, generator=gen, device="cuda").bfloat16())
-        out = reducer.reduce()
-        torch.cuda.synchronize()
-        reducer.check()
         gathered = [torch.empty_like(grad) for _ in range(world)]
-        dist.all_gather(gathered, grad)
+        dist.all_gather(gathered, grad)  # before the reduction: in place it overwrites grad
         expected = gathered[0].float()
         for t in gathered[1:]:
             expected = expected + t.float()
         expected = expected * (1.0 / world)
-        result["max_err"] = float((out - expected).abs().max())
-        # a second reduction reuses the signal area (epochs increase)
-        grad.mul_(2)
         out = reducer.reduce()
         torch.cuda.synchronize()
         reducer.check()
-        result["max_err2"] = float((out - 2 * expected).abs().max())
+        result["max_err"] = float((out.float() - exact(expected)).abs().max())
+        # a second reduction reuses the signal area (epochs increase)
+        grad.copy_(2 * gathered[rank])
+        out = reducer.reduce()
+        torch.cuda.synchronize()
+        reducer.check()
+        result["max_err2"] = float((out.float() - exact(2 * expected)).abs().max())
         # one optimizer step through the reducer keeps the replicas identical
         opt.step()
         checksum = rt.flat.master.double().sum().reshape(1)
@@ -89,7 +92,7 @@ def _worker(rank: int, world: int, port: int, queue) -> None:
         out = reducer.reduce()
         torch.cuda.synchronize()
         reducer.check()
-        result["max_err3"] = float((out - expected).abs().max())
+        result["max_err3"] = float((out.float() - exact(expected)).abs().max())
         # a real step through the native training stack (the hooks fire during its backward)
         opt.zero_grad()
         loss, _ = _pra_batch_step(model, batch, "cuda", tok, ResolverServiceConfig(), None)
@@ -120,7 +123,8 @@ def _worker(rank: int, world: int, port: int, queue) -> None:
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_peer_gradient_allreduce_two_gpus():
+@pytest.mark.parametrize("out_dtype", ["bf16", "fp32"])
+def test_peer_gradient_allreduce_two_gpus(out_dtype):
     from pdattention_b200.ops import _ext
 
     if not _ext.available():
@@ -129,7 +133,7 @@ def test_peer_gradient_allreduce_two_gpus():
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, queue)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, queue, out_dtype)) for r in range(world)]
     for p in procs:
         p.start()
     results = {}
