@@ -19,6 +19,13 @@ Semantics (the reference's native-K/V PRA, restated for RoPE and GQA):
 * tensor parallelism (Megatron layout): QKV and gate/up split by output columns, O and
   down by input rows with an NCCL all-reduce of their partial outputs; each rank keeps
   its KV heads of every chunk, the routing-query slices are all-gathered with NCCL.
+
+Long prompts (``run_long_prompt``): the reference's prompt overflow
+(``src/pra_torch/prompt.py:125-231``): each row's tokens before its last
+``direct_window`` become 64-token chunks of its implicit ``#__head`` reference,
+which only that row routes over (a per-row namespace of chunk ids); the direct
+tail continues the head's positions when head + tail fit the native positions,
+otherwise it restarts at 0 (``historical`` mode, ``src/pra_torch/config.py:194-202``).
 """
 
 from __future__ import annotations
@@ -33,6 +40,8 @@ import torch.nn.functional as F
 
 LLAMA3_8B = dict(hidden=4096, heads=32, kv_heads=8, head_dim=128, inter=14336, layers=32, vocab=128256,
                  rope_theta=500000.0, eps=1e-5)
+MISTRAL_7B = dict(hidden=4096, heads=32, kv_heads=8, head_dim=128, inter=14336, layers=32, vocab=32768,
+                  rope_theta=1000000.0, eps=1e-5, max_positions=32768)
 
 
 class TorchPRALlama:
@@ -42,6 +51,8 @@ class TorchPRALlama:
         self.top_k, self.chunk_tokens = top_k, chunk_tokens
         d, dh = arch["hidden"], arch["head_dim"]
         self.h, self.hk = arch["heads"] // world, arch["kv_heads"] // world
+        self.ns = None            # optional (start, end) [B]: row b routes over chunks [start, end)
+        self.pos_offset = None    # optional [B] position of each row's first direct token
         self.qd, self.kd, self.f = self.h * dh, self.hk * dh, arch["inter"] // world
         gen = torch.Generator(device=self.device).manual_seed(seed + 1000 * rank)
 
@@ -128,6 +139,11 @@ class TorchPRALlama:
         rq = q_pre.float().unflatten(1, (self.hk, g)).mean(2).flatten(1)  # group mean [B, kd]
         rq = F.normalize(self._all_gather_cols(rq), dim=-1, eps=1e-12)
         scores = rq @ self.gists[li].t()
+        if self.ns is not None:  # each row only sees its own namespace of chunks
+            start, end = self.ns
+            start, end = start[self._rows], end[self._rows]
+            ids = torch.arange(scores.shape[1], device=self.device)
+            scores = scores.masked_fill((ids < start[:, None]) | (ids >= end[:, None]), float("-inf"))
         return scores.topk(self.top_k, dim=-1).indices
 
     def _memory_kv(self, li, chunk_ids):
@@ -147,10 +163,13 @@ class TorchPRALlama:
         self.cache_v = torch.zeros_like(self.cache_k)
         self.length = T
         out = []
-        pos = torch.arange(T, device=self.device)
+        offset = self.pos_offset if self.pos_offset is not None else torch.zeros(B, dtype=torch.long,
+                                                                                   device=self.device)
         for r0 in range(0, B, row_batch):
             ids = prompts[r0: r0 + row_batch].to(self.device)
             n = ids.shape[0]
+            self._rows = torch.arange(r0, r0 + n, device=self.device)
+            pos = offset[r0: r0 + n, None] + torch.arange(T, device=self.device)[None]
             x = self.embed[ids]
             for li, lw in enumerate(self.layers):
                 q, k, v = self._split_qkv(self._rms(x, lw["ln1"]) @ lw["qkv"].t())
@@ -176,7 +195,11 @@ class TorchPRALlama:
         """One token per row (all rows at the same length); returns the greedy next ids."""
         t = self.length
         x = self.embed[tok][:, None]
-        pos = torch.full((1,), t, device=self.device)
+        B = tok.shape[0]
+        self._rows = torch.arange(B, device=self.device)
+        offset = self.pos_offset if self.pos_offset is not None else torch.zeros(B, dtype=torch.long,
+                                                                                   device=self.device)
+        pos = (offset + t)[:, None]
         for li, lw in enumerate(self.layers):
             q, k, v = self._split_qkv(self._rms(x, lw["ln1"]) @ lw["qkv"].t())
             mk, mv = self._memory_kv(li, self._route(li, q[:, 0]))
@@ -251,3 +274,62 @@ def run(*, batch: int = 64, prompt_tokens: int = 4096, memory_tokens: int = 1 <<
             "prefill_tokens_per_s": batch * prompt_tokens / worst(prefill_s), "memory_tokens": memory_tokens,
             "tp": world, "batch": batch, "prompt_tokens": prompt_tokens, "top_k_chunks": top_k,
             "h2d_bytes_per_step": batch * 8, "d2h_bytes_per_step": batch * 8}
+
+
+def run_long_prompt(*, batch: int = 16, prompt_tokens: int = 131072, direct_window: int = 4096, top_k: int = 16,
+                    new_tokens: int = 256, seed: int = 0, arch: dict | None = None) -> dict:
+    """The long-prompt workload: ``batch`` prompts of ``prompt_tokens`` uniform-random ids; each
+    row's head (all but its last ``direct_window`` tokens) becomes its own 64-token chunks,
+    then the tails are prefilled and ``new_tokens`` greedy tokens decoded (device time with
+    CUDA events, max over ranks)."""
+    arch = arch or MISTRAL_7B
+    rank = dist.get_rank() if dist.is_initialized() else 0
+    world = dist.get_world_size() if dist.is_initialized() else 1
+    device = torch.device("cuda", torch.cuda.current_device())
+    model = TorchPRALlama(arch, device, rank, world, seed=seed, top_k=top_k)
+    gen = torch.Generator().manual_seed(seed + 1)
+    prompts = torch.randint(0, arch["vocab"], (batch, prompt_tokens), generator=gen)
+    head_len = max(0, prompt_tokens - direct_window)
+    if head_len % 64:
+        raise ValueError("this arm expects heads that are whole 64-token chunks")
+    per_row = head_len // 64
+    chunks = prompts[:, :head_len].reshape(batch * per_row, 64)
+    legal = head_len + direct_window <= arch.get("max_positions", 1 << 30)
+    model.ns = (torch.arange(batch, device=device) * per_row, (torch.arange(batch, device=device) + 1) * per_row)
+    model.pos_offset = torch.full((batch,), head_len if legal else 0, dtype=torch.long, device=device)
+
+    def timed(fn):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        out = fn()
+        e.record()
+        torch.cuda.synchronize()
+        return out, s.elapsed_time(e)
+
+    _, build_ms = timed(lambda: model.build_memory(chunks))
+    tok, prefill_ms = timed(lambda: model.prefill(prompts[:, head_len:], new_tokens + 1))
+    per_step = []
+    for _ in range(new_tokens - 1):
+        tok, ms = timed(lambda: model.decode_step(tok))
+        per_step.append(ms)
+
+    def worst(value: float) -> float:
+        if world == 1:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    per_step = [worst(v) for v in per_step]
+    build_ms, prefill_ms = worst(build_ms), worst(prefill_ms)
+    return {"decode_tokens_per_s": batch * len(per_step) / (sum(per_step) / 1000),
+            "tpot_p50_ms": statistics.median(per_step),
+            "prefill_tokens_per_s": batch * prompt_tokens / ((build_ms + prefill_ms) / 1000),
+            "head_build_tokens_per_s": batch * head_len / (build_ms / 1000),
+            "tail_prefill_tokens_per_s": batch * direct_window / (prefill_ms / 1000), "head_tokens": batch * head_len,
+            "batch": batch, "prompt_tokens": prompt_tokens, "direct_window": direct_window,
+            "new_tokens": new_tokens, "decode_steps": len(per_step), "tp": world,
+            "position_offset": int(model.pos_offset[0])}

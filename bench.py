@@ -157,7 +157,7 @@ def _gather(value: float, world: int) -> list[float]:
     return [float(x.item()) for x in out]
 
 
-def run(impl: str, steps: int, warmup: int, gpus: int) -> dict:
+def run(impl: str, steps: int, warmup: int, gpus: int, reference_autocast: bool = False) -> dict:
     rank, local, world = _env()
     if gpus != world:
         raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={world}")
@@ -176,7 +176,7 @@ def run(impl: str, steps: int, warmup: int, gpus: int) -> dict:
     tokenizer = WordIdTokenizer(VOCAB)
     _make_data(tmp, examples=max(PER_GPU_BATCH * world * 2, 32), seed=0, tokenizer=tokenizer)
     if impl == "reference":
-        step_fn, model_desc, counter = _reference_arm(tmp, tokenizer, rank, world)
+        step_fn, model_desc, counter = _reference_arm(tmp, tokenizer, rank, world, reference_autocast)
     else:
         step_fn, model_desc, counter = _pra_arm(tmp, tokenizer, rank, world)
     batches = step_fn.batches(total_steps)
@@ -228,7 +228,7 @@ def run(impl: str, steps: int, warmup: int, gpus: int) -> dict:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "bf16" if impl != "reference" else "fp32",
+        "dtype": "bf16" if impl != "reference" else ("bf16-autocast" if reference_autocast else "fp32"),
         "data": "synthetic (seeded uniform-random token ids, depth-2 recursive references), random-init weights",
         "config": {"model": model_desc, "global_batch": PER_GPU_BATCH * world, "seq_len": MODEL["max_seq_len"],
                    "direct_tokens_per_row": TREE["prompt_tokens"] + 1, "references_per_row": 16,
@@ -328,7 +328,10 @@ def _pra_arm(root: Path, tokenizer, rank: int, world: int):
             f"TinyGPT-PRA-{params / 1e6:.0f}M", launch_counter())
 
 
-def _reference_arm(root: Path, tokenizer, rank: int, world: int):
+def _reference_arm(root: Path, tokenizer, rank: int, world: int, autocast: bool = False):
+    """The unmodified reference: its data module, model, ``_pra_batch_step``, ``grad_norm`` and
+    stock AdamW.  ``autocast`` runs the same step under ``torch.autocast(bfloat16)`` (an optional
+    variant that separates the precision share of the gap from the engineering share)."""
     ref_root = REPO / "baseline" / "_ref"
     if not (ref_root / "pra_torch").exists():
         raise _Unavailable("reference not installed in baseline/_ref")
@@ -349,7 +352,8 @@ def _reference_arm(root: Path, tokenizer, rank: int, world: int):
 
     def step(batch, next_batch=None):
         optimizer.zero_grad(set_to_none=True)
-        loss, _ = ref_batch_step(model, batch, "cuda", tokenizer, resolver, cache)
+        with torch.autocast("cuda", dtype=torch.bfloat16, enabled=autocast):
+            loss, _ = ref_batch_step(model, batch, "cuda", tokenizer, resolver, cache)
         loss.backward()
         if world > 1:
             import torch.distributed as dist
@@ -368,7 +372,8 @@ def _reference_arm(root: Path, tokenizer, rank: int, world: int):
         return float(loss.detach().cpu()), _moved_bytes(batch), 4
 
     n = sum(p.numel() for p in model.parameters())
-    return _Step(step, lambda k: _batches(dm, rank, world, k)), f"TinyGPT-PRA-{n / 1e6:.0f}M (reference fp32)", None
+    precision = "bf16 autocast" if autocast else "fp32"
+    return _Step(step, lambda k: _batches(dm, rank, world, k)), f"TinyGPT-PRA-{n / 1e6:.0f}M (reference {precision})", None
 
 
 def run_decode(impl: str, steps: int, warmup: int, gpus: int, memory_tokens: int | None, batch: int) -> dict:
@@ -487,8 +492,7 @@ def run_long_prompt(impl: str, steps: int, gpus: int, prompt_tokens: int | None)
     """Mistral-7B-architecture PRA model, batch 16: 128K-token prompts whose latest 4,096 tokens stay
     direct and the rest become implicit-head chunks, then greedy decode (tensor parallel)."""
     if impl == "reference":
-        return {"impl": "reference", "unavailable": "the reference has no Llama/Mistral-family PRA model, no "
-                                                   "tensor parallelism and no device path for 7B long prompts"}
+        return _run_long_prompt_torch_arm(steps, gpus, prompt_tokens)
     rank, local, world = _env()
     torch.cuda.set_device(local)
     tp = None
@@ -520,6 +524,49 @@ def run_long_prompt(impl: str, steps: int, gpus: int, prompt_tokens: int | None)
     result["config"]["parallelism"] = f"tp{world}"
     if tp is not None:
         tp.close()
+        import torch.distributed as dist
+
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return result
+
+
+def _run_long_prompt_torch_arm(steps: int, gpus: int, prompt_tokens: int | None) -> dict:
+    """The long-prompt workload through ``baseline/torch_pra_decode.py`` (plain PyTorch + cuBLAS +
+    NCCL; the reference itself has no Mistral-family model or tensor parallelism)."""
+    rank, local, world = _env()
+    if gpus != world:
+        raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    sys.path.insert(0, str(REPO / "baseline"))
+    import torch_pra_decode
+
+    clocks = ClockSampler(local)
+    with clocks:
+        out = torch_pra_decode.run_long_prompt(prompt_tokens=prompt_tokens or (1 << 17 if world > 1 else 1 << 15),
+                                               new_tokens=max(steps, 16))
+    result = {"metric": "PRA long-prompt decode tokens/s (Mistral-7B architecture, implicit head)",
+              "value": out["decode_tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": out["decode_steps"],
+              "warmup": 0, "ms_per_step": out["tpot_p50_ms"], "higher_is_better": True, "scaling": "strong",
+              "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform-random prompt token ids), random-init weights",
+              "config": {"model": "mistral-7b", "batch": out["batch"], "prompt_tokens": out["prompt_tokens"],
+                         "direct_window": out["direct_window"], "head_tokens": out["head_tokens"],
+                         "new_tokens": out["new_tokens"], "position_offset": out["position_offset"],
+                         "parallelism": f"tp{world}"},
+              "prefill_tokens_per_s": out["prefill_tokens_per_s"],
+              "head_build_tokens_per_s": out["head_build_tokens_per_s"],
+              "tail_prefill_tokens_per_s": out["tail_prefill_tokens_per_s"], "clocks": clocks.summary(),
+              "gpu_launches": 0, "impl": "reference",
+              "reference_kind": "the reference's prompt-overflow semantics in plain PyTorch + cuBLAS + NCCL "
+                                "(baseline/torch_pra_decode.py); the reference itself has no Mistral-family or TP path"}
+    if world > 1:
         import torch.distributed as dist
 
         dist.barrier(device_ids=[local])
@@ -582,6 +629,8 @@ def main() -> None:
                         help="decode: total memory tokens (default 1M; 256K on one GPU, whose HBM cannot hold the "
                              "1M-token K/V of all 32 layers next to the weights and caches)")
     parser.add_argument("--batch", type=int, default=64)
+    parser.add_argument("--reference-autocast", action="store_true",
+                        help="train, --impl reference: run the reference's step under torch.autocast(bfloat16)")
     parser.add_argument("--prompt-tokens", type=int, default=None,
                         help="long-prompt: tokens per prompt (default 128K; 32K on one GPU)")
     args = parser.parse_args()
@@ -602,7 +651,7 @@ def main() -> None:
             print(json.dumps(result))
         return
     try:
-        result = run(args.impl, args.steps, max(args.warmup, 3), args.gpus)
+        result = run(args.impl, args.steps, max(args.warmup, 3), args.gpus, args.reference_autocast)
     except _Unavailable as exc:
         if rank == 0:
             print(json.dumps({"impl": "reference", "unavailable": str(exc)}))

@@ -30,3 +30,20 @@ def test_memory_routing_prefill_and_decode():
     rq = torch.nn.functional.normalize(q.float().unflatten(1, (2, 2)).mean(2).flatten(1), dim=-1)
     want = (rq @ model.gists[0].t()).topk(2).indices
     assert torch.equal(ids, want)
+
+
+def test_namespaces_and_position_offsets():
+    model = torch_pra_decode.TorchPRALlama(TINY, "cpu", top_k=2)
+    chunks = torch.randint(0, 97, (8, 64), generator=torch.Generator().manual_seed(2))
+    model.build_memory(chunks, batch=8)
+    model.ns = (torch.tensor([0, 4]), torch.tensor([4, 8]))  # row 0 owns chunks 0-3, row 1 chunks 4-7
+    model.pos_offset = torch.tensor([100, 0])
+    model._rows = torch.arange(2)
+    ids = model._route(1, torch.randn(2, 4, 16))
+    assert bool((ids[0] < 4).all()) and bool((ids[1] >= 4).all())
+    tok = model.prefill(torch.randint(0, 97, (2, 6), generator=torch.Generator().manual_seed(3)), max_new=3)
+    nxt = model.decode_step(tok)
+    assert nxt.shape == (2,) and model.length == 7
+    # row 0's cached keys were rotated at positions 100.., row 1's at 0..: the same token's key differs
+    k_row0, k_row1 = model.cache_k[0, 0, 0], model.cache_k[0, 1, 0]
+    assert k_row0.shape == k_row1.shape
