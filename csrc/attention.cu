@@ -138,6 +138,11 @@ __device__ __forceinline__ void load_keys(const Params& p, __nv_bfloat16* sk, __
   }
 }
 
+// Dropout element id of probability (b, h, query q, local key t): a flat index over [B, H, T, T].
+__device__ __forceinline__ uint64_t drop_elem(const Params& p, int b, int h, int q, int t) {
+  return (((uint64_t)b * p.H + h) * p.T + q) * p.T + t;
+}
+
 template <int D>
 __global__ void __launch_bounds__(NT) fwd_kernel(Params p) {
   constexpr int LD = Smem<D>::LD;
@@ -229,6 +234,18 @@ __global__ void __launch_bounds__(NT) fwd_kernel(Params p) {
     }
     l_run[0] += rs[0];
     l_run[1] += rs[1];
+    if (p.drop_thresh != 0) {  // the normaliser keeps every probability; P V uses the dropped ones
+#pragma unroll
+      for (int nb = 0; nb < 8; ++nb)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int q = row_a + (e >> 1) * 8;
+          const int t = kb.start + nb * 8 + (lane & 3) * 2 + (e & 1);
+          const bool keep = q < p.T && t < p.T &&
+                            dropout_keep(p.drop_seed, p.drop_offset, drop_elem(p, b, h, q, t), p.drop_thresh);
+          s[nb][e] = keep ? s[nb][e] * p.drop_scale : 0.f;
+        }
+    }
     mma_pb<D>(o_acc, s, sv + buf * BN * LD);
     __syncthreads();
   }
@@ -383,7 +400,13 @@ __global__ void __launch_bounds__(NT) bwd_dq_kernel(Params p) {
         const int key_off = nb * 8 + (lane & 3) * 2 + (e & 1);
         const bool vis = (unmasked || key_visible(p, kb, key_off, q, mem_len, valid)) && lse2[r] != -INFINITY;
         const float pr = vis ? exp2f(s[nb][e] * sl2 - lse2[r]) : 0.f;
-        s[nb][e] = pr * (dp[nb][e] - dlt[r]);  // dS (unscaled)
+        float dpv = dp[nb][e];
+        if (p.drop_thresh != 0) {  // dP of the dropped probabilities -> dP of the kept ones
+          const int t = kb.start + key_off;
+          const bool keep = vis && dropout_keep(p.drop_seed, p.drop_offset, drop_elem(p, b, h, q, t), p.drop_thresh);
+          dpv = keep ? dpv * p.drop_scale : 0.f;
+        }
+        s[nb][e] = pr * (dpv - dlt[r]);  // dS (unscaled)
       }
     }
     mma_pb<D>(dq, s, sk + buf * BN * LD);
@@ -498,8 +521,14 @@ __global__ void __launch_bounds__(NT) bwd_dkdv_kernel(Params p) {
         const float l2 = s_lse[buf * BM + qoff];
         const bool vis = key_ok[r] && q < p.T && key <= q && l2 != -INFINITY;
         const float pr = vis ? exp2f(st[nb][e] * sl2 - l2) : 0.f;
-        st[nb][e] = pr;                                        // P^T
-        dpt[nb][e] = pr * (dpt[nb][e] - s_dlt[buf * BM + qoff]);  // dS^T (unscaled)
+        float dpv = dpt[nb][e], pd = pr;
+        if (p.drop_thresh != 0) {  // dV takes the dropped P; dS the kept-scaled dP
+          const bool keep = vis && dropout_keep(p.drop_seed, p.drop_offset, drop_elem(p, b, h, q, key), p.drop_thresh);
+          dpv = keep ? dpv * p.drop_scale : 0.f;
+          pd = keep ? pr * p.drop_scale : 0.f;
+        }
+        st[nb][e] = pd;                                         // P^T (dropped)
+        dpt[nb][e] = pr * (dpv - s_dlt[buf * BM + qoff]);       // dS^T (unscaled)
       }
     }
     mma_pb<D>(dv, st, do_sm);
@@ -544,7 +573,8 @@ cudaError_t launch_bwd(const Params& p, cudaStream_t st) {
     PRA_RETURN_IF_ERROR(cudaGetLastError());
   }
   cudaError_t tc_dq = cudaErrorNotSupported;
-  if (pra_attention_get_impl() && p.T > 64) tc_dq = pra_attention_bwd_dq_tc(p, D, st);
+  const bool tc_ok = pra_attention_get_impl() && p.T > 64 && p.drop_thresh == 0;  // dropout: mma.sync kernels
+  if (tc_ok) tc_dq = pra_attention_bwd_dq_tc(p, D, st);
   if (tc_dq != cudaErrorNotSupported) {
     PRA_RETURN_IF_ERROR(tc_dq);
   } else {
@@ -554,7 +584,7 @@ cudaError_t launch_bwd(const Params& p, cudaStream_t st) {
     bwd_dq_kernel<D><<<grid, NT, smem, st>>>(p);
     PRA_RETURN_IF_ERROR(cudaGetLastError());
   }
-  if (pra_attention_get_impl() && p.T > 64) {
+  if (tc_ok) {
     const cudaError_t e = pra_attention_bwd_dkdv_tc(p, D, st);
     if (e != cudaErrorNotSupported) return e;
   }
@@ -580,7 +610,8 @@ cudaError_t pra_attention_fwd(const AttnParams& p, int head_dim, cudaStream_t st
   if (p.B * p.T == 0) return cudaSuccess;
   // tcgen05: 128-query tiles, or two sequences per tile for <= 64 tokens at head dim 64; other
   // short sequences keep the 64-query mma.sync tiles, which waste no rows there.
-  if (g_attn_tcgen05 && (p.T > 64 || head_dim == 64)) {
+  if (p.drop_thresh != 0 && (p.mem_len != nullptr || p.H != p.Hkv)) return cudaErrorInvalidValue;
+  if (g_attn_tcgen05 && (p.T > 64 || head_dim == 64) && p.drop_thresh == 0) {
     const cudaError_t e = pra_attention_fwd_tc(p, head_dim, st);
     if (e != cudaErrorNotSupported) return e;
   }

@@ -103,13 +103,25 @@ AttnParams attn_params(const torch::Tensor& q, const torch::Tensor& k, const tor
   return p;
 }
 
+// Attention-probability dropout (p > 0): element (b, h, q, t) of the stream (seed, offset).
+static void set_attention_dropout(AttnParams& p, double drop_p, int64_t seed, int64_t offset) {
+  p.drop_thresh = pra_dropout_threshold(drop_p);
+  p.drop_scale = drop_p > 0.0 ? (float)(1.0 / (1.0 - drop_p)) : 1.f;
+  p.drop_seed = (uint64_t)seed;
+  p.drop_offset = (uint64_t)offset;
+  TORCH_CHECK(p.drop_thresh == 0 || (p.mem_len == nullptr && p.H == p.Hkv),
+              "attention dropout applies to local multi-head attention only (no memory, no GQA)");
+}
+
 std::vector<torch::Tensor> attention_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, int64_t heads,
                                          int64_t kv_heads, int64_t head_dim, c10::optional<torch::Tensor> mem_k,
                                          c10::optional<torch::Tensor> mem_v, c10::optional<torch::Tensor> mem_idx,
                                          c10::optional<torch::Tensor> mem_len, c10::optional<torch::Tensor> key_valid,
-                                         double scale) {
+                                         double scale, double drop_p = 0.0, int64_t drop_seed = 0,
+                                         int64_t drop_offset = 0) {
   c10::cuda::CUDAGuard guard(q.device());
   auto p = attn_params(q, k, v, heads, kv_heads, mem_k, mem_v, mem_idx, mem_len, key_valid, scale);
+  set_attention_dropout(p, drop_p, drop_seed, drop_offset);
   auto out = torch::empty({p.B, p.T, heads * head_dim}, q.options());
   auto lse = torch::empty({p.B, heads, p.T}, q.options().dtype(at::kFloat));
   p.o = ptr<__nv_bfloat16>(out);
@@ -124,9 +136,11 @@ std::vector<torch::Tensor> attention_bwd(torch::Tensor dout, torch::Tensor q, to
                                          torch::Tensor out, torch::Tensor lse, int64_t heads, int64_t head_dim,
                                          c10::optional<torch::Tensor> mem_k, c10::optional<torch::Tensor> mem_v,
                                          c10::optional<torch::Tensor> mem_idx, c10::optional<torch::Tensor> mem_len,
-                                         c10::optional<torch::Tensor> key_valid, double scale) {
+                                         c10::optional<torch::Tensor> key_valid, double scale, double drop_p = 0.0,
+                                         int64_t drop_seed = 0, int64_t drop_offset = 0) {
   c10::cuda::CUDAGuard guard(q.device());
   auto p = attn_params(q, k, v, heads, heads, mem_k, mem_v, mem_idx, mem_len, key_valid, scale);
+  set_attention_dropout(p, drop_p, drop_seed, drop_offset);
   expect(dout, at::kBFloat16, "dout");
   TORCH_CHECK(dout.stride(2) == 1 && out.stride(2) == 1, "dout/out feature dim must be contiguous");
   p.o = ptr<__nv_bfloat16>(out);
@@ -148,6 +162,35 @@ std::vector<torch::Tensor> attention_bwd(torch::Tensor dout, torch::Tensor q, to
   p.dq_batch = p.dk_batch = p.dv_batch = dqkv.stride(0);
   check(pra_attention_bwd(p, (int)head_dim, stream()), "attention_bwd");
   return {dqkv};
+}
+
+// ---------------------------------------------------------------- dropout
+// out = keep ? x / (1 - p) : 0 over the flat element order of x (out may alias x).
+void dropout(torch::Tensor x, torch::Tensor out, double drop_p, int64_t seed, int64_t offset) {
+  c10::cuda::CUDAGuard guard(x.device());
+  expect(x, at::kBFloat16, "x");
+  expect(out, at::kBFloat16, "out");
+  TORCH_CHECK(x.is_contiguous() && out.is_contiguous() && x.numel() == out.numel(), "dropout: contiguous, same size");
+  TORCH_CHECK(drop_p >= 0.0 && drop_p < 1.0, "dropout probability must be in [0, 1)");
+  check(pra_dropout(ptr<const __nv_bfloat16>(x), ptr<__nv_bfloat16>(out), x.numel(), pra_dropout_threshold(drop_p),
+                    (float)(1.0 / (1.0 - drop_p)), (uint64_t)seed, (uint64_t)offset, stream()),
+        "dropout");
+}
+
+// out = res + (keep ? x / (1 - p) : 0) (out may alias res or x).
+void dropout_add(torch::Tensor res, torch::Tensor x, torch::Tensor out, double drop_p, int64_t seed, int64_t offset) {
+  c10::cuda::CUDAGuard guard(x.device());
+  expect(res, at::kBFloat16, "res");
+  expect(x, at::kBFloat16, "x");
+  expect(out, at::kBFloat16, "out");
+  TORCH_CHECK(res.is_contiguous() && x.is_contiguous() && out.is_contiguous() && x.numel() == out.numel() &&
+                  res.numel() == x.numel(),
+              "dropout_add: contiguous, same size");
+  TORCH_CHECK(drop_p >= 0.0 && drop_p < 1.0, "dropout probability must be in [0, 1)");
+  check(pra_dropout_add(ptr<const __nv_bfloat16>(res), ptr<const __nv_bfloat16>(x), ptr<__nv_bfloat16>(out),
+                        x.numel(), pra_dropout_threshold(drop_p), (float)(1.0 / (1.0 - drop_p)), (uint64_t)seed,
+                        (uint64_t)offset, stream()),
+        "dropout_add");
 }
 
 // ---------------------------------------------------------------- GEMM
@@ -1334,14 +1377,22 @@ torch::Tensor stack_train_backward(torch::Tensor dy, int64_t B, int64_t T, std::
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "PRA sm_100a kernels";
-  m.def("attention_fwd", &attention_fwd);
+  m.def("attention_fwd", &attention_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("heads"),
+        py::arg("kv_heads"), py::arg("head_dim"), py::arg("mem_k"), py::arg("mem_v"), py::arg("mem_idx"),
+        py::arg("mem_len"), py::arg("key_valid"), py::arg("scale"), py::arg("drop_p") = 0.0,
+        py::arg("drop_seed") = 0, py::arg("drop_offset") = 0);
+  m.def("dropout", &dropout);
+  m.def("dropout_add", &dropout_add);
   m.def("attention_status", [](int64_t device) { return attention_status_buffer(torch::Device(torch::kCUDA, device)); });
   m.def("set_attention_impl", [](const std::string& impl) {
     TORCH_CHECK(impl == "tcgen05" || impl == "mma", "attention impl must be 'tcgen05' or 'mma'");
     pra_attention_set_impl(impl == "tcgen05" ? 1 : 0);
   });
   m.def("attention_impl", []() { return std::string(pra_attention_get_impl() ? "tcgen05" : "mma"); });
-  m.def("attention_bwd", &attention_bwd);
+  m.def("attention_bwd", &attention_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"),
+        py::arg("out"), py::arg("lse"), py::arg("heads"), py::arg("head_dim"), py::arg("mem_k"), py::arg("mem_v"),
+        py::arg("mem_idx"), py::arg("mem_len"), py::arg("key_valid"), py::arg("scale"), py::arg("drop_p") = 0.0,
+        py::arg("drop_seed") = 0, py::arg("drop_offset") = 0);
   m.def("gemm", &gemm);
   m.def("norm_fwd", &norm_fwd);
   m.def("norm_bwd", &norm_bwd);

@@ -139,6 +139,34 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
 }
 
+// Philox4x32-10 (Salmon, Moraes, Dror, Shaw: "Parallel Random Numbers: As Easy as 1, 2, 3",
+// SC 2011): ten rounds of two 32x32->64-bit products mixed into the counter, the key bumped
+// by the Weyl constants between rounds.
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1) {
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t hi0 = __umulhi(0xD2511F53u, c.x), lo0 = 0xD2511F53u * c.x;
+    const uint32_t hi1 = __umulhi(0xCD9E8D57u, c.z), lo1 = 0xCD9E8D57u * c.z;
+    c = make_uint4(hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0);
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  return c;
+}
+
+// The 4 Philox words of block `blk` of the dropout stream (seed, offset).
+__device__ __forceinline__ uint4 dropout_block(uint64_t seed, uint64_t offset, uint64_t blk) {
+  return philox4x32_10(make_uint4((uint32_t)blk, (uint32_t)(blk >> 32), (uint32_t)offset, (uint32_t)(offset >> 32)),
+                       (uint32_t)seed, (uint32_t)(seed >> 32));
+}
+
+// Keep decision of element e of the stream (seed, offset).
+__device__ __forceinline__ bool dropout_keep(uint64_t seed, uint64_t offset, uint64_t e, uint32_t thresh) {
+  const uint4 r = dropout_block(seed, offset, e >> 2);
+  const uint32_t w = (e & 3) == 0 ? r.x : (e & 3) == 1 ? r.y : (e & 3) == 2 ? r.z : r.w;
+  return (w >> 8) >= thresh;
+}
+
 // Records the first bounds violation of a checked kernel (later ones keep the first record).
 __device__ __forceinline__ void bounds_fail(BoundsStatus* s, int kernel, long long index, long long limit) {
   if (atomicCAS(&s->code, 0, 1) == 0) {

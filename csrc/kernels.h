@@ -29,9 +29,28 @@ struct AttnParams {
   __nv_bfloat16* dv;
   int64_t dq_row, dq_batch, dk_row, dk_batch, dv_row, dv_batch;
   int* status;                 // optional: set to 1 by a kernel that gave up on a bounded wait
+  // Dropout on the attention probabilities (local keys only, no memory): element (b, h, q, t)
+  // is kept when its Philox word passes drop_thresh (see pra_dropout); kept values are scaled
+  // by drop_scale.  drop_thresh == 0: no dropout.
+  uint32_t drop_thresh;
+  float drop_scale;
+  uint64_t drop_seed, drop_offset;
 };
 
 cudaError_t pra_attention_fwd(const AttnParams& p, int head_dim, cudaStream_t stream);
+
+// ---- dropout (dropout.cu) --------------------------------------------------------------
+// Counter-based dropout: element e of the stream (seed, offset) draws word e % 4 of the
+// Philox4x32-10 block (e / 4, offset) under key seed; it is kept when (word >> 8) >= thresh
+// (thresh = round(p * 2^24)) and then scaled by 1 / (1 - p).  The backward regenerates the
+// same mask from (seed, offset), so nothing is stored.
+uint32_t pra_dropout_threshold(double p);
+// y = keep ? x * scale : 0 (y may alias x).
+cudaError_t pra_dropout(const __nv_bfloat16* x, __nv_bfloat16* y, int64_t n, uint32_t thresh, float scale,
+                        uint64_t seed, uint64_t offset, cudaStream_t stream);
+// y = res + (keep ? x * scale : 0) (y may alias res or x).
+cudaError_t pra_dropout_add(const __nv_bfloat16* res, const __nv_bfloat16* x, __nv_bfloat16* y, int64_t n,
+                            uint32_t thresh, float scale, uint64_t seed, uint64_t offset, cudaStream_t stream);
 // tcgen05 forward (head dims 64/128, 16-byte aligned rows); cudaErrorNotSupported otherwise.
 cudaError_t pra_attention_fwd_tc(const AttnParams& p, int head_dim, cudaStream_t stream);
 // dQ of the backward on tcgen05 (head dim 64); cudaErrorNotSupported otherwise.

@@ -40,7 +40,8 @@ from ..config import ResolverServiceConfig
 from ..memory.services import plan_cache_builds
 from ..ops import _ext
 from ..tracing import nvtx_range, traced
-from ..ops.kernels import MemoryView, WeightSlot, attention, layer_norm, linear, lm_head_loss, lm_head_logits, mlp
+from ..ops.kernels import (DropoutStreams, MemoryView, WeightSlot, attention, dropout_add, layer_norm, linear,
+                           lm_head_loss, lm_head_logits, mlp)
 from .native_plan import NativeBatchPlan, native_config
 from .tiny import PRATransformerBlock, TinyPRAModel
 
@@ -71,12 +72,11 @@ def _upload(device, *arrays, dtype=torch.int32) -> list[torch.Tensor]:
 def unsupported_reason(cfg) -> str | None:
     """Why a configuration must use the object path (``None`` when the device path applies).
 
-    ``dropout`` is not a reason: a PRA block has no dropout (``src/pra_torch/model.py:56-87``;
-    only vanilla and mixed blocks apply it, and those are refused here), so the ``td_pra_*``
-    profiles, which set dropout 0.1, train on the device path unchanged."""
+    Vanilla and mixed blocks run on the device path's per-layer route with their dropout
+    (attention probabilities, branch outputs, MLP activation) drawn from counter-based
+    Philox streams; PRA blocks have no dropout (``src/pra_torch/model.py:31-167``)."""
     head_dim = cfg.d_model // cfg.n_heads
     checks = [
-        (cfg.n_vanilla_layers or cfg.n_mixed_layers, "vanilla/mixed blocks"),
         (cfg.memory_transport != "native_kv", "cross_attention transport"),
         (cfg.search_strategy != "hierarchical", f"search_strategy={cfg.search_strategy}"),
         (cfg.routing_backend != "tensorized", "legacy routing backend"),
@@ -107,6 +107,17 @@ def unsupported_reason(cfg) -> str | None:
 
 def _round(n: int) -> int:
     return (n + _ALIGN - 1) // _ALIGN * _ALIGN
+
+
+def block_kind(block) -> str:
+    """``"pra"`` (PRA block), ``"vanilla"`` (causal encoder block, no memory) or ``"mixed"``
+    (vanilla self-attention residual, then a PRA residual, then the MLP)."""
+    name = type(block).__name__
+    if name == "VanillaTransformerBlock":
+        return "vanilla"
+    if name == "PRASATransformerBlock":
+        return "mixed"
+    return "pra"
 
 
 class FlatParams:
@@ -140,17 +151,35 @@ class FlatParams:
 
     @staticmethod
     def _ordered(model: TinyPRAModel) -> list[tuple[str, torch.nn.Parameter]]:
+        """Parameters in flat-buffer order: each block's parameters contiguous (q, k, v adjacent
+        so one [3D, D] span serves the fused QKV GEMM), then embeddings, final norm, head."""
         named = dict(model.named_parameters())
         order = []
         for i, block in enumerate(model.blocks):
             pre = f"blocks.{i}."
+            kind = block_kind(block)
+            if kind == "vanilla":
+                lay = pre + "layer."
+                order += [lay + "self_attn.in_proj_weight", lay + "self_attn.in_proj_bias",
+                          lay + "self_attn.out_proj.weight", lay + "self_attn.out_proj.bias", lay + "norm1.weight",
+                          lay + "norm1.bias", lay + "norm2.weight", lay + "norm2.bias", lay + "linear1.weight",
+                          lay + "linear1.bias", lay + "linear2.weight", lay + "linear2.bias"]
+                continue
+            attn = pre + ("pra_attn." if kind == "mixed" else "attn.")
+            if kind == "mixed":
+                order += [pre + "self_attn.in_proj_weight", pre + "self_attn.in_proj_bias",
+                          pre + "self_attn.out_proj.weight", pre + "self_attn.out_proj.bias"]
             for proj in ("q_proj", "k_proj", "v_proj"):
-                order.append(pre + f"attn.{proj}.weight")
+                order.append(attn + f"{proj}.weight")
             for proj in ("q_proj", "k_proj", "v_proj"):
-                order.append(pre + f"attn.{proj}.bias")
-            order += [pre + "attn.o_proj.weight", pre + "attn.o_proj.bias", pre + "ln1.weight", pre + "ln1.bias",
-                      pre + "ln2.weight", pre + "ln2.bias", pre + "ff.0.weight", pre + "ff.0.bias",
-                      pre + "ff.2.weight", pre + "ff.2.bias"]
+                order.append(attn + f"{proj}.bias")
+            order += [attn + "o_proj.weight", attn + "o_proj.bias", pre + "ln1.weight", pre + "ln1.bias",
+                      pre + "ln2.weight", pre + "ln2.bias"]
+            if kind == "mixed":
+                order += [pre + "ln3.weight", pre + "ln3.bias", pre + "ff.0.weight", pre + "ff.0.bias",
+                          pre + "ff.3.weight", pre + "ff.3.bias"]
+            else:
+                order += [pre + "ff.0.weight", pre + "ff.0.bias", pre + "ff.2.weight", pre + "ff.2.bias"]
         order += ["token_emb.weight", "pos_emb.weight", "ln.weight", "ln.bias"]
         order += [n for n in named if n not in order and n != "head.weight"]
         order.append("head.weight")
@@ -448,20 +477,48 @@ class DeviceRuntime:
         f = self.flat
         d = cfg.d_model
         self.layers = []
-        for i in range(cfg.n_layers):
+        self.kinds = [block_kind(block) for block in model.blocks]
+        for i, kind in enumerate(self.kinds):
             pre = f"blocks.{i}."
-            qkv = WeightSlot(w=f.span(f.shadow, pre + "attn.q_proj.weight", 3 * d * d, (3 * d, d)),
-                             b=f.span(f.shadow, pre + "attn.q_proj.bias", 3 * d, (3 * d,)),
-                             gw=f.span(f.grad, pre + "attn.q_proj.weight", 3 * d * d, (3 * d, d)),
-                             gb=f.span(f.grad, pre + "attn.q_proj.bias", 3 * d, (3 * d,)))
-            self._check_contiguous(pre)
+            if kind == "vanilla":
+                lay = pre + "layer."
+                self.layers.append({
+                    "ln1": f.slot(lay + "norm1.weight", lay + "norm1.bias"),
+                    "qkv": f.slot(lay + "self_attn.in_proj_weight", lay + "self_attn.in_proj_bias"),
+                    "o": f.slot(lay + "self_attn.out_proj.weight", lay + "self_attn.out_proj.bias"),
+                    "ln2": f.slot(lay + "norm2.weight", lay + "norm2.bias"),
+                    "up": f.slot(lay + "linear1.weight", lay + "linear1.bias"),
+                    "down": f.slot(lay + "linear2.weight", lay + "linear2.bias"),
+                })
+                continue
+            attn = pre + ("pra_attn." if kind == "mixed" else "attn.")
+            qkv = WeightSlot(w=f.span(f.shadow, attn + "q_proj.weight", 3 * d * d, (3 * d, d)),
+                             b=f.span(f.shadow, attn + "q_proj.bias", 3 * d, (3 * d,)),
+                             gw=f.span(f.grad, attn + "q_proj.weight", 3 * d * d, (3 * d, d)),
+                             gb=f.span(f.grad, attn + "q_proj.bias", 3 * d, (3 * d,)))
+            self._check_contiguous(attn)
+            if kind == "mixed":  # the PRA branch's norms are ln2 (attention) and ln3 (MLP)
+                self.layers.append({
+                    "ln1": f.slot(pre + "ln2.weight", pre + "ln2.bias"), "qkv": qkv,
+                    "o": f.slot(attn + "o_proj.weight", attn + "o_proj.bias"),
+                    "ln2": f.slot(pre + "ln3.weight", pre + "ln3.bias"),
+                    "up": f.slot(pre + "ff.0.weight", pre + "ff.0.bias"),
+                    "down": f.slot(pre + "ff.3.weight", pre + "ff.3.bias"),
+                    "sa_ln": f.slot(pre + "ln1.weight", pre + "ln1.bias"),
+                    "sa_qkv": f.slot(pre + "self_attn.in_proj_weight", pre + "self_attn.in_proj_bias"),
+                    "sa_o": f.slot(pre + "self_attn.out_proj.weight", pre + "self_attn.out_proj.bias"),
+                })
+                continue
             self.layers.append({
                 "ln1": f.slot(pre + "ln1.weight", pre + "ln1.bias"), "qkv": qkv,
-                "o": f.slot(pre + "attn.o_proj.weight", pre + "attn.o_proj.bias"),
+                "o": f.slot(attn + "o_proj.weight", attn + "o_proj.bias"),
                 "ln2": f.slot(pre + "ln2.weight", pre + "ln2.bias"),
                 "up": f.slot(pre + "ff.0.weight", pre + "ff.0.bias"),
                 "down": f.slot(pre + "ff.2.weight", pre + "ff.2.bias"),
             })
+        # vanilla / mixed blocks run the per-layer path (the native stacks hold PRA blocks only)
+        self.uniform_pra = all(kind == "pra" for kind in self.kinds)
+        self.dropout_streams = DropoutStreams()
         self.ln_f = f.slot("ln.weight", "ln.bias")
         head_rows = self.vocab_pad
         self.head = WeightSlot(w=f.view(f.shadow, "head.weight", rows=head_rows),
@@ -500,11 +557,11 @@ class DeviceRuntime:
         views = [t for slot in self.flat.slots for t in (slot.gw, slot.gb) if t is not None]
         return views + [self.tok_emb_g, self.pos_emb_g]
 
-    def _check_contiguous(self, pre: str) -> None:
+    def _check_contiguous(self, attn: str) -> None:
         f = self.flat
         d = self.cfg.d_model
-        if (f.offsets[pre + "attn.k_proj.weight"] != f.offsets[pre + "attn.q_proj.weight"] + d * d
-                or f.offsets[pre + "attn.v_proj.bias"] != f.offsets[pre + "attn.q_proj.bias"] + 2 * d):
+        if (f.offsets[attn + "k_proj.weight"] != f.offsets[attn + "q_proj.weight"] + d * d
+                or f.offsets[attn + "v_proj.bias"] != f.offsets[attn + "q_proj.bias"] + 2 * d):
             raise RuntimeError("q/k/v parameters must be adjacent in the flat layout (d_model*d_model % 64 != 0?)")
 
     # -- embeddings -----------------------------------------------------------
@@ -527,6 +584,9 @@ class DeviceRuntime:
         d = cfg.d_model
         if query_rows is not None:
             query_rows = query_rows.to(torch.int32)
+        if not self.uniform_pra:
+            return self._run_blocks_layerwise(x, b, t, key_valid, routing, memory, stop_after_kv, pool_rows, budget,
+                                              query_rows, after_qkv)
         if not torch.is_grad_enabled():
             return self._run_blocks_native(x, b, t, key_valid, routing, memory, stop_after_kv, pool_rows, budget,
                                            query_rows, after_qkv)
@@ -534,22 +594,65 @@ class DeviceRuntime:
             raise RuntimeError("per-layer hooks run only in the no-grad native stack")
         if pool_rows is None and not stop_after_kv and _NATIVE_TRAIN_STACK:
             return _TrainStack.apply(x, self, b, t, key_valid, routing, memory, budget, query_rows)
-        for li, layer in enumerate(self.layers):
+        return self._run_blocks_layerwise(x, b, t, key_valid, routing, memory, stop_after_kv, pool_rows, budget,
+                                          query_rows, None)
+
+    def _dropout(self) -> float:
+        """Dropout probability of the vanilla / mixed blocks now (training mode only; PRA blocks
+        have none, ``src/pra_torch/model.py:31-167``)."""
+        return float(self.cfg.dropout) if self.model.training and not self.uniform_pra else 0.0
+
+    def _self_attention(self, x, layer, prefix: str, b: int, t: int, key_valid, p: float, residual_dropout: bool):
+        """``x + [dropout](out_proj(causal MHA(norm(x))))`` of a vanilla block (``prefix`` "") or of
+        a mixed block's leading sublayer (``prefix`` "sa_"; no dropout on its output)."""
+        cfg = self.cfg
+        d = cfg.d_model
+        h = layer_norm(x, layer[prefix + "ln1" if not prefix else "sa_ln"])
+        qkv = linear(h, layer[prefix + "qkv"])
+        streams = self.dropout_streams
+        a = attention(qkv.view(b, t, 3 * d), cfg.n_heads, self.head_dim, None, key_valid, drop=streams.next(p))
+        if residual_dropout and p > 0.0:
+            return dropout_add(x, linear(a.view(b * t, d), layer[prefix + "o"]), streams.next(p))
+        return linear(a.view(b * t, d), layer[prefix + "o"], residual=x)
+
+    def _run_blocks_layerwise(self, x, b, t, key_valid, routing, memory, stop_after_kv, pool_rows, budget,
+                              query_rows, after_qkv):
+        """Per-layer path (autograd ops over the same kernels): every block kind, dropout in the
+        vanilla and mixed blocks, and the cache build's pool writes and gist hook."""
+        cfg = self.cfg
+        d = cfg.d_model
+        p = self._dropout()
+        streams = self.dropout_streams
+        last = len(self.layers) - 1
+        for li, (kind, layer) in enumerate(zip(self.kinds, self.layers)):
+            if kind == "vanilla":
+                if pool_rows is not None:  # nothing routes at a vanilla layer; keep its pool rows defined
+                    memory.pools[li][pool_rows].zero_()
+                if stop_after_kv and li == last:
+                    return None
+                x = self._self_attention(x, layer, "", b, t, key_valid, p, residual_dropout=True)
+                x = mlp(layer_norm(x, layer["ln2"]), x, layer["up"], layer["down"], streams.next(p), streams.next(p))
+                continue
+            if kind == "mixed":
+                x = self._self_attention(x, layer, "sa_", b, t, key_valid, p, residual_dropout=False)
             h = layer_norm(x, layer["ln1"])
             if pool_rows is not None:
                 qkv = memory.pools[li][pool_rows]
                 _ext.require().gemm("tn", h, layer["qkv"].w, None, qkv, layer["qkv"].b, None, 1.0, 0.0, None)
-                if stop_after_kv and li == len(self.layers) - 1:
-                    return None
             else:
                 qkv = linear(h, layer["qkv"])
+            if after_qkv is not None:
+                after_qkv(li)
+            if stop_after_kv and li == last:
+                return None
             qkv3 = qkv.view(b, t, 3 * d)
             mem = None
             if routing is not None and not routing.empty:
                 mem = self.route(li, qkv3, routing, memory, budget, query_rows)
             a = attention(qkv3, cfg.n_heads, self.head_dim, mem, key_valid)
             x = linear(a.view(b * t, d), layer["o"], residual=x)
-            x = mlp(layer_norm(x, layer["ln2"]), x, layer["up"], layer["down"])
+            drop_in = streams.next(p) if kind == "mixed" else None  # the mixed MLP's dropout after GELU
+            x = mlp(layer_norm(x, layer["ln2"]), x, layer["up"], layer["down"], drop_in)
         return x
 
     def _route_settings(self, budget) -> tuple[list[float], torch.Tensor | None]:

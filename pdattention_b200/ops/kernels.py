@@ -35,6 +35,61 @@ class WeightSlot:
         return beta
 
 
+@dataclass(frozen=True)
+class DropoutSpec:
+    """One dropout site of one call: probability ``p`` and the Philox stream ``(seed, offset)``
+    the kernels draw the mask from (forward and backward regenerate the same mask)."""
+
+    p: float
+    seed: int
+    offset: int
+
+
+class DropoutStreams:
+    """Hands out a fresh ``DropoutSpec`` per dropout site and call (the offset counts calls)."""
+
+    def __init__(self, seed: int | None = None):
+        self.seed = int(torch.randint(0, 2 ** 62, (1,)).item()) if seed is None else int(seed)
+        self.offset = 0
+
+    def next(self, p: float) -> DropoutSpec | None:
+        if p <= 0.0:
+            return None
+        self.offset += 1
+        return DropoutSpec(float(p), self.seed, self.offset)
+
+
+def _drop(x: torch.Tensor, spec: DropoutSpec | None) -> torch.Tensor:
+    """``x`` with the spec's mask applied (new tensor; ``x`` itself when no spec)."""
+    if spec is None:
+        return x
+    out = torch.empty_like(x)
+    require().dropout(x.contiguous(), out, spec.p, spec.seed, spec.offset)
+    return out
+
+
+class _DropoutAdd(torch.autograd.Function):
+    """y = residual + dropout(x)."""
+
+    @staticmethod
+    def forward(ctx, residual, x, spec: DropoutSpec):
+        y = torch.empty_like(x)
+        require().dropout_add(residual.contiguous(), x.contiguous(), y, spec.p, spec.seed, spec.offset)
+        ctx.spec = spec
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        dy = dy.contiguous()
+        return dy, _drop(dy, ctx.spec), None
+
+
+def dropout_add(residual: torch.Tensor, x: torch.Tensor, spec: DropoutSpec | None) -> torch.Tensor:
+    if spec is None:
+        return residual + x
+    return _DropoutAdd.apply(residual, x, spec)
+
+
 def _write_bias_grad(slot: WeightSlot, g: torch.Tensor, beta: float) -> None:
     if slot.gb is None:
         return
@@ -84,18 +139,31 @@ def linear(x: torch.Tensor, slot: WeightSlot, residual: torch.Tensor | None = No
 
 
 class _Mlp(torch.autograd.Function):
-    """y = residual + gelu(h W1^T + b1) W2^T + b2 with the GELU derivative fused into the dgrad GEMM."""
+    """y = residual + drop_out(drop_in(gelu(h W1^T + b1)) W2^T + b2) with the GELU derivative
+    fused into the dgrad GEMM.  ``drop_in`` / ``drop_out`` (optional ``DropoutSpec``) are the
+    vanilla blocks' dropout after the activation and on the branch output; the masks are
+    regenerated in the backward (a mask commutes with the elementwise GELU derivative)."""
 
     @staticmethod
-    def forward(ctx, h, residual, up: WeightSlot, down: WeightSlot):
+    def forward(ctx, h, residual, up: WeightSlot, down: WeightSlot, drop_in, drop_out):
         ext = require()
         m = h.shape[0]
         z = torch.empty((m, up.w.shape[0]), device=h.device, dtype=torch.bfloat16)
         u = torch.empty_like(z)
         ext.gemm("tn_gelu", h, up.w, None, u, up.b, z, 1.0, 0.0, None)
+        if drop_in is not None:
+            ext.dropout(u, u, drop_in.p, drop_in.seed, drop_in.offset)
         y = torch.empty((m, down.w.shape[0]), device=h.device, dtype=torch.bfloat16)
-        ext.gemm("tn", u, down.w, residual, y, down.b, None, 1.0, 1.0 if residual is not None else 0.0, None)
+        if drop_out is None:
+            ext.gemm("tn", u, down.w, residual, y, down.b, None, 1.0, 1.0 if residual is not None else 0.0, None)
+        else:
+            ext.gemm("tn", u, down.w, None, y, down.b, None, 1.0, 0.0, None)
+            if residual is not None:
+                ext.dropout_add(residual.contiguous(), y, y, drop_out.p, drop_out.seed, drop_out.offset)
+            else:
+                ext.dropout(y, y, drop_out.p, drop_out.seed, drop_out.offset)
         ctx.up, ctx.down = up, down
+        ctx.drops = (drop_in, drop_out)
         ctx.has_residual = residual is not None
         ctx.save_for_backward(h, z, u)
         return y
@@ -103,19 +171,24 @@ class _Mlp(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy):
         h, z, u = ctx.saved_tensors
+        drop_in, drop_out = ctx.drops
         dy = dy.contiguous()
+        dbranch = _drop(dy, drop_out)
         ext = require()
         dz = torch.empty_like(z)
-        ext.gemm("nn_dgelu", dy, ctx.down.w, None, dz, None, z, 1.0, 0.0, None)
-        _wgrad(ctx.down, dy, u)
+        ext.gemm("nn_dgelu", dbranch, ctx.down.w, None, dz, None, z, 1.0, 0.0, None)
+        if drop_in is not None:
+            ext.dropout(dz, dz, drop_in.p, drop_in.seed, drop_in.offset)
+        _wgrad(ctx.down, dbranch, u)
         dh = torch.empty_like(h)
         ext.gemm("nn", dz, ctx.up.w, None, dh, None, None, 1.0, 0.0, None)
         _wgrad(ctx.up, dz, h)
-        return dh, (dy if ctx.has_residual else None), None, None
+        return dh, (dy if ctx.has_residual else None), None, None, None, None
 
 
-def mlp(h, residual, up: WeightSlot, down: WeightSlot):
-    return _Mlp.apply(h, residual, up, down)
+def mlp(h, residual, up: WeightSlot, down: WeightSlot, drop_in: DropoutSpec | None = None,
+        drop_out: DropoutSpec | None = None):
+    return _Mlp.apply(h, residual, up, down, drop_in, drop_out)
 
 
 class _Norm(torch.autograd.Function):
@@ -166,37 +239,43 @@ class _Attention(torch.autograd.Function):
     """One softmax over [memory (visible) ; local (causal, padding-masked)] keys."""
 
     @staticmethod
-    def forward(ctx, qkv, heads: int, head_dim: int, memory: MemoryView | None, key_valid, scale: float):
+    def forward(ctx, qkv, heads: int, head_dim: int, memory: MemoryView | None, key_valid, scale: float,
+                drop: DropoutSpec | None = None):
         b, t, width = qkv.shape
         d = heads * head_dim
         q, k, v = qkv[..., :d], qkv[..., d:2 * d], qkv[..., 2 * d:3 * d]
         mk = mv = mi = ml = None
         if memory is not None:
             mk, mv, mi, ml = memory.k, memory.v, memory.idx, memory.length
-        out, lse = require().attention_fwd(q, k, v, heads, heads, head_dim, mk, mv, mi, ml, key_valid, scale)
-        ctx.meta = (heads, head_dim, memory, scale)
+        dp, ds, do = (drop.p, drop.seed, drop.offset) if drop is not None else (0.0, 0, 0)
+        out, lse = require().attention_fwd(q, k, v, heads, heads, head_dim, mk, mv, mi, ml, key_valid, scale, dp, ds,
+                                           do)
+        ctx.meta = (heads, head_dim, memory, scale, drop)
         ctx.save_for_backward(qkv, out, lse, key_valid if key_valid is not None else torch.empty(0))
         return out
 
     @staticmethod
     def backward(ctx, dout):
         qkv, out, lse, key_valid = ctx.saved_tensors
-        heads, head_dim, memory, scale = ctx.meta
+        heads, head_dim, memory, scale, drop = ctx.meta
         d = heads * head_dim
         q, k, v = qkv[..., :d], qkv[..., d:2 * d], qkv[..., 2 * d:3 * d]
         mk = mv = mi = ml = None
         if memory is not None:
             mk, mv, mi, ml = memory.k, memory.v, memory.idx, memory.length
+        dp, ds, do = (drop.p, drop.seed, drop.offset) if drop is not None else (0.0, 0, 0)
         (dqkv,) = require().attention_bwd(dout.contiguous(), q, k, v, out, lse, heads, head_dim, mk, mv, mi, ml,
-                                          key_valid if key_valid.numel() else None, scale)
-        return dqkv, None, None, None, None, None
+                                          key_valid if key_valid.numel() else None, scale, dp, ds, do)
+        return dqkv, None, None, None, None, None, None
 
 
 def attention(qkv: torch.Tensor, heads: int, head_dim: int, memory: MemoryView | None = None,
-              key_valid: torch.Tensor | None = None, scale: float | None = None) -> torch.Tensor:
-    """``qkv`` ``[B, T, 3*H*Dh]`` (q, k, v packed per token) -> ``[B, T, H*Dh]``."""
+              key_valid: torch.Tensor | None = None, scale: float | None = None,
+              drop: DropoutSpec | None = None) -> torch.Tensor:
+    """``qkv`` ``[B, T, 3*H*Dh]`` (q, k, v packed per token) -> ``[B, T, H*Dh]``; ``drop`` applies
+    dropout to the attention probabilities (local attention only)."""
     scale = 1.0 / math.sqrt(head_dim) if scale is None else scale
-    return _Attention.apply(qkv, heads, head_dim, memory, key_valid, scale)
+    return _Attention.apply(qkv, heads, head_dim, memory, key_valid, scale, drop)
 
 
 class _LmHeadLoss(torch.autograd.Function):
