@@ -35,6 +35,24 @@ T* ptr(const torch::Tensor& t) {
   return reinterpret_cast<T*>(t.data_ptr());
 }
 
+// Memory pools may be device tensors or pinned host tensors (the CPU-resident K/V tier): a
+// kernel then gathers only the selected rows over the host link, through the address under
+// which the current device sees the pinned allocation.
+void expect_pool(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() || t.is_pinned(), name, " must be a CUDA tensor or pinned host memory");
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, name, " must be bf16");
+}
+
+template <typename T>
+T* pool_ptr(const torch::Tensor& t) {
+  if (t.is_cuda()) return ptr<T>(t);
+  cudaPointerAttributes attr{};
+  const cudaError_t e = cudaPointerGetAttributes(&attr, t.data_ptr());
+  TORCH_CHECK(e == cudaSuccess && attr.devicePointer != nullptr,
+              "pinned host pool is not mapped into the device address space: ", cudaGetErrorString(e));
+  return reinterpret_cast<T*>(attr.devicePointer);
+}
+
 template <typename T>
 const T* optr(const c10::optional<torch::Tensor>& t) {
   return (t.has_value() && t->defined() && t->numel() > 0) ? reinterpret_cast<const T*>(t->data_ptr()) : nullptr;
@@ -79,16 +97,16 @@ AttnParams attn_params(const torch::Tensor& q, const torch::Tensor& k, const tor
   p.scale = static_cast<float>(scale);
   if (mem_idx.has_value() && mem_idx->numel() > 0) {
     TORCH_CHECK(mem_k.has_value() && mem_v.has_value() && mem_len.has_value(), "memory needs k, v, idx and len");
-    expect(*mem_k, at::kBFloat16, "mem_k");
-    expect(*mem_v, at::kBFloat16, "mem_v");
+    expect_pool(*mem_k, "mem_k");
+    expect_pool(*mem_v, "mem_v");
     expect(*mem_idx, at::kInt, "mem_idx");
     expect(*mem_len, at::kInt, "mem_len");
     TORCH_CHECK(mem_k->dim() == 2 && mem_k->stride(1) == 1 && mem_v->stride(1) == 1 &&
                     mem_k->stride(0) == mem_v->stride(0),
                 "memory pools must be row-major [rows, width] with equal strides");
     TORCH_CHECK(mem_idx->is_contiguous() && mem_idx->size(0) == p.B, "mem_idx must be [B, max]");
-    p.mem_k = ptr<const __nv_bfloat16>(*mem_k);
-    p.mem_v = ptr<const __nv_bfloat16>(*mem_v);
+    p.mem_k = pool_ptr<const __nv_bfloat16>(*mem_k);
+    p.mem_v = pool_ptr<const __nv_bfloat16>(*mem_v);
     p.mem_row = mem_k->stride(0);
     p.mem_idx = ptr<const int>(*mem_idx);
     p.mem_len = ptr<const int>(*mem_len);
@@ -830,8 +848,10 @@ std::vector<torch::Tensor> decode_attention(torch::Tensor q, int64_t heads, int6
   if (mem_idx.has_value() && mem_idx->numel() > 0) {
     TORCH_CHECK(mem_k.has_value() && mem_v.has_value() && mem_len.has_value(), "memory needs k, v, idx and len");
     TORCH_CHECK(mem_k->stride(-1) == 1 && mem_v->stride(0) == mem_k->stride(0), "memory pools share a row stride");
-    p.mem_k = ptr<const __nv_bfloat16>(*mem_k);
-    p.mem_v = ptr<const __nv_bfloat16>(*mem_v);
+    expect_pool(*mem_k, "mem_k");
+    expect_pool(*mem_v, "mem_v");
+    p.mem_k = pool_ptr<const __nv_bfloat16>(*mem_k);
+    p.mem_v = pool_ptr<const __nv_bfloat16>(*mem_v);
     p.mem_row = mem_k->stride(0);
     p.mem_idx = ptr<const int>(*mem_idx);
     p.mem_max = mem_idx->size(1);

@@ -164,7 +164,7 @@ class PRALlamaEngine:
     """Batched prefill / decode of a PRA Llama-family model on one GPU (or one TP shard)."""
 
     def __init__(self, weights: LlamaWeights, device, tp=None, decode_split_keys: int = 512, k_cand_factor: int = 4,
-                 shard_routing: bool = True):
+                 shard_routing: bool = True, kv_residency: str = "gpu"):
         self.w = weights
         self.cfg = weights.cfg
         self.device = torch.device(device)
@@ -178,6 +178,12 @@ class PRALlamaEngine:
         self.split_keys = decode_split_keys
         self.k_cand_factor = k_cand_factor
         self.shard_routing = shard_routing  # TP: score chunk slices per rank + cross-GPU top-k merge
+        if kv_residency not in ("gpu", "cpu"):
+            raise ValueError("kv_residency must be 'gpu' or 'cpu'")
+        # "cpu": the chunk K/V pool lives in pinned host memory after the build; routing stays
+        # on the device (gists) and the attention kernels gather only the selected rows over the
+        # host link (a memory larger than the GPU's HBM at the cost of link bandwidth per step)
+        self.kv_residency = kv_residency
         self.ext = _ext.require()
         self._rope_cache: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
         self.memory: ChunkMemory | None = None
@@ -352,6 +358,11 @@ class PRALlamaEngine:
             self.tp.gather_gists(mem)
         # bf16 routing copy for the tensor-core scoring GEMM
         mem.gn_bf16.copy_(mem.gn.view(cfg.num_hidden_layers, mem.C_pad, -1))
+        if self.kv_residency == "cpu":
+            host = torch.empty(mem.pool.shape, dtype=mem.pool.dtype, pin_memory=True)
+            host.copy_(mem.pool, non_blocking=True)
+            torch.cuda.current_stream(self.device).synchronize()  # the device pool is released next
+            mem.pool = host
         self.memory = mem
         return mem
 

@@ -77,14 +77,12 @@ def unsupported_reason(cfg) -> str | None:
     Philox streams; PRA blocks have no dropout (``src/pra_torch/model.py:31-167``)."""
     head_dim = cfg.d_model // cfg.n_heads
     checks = [
-        (cfg.memory_transport != "native_kv", "cross_attention transport"),
         (cfg.search_strategy != "hierarchical", f"search_strategy={cfg.search_strategy}"),
         (cfg.routing_backend != "tensorized", "legacy routing backend"),
         (cfg.use_summary, "summary routing"),
         (cfg.cache_build_mode != "detached", "trainable gists"),
         (cfg.reference_encoding_strategy != "independent", "grouped encoding"),
         (cfg.encoding_chunking is not None, "bounded encoding"),
-        (cfg.kv_cache_residency != "gpu", "CPU-resident K/V"),
         (cfg.gist_mode not in {"mean", "kmeans"}, f"gist_mode={cfg.gist_mode}"),
         (cfg.gist_mode == "kmeans" and cfg.gist_kmeans_empty_cluster_policy == "error",
          "k-means error-on-empty-cluster policy"),
@@ -351,6 +349,8 @@ class BatchMemory:
         # one allocation per table; per-layer views keep the indexing simple
         self.pool = torch.empty((L, n_seq * seq_len, width), device=device, dtype=torch.bfloat16)
         self.pools = list(self.pool.unbind(0))
+        self.kv_bytes = 0         # cached K/V bytes (bf16 keys + values of every chunk token and layer)
+        self.device_kv_bytes = 0  # of which on the device (0 once the pool moves to the host tier)
         g = max(cfg.gists_per_chunk if cfg.gist_mode == "kmeans" else 1, 1)
         self.G = g
         self.n_seq = n_seq
@@ -516,9 +516,18 @@ class DeviceRuntime:
                 "up": f.slot(pre + "ff.0.weight", pre + "ff.0.bias"),
                 "down": f.slot(pre + "ff.2.weight", pre + "ff.2.bias"),
             })
-        # vanilla / mixed blocks run the per-layer path (the native stacks hold PRA blocks only)
-        self.uniform_pra = all(kind == "pra" for kind in self.kinds)
+        self.cross_attention = cfg.memory_transport == "cross_attention"
+        if self.cross_attention:  # legacy transport: the memory branch has its own output projection
+            for i, (kind, layer) in enumerate(zip(self.kinds, self.layers)):
+                if kind != "vanilla":
+                    attn = f"blocks.{i}." + ("pra_attn." if kind == "mixed" else "attn.")
+                    layer["mem_o"] = f.slot(attn + "mem_o_proj.weight", attn + "mem_o_proj.bias")
+        # vanilla / mixed blocks and the cross-attention transport run the per-layer path (the
+        # native stacks hold native-K/V PRA blocks only)
+        self.uniform_pra = all(kind == "pra" for kind in self.kinds) and not self.cross_attention
         self.dropout_streams = DropoutStreams()
+        self._host_pool: torch.Tensor | None = None  # pinned K/V pool of the CPU-resident tier
+        self._retired_host_pools: list[torch.Tensor] = []
         self.ln_f = f.slot("ln.weight", "ln.bias")
         head_rows = self.vocab_pad
         self.head = WeightSlot(w=f.view(f.shadow, "head.weight", rows=head_rows),
@@ -615,6 +624,23 @@ class DeviceRuntime:
             return dropout_add(x, linear(a.view(b * t, d), layer[prefix + "o"]), streams.next(p))
         return linear(a.view(b * t, d), layer[prefix + "o"], residual=x)
 
+    def _cross_attention(self, x, qkv3, layer, mem: MemoryView | None, key_valid, b: int, t: int):
+        """Legacy ``cross_attention`` transport (``src/pra_torch/attention.py:557-628``): local causal
+        attention through ``o_proj`` plus ``memory_alpha`` times a separately normalised attention
+        over the row's selected memory keys through ``mem_o_proj``; rows without memory add
+        nothing.  The memory branch is the ragged kernel with every local key masked."""
+        cfg = self.cfg
+        d = cfg.d_model
+        a = attention(qkv3, cfg.n_heads, self.head_dim, None, key_valid)
+        x = linear(a.view(b * t, d), layer["o"], residual=x)
+        if mem is None:
+            return x
+        hidden = torch.zeros((b, t), device=qkv3.device, dtype=torch.uint8)  # no local key is visible
+        am = attention(qkv3, cfg.n_heads, self.head_dim, mem, hidden)
+        m = linear(am.view(b * t, d), layer["mem_o"])
+        rows = (mem.length > 0).to(m.dtype) * float(cfg.memory_alpha)
+        return x + m * rows.repeat_interleave(t)[:, None]
+
     def _run_blocks_layerwise(self, x, b, t, key_valid, routing, memory, stop_after_kv, pool_rows, budget,
                               query_rows, after_qkv):
         """Per-layer path (autograd ops over the same kernels): every block kind, dropout in the
@@ -649,8 +675,11 @@ class DeviceRuntime:
             mem = None
             if routing is not None and not routing.empty:
                 mem = self.route(li, qkv3, routing, memory, budget, query_rows)
-            a = attention(qkv3, cfg.n_heads, self.head_dim, mem, key_valid)
-            x = linear(a.view(b * t, d), layer["o"], residual=x)
+            if self.cross_attention:
+                x = self._cross_attention(x, qkv3, layer, mem, key_valid, b, t)
+            else:
+                a = attention(qkv3, cfg.n_heads, self.head_dim, mem, key_valid)
+                x = linear(a.view(b * t, d), layer["o"], residual=x)
             drop_in = streams.next(p) if kind == "mixed" else None  # the mixed MLP's dropout after GELU
             x = mlp(layer_norm(x, layer["ln2"]), x, layer["up"], layer["down"], drop_in)
         return x
@@ -967,6 +996,10 @@ class DeviceRuntime:
             chunk_tables = (view("chunk_start"), view("chunk_len"), view("chunk_pool_row"))
             prompt_ns = ([view(f"ns{i}") for i in range(6)], bool(pt["ns_empty"]))
         memory = BatchMemory(self, entries, chunks, rows, seq_len, self.device, chunk_tables, prompt_ns)
+        out = getattr(plan, "out", None)
+        tokens = int(out["chunk_token_off"][-1]) if out is not None and len(out["chunk_token_off"]) else \
+            sum(len(c.token_ids) for c in chunks)
+        memory.kv_bytes = memory.device_kv_bytes = tokens * self.cfg.n_layers * 2 * self.cfg.d_model * 2
         with torch.no_grad():
             start = 0
             for wave_chunks, table in zip(plan.waves, plan.wave_tables):
@@ -974,8 +1007,32 @@ class DeviceRuntime:
                     continue
                 self._encode_wave(memory, wave_chunks, start, table, packed)
                 start += len(wave_chunks)
+        if self.cfg.kv_cache_residency == "cpu":
+            self._move_pool_to_host(memory)
         self.last_memory = memory
         return memory, caches, builders
+
+    def _move_pool_to_host(self, memory: "BatchMemory") -> None:
+        """CPU-resident K/V (``kv_cache_residency="cpu"``, ``src/pra_torch/model.py:473-482``): the
+        encoded pool moves to pinned host memory (one asynchronous copy on the stream) and the
+        device pool is released; the attention kernels then gather only the selected rows over
+        the host link (zero-copy), which is the reference's selective host-to-device transfer
+        fused into the attention's own row gather.  The gists stay on the device for routing.
+        The host buffer is kept by the runtime and reused: only stream-ordered work touches it
+        (the next step's copy runs after this step's kernels)."""
+        need = memory.pool.numel()
+        host = self._host_pool
+        if host is None or host.numel() < need:
+            if host is not None:
+                self._retired_host_pools.append(host)  # never handed back while kernels may read it
+            size = 1 << max(need - 1, 1).bit_length()
+            host = torch.empty(size, dtype=torch.bfloat16, pin_memory=True)
+            self._host_pool = host
+        view = host[:need].view(memory.pool.shape)
+        view.copy_(memory.pool, non_blocking=True)
+        memory.device_kv_bytes = 0
+        memory.pool = view
+        memory.pools = list(view.unbind(0))
 
     def _encode_wave(self, memory: BatchMemory, wave_chunks: list[int], first_seq: int, table: dict,
                      packed: torch.Tensor) -> None:
@@ -1273,7 +1330,8 @@ def device_batch_step(model, batch, device, tokenizer, resolver_config, cache_co
     tokens = int(am.sum()) if am.device.type == "cpu" else am.sum()
     b = ids.shape[0]
     metrics = {"cache_build_duration_seconds": build_s / max(b, 1), "cache_build_total_duration_seconds": build_s,
-               "logical_batch_size": float(b), "prompt_forward_calls": 1.0}
+               "logical_batch_size": float(b), "prompt_forward_calls": 1.0,
+               "cached_kv_bytes": float(memory.kv_bytes), "gpu_cached_kv_bytes": float(memory.device_kv_bytes)}
     return loss, {"tokens": tokens, "examples": b, "batch": batch, "caches": caches, "metrics": metrics,
                   "memory": memory, "hidden": hidden}
 

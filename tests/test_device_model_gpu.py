@@ -184,3 +184,32 @@ def test_device_logits_and_selected_chunks_match_object_path(cuda, tmp_path):
             same += got == want
         # layer 0 routes queries that differ from the fp32 ones only by bf16 rounding
         assert same == b if layer == 0 else same >= 0.75 * b, (layer, same, b)
+
+
+def test_cpu_resident_kv_tier_matches_gpu_residency(cuda, tmp_path):
+    """kv_cache_residency="cpu": the encoded pool lives in pinned host memory and the attention
+    kernels gather the selected rows over the host link; the loss and its gradients equal the
+    device-resident run, and no cached K/V stays on the device."""
+    torch.manual_seed(21)
+    tok, batch = tiny_batch(Path(tmp_path))
+    results = {}
+    for residency in ("gpu", "cpu"):
+        cfg = tiny_config(tok.vocab_size)
+        cfg.kv_cache_residency = residency
+        torch.manual_seed(22)
+        model = TinyPRAModel(cfg).to(cuda)
+        attach_device_runtime(model)
+        assert model._device_runtime is not None
+        opt = model.build_optimizer(TrainConfig(device="cuda", learning_rate=1e-3))
+        opt.zero_grad()
+        loss, out = _pra_batch_step(model, batch, "cuda", tok, ResolverServiceConfig(), None)
+        loss.backward()
+        torch.cuda.synchronize()
+        mem = out["memory"]
+        results[residency] = (loss.item(), model._device_runtime.flat.grad.float().clone(), out["metrics"],
+                              mem.pool.is_cuda)
+    (l_gpu, g_gpu, m_gpu, on_gpu), (l_cpu, g_cpu, m_cpu, on_cpu_dev) = results["gpu"], results["cpu"]
+    assert on_gpu and not on_cpu_dev
+    assert l_cpu == l_gpu
+    assert torch.equal(g_cpu, g_gpu)
+    assert m_cpu["gpu_cached_kv_bytes"] == 0 and m_cpu["cached_kv_bytes"] == m_gpu["cached_kv_bytes"] > 0

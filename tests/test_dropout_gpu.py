@@ -168,3 +168,37 @@ def test_dropout_training_on_the_device_path(ext, tmp_path):
         losses.append(loss.item())
     assert rt.dropout_streams.offset > 0  # dropout streams were drawn
     assert losses[-1] < 0.8 * losses[0], losses
+
+
+def test_cross_attention_transport_matches_object_path(ext, tmp_path):
+    """Legacy transport: separately normalised memory attention through mem_o_proj, scaled by
+    memory_alpha, next to the local attention (the ragged kernel with every local key masked)."""
+    torch.manual_seed(14)
+    tok, batch = tiny_batch(Path(tmp_path))
+    cfg = copy.deepcopy(tiny_config(tok.vocab_size))
+    cfg.memory_transport, cfg.memory_alpha = "cross_attention", 0.5
+    cfg.__post_init__()
+    reference = TinyPRAModel(copy.deepcopy(cfg)).cuda().eval()
+    device_model = TinyPRAModel(copy.deepcopy(cfg)).cuda().eval()
+    device_model.load_state_dict(reference.state_dict())
+    attach_device_runtime(device_model)
+    rt = device_model._device_runtime
+    assert rt is not None and rt.cross_attention and "mem_o" in rt.layers[0]
+    with torch.no_grad():
+        ref_loss, ref_out = _pra_batch_step(reference, batch, "cuda", tok, ResolverServiceConfig(), None)
+        dev_loss, dev_out = _pra_batch_step(device_model, batch, "cuda", tok, ResolverServiceConfig(), None)
+    assert int(rt.last_routing[0].ints[0].sum()) > 0  # memory was materialised
+    b, t = batch["input_ids"].shape
+    dev_logits = rt.logits(dev_out["hidden"], b, t).float()
+    ref_logits = ref_out["logits"].float()
+    valid = batch["attention_mask"].bool().cuda()
+    err = (dev_logits - ref_logits).abs()[valid]
+    assert err.max() <= 0.05 * ref_logits.abs()[valid].max(), err.max()
+    # and it trains (gradients flow through both branches)
+    device_model.train()
+    opt = device_model.build_optimizer(TrainConfig(device="cuda", learning_rate=1e-3))
+    opt.zero_grad()
+    loss, _ = _pra_batch_step(device_model, batch, "cuda", tok, ResolverServiceConfig(), None)
+    loss.backward()
+    gw = rt.layers[0]["mem_o"].gw
+    assert torch.isfinite(rt.flat.grad.float()).all() and float(gw.float().abs().sum()) > 0

@@ -282,3 +282,24 @@ def test_segmented_selection_equals_single_pass(ext, monkeypatch):
                                     gists_per_chunk=G)
         monkeypatch.setattr(routing, "SEGMENT", 8192)
         assert torch.equal(got[1], want[1]) and torch.equal(got[2], want[2]), (G, got[2], want[2])
+
+
+def test_host_resident_chunk_memory_equals_device_memory(ext):
+    """kv_residency="cpu": the chunk K/V pool moves to pinned host memory after the build and the
+    prefill / decode attention gathers the selected rows over the host link: same logits."""
+    from pdattention_b200.inference.llama_engine import LlamaWeights, PRALlamaEngine
+
+    cfg, model, chunks, lengths = _tiny_setup(2)
+    weights = LlamaWeights.from_reference(model, "cuda")
+    out = {}
+    for residency in ("gpu", "cpu"):
+        engine = PRALlamaEngine(weights, "cuda", decode_split_keys=64, kv_residency=residency)
+        mem = engine.build_memory(chunks, lengths)
+        assert mem.pool.is_cuda == (residency == "gpu")
+        engine.set_namespace(torch.tensor([0, 0]), torch.tensor([12, 6]))
+        ids = torch.randint(0, cfg.vocab_size, (2, 9), generator=torch.Generator().manual_seed(3))
+        first = engine.prefill(ids, torch.tensor([9, 5]), max_new_tokens=3).float().cpu()
+        step = engine.decode_step(first.argmax(-1).cuda()).float().cpu()
+        out[residency] = (first, step)
+    assert torch.equal(out["gpu"][0], out["cpu"][0])
+    assert torch.equal(out["gpu"][1], out["cpu"][1])
