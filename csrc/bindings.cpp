@@ -482,7 +482,8 @@ std::vector<torch::Tensor> route(torch::Tensor query, torch::Tensor gists, torch
                                  torch::Tensor chunk_len, torch::Tensor chunk_pool_row, int64_t k_ref, int64_t k_chunk,
                                  int64_t gist_agg, int64_t ref_agg, double threshold, int64_t budget, bool gist_only,
                                  bool full_reference, bool deduplicate, int64_t max_sel, int64_t max_mem,
-                                 c10::optional<torch::Tensor> budget_rows, c10::optional<torch::Tensor> query_rows) {
+                                 c10::optional<torch::Tensor> budget_rows, c10::optional<torch::Tensor> query_rows,
+                                 bool global_chunks = false) {
   c10::cuda::CUDAGuard guard(query.device());
   expect(query, at::kBFloat16, "query");
   expect(gists, at::kFloat, "gists");
@@ -522,6 +523,8 @@ std::vector<torch::Tensor> route(torch::Tensor query, torch::Tensor gists, torch
   p.gist_only = gist_only;
   p.full_reference = full_reference;
   p.deduplicate = deduplicate;
+  p.global_chunks = global_chunks;
+  TORCH_CHECK(!(global_chunks && full_reference), "global_chunks search with full-reference expansion is not supported");
   p.max_sel = max_sel;
   p.max_mem = max_mem;
   auto io = query.options().dtype(at::kInt);
@@ -1136,7 +1139,7 @@ std::vector<torch::Tensor> stack_forward(torch::Tensor x, int64_t B, int64_t T, 
   TORCH_CHECK(x.dim() == 2 && x.size(0) == M && x.size(1) == D && x.is_contiguous(), "x must be [B*T, D]");
   const bool routed = !ns.empty();
   if (routed) {
-    TORCH_CHECK(ns.size() == 9 && gists.has_value() && gist_count.has_value() && route_cfg.size() == 11,
+    TORCH_CHECK(ns.size() == 9 && gists.has_value() && gist_count.has_value() && route_cfg.size() >= 11,
                 "routing needs 9 namespace tensors, gists, gist_count and 11 settings");
     TORCH_CHECK(mem_pool.has_value() || gist_kv.has_value(), "routing needs the memory K/V pool");
   }
@@ -1160,7 +1163,8 @@ std::vector<torch::Tensor> stack_forward(torch::Tensor x, int64_t B, int64_t T, 
                      (int64_t)route_cfg[2], (int64_t)route_cfg[3], route_cfg[4], (int64_t)route_cfg[5], gist_only,
                      route_cfg[7] != 0.0, route_cfg[8] != 0.0, (int64_t)route_cfg[9], (int64_t)route_cfg[10],
                      budget_rows, query_rows.has_value() ? query_rows : c10::optional<torch::Tensor>(
-                                                               torch::full({B}, (int)(T - 1), x.options().dtype(at::kInt))));
+                                                               torch::full({B}, (int)(T - 1), x.options().dtype(at::kInt))),
+                     route_cfg.size() > 11 && route_cfg[11] != 0.0);
       if (gist_only) {
         mk = gist_kv->select(0, 0).select(0, l);
         mv = gist_kv->select(0, 1).select(0, l);
@@ -1213,7 +1217,7 @@ std::vector<torch::Tensor> stack_train_forward(torch::Tensor x, int64_t B, int64
   TORCH_CHECK(x.dim() == 2 && x.size(0) == M && x.size(1) == D && x.is_contiguous(), "x must be [B*T, D]");
   const bool routed = !ns.empty();
   if (routed) {
-    TORCH_CHECK(ns.size() == 9 && gists.has_value() && gist_count.has_value() && route_cfg.size() == 11,
+    TORCH_CHECK(ns.size() == 9 && gists.has_value() && gist_count.has_value() && route_cfg.size() >= 11,
                 "routing needs 9 namespace tensors, gists, gist_count and 11 settings");
     TORCH_CHECK(mem_pool.has_value() || gist_kv.has_value(), "routing needs the memory K/V pool");
   }
@@ -1239,7 +1243,7 @@ std::vector<torch::Tensor> stack_train_forward(torch::Tensor x, int64_t B, int64
                      ns[4], ns[5], ns[6], ns[7], ns[8], (int64_t)route_cfg[0], (int64_t)route_cfg[1],
                      (int64_t)route_cfg[2], (int64_t)route_cfg[3], route_cfg[4], (int64_t)route_cfg[5], gist_only,
                      route_cfg[7] != 0.0, route_cfg[8] != 0.0, (int64_t)route_cfg[9], (int64_t)route_cfg[10],
-                     budget_rows, last_rows);
+                     budget_rows, last_rows, route_cfg.size() > 11 && route_cfg[11] != 0.0);
       if (gist_only) {
         mk = gist_kv->select(0, 0).select(0, l);
         mv = gist_kv->select(0, 1).select(0, l);
@@ -1424,7 +1428,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gist_kmeans", &gist_kmeans);
   m.def("gist_mean_into", &gist_mean_into);
   m.def("gist_kmeans_into", &gist_kmeans_into);
-  m.def("route", &route);
+  m.def("route", &route, py::arg("query"), py::arg("gists"), py::arg("gist_count"), py::arg("row_pos_off"),
+        py::arg("row_ref_off"), py::arg("ref_pos_off"), py::arg("pos_chunk"), py::arg("pos_ref"), py::arg("pos_rank"),
+        py::arg("chunk_start"), py::arg("chunk_len"), py::arg("chunk_pool_row"), py::arg("k_ref"), py::arg("k_chunk"),
+        py::arg("gist_agg"), py::arg("ref_agg"), py::arg("threshold"), py::arg("budget"), py::arg("gist_only"),
+        py::arg("full_reference"), py::arg("deduplicate"), py::arg("max_sel"), py::arg("max_mem"),
+        py::arg("budget_rows"), py::arg("query_rows"), py::arg("global_chunks") = false);
   m.def("stack_forward", &stack_forward);
   m.def("stack_train_forward", &stack_train_forward);
   m.def("stack_train_backward", &stack_train_backward);

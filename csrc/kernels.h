@@ -181,6 +181,8 @@ struct RouteParams {
   int budget;
   const int* budget_rows;      // [B] per-row budgets, or null (scalar budget)
   bool gist_only, full_reference, deduplicate;
+  bool global_chunks;          // search_strategy "global_chunks": one global chunk ranking under
+                               // the distinct-URI and per-URI limits (else hierarchical)
   int max_sel, max_mem;
   int* mem_idx;                // [B, max_mem]
   int* mem_len;                // [B]

@@ -6,7 +6,9 @@
 //      winning gist index and score;
 //   2. URI scores = the same reduction over each URI's chunk scores;
 //   3. hierarchical selection: top URIs ordered (-score, uri rank), then inside
-//      each the top chunks ordered (-score, chunk-id rank);
+//      each the top chunks ordered (-score, chunk-id rank); or (global_chunks) every
+//      chunk ranked by (-score, uri rank, chunk-id rank) and taken greedily while its
+//      URI has fewer than k_chunk picks and the distinct URIs stay within k_ref;
 //   4. optional full-reference expansion, score threshold, greedy whole-chunk
 //      budget in (-score, uri, chunk-id) order, then materialisation order
 //      (uri, token_start, chunk-id) with overlap already covered by the same URI
@@ -82,6 +84,8 @@ __global__ void __launch_bounds__(NT) route_kernel(RouteParams p) {
   int* crank = widx + MAX_ROW_CHUNKS;                 // [MAX_ROW_CHUNKS] lexical chunk rank (pos_rank)
   float* rscore = reinterpret_cast<float*>(crank + MAX_ROW_CHUNKS);  // [MAX_ROW_REFS]
   int* ref_taken = reinterpret_cast<int*>(rscore + MAX_ROW_REFS);    // [MAX_ROW_REFS]
+  int* cref = ref_taken + MAX_ROW_REFS;                              // [MAX_ROW_CHUNKS] global mode: URI of a chunk
+  int* rslot = cref + MAX_ROW_CHUNKS;                                // [MAX_ROW_REFS] global mode: URI pick order
   __shared__ float scratch[32];
   __shared__ int warp_tot[NT / 32];
   __shared__ float red_v[NT / 32];
@@ -168,32 +172,51 @@ __global__ void __launch_bounds__(NT) route_kernel(RouteParams p) {
   }
   __syncthreads();
 
-  // 4a. top URIs under (-score, uri rank): rank counting when every ref has its own
-  // thread, otherwise repeated block argmax
-  const int kr = min(min(p.k_ref, nr), 64);
-  if (nr <= NT) {
-    if (threadIdx.x < nr) {
-      const int r = threadIdx.x;
-      int rank = 0;
-      for (int o = 0; o < nr; ++o) rank += before(rscore[o], o, rscore[r], r) ? 1 : 0;
-      if (rank < kr) top_ref[rank] = r;
+  if (p.global_chunks) {
+    // 4g. global chunk ranking (-score, uri rank, chunk rank) taken greedily: a chunk is
+    // eligible while its URI has fewer than k_chunk picks and the URI is already picked or
+    // fewer than k_ref URIs are (the constraints only tighten, so the greedy over the global
+    // order is repeated block argmax over the eligible chunks)
+    for (int r = threadIdx.x; r < nr; r += NT) {
+      const int a = p.ref_pos_off[r0 + r] - c0, z = p.ref_pos_off[r0 + r + 1] - c0;
+      for (int i = a; i < z; ++i) cref[i] = r;
+      ref_taken[r] = 0;  // picks of URI r
+      rslot[r] = -1;
     }
-  } else {
-    for (int j = 0; j < kr; ++j) {
+    __shared__ int n_refs_picked;
+    if (threadIdx.x == 0) {
+      n_refs_picked = 0;
+      n_sel = 0;
+    }
+    __syncthreads();
+    const int limit = min(min(p.k_ref, 64) * p.k_chunk, MAX_SEL);
+    constexpr int kTaken = 1 << 30;
+    for (int q = 0; q < limit; ++q) {
       float bv = -INFINITY;
-      int bi = -1;
-      for (int r = threadIdx.x; r < nr; r += NT)
-        if (!ref_taken[r] && (bi < 0 || before(rscore[r], r, bv, bi))) {
-          bv = rscore[r];
-          bi = r;
+      int bi = -1, br = 0, bc = 0;
+      for (int i = threadIdx.x; i < nc; i += NT) {
+        const int r = cref[i];
+        if (r & kTaken) continue;
+        if (ref_taken[r] >= p.k_chunk || (rslot[r] < 0 && n_refs_picked >= p.k_ref)) continue;
+        const float v = cscore[i];
+        if (bi < 0 || v > bv || (v == bv && (r < br || (r == br && crank[i] < bc)))) {
+          bv = v;
+          bi = i;
+          br = r;
+          bc = crank[i];
         }
+      }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
         const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (oi >= 0 && (bi < 0 || before(ov, oi, bv, bi))) {
+        const int orr = __shfl_xor_sync(0xffffffffu, br, o);
+        const int oc = __shfl_xor_sync(0xffffffffu, bc, o);
+        if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && (orr < br || (orr == br && oc < bc))))) {
           bv = ov;
           bi = oi;
+          br = orr;
+          bc = oc;
         }
       }
       if (lane == 0) {
@@ -202,85 +225,152 @@ __global__ void __launch_bounds__(NT) route_kernel(RouteParams p) {
       }
       __syncthreads();
       if (threadIdx.x == 0) {
-        float v = red_v[0];
-        int i = red_i[0];
-        for (int w = 1; w < nwarps; ++w)
-          if (red_i[w] >= 0 && (i < 0 || before(red_v[w], red_i[w], v, i))) {
-            v = red_v[w];
-            i = red_i[w];
+        int i = -1;
+        float v = -INFINITY;
+        for (int w = 0; w < nwarps; ++w) {
+          const int wi = red_i[w];
+          if (wi < 0) continue;
+          const float wv = red_v[w];
+          if (i < 0 || wv > v ||
+              (wv == v && (cref[wi] < cref[i] || (cref[wi] == cref[i] && crank[wi] < crank[i])))) {
+            v = wv;
+            i = wi;
           }
-        top_ref[j] = i;
-        ref_taken[i] = 1;
-      }
-      __syncthreads();
-    }
-  }
-  __syncthreads();
-  // 4b. items per selected URI, their offsets, and each URI's best chunk
-  if (threadIdx.x == 0) {
-    int acc = 0;
-    for (int j = 0; j < kr; ++j) {
-      const int r = top_ref[j];
-      const int len = p.ref_pos_off[r0 + r + 1] - p.ref_pos_off[r0 + r];
-      ref_base[j] = acc;
-      acc += p.full_reference ? len : min(p.k_chunk, len);
-    }
-    ref_base[kr] = acc;
-    n_sel = min(acc, MAX_SEL);
-  }
-  __syncthreads();
-  for (int j = warp; j < kr; j += nwarps) {
-    const int r = top_ref[j];
-    const int a = p.ref_pos_off[r0 + r] - c0, z = p.ref_pos_off[r0 + r + 1] - c0;
-    if (p.full_reference) {
-      // best chunk of the URI (its score is carried by every expanded chunk)
-      float bv = -INFINITY;
-      int bi = -1, br = 0;
-      for (int i = a + lane; i < z; i += 32)
-        if (bi < 0 || before(cscore[i], crank[i], bv, br)) {
-          bv = cscore[i];
-          bi = i;
-          br = crank[i];
         }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        const int orr = __shfl_xor_sync(0xffffffffu, br, o);
-        if (oi >= 0 && (bi < 0 || before(ov, orr, bv, br))) {
-          bv = ov;
-          bi = oi;
-          br = orr;
-        }
-      }
-      if (lane == 0) ref_first[j] = bi;
-      __syncwarp();
-      for (int i = a + lane; i < z; i += 32) {
-        const int q = ref_base[j] + (i - a);
-        if (q >= MAX_SEL) continue;
-        it_pos[q] = i;
-        it_rrank[q] = j + 1;
-        it_crank[q] = i - a + 1;
-        it_rscore[q] = rscore[r];
-        it_cscore[q] = cscore[bi];
-      }
-    } else {
-      const int kc = min(p.k_chunk, z - a);
-      for (int i = a + lane; i < z; i += 32) {
-        int rank = 0;
-        for (int o = a; o < z; ++o) rank += before(cscore[o], crank[o], cscore[i], crank[i]) ? 1 : 0;
-        const int q = ref_base[j] + rank;
-        if (rank < kc && q < MAX_SEL) {
+        if (i >= 0) {
+          const int r = cref[i];
+          if (rslot[r] < 0) rslot[r] = n_refs_picked++;
+          ref_taken[r] += 1;
           it_pos[q] = i;
-          it_rrank[q] = j + 1;
-          it_crank[q] = rank + 1;
+          it_rrank[q] = rslot[r] + 1;
+          it_crank[q] = ref_taken[r];
           it_rscore[q] = rscore[r];
           it_cscore[q] = cscore[i];
+          cref[i] = r | kTaken;
+          n_sel = q + 1;
+        }
+        red_i[0] = i;  // broadcast "found"
+      }
+      __syncthreads();
+      const bool found = red_i[0] >= 0;
+      __syncthreads();
+      if (!found) break;
+    }
+  } else {
+    // 4a. top URIs under (-score, uri rank): rank counting when every ref has its own
+    // thread, otherwise repeated block argmax
+    const int kr = min(min(p.k_ref, nr), 64);
+    if (nr <= NT) {
+      if (threadIdx.x < nr) {
+        const int r = threadIdx.x;
+        int rank = 0;
+        for (int o = 0; o < nr; ++o) rank += before(rscore[o], o, rscore[r], r) ? 1 : 0;
+        if (rank < kr) top_ref[rank] = r;
+      }
+    } else {
+      for (int j = 0; j < kr; ++j) {
+        float bv = -INFINITY;
+        int bi = -1;
+        for (int r = threadIdx.x; r < nr; r += NT)
+          if (!ref_taken[r] && (bi < 0 || before(rscore[r], r, bv, bi))) {
+            bv = rscore[r];
+            bi = r;
+          }
+  #pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (oi >= 0 && (bi < 0 || before(ov, oi, bv, bi))) {
+            bv = ov;
+            bi = oi;
+          }
+        }
+        if (lane == 0) {
+          red_v[warp] = bv;
+          red_i[warp] = bi;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+          float v = red_v[0];
+          int i = red_i[0];
+          for (int w = 1; w < nwarps; ++w)
+            if (red_i[w] >= 0 && (i < 0 || before(red_v[w], red_i[w], v, i))) {
+              v = red_v[w];
+              i = red_i[w];
+            }
+          top_ref[j] = i;
+          ref_taken[i] = 1;
+        }
+        __syncthreads();
+      }
+    }
+    __syncthreads();
+    // 4b. items per selected URI, their offsets, and each URI's best chunk
+    if (threadIdx.x == 0) {
+      int acc = 0;
+      for (int j = 0; j < kr; ++j) {
+        const int r = top_ref[j];
+        const int len = p.ref_pos_off[r0 + r + 1] - p.ref_pos_off[r0 + r];
+        ref_base[j] = acc;
+        acc += p.full_reference ? len : min(p.k_chunk, len);
+      }
+      ref_base[kr] = acc;
+      n_sel = min(acc, MAX_SEL);
+    }
+    __syncthreads();
+    for (int j = warp; j < kr; j += nwarps) {
+      const int r = top_ref[j];
+      const int a = p.ref_pos_off[r0 + r] - c0, z = p.ref_pos_off[r0 + r + 1] - c0;
+      if (p.full_reference) {
+        // best chunk of the URI (its score is carried by every expanded chunk)
+        float bv = -INFINITY;
+        int bi = -1, br = 0;
+        for (int i = a + lane; i < z; i += 32)
+          if (bi < 0 || before(cscore[i], crank[i], bv, br)) {
+            bv = cscore[i];
+            bi = i;
+            br = crank[i];
+          }
+  #pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          const int orr = __shfl_xor_sync(0xffffffffu, br, o);
+          if (oi >= 0 && (bi < 0 || before(ov, orr, bv, br))) {
+            bv = ov;
+            bi = oi;
+            br = orr;
+          }
+        }
+        if (lane == 0) ref_first[j] = bi;
+        __syncwarp();
+        for (int i = a + lane; i < z; i += 32) {
+          const int q = ref_base[j] + (i - a);
+          if (q >= MAX_SEL) continue;
+          it_pos[q] = i;
+          it_rrank[q] = j + 1;
+          it_crank[q] = i - a + 1;
+          it_rscore[q] = rscore[r];
+          it_cscore[q] = cscore[bi];
+        }
+      } else {
+        const int kc = min(p.k_chunk, z - a);
+        for (int i = a + lane; i < z; i += 32) {
+          int rank = 0;
+          for (int o = a; o < z; ++o) rank += before(cscore[o], crank[o], cscore[i], crank[i]) ? 1 : 0;
+          const int q = ref_base[j] + rank;
+          if (rank < kc && q < MAX_SEL) {
+            it_pos[q] = i;
+            it_rrank[q] = j + 1;
+            it_crank[q] = rank + 1;
+            it_rscore[q] = rscore[r];
+            it_cscore[q] = cscore[i];
+          }
         }
       }
     }
+    __syncthreads();
   }
-  __syncthreads();
   const int count = n_sel;
   // item attributes (threshold, namespace order, source span)
   for (int q = threadIdx.x; q < count; q += NT) {
@@ -408,8 +498,8 @@ cudaError_t pra_route(const RouteParams& p, cudaStream_t st) {
   if (p.B == 0) return cudaSuccess;
   if (p.G > 8) return cudaErrorInvalidValue;
   if (p.D % 4 != 0 || (reinterpret_cast<uintptr_t>(p.gists) & 15)) return cudaErrorInvalidValue;
-  const size_t smem = (size_t)p.D * sizeof(float) + (size_t)MAX_ROW_CHUNKS * (2 * sizeof(float) + 2 * sizeof(int)) +
-                      (size_t)MAX_ROW_REFS * (sizeof(float) + sizeof(int));
+  const size_t smem = (size_t)p.D * sizeof(float) + (size_t)MAX_ROW_CHUNKS * (2 * sizeof(float) + 3 * sizeof(int)) +
+                      (size_t)MAX_ROW_REFS * (sizeof(float) + 2 * sizeof(int));
   PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(route_kernel), (int)smem));
   route_kernel<<<p.B, NT, smem, st>>>(p);
   return cudaGetLastError();

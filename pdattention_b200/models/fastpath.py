@@ -31,6 +31,7 @@ import os
 import time
 from dataclasses import dataclass, field
 
+import numpy as np
 import torch
 
 from ..chunking import partition_reference_tokens
@@ -77,13 +78,15 @@ def unsupported_reason(cfg) -> str | None:
     Philox streams; PRA blocks have no dropout (``src/pra_torch/model.py:31-167``)."""
     head_dim = cfg.d_model // cfg.n_heads
     checks = [
-        (cfg.search_strategy != "hierarchical", f"search_strategy={cfg.search_strategy}"),
+        (cfg.search_strategy not in ("hierarchical", "global_chunks"), f"search_strategy={cfg.search_strategy}"),
+        (cfg.search_strategy == "global_chunks" and cfg.detail_materialization == "full_reference",
+         "global_chunks with full-reference expansion"),
         (cfg.routing_backend != "tensorized", "legacy routing backend"),
         (cfg.use_summary, "summary routing"),
         (cfg.cache_build_mode != "detached", "trainable gists"),
         (cfg.reference_encoding_strategy != "independent", "grouped encoding"),
         (cfg.encoding_chunking is not None, "bounded encoding"),
-        (cfg.gist_mode not in {"mean", "kmeans"}, f"gist_mode={cfg.gist_mode}"),
+        (cfg.gist_mode not in {"mean", "kmeans", "last", "ref_end"}, f"gist_mode={cfg.gist_mode}"),
         (cfg.gist_mode == "kmeans" and cfg.gist_kmeans_empty_cluster_policy == "error",
          "k-means error-on-empty-cluster policy"),
         (cfg.reference_level_gist_mode is not None, "URI-level gists"),
@@ -695,7 +698,8 @@ class DeviceRuntime:
                     _AGG[cfg.reference_score_aggregation], float(cfg.trigger_threshold), scalar_budget,
                     float(cfg.detail_materialization == "gist_only"),
                     float(cfg.detail_materialization == "full_reference"),
-                    float(cfg.overlap_materialization == "deduplicate"), max_sel, max(scalar_budget, 1)]
+                    float(cfg.overlap_materialization == "deduplicate"), max_sel, max(scalar_budget, 1),
+                    float(cfg.search_strategy == "global_chunks")]
         return settings, budget_rows
 
     def _stack_weights(self) -> list[torch.Tensor]:
@@ -752,7 +756,7 @@ class DeviceRuntime:
             ns.pos_chunk, ns.pos_ref, ns.pos_rank, memory.chunk_start, memory.chunk_len, memory.chunk_pool_row,
             int(settings[0]), int(settings[1]), int(settings[2]), int(settings[3]), settings[4], int(settings[5]),
             gist_only, bool(settings[7]), bool(settings[8]), int(settings[9]), int(settings[10]), budget_rows,
-            query_rows)
+            query_rows, bool(settings[11]))
         self.last_routing[li] = LayerRouting(mem_idx, ints, sel_i, sel_f)
         if gist_only:
             gk = memory.gist_k[li].view(-1, d).bfloat16()
@@ -996,6 +1000,8 @@ class DeviceRuntime:
             chunk_tables = (view("chunk_start"), view("chunk_len"), view("chunk_pool_row"))
             prompt_ns = ([view(f"ns{i}") for i in range(6)], bool(pt["ns_empty"]))
         memory = BatchMemory(self, entries, chunks, rows, seq_len, self.device, chunk_tables, prompt_ns)
+        if self.cfg.gist_mode in ("last", "ref_end"):
+            self._single_gist_rows(plan, tokenizer)
         out = getattr(plan, "out", None)
         tokens = int(out["chunk_token_off"][-1]) if out is not None and len(out["chunk_token_off"]) else \
             sum(len(c.token_ids) for c in chunks)
@@ -1011,6 +1017,42 @@ class DeviceRuntime:
             self._move_pool_to_host(memory)
         self.last_memory = memory
         return memory, caches, builders
+
+    def _single_gist_rows(self, plan, tokenizer) -> None:
+        """``last`` / ``ref_end`` gists (``src/pra_torch/gists/single.py``): a chunk's gist is the
+        key (and value) of one of its tokens -- the last one, or the reference terminator, which
+        must occur exactly once in the chunk.  Each wave gets the pool row of that token and a
+        length of one, so the mean-gist kernel reads exactly that row."""
+        cfg = self.cfg
+        marker = None
+        if cfg.gist_mode == "ref_end":
+            ids = list(tokenizer.encode(cfg.ref_end_token))
+            if len(ids) != 1:
+                raise ValueError(f"Reference terminator {cfg.ref_end_token!r} is not one atomic token.")
+            marker = ids[0]
+        packed, L = plan.packed, plan.seq_len
+        for table in plan.wave_tables:
+            if not table.get("n", table["lens"][2]):
+                continue
+
+            def host(name):
+                off, _, count = table[name]
+                return np.asarray(packed[off: off + count], dtype=np.int64)
+
+            rows, lens = host("gist_rows"), host("lens")
+            if marker is None:
+                pick = np.maximum(lens - 1, 0)
+            else:
+                off = table["ids"][0]
+                ids = np.asarray(packed[off: off + lens.size * L]).reshape(lens.size, L)
+                hit = (ids == marker) & (np.arange(L)[None, :] < lens[:, None])
+                counts = hit.sum(axis=1)
+                if (counts[lens > 0] != 1).any():
+                    bad = int(counts[lens > 0][counts[lens > 0] != 1][0])
+                    raise ValueError(f"Expected exactly one {cfg.ref_end_token!r} token, found {bad}.")
+                pick = hit.argmax(axis=1)
+            arr = np.stack([rows + pick, np.minimum(lens, 1)]).astype(np.int32)
+            table["_single_gist"] = torch.from_numpy(arr).to(self.device, non_blocking=True)
 
     def _move_pool_to_host(self, memory: "BatchMemory") -> None:
         """CPU-resident K/V (``kv_cache_residency="cpu"``, ``src/pra_torch/model.py:473-482``): the
@@ -1072,7 +1114,9 @@ class DeviceRuntime:
             sel = slice(layer, layer + 1)
             pk, pv, gk, gv, gn, gc = pk[sel], pv[sel], gk[sel], gv[sel], gn[sel], gc[sel]
         start, length, dest = view("gist_rows"), view("lens"), view("dest")
-        if cfg.gist_mode == "mean":
+        if cfg.gist_mode in ("last", "ref_end"):  # the mean over one picked row is that row
+            start, length = table["_single_gist"][0], table["_single_gist"][1]
+        if cfg.gist_mode in ("mean", "last", "ref_end"):
             ext.gist_mean_into(pk, pv, start, length, dest, gk, gv, gn, gc)
             return
         ext.gist_kmeans_into(pk, pv, start, length, dest, gk, gv, gn, gc, table["max_len"], cfg.gist_kmeans_max_iters,

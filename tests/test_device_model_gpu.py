@@ -213,3 +213,85 @@ def test_cpu_resident_kv_tier_matches_gpu_residency(cuda, tmp_path):
     assert l_cpu == l_gpu
     assert torch.equal(g_cpu, g_gpu)
     assert m_cpu["gpu_cached_kv_bytes"] == 0 and m_cpu["cached_kv_bytes"] == m_gpu["cached_kv_bytes"] > 0
+
+
+@pytest.mark.parametrize("mode", ["last", "ref_end"])
+def test_single_token_gists_match_object_path(cuda, tmp_path, mode):
+    """``last`` / ``ref_end`` gists: a chunk's gist is one token's key (the last one, or the single
+    reference terminator); device logits and per-layer selections against the object path."""
+    import json
+
+    from pdattention_b200.data import PRADataModule, WordIdTokenizer
+    from pdattention_b200.data.generators import generate_hierarchical_tokens
+
+    root = Path(tmp_path)
+    stage = generate_hierarchical_tokens(root / "synthetic_hierarchical_tokens", examples=4, doc_tokens=40,
+                                         prompt_tokens=95, vocab=500, roots=2, children=1, grandchildren=2)
+    docs = [json.loads(line) for line in (stage / "documents.jsonl").read_text().splitlines() if line.strip()]
+    with (stage / "documents.jsonl").open("w") as fh:
+        for doc in docs:  # the terminator mid-document, so "ref_end" and "last" pick different tokens
+            words = doc["text"].split()
+            doc["text"] = " ".join(words[:7] + ["<REF_END>"] + words[7:])
+            fh.write(json.dumps(doc) + "\n")
+    tok = WordIdTokenizer(500)
+    dm = PRADataModule("synthetic_hierarchical_tokens", str(root), batch_size=4, max_seq_len=256, tokenizer=tok,
+                       shuffle=False).load()
+    batch = next(iter(dm._loader(dm.dataset, shuffle=False)))
+    cfg = tiny_config(tok.vocab_size)
+    cfg.gist_mode, cfg.gists_per_chunk, cfg.chunking_mode = mode, 1, "none"
+    torch.manual_seed(23)
+    reference = TinyPRAModel(copy.deepcopy(cfg)).to(cuda).eval()
+    device_model = TinyPRAModel(copy.deepcopy(cfg)).to(cuda)
+    device_model.load_state_dict(reference.state_dict())
+    attach_device_runtime(device_model)
+    rt = device_model._device_runtime
+    assert rt is not None
+    with torch.no_grad():
+        _, ref_out = _pra_batch_step(reference, batch, "cuda", tok, ResolverServiceConfig(), None)
+        _, dev_out = _pra_batch_step(device_model, batch, "cuda", tok, ResolverServiceConfig(), None)
+    b, t = batch["input_ids"].shape
+    dev_logits = rt.logits(dev_out["hidden"], b, t).float()
+    ref_logits = ref_out["logits"].float()
+    valid = batch["attention_mask"].bool().to(cuda)
+    err = (dev_logits - ref_logits).abs()[valid]
+    assert err.max() <= 0.05 * ref_logits.abs()[valid].max(), err.max()
+    memory = dev_out["memory"]
+    expected = reference.selected_chunks_by_layer()
+    routing = rt.last_routing[0]
+    for row in range(b):
+        count = int(routing.ints[1, row])
+        got = sorted(memory.chunks[int(c)].chunk_id for c in routing.sel_i[0, row, :count].tolist())
+        assert got == sorted(hit.chunk_id for hit in expected[0][row])
+
+
+def test_global_chunk_search_matches_object_path(cuda, tmp_path):
+    """search_strategy="global_chunks": one ranking of every chunk under the distinct-URI and
+    per-URI limits (route kernel) against the object path's selections and logits."""
+    torch.manual_seed(24)
+    tok, batch = tiny_batch(Path(tmp_path))
+    cfg = tiny_config(tok.vocab_size)
+    cfg.search_strategy, cfg.top_k_references, cfg.top_k_chunks_per_reference = "global_chunks", 2, 2
+    reference = TinyPRAModel(copy.deepcopy(cfg)).to(cuda).eval()
+    device_model = TinyPRAModel(copy.deepcopy(cfg)).to(cuda)
+    device_model.load_state_dict(reference.state_dict())
+    attach_device_runtime(device_model)
+    rt = device_model._device_runtime
+    assert rt is not None
+    with torch.no_grad():
+        _, ref_out = _pra_batch_step(reference, batch, "cuda", tok, ResolverServiceConfig(), None)
+        _, dev_out = _pra_batch_step(device_model, batch, "cuda", tok, ResolverServiceConfig(), None)
+    b, t = batch["input_ids"].shape
+    dev_logits = rt.logits(dev_out["hidden"], b, t).float()
+    ref_logits = ref_out["logits"].float()
+    valid = batch["attention_mask"].bool().to(cuda)
+    err = (dev_logits - ref_logits).abs()[valid]
+    assert err.max() <= 0.05 * ref_logits.abs()[valid].max(), err.max()
+    memory = dev_out["memory"]
+    expected = reference.selected_chunks_by_layer()
+    routing = rt.last_routing[0]
+    for row in range(b):
+        count = int(routing.ints[1, row])
+        got = [memory.chunks[int(c)].chunk_id for c in routing.sel_i[0, row, :count].tolist()]
+        want = [hit.chunk_id for hit in expected[0][row]]
+        assert sorted(got) == sorted(want), (row, got, want)
+        assert len({c.split("#")[0] for c in got}) <= 2
