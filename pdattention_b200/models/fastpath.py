@@ -563,6 +563,7 @@ class DeviceRuntime:
         return rt
 
     grad_hooks = None  # optional: before_stack() / after_layer(l) calls during the backward
+    route_timer = None  # optional list: (start, end) CUDA events around each per-layer routing launch
 
     def grad_views(self) -> list[torch.Tensor]:
         """Every tensor that aliases the flat gradient buffer."""
@@ -751,12 +752,18 @@ class DeviceRuntime:
         gist_only = bool(settings[6])
         if query_rows is None:
             query_rows = torch.full((qkv3.shape[0],), qkv3.shape[1] - 1, dtype=torch.int32, device=qkv3.device)
+        timer = self.route_timer
+        if timer is not None:  # device time of each routing launch (systems benchmarks)
+            timer.append((torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)))
+            timer[-1][0].record()
         mem_idx, ints, sel_i, sel_f = _ext.require().route(
             qkv3[:, :, :d], memory.gists[li], memory.gist_count[li], ns.row_pos_off, ns.row_ref_off, ns.ref_pos_off,
             ns.pos_chunk, ns.pos_ref, ns.pos_rank, memory.chunk_start, memory.chunk_len, memory.chunk_pool_row,
             int(settings[0]), int(settings[1]), int(settings[2]), int(settings[3]), settings[4], int(settings[5]),
             gist_only, bool(settings[7]), bool(settings[8]), int(settings[9]), int(settings[10]), budget_rows,
             query_rows, bool(settings[11]))
+        if timer is not None:
+            timer[-1][1].record()
         self.last_routing[li] = LayerRouting(mem_idx, ints, sel_i, sel_f)
         if gist_only:
             gk = memory.gist_k[li].view(-1, d).bfloat16()
