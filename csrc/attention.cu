@@ -616,6 +616,7 @@ cudaError_t pra_attention_fwd(const AttnParams& p, int head_dim, cudaStream_t st
     if (e != cudaErrorNotSupported) return e;
   }
   switch (head_dim) {
+    case 16: return launch_fwd<16>(p, st);
     case 32: return launch_fwd<32>(p, st);
     case 64: return launch_fwd<64>(p, st);
     case 128: return launch_fwd<128>(p, st);
@@ -627,6 +628,7 @@ cudaError_t pra_attention_bwd(const AttnParams& p, int head_dim, cudaStream_t st
   using namespace pra::attn;
   if (p.B * p.T == 0) return cudaSuccess;
   switch (head_dim) {
+    case 16: return launch_bwd<16>(p, st);
     case 32: return launch_bwd<32>(p, st);
     case 64: return launch_bwd<64>(p, st);
     case 128: return launch_bwd<128>(p, st);

@@ -860,6 +860,7 @@ std::vector<torch::Tensor> decode_attention(torch::Tensor q, int64_t heads, int6
     p.mem_max = mem_idx->size(1);
     p.mem_len = ptr<const int>(*mem_len);
     p.mem_rows = mem_k->size(0);
+    p.mem_on_device = mem_k->is_cuda() ? 1 : 0;
   }
   if (loc_k.has_value() && loc_k->numel() > 0) {
     TORCH_CHECK(loc_k->dim() == 3 && loc_k->stride(2) == 1 && loc_v->strides() == loc_k->strides(),
@@ -952,6 +953,70 @@ std::vector<torch::Tensor> route_topk(torch::Tensor scores, torch::Tensor query,
   a.mem_len = ptr<int>(mem_len);
   a.sel_out = ptr<int>(sel);
   check(pra_route_topk(a, stream()), "route_topk");
+  return {mem_idx, mem_len, sel};
+}
+
+// Local exact top-k with the cross-GPU candidate exchange and merge fused in (one kernel, one
+// segment per row).  Returns {mem_idx [B, mem_max], mem_len [B], selected chunk ids [B, k]}.
+std::vector<torch::Tensor> route_topk_exchange(torch::Tensor scores, torch::Tensor query, torch::Tensor gists,
+                                               torch::Tensor ns_start, torch::Tensor ns_end, int64_t k, int64_t k_cand,
+                                               int64_t budget, int64_t mem_max, int64_t id_offset,
+                                               int64_t gists_per_chunk, std::vector<int64_t> recv,
+                                               std::vector<int64_t> flags, torch::Tensor epochs, int64_t rank,
+                                               int64_t B_max, torch::Tensor global_len, torch::Tensor global_row0,
+                                               int64_t max_spins, torch::Tensor error, int64_t pool_rows) {
+  c10::cuda::CUDAGuard guard(scores.device());
+  expect(scores, at::kFloat, "scores");
+  expect(query, at::kFloat, "query");
+  expect(gists, at::kFloat, "gists");
+  TORCH_CHECK(scores.dim() == 2 && scores.stride(1) == 1 && query.stride(-1) == 1 && gists.is_contiguous(),
+              "route_topk_exchange layouts");
+  TORCH_CHECK(recv.size() == flags.size() && recv.size() >= 2 && recv.size() <= (size_t)TP_MAX_RANKS,
+              "one receive buffer and one flag array per rank");
+  TORCH_CHECK(epochs.scalar_type() == at::kInt && error.scalar_type() == at::kInt, "int32 epochs / error");
+  RouteTopkArgs a{};
+  a.B = scores.size(0);
+  a.D = gists.size(-1);
+  a.G = gists_per_chunk;
+  a.segments = 1;
+  a.scores = ptr<const float>(scores);
+  a.score_stride = scores.stride(0);
+  a.query = ptr<const float>(query);
+  a.query_stride = query.stride(0);
+  a.gists = ptr<const float>(gists);
+  a.ns_start = ptr<const int>(ns_start);
+  a.ns_end = ptr<const int>(ns_end);
+  a.chunk_len = ptr<const int>(global_len);
+  a.chunk_row0 = ptr<const int>(global_row0);
+  a.k = k;
+  a.k_cand = k_cand;
+  a.budget = budget;
+  a.id_offset = id_offset;
+  a.n_chunks = scores.size(1) / std::max<int64_t>(gists_per_chunk, 1);
+  a.pool_rows = pool_rows;
+  a.bounds = bounds_word(scores.device());
+  auto io = scores.options().dtype(at::kInt);
+  auto mem_idx = torch::empty({a.B, std::max<int64_t>(mem_max, 1)}, io);
+  auto mem_len = torch::empty({a.B}, io);
+  auto sel = torch::empty({a.B, std::max<int64_t>(k, 1)}, io);
+  a.mem_idx = ptr<int>(mem_idx);
+  a.mem_max = std::max<int64_t>(mem_max, 1);
+  a.mem_len = ptr<int>(mem_len);
+  a.sel_out = ptr<int>(sel);
+  RouteExchangeArgs x{};
+  x.world = recv.size();
+  for (int p = 0; p < x.world; ++p) {
+    x.recv[p] = reinterpret_cast<float*>(recv[p]);
+    x.flags[p] = reinterpret_cast<uint32_t*>(flags[p]);
+  }
+  x.epochs = reinterpret_cast<uint32_t*>(epochs.data_ptr());
+  x.rank = rank;
+  x.B_max = B_max;
+  x.global_len = ptr<const int>(global_len);
+  x.global_row0 = ptr<const int>(global_row0);
+  x.max_spins = max_spins;
+  x.error = ptr<int>(error);
+  check(pra_route_topk_exchange(a, x, stream()), "route_topk_exchange");
   return {mem_idx, mem_len, sel};
 }
 
@@ -1451,7 +1516,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("route_merge", &route_merge, py::arg("cands"), py::arg("world"), py::arg("k"), py::arg("budget"),
         py::arg("chunk_len"), py::arg("chunk_row0"), py::arg("mem_max"), py::arg("local"),
         py::arg("pool_rows") = -1);
+  m.def("route_topk_exchange", &route_topk_exchange);
   m.def("set_bounds_check", &set_bounds_check);
+  m.def("decode_set_tma", [](bool on) { pra_decode_set_tma(on ? 1 : 0); });
   m.def("bounds_check_enabled", &bounds_check_enabled);
   m.def("bounds_status", &bounds_status);
   m.def("bounds_reset", &bounds_reset);

@@ -139,6 +139,21 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
 }
 
+// TMA: arm `bar` for `bytes` of incoming copies (one arrival).
+__device__ __forceinline__ void expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// 2-D tile copy of this GPU's global memory into this CTA's shared memory, completing on `bar`
+// (no cluster, no multicast); x = the column element (16-byte aligned), y = the row.
+__device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Philox4x32-10 (Salmon, Moraes, Dror, Shaw: "Parallel Random Numbers: As Easy as 1, 2, 3",
 // SC 2011): ten rounds of two 32x32->64-bit products mixed into the counter, the key bumped
 // by the Weyl constants between rounds.
@@ -217,3 +232,8 @@ __device__ __forceinline__ bool mbar_try_wait_parity(uint64_t* bar, uint32_t par
 }
 
 }  // namespace pra
+
+// Tensor map of a [rows, cols] bf16 matrix (row stride ld elements, 16-byte aligned) cut into
+// 64-column x box_rows boxes in the 128-byte swizzle layout; cached per (address, shape);
+// nullptr when the driver rejects it.  Defined in decode_gemm.cu.
+const CUtensorMap* pra_tile_map_bf16(const void* ptr, int64_t cols, int64_t rows, int64_t ld, int box_rows);

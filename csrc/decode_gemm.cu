@@ -59,20 +59,6 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
                : "memory");
 }
 
-__device__ __forceinline__ void expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-
-// 2-D tile copy of this GPU's global memory into this CTA's shared memory, completing on `bar`
-// (no cluster, no multicast); x = the K element (a multiple of 64), y = the row.
-__device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
-          smem_u32(dst)),
-      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-
 // Shared-memory descriptor of a K-major bf16 tile in the 128-byte swizzle layout TMA writes:
 // rows of 128 bytes (64 K elements) in 1024-byte atoms of 8 rows (SBO = 1024); the K offset
 // within the atom moves the start address by 32 bytes per 16 elements.
@@ -362,7 +348,9 @@ struct MapKeyHash {
   }
 };
 
-const CUtensorMap* tile_map(const void* ptr, int64_t cols, int64_t rows, int64_t ld, int box_rows) {
+}  // namespace
+
+const CUtensorMap* pra_tile_map_bf16(const void* ptr, int64_t cols, int64_t rows, int64_t ld, int box_rows) {
   static std::mutex mutex;
   static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
   const MapKey key{ptr, cols, rows, ld, box_rows};
@@ -381,8 +369,6 @@ const CUtensorMap* tile_map(const void* ptr, int64_t cols, int64_t rows, int64_t
     return nullptr;
   return &cache.emplace(key, map).first->second;
 }
-
-}  // namespace
 
 size_t pra_decode_gemm_workspace_floats() { return (size_t)DG_MAX_TILES * pra::dg::BF * pra::dg::MT; }
 
@@ -411,8 +397,8 @@ cudaError_t pra_decode_gemm(const DecodeGemmArgs& a, cudaStream_t st) {
     configured[dev] = 1;
   }
   if ((reinterpret_cast<uintptr_t>(a.w) | reinterpret_cast<uintptr_t>(a.x)) & 15) return cudaErrorInvalidValue;
-  const CUtensorMap* map_w = tile_map(a.w, a.K, a.N, a.K, BF);
-  const CUtensorMap* map_x = tile_map(a.x, a.K, a.M, a.ldx, MT);
+  const CUtensorMap* map_w = pra_tile_map_bf16(a.w, a.K, a.N, a.K, BF);
+  const CUtensorMap* map_x = pra_tile_map_bf16(a.x, a.K, a.M, a.ldx, MT);
   if (map_w == nullptr || map_x == nullptr) return cudaErrorInvalidValue;
   DecodeGemmArgs b = a;
   b.splits = splits;

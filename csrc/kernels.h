@@ -275,11 +275,15 @@ struct DecodeAttnParams {
   int64_t out_row;
   float* export_o;             // [B, H, Dh] merged unnormalised output, or null
   float* export_ml;            // [B, H, 2] merged (max, sum), or null
-  int64_t mem_rows;            // rows of the memory pool (bounds-checked variant)
-  int loc_cap;                 // local cache capacity per row (bounds-checked variant)
+  int64_t mem_rows;            // rows of the memory pool (bounds-checked variant, TMA maps)
+  int loc_cap;                 // local cache capacity per row (bounds-checked variant, TMA maps)
   BoundsStatus* bounds;        // non-null: run the bounds-checked variant
+  int mem_on_device;           // the memory pool is device memory (TMA-fed kernel allowed)
+  int* status;                 // optional: set to 1 by a CTA that gave up on a bounded wait
 };
 cudaError_t pra_decode_attention(const DecodeAttnParams& p, int head_dim, cudaStream_t stream);
+// 1 (default): eligible decode attention calls run the TMA-fed kernel; 0: the cp.async kernel.
+void pra_decode_set_tma(int on);
 
 struct RouteTopkArgs {
   int B, D;
@@ -334,6 +338,24 @@ cudaError_t pra_combine_partials(const float* parts, int B, int world, int H, in
 // ---- tensor-parallel collectives over peer memory (tp_comm.cu) -------------------------
 constexpr int TP_MAX_RANKS = 8;
 constexpr int TP_MAX_BLOCKS = 296;  // signal slots per rank: TP_MAX_BLOCKS * world
+// Cross-GPU candidate exchange fused into the routing kernel (chunk-sharded memory, one
+// segment per row): each row's local exact top-k goes into every rank's receive buffer over
+// NVLink (plain peer stores), a per-row flag carrying the call epoch is raised on every rank,
+// and once every rank's candidates of that row have landed (bounded wait) the same CTA merges
+// them into the selection and the memory row list.  Receive halves alternate with the call
+// parity, so a rank one call ahead never overwrites candidates a peer is still reading.
+struct RouteExchangeArgs {
+  float* recv[TP_MAX_RANKS];      // every rank's [2][B_max][world][2k] receive buffer
+  uint32_t* flags[TP_MAX_RANKS];  // every rank's [B_max][world] flags
+  uint32_t* epochs;               // local [B_max] per-row call counters (start at 0)
+  int rank, world, B_max;
+  const int* global_len;          // [C] every chunk's length (global ids)
+  const int* global_row0;         // [C] first pool row of every chunk
+  long long max_spins;
+  int* error;                     // local flag: 1 when a wait gave up
+};
+cudaError_t pra_route_topk_exchange(const RouteTopkArgs& args, const RouteExchangeArgs& x, cudaStream_t stream);
+
 struct TpAllreduceArgs {
   const __nv_bfloat16* part[TP_MAX_RANKS];  // every rank's partial (peer addresses)
   const __nv_bfloat16* residual;            // local [n] or null

@@ -18,6 +18,7 @@
 #include <climits>
 
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace pra {
 namespace llama {
@@ -264,6 +265,271 @@ __global__ void __launch_bounds__(DT) decode_kernel(DecodeAttnParams p) {
   }
 }
 
+// ---------------------------------------------------------------- decode attention, TMA-fed
+// The same split-K GQA flash decoding as decode_kernel, with the key / value blocks brought in
+// by the tensor-memory accelerator: a 64-key block of one KV head is a 64-row x D-column box of
+// the local cache or of the memory pool (a selected chunk is 64 consecutive pool rows), so one
+// thread issues 2 * D / 64 tile copies per block against an mbarrier instead of every thread
+// issuing 16-byte copies and resolving row addresses.  Blocks whose memory rows are not one
+// contiguous run (partial chunks, or a block straddling memory and local keys) are gathered
+// with cp.async into the same 128-byte-swizzled layout.  The tiles are read with ldmatrix at
+// swizzled addresses; scores, softmax and the warp merge are decode_kernel's.
+constexpr int TST = 3;           // pipeline stages (blocks in flight per CTA)
+constexpr int TBOX = 64 * 64 * 2;  // one 64-key x 64-column bf16 box (8 KB, 128-byte rows)
+constexpr int TMAX_BLOCKS = 64;  // split_keys <= 4096
+constexpr long long TWAIT_CYCLES = 4000000000LL;  // about two seconds at the boost clock
+
+template <int D>
+struct TLayout {
+  static constexpr int NBOX = D / 64;
+  static constexpr int TILE = NBOX * TBOX;  // K (or V) tile of one block
+  static constexpr int STAGE = 2 * TILE;
+  static constexpr int QLD = D + 8;
+};
+
+// Byte offset of (row r, column c) of a swizzled 64-row tile: 64-column boxes of 128-byte rows,
+// 16-byte chunk k of row r stored at chunk k ^ (r % 8).
+__device__ __forceinline__ uint32_t sw_off(int r, int c) {
+  return (uint32_t)((c >> 6) * TBOX + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4) + ((c & 7) << 1));
+}
+
+template <int D>
+__global__ void __launch_bounds__(DT) decode_tma_kernel(const __grid_constant__ CUtensorMap map_mk,
+                                                        const __grid_constant__ CUtensorMap map_mv,
+                                                        const __grid_constant__ CUtensorMap map_lk,
+                                                        const __grid_constant__ CUtensorMap map_lv,
+                                                        DecodeAttnParams p) {
+  using Lay = TLayout<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __nv_bfloat16* sq = reinterpret_cast<__nv_bfloat16*>(stages + TST * Lay::STAGE);  // [16][QLD]
+  int* srow = reinterpret_cast<int*>(sq + 16 * Lay::QLD);                          // [split_keys]
+  int* blk_mode = srow + p.split_keys;   // per block: 0 TMA memory, 1 TMA local, 2 gathered
+  int* blk_y = blk_mode + TMAX_BLOCKS;   // TMA row coordinate
+  uint64_t* full = reinterpret_cast<uint64_t*>(blk_y + TMAX_BLOCKS);  // [TST] (8-byte aligned: even int count)
+  __shared__ int s_fail;
+  float* red = reinterpret_cast<float*>(stages);  // [4][16][D + 2], after the key loop
+
+  const int G = p.H / p.Hkv;
+  const int b = blockIdx.x / p.Hkv, kvh = blockIdx.x % p.Hkv;
+  const int split = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mem_len = p.mem_len ? p.mem_len[b] : 0;
+  const int total = mem_len + (p.loc_len ? p.loc_len[b] : 0);
+  const int k0 = split * p.split_keys, k1 = min(total, k0 + p.split_keys);
+  const int64_t part = ((int64_t)b * p.H + kvh * G) * p.n_split + split;
+  const int loc_rows = (int)(p.loc_batch / p.loc_row);  // cache rows per batch row
+
+  for (int c = threadIdx.x; c < 16 * (D / 8); c += DT) {
+    const int r = c / (D / 8), col = (c % (D / 8)) * 8;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < G) v = *reinterpret_cast<const uint4*>(p.q + (int64_t)b * p.q_row + (kvh * G + r) * D + col);
+    *reinterpret_cast<uint4*>(sq + r * Lay::QLD + col) = v;
+  }
+  for (int j = k0 + threadIdx.x; j < k1; j += DT)
+    srow[j - k0] = j < mem_len ? p.mem_idx[(int64_t)b * p.mem_max + j] : -(j - mem_len + 1);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TST; ++s) mbar_init(full + s, 1);
+    s_fail = 0;
+    tc::fence_mbarrier_init();
+  }
+  __syncthreads();
+  const int n_blocks = k1 > k0 ? (k1 - k0 + DBN - 1) / DBN : 0;
+  // classify the blocks (warp per block): one contiguous run of rows -> one TMA box per 64 columns
+  for (int blk = warp; blk < n_blocks; blk += DT / 32) {
+    const int j0 = k0 + blk * DBN, n = min(DBN, k1 - j0);
+    int mode = 2, y = 0;
+    if (j0 >= mem_len) {
+      mode = 1;
+      y = b * loc_rows + (j0 - mem_len);
+    } else if (j0 + n <= mem_len) {
+      const int r0 = srow[j0 - k0];
+      bool run = true;
+      for (int i = lane; i < n; i += 32) run = run && srow[j0 - k0 + i] == r0 + i;
+      run = __all_sync(0xffffffffu, run);
+      if (run) {
+        mode = 0;
+        y = r0;
+      }
+    }
+    if (lane == 0) {
+      blk_mode[blk] = mode;
+      blk_y[blk] = y;
+    }
+  }
+  __syncthreads();
+  auto key_addr = [&](int j, bool value) -> const __nv_bfloat16* {
+    const int r = srow[j - k0];
+    if (r >= 0) return (value ? p.mem_v : p.mem_k) + (int64_t)r * p.mem_row + kvh * D;
+    return (value ? p.loc_v : p.loc_k) + (int64_t)b * p.loc_batch + (int64_t)(-r - 1) * p.loc_row + kvh * D;
+  };
+  auto issue = [&](int blk, int buf) {
+    uint8_t* st = stages + buf * Lay::STAGE;
+    const int mode = blk_mode[blk];
+    if (mode < 2) {
+      if (threadIdx.x == 0) {
+        expect_tx(full + buf, Lay::STAGE);
+        const CUtensorMap* mk = mode == 0 ? &map_mk : &map_lk;
+        const CUtensorMap* mv = mode == 0 ? &map_mv : &map_lv;
+#pragma unroll
+        for (int bx = 0; bx < Lay::NBOX; ++bx) {
+          tma_load(st + bx * TBOX, mk, kvh * D + bx * 64, blk_y[blk], full + buf);
+          tma_load(st + Lay::TILE + bx * TBOX, mv, kvh * D + bx * 64, blk_y[blk], full + buf);
+        }
+      }
+    } else {
+      const int j0 = k0 + blk * DBN;
+      for (int c = threadIdx.x; c < DBN * (D / 8); c += DT) {
+        const int r = c / (D / 8), col = (c % (D / 8)) * 8;
+        const int j = j0 + r;
+        const bool ok = j < k1;
+        cp_async16(st + sw_off(r, col), ok ? key_addr(j, false) + col : p.q, ok);
+        cp_async16(st + Lay::TILE + sw_off(r, col), ok ? key_addr(j, true) + col : p.q, ok);
+      }
+    }
+    cp_async_commit();  // one group per block (empty for TMA blocks) keeps the wait counts uniform
+  };
+
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  const float sl2 = p.scale * LOG2E;
+  uint32_t phase = 0;  // bit s: parity the next TMA completion of stage s shows
+#pragma unroll
+  for (int st = 0; st < TST - 1; ++st) {
+    if (st < n_blocks) issue(st, st);
+    else cp_async_commit();
+  }
+  int it = 0;
+  for (; it < n_blocks; ++it) {
+    const int buf = it % TST;
+    cp_async_wait<TST - 2>();
+    if (blk_mode[it] < 2) {
+      if (!tc::mbar_wait_cycles(full + buf, (phase >> buf) & 1u, TWAIT_CYCLES)) s_fail = 1;
+      phase ^= 1u << buf;
+    }
+    __syncthreads();  // block `it` landed for every thread; every warp is done with block it - 1
+    if (s_fail) break;
+    if (it + TST - 1 < n_blocks) issue(it + TST - 1, (it + TST - 1) % TST);
+    else cp_async_commit();
+    const uint32_t kst = smem_u32(stages + buf * Lay::STAGE), vst = kst + Lay::TILE;
+    float s[2][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t a[4], bb[4];
+      ldmatrix_x4(a, smem_u32(sq + (lane & 15) * Lay::QLD + kk * 16 + (lane >> 4) * 8));
+      const int row = warp * 16 + ((lane >> 4) & 1) * 8 + (lane & 7);
+      ldmatrix_x4(bb, kst + sw_off(row, kk * 16 + ((lane >> 3) & 1) * 8));
+      mma_bf16_16816(s[0], a, bb);
+      mma_bf16_16816(s[1], a, bb + 2);
+    }
+    const int key_base = k0 + it * DBN + warp * 16;
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = key_base + nb * 8 + (lane & 3) * 2 + (e & 1);
+        if (key >= k1) s[nb][e] = -INFINITY;
+        mx[e >> 1] = fmaxf(mx[e >> 1], s[nb][e]);
+      }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+      const float m_new = fmaxf(m_run[r], mx[r]);
+      const float corr = (m_new == -INFINITY) ? 1.f : exp2f((m_run[r] - m_new) * sl2);
+      m_run[r] = m_new;
+      l_run[r] *= corr;
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) {
+        o[i][2 * r] *= corr;
+        o[i][2 * r + 1] *= corr;
+      }
+    }
+#pragma unroll
+    for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = e >> 1;
+        const float v = (m_run[r] == -INFINITY) ? 0.f : exp2f((s[nb][e] - m_run[r]) * sl2);
+        s[nb][e] = v;
+        l_run[r] += v;
+      }
+    uint32_t a[4];
+    a[0] = pack_bf16(s[0][0], s[0][1]);
+    a[1] = pack_bf16(s[0][2], s[0][3]);
+    a[2] = pack_bf16(s[1][0], s[1][1]);
+    a[3] = pack_bf16(s[1][2], s[1][3]);
+#pragma unroll
+    for (int np = 0; np < D / 16; ++np) {
+      uint32_t bb[4];
+      const int mm = lane >> 3;
+      const int row = warp * 16 + (mm & 1) * 8 + (lane & 7);
+      ldmatrix_x4_trans(bb, vst + sw_off(row, np * 16 + (mm >> 1) * 8));
+      mma_bf16_16816(o[2 * np], a, bb);
+      mma_bf16_16816(o[2 * np + 1], a, bb + 2);
+    }
+  }
+  cp_async_wait<0>();
+  if (s_fail) {  // a copy never completed: wait (bounded) for every TMA block still in flight
+    for (int k = it; k < min(n_blocks, it + TST - 1); ++k) {
+      const int buf = k % TST;
+      if (blk_mode[k] < 2 && threadIdx.x == 0) {
+        tc::mbar_wait_cycles(full + buf, (phase >> buf) & 1u, TWAIT_CYCLES);
+        phase ^= 1u << buf;
+      }
+    }
+    if (threadIdx.x == 0 && p.status) atomicExch(p.status, 1);
+    __syncthreads();
+    return;
+  }
+  __syncthreads();  // the staging area becomes the warp-merge buffer
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 1);
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 2);
+  }
+  constexpr int RS = D + 2;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int row = (lane >> 2) + 8 * r;
+    float* dst = red + (warp * 16 + row) * RS;
+#pragma unroll
+    for (int nb = 0; nb < D / 8; ++nb) {
+      const int col = nb * 8 + (lane & 3) * 2;
+      dst[col] = o[nb][2 * r];
+      dst[col + 1] = o[nb][2 * r + 1];
+    }
+    if ((lane & 3) == 0) {
+      dst[D] = m_run[r];
+      dst[D + 1] = l_run[r];
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * D; e += DT) {
+    const int row = e / D, col = e % D;
+    float M = -INFINITY;
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, red[(w * 16 + row) * RS + D]);
+    float acc = 0.f, L = 0.f;
+    for (int w = 0; w < 4; ++w) {
+      const float* src = red + (w * 16 + row) * RS;
+      const float f = (src[D] == -INFINITY) ? 0.f : exp2f((src[D] - M) * sl2);
+      acc += src[col] * f;
+      L += src[D + 1] * f;
+    }
+    const int64_t at = part + (int64_t)row * p.n_split;
+    p.part_o[at * D + col] = acc;
+    if (col == 0) {
+      p.part_ml[at * 2] = M == -INFINITY ? -INFINITY : M * p.scale;
+      p.part_ml[at * 2 + 1] = L;
+    }
+  }
+}
+
 // Merge the splits of each (row, head): out = sum_s o_s e^{m_s - M} / sum_s l_s e^{m_s - M}.
 // With export_ml the merged (M, L) and unnormalised out are also written (cross-GPU combine).
 __global__ void decode_merge_kernel(DecodeAttnParams p, int D) {
@@ -405,8 +671,12 @@ __device__ void finish_selection(const float* cscore, const int* cand, int nc, i
   }
 }
 
-template <bool CHECK>
-__global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
+__device__ __forceinline__ void signal_release(uint32_t* addr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(addr), "r"(v) : "memory");
+}
+
+template <bool CHECK, bool EXCH>
+__global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a, RouteExchangeArgs x) {
   __shared__ uint32_t hist[256];
   __shared__ uint32_t prefix, prefix_mask;
   __shared__ int need;
@@ -561,6 +831,59 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a) {
     if (lane == 0) cscore[i] = best * qinv;
   }
   __syncthreads();
+  if constexpr (EXCH) {
+    // 4x. this rank's exact top-k (rank order, global ids) -> every rank; then merge all ranks'
+    __shared__ float lcs[64];
+    __shared__ int lci[64];
+    __shared__ uint32_t s_ep;
+    __shared__ int s_ok;
+    finish_selection<false>(cscore, cand, nc, 0, a.k, -1, nullptr, nullptr, nullptr, 0, nullptr, nullptr, lcs, lci,
+                            a.id_offset, picked, sel_chunk, sel_off, &n_sel, -1, nullptr);
+    if (threadIdx.x == 0) {
+      s_ep = x.epochs[qb] + 1;
+      x.epochs[qb] = s_ep;
+      s_ok = 1;
+    }
+    __syncthreads();
+    const uint32_t ep = s_ep;
+    const int half = (int)(ep & 1u), K2 = 2 * a.k;
+    for (int t = threadIdx.x; t < x.world * K2; t += RT) {
+      const int pr = t / K2, i = t % K2;
+      const float v = i < a.k ? lcs[i] : __int_as_float(lci[i - a.k]);
+      x.recv[pr][(((int64_t)half * x.B_max + qb) * x.world + x.rank) * K2 + i] = v;
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < x.world) {
+      signal_release(x.flags[threadIdx.x] + qb * x.world + x.rank, ep);
+      if (!bounded_wait_geq(x.flags[x.rank] + qb * x.world + threadIdx.x, ep, x.max_spins)) {
+        s_ok = 0;
+        atomicExch(x.error, 1);
+      }
+    }
+    if (threadIdx.x == 0) n_cand = 0;
+    __syncthreads();
+    if (!s_ok) {  // a peer never delivered: no memory for this row (the error flag tells the host)
+      if (threadIdx.x == 0) a.mem_len[qb] = 0;
+      for (int i = threadIdx.x; i < a.k && a.sel_out; i += RT) a.sel_out[(int64_t)qb * a.k + i] = -1;
+      return;
+    }
+    for (int t = threadIdx.x; t < x.world * a.k; t += RT) {
+      const int pr = t / a.k, i = t % a.k;
+      const float* src = x.recv[x.rank] + (((int64_t)half * x.B_max + qb) * x.world + pr) * K2;
+      const int id = __float_as_int(__ldcv(src + a.k + i));
+      if (id >= 0) {
+        const int slot = atomicAdd(&n_cand, 1);
+        cand[slot] = id;
+        cscore[slot] = __ldcv(src + i);
+      }
+    }
+    __syncthreads();
+    finish_selection<CHECK>(cscore, cand, n_cand, qb, a.k, a.budget, x.global_len, x.global_row0, a.mem_idx,
+                            a.mem_max, a.mem_len, a.sel_out, nullptr, nullptr, 0, picked, sel_chunk, sel_off, &n_sel,
+                            a.pool_rows, a.bounds);
+    return;
+  }
   // 4. top-k by (-score, chunk id) (+ greedy budget, chunk order and the row list)
   finish_selection<CHECK>(cscore, cand, nc, b, a.k, a.budget, a.chunk_len, a.chunk_row0, a.mem_idx, a.mem_max,
                           a.mem_len, a.sel_out, a.cand_score, a.cand_id, a.id_offset, picked, sel_chunk, sel_off,
@@ -670,10 +993,44 @@ static cudaError_t launch_decode(DecodeAttnParams p, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+static int g_decode_tma = 1;
+void pra_decode_set_tma(int on) { g_decode_tma = on; }
+
+// The TMA-fed kernel, or cudaErrorNotSupported when a layout or option rules it out.
+template <int D>
+static cudaError_t launch_decode_tma(const DecodeAttnParams& p, cudaStream_t st) {
+  using namespace pra::llama;
+  using Lay = TLayout<D>;
+  const auto aligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  const bool has_mem = p.mem_idx != nullptr;
+  if (!g_decode_tma || p.bounds != nullptr || p.loc_k == nullptr || p.loc_row % 8 || p.loc_batch % p.loc_row ||
+      !aligned(p.loc_k) || !aligned(p.loc_v) || (has_mem && (!p.mem_on_device || p.mem_row % 8 || !aligned(p.mem_k) ||
+                                                               !aligned(p.mem_v) || p.mem_rows <= 0)))
+    return cudaErrorNotSupported;
+  const int64_t width = (int64_t)p.Hkv * D;
+  const int64_t loc_rows = (int64_t)p.B * (p.loc_batch / p.loc_row);
+  const CUtensorMap* lk = pra_tile_map_bf16(p.loc_k, width, loc_rows, p.loc_row, DBN);
+  const CUtensorMap* lv = pra_tile_map_bf16(p.loc_v, width, loc_rows, p.loc_row, DBN);
+  const CUtensorMap* mk = has_mem ? pra_tile_map_bf16(p.mem_k, width, p.mem_rows, p.mem_row, DBN) : lk;
+  const CUtensorMap* mv = has_mem ? pra_tile_map_bf16(p.mem_v, width, p.mem_rows, p.mem_row, DBN) : lv;
+  if (!lk || !lv || !mk || !mv) return cudaErrorNotSupported;
+  const size_t smem = 1024 + (size_t)TST * Lay::STAGE + 16 * Lay::QLD * 2 + (size_t)(p.split_keys + 2 * TMAX_BLOCKS) * 4 +
+                      TST * 8;
+  PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(decode_tma_kernel<D>), (int)smem));
+  decode_tma_kernel<D><<<dim3(p.B * p.Hkv, p.n_split), DT, smem, st>>>(*mk, *mv, *lk, *lv, p);
+  PRA_RETURN_IF_ERROR(cudaGetLastError());
+  decode_merge_kernel<<<p.B * p.H, 128, 0, st>>>(p, D);
+  return cudaGetLastError();
+}
+
 cudaError_t pra_decode_attention(const DecodeAttnParams& p, int head_dim, cudaStream_t st) {
   if (p.B == 0) return cudaSuccess;
   if (p.H % p.Hkv || p.H / p.Hkv > 16 || p.split_keys % pra::llama::DBN || p.split_keys > 4096)
     return cudaErrorInvalidValue;
+  cudaError_t e = cudaErrorNotSupported;
+  if (head_dim == 128) e = launch_decode_tma<128>(p, st);
+  else if (head_dim == 64) e = launch_decode_tma<64>(p, st);
+  if (e != cudaErrorNotSupported) return e;
   switch (head_dim) {
     case 64: return launch_decode<64>(p, st);
     case 128: return launch_decode<128>(p, st);
@@ -701,7 +1058,21 @@ cudaError_t pra_route_topk(const RouteTopkArgs& a, cudaStream_t st) {
   if (a.k > 64 || a.k_cand > pra::llama::MAX_CAND) return cudaErrorInvalidValue;
   const int S = a.segments > 0 ? a.segments : 1;
   if (S > 1 && (a.cand_score == nullptr || a.seg_len <= 0)) return cudaErrorInvalidValue;  // segments need a merge
-  if (a.bounds != nullptr) pra::llama::route_topk_kernel<true><<<a.B * S, pra::llama::RT, 0, st>>>(a);
-  else pra::llama::route_topk_kernel<false><<<a.B * S, pra::llama::RT, 0, st>>>(a);
+  const RouteExchangeArgs none{};
+  if (a.bounds != nullptr) pra::llama::route_topk_kernel<true, false><<<a.B * S, pra::llama::RT, 0, st>>>(a, none);
+  else pra::llama::route_topk_kernel<false, false><<<a.B * S, pra::llama::RT, 0, st>>>(a, none);
+  return cudaGetLastError();
+}
+
+cudaError_t pra_route_topk_exchange(const RouteTopkArgs& a, const RouteExchangeArgs& x, cudaStream_t st) {
+  if (a.B == 0) return cudaSuccess;
+  if (a.k > 64 || a.k_cand > pra::llama::MAX_CAND || a.segments > 1 || x.world < 2 || x.world > TP_MAX_RANKS ||
+      x.world * a.k > pra::llama::MAX_CAND || a.B > x.B_max || x.rank < 0 || x.rank >= x.world || !x.epochs ||
+      !x.error || !x.global_len || !x.global_row0 || !a.mem_idx || !a.mem_len)
+    return cudaErrorInvalidValue;
+  for (int p = 0; p < x.world; ++p)
+    if (!x.recv[p] || !x.flags[p]) return cudaErrorInvalidValue;
+  if (a.bounds != nullptr) pra::llama::route_topk_kernel<true, true><<<a.B, pra::llama::RT, 0, st>>>(a, x);
+  else pra::llama::route_topk_kernel<false, true><<<a.B, pra::llama::RT, 0, st>>>(a, x);
   return cudaGetLastError();
 }

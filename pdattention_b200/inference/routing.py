@@ -8,7 +8,9 @@ Scores come from a tensor-core GEMM (bf16 normalised queries x bf16 normalised g
   segment radix-selects its candidates and rescores them in fp32;
 * the segments' candidates are merged on the GPU (``route_merge``);
 * across GPUs (chunk-sharded memory) each rank's merged top-k candidates are
-  all-gathered over NVLink peer stores and merged again, identically on every rank.
+  exchanged over NVLink peer stores and merged again, identically on every rank; with
+  one segment per row (up to 8,192 chunks per rank) the exchange and the merge are fused
+  into the routing kernel itself (``TensorParallel.route_exchange``).
 
 Ties break towards the lower chunk id; the greedy token budget and the memory row list
 (only rows this rank holds) are produced by the final merge.
@@ -45,6 +47,10 @@ def select_chunks(ext, scores, query, gists, start, end, chunk_len, chunk_row0, 
         return ext.route_topk(scores, query, gists, start, end, chunk_len, chunk_row0, k, k_cand, budget, mem_max,
                               False, 0, G, 1, pool_rows)
     rows = query.shape[0]
+    if world > 1 and S == 1 and hasattr(comm, "route_exchange") and rows <= comm.decode_rows and \
+            k <= comm.ROUTE_K_MAX and world * k <= MAX_CANDIDATES:
+        return comm.route_exchange(scores, query, gists, start, end, k, k_cand, budget, mem_max, id_offset, G,
+                                   global_len, global_row0, pool_rows)
     cs, ci = ext.route_topk(scores, query, gists, start, end, chunk_len, chunk_row0, k, k_cand, -1, 0, True,
                             id_offset, G, S)
     if S > 1:

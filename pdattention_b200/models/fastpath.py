@@ -91,7 +91,7 @@ def unsupported_reason(cfg) -> str | None:
          "k-means error-on-empty-cluster policy"),
         (cfg.reference_level_gist_mode is not None, "URI-level gists"),
         (cfg.gists_per_chunk > 8, "more than 8 gists"),
-        (head_dim not in (32, 64, 128), f"head_dim={head_dim}"),
+        (head_dim not in (16, 32, 64, 128), f"head_dim={head_dim}"),
         (cfg.d_model % 8 or cfg.d_ff % 8, "widths not multiple of 8"),
         (cfg.collect_routing_metrics or cfg.collect_rank_diagnostics, "full ranking diagnostics"),
         (cfg.collect_detailed_timing, "host-timed diagnostics"),

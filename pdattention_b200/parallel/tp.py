@@ -27,6 +27,7 @@ from .peer import PeerBuffers
 
 class TensorParallel:
     SMALL_ELEMS = 1 << 16  # single-buffered gathers of a few values per row (greedy sampling)
+    ROUTE_K_MAX = 64       # chunks selected per row by the fused routing exchange
 
     def __init__(self, group=None, max_partial_elems: int = 64 << 20, max_gather_elems: int = 1 << 20,
                  max_spins: int = 1 << 23, decode_rows: int = 64, decode_width: int = 8192):
@@ -46,6 +47,8 @@ class TensorParallel:
             "dg_recv0": (self.world * decode_rows * decode_width, torch.bfloat16),
             "dg_recv1": (self.world * decode_rows * decode_width, torch.bfloat16),
             "dg_flag0": (tiles * self.world, torch.int32), "dg_flag1": (tiles * self.world, torch.int32),
+            "route_recv": (2 * decode_rows * self.world * 2 * self.ROUTE_K_MAX, torch.float32),
+            "route_flag": (decode_rows * self.world, torch.int32),
             "sig_ar": (words, torch.int32), "sig_ag": (words, torch.int32), "sig_small": (words, torch.int32)},
             self.group, self.device)
         self.parts = [self.buffers.local("part0"), self.buffers.local("part1")]
@@ -63,6 +66,10 @@ class TensorParallel:
         self.dg_flags = [self.buffers.addresses("dg_flag0"), self.buffers.addresses("dg_flag1")]
         self.dg_epochs = torch.zeros(tiles, dtype=torch.int32, device=self.device)
         self.epoch_dg = 0
+        # fused routing exchange (local top-k pushed to every rank, merged where it lands)
+        self.route_recv = self.buffers.addresses("route_recv")
+        self.route_flags = self.buffers.addresses("route_flag")
+        self.route_epochs = torch.zeros(decode_rows, dtype=torch.int32, device=self.device)
         self.epoch_ar = 0  # host call counters: pick the double buffer half
         self.epoch_ag = 0
         # per-CTA device call counters of the two collectives (graph-replay safe epochs)
@@ -101,6 +108,18 @@ class TensorParallel:
         _ext.require().decode_gemm(x, w, bias, residual, out, None, 0, 0, self.dg_recv[half], self.dg_flags[half],
                                    self.rank, self.dg_epochs, self.max_spins, self.error)
         return out
+
+    def route_exchange(self, scores, query, gists, lo, hi, k: int, k_cand: int, budget: int, mem_max: int,
+                       id_offset: int, gists_per_chunk: int, global_len, global_row0, pool_rows: int = -1):
+        """This rank's exact top-k over its chunk slice, exchanged with every rank and merged in
+        the same kernel (``route_topk_exchange``): ``(mem_idx, mem_len, selected ids)``, identical
+        on every rank."""
+        if scores.shape[0] > self.decode_rows or k > self.ROUTE_K_MAX:
+            raise ValueError("routing exchange sized for decode rows and k <= 64")
+        return _ext.require().route_topk_exchange(
+            scores, query, gists, lo, hi, k, k_cand, budget, mem_max, id_offset, gists_per_chunk, self.route_recv,
+            self.route_flags, self.route_epochs, self.rank, self.decode_rows, global_len, global_row0,
+            self.max_spins, self.error, pool_rows)
 
     def all_gather_columns(self, x: torch.Tensor) -> torch.Tensor:
         """``[rows, cols]`` fp32 slices -> ``[rows, world * cols]`` (rank-major column blocks)."""

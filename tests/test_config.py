@@ -79,3 +79,23 @@ def test_deep_update_merges_nested():
     base = {"a": {"b": 1, "c": 2}, "d": 3}
     deep_update(base, {"a": {"b": 5}, "e": 1})
     assert base == {"a": {"b": 5, "c": 2}, "d": 3, "e": 1}
+
+
+def test_every_named_profile_runs_on_the_device_path_except_head_dim_8():
+    """Every ``models.*`` profile of config/config.yml maps onto the device path (vanilla / mixed
+    blocks, dropout, the tiny head widths); only ``standalone_tiny`` (d_model 32 over 4 heads:
+    head width 8, below the tensor-core fragment) keeps the object path."""
+    from pathlib import Path
+
+    from pdattention_b200.cli import build_pra_config, load_config, read_yaml
+    from pdattention_b200.models.fastpath import unsupported_reason
+
+    path = Path(__file__).resolve().parents[1] / "config" / "config.yml"
+    names = sorted(read_yaml(path)["models"])
+    reasons = {}
+    for name in names:
+        cfg = build_pra_config(load_config(str(path), name), vocab_size=512, batch_size=2, lr=1e-3, steps=1,
+                               device="cuda")
+        reasons[name] = unsupported_reason(cfg)
+    assert reasons.pop("standalone_tiny") == "head_dim=8"
+    assert all(reason is None for reason in reasons.values()), reasons

@@ -202,3 +202,39 @@ def test_cross_attention_transport_matches_object_path(ext, tmp_path):
     loss.backward()
     gw = rt.layers[0]["mem_o"].gw
     assert torch.isfinite(rt.flat.grad.float()).all() and float(gw.float().abs().sum()) > 0
+
+
+@pytest.mark.parametrize("profile", ["tiny", "medium", "td_sa_tiny", "tdx_pra_tiny", "td_pra_tiny", "kvqa_tiny"])
+def test_named_profiles_match_object_path(ext, tmp_path, profile):
+    """The config.yml model profiles (head widths 16 / 32 / 64, vanilla and mixed blocks) on the
+    device path against the fp32 object path in eval mode."""
+    from pdattention_b200.cli import build_pra_config, load_config
+    from pdattention_b200.data import PRADataModule, WordIdTokenizer
+    from pdattention_b200.data.generators import generate_hierarchical_tokens
+
+    root = Path(tmp_path)
+    generate_hierarchical_tokens(root / "synthetic_hierarchical_tokens", examples=4, doc_tokens=24, prompt_tokens=40,
+                                 vocab=300, roots=2, children=1, grandchildren=1)
+    tok = WordIdTokenizer(300)
+    dm = PRADataModule("synthetic_hierarchical_tokens", str(root), batch_size=4, max_seq_len=64, tokenizer=tok,
+                       shuffle=False).load()
+    batch = next(iter(dm._loader(dm.dataset, shuffle=False)))
+    path = Path(__file__).resolve().parents[1] / "config" / "config.yml"
+    cfg = build_pra_config(load_config(str(path), profile), vocab_size=tok.vocab_size, batch_size=4, lr=1e-3,
+                           steps=1, device="cuda")
+    torch.manual_seed(31)
+    reference = TinyPRAModel(copy.deepcopy(cfg)).cuda().eval()
+    device_model = TinyPRAModel(copy.deepcopy(cfg)).cuda().eval()
+    device_model.load_state_dict(reference.state_dict())
+    attach_device_runtime(device_model)
+    rt = device_model._device_runtime
+    assert rt is not None, profile
+    with torch.no_grad():
+        _, ref_out = _pra_batch_step(reference, batch, "cuda", tok, ResolverServiceConfig(), None)
+        _, dev_out = _pra_batch_step(device_model, batch, "cuda", tok, ResolverServiceConfig(), None)
+    b, t = batch["input_ids"].shape
+    dev_logits = rt.logits(dev_out["hidden"], b, t).float()
+    ref_logits = ref_out["logits"].float()
+    valid = batch["attention_mask"].bool().cuda()
+    err = (dev_logits - ref_logits).abs()[valid]
+    assert err.max() <= 0.05 * ref_logits.abs()[valid].max(), (profile, err.max())

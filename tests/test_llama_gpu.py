@@ -303,3 +303,42 @@ def test_host_resident_chunk_memory_equals_device_memory(ext):
         out[residency] = (first, step)
     assert torch.equal(out["gpu"][0], out["cpu"][0])
     assert torch.equal(out["gpu"][1], out["cpu"][1])
+
+
+@pytest.mark.parametrize("head_dim,run,mem_len", [(128, 64, 1024), (128, 40, 600), (64, 64, 100), (128, 64, 0)])
+def test_tma_decode_attention_matches_cp_async_kernel(ext, head_dim, run, mem_len):
+    """The TMA-fed decode kernel (selected chunks as 64-row runs of the pool -> one box per 64
+    columns; other runs gathered into the same swizzled layout) equals the cp.async kernel and
+    the fp32 softmax."""
+    torch.manual_seed(8)
+    B, H, Hkv, max_len, tc = 5, 16, 4, 700, 64
+    chunks = 40
+    q = torch.randn(B, H * head_dim, device="cuda").bfloat16()
+    pool = torch.randn(chunks * tc, 2 * Hkv * head_dim, device="cuda").bfloat16()
+    mk, mv = pool[:, : Hkv * head_dim], pool[:, Hkv * head_dim:]
+    mem_idx = torch.zeros(B, max(mem_len, 1), device="cuda", dtype=torch.int32)
+    for b in range(B):  # runs of `run` consecutive rows from distinct chunks
+        picks = torch.randperm(chunks)[: (mem_len + run - 1) // run + 1]
+        rows = torch.cat([c * tc + torch.arange(run) for c in picks.tolist()])[:mem_len]
+        mem_idx[b, :mem_len] = rows.to(torch.int32).cuda()
+    lens = torch.tensor([mem_len, mem_len // 2, mem_len, 0, mem_len], device="cuda", dtype=torch.int32)
+    cache = torch.randn(2, B, max_len, Hkv * head_dim, device="cuda").bfloat16()
+    loc_len = torch.tensor([700, 1, 333, 64, 129], device="cuda", dtype=torch.int32)
+    args = (mk, mv, mem_idx, lens, cache[0], cache[1], loc_len, mem_len + max_len, 512, True)
+    try:
+        ext.decode_set_tma(True)
+        out_t, eo_t, eml_t = ext.decode_attention(q, H, Hkv, head_dim, *args)
+        ext.decode_set_tma(False)
+        out_c, eo_c, eml_c = ext.decode_attention(q, H, Hkv, head_dim, *args)
+    finally:
+        ext.decode_set_tma(True)
+    assert torch.allclose(out_t.float(), out_c.float(), atol=1e-2, rtol=1e-2), (out_t.float() - out_c.float()).abs().max()
+    assert torch.allclose(eml_t, eml_c, atol=1e-3, rtol=1e-3)
+    g = H // Hkv
+    for b in range(B):
+        n_m, n_l = int(lens[b]), int(loc_len[b])
+        keys = torch.cat([mk[mem_idx[b, :n_m].long()], cache[0, b, :n_l]]).float().view(-1, Hkv, head_dim)
+        vals = torch.cat([mv[mem_idx[b, :n_m].long()], cache[1, b, :n_l]]).float().view(-1, Hkv, head_dim)
+        s = torch.einsum("hd,khd->hk", q[b].float().view(H, head_dim), keys.repeat_interleave(g, 1)) / math.sqrt(head_dim)
+        ref = torch.einsum("hk,khd->hd", torch.softmax(s, -1), vals.repeat_interleave(g, 1)).reshape(-1)
+        assert torch.allclose(out_t[b].float(), ref, atol=2e-2, rtol=2e-2), (b, (out_t[b].float() - ref).abs().max())

@@ -81,6 +81,36 @@ def _worker(rank, world, port, queue):
         torch.cuda.synchronize()
         tp.check()
         result["fused_err"] = errs
+        # the routing kernel with the candidate exchange fused in == local top-k + all-gather + merge
+        from pdattention_b200.ops import _ext
+
+        ext = _ext.require()
+        C, D, k, per = 300, 64, 5, 150
+        g = torch.Generator(device="cuda").manual_seed(55)
+        gists_all = F.normalize(torch.randn(C, D, device="cuda", generator=g), dim=-1)
+        query = torch.randn(6, D, device="cuda", generator=g)  # identical on both ranks
+        c0 = rank * per
+        local_gists = gists_all[c0: c0 + per].contiguous()
+        scores = (F.normalize(query, dim=-1) @ local_gists.t()).contiguous()
+        start = torch.tensor([0, 20, 0, 100, 140, 0], device="cuda")
+        end = torch.tensor([300, 250, 10, 300, 160, 150], device="cuda")
+        lo = (start - c0).clamp(0, per).to(torch.int32)
+        hi = (end - c0).clamp(0, per).to(torch.int32)
+        clen = torch.full((C,), 8, device="cuda", dtype=torch.int32)
+        row0 = torch.arange(C, device="cuda", dtype=torch.int32) * 8
+        same = True
+        for _ in range(3):  # consecutive calls alternate the receive halves
+            fused = tp.route_exchange(scores, query, local_gists, lo, hi, k, 32, 20, k * 8, c0, 1, clen, row0)
+            cs, ci = ext.route_topk(scores, query, local_gists, lo, hi, clen, row0, k, 32, -1, 0, True, c0, 1, 1)
+            merged = tp.all_gather_columns(torch.cat([cs, ci.view(torch.float32)], dim=1))
+            want = ext.route_merge(merged, world, k, 20, clen, row0, k * 8, False)
+            same = same and torch.equal(fused[1], want[1]) and torch.equal(fused[2], want[2])
+            for r in range(6):
+                n = int(want[1][r])
+                same = same and torch.equal(fused[0][r, :n], want[0][r, :n])
+        torch.cuda.synchronize()
+        tp.check()
+        result["route_exchange_equal"] = same
         # timeout: rank 1 skips one all-reduce; rank 0's wait must run out and report
         dist.barrier()
         tp.max_spins = 1 << 14
@@ -98,6 +128,12 @@ def _worker(rank, world, port, queue):
             tp.fused_gemm_allreduce(x, w, None)
             torch.cuda.synchronize()
             result["fused_timeout_code"] = int(tp.error.item())
+            tp.error.zero_()
+        dist.barrier()
+        if rank == 0:  # and the fused routing exchange's per-row wait
+            tp.route_exchange(scores, query, local_gists, lo, hi, k, 32, 20, k * 8, c0, 1, clen, row0)
+            torch.cuda.synchronize()
+            result["route_timeout_code"] = int(tp.error.item())
             tp.error.zero_()
         dist.barrier()
         tp.buffers.close()
@@ -129,5 +165,7 @@ def test_tensor_parallel_engine_two_gpus():
         assert "error" not in item, item["error"]
         assert min(item["cos"]) > 0.99, item["cos"]
         assert max(item["fused_err"]) < 2e-2, item["fused_err"]
+        assert item["route_exchange_equal"]
     assert results[0]["timeout_code"] == 1
     assert results[0]["fused_timeout_code"] == 2
+    assert results[0]["route_timeout_code"] == 1
