@@ -153,6 +153,8 @@ def require():
         module.set_attention_impl(impl)
     if os.environ.get("PRA_BOUNDS_CHECK", "0") == "1":  # bounds-checked gather / routing kernels
         module.set_bounds_check(True)
+    if os.environ.get("PRA_DECODE_TMA", "1") == "0":  # the cp.async decode attention kernel
+        module.decode_set_tma(False)
     _counter = LaunchCounter(module)
     return _counter
 
