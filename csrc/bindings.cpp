@@ -1519,6 +1519,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("route_topk_exchange", &route_topk_exchange);
   m.def("set_bounds_check", &set_bounds_check);
   m.def("decode_set_tma", [](bool on) { pra_decode_set_tma(on ? 1 : 0); });
+  m.def("decode_set_stages", [](int64_t stages) { pra_decode_set_stages((int)stages); });
   m.def("bounds_check_enabled", &bounds_check_enabled);
   m.def("bounds_status", &bounds_status);
   m.def("bounds_reset", &bounds_reset);

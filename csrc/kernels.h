@@ -284,6 +284,8 @@ struct DecodeAttnParams {
 cudaError_t pra_decode_attention(const DecodeAttnParams& p, int head_dim, cudaStream_t stream);
 // 1 (default): eligible decode attention calls run the TMA-fed kernel; 0: the cp.async kernel.
 void pra_decode_set_tma(int on);
+// Pipeline stages of the TMA-fed decode kernel (2, 3 or 4; 2 by default).
+void pra_decode_set_stages(int stages);
 
 struct RouteTopkArgs {
   int B, D;

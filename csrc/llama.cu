@@ -274,7 +274,7 @@ __global__ void __launch_bounds__(DT) decode_kernel(DecodeAttnParams p) {
 // contiguous run (partial chunks, or a block straddling memory and local keys) are gathered
 // with cp.async into the same 128-byte-swizzled layout.  The tiles are read with ldmatrix at
 // swizzled addresses; scores, softmax and the warp merge are decode_kernel's.
-constexpr int TST = 3;           // pipeline stages (blocks in flight per CTA)
+constexpr int TST_DEFAULT = 2;   // pipeline stages (blocks in flight per CTA): 3 CTAs per SM
 constexpr int TBOX = 64 * 64 * 2;  // one 64-key x 64-column bf16 box (8 KB, 128-byte rows)
 constexpr int TMAX_BLOCKS = 64;  // split_keys <= 4096
 constexpr long long TWAIT_CYCLES = 4000000000LL;  // about two seconds at the boost clock
@@ -293,7 +293,7 @@ __device__ __forceinline__ uint32_t sw_off(int r, int c) {
   return (uint32_t)((c >> 6) * TBOX + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4) + ((c & 7) << 1));
 }
 
-template <int D>
+template <int D, int TST>
 __global__ void __launch_bounds__(DT) decode_tma_kernel(const __grid_constant__ CUtensorMap map_mk,
                                                         const __grid_constant__ CUtensorMap map_mv,
                                                         const __grid_constant__ CUtensorMap map_lk,
@@ -994,13 +994,26 @@ static cudaError_t launch_decode(DecodeAttnParams p, cudaStream_t st) {
 }
 
 static int g_decode_tma = 1;
+static int g_decode_stages = pra::llama::TST_DEFAULT;
 void pra_decode_set_tma(int on) { g_decode_tma = on; }
+void pra_decode_set_stages(int stages) { g_decode_stages = stages; }
+
+template <int D, int TST>
+static cudaError_t launch_decode_tma_stages(const DecodeAttnParams& p, const CUtensorMap* mk, const CUtensorMap* mv,
+                                            const CUtensorMap* lk, const CUtensorMap* lv, cudaStream_t st) {
+  using namespace pra::llama;
+  using Lay = TLayout<D>;
+  const size_t smem = 1024 + (size_t)TST * Lay::STAGE + 16 * Lay::QLD * 2 + (size_t)(p.split_keys + 2 * TMAX_BLOCKS) * 4 +
+                      TST * 8;
+  PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(decode_tma_kernel<D, TST>), (int)smem));
+  decode_tma_kernel<D, TST><<<dim3(p.B * p.Hkv, p.n_split), DT, smem, st>>>(*mk, *mv, *lk, *lv, p);
+  return cudaGetLastError();
+}
 
 // The TMA-fed kernel, or cudaErrorNotSupported when a layout or option rules it out.
 template <int D>
 static cudaError_t launch_decode_tma(const DecodeAttnParams& p, cudaStream_t st) {
   using namespace pra::llama;
-  using Lay = TLayout<D>;
   const auto aligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   const bool has_mem = p.mem_idx != nullptr;
   if (!g_decode_tma || p.bounds != nullptr || p.loc_k == nullptr || p.loc_row % 8 || p.loc_batch % p.loc_row ||
@@ -1014,11 +1027,9 @@ static cudaError_t launch_decode_tma(const DecodeAttnParams& p, cudaStream_t st)
   const CUtensorMap* mk = has_mem ? pra_tile_map_bf16(p.mem_k, width, p.mem_rows, p.mem_row, DBN) : lk;
   const CUtensorMap* mv = has_mem ? pra_tile_map_bf16(p.mem_v, width, p.mem_rows, p.mem_row, DBN) : lv;
   if (!lk || !lv || !mk || !mv) return cudaErrorNotSupported;
-  const size_t smem = 1024 + (size_t)TST * Lay::STAGE + 16 * Lay::QLD * 2 + (size_t)(p.split_keys + 2 * TMAX_BLOCKS) * 4 +
-                      TST * 8;
-  PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(decode_tma_kernel<D>), (int)smem));
-  decode_tma_kernel<D><<<dim3(p.B * p.Hkv, p.n_split), DT, smem, st>>>(*mk, *mv, *lk, *lv, p);
-  PRA_RETURN_IF_ERROR(cudaGetLastError());
+  if (g_decode_stages == 2) PRA_RETURN_IF_ERROR((launch_decode_tma_stages<D, 2>(p, mk, mv, lk, lv, st)));
+  else if (g_decode_stages == 4) PRA_RETURN_IF_ERROR((launch_decode_tma_stages<D, 4>(p, mk, mv, lk, lv, st)));
+  else PRA_RETURN_IF_ERROR((launch_decode_tma_stages<D, 3>(p, mk, mv, lk, lv, st)));
   decode_merge_kernel<<<p.B * p.H, 128, 0, st>>>(p, D);
   return cudaGetLastError();
 }

@@ -229,8 +229,52 @@ def sweep_table(tokens: int = 1 << 24, gists: int = 1, k: int = 16) -> None:
     _table(lambda: fused_layer_step(mem, rq, q, k), rows=15)
 
 
+def decode_attention_sweep(iters: int = 20) -> None:
+    """Device time of one Llama-3-8B layer's decode attention (64 rows, 4,352-slot local caches with
+    4,096 + a few keys, 16 routed 64-token chunks per row; K/V > the L2) for the TMA-fed kernel at
+    2 / 3 / 4 pipeline stages and split sizes 512 / 1024, and the cp.async kernel."""
+    from .ops import _ext
+
+    ext = _ext.require()
+    dev = torch.device("cuda", 0)
+    B, H, Hkv, D, max_len, chunks = 64, 32, 8, 128, 4352, 4096
+    gen = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn(B, H * D, device=dev, generator=gen).bfloat16()
+    pool = torch.randn(chunks * 64, 2 * Hkv * D, device=dev, generator=gen).bfloat16()
+    cache = torch.randn(2, B, max_len, Hkv * D, device=dev, generator=gen).bfloat16()
+    picks = torch.stack([torch.randperm(chunks, device=dev)[:16] for _ in range(B)])
+    mem_idx = (picks[:, :, None] * 64 + torch.arange(64, device=dev)).reshape(B, -1).to(torch.int32).contiguous()
+    mem_len = torch.full((B,), 1024, device=dev, dtype=torch.int32)
+    loc_len = torch.full((B,), 4100, device=dev, dtype=torch.int32)
+    nbytes = B * Hkv * (1024 + 4100) * D * 2 * 2
+    rows = []
+    configs = [("cp.async", False, 3, 512)] + [(f"tma s{st} split{sp}", True, st, sp) for st in (2, 3)
+                                               for sp in (512, 1024, 2048)]
+    for name, tma, stages, split in configs:
+        ext.decode_set_tma(tma)
+        ext.decode_set_stages(stages)
+        args = (q, H, Hkv, D, pool[:, : Hkv * D], pool[:, Hkv * D:], mem_idx, mem_len, cache[0], cache[1], loc_len,
+                1024 + max_len, split, False)
+        for _ in range(3):
+            ext.decode_attention(*args)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(iters):
+            ext.decode_attention(*args)
+        e.record()
+        torch.cuda.synchronize()
+        us = 1000 * s.elapsed_time(e) / iters
+        rows.append((name, us, nbytes / us / 1e6))
+    ext.decode_set_tma(True)
+    ext.decode_set_stages(3)
+    for name, us, tbs in rows:
+        print(f"{name:20s} {us:8.1f} us  {tbs:5.2f} TB/s (attention + split merge, {nbytes / 1e9:.2f} GB of K/V)")
+
+
 CASES = {"attention-fwd": attention_fwd, "sweep-table": sweep_table, "train-small": train_small, "decode-small": decode_small, "train-table": train_table,
-         "decode-table": decode_table, "decode-table-tp": decode_table_tp}
+         "decode-table": decode_table, "decode-table-tp": decode_table_tp,
+         "decode-attention-sweep": decode_attention_sweep}
 
 
 def main(argv=None) -> None:
