@@ -903,7 +903,7 @@ std::vector<torch::Tensor> route_topk(torch::Tensor scores, torch::Tensor query,
                                       torch::Tensor ns_start, torch::Tensor ns_end, torch::Tensor chunk_len,
                                       torch::Tensor chunk_row0, int64_t k, int64_t k_cand, int64_t budget,
                                       int64_t mem_max, bool local, int64_t id_offset, int64_t gists_per_chunk,
-                                      int64_t segments, int64_t pool_rows) {
+                                      int64_t segments, int64_t pool_rows, c10::optional<torch::Tensor> page_table) {
   c10::cuda::CUDAGuard guard(scores.device());
   expect(scores, at::kFloat, "scores");
   expect(query, at::kFloat, "query");
@@ -931,6 +931,13 @@ std::vector<torch::Tensor> route_topk(torch::Tensor scores, torch::Tensor query,
   a.n_chunks = scores.size(1) / std::max<int64_t>(gists_per_chunk, 1);
   a.pool_rows = pool_rows;
   a.bounds = bounds_word(scores.device());
+  if (page_table.has_value() && page_table->numel() > 0) {
+    TORCH_CHECK(page_table->scalar_type() == at::kInt && page_table->dim() == 2 && page_table->stride(1) == 1 &&
+                    page_table->size(0) == a.B && a.segments == 1,
+                "page_table must be int32 [B, pages] (one segment per row)");
+    a.page_table = ptr<const int>(*page_table);
+    a.page_stride = page_table->stride(0);
+  }
   auto io = scores.options().dtype(at::kInt);
   if (local) {  // best k per (row, segment) (exact scores, global ids) for a merge
     if (a.segments > 1) {
@@ -1512,7 +1519,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("route_topk", &route_topk, py::arg("scores"), py::arg("query"), py::arg("gists"), py::arg("ns_start"),
         py::arg("ns_end"), py::arg("chunk_len"), py::arg("chunk_row0"), py::arg("k"), py::arg("k_cand"),
         py::arg("budget"), py::arg("mem_max"), py::arg("local"), py::arg("id_offset"), py::arg("gists_per_chunk"),
-        py::arg("segments"), py::arg("pool_rows") = -1);
+        py::arg("segments"), py::arg("pool_rows") = -1, py::arg("page_table") = py::none());
   m.def("route_merge", &route_merge, py::arg("cands"), py::arg("world"), py::arg("k"), py::arg("budget"),
         py::arg("chunk_len"), py::arg("chunk_row0"), py::arg("mem_max"), py::arg("local"),
         py::arg("pool_rows") = -1);

@@ -312,6 +312,8 @@ struct RouteTopkArgs {
   int n_chunks;                // chunks in the table (bounds-checked variant)
   int64_t pool_rows;           // rows of the memory pool (bounds-checked variant)
   BoundsStatus* bounds;        // non-null: run the bounds-checked variant
+  const int* page_table;       // [B, page_stride] or null: namespace position j of row b is chunk
+  int64_t page_stride;         // page_table[b * page_stride + j] (scores / gists / tables by chunk id)
 };
 cudaError_t pra_route_topk(const RouteTopkArgs& args, cudaStream_t stream);
 

@@ -706,6 +706,10 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a, RouteEx
   }
   const int n = max(c1 - c0, 0);
   const float* row = a.scores + (int64_t)qb * a.score_stride;
+  // chunk id of namespace position c0 + i: through the row's page table (a paged chunk cache,
+  // whose rows read scattered pages), else the contiguous range itself
+  const int* pages = a.page_table ? a.page_table + (int64_t)qb * a.page_stride : nullptr;
+  auto phys = [&](int i) -> int { return pages ? pages[c0 + i] : c0 + i; };
   const int G = a.G > 0 ? a.G : 1;
   // a chunk's score is the best of its G gists' scores (gist aggregation "max")
   auto chunk_score = [&](int c) -> float {
@@ -718,8 +722,8 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a, RouteEx
   // candidate scans then read on-chip data (rows longer than STAGE_N read global memory)
   const bool staged = n <= STAGE_N;
   if (staged)
-    for (int i = threadIdx.x; i < n; i += RT) seg_scores[i] = chunk_score(c0 + i);
-  auto score_at = [&](int i) -> float { return staged ? seg_scores[i] : chunk_score(c0 + i); };
+    for (int i = threadIdx.x; i < n; i += RT) seg_scores[i] = chunk_score(phys(i));
+  auto score_at = [&](int i) -> float { return staged ? seg_scores[i] : chunk_score(phys(i)); };
   const int kc = min(a.k_cand, min(n, MAX_CAND));
   if (threadIdx.x == 0) {
     prefix = 0;
@@ -780,7 +784,7 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a, RouteEx
   for (int i = threadIdx.x; i < n && kc > 0; i += RT) {
     if (order_key(score_at(i)) > thr) {
       const int slot = atomicAdd(&n_cand, 1);
-      if (slot < MAX_CAND) cand[slot] = c0 + i;
+      if (slot < MAX_CAND) cand[slot] = phys(i);
     }
   }
   __syncthreads();
@@ -796,7 +800,7 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a, RouteEx
     const int want = kc - above;
     int slot = above + before;
     for (int i = s0; i < s1 && kc > 0 && slot < above + want; ++i)
-      if (order_key(score_at(i)) == thr) cand[slot++] = c0 + i;
+      if (order_key(score_at(i)) == thr) cand[slot++] = phys(i);
     __syncthreads();
     if (threadIdx.x == 0) n_cand = kc > 0 ? above + min(want, total) : 0;
     __syncthreads();

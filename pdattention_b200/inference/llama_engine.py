@@ -191,6 +191,8 @@ class PRALlamaEngine:
         self.cache: torch.Tensor | None = None
         self.cache_len: torch.Tensor | None = None
         self.namespace: tuple[torch.Tensor, torch.Tensor] | None = None
+        self.page_table: torch.Tensor | None = None  # [B, P] pages per row (paged chunk cache)
+        self._row0 = 0  # first row of the prefill row batch being routed
         self.last_selection: dict[int, torch.Tensor] = {}
         # Vocabulary-parallel LM head: under tensor parallelism each rank holds rows
         # [vocab_start, vocab_end) of the head and computes only that slice of the logits.
@@ -322,13 +324,16 @@ class PRALlamaEngine:
         mem_max = cfg.memory_tokens_per_row
         start, end = namespace if namespace is not None else self.namespace
         gn = mem.gn[layer].view(mem.C_pad, -1)
-        shards = self.tp.world if (self.tp is not None and self.shard_routing) else 1
+        pages = self.page_table
+        if pages is not None and namespace is not None and pages.shape[0] != rows:
+            pages = pages[self._row0: self._row0 + rows].contiguous()  # a prefill row batch
+        shards = self.tp.world if (self.tp is not None and self.shard_routing and pages is None) else 1
         if shards == 1:
             scores = torch.empty((rows, mem.C_pad), device=self.device, dtype=torch.float32)
             self.ext.gemm("tn_f32", rqn, mem.gn_bf16[layer], None, scores, None, None, 1.0, 0.0, None)
             mem_idx, mem_len, sel = select_chunks(self.ext, scores, rq, gn, start, end, mem.chunk_len,
                                                   mem.chunk_row0, k, k_cand, budget, mem_max,
-                                                  pool_rows=mem.pool.shape[1])
+                                                  pool_rows=mem.pool.shape[1], page_table=pages)
         else:
             # chunk-sharded routing: this rank scores its slice of the chunks, keeps its exact
             # local top-k, and the ranks' candidates are all-gathered and merged
@@ -360,17 +365,7 @@ class PRALlamaEngine:
         cfg = self.cfg
         C, tc = chunks.shape
         mem = ChunkMemory(cfg, C, self.kv_dim, self.device, tc, gist_dim=cfg.kv_dim)
-        mem.chunk_len[:C].copy_(lengths.to(self.device, torch.int32))
-        cos, sin = self.rope_tables(tc)
-        if self.tp is not None:  # each row-parallel partial must fit the peer buffer
-            batch_chunks = max(1, min(batch_chunks, self.tp.max_partial // (tc * cfg.hidden_size)))
-        for c0 in range(0, C, batch_chunks):
-            c1 = min(C, c0 + batch_chunks)
-            self._encode_chunk_batch(mem, chunks[c0:c1].to(self.device), mem.chunk_len[c0:c1], c0, cos, sin)
-        if self.tp is not None:  # gists are computed per KV-head slice; every rank gets all of them
-            self.tp.gather_gists(mem)
-        # bf16 routing copy for the tensor-core scoring GEMM
-        mem.gn_bf16.copy_(mem.gn.view(cfg.num_hidden_layers, mem.C_pad, -1))
+        self.encode_into(mem, chunks, lengths, 0, batch_chunks)
         if self.kv_residency == "cpu":
             host = torch.empty(mem.pool.shape, dtype=mem.pool.dtype, pin_memory=True)
             host.copy_(mem.pool, non_blocking=True)
@@ -378,6 +373,29 @@ class PRALlamaEngine:
             mem.pool = host
         self.memory = mem
         return mem
+
+    @torch.no_grad()
+    def encode_into(self, mem: ChunkMemory, chunks: torch.Tensor, lengths: torch.Tensor, first: int,
+                    batch_chunks: int = 256) -> None:
+        """Encode ``chunks`` ``[n, Tc]`` into chunk slots ``first .. first + n`` of ``mem`` (K/V pool
+        rows, gists and their bf16 routing copy, lengths); slots outside are untouched."""
+        cfg = self.cfg
+        n, tc = chunks.shape
+        if n == 0:
+            return
+        mem.chunk_len[first: first + n].copy_(lengths.to(self.device, torch.int32))
+        cos, sin = self.rope_tables(tc)
+        if self.tp is not None:  # each row-parallel partial must fit the peer buffer
+            batch_chunks = max(1, min(batch_chunks, self.tp.max_partial // (tc * cfg.hidden_size)))
+        for c0 in range(0, n, batch_chunks):
+            c1 = min(n, c0 + batch_chunks)
+            self._encode_chunk_batch(mem, chunks[c0:c1].to(self.device), mem.chunk_len[first + c0: first + c1],
+                                     first + c0, cos, sin)
+        if self.tp is not None:  # gists are computed per KV-head slice; every rank gets all of them
+            self.tp.gather_gists(mem, first, n)
+        # bf16 routing copy for the tensor-core scoring GEMM
+        sl = slice(first, first + n)
+        mem.gn_bf16[:, sl].copy_(mem.gn.view(cfg.num_hidden_layers, mem.C_pad, -1)[:, sl])
 
     def _encode_chunk_batch(self, mem: ChunkMemory, ids, lengths, c0, cos, sin):
         cfg, ext = self.cfg, self.ext
@@ -416,6 +434,13 @@ class PRALlamaEngine:
     def set_namespace(self, start: torch.Tensor, end: torch.Tensor) -> None:
         """Row b may read chunks ``[start[b], end[b])`` of the memory."""
         self.namespace = (start.to(self.device, torch.int32).contiguous(), end.to(self.device, torch.int32).contiguous())
+        self.page_table = None
+
+    def set_page_table(self, table: torch.Tensor, counts: torch.Tensor) -> None:
+        """Row b may read chunks ``table[b, :counts[b]]`` (a paged chunk cache's pages)."""
+        n = counts.to(self.device, torch.int32).contiguous()
+        self.namespace = (torch.zeros_like(n), n)
+        self.page_table = table.to(self.device, torch.int32).contiguous()
 
     @torch.no_grad()
     @traced("pra.llama.prefill")
@@ -460,6 +485,7 @@ class PRALlamaEngine:
         namespace = None
         if use_memory:
             namespace = (self.namespace[0][r0: r0 + B].contiguous(), self.namespace[1][r0: r0 + B].contiguous())
+            self._row0 = r0
         for li, lw in enumerate(self.w.layers):
             h = self._norm(x, lw.ln_in)
             qkv = self._gemm(h, lw.qkv, lw.qkv_bias)

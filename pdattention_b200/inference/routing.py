@@ -33,16 +33,22 @@ def segments_for(n_chunks: int, k: int) -> int:
 
 def select_chunks(ext, scores, query, gists, start, end, chunk_len, chunk_row0, k: int, k_cand: int, budget: int,
                   mem_max: int, *, gists_per_chunk: int = 1, id_offset: int = 0, comm=None,
-                  global_len=None, global_row0=None, pool_rows: int = -1):
+                  global_len=None, global_row0=None, pool_rows: int = -1, page_table=None):
     """``(mem_idx, mem_len, selected ids)`` for every row.  ``scores`` ``[B, C_local * G]``;
     with ``comm`` the chunk ids are global (``id_offset`` = this rank's first chunk) and
     ``global_len`` / ``global_row0`` describe every chunk (row0 < 0: held by another rank).
     ``pool_rows`` (the memory pool's row count) lets the bounds-checked kernels verify the row
-    lists they write."""
+    lists they write.  ``page_table`` ``[B, P]`` (a paged chunk cache) maps each row's namespace
+    positions to chunk ids; it needs one segment per row."""
     G = gists_per_chunk
     n = scores.shape[1] // G
     S = segments_for(n, k)
     world = comm.world if comm is not None else 1
+    if page_table is not None:
+        if world != 1 or page_table.shape[1] > SEGMENT:
+            raise ValueError("a page table needs unsharded routing and at most 8,192 pages per row")
+        return ext.route_topk(scores, query, gists, start, end, chunk_len, chunk_row0, k, k_cand, budget, mem_max,
+                              False, 0, G, 1, pool_rows, page_table)
     if world == 1 and S == 1:
         return ext.route_topk(scores, query, gists, start, end, chunk_len, chunk_row0, k, k_cand, budget, mem_max,
                               False, 0, G, 1, pool_rows)

@@ -145,3 +145,23 @@ def plan_cache_builds(model, tokenizer, metadata_rows: list[dict], *, resolver_c
         caches.append(cache)
         builders.append(builder)
     return caches, builders
+
+
+# Device caches of the Llama-family engine: ``CacheServiceConfig(type="paged", options={...})``
+# builds a deduplicated device page pool (``inference.page_cache.PagedChunkCache``) bound to an
+# engine; options: ``capacity_pages``, ``host_capacity_pages``, ``chunk_tokens``.
+DEVICE_CACHES: dict[str, Callable] = {}
+
+
+def register_device_cache(name: str, factory: Callable) -> None:
+    """Make ``create_device_cache(engine, CacheServiceConfig(type=name))`` build ``factory(engine, **options)``."""
+    DEVICE_CACHES[name] = factory
+
+
+def create_device_cache(engine, config: CacheServiceConfig | dict | None = None):
+    config = CacheServiceConfig.from_value(config) if config is not None else CacheServiceConfig(type="paged")
+    if config.type not in DEVICE_CACHES and config.type == "paged":
+        from ..inference.page_cache import PagedChunkCache
+
+        register_device_cache("paged", PagedChunkCache)
+    return _factory(DEVICE_CACHES, "device cache", config.type)(engine, **dict(config.options or {}))

@@ -156,15 +156,17 @@ class TensorParallel:
         t = self._gist_slices[layer]
         return t[1], t[2], t[0]
 
-    def gather_gists(self, mem) -> None:
-        """All-gather every layer's per-slice key means and renormalise over the full width."""
+    def gather_gists(self, mem, first: int = 0, count: int | None = None) -> None:
+        """All-gather every layer's per-slice key means of chunk slots ``first .. first + count``
+        (all slots by default) and renormalise them over the full width."""
+        end = mem.C_pad if count is None else first + count
         for layer, t in sorted(self._gist_slices.items()):
-            local = t[1, 0, :, 0].contiguous()  # un-normalised key mean slice [C_pad, kd]
+            local = t[1, 0, first:end, 0].contiguous()  # un-normalised key mean slice [n, kd]
             parts = [torch.empty_like(local) for _ in range(self.world)]
             dist.all_gather(parts, local, group=self.group)
             full = torch.cat(parts, dim=1)
-            mem.gk[layer, :, 0].copy_(full)
-            mem.gn[layer, :, 0].copy_(torch.nn.functional.normalize(full, dim=-1, eps=1e-12))
+            mem.gk[layer, first:end, 0].copy_(full)
+            mem.gn[layer, first:end, 0].copy_(torch.nn.functional.normalize(full, dim=-1, eps=1e-12))
         self._gist_slices = {}
 
     # -- host helpers ---------------------------------------------------------------
