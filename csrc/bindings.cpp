@@ -668,11 +668,7 @@ void decode_gemm(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> 
   static int sm_cache[64] = {};
   int& sms = sm_cache[x.device().index() & 63];
   if (sms == 0) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, x.device().index());
-  if (splits <= 0) {
-    // split K only while every split keeps >= 8 stages of 64 (shorter splits pay more in the
-    // workspace reduction than they gain in parallel weight streams)
-    splits = std::max(1, std::min(nkb / 8, sms / std::max(tiles, 1)));
-  }
+  if (splits <= 0) splits = pra_decode_gemm_splits(tiles, nkb, sms);
   a.splits = (int)splits;
   a.workspace = ptr<float>(decode_gemm_state(x.device(), false));
   a.counters = reinterpret_cast<uint32_t*>(decode_gemm_state(x.device(), true).data_ptr());
@@ -682,8 +678,8 @@ void decode_gemm(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> 
     TORCH_CHECK(world <= TP_MAX_RANKS && (int)flags.size() == world && epochs.has_value() && error.has_value(),
                 "fused all-reduce needs one receive buffer and one flag area per rank, epochs and an error word");
     TORCH_CHECK(!out2.has_value(), "the fused all-reduce writes one output");
-    TORCH_CHECK((int64_t)tiles * std::max<int64_t>(splits, 1) <= sms,
-                "fused all-reduce grids must fit on the SMs at once (tiles x splits <= SM count)");
+    TORCH_CHECK((int64_t)tiles * std::max<int64_t>(splits, 1) <= (int64_t)sms * pra_decode_gemm_ctas_per_sm(),
+                "fused all-reduce grids must fit on the GPU at once (tiles x splits <= CTA slots)");
     TORCH_CHECK(out.is_contiguous() && out.size(1) == a.N, "fused all-reduce: out [M, N] contiguous");
     a.world = world;
     a.rank = rank;
@@ -750,7 +746,7 @@ void decode_qkv_rope(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tens
   int& sms = sm_cache[x.device().index() & 63];
   if (sms == 0) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, x.device().index());
   const int tiles = (a.N + 127) / 128, nkb = a.K / 64;
-  a.splits = std::max(1, std::min(nkb / 8, sms / std::max(tiles, 1)));
+  a.splits = pra_decode_gemm_splits(tiles, nkb, sms);
   a.workspace = ptr<float>(decode_gemm_state(x.device(), false));
   a.counters = reinterpret_cast<uint32_t*>(decode_gemm_state(x.device(), true).data_ptr());
   a.world = 1;
@@ -903,7 +899,8 @@ std::vector<torch::Tensor> route_topk(torch::Tensor scores, torch::Tensor query,
                                       torch::Tensor ns_start, torch::Tensor ns_end, torch::Tensor chunk_len,
                                       torch::Tensor chunk_row0, int64_t k, int64_t k_cand, int64_t budget,
                                       int64_t mem_max, bool local, int64_t id_offset, int64_t gists_per_chunk,
-                                      int64_t segments, int64_t pool_rows, c10::optional<torch::Tensor> page_table) {
+                                      int64_t segments, int64_t pool_rows, c10::optional<torch::Tensor> page_table,
+                                      c10::optional<torch::Tensor> trace) {
   c10::cuda::CUDAGuard guard(scores.device());
   expect(scores, at::kFloat, "scores");
   expect(query, at::kFloat, "query");
@@ -937,6 +934,10 @@ std::vector<torch::Tensor> route_topk(torch::Tensor scores, torch::Tensor query,
                 "page_table must be int32 [B, pages] (one segment per row)");
     a.page_table = ptr<const int>(*page_table);
     a.page_stride = page_table->stride(0);
+  }
+  if (trace.has_value()) {
+    TORCH_CHECK(trace->scalar_type() == at::kLong && trace->numel() >= 8 && trace->is_cuda(), "trace: int64 [8]");
+    a.trace = reinterpret_cast<long long*>(trace->data_ptr());
   }
   auto io = scores.options().dtype(at::kInt);
   if (local) {  // best k per (row, segment) (exact scores, global ids) for a merge
@@ -1519,13 +1520,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("route_topk", &route_topk, py::arg("scores"), py::arg("query"), py::arg("gists"), py::arg("ns_start"),
         py::arg("ns_end"), py::arg("chunk_len"), py::arg("chunk_row0"), py::arg("k"), py::arg("k_cand"),
         py::arg("budget"), py::arg("mem_max"), py::arg("local"), py::arg("id_offset"), py::arg("gists_per_chunk"),
-        py::arg("segments"), py::arg("pool_rows") = -1, py::arg("page_table") = py::none());
+        py::arg("segments"), py::arg("pool_rows") = -1, py::arg("page_table") = py::none(),
+        py::arg("trace") = py::none());
   m.def("route_merge", &route_merge, py::arg("cands"), py::arg("world"), py::arg("k"), py::arg("budget"),
         py::arg("chunk_len"), py::arg("chunk_row0"), py::arg("mem_max"), py::arg("local"),
         py::arg("pool_rows") = -1);
   m.def("route_topk_exchange", &route_topk_exchange);
   m.def("set_bounds_check", &set_bounds_check);
   m.def("decode_set_tma", [](bool on) { pra_decode_set_tma(on ? 1 : 0); });
+  m.def("decode_gemm_configure", [](int64_t ctas, int64_t min_kb) { pra_decode_gemm_configure((int)ctas, (int)min_kb); });
   m.def("decode_set_stages", [](int64_t stages) { pra_decode_set_stages((int)stages); });
   m.def("bounds_check_enabled", &bounds_check_enabled);
   m.def("bounds_status", &bounds_status);

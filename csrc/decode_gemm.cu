@@ -26,6 +26,7 @@
 //    never writes a half its peers may still be reading.
 #include <cuda.h>
 
+#include <algorithm>
 #include <mutex>
 #include <unordered_map>
 
@@ -40,15 +41,17 @@ constexpr int NT = 128;   // 4 warps: TMEM lanes 0..127 are the tile's 128 outpu
 constexpr int BF = 128;   // output features per tile
 constexpr int BK = 64;    // reduction depth per stage: one 128-byte swizzle atom of bf16
 constexpr int MT = 64;    // token rows per tile (MMA N)
-constexpr int STAGES = 6;
+// pipeline depth: a template parameter of the kernel (6: one CTA per SM; 4: two CTAs per SM)
 constexpr int A_BYTES = BF * BK * 2;  // 16 KB
 constexpr int B_BYTES = MT * BK * 2;  // 8 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int OFF_BAR = STAGES * STAGE_BYTES;
-constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;  // + barriers, + alignment slack for the 1024-byte swizzle atoms
+template <int STAGES>
+struct Ring {
+  static constexpr int OFF_BAR = STAGES * STAGE_BYTES;
+  static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;  // + barriers, + alignment slack for the 1024-byte atoms
+  };
 constexpr int TMEM_COLS = MT;
 constexpr long long WAIT_CYCLES = 4000000000LL;  // about two seconds at the boost clock
-static_assert(MT * BF * 4 <= OFF_BAR, "the fp32 epilogue tile reuses the stage memory");
 
 __device__ __forceinline__ void signal_store(uint32_t* addr, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(addr), "r"(v) : "memory");
@@ -95,12 +98,13 @@ __device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
   return out;
 }
 
+template <int STAGES>
 __global__ void __launch_bounds__(NT) decode_gemm_kernel(const __grid_constant__ CUtensorMap map_w,
                                                           const __grid_constant__ CUtensorMap map_x, DecodeGemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
   // the swizzle atoms need 1024-byte alignment
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Ring<STAGES>::OFF_BAR);
   uint64_t* empty = full + STAGES;
   uint64_t* done = empty + STAGES;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(done + 1);
@@ -370,6 +374,19 @@ const CUtensorMap* pra_tile_map_bf16(const void* ptr, int64_t cols, int64_t rows
   return &cache.emplace(key, map).first->second;
 }
 
+static int g_dg_ctas_per_sm = 2;
+static int g_dg_min_kb = 8;
+void pra_decode_gemm_configure(int ctas_per_sm, int min_blocks_per_split) {
+  if (ctas_per_sm == 1 || ctas_per_sm == 2) g_dg_ctas_per_sm = ctas_per_sm;
+  if (min_blocks_per_split >= 1) g_dg_min_kb = min_blocks_per_split;
+}
+int pra_decode_gemm_ctas_per_sm() { return g_dg_ctas_per_sm; }
+
+int pra_decode_gemm_splits(int tiles, int nkb, int sms) {
+  const int slots = sms * g_dg_ctas_per_sm;
+  return std::max(1, std::min(nkb / g_dg_min_kb, slots / std::max(tiles, 1)));
+}
+
 size_t pra_decode_gemm_workspace_floats() { return (size_t)DG_MAX_TILES * pra::dg::BF * pra::dg::MT; }
 
 cudaError_t pra_decode_gemm(const DecodeGemmArgs& a, cudaStream_t st) {
@@ -393,7 +410,10 @@ cudaError_t pra_decode_gemm(const DecodeGemmArgs& a, cudaStream_t st) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(decode_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(decode_gemm_kernel<6>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Ring<6>::SMEM_BYTES));
+    PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(decode_gemm_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Ring<4>::SMEM_BYTES));
     configured[dev] = 1;
   }
   if ((reinterpret_cast<uintptr_t>(a.w) | reinterpret_cast<uintptr_t>(a.x)) & 15) return cudaErrorInvalidValue;
@@ -402,6 +422,9 @@ cudaError_t pra_decode_gemm(const DecodeGemmArgs& a, cudaStream_t st) {
   if (map_w == nullptr || map_x == nullptr) return cudaErrorInvalidValue;
   DecodeGemmArgs b = a;
   b.splits = splits;
-  decode_gemm_kernel<<<dim3(tiles, splits), NT, SMEM_BYTES, st>>>(*map_w, *map_x, b);
+  if (pra_decode_gemm_ctas_per_sm() == 2)
+    decode_gemm_kernel<4><<<dim3(tiles, splits), NT, Ring<4>::SMEM_BYTES, st>>>(*map_w, *map_x, b);
+  else
+    decode_gemm_kernel<6><<<dim3(tiles, splits), NT, Ring<6>::SMEM_BYTES, st>>>(*map_w, *map_x, b);
   return cudaGetLastError();
 }

@@ -314,6 +314,7 @@ struct RouteTopkArgs {
   BoundsStatus* bounds;        // non-null: run the bounds-checked variant
   const int* page_table;       // [B, page_stride] or null: namespace position j of row b is chunk
   int64_t page_stride;         // page_table[b * page_stride + j] (scores / gists / tables by chunk id)
+  long long* trace;            // optional [8]: clock64 at the phase boundaries of CTA 0 (profiling)
 };
 cudaError_t pra_route_topk(const RouteTopkArgs& args, cudaStream_t stream);
 
@@ -432,4 +433,10 @@ struct DecodeGemmArgs {
   const int* cache_rows;              // [M]
 };
 size_t pra_decode_gemm_workspace_floats();
+// Launch shape of the decode GEMM: 1 (6-stage ring) or 2 (4-stage ring) CTAs per SM, and the
+// fewest 64-deep K blocks a split keeps; defaults 2 and 8.  pra_decode_gemm_splits picks the
+// K split of a launch from them (the grid fills the CTA slots once).
+void pra_decode_gemm_configure(int ctas_per_sm, int min_blocks_per_split);
+int pra_decode_gemm_ctas_per_sm();
+int pra_decode_gemm_splits(int tiles, int nkb, int sms);
 cudaError_t pra_decode_gemm(const DecodeGemmArgs& a, cudaStream_t stream);

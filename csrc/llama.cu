@@ -620,54 +620,76 @@ __device__ void finish_selection(const float* cscore, const int* cand, int nc, i
     }
     return;
   }
-  if (threadIdx.x == 0) {
-    int order[64];
-    const int kk = min(k, 64);
-    for (int i = 0; i < nc; ++i)
-      if (picked[i] < kk) order[picked[i]] = i;
-    int used = 0, chosen = 0;
-    int sel[64];
-    for (int r = 0; r < kk; ++r) {
-      const int c = cand[order[r]];
-      const int len = chunk_len[c];
-      if (budget >= 0 && used + len > budget) continue;
-      used += len;
-      sel[chosen++] = c;
+  // the top-k candidates' ids, lengths and first pool rows in rank order, loaded in parallel
+  // (the greedy budget below is sequential; dependent global loads there cost microseconds)
+  __shared__ int s_cid[64], s_len[64], s_row0[64], sel_row0[64];
+  const int kk = min(k, 64);
+  for (int i = threadIdx.x; i < nc; i += blockDim.x) {
+    const int r = picked[i];
+    if (r < kk) {
+      const int c = cand[i];
+      s_cid[r] = c;
+      s_len[r] = chunk_len[c];
+      s_row0[r] = chunk_row0[c];
     }
-    for (int i = 1; i < chosen; ++i) {  // chunk order (insertion sort, k <= 64)
-      const int v = sel[i];
-      int j = i - 1;
-      while (j >= 0 && sel[j] > v) {
-        sel[j + 1] = sel[j];
-        --j;
-      }
-      sel[j + 1] = v;
-    }
-    int written = 0;  // chunks held elsewhere (row0 < 0) stay selected but add no rows here
-    for (int i = 0; i < chosen; ++i) {
-      sel_chunk[i] = sel[i];
-      sel_off[i] = written;
-      written += chunk_row0[sel[i]] >= 0 ? chunk_len[sel[i]] : 0;
-    }
-    sel_off[chosen] = written;
-    *n_sel = chosen;
-    for (int i = 0; i < k_req && sel_out; ++i) sel_out[(int64_t)b * k_req + i] = i < chosen ? sel[i] : -1;
-    mem_len[b] = min(written, mem_max);
   }
   __syncthreads();
-  for (int i = 0; i < *n_sel; ++i) {  // the memory row list, written by all threads
-    const int c = sel_chunk[i], base = sel_off[i], len = sel_off[i + 1] - base;
-    for (int t = threadIdx.x; t < len; t += blockDim.x) {
-      if (base + t >= mem_max) continue;
-      int row = chunk_row0[c] + t;
-      if constexpr (CHECK) {
-        if (pool_rows >= 0 && (int64_t)row >= pool_rows) {  // the chunk's rows run past the pool: record, mark the key bad
-          bounds_fail(bounds, PRA_BOUNDS_ROUTE_POOL_ROW, row, pool_rows);
-          row = -1;
-        }
+  // greedy token budget in rank order (sequential by definition; shared-memory only)
+  __shared__ int s_keep[64], sel_len[64];
+  if (threadIdx.x == 0) {
+    int used = 0, chosen = 0;
+    for (int r = 0; r < kk; ++r) {
+      const int len = s_len[r];
+      const bool keep = !(budget >= 0 && used + len > budget);
+      if (keep) {
+        used += len;
+        ++chosen;
       }
-      mem_idx[(int64_t)b * mem_max + base + t] = row;
+      s_keep[r] = keep;
     }
+    *n_sel = chosen;
+  }
+  __syncthreads();
+  // the kept chunks in chunk-id order: each finds its place by counting smaller kept ids
+  const int chosen = *n_sel;
+  if (threadIdx.x < kk && s_keep[threadIdx.x]) {
+    const int r = threadIdx.x, c = s_cid[r];
+    int pos = 0;
+    for (int o = 0; o < kk; ++o) pos += (s_keep[o] && s_cid[o] < c) ? 1 : 0;
+    sel_chunk[pos] = c;
+    sel_len[pos] = s_len[r];
+    sel_row0[pos] = s_row0[r];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {  // row offsets (chunks held elsewhere, row0 < 0, add no rows here)
+    int written = 0;
+    for (int i = 0; i < chosen; ++i) {
+      sel_off[i] = written;
+      written += sel_row0[i] >= 0 ? sel_len[i] : 0;
+    }
+    sel_off[chosen] = written;
+    mem_len[b] = min(written, mem_max);
+  }
+  for (int i = threadIdx.x; i < k_req && sel_out; i += blockDim.x)
+    sel_out[(int64_t)b * k_req + i] = i < chosen ? sel_chunk[i] : -1;
+  __syncthreads();
+  // the memory row list, one row per thread: row t belongs to the last chunk whose offset <= t
+  const int rows_out = min(sel_off[chosen], mem_max);
+  for (int t = threadIdx.x; t < rows_out; t += blockDim.x) {
+    int lo = 0, hi = chosen - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (sel_off[mid] <= t) lo = mid;
+      else hi = mid - 1;
+    }
+    int row = sel_row0[lo] + (t - sel_off[lo]);
+    if constexpr (CHECK) {
+      if (pool_rows >= 0 && (int64_t)row >= pool_rows) {  // the chunk's rows run past the pool: record, mark the key bad
+        bounds_fail(bounds, PRA_BOUNDS_ROUTE_POOL_ROW, row, pool_rows);
+        row = -1;
+      }
+    }
+    mem_idx[(int64_t)b * mem_max + t] = row;
   }
 }
 
@@ -732,6 +754,11 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a, RouteEx
     n_cand = 0;
   }
   __syncthreads();
+  // phase timestamps of CTA 0 (profiling aid, off unless a trace buffer is given)
+  auto mark = [&](int k) {
+    if (a.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0) a.trace[k] = clock64();
+  };
+  mark(0);
   // 1. radix select (MSB first, 8-bit digits): the kc-th largest approximate score
   for (int shift = 24; shift >= 0 && kc > 0; shift -= 8) {
     for (int i = threadIdx.x; i < 256; i += RT) hist[i] = 0;
@@ -779,6 +806,7 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a, RouteEx
     }
     __syncthreads();
   }
+  mark(1);
   // 2. candidates: every chunk strictly above the threshold, then ties at it (lowest ids first)
   const uint32_t thr = prefix;
   for (int i = threadIdx.x; i < n && kc > 0; i += RT) {
@@ -806,11 +834,15 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a, RouteEx
     __syncthreads();
   }
   const int nc = n_cand;
-  // 3. exact fp32 cosine of the candidates (warp per candidate)
+  mark(2);
+  // 3. exact fp32 cosine of the candidates: the query staged in shared memory (over the staged
+  // scores, no longer read), each warp one candidate at a time with independent 16-byte gist loads
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* qs = seg_scores;
   float sq = 0.f;
   for (int d = threadIdx.x; d < a.D; d += RT) {
     const float v = a.query[(int64_t)qb * a.query_stride + d];
+    qs[d] = v;
     sq += v * v;
   }
   sq = warp_sum(sq);
@@ -823,13 +855,23 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a, RouteEx
   }
   __syncthreads();
   const float qinv = red[0];
+  const bool vec = (a.D & 3) == 0 && (reinterpret_cast<uintptr_t>(a.gists) & 15) == 0;
   for (int i = warp; i < nc; i += RT / 32) {
-    const float* q = a.query + (int64_t)qb * a.query_stride;
     float best = -INFINITY;
     for (int gi = 0; gi < G; ++gi) {
       const float* g = a.gists + ((int64_t)cand[i] * G + gi) * a.D;
       float acc = 0.f;
-      for (int d = lane; d < a.D; d += 32) acc += q[d] * g[d];
+      if (vec) {
+        const float4* g4 = reinterpret_cast<const float4*>(g);
+        const float4* q4 = reinterpret_cast<const float4*>(qs);
+#pragma unroll 8
+        for (int j = lane; j < a.D / 4; j += 32) {
+          const float4 gv = __ldg(g4 + j), qv = q4[j];
+          acc += gv.x * qv.x + gv.y * qv.y + gv.z * qv.z + gv.w * qv.w;
+        }
+      } else {
+        for (int d = lane; d < a.D; d += 32) acc += qs[d] * g[d];
+      }
       best = fmaxf(best, warp_sum(acc));
     }
     if (lane == 0) cscore[i] = best * qinv;
@@ -888,10 +930,12 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a, RouteEx
                             a.pool_rows, a.bounds);
     return;
   }
+  mark(3);
   // 4. top-k by (-score, chunk id) (+ greedy budget, chunk order and the row list)
   finish_selection<CHECK>(cscore, cand, nc, b, a.k, a.budget, a.chunk_len, a.chunk_row0, a.mem_idx, a.mem_max,
                           a.mem_len, a.sel_out, a.cand_score, a.cand_id, a.id_offset, picked, sel_chunk, sel_off,
                           &n_sel, a.pool_rows, a.bounds);
+  mark(4);
 }
 
 // Cross-GPU merge of the per-rank candidates: row b holds world blocks of [k scores | k ids
@@ -1070,7 +1114,7 @@ cudaError_t pra_route_merge(const RouteMergeArgs& a, cudaStream_t st) {
 
 cudaError_t pra_route_topk(const RouteTopkArgs& a, cudaStream_t st) {
   if (a.B == 0) return cudaSuccess;
-  if (a.k > 64 || a.k_cand > pra::llama::MAX_CAND) return cudaErrorInvalidValue;
+  if (a.k > 64 || a.k_cand > pra::llama::MAX_CAND || a.D > pra::llama::STAGE_N) return cudaErrorInvalidValue;
   const int S = a.segments > 0 ? a.segments : 1;
   if (S > 1 && (a.cand_score == nullptr || a.seg_len <= 0)) return cudaErrorInvalidValue;  // segments need a merge
   const RouteExchangeArgs none{};
@@ -1081,7 +1125,8 @@ cudaError_t pra_route_topk(const RouteTopkArgs& a, cudaStream_t st) {
 
 cudaError_t pra_route_topk_exchange(const RouteTopkArgs& a, const RouteExchangeArgs& x, cudaStream_t st) {
   if (a.B == 0) return cudaSuccess;
-  if (a.k > 64 || a.k_cand > pra::llama::MAX_CAND || a.segments > 1 || x.world < 2 || x.world > TP_MAX_RANKS ||
+  if (a.k > 64 || a.k_cand > pra::llama::MAX_CAND || a.D > pra::llama::STAGE_N || a.segments > 1 || x.world < 2 ||
+      x.world > TP_MAX_RANKS ||
       x.world * a.k > pra::llama::MAX_CAND || a.B > x.B_max || x.rank < 0 || x.rank >= x.world || !x.epochs ||
       !x.error || !x.global_len || !x.global_row0 || !a.mem_idx || !a.mem_len)
     return cudaErrorInvalidValue;

@@ -38,7 +38,7 @@ KERNELS_PER_CALL = {"attention_fwd": 1, "attention_bwd": 3, "gemm": 1, "norm_fwd
                     "ipc_alloc": 0, "ipc_open": 0, "ipc_close": 0,
                     "rope_copy": 1, "silu_mul": 1, "decode_attention": 2, "route_topk": 1,
                     "tp_allreduce": 1, "tp_allgather": 1, "tp_signal_words": 0, "route_merge": 1, "embed_add": 1, "combine_partials": 1, "attention_status": 0, "plan_batch": 0, "decode_gemm": 1, "decode_qkv_rope": 1, "decode_gemm_max_tiles": 0, "set_attention_impl": 0, "attention_impl": 0,
-                    "dropout": 1, "dropout_add": 1, "decode_set_tma": 0, "decode_set_stages": 0, "route_topk_exchange": 1, "set_bounds_check": 0, "bounds_check_enabled": 0, "bounds_status": 0, "bounds_reset": 0}  # stack_*: counted per layer by their callers
+                    "dropout": 1, "dropout_add": 1, "decode_set_tma": 0, "decode_set_stages": 0, "decode_gemm_configure": 0, "route_topk_exchange": 1, "set_bounds_check": 0, "bounds_check_enabled": 0, "bounds_status": 0, "bounds_reset": 0}  # stack_*: counted per layer by their callers
 
 
 class LaunchCounter:
@@ -155,6 +155,8 @@ def require():
         module.set_bounds_check(True)
     if os.environ.get("PRA_DECODE_TMA", "1") == "0":  # the cp.async decode attention kernel
         module.decode_set_tma(False)
+    if os.environ.get("PRA_DG_CTAS") or os.environ.get("PRA_DG_MIN_KB"):  # decode GEMM launch shape
+        module.decode_gemm_configure(int(os.environ.get("PRA_DG_CTAS", 2)), int(os.environ.get("PRA_DG_MIN_KB", 8)))
     if os.environ.get("PRA_DECODE_STAGES"):  # pipeline depth of the TMA-fed decode kernel
         module.decode_set_stages(int(os.environ["PRA_DECODE_STAGES"]))
     _counter = LaunchCounter(module)

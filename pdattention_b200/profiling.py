@@ -272,9 +272,86 @@ def decode_attention_sweep(iters: int = 20) -> None:
         print(f"{name:20s} {us:8.1f} us  {tbs:5.2f} TB/s (attention + split merge, {nbytes / 1e9:.2f} GB of K/V)")
 
 
+def route_topk_bench(iters: int = 50) -> None:
+    """Device time of the exact top-k routing kernel for the decode shapes: 64 query rows,
+    2,048 / 4,096 / 8,192 chunks per rank, 1,024-wide gists, top-16 from 64 candidates."""
+    import torch.nn.functional as F
+
+    from .ops import _ext
+
+    ext = _ext.require()
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    for n in (2048, 4096, 8192):
+        gists = F.normalize(torch.randn(n, 1024, device=dev, generator=gen), dim=-1)
+        query = torch.randn(64, 1024, device=dev, generator=gen)
+        scores = (F.normalize(query, dim=-1).bfloat16().float() @ gists.bfloat16().float().t()).contiguous()
+        lo = torch.zeros(64, dtype=torch.int32, device=dev)
+        hi = torch.full((64,), n, dtype=torch.int32, device=dev)
+        clen = torch.full((n,), 64, dtype=torch.int32, device=dev)
+        row0 = torch.arange(n, dtype=torch.int32, device=dev) * 64
+
+        def call():
+            ext.route_topk(scores, query, gists, lo, hi, clen, row0, 16, 64, -1, 1024, False, 0, 1, 1)
+
+        for _ in range(3):
+            call()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(iters):
+            call()
+        e.record()
+        torch.cuda.synchronize()
+        trace = torch.zeros(8, dtype=torch.int64, device=dev)
+        ext.route_topk(scores, query, gists, lo, hi, clen, row0, 16, 64, -1, 1024, False, 0, 1, 1, -1, None, trace)
+        torch.cuda.synchronize()
+        t = trace.tolist()
+        phases = [t[i + 1] - t[i] for i in range(4)]
+        print(f"route_topk 64 rows x {n} chunks: {1000 * s.elapsed_time(e) / iters:.1f} us; CTA 0 cycles: radix "
+              f"{phases[0]}, candidates {phases[1]}, rescoring {phases[2]}, selection {phases[3]}")
+
+
+def decode_gemm_sweep(iters: int = 30) -> None:
+    """Device time of the decode GEMM (64 token rows) on the Llama-3-8B projection shapes of one
+    GPU and of tensor-parallel shards (2 and 8 ranks), for one or two CTAs per SM and the fewest
+    K blocks a split keeps; weights > the L2 are rotated between launches."""
+    from .ops import _ext
+
+    ext = _ext.require()
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    shapes = {"qkv tp1": (7168, 4096), "o tp1": (4096, 4096), "gate_up tp1": (28672, 4096), "down tp1": (4096, 14336),
+              "qkv tp8": (1792, 4096), "o tp8": (4096, 512), "gate_up tp8": (3584, 4096), "down tp8": (4096, 1792)}
+    configs = [(1, 8), (2, 8), (2, 4), (2, 2)]
+    print("shape            " + "  ".join(f"ctas{c}/minkb{k}" for c, k in configs))
+    for name, (n, k) in shapes.items():
+        copies = max(2, int(2 * 128e6 // (n * k * 2)) + 1)  # > L2 in total
+        ws = [(torch.randn(n, k, device=dev, generator=gen) * 0.02).bfloat16() for _ in range(copies)]
+        x = torch.randn(64, k, device=dev, generator=gen).bfloat16()
+        out = torch.empty(64, n, device=dev, dtype=torch.bfloat16)
+        cells = []
+        for ctas, min_kb in configs:
+            ext.decode_gemm_configure(ctas, min_kb)
+            for w in ws:
+                ext.decode_gemm(x, w, None, None, out, None, 0, 0, [], [], 0, None, 0, None)
+            torch.cuda.synchronize()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for i in range(iters):
+                ext.decode_gemm(x, ws[i % copies], None, None, out, None, 0, 0, [], [], 0, None, 0, None)
+            e.record()
+            torch.cuda.synchronize()
+            us = 1000 * s.elapsed_time(e) / iters
+            cells.append(f"{us:6.1f}us {n * k * 2 / us / 1e6:4.2f}TB/s")
+        print(f"{name:16s} " + "  ".join(cells))
+    ext.decode_gemm_configure(2, 8)
+
+
 CASES = {"attention-fwd": attention_fwd, "sweep-table": sweep_table, "train-small": train_small, "decode-small": decode_small, "train-table": train_table,
          "decode-table": decode_table, "decode-table-tp": decode_table_tp,
-         "decode-attention-sweep": decode_attention_sweep}
+         "decode-attention-sweep": decode_attention_sweep, "route-topk-bench": route_topk_bench,
+         "decode-gemm-sweep": decode_gemm_sweep}
 
 
 def main(argv=None) -> None:
