@@ -219,6 +219,14 @@ torch::Tensor& workspace(const torch::Tensor& like) {
   return per_device[dev];
 }
 
+// Long reductions into few 128 x 256 output tiles (the LM head's data gradient: K = vocabulary)
+// run under the stream-K scheduler; measured 0.76x vs 0.58x of cuBLAS for 8,192 x 768 x 50,304,
+// and slower than the data-parallel tiles for every d_model-sized reduction.
+static bool long_reduction(const GemmArgs& g) {
+  const int64_t tiles = (int64_t)((g.M + 127) / 128) * ((g.N + 255) / 256);
+  return g.K >= 16384 && tiles < 4 * 148;
+}
+
 void gemm(const std::string& kind, torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> C, torch::Tensor D,
           c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> aux, double alpha, double beta,
           c10::optional<torch::Tensor> alpha_ptr) {
@@ -243,10 +251,10 @@ void gemm(const std::string& kind, torch::Tensor A, torch::Tensor B, c10::option
   if (kind == "tn" || kind == "tn_gelu" || kind == "tn_f32") {  // D[M,N] = A[M,K] B[N,K]^T
     g.M = A.size(0); g.K = A.size(1); g.N = B.size(0);
     TORCH_CHECK(B.size(1) == g.K && D.size(0) == g.M && D.size(1) == g.N, "tn shape mismatch");
-  } else if (kind == "nn" || kind == "nn_dgelu") {  // D[M,N] = A[M,K] B[K,N]
+  } else if (kind == "nn" || kind == "nn_dgelu" || kind == "nn_sk") {  // D[M,N] = A[M,K] B[K,N]
     g.M = A.size(0); g.K = A.size(1); g.N = B.size(1);
     TORCH_CHECK(B.size(0) == g.K && D.size(0) == g.M && D.size(1) == g.N, "nn shape mismatch");
-  } else if (kind == "wgrad") {  // D[M,N] = A[K,M]^T B[K,N]
+  } else if (kind == "wgrad" || kind == "wgrad_sk") {  // D[M,N] = A[K,M]^T B[K,N]
     g.K = A.size(0); g.M = A.size(1); g.N = B.size(1);
     TORCH_CHECK(B.size(0) == g.K && D.size(0) == g.M && D.size(1) == g.N, "wgrad shape mismatch");
   } else {
@@ -260,10 +268,22 @@ void gemm(const std::string& kind, torch::Tensor A, torch::Tensor B, c10::option
                    : (g.N <= 1024 ? pra_gemm_tn_bias_narrow(g, stream()) : pra_gemm_tn_bias(g, stream()));
   else if (kind == "tn_f32") e = pra_gemm_tn_f32(g, stream());
   else if (kind == "tn_gelu") e = pra_gemm_tn_bias_gelu(g, stream());
-  else if (kind == "nn") e = pra_gemm_nn(g, stream());
+  else if (kind == "nn") e = long_reduction(g) ? pra_gemm_nn_sk(g, stream()) : pra_gemm_nn(g, stream());
   else if (kind == "nn_dgelu") e = pra_gemm_nn_dgelu(g, stream());
-  else e = pra_gemm_wgrad(g, stream());
+  else if (kind == "nn_sk") e = pra_gemm_nn_sk(g, stream());
+  else if (kind == "wgrad_sk") e = pra_gemm_wgrad_sk(g, stream());
+  else  // large outputs (the LM head's weight gradient) on 128 x 256 stream-K tiles: 0.76x vs 0.72x of cuBLAS
+    e = (int64_t)g.M * g.N >= (16 << 20) ? pra_gemm_wgrad_sk(g, stream()) : pra_gemm_wgrad(g, stream());
   check(e, kind.c_str());
+}
+
+std::vector<torch::Tensor> gelu_probe(torch::Tensor z) {
+  c10::cuda::CUDAGuard guard(z.device());
+  expect(z, at::kFloat, "z");
+  TORCH_CHECK(z.is_contiguous(), "z must be contiguous");
+  auto y = torch::empty_like(z), dy = torch::empty_like(z);
+  check(pra_gelu_probe(ptr<const float>(z), ptr<float>(y), ptr<float>(dy), z.numel(), stream()), "gelu_probe");
+  return {y, dy};
 }
 
 // ---------------------------------------------------------------- norms
@@ -611,19 +631,6 @@ void tp_allgather(torch::Tensor src, std::vector<int64_t> dsts, std::vector<int6
 }
 
 // ---------------------------------------------------------------- decode GEMM
-// Per-device split-K workspace and arrival counters (zero between calls: the finishing CTA of a
-// tile clears its part), allocated on first use and kept for the process.
-torch::Tensor& decode_gemm_state(const torch::Device& dev, bool counters) {
-  static auto* bufs = new std::map<std::pair<int, bool>, torch::Tensor>();
-  auto& t = (*bufs)[{dev.index(), counters}];
-  if (!t.defined()) {
-    auto opts = torch::TensorOptions().device(dev);
-    t = counters ? torch::zeros({DG_MAX_TILES}, opts.dtype(at::kInt))
-                 : torch::zeros({(int64_t)pra_decode_gemm_workspace_floats()}, opts.dtype(at::kFloat));
-  }
-  return t;
-}
-
 // out[M, N] (+ out2 for columns >= split_col) = x[M, K] w[N, K]^T (+ bias, + residual); with peer
 // addresses in recv / flags (one per rank) the result is summed over the ranks (row-parallel
 // projection) inside the same kernel.  splits <= 0 picks the K split from the SM count.
@@ -634,7 +641,10 @@ void decode_gemm(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> 
   c10::cuda::CUDAGuard guard(x.device());
   expect(x, at::kBFloat16, "x");
   expect(w, at::kBFloat16, "w");
-  expect(out, at::kBFloat16, "out");
+  const bool f32 = out.scalar_type() == at::kFloat;  // routing scores: fp32, no epilogue terms
+  if (!f32) expect(out, at::kBFloat16, "out");
+  TORCH_CHECK(!f32 || (out.is_cuda() && !bias.has_value() && !residual.has_value() && !out2.has_value() && recv.empty()),
+              "decode_gemm: an fp32 output takes no bias, residual, second output or all-reduce");
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && w.dim() == 2 && w.is_contiguous() && w.size(1) == x.size(1),
               "decode_gemm: x [M, K] (unit column stride) and w [N, K] contiguous");
   TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1 && out.size(0) == x.size(0), "decode_gemm: out [M, >=cols]");
@@ -645,7 +655,8 @@ void decode_gemm(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> 
   a.M = x.size(0);
   a.N = w.size(0);
   a.K = w.size(1);
-  a.out = ptr<__nv_bfloat16>(out);
+  if (f32) a.out_f32 = ptr<float>(out);
+  else a.out = ptr<__nv_bfloat16>(out);
   a.ldo = out.stride(0);
   a.bias = optr<__nv_bfloat16>(bias);
   if (bias.has_value()) TORCH_CHECK(bias->numel() == a.N && bias->scalar_type() == at::kBFloat16, "bias [N] bf16");
@@ -670,16 +681,12 @@ void decode_gemm(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> 
   if (sms == 0) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, x.device().index());
   if (splits <= 0) splits = pra_decode_gemm_splits(tiles, nkb, sms);
   a.splits = (int)splits;
-  a.workspace = ptr<float>(decode_gemm_state(x.device(), false));
-  a.counters = reinterpret_cast<uint32_t*>(decode_gemm_state(x.device(), true).data_ptr());
   a.world = 1;
   if (!recv.empty()) {
     const int world = recv.size();
     TORCH_CHECK(world <= TP_MAX_RANKS && (int)flags.size() == world && epochs.has_value() && error.has_value(),
                 "fused all-reduce needs one receive buffer and one flag area per rank, epochs and an error word");
     TORCH_CHECK(!out2.has_value(), "the fused all-reduce writes one output");
-    TORCH_CHECK((int64_t)tiles * std::max<int64_t>(splits, 1) <= (int64_t)sms * pra_decode_gemm_ctas_per_sm(),
-                "fused all-reduce grids must fit on the GPU at once (tiles x splits <= CTA slots)");
     TORCH_CHECK(out.is_contiguous() && out.size(1) == a.N, "fused all-reduce: out [M, N] contiguous");
     a.world = world;
     a.rank = rank;
@@ -687,7 +694,8 @@ void decode_gemm(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> 
       a.recv[p] = reinterpret_cast<__nv_bfloat16*>(recv[p]);
       a.flags[p] = reinterpret_cast<uint32_t*>(flags[p]);
     }
-    TORCH_CHECK(epochs->scalar_type() == at::kInt && epochs->numel() >= DG_MAX_TILES, "epochs: int32 [DG_MAX_TILES]");
+    TORCH_CHECK(epochs->scalar_type() == at::kInt && epochs->numel() >= DG_MAX_TILES * DG_MAX_SPLITS,
+                "epochs: int32 [decode_gemm_flag_slots()]");
     a.epochs = reinterpret_cast<uint32_t*>(epochs->data_ptr());
     a.max_spins = max_spins;
     a.error = ptr<int>(*error);
@@ -747,8 +755,6 @@ void decode_qkv_rope(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tens
   if (sms == 0) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, x.device().index());
   const int tiles = (a.N + 127) / 128, nkb = a.K / 64;
   a.splits = pra_decode_gemm_splits(tiles, nkb, sms);
-  a.workspace = ptr<float>(decode_gemm_state(x.device(), false));
-  a.counters = reinterpret_cast<uint32_t*>(decode_gemm_state(x.device(), true).data_ptr());
   a.world = 1;
   check(pra_decode_gemm(a, stream()), "decode_qkv_rope");
 }
@@ -834,7 +840,11 @@ std::vector<torch::Tensor> decode_attention(torch::Tensor q, int64_t heads, int6
                                             c10::optional<torch::Tensor> mem_len,
                                             c10::optional<torch::Tensor> loc_k, c10::optional<torch::Tensor> loc_v,
                                             c10::optional<torch::Tensor> loc_len, int64_t max_keys,
-                                            int64_t split_keys, bool export_partials) {
+                                            int64_t split_keys, bool export_partials, int64_t mem_splits,
+                                            int64_t mem_split_keys,
+                                            int64_t split_lo, int64_t split_count, int64_t phase,
+                                            c10::optional<torch::Tensor> part_o_in,
+                                            c10::optional<torch::Tensor> part_ml_in) {
   c10::cuda::CUDAGuard guard(q.device());
   expect(q, at::kBFloat16, "q");
   TORCH_CHECK(q.dim() == 2 && q.stride(1) == 1 && q.size(1) == heads * head_dim, "q must be [B, H*Dh]");
@@ -873,9 +883,32 @@ std::vector<torch::Tensor> decode_attention(torch::Tensor q, int64_t heads, int6
   p.scale = 1.0f / std::sqrt((float)head_dim);
   p.split_keys = split_keys;
   p.n_split = std::max<int64_t>(1, (max_keys + split_keys - 1) / split_keys);
+  if (mem_splits > 0) {  // separate memory and local splits: the local ones tile the cache capacity
+    TORCH_CHECK(loc_k.has_value() && loc_k->numel() > 0, "separate memory / local splits need the local cache");
+    p.mem_splits = mem_splits;
+    p.mem_split_keys = mem_split_keys;
+    p.n_split = mem_splits + (loc_k->size(1) + split_keys - 1) / split_keys;
+  }
+  p.split_lo = split_lo;
+  p.split_count = split_count;
+  p.phase = phase;
   auto fo = q.options().dtype(at::kFloat);
-  auto part_o = torch::empty({p.B, heads, p.n_split, head_dim}, fo);
-  auto part_ml = torch::empty({p.B, heads, p.n_split, 2}, fo);
+  torch::Tensor part_o, part_ml;
+  if (part_o_in.has_value()) {  // caller-owned partials (a launch split across streams shares them)
+    TORCH_CHECK(part_ml_in.has_value(), "part_o and part_ml go together");
+    part_o = *part_o_in;
+    part_ml = *part_ml_in;
+    expect(part_o, at::kFloat, "part_o");
+    expect(part_ml, at::kFloat, "part_ml");
+    TORCH_CHECK(part_o.is_contiguous() && part_ml.is_contiguous() &&
+                    part_o.numel() >= (int64_t)p.B * heads * p.n_split * head_dim &&
+                    part_ml.numel() >= (int64_t)p.B * heads * p.n_split * 2,
+                "partials too small for [B, H, n_split, Dh]");
+  } else {
+    TORCH_CHECK(phase == 0, "a phase-split decode attention needs caller-owned partials");
+    part_o = torch::empty({p.B, heads, p.n_split, head_dim}, fo);
+    part_ml = torch::empty({p.B, heads, p.n_split, 2}, fo);
+  }
   auto out = torch::empty({p.B, heads * head_dim}, q.options());
   p.part_o = ptr<float>(part_o);
   p.part_ml = ptr<float>(part_ml);
@@ -903,7 +936,8 @@ std::vector<torch::Tensor> route_topk(torch::Tensor scores, torch::Tensor query,
                                       c10::optional<torch::Tensor> trace) {
   c10::cuda::CUDAGuard guard(scores.device());
   expect(scores, at::kFloat, "scores");
-  expect(query, at::kFloat, "query");
+  TORCH_CHECK(query.is_cuda() && (query.scalar_type() == at::kFloat || query.scalar_type() == at::kBFloat16),
+              "query must be a CUDA fp32 or bf16 tensor");
   expect(gists, at::kFloat, "gists");
   TORCH_CHECK(scores.dim() == 2 && scores.stride(1) == 1 && query.stride(-1) == 1 && gists.is_contiguous(),
               "route_topk layouts");
@@ -915,7 +949,8 @@ std::vector<torch::Tensor> route_topk(torch::Tensor scores, torch::Tensor query,
   TORCH_CHECK(a.segments == 1 || local, "segmented selection writes local candidates (merge them afterwards)");
   a.scores = ptr<const float>(scores);
   a.score_stride = scores.stride(0);
-  a.query = ptr<const float>(query);
+  if (query.scalar_type() == at::kBFloat16) a.query_bf16 = ptr<const __nv_bfloat16>(query);
+  else a.query = ptr<const float>(query);
   a.query_stride = query.stride(0);
   a.gists = ptr<const float>(gists);
   a.ns_start = ptr<const int>(ns_start);
@@ -975,7 +1010,8 @@ std::vector<torch::Tensor> route_topk_exchange(torch::Tensor scores, torch::Tens
                                                int64_t max_spins, torch::Tensor error, int64_t pool_rows) {
   c10::cuda::CUDAGuard guard(scores.device());
   expect(scores, at::kFloat, "scores");
-  expect(query, at::kFloat, "query");
+  TORCH_CHECK(query.is_cuda() && (query.scalar_type() == at::kFloat || query.scalar_type() == at::kBFloat16),
+              "query must be a CUDA fp32 or bf16 tensor");
   expect(gists, at::kFloat, "gists");
   TORCH_CHECK(scores.dim() == 2 && scores.stride(1) == 1 && query.stride(-1) == 1 && gists.is_contiguous(),
               "route_topk_exchange layouts");
@@ -989,7 +1025,8 @@ std::vector<torch::Tensor> route_topk_exchange(torch::Tensor scores, torch::Tens
   a.segments = 1;
   a.scores = ptr<const float>(scores);
   a.score_stride = scores.stride(0);
-  a.query = ptr<const float>(query);
+  if (query.scalar_type() == at::kBFloat16) a.query_bf16 = ptr<const __nv_bfloat16>(query);
+  else a.query = ptr<const float>(query);
   a.query_stride = query.stride(0);
   a.gists = ptr<const float>(gists);
   a.ns_start = ptr<const int>(ns_start);
@@ -1516,7 +1553,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_allgather", &tp_allgather);
   m.def("tp_signal_words", [](int64_t world) { return (int64_t)TP_MAX_BLOCKS * world; });
   m.def("silu_mul", &silu_mul);
-  m.def("decode_attention", &decode_attention);
+  m.def("decode_attention", &decode_attention, py::arg("q"), py::arg("heads"), py::arg("kv_heads"),
+        py::arg("head_dim"), py::arg("mem_k"), py::arg("mem_v"), py::arg("mem_idx"), py::arg("mem_len"),
+        py::arg("loc_k"), py::arg("loc_v"), py::arg("loc_len"), py::arg("max_keys"), py::arg("split_keys"),
+        py::arg("export_partials"), py::arg("mem_splits") = 0, py::arg("mem_split_keys") = 0, py::arg("split_lo") = 0, py::arg("split_count") = 0,
+        py::arg("phase") = 0, py::arg("part_o") = py::none(), py::arg("part_ml") = py::none());
   m.def("route_topk", &route_topk, py::arg("scores"), py::arg("query"), py::arg("gists"), py::arg("ns_start"),
         py::arg("ns_end"), py::arg("chunk_len"), py::arg("chunk_row0"), py::arg("k"), py::arg("k_cand"),
         py::arg("budget"), py::arg("mem_max"), py::arg("local"), py::arg("id_offset"), py::arg("gists_per_chunk"),
@@ -1528,6 +1569,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("route_topk_exchange", &route_topk_exchange);
   m.def("set_bounds_check", &set_bounds_check);
   m.def("decode_set_tma", [](bool on) { pra_decode_set_tma(on ? 1 : 0); });
+  m.def("set_pdl", [](bool on) { pra_set_pdl(on ? 1 : 0); });
+  m.def("gelu_probe", &gelu_probe);
+  m.def("pdl_enabled", []() { return pra_pdl_enabled() != 0; });
   m.def("decode_gemm_configure", [](int64_t ctas, int64_t min_kb) { pra_decode_gemm_configure((int)ctas, (int)min_kb); });
   m.def("decode_set_stages", [](int64_t stages) { pra_decode_set_stages((int)stages); });
   m.def("bounds_check_enabled", &bounds_check_enabled);
@@ -1538,6 +1582,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_gemm", &decode_gemm);
   m.def("decode_qkv_rope", &decode_qkv_rope);
   m.def("decode_gemm_max_tiles", []() { return (int64_t)DG_MAX_TILES; });
+  m.def("decode_gemm_flag_slots", []() { return (int64_t)DG_MAX_TILES * DG_MAX_SPLITS; });
   m.def("plan_batch", &pra_plan_batch, "native cache-build planner (returns None when a batch needs the Python planner)");
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_open", &ipc_open);

@@ -237,3 +237,42 @@ __device__ __forceinline__ bool mbar_try_wait_parity(uint64_t* bar, uint32_t par
 // 64-column x box_rows boxes in the 128-byte swizzle layout; cached per (address, shape);
 // nullptr when the driver rejects it.  Defined in decode_gemm.cu.
 const CUtensorMap* pra_tile_map_bf16(const void* ptr, int64_t cols, int64_t rows, int64_t ld, int box_rows);
+
+namespace pra {
+
+// ---- programmatic dependent launch (the decode chain) ----------------------------------
+// A decode step is a chain of short kernels (norm -> QKV GEMM -> routing -> attention ->
+// merge -> O GEMM -> norm -> gate/up GEMM -> SwiGLU -> down GEMM, per layer).  Launched with
+// the programmatic-serialization attribute, kernel N+1 is scheduled as soon as every CTA of
+// kernel N has executed `pdl_launch_dependents`, and runs the part of its prologue that reads
+// nothing kernel N writes (barrier set-up, TMEM allocation, tensor-map prefetch, the weight
+// tiles of its first pipeline stages) while kernel N drains.  `pdl_wait` then blocks until
+// kernel N has completed and its writes are visible.  Rules every instrumented kernel keeps:
+// every thread calls `pdl_wait` before its first read of data an earlier kernel produces and
+// before its first global write (so no write races a predecessor's read), and no thread exits
+// without having called it (kernel N+1 completing then implies kernel N completed, which keeps
+// the chain transitive).  Without the attribute both instructions are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
+}  // namespace pra
+
+// Launch `kernel` on `st`, with programmatic stream serialization when PDL is enabled.  Only
+// for kernels that follow the `pdl_wait` rules above.
+template <typename... Params, typename... Args>
+inline cudaError_t pra_launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                  Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pra_pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}

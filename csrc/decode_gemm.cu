@@ -14,14 +14,17 @@
 // global access is a 16-byte row chunk):
 //  * plain: + bias, + residual, bf16 store; columns >= split_col go to a second output (the
 //    routing query rows appended to a QKV weight land in their own buffer);
-//  * split-K: every split adds its fp32 partial into a workspace tile with vector reductions;
-//    the last split to arrive (per-tile counter) finishes the tile and clears the workspace;
-//  * fused all-reduce (tensor-parallel row-parallel projection, world > 1): the finishing CTA
-//    pushes its bf16 partial tile into every rank's receive buffer (plain NVLink peer stores),
-//    raises a per-tile flag on every rank with a release store, waits (bounded) for every
-//    rank's flag of the same tile, then adds the residual to the sum of all ranks' partials.
-//    Tile j of every rank meets tile j of every peer, so no grid-wide barrier is needed, and
-//    the per-tile call counters live in device memory (graph capture replays stay in step).
+//  * split-K: the splits of a tile run as one thread-block cluster; each stages its fp32
+//    partial in shared memory, and after a cluster barrier each CTA sums a slice of the token
+//    rows over all splits' partials through distributed shared memory and finishes those rows
+//    (no global workspace, no atomics, the epilogue spread over the splits);
+//  * fused all-reduce (tensor-parallel row-parallel projection, world > 1): each CTA pushes
+//    its rows of the bf16 partial tile into every rank's receive buffer (plain NVLink peer
+//    stores), raises the (tile, row slice) flag on every rank with a release store, waits
+//    (bounded) for every rank's flag of the same slice, then adds the residual to the sum of
+//    all ranks' partials.  Slice (j, r) of every rank meets slice (j, r) of every peer, so no
+//    grid-wide barrier is needed, and the per-slice call counters live in device memory
+//    (graph capture replays stay in step).
 //    Callers alternate two receive/flag halves between calls, so a rank that runs ahead
 //    never writes a half its peers may still be reading.
 #include <cuda.h>
@@ -47,6 +50,7 @@ constexpr int B_BYTES = MT * BK * 2;  // 8 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 template <int STAGES>
 struct Ring {
+  static_assert(STAGES * STAGE_BYTES >= MT * BF * 4, "the epilogue stages the fp32 tile in the ring");
   static constexpr int OFF_BAR = STAGES * STAGE_BYTES;
   static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;  // + barriers, + alignment slack for the 1024-byte atoms
   };
@@ -57,9 +61,31 @@ __device__ __forceinline__ void signal_store(uint32_t* addr, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(addr), "r"(v) : "memory");
 }
 
-__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+// ---- thread-block cluster: the split-K CTAs of one output tile
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory location in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t dsmem_map(uint32_t local, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(out) : "r"(local), "r"(rank));
+  return out;
+}
+
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];\n"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
                : "memory");
+  return v;
 }
 
 // Shared-memory descriptor of a K-major bf16 tile in the 128-byte swizzle layout TMA writes:
@@ -136,9 +162,20 @@ __global__ void __launch_bounds__(NT) decode_gemm_kernel(const __grid_constant__
   tc::fence_after();
   const uint32_t tmem = *s_tmem;
 
+  pdl_launch_dependents();
   if (warp == 0 && lane == 0) {  // TMA producer
     asm volatile("prefetch.tensormap [%0];\n" ::"l"(&map_w) : "memory");
-    for (int kb = 0; kb < nk; ++kb) {
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(&map_x) : "memory");
+    // the weight tiles of the first stages do not depend on the kernels before: under a
+    // programmatic dependent launch they stream in while those kernels drain
+    const int pre = min(nk, STAGES);
+    for (int kb = 0; kb < pre; ++kb) {
+      expect_tx(full + kb, STAGE_BYTES);
+      tma_load(smem + kb * STAGE_BYTES, &map_w, (kb0 + kb) * BK, n0, full + kb);
+    }
+    pdl_wait();  // the token rows are the previous kernel's output
+    for (int kb = 0; kb < pre; ++kb) tma_load(smem + kb * STAGE_BYTES + A_BYTES, &map_x, (kb0 + kb) * BK, 0, full + kb);
+    for (int kb = pre; kb < nk; ++kb) {
       const int slot = kb % STAGES;
       if (kb >= STAGES && !tc::mbar_wait_cycles(empty + slot, (uint32_t)((kb / STAGES - 1) & 1), WAIT_CYCLES)) {
         s_flag[0] = 1;
@@ -169,6 +206,7 @@ __global__ void __launch_bounds__(NT) decode_gemm_kernel(const __grid_constant__
   }
   // everyone: the accumulator is complete once `done` fires
   if (!tc::mbar_wait_cycles(done, 0, WAIT_CYCLES)) s_flag[0] = 1;
+  pdl_wait();  // before the epilogue's reads (residual, workspace) and every global write
   tc::fence_after();
   __syncthreads();
   const bool timed_out = s_flag[0] != 0;
@@ -184,53 +222,54 @@ __global__ void __launch_bounds__(NT) decode_gemm_kernel(const __grid_constant__
   if (warp == 0) tc::dealloc(tmem, TMEM_COLS);
   if (timed_out) {
     if (tid == 0 && a.error) atomicExch(a.error, 1);
+    if (a.splits > 1) {  // the cluster's other CTAs still meet this one at both cluster barriers
+      cluster_sync();
+      cluster_sync();
+    }
     return;
   }
   const int feat = tid;  // this thread's output feature within the tile (TMEM lane)
-
-  // ---- split-K: sum the splits' partials in the workspace; the last split finishes the tile
-  if (a.splits > 1) {
-    float* ws = a.workspace + ((int64_t)tile * BF + feat) * MT;
-#pragma unroll
-    for (int m = 0; m < MT; m += 4) red_add_v4(ws + m, acc[m], acc[m + 1], acc[m + 2], acc[m + 3]);
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_flag[1] = atomicAdd(a.counters + tile, 1u) == (uint32_t)(a.splits - 1);
-    __syncthreads();
-    if (!s_flag[1]) return;
-    __threadfence();
-    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int m = 0; m < MT; m += 4) {
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(ws + m));
-      acc[m] = v.x;
-      acc[m + 1] = v.y;
-      acc[m + 2] = v.z;
-      acc[m + 3] = v.w;
-      __stcg(reinterpret_cast<float4*>(ws + m), zero);  // the workspace starts at zero for the next call
-    }
-    if (tid == 0) a.counters[tile] = 0;
-  }
 
   // ---- stage the fp32 tile as [token][feature] so every global access is a 16-byte row chunk
   float* tile_s = reinterpret_cast<float*>(smem);
 #pragma unroll
   for (int m = 0; m < MT; ++m) tile_s[m * BF + feat] = acc[m];
-  __syncthreads();
-  constexpr int CHUNKS = MT * (BF / 8);  // 8 features per chunk
+  // ---- split-K: the splits of a tile are one thread-block cluster.  Each CTA sums a slice of
+  // the token rows over every split's staged partial through distributed shared memory (split
+  // order, so every rank and every call sums identically) and finishes those rows itself.
+  const int S = a.splits;
+  const int r = S > 1 ? (int)cluster_rank() : 0;
+  const int m_lo = r * a.M / S, m_hi = (r + 1) * a.M / S;
+  if (S > 1) {
+    cluster_sync();  // every split's partial is staged
+    for (int i = tid; i < (m_hi - m_lo) * (BF / 4); i += NT) {
+      float* at = tile_s + (m_lo + i / (BF / 4)) * BF + (i % (BF / 4)) * 4;
+      const uint32_t local = smem_u32(at);
+      float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int q = 0; q < S; ++q) {
+        const float4 v = ld_dsmem_f4(dsmem_map(local, (uint32_t)q));
+        sum.x += v.x, sum.y += v.y, sum.z += v.z, sum.w += v.w;
+      }
+      *reinterpret_cast<float4*>(at) = sum;  // rows [m_lo, m_hi) are read remotely by nobody
+    }
+    cluster_sync();  // no CTA leaves (or reuses its shared memory) while another reads it
+  } else {
+    __syncthreads();
+  }
+  const int c_lo = m_lo * (BF / 8), c_hi = m_hi * (BF / 8);  // this CTA's 8-feature row chunks
 
   if (a.world <= 1 && a.pos != nullptr) {  // decode QKV: bias, rotary, scatter into q / caches / routing query
     const int half = a.head_dim / 2;
-    for (int i = tid; i < CHUNKS; i += NT) {
+    for (int i = c_lo + tid; i < c_hi; i += NT) {
       const int m = i / (BF / 8), c = i % (BF / 8), n = n0 + c * 8;
-      if (m >= a.M || n >= a.N) continue;
+      if (n >= a.N) continue;
       float v[8];
       staged8(tile_s + m * BF + c * 8, v);
       float b[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       if (a.bias) load8(a.bias + n, b);
       if (n < a.k_end) {  // query or key head: rotate pairs (i, i + half) of each head
         const int p = a.pos[m];
-        float r[8];
+        float rr[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int f = c * 8 + j, hi = (n + j) % a.head_dim;  // tile-local feature, index within its head
@@ -240,11 +279,11 @@ __global__ void __launch_bounds__(NT) decode_gemm_kernel(const __grid_constant__
           const float xp = tile_s[m * BF + partner] + (a.bias ? __bfloat162float(a.bias[n0 + partner]) : 0.f);
           const int ii = first ? hi : hi - half;
           const float cs = a.cos_t[(int64_t)p * half + ii], sn = a.sin_t[(int64_t)p * half + ii];
-          r[j] = first ? x * cs - xp * sn : x * cs + xp * sn;
+          rr[j] = first ? x * cs - xp * sn : x * cs + xp * sn;
         }
         __nv_bfloat16* dst = n < a.q_end ? a.q_out + (int64_t)m * a.ldq + n
                                          : a.k_cache + (int64_t)a.cache_rows[m] * a.ld_cache + (n - a.q_end);
-        *reinterpret_cast<uint4*>(dst) = pack8(r);
+        *reinterpret_cast<uint4*>(dst) = pack8(rr);
         continue;
       }
 #pragma unroll
@@ -256,10 +295,22 @@ __global__ void __launch_bounds__(NT) decode_gemm_kernel(const __grid_constant__
     return;
   }
 
-  if (a.world <= 1) {
-    for (int i = tid; i < CHUNKS; i += NT) {
+  if (a.out_f32 != nullptr) {  // fp32 results (routing scores): 2 x 16-byte stores per chunk
+    for (int i = c_lo + tid; i < c_hi; i += NT) {
       const int m = i / (BF / 8), c = i % (BF / 8), n = n0 + c * 8;
-      if (m >= a.M || n >= a.N) continue;
+      if (n >= a.N) continue;
+      const float4* src = reinterpret_cast<const float4*>(tile_s + m * BF + c * 8);
+      float4* dst = reinterpret_cast<float4*>(a.out_f32 + (int64_t)m * a.ldo + n);
+      dst[0] = src[0];
+      dst[1] = src[1];
+    }
+    return;
+  }
+
+  if (a.world <= 1) {
+    for (int i = c_lo + tid; i < c_hi; i += NT) {
+      const int m = i / (BF / 8), c = i % (BF / 8), n = n0 + c * 8;
+      if (n >= a.N) continue;
       float v[8];
       staged8(tile_s + m * BF + c * 8, v);
       if (a.bias) {
@@ -269,10 +320,10 @@ __global__ void __launch_bounds__(NT) decode_gemm_kernel(const __grid_constant__
         for (int j = 0; j < 8; ++j) v[j] += b[j];
       }
       if (a.residual) {
-        float r[8];
-        load8(a.residual + (int64_t)m * a.ldo + n, r);
+        float rr[8];
+        load8(a.residual + (int64_t)m * a.ldo + n, rr);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] += r[j];
+        for (int j = 0; j < 8; ++j) v[j] += rr[j];
       }
       const bool second = a.out2 != nullptr && n >= a.split_col;
       __nv_bfloat16* dst = second ? a.out2 + (int64_t)m * a.ldo2 + (n - a.split_col) : a.out + (int64_t)m * a.ldo + n;
@@ -281,15 +332,19 @@ __global__ void __launch_bounds__(NT) decode_gemm_kernel(const __grid_constant__
     return;
   }
 
-  // ---- fused all-reduce: push this rank's bf16 partial tile to every rank, flag, wait, reduce
+  // ---- fused all-reduce: push this CTA's rows of the bf16 partial tile to every rank, raise
+  // this (tile, row slice)'s flag on every rank, wait for every rank's flag of the same slice,
+  // then sum the ranks' partials of those rows.  Row slices are the same on every rank (same
+  // split count), so slice (j, r) of every rank meets slice (j, r) of every peer.
+  const int slot = tile * DG_MAX_SPLITS + r;
   if (tid == 0) {
-    const uint32_t e = a.epochs[tile] + 1;
-    a.epochs[tile] = e;
+    const uint32_t e = a.epochs[slot] + 1;
+    a.epochs[slot] = e;
     *s_epoch = e;
   }
-  for (int i = tid; i < CHUNKS; i += NT) {
+  for (int i = c_lo + tid; i < c_hi; i += NT) {
     const int m = i / (BF / 8), c = i % (BF / 8), n = n0 + c * 8;
-    if (m >= a.M || n >= a.N) continue;
+    if (n >= a.N) continue;
     float v[8];
     staged8(tile_s + m * BF + c * 8, v);
     const uint4 packed = pack8(v);
@@ -300,19 +355,19 @@ __global__ void __launch_bounds__(NT) decode_gemm_kernel(const __grid_constant__
   const uint32_t epoch = *s_epoch;
   if (tid < a.world) {
     __threadfence_system();
-    signal_store(a.flags[tid] + (int64_t)tile * a.world + a.rank, epoch);
+    signal_store(a.flags[tid] + (int64_t)slot * a.world + a.rank, epoch);
   }
   if (tid < a.world) {
-    if (!bounded_wait_geq(a.flags[a.rank] + (int64_t)tile * a.world + tid, epoch, a.max_spins)) {
+    if (!bounded_wait_geq(a.flags[a.rank] + (int64_t)slot * a.world + tid, epoch, a.max_spins)) {
       s_flag[2] = 1;
       atomicExch(a.error, 2);
     }
   }
   __syncthreads();
   if (s_flag[2]) return;
-  for (int i = tid; i < CHUNKS; i += NT) {
+  for (int i = c_lo + tid; i < c_hi; i += NT) {
     const int m = i / (BF / 8), c = i % (BF / 8), n = n0 + c * 8;
-    if (m >= a.M || n >= a.N) continue;
+    if (n >= a.N) continue;
     float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (a.residual) load8(a.residual + (int64_t)m * a.ldo + n, v);
     if (a.bias) {
@@ -384,10 +439,42 @@ int pra_decode_gemm_ctas_per_sm() { return g_dg_ctas_per_sm; }
 
 int pra_decode_gemm_splits(int tiles, int nkb, int sms) {
   const int slots = sms * g_dg_ctas_per_sm;
-  return std::max(1, std::min(nkb / g_dg_min_kb, slots / std::max(tiles, 1)));
+  return std::max(1, std::min(std::min(nkb / g_dg_min_kb, slots / std::max(tiles, 1)), DG_MAX_SPLITS));
 }
 
-size_t pra_decode_gemm_workspace_floats() { return (size_t)DG_MAX_TILES * pra::dg::BF * pra::dg::MT; }
+// Launch with the split-K cluster (1 x splits CTAs) and programmatic dependent launch.
+template <int STAGES>
+static cudaError_t launch_dg(const CUtensorMap& map_w, const CUtensorMap& map_x, const DecodeGemmArgs& b, int tiles,
+                             cudaStream_t st) {
+  using namespace pra::dg;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles, b.splits);
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = Ring<STAGES>::SMEM_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (b.splits > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.y = b.splits;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (pra_pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  if (b.world > 1) {  // every slice waits for its peers: the whole grid must be resident at once
+    int clusters = 0;
+    PRA_RETURN_IF_ERROR(cudaOccupancyMaxActiveClusters(&clusters, decode_gemm_kernel<STAGES>, &cfg));
+    if (b.splits > 1 ? clusters < tiles : clusters < tiles * b.splits) return cudaErrorInvalidConfiguration;
+  }
+  return cudaLaunchKernelEx(&cfg, decode_gemm_kernel<STAGES>, map_w, map_x, b);
+}
 
 cudaError_t pra_decode_gemm(const DecodeGemmArgs& a, cudaStream_t st) {
   using namespace pra::dg;
@@ -401,11 +488,11 @@ cudaError_t pra_decode_gemm(const DecodeGemmArgs& a, cudaStream_t st) {
   const int tiles = (a.N + BF - 1) / BF;
   if (tiles > DG_MAX_TILES) return cudaErrorInvalidValue;
   const int nkb = a.K / BK;
-  int splits = a.splits < 1 ? 1 : (a.splits > nkb ? nkb : a.splits);
+  int splits = std::min(std::max(a.splits, 1), std::min(nkb, DG_MAX_SPLITS));
   const int per = (nkb + splits - 1) / splits;
   splits = (nkb + per - 1) / per;  // no empty split
-  if (splits > 1 && (a.workspace == nullptr || a.counters == nullptr)) return cudaErrorInvalidValue;
   if (a.world > 1 && (a.epochs == nullptr || a.error == nullptr)) return cudaErrorInvalidValue;
+  if (a.out_f32 && (a.bias || a.residual || a.out2 || a.pos || a.world > 1 || a.ldo % 4)) return cudaErrorInvalidValue;
   static int configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -414,6 +501,8 @@ cudaError_t pra_decode_gemm(const DecodeGemmArgs& a, cudaStream_t st) {
                                              Ring<6>::SMEM_BYTES));
     PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(decode_gemm_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              Ring<4>::SMEM_BYTES));
+    PRA_RETURN_IF_ERROR(cudaFuncSetAttribute(decode_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Ring<2>::SMEM_BYTES));
     configured[dev] = 1;
   }
   if ((reinterpret_cast<uintptr_t>(a.w) | reinterpret_cast<uintptr_t>(a.x)) & 15) return cudaErrorInvalidValue;
@@ -422,9 +511,7 @@ cudaError_t pra_decode_gemm(const DecodeGemmArgs& a, cudaStream_t st) {
   if (map_w == nullptr || map_x == nullptr) return cudaErrorInvalidValue;
   DecodeGemmArgs b = a;
   b.splits = splits;
-  if (pra_decode_gemm_ctas_per_sm() == 2)
-    decode_gemm_kernel<4><<<dim3(tiles, splits), NT, Ring<4>::SMEM_BYTES, st>>>(*map_w, *map_x, b);
-  else
-    decode_gemm_kernel<6><<<dim3(tiles, splits), NT, Ring<6>::SMEM_BYTES, st>>>(*map_w, *map_x, b);
-  return cudaGetLastError();
+  if (a.out_f32 != nullptr) return launch_dg<2>(*map_w, *map_x, b, tiles, st);
+  if (pra_decode_gemm_ctas_per_sm() == 2) return launch_dg<4>(*map_w, *map_x, b, tiles, st);
+  return launch_dg<6>(*map_w, *map_x, b, tiles, st);
 }

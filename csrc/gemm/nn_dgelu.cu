@@ -5,7 +5,53 @@ using Op = cutlass::epilogue::fusion::LinCombDeEltAct<cutlass::layout::RowMajor,
                                                       float>;
 using G = Gemm<cutlass::layout::RowMajor, cutlass::layout::RowMajor, BF16, Op>;
 
+cudaError_t pra_gemm_nn_dgelu_fused(const GemmArgs& g, cudaStream_t st);
+
+namespace pra {
+namespace gemm_ew {
+
+// D *= gelu'(Z) over bf16 rows, eight elements per thread and step.
+__global__ void __launch_bounds__(256) dgelu_rows_kernel(__nv_bfloat16* __restrict__ d,
+                                                         const __nv_bfloat16* __restrict__ z, int64_t n) {
+  const int64_t n8 = n / 8;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 rz = reinterpret_cast<const uint4*>(z)[i];
+    uint4 rd = reinterpret_cast<const uint4*>(d)[i];
+    const __nv_bfloat162* hz = reinterpret_cast<const __nv_bfloat162*>(&rz);
+    __nv_bfloat162* hd = reinterpret_cast<__nv_bfloat162*>(&rd);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 fz = __bfloat1622float2(hz[j]), fd = __bfloat1622float2(hd[j]);
+      hd[j] = __floats2bfloat162_rn(GeluErfGrad<float>()(fd.x, fz.x), GeluErfGrad<float>()(fd.y, fz.y));
+    }
+    reinterpret_cast<uint4*>(d)[i] = rd;
+  }
+  for (int64_t e = n8 * 8 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x)
+    d[e] = __float2bfloat16(GeluErfGrad<float>()(__bfloat162float(d[e]), __bfloat162float(z[e])));
+}
+
+}  // namespace gemm_ew
+}  // namespace pra
+
+// D = gelu'(Z) * (A . B): the plain GEMM, then the derivative applied in one streaming pass
+// (the fused form, which loads Z in the epilogue, measured ~2.8x the plain GEMM).
 cudaError_t pra_gemm_nn_dgelu(const GemmArgs& g, cudaStream_t st) {
+  if (g.alpha_ptr == nullptr && g.aux != nullptr) {
+    GemmArgs p = g;
+    p.C = nullptr;
+    p.beta = 0.f;
+    const cudaError_t e = pra_gemm_nn(p, st);
+    if (e != cudaSuccess) return e;
+    const int64_t n = (int64_t)g.M * g.N;
+    const int blocks = (int)std::min<int64_t>((n / 8 + 255) / 256 + 1, 148 * 16);
+    pra::gemm_ew::dgelu_rows_kernel<<<blocks, 256, 0, st>>>(static_cast<__nv_bfloat16*>(g.D), static_cast<const __nv_bfloat16*>(g.aux),
+                                              n);
+    return cudaGetLastError();
+  }
+  return pra_gemm_nn_dgelu_fused(g, st);
+}
+
+cudaError_t pra_gemm_nn_dgelu_fused(const GemmArgs& g, cudaStream_t st) {
   typename G::Epilogue::FusionCallbacks::Arguments fusion{};
   fusion.alpha = g.alpha;
   fusion.beta = 0.f;

@@ -80,8 +80,13 @@ cudaError_t pra_gemm_tn_bias(const GemmArgs& g, cudaStream_t stream);
 cudaError_t pra_gemm_tn_f32(const GemmArgs& g, cudaStream_t stream);  // fp32 D, no bias / C
 cudaError_t pra_gemm_tn_bias_small(const GemmArgs& g, cudaStream_t stream);  // M <= 128, stream-K
 cudaError_t pra_gemm_tn_bias_narrow(const GemmArgs& g, cudaStream_t stream);  // N <= 1024, 128x128 tiles
+// The GELU / GELU-derivative of the GEMM epilogues on fp32 values (numerics probe).
+cudaError_t pra_gelu_probe(const float* z, float* y, float* dy, int64_t n, cudaStream_t stream);
 cudaError_t pra_gemm_tn_bias_gelu(const GemmArgs& g, cudaStream_t stream);
 cudaError_t pra_gemm_nn(const GemmArgs& g, cudaStream_t stream);
+// Stream-K variants (128 x 256 tiles) for long reductions into few output tiles.
+cudaError_t pra_gemm_nn_sk(const GemmArgs& g, cudaStream_t stream);
+cudaError_t pra_gemm_wgrad_sk(const GemmArgs& g, cudaStream_t stream);
 cudaError_t pra_gemm_nn_dgelu(const GemmArgs& g, cudaStream_t stream);
 cudaError_t pra_gemm_wgrad(const GemmArgs& g, cudaStream_t stream);
 
@@ -280,10 +285,22 @@ struct DecodeAttnParams {
   BoundsStatus* bounds;        // non-null: run the bounds-checked variant
   int mem_on_device;           // the memory pool is device memory (TMA-fed kernel allowed)
   int* status;                 // optional: set to 1 by a CTA that gave up on a bounded wait
+  // Split layout.  mem_splits == 0: the splits tile each row's [memory ; local] key sequence.
+  // mem_splits > 0: splits [0, mem_splits) tile the memory keys and splits [mem_splits,
+  // n_split) tile the local cache on their own, so the local splits never read mem_len / mem_idx
+  // and can run while the routing that produces them is still in flight.
+  int mem_splits;
+  int mem_split_keys;          // keys per memory split when mem_splits > 0 (0: split_keys; <= split_keys)
+  int split_lo, split_count;   // the splits this launch runs (split_count 0: all n_split)
+  int phase;                   // 0: attention then merge; 1: attention only; 2: merge only
 };
 cudaError_t pra_decode_attention(const DecodeAttnParams& p, int head_dim, cudaStream_t stream);
 // 1 (default): eligible decode attention calls run the TMA-fed kernel; 0: the cp.async kernel.
 void pra_decode_set_tma(int on);
+// Whether the instrumented decode kernels (decode GEMM, RMSNorm, SwiGLU, routing, decode
+// attention and its merge) are launched with programmatic stream serialization (default on).
+void pra_set_pdl(int on);
+int pra_pdl_enabled();
 // Pipeline stages of the TMA-fed decode kernel (2, 3 or 4; 2 by default).
 void pra_decode_set_stages(int stages);
 
@@ -292,7 +309,8 @@ struct RouteTopkArgs {
   int G;                       // gists per chunk: scores / gists hold C * G rows, chunk score = max over G
   const float* scores;         // [B, score_stride] approximate cosine scores (tensor-core GEMM)
   int64_t score_stride;
-  const float* query;          // [B, query_stride] routing queries (fp32, unnormalised)
+  const float* query;          // [B, query_stride] routing queries (fp32, unnormalised), or
+  const __nv_bfloat16* query_bf16;  // the same in bf16 (set instead of query: read and widened in the kernel)
   int64_t query_stride;
   const float* gists;          // [C, D] L2-normalised fp32 gists (exact rescoring)
   const int* ns_start;         // [B] namespace of row b: chunks [ns_start, ns_end)
@@ -396,6 +414,7 @@ cudaError_t pra_embed_add(const int* ids, const int* positions, int period, cons
 // (columns >= split_col go to out2), or, with world > 1, the fused all-reduce of a row-parallel
 // projection (every rank's bf16 partial tile pushed to every rank, per-tile flags, residual + sum).
 constexpr int DG_MAX_TILES = 1024;
+constexpr int DG_MAX_SPLITS = 8;  // split-K CTAs of one tile: one portable thread-block cluster
 struct DecodeGemmArgs {
   const __nv_bfloat16* x;  // [M, K] rows at stride ldx
   int64_t ldx;
@@ -404,17 +423,16 @@ struct DecodeGemmArgs {
   const __nv_bfloat16* bias;      // [N] or null
   const __nv_bfloat16* residual;  // [M, N] (row stride ldo) or null
   __nv_bfloat16* out;             // columns [0, split_col): out[m * ldo + n]
+  float* out_f32;                 // instead of out: fp32 results (no bias / residual / out2; one GPU)
   int64_t ldo;
   __nv_bfloat16* out2;            // columns [split_col, N): out2[m * ldo2 + n - split_col] (null: none)
   int64_t ldo2;
   int split_col;
-  float* workspace;               // split-K partial sums [tiles, 128, 64] (zero between calls)
-  uint32_t* counters;             // split-K arrivals [tiles] (zero between calls)
   // fused all-reduce (world > 1)
   int world, rank;
   __nv_bfloat16* recv[TP_MAX_RANKS];  // every rank's receive half: [world][M][N]
-  uint32_t* flags[TP_MAX_RANKS];      // every rank's flag half: [DG_MAX_TILES][world]
-  uint32_t* epochs;                   // local per-tile call counters [DG_MAX_TILES]
+  uint32_t* flags[TP_MAX_RANKS];      // every rank's flag half: [DG_MAX_TILES * DG_MAX_SPLITS][world]
+  uint32_t* epochs;                   // local per-(tile, row slice) call counters [DG_MAX_TILES * DG_MAX_SPLITS]
   long long max_spins;
   int* error;                         // 1 + phase after a bounded wait gave up
   // rotary decode-QKV epilogue (pos != null, world == 1): columns [0, q_end) are query heads
@@ -432,8 +450,9 @@ struct DecodeGemmArgs {
   int64_t ld_cache;
   const int* cache_rows;              // [M]
 };
-size_t pra_decode_gemm_workspace_floats();
-// Launch shape of the decode GEMM: 1 (6-stage ring) or 2 (4-stage ring) CTAs per SM, and the
+// Launch shape of the decode GEMM: 1 (6-stage ring) or 2 (4-stage ring) CTAs per SM (fp32-output
+// launches, the routing scores, use a 2-stage ring: a small footprint that fits beside the
+// decode-attention CTAs it runs concurrently with), and the
 // fewest 64-deep K blocks a split keeps; defaults 2 and 8.  pra_decode_gemm_splits picks the
 // K split of a launch from them (the grid fills the CTA slots once).
 void pra_decode_gemm_configure(int ctas_per_sm, int min_blocks_per_split);

@@ -49,6 +49,8 @@ __global__ void rope_copy_kernel(RopeCopyArgs a) {
 
 // ---------------------------------------------------------------- swiglu
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int64_t M, int F, __nv_bfloat16* __restrict__ out) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t pairs = M * (F / 2);
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < pairs; e += (int64_t)gridDim.x * blockDim.x) {
     const int64_t m = e / (F / 2);
@@ -86,10 +88,12 @@ __global__ void __launch_bounds__(DT) decode_kernel(DecodeAttnParams p) {
 
   const int G = p.H / p.Hkv;
   const int b = blockIdx.x / p.Hkv, kvh = blockIdx.x % p.Hkv;
-  const int split = blockIdx.y;
+  const int split = p.split_lo + blockIdx.y;
+  const bool local_only = p.mem_splits > 0 && split >= p.mem_splits;
+  const bool mem_only = p.mem_splits > 0 && split < p.mem_splits;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int mem_len = p.mem_len ? p.mem_len[b] : 0;
-  int loc_len = p.loc_len ? p.loc_len[b] : 0;
+  int mem_len = (!local_only && p.mem_len) ? p.mem_len[b] : 0;
+  int loc_len = (!mem_only && p.loc_len) ? p.loc_len[b] : 0;
   if constexpr (CHECK) {  // lengths past their buffers: record, then clamp (the extra keys are skipped)
     if (mem_len < 0 || mem_len > p.mem_max) {
       if (threadIdx.x == 0) bounds_fail(p.bounds, PRA_BOUNDS_DECODE_MEM_LEN, mem_len, p.mem_max);
@@ -101,7 +105,8 @@ __global__ void __launch_bounds__(DT) decode_kernel(DecodeAttnParams p) {
     }
   }
   const int total = mem_len + loc_len;
-  const int k0 = split * p.split_keys, k1 = min(total, k0 + p.split_keys);
+  const int keys = mem_only && p.mem_split_keys > 0 ? p.mem_split_keys : p.split_keys;
+  const int k0 = (local_only ? split - p.mem_splits : split) * keys, k1 = min(total, k0 + keys);
   const int64_t part = ((int64_t)b * p.H + kvh * G) * p.n_split + split;  // first head of the group
 
   // queries of the group (rows >= G are zero)
@@ -312,11 +317,23 @@ __global__ void __launch_bounds__(DT) decode_tma_kernel(const __grid_constant__ 
 
   const int G = p.H / p.Hkv;
   const int b = blockIdx.x / p.Hkv, kvh = blockIdx.x % p.Hkv;
-  const int split = blockIdx.y;
+  const int split = p.split_lo + blockIdx.y;
+  const bool local_only = p.mem_splits > 0 && split >= p.mem_splits;
+  const bool mem_only = p.mem_splits > 0 && split < p.mem_splits;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int mem_len = p.mem_len ? p.mem_len[b] : 0;
-  const int total = mem_len + (p.loc_len ? p.loc_len[b] : 0);
-  const int k0 = split * p.split_keys, k1 = min(total, k0 + p.split_keys);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TST; ++s) mbar_init(full + s, 1);
+    s_fail = 0;
+    tc::fence_mbarrier_init();
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(&map_lk) : "memory");
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(&map_lv) : "memory");
+  }
+  pdl_launch_dependents();
+  pdl_wait();  // q, the new cache row and the routed row lists come from the kernels before
+  const int mem_len = (!local_only && p.mem_len) ? p.mem_len[b] : 0;
+  const int total = mem_len + ((!mem_only && p.loc_len) ? p.loc_len[b] : 0);
+  const int keys = mem_only && p.mem_split_keys > 0 ? p.mem_split_keys : p.split_keys;
+  const int k0 = (local_only ? split - p.mem_splits : split) * keys, k1 = min(total, k0 + keys);
   const int64_t part = ((int64_t)b * p.H + kvh * G) * p.n_split + split;
   const int loc_rows = (int)(p.loc_batch / p.loc_row);  // cache rows per batch row
 
@@ -328,11 +345,6 @@ __global__ void __launch_bounds__(DT) decode_tma_kernel(const __grid_constant__ 
   }
   for (int j = k0 + threadIdx.x; j < k1; j += DT)
     srow[j - k0] = j < mem_len ? p.mem_idx[(int64_t)b * p.mem_max + j] : -(j - mem_len + 1);
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < TST; ++s) mbar_init(full + s, 1);
-    s_fail = 0;
-    tc::fence_mbarrier_init();
-  }
   __syncthreads();
   const int n_blocks = k1 > k0 ? (k1 - k0 + DBN - 1) / DBN : 0;
   // classify the blocks (warp per block): one contiguous run of rows -> one TMA box per 64 columns
@@ -533,6 +545,8 @@ __global__ void __launch_bounds__(DT) decode_tma_kernel(const __grid_constant__ 
 // Merge the splits of each (row, head): out = sum_s o_s e^{m_s - M} / sum_s l_s e^{m_s - M}.
 // With export_ml the merged (M, L) and unnormalised out are also written (cross-GPU combine).
 __global__ void decode_merge_kernel(DecodeAttnParams p, int D) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int bh = blockIdx.x;
   const int b = bh / p.H, h = bh % p.H;
   const int64_t base = (int64_t)bh * p.n_split;
@@ -713,6 +727,8 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a, RouteEx
   __shared__ int n_sel;
   // CTA = (query row, segment): with several segments each CTA selects among one slice
   // of the row's chunks and writes local candidates that a merge pass combines
+  pdl_launch_dependents();
+  pdl_wait();  // the scores and the routing query come from the GEMMs before
   const int S = a.segments > 0 ? a.segments : 1;
   const int b = blockIdx.x;
   const int qb = b / S, seg = b % S;
@@ -841,7 +857,8 @@ __global__ void __launch_bounds__(RT) route_topk_kernel(RouteTopkArgs a, RouteEx
   float* qs = seg_scores;
   float sq = 0.f;
   for (int d = threadIdx.x; d < a.D; d += RT) {
-    const float v = a.query[(int64_t)qb * a.query_stride + d];
+    const float v = a.query_bf16 ? __bfloat162float(a.query_bf16[(int64_t)qb * a.query_stride + d])
+                                 : a.query[(int64_t)qb * a.query_stride + d];
     qs[d] = v;
     sq += v * v;
   }
@@ -1017,7 +1034,7 @@ cudaError_t pra_silu_mul(const __nv_bfloat16* gate_up, int64_t M, int F, __nv_bf
   const int64_t pairs = M * (F / 2);
   const int64_t want = (pairs + 255) / 256;
   const int blocks = (int)(want < 148 * 16 ? want : 148 * 16);
-  pra::llama::silu_mul_kernel<<<blocks, 256, 0, st>>>(gate_up, M, F, out);
+  PRA_RETURN_IF_ERROR(pra_launch_pdl(pra::llama::silu_mul_kernel, dim3(blocks), dim3(256), 0, st, gate_up, M, F, out));
   return cudaGetLastError();
 }
 
@@ -1028,20 +1045,25 @@ static cudaError_t launch_decode(DecodeAttnParams p, cudaStream_t st) {
   static_assert(2 * DSTAGES * DBN * LD * sizeof(__nv_bfloat16) >= 4 * 16 * (D + 2) * sizeof(float),
                 "merge buffer must fit in the staging area");
   const size_t smem = (size_t)(16 + 2 * DSTAGES * DBN) * LD * sizeof(__nv_bfloat16) + (size_t)p.split_keys * sizeof(int);
-  const dim3 grid(p.B * p.Hkv, p.n_split);
-  if (p.bounds != nullptr) {
-    PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(decode_kernel<D, true>), (int)smem));
-    decode_kernel<D, true><<<grid, DT, smem, st>>>(p);
-  } else {
-    PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(decode_kernel<D, false>), (int)smem));
-    decode_kernel<D, false><<<grid, DT, smem, st>>>(p);
+  const dim3 grid(p.B * p.Hkv, p.split_count > 0 ? p.split_count : p.n_split);
+  if (p.phase != 2) {
+    if (p.bounds != nullptr) {
+      PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(decode_kernel<D, true>), (int)smem));
+      decode_kernel<D, true><<<grid, DT, smem, st>>>(p);
+    } else {
+      PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(decode_kernel<D, false>), (int)smem));
+      decode_kernel<D, false><<<grid, DT, smem, st>>>(p);
+    }
+    PRA_RETURN_IF_ERROR(cudaGetLastError());
   }
-  PRA_RETURN_IF_ERROR(cudaGetLastError());
-  decode_merge_kernel<<<p.B * p.H, 128, 0, st>>>(p, D);
+  if (p.phase != 1) decode_merge_kernel<<<p.B * p.H, 128, 0, st>>>(p, D);
   return cudaGetLastError();
 }
 
 static int g_decode_tma = 1;
+static int g_pdl = 1;
+void pra_set_pdl(int on) { g_pdl = on ? 1 : 0; }
+int pra_pdl_enabled() { return g_pdl; }
 static int g_decode_stages = pra::llama::TST_DEFAULT;
 void pra_decode_set_tma(int on) { g_decode_tma = on; }
 void pra_decode_set_stages(int stages) { g_decode_stages = stages; }
@@ -1054,7 +1076,9 @@ static cudaError_t launch_decode_tma_stages(const DecodeAttnParams& p, const CUt
   const size_t smem = 1024 + (size_t)TST * Lay::STAGE + 16 * Lay::QLD * 2 + (size_t)(p.split_keys + 2 * TMAX_BLOCKS) * 4 +
                       TST * 8;
   PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(decode_tma_kernel<D, TST>), (int)smem));
-  decode_tma_kernel<D, TST><<<dim3(p.B * p.Hkv, p.n_split), DT, smem, st>>>(*mk, *mv, *lk, *lv, p);
+  PRA_RETURN_IF_ERROR(pra_launch_pdl(decode_tma_kernel<D, TST>,
+                                     dim3(p.B * p.Hkv, p.split_count > 0 ? p.split_count : p.n_split), dim3(DT), smem,
+                                     st, *mk, *mv, *lk, *lv, p));
   return cudaGetLastError();
 }
 
@@ -1075,16 +1099,23 @@ static cudaError_t launch_decode_tma(const DecodeAttnParams& p, cudaStream_t st)
   const CUtensorMap* mk = has_mem ? pra_tile_map_bf16(p.mem_k, width, p.mem_rows, p.mem_row, DBN) : lk;
   const CUtensorMap* mv = has_mem ? pra_tile_map_bf16(p.mem_v, width, p.mem_rows, p.mem_row, DBN) : lv;
   if (!lk || !lv || !mk || !mv) return cudaErrorNotSupported;
-  if (g_decode_stages == 2) PRA_RETURN_IF_ERROR((launch_decode_tma_stages<D, 2>(p, mk, mv, lk, lv, st)));
-  else if (g_decode_stages == 4) PRA_RETURN_IF_ERROR((launch_decode_tma_stages<D, 4>(p, mk, mv, lk, lv, st)));
-  else PRA_RETURN_IF_ERROR((launch_decode_tma_stages<D, 3>(p, mk, mv, lk, lv, st)));
-  decode_merge_kernel<<<p.B * p.H, 128, 0, st>>>(p, D);
+  if (p.phase != 2) {
+    if (g_decode_stages == 2) PRA_RETURN_IF_ERROR((launch_decode_tma_stages<D, 2>(p, mk, mv, lk, lv, st)));
+    else if (g_decode_stages == 4) PRA_RETURN_IF_ERROR((launch_decode_tma_stages<D, 4>(p, mk, mv, lk, lv, st)));
+    else PRA_RETURN_IF_ERROR((launch_decode_tma_stages<D, 3>(p, mk, mv, lk, lv, st)));
+  }
+  if (p.phase != 1) PRA_RETURN_IF_ERROR(pra_launch_pdl(decode_merge_kernel, dim3(p.B * p.H), dim3(128), 0, st, p, D));
   return cudaGetLastError();
 }
 
 cudaError_t pra_decode_attention(const DecodeAttnParams& p, int head_dim, cudaStream_t st) {
   if (p.B == 0) return cudaSuccess;
   if (p.H % p.Hkv || p.H / p.Hkv > 16 || p.split_keys % pra::llama::DBN || p.split_keys > 4096)
+    return cudaErrorInvalidValue;
+  const int count = p.split_count > 0 ? p.split_count : p.n_split;
+  if (p.mem_splits < 0 || p.mem_splits > p.n_split || p.split_lo < 0 || p.split_lo + count > p.n_split ||
+      p.phase < 0 || p.phase > 2 || p.mem_split_keys < 0 || p.mem_split_keys % pra::llama::DBN ||
+      p.mem_split_keys > p.split_keys)
     return cudaErrorInvalidValue;
   cudaError_t e = cudaErrorNotSupported;
   if (head_dim == 128) e = launch_decode_tma<128>(p, st);
@@ -1118,8 +1149,12 @@ cudaError_t pra_route_topk(const RouteTopkArgs& a, cudaStream_t st) {
   const int S = a.segments > 0 ? a.segments : 1;
   if (S > 1 && (a.cand_score == nullptr || a.seg_len <= 0)) return cudaErrorInvalidValue;  // segments need a merge
   const RouteExchangeArgs none{};
-  if (a.bounds != nullptr) pra::llama::route_topk_kernel<true, false><<<a.B * S, pra::llama::RT, 0, st>>>(a, none);
-  else pra::llama::route_topk_kernel<false, false><<<a.B * S, pra::llama::RT, 0, st>>>(a, none);
+  if (a.bounds != nullptr)
+    PRA_RETURN_IF_ERROR(pra_launch_pdl(pra::llama::route_topk_kernel<true, false>, dim3(a.B * S), dim3(pra::llama::RT),
+                                       0, st, a, none));
+  else
+    PRA_RETURN_IF_ERROR(pra_launch_pdl(pra::llama::route_topk_kernel<false, false>, dim3(a.B * S),
+                                       dim3(pra::llama::RT), 0, st, a, none));
   return cudaGetLastError();
 }
 
@@ -1132,7 +1167,11 @@ cudaError_t pra_route_topk_exchange(const RouteTopkArgs& a, const RouteExchangeA
     return cudaErrorInvalidValue;
   for (int p = 0; p < x.world; ++p)
     if (!x.recv[p] || !x.flags[p]) return cudaErrorInvalidValue;
-  if (a.bounds != nullptr) pra::llama::route_topk_kernel<true, true><<<a.B, pra::llama::RT, 0, st>>>(a, x);
-  else pra::llama::route_topk_kernel<false, true><<<a.B, pra::llama::RT, 0, st>>>(a, x);
+  if (a.bounds != nullptr)
+    PRA_RETURN_IF_ERROR(pra_launch_pdl(pra::llama::route_topk_kernel<true, true>, dim3(a.B), dim3(pra::llama::RT), 0,
+                                       st, a, x));
+  else
+    PRA_RETURN_IF_ERROR(pra_launch_pdl(pra::llama::route_topk_kernel<false, true>, dim3(a.B), dim3(pra::llama::RT), 0,
+                                       st, a, x));
   return cudaGetLastError();
 }

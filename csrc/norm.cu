@@ -17,6 +17,8 @@ __global__ void __launch_bounds__(NT) fwd_kernel(const __nv_bfloat16* __restrict
                                                  float* __restrict__ mean_out, float* __restrict__ rstd_out, int M,
                                                  int D, float eps) {
   __shared__ float scratch[32];
+  pdl_launch_dependents();
+  pdl_wait();
   const int row = blockIdx.x;
   if (row >= M) return;
   const __nv_bfloat162* xr = reinterpret_cast<const __nv_bfloat162*>(x + (int64_t)row * D);
@@ -85,6 +87,8 @@ __global__ void __launch_bounds__(256) fwd_warp_kernel(const __nv_bfloat16* __re
                                                        const __nv_bfloat16* __restrict__ b, __nv_bfloat16* __restrict__ y,
                                                        float* __restrict__ mean_out, float* __restrict__ rstd_out,
                                                        int M, int D, float eps) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= M) return;
@@ -335,13 +339,17 @@ cudaError_t pra_norm_fwd(const __nv_bfloat16* x, const __nv_bfloat16* w, const _
   if (M == 0) return cudaSuccess;
   if (D % 8 == 0 && D <= 32 * 8 * WCH) {
     const int blocks = (M + 7) / 8;
-    if (rms) fwd_warp_kernel<true><<<blocks, 256, 0, st>>>(x, w, nullptr, y, nullptr, rstd, M, D, eps);
-    else fwd_warp_kernel<false><<<blocks, 256, 0, st>>>(x, w, b, y, mean, rstd, M, D, eps);
-    return cudaGetLastError();
+    const __nv_bfloat16* no_bias = nullptr;
+    float* no_mean = nullptr;
+    if (rms)
+      return pra_launch_pdl(fwd_warp_kernel<true>, dim3(blocks), dim3(256), 0, st, x, w, no_bias, y, no_mean, rstd, M, D,
+                            eps);
+    return pra_launch_pdl(fwd_warp_kernel<false>, dim3(blocks), dim3(256), 0, st, x, w, b, y, mean, rstd, M, D, eps);
   }
-  if (rms) fwd_kernel<true><<<M, NT, 0, st>>>(x, w, nullptr, y, nullptr, rstd, M, D, eps);
-  else fwd_kernel<false><<<M, NT, 0, st>>>(x, w, b, y, mean, rstd, M, D, eps);
-  return cudaGetLastError();
+  const __nv_bfloat16* no_bias = nullptr;
+  float* no_mean = nullptr;
+  if (rms) return pra_launch_pdl(fwd_kernel<true>, dim3(M), dim3(NT), 0, st, x, w, no_bias, y, no_mean, rstd, M, D, eps);
+  return pra_launch_pdl(fwd_kernel<false>, dim3(M), dim3(NT), 0, st, x, w, b, y, mean, rstd, M, D, eps);
 }
 
 int pra_norm_bwd_partials(int M) { return M == 0 ? 1 : (M + 31) / 32 > 592 ? 592 : (M + 31) / 32; }

@@ -7,8 +7,10 @@ warm-up, the max over ranks.  The roofline of a fused kernel is the slower of it
 measured peer-copy rate (770 GB/s per direction per GPU on this pool):
 
 * ``dp_allreduce``: the data-parallel gradient reduction of the TinyGPT-PRA-163M flat
-  buffer (bf16 in place): each rank reads (w-1)/w of the buffer from its peers and writes
-  its slice's result into every peer, 2 bytes per element each way;
+  buffer (bf16 in place).  Rank r reduces slice r: it reads that slice from its w-1 peers
+  while they read their slices from it, then stores its result into every peer while they
+  store theirs into it, so each link direction carries 2 (w-1)/w of the buffer (the
+  all-reduce "bus" volume);
 * ``decode_gemm_allreduce``: the row-parallel decode projections (64 rows; Llama-3-8B O
   and down shards) with the partial pushed to every rank and summed where it lands,
   against the unfused GEMM + one-shot all-reduce; HBM floor = the weight shard read once;
@@ -75,11 +77,11 @@ def dp_allreduce(world: int, rank: int, device, iters: int = 20, numel: int = 16
 
     us = _time(call, iters, world, device)
     assert int(error.item()) == 0, "a wait of the reduction timed out"
-    link_bytes = (world - 1) / world * 2 * n  # per direction per GPU (bf16 in, bf16 out)
+    link_bytes = 2 * (world - 1) / world * 2 * n  # per direction per GPU: peer reads + result stores, bf16
     floor_us = link_bytes / (NVLINK_GBS * 1e3)
     bufs.close()
     return {"case": "dp_allreduce (bf16 in place)", "elements": n, "us": us,
-            "nvlink_gb_per_direction": link_bytes / 1e9, "achieved_gbs": link_bytes / us / 1e3,
+            "nvlink_gb_per_direction": link_bytes / 1e9, "bus_gbs": link_bytes / us / 1e3,
             "roofline_us": floor_us, "fraction_of_roofline": floor_us / us}
 
 

@@ -165,7 +165,7 @@ class PRALlamaEngine:
 
     def __init__(self, weights: LlamaWeights, device, tp=None, decode_split_keys: int | None = None,
                  k_cand_factor: int = 4,
-                 shard_routing: bool = True, kv_residency: str = "gpu"):
+                 shard_routing: bool = True, kv_residency: str = "gpu", overlap_routing: bool | None = None):
         self.w = weights
         self.cfg = weights.cfg
         self.device = torch.device(device)
@@ -185,6 +185,14 @@ class PRALlamaEngine:
         # on the device (gists) and the attention kernels gather only the selected rows over the
         # host link (a memory larger than the GPU's HBM at the cost of link bandwidth per step)
         self.kv_residency = kv_residency
+        # Decode: the local-window attention splits run on the current stream while routing and
+        # the memory splits run on a high-priority side stream (PRA_ROUTE_OVERLAP=0: serial).
+        if overlap_routing is None:
+            overlap_routing = os.environ.get("PRA_ROUTE_OVERLAP", "1") != "0"
+        self.overlap_routing = overlap_routing and self.device.type == "cuda"
+        self._route_stream: torch.cuda.Stream | None = None
+        self._parts: tuple[tuple[int, int], torch.Tensor, torch.Tensor] | None = None
+        self._bounds_cache: tuple | None = None
         self.ext = _ext.require()
         self._rope_cache: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
         self.memory: ChunkMemory | None = None
@@ -312,7 +320,7 @@ class PRALlamaEngine:
         cfg, mem = self.cfg, self.memory
         if route_query is not None:
             rqn = route_query
-            rq = route_query.float()
+            rq = route_query  # bf16: the routing kernel widens it while staging it in shared memory
         else:
             rq = q_rows.float().view(rows, self.kv_heads, cfg.group, cfg.head_dim).mean(2).reshape(rows, self.kv_dim)
             if self.tp is not None:
@@ -330,7 +338,7 @@ class PRALlamaEngine:
         shards = self.tp.world if (self.tp is not None and self.shard_routing and pages is None) else 1
         if shards == 1:
             scores = torch.empty((rows, mem.C_pad), device=self.device, dtype=torch.float32)
-            self.ext.gemm("tn_f32", rqn, mem.gn_bf16[layer], None, scores, None, None, 1.0, 0.0, None)
+            self._score(rqn, mem.gn_bf16[layer], scores)
             mem_idx, mem_len, sel = select_chunks(self.ext, scores, rq, gn, start, end, mem.chunk_len,
                                                   mem.chunk_row0, k, k_cand, budget, mem_max,
                                                   pool_rows=mem.pool.shape[1], page_table=pages)
@@ -340,15 +348,35 @@ class PRALlamaEngine:
             c0, c1 = self._route_slice(mem)
             width = c1 - c0
             scores = torch.empty((rows, width), device=self.device, dtype=torch.float32)
-            self.ext.gemm("tn_f32", rqn, mem.gn_bf16[layer][c0:c1], None, scores, None, None, 1.0, 0.0, None)
-            lo = (start - c0).clamp(0, width).to(torch.int32)
-            hi = (end - c0).clamp(0, width).to(torch.int32)
+            self._score(rqn, mem.gn_bf16[layer][c0:c1], scores)
+            lo, hi = self._slice_bounds(start, end, c0, width)
             mem_idx, mem_len, sel = select_chunks(self.ext, scores, rq, gn[c0:c1], lo, hi, mem.chunk_len,
                                                   mem.chunk_row0, k, k_cand, budget, mem_max, id_offset=c0,
                                                   comm=self.tp, global_len=mem.chunk_len,
                                                   global_row0=mem.chunk_row0, pool_rows=mem.pool.shape[1])
         self.last_selection[layer] = sel
         return mem_idx, mem_len
+
+    def _score(self, rqn: torch.Tensor, gists: torch.Tensor, scores: torch.Tensor) -> None:
+        """fp32 query x gist scores.  Decode rows use the tcgen05 decode GEMM with a 2-stage ring:
+        its CTAs fit beside the local-window attention CTAs they overlap with (a persistent
+        library-style GEMM needs a whole SM and waits for the attention to drain one)."""
+        if self._decode_rows(rqn) and gists.shape[1] % 64 == 0 and gists.shape[0] % 8 == 0:
+            self.ext.decode_gemm(rqn, gists, None, None, scores, None, 0, 0, [], [], 0, None, 0, None)
+        else:
+            self.ext.gemm("tn_f32", rqn, gists, None, scores, None, None, 1.0, 0.0, None)
+
+    def _slice_bounds(self, start: torch.Tensor, end: torch.Tensor, c0: int, width: int):
+        """Each row's namespace clipped to this rank's chunk slice, as slice-local int32 bounds.
+        Computed once per (namespace, slice) and kept: the decode steps of a batch share it (a
+        new namespace is a new pair of tensors from ``set_namespace``)."""
+        key = (start.data_ptr(), end.data_ptr(), start.numel(), end.numel(), start._version, end._version, c0, width)
+        cached = self._bounds_cache
+        if cached is None or cached[0] != key:
+            lo = (start - c0).clamp(0, width).to(torch.int32)
+            hi = (end - c0).clamp(0, width).to(torch.int32)
+            self._bounds_cache = cached = (key, lo, hi, start, end)  # holds the inputs: their addresses stay theirs
+        return cached[1], cached[2]
 
     def _route_slice(self, mem) -> tuple[int, int]:
         """This rank's chunk slice for sharded routing (8-aligned, covers the padded table)."""
@@ -572,15 +600,67 @@ class PRALlamaEngine:
                 ext.rope_copy(qkv[:, qd + kd:], vc, rows, None, None, None, self.kv_heads, cfg.head_dim)
                 ext.rope_copy(qkv[:, :qd], q, None, pos, cos, sin, self.heads, cfg.head_dim)
             mem_args = (None, None, None, None)
-            if use_memory and cfg.is_pra_layer(li):
-                mem_idx, mem_len = self._route(li, None if qkv is None else qkv[:, :qd], B, route_query=rq)
-                mem_args = (self.memory.k(li), self.memory.v(li), mem_idx, mem_len)
-            a = ext.decode_attention(q, self.heads, self.kv_heads, cfg.head_dim, *mem_args, self.cache[li, 0],
-                                     self.cache[li, 1], new_len, max_keys, self._split_for(B, max_keys), False)[0]
+            routed = use_memory and cfg.is_pra_layer(li)
+            if routed and self.overlap_routing:
+                a = self._attend_overlapped(li, q, None if qkv is None else qkv[:, :qd], rq, new_len, max_keys)
+            else:
+                if routed:
+                    mem_idx, mem_len = self._route(li, None if qkv is None else qkv[:, :qd], B, route_query=rq)
+                    mem_args = (self.memory.k(li), self.memory.v(li), mem_idx, mem_len)
+                a = ext.decode_attention(q, self.heads, self.kv_heads, cfg.head_dim, *mem_args, self.cache[li, 0],
+                                         self.cache[li, 1], new_len, max_keys, self._split_for(B, max_keys), False)[0]
             x = self._row_parallel(a, lw.o, x)
             x = self._mlp(lw, x)
         self.cache_len.copy_(new_len)  # in place: a captured step replays on the same tensors
         return self._greedy(x) if sample else self._logits(x)
+
+    def _partials(self, B: int, n_split: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """Split partials ``(o [B, H, n, Dh], (max, sum) [B, H, n, 2])`` shared by the phases of
+        one overlapped decode attention; kept across layers and steps (stream order separates
+        their uses: the next layer's splits are enqueued after this layer's merge)."""
+        key = (B, n_split)
+        if self._parts is None or self._parts[0] != key:
+            H, D = self.heads, self.cfg.head_dim
+            self._parts = (key, torch.empty((B, H, n_split, D), device=self.device, dtype=torch.float32),
+                           torch.empty((B, H, n_split, 2), device=self.device, dtype=torch.float32))
+        return self._parts[1], self._parts[2]
+
+    def _attend_overlapped(self, li: int, q: torch.Tensor, q_rows, rq, new_len: torch.Tensor,
+                           max_keys: int) -> torch.Tensor:
+        """Decode attention of a routed layer with routing off the critical path.
+
+        The local-window splits need only the queries and the cache, so they are enqueued first
+        on the current stream; a high-priority side stream then scores the gists, selects the
+        chunks (with the cross-GPU exchange under tensor parallelism) and attends over the
+        selected memory rows into splits ``[0, n_mem)`` of the same partials; the merge runs
+        after both.  Same result as the single launch: the merge weighs every split by its own
+        (max, sum), whatever the split layout."""
+        cfg, ext = self.cfg, self.ext
+        B = q.shape[0]
+        sk = self._split_for(B, max_keys)
+        # memory splits of at most 256 keys: many short CTAs that start as soon as routing ends
+        # and slot in between the local splits' CTAs
+        msk = min(sk, 256)
+        n_mem = max(1, -(-cfg.memory_tokens_per_row // msk))
+        n_loc = -(-self.max_len // sk)
+        part_o, part_ml = self._partials(B, n_mem + n_loc)
+        kc, vc = self.cache[li, 0], self.cache[li, 1]
+        H, Hkv, D = self.heads, self.kv_heads, cfg.head_dim
+        common = dict(mem_splits=n_mem, mem_split_keys=msk, part_o=part_o, part_ml=part_ml)
+        main = torch.cuda.current_stream(self.device)
+        if self._route_stream is None:
+            self._route_stream = torch.cuda.Stream(self.device, priority=-1)
+        side = self._route_stream
+        side.wait_stream(main)  # fork before the local splits: routing must not wait for them
+        ext.decode_attention(q, H, Hkv, D, None, None, None, None, kc, vc, new_len, 0, sk, False,
+                             split_lo=n_mem, split_count=n_loc, phase=1, **common)
+        with torch.cuda.stream(side):
+            mem_idx, mem_len = self._route(li, q_rows, B, route_query=rq)
+            ext.decode_attention(q, H, Hkv, D, self.memory.k(li), self.memory.v(li), mem_idx, mem_len, kc, vc,
+                                 new_len, 0, sk, False, split_lo=0, split_count=n_mem, phase=1, **common)
+        main.wait_stream(side)
+        return ext.decode_attention(q, H, Hkv, D, None, None, None, None, kc, vc, new_len, 0, sk, False, phase=2,
+                                    **common)[0]
 
     # -- CUDA-graph decode ------------------------------------------------------------
     def capture_decode(self, sample: bool = False) -> None:

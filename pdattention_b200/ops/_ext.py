@@ -24,7 +24,7 @@ BUILD_DIR = Path(__file__).resolve().parent / "_build"
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 _SOURCES = ["bindings.cpp", "attention.cu", "attention_tc.cu", "norm.cu", "loss_optim.cu", "gist.cu", "routing.cu", "llama.cu",
-            "gemm/tn_bias.cu", "gemm/tn_bias_gelu.cu", "gemm/nn.cu", "gemm/nn_dgelu.cu", "gemm/wgrad.cu", "gemm/tn_f32.cu", "gemm/tn_bias_small.cu", "gemm/tn_bias_narrow.cu",
+            "gemm/tn_bias.cu", "gemm/tn_bias_gelu.cu", "gemm/nn.cu", "gemm/nn_dgelu.cu", "gemm/wgrad.cu", "gemm/tn_f32.cu", "gemm/tn_bias_small.cu", "gemm/tn_bias_narrow.cu", "gemm/nn_sk.cu", "gemm/wgrad_sk.cu",
             "planner.cpp", "decode_gemm.cu", "dropout.cu", "colsum_noalloc.cu", "dp_reduce.cu", "tp_comm.cu", "embed.cu", "driver_shim.cu"]
 
 _module = None
@@ -37,8 +37,8 @@ KERNELS_PER_CALL = {"attention_fwd": 1, "attention_bwd": 3, "gemm": 1, "norm_fwd
                     "stack_forward": 0, "stack_train_forward": 0, "stack_train_backward": 0, "dp_allreduce": 1, "dp_signal_words": 0,
                     "ipc_alloc": 0, "ipc_open": 0, "ipc_close": 0,
                     "rope_copy": 1, "silu_mul": 1, "decode_attention": 2, "route_topk": 1,
-                    "tp_allreduce": 1, "tp_allgather": 1, "tp_signal_words": 0, "route_merge": 1, "embed_add": 1, "combine_partials": 1, "attention_status": 0, "plan_batch": 0, "decode_gemm": 1, "decode_qkv_rope": 1, "decode_gemm_max_tiles": 0, "set_attention_impl": 0, "attention_impl": 0,
-                    "dropout": 1, "dropout_add": 1, "decode_set_tma": 0, "decode_set_stages": 0, "decode_gemm_configure": 0, "route_topk_exchange": 1, "set_bounds_check": 0, "bounds_check_enabled": 0, "bounds_status": 0, "bounds_reset": 0}  # stack_*: counted per layer by their callers
+                    "tp_allreduce": 1, "tp_allgather": 1, "tp_signal_words": 0, "route_merge": 1, "embed_add": 1, "combine_partials": 1, "attention_status": 0, "plan_batch": 0, "decode_gemm": 1, "decode_qkv_rope": 1, "decode_gemm_max_tiles": 0, "decode_gemm_flag_slots": 0, "set_attention_impl": 0, "attention_impl": 0,
+                    "dropout": 1, "dropout_add": 1, "decode_set_tma": 0, "set_pdl": 0, "pdl_enabled": 0, "gelu_probe": 1, "decode_set_stages": 0, "decode_gemm_configure": 0, "route_topk_exchange": 1, "set_bounds_check": 0, "bounds_check_enabled": 0, "bounds_status": 0, "bounds_reset": 0}  # stack_*: counted per layer by their callers
 
 
 class LaunchCounter:
@@ -57,7 +57,10 @@ class LaunchCounter:
 
         def counted(*args, **kwargs):
             if self.enabled:
-                self.launches += KERNELS_PER_CALL.get(name, 1)
+                n = KERNELS_PER_CALL.get(name, 1)
+                if name == "decode_attention" and kwargs.get("phase", 0) != 0:
+                    n = 1  # one phase of a split launch: the attention splits or the merge
+                self.launches += n
                 self.calls[name] = self.calls.get(name, 0) + 1
             return fn(*args, **kwargs)
 
@@ -155,6 +158,8 @@ def require():
         module.set_bounds_check(True)
     if os.environ.get("PRA_DECODE_TMA", "1") == "0":  # the cp.async decode attention kernel
         module.decode_set_tma(False)
+    if os.environ.get("PRA_PDL", "1") == "0":  # decode chain without programmatic dependent launch
+        module.set_pdl(False)
     if os.environ.get("PRA_DG_CTAS") or os.environ.get("PRA_DG_MIN_KB"):  # decode GEMM launch shape
         module.decode_gemm_configure(int(os.environ.get("PRA_DG_CTAS", 2)), int(os.environ.get("PRA_DG_MIN_KB", 8)))
     if os.environ.get("PRA_DECODE_STAGES"):  # pipeline depth of the TMA-fed decode kernel

@@ -34,7 +34,7 @@ class TensorParallel:
         ext = _ext.require()
         self.group = group or dist.group.WORLD
         self.world = dist.get_world_size(self.group)
-        tiles = int(ext.decode_gemm_max_tiles())
+        slots = int(ext.decode_gemm_flag_slots())  # (tile, row slice) pairs of the fused decode GEMM
         self.rank = dist.get_rank(self.group)
         self.device = torch.device("cuda", torch.cuda.current_device())
         words = int(ext.tp_signal_words(self.world))
@@ -46,7 +46,7 @@ class TensorParallel:
             "small": (self.SMALL_ELEMS, torch.float32),
             "dg_recv0": (self.world * decode_rows * decode_width, torch.bfloat16),
             "dg_recv1": (self.world * decode_rows * decode_width, torch.bfloat16),
-            "dg_flag0": (tiles * self.world, torch.int32), "dg_flag1": (tiles * self.world, torch.int32),
+            "dg_flag0": (slots * self.world, torch.int32), "dg_flag1": (slots * self.world, torch.int32),
             "route_recv": (2 * decode_rows * self.world * 2 * self.ROUTE_K_MAX, torch.float32),
             "route_flag": (decode_rows * self.world, torch.int32),
             "sig_ar": (words, torch.int32), "sig_ag": (words, torch.int32), "sig_small": (words, torch.int32)},
@@ -64,7 +64,7 @@ class TensorParallel:
         self.decode_rows, self.decode_width = decode_rows, decode_width
         self.dg_recv = [self.buffers.addresses("dg_recv0"), self.buffers.addresses("dg_recv1")]
         self.dg_flags = [self.buffers.addresses("dg_flag0"), self.buffers.addresses("dg_flag1")]
-        self.dg_epochs = torch.zeros(tiles, dtype=torch.int32, device=self.device)
+        self.dg_epochs = torch.zeros(slots, dtype=torch.int32, device=self.device)
         self.epoch_dg = 0
         # fused routing exchange (local top-k pushed to every rank, merged where it lands)
         self.route_recv = self.buffers.addresses("route_recv")

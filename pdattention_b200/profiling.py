@@ -348,7 +348,114 @@ def decode_gemm_sweep(iters: int = 30) -> None:
     ext.decode_gemm_configure(2, 8)
 
 
-CASES = {"attention-fwd": attention_fwd, "sweep-table": sweep_table, "train-small": train_small, "decode-small": decode_small, "train-table": train_table,
+def decode_gemm_one(iters: int = 4) -> None:
+    """A few launches of one decode GEMM (64 token rows x the Llama-3-8B QKV weight with the
+    routing-query rows, 7,168 x 4,096 bf16 = 58.7 MB, above nothing but the L2 of a previous
+    launch's other copy): the small case for a full profiler capture of ``decode_gemm_kernel``."""
+    from .ops import _ext
+
+    ext = _ext.require()
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    n, k = 7168, 4096
+    ws = [(torch.randn(n, k, device=dev, generator=gen) * 0.02).bfloat16() for _ in range(3)]  # 176 MB > L2
+    x = torch.randn(64, k, device=dev, generator=gen).bfloat16()
+    out = torch.empty(64, n, device=dev, dtype=torch.bfloat16)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record()
+    for i in range(iters):
+        ext.decode_gemm(x, ws[i % 3], None, None, out, None, 0, 0, [], [], 0, None, 0, None)
+    e.record()
+    torch.cuda.synchronize()
+    ref = x.float() @ ws[(iters - 1) % 3].float().t()
+    err = (out.float() - ref).abs().max().item()
+    print(f"decode_gemm 64x{n}x{k}: {1000 * s.elapsed_time(e) / iters:.1f} us per launch (incl. first), max err {err:.3g}")
+
+
+def gemm_train_shapes(iters: int = 20) -> None:
+    """Device time of this library's training GEMMs (CUTLASS sm100 tcgen05 kernels behind
+    ``ext.gemm``) against cuBLAS through torch on the TinyGPT-PRA-163M shapes: prompt rows
+    8,192, cache-encode rows 16,384, d_model 768, MLP 3,072, vocabulary 50,304."""
+    from .ops import _ext
+
+    ext = _ext.require()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def rnd(*shape):
+        return (torch.randn(*shape, device=dev, generator=g) * 0.05).bfloat16()
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        return 1000 * s.elapsed_time(e) / iters
+
+    print(f"{'shape':44s} {'ours us':>8s} {'cuBLAS us':>9s} {'ours TF/s':>9s} {'ratio':>6s}")
+    for m in (8192, 16384):
+        for name, n, k in (("qkv", 2304, 768), ("o", 768, 768), ("fc1", 3072, 768), ("fc2", 768, 3072)):
+            a, w, bias = rnd(m, k), rnd(n, k), rnd(n)
+            d = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+            ours = timed(lambda: ext.gemm("tn", a, w, None, d, bias, None, 1.0, 0.0, None))
+            ref = timed(lambda: torch.nn.functional.linear(a, w, bias))
+            fl = 2 * m * n * k
+            print(f"{'fwd ' + name + f' {m}x{n}x{k}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
+            if name == "fc1":  # + GELU epilogue storing the pre-activation too, against linear + gelu
+                z = torch.empty_like(d)
+                ours = timed(lambda: ext.gemm("tn_gelu", a, w, None, d, bias, z, 1.0, 0.0, None))
+                ref = timed(lambda: torch.nn.functional.gelu(torch.nn.functional.linear(a, w, bias)))
+                print(f"{'fwd fc1+gelu' + f' {m}x{n}x{k}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} "
+                      f"{ref / ours:6.2f}")
+            if name == "fc2" and m == 8192:  # dgrad through fc2 with the GELU derivative of fc1's output
+                dy2, z1 = rnd(m, n), rnd(m, k)
+                dz = torch.empty(m, k, device=dev, dtype=torch.bfloat16)
+                ours = timed(lambda: ext.gemm("nn_dgelu", dy2, w, None, dz, None, z1, 1.0, 0.0, None))
+                ref = timed(lambda: dy2 @ w)
+                print(f"{'dgrad fc2+dgelu' + f' {m}x{k}x{n}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} "
+                      f"{ref / ours:6.2f}")
+            if m == 8192:
+                dy = rnd(m, n)
+                dx = torch.empty(m, k, device=dev, dtype=torch.bfloat16)
+                ours = timed(lambda: ext.gemm("nn", dy, w, None, dx, None, None, 1.0, 0.0, None))
+                ref = timed(lambda: dy @ w)
+                print(f"{'dgrad ' + name + f' {m}x{k}x{n}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
+                ours = timed(lambda: ext.gemm("nn_sk", dy, w, None, dx, None, None, 1.0, 0.0, None))
+                print(f"{'dgrad(sk) ' + name + f' {m}x{k}x{n}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
+                dw = torch.empty(n, k, device=dev, dtype=torch.bfloat16)
+                ours = timed(lambda: ext.gemm("wgrad", dy, a, None, dw, None, None, 1.0, 0.0, None))
+                ref = timed(lambda: dy.t() @ a)
+                print(f"{'wgrad ' + name + f' {n}x{k}x{m}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
+                ours = timed(lambda: ext.gemm("wgrad_sk", dy, a, None, dw, None, None, 1.0, 0.0, None))
+                print(f"{'wgrad(sk) ' + name + f' {n}x{k}x{m}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
+    m, v, k = 8192, 50304, 768
+    a, w = rnd(m, k), rnd(v, k)
+    d = torch.empty(m, v, device=dev, dtype=torch.bfloat16)
+    fl = 2 * m * v * k
+    ours = timed(lambda: ext.gemm("tn", a, w, None, d, None, None, 1.0, 0.0, None))
+    ref = timed(lambda: a @ w.t())
+    print(f"{'fwd lm_head ' + f'{m}x{v}x{k}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
+    dx = torch.empty(m, k, device=dev, dtype=torch.bfloat16)
+    ours = timed(lambda: ext.gemm("nn", d, w, None, dx, None, None, 1.0, 0.0, None))
+    ref = timed(lambda: d @ w)
+    print(f"{'dgrad lm_head ' + f'{m}x{k}x{v}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
+    ours = timed(lambda: ext.gemm("nn_sk", d, w, None, dx, None, None, 1.0, 0.0, None))
+    print(f"{'dgrad(sk) lm_head ' + f'{m}x{k}x{v}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
+    dw = torch.empty(v, k, device=dev, dtype=torch.bfloat16)
+    ours = timed(lambda: ext.gemm("wgrad", d, a, None, dw, None, None, 1.0, 0.0, None))
+    ref = timed(lambda: d.t() @ a)
+    print(f"{'wgrad lm_head ' + f'{v}x{k}x{m}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
+    ours = timed(lambda: ext.gemm("wgrad_sk", d, a, None, dw, None, None, 1.0, 0.0, None))
+    print(f"{'wgrad(sk) lm_head ' + f'{v}x{k}x{m}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
+
+
+CASES = {"attention-fwd": attention_fwd, "decode-gemm-one": decode_gemm_one, "gemm-train-shapes": gemm_train_shapes, "sweep-table": sweep_table, "train-small": train_small, "decode-small": decode_small, "train-table": train_table,
          "decode-table": decode_table, "decode-table-tp": decode_table_tp,
          "decode-attention-sweep": decode_attention_sweep, "route-topk-bench": route_topk_bench,
          "decode-gemm-sweep": decode_gemm_sweep}

@@ -1,4 +1,5 @@
-"""The decode GEMM (tcgen05, swapped operands, split-K with an on-GPU reduction) against fp32."""
+"""The decode GEMM (tcgen05, swapped operands, split-K reduced across a thread-block cluster in
+distributed shared memory) against fp32."""
 
 import pytest
 import torch
@@ -24,7 +25,7 @@ def test_matches_fp32(ext, m, n, k, splits):
     bias = torch.randn(n, device="cuda", generator=gen).bfloat16()
     res = torch.randn(m, n, device="cuda", generator=gen).bfloat16()
     out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
-    for _ in range(2):  # the split-K workspace and counters are reused: a second call must agree
+    for _ in range(2):  # a second call (same tensor maps, same launch) must agree
         ext.decode_gemm(x, w, bias, res, out, None, 0, splits, [], [], 0, None, 0, None)
         want = x.float() @ w.float().t() + bias.float() + res.float()
         torch.cuda.synchronize()
@@ -85,3 +86,15 @@ def test_rotary_qkv_epilogue_matches_gemm_then_rope(ext, head_dim, heads, kv_hea
     assert close(q_fused, q_ref)
     assert close(caches[0], caches[2]) and close(caches[1], caches[3])
     assert close(r_fused, full[:, qd + 2 * kd:])
+
+
+@pytest.mark.parametrize("m,n,k", [(64, 4096, 1024), (3, 512, 1024), (64, 2048, 128)])
+def test_fp32_scores_output(ext, m, n, k):
+    """fp32 output (the routing scores; 2-stage ring) against the fp32 product."""
+    gen = torch.Generator(device="cuda").manual_seed(n + k)
+    x = torch.randn(m, k, device="cuda", generator=gen).bfloat16()
+    w = torch.nn.functional.normalize(torch.randn(n, k, device="cuda", generator=gen), dim=-1).bfloat16()
+    out = torch.full((m, n), float("nan"), device="cuda")
+    ext.decode_gemm(x, w, None, None, out, None, 0, 0, [], [], 0, None, 0, None)
+    want = x.float() @ w.float().t()
+    assert torch.allclose(out, want, atol=1e-3, rtol=1e-3), (out - want).abs().max()

@@ -60,6 +60,20 @@ def test_gemm_variants(ext, m, n, k):
     _close(gw, 1.5 * (dy.float().T @ a.float()), 2e-2)
 
 
+def test_epilogue_gelu_matches_erf_gelu(ext):
+    """The GEMM epilogues' GELU (Abramowitz & Stegun 7.1.26 erf) and its derivative against
+    fp32 PyTorch erf GELU over [-12, 12]: the formula's 1.5e-7 bound plus fp32 rounding."""
+    z = torch.cat([torch.linspace(-12, 12, 200001, device="cuda"), torch.randn(100000, device="cuda") * 3])
+    y, dy = ext.gelu_probe(z.contiguous())
+    zd = z.double().requires_grad_(True)
+    ref = torch.nn.functional.gelu(zd)
+    ref.backward(torch.ones_like(zd))
+    err = (y.double() - ref.detach()).abs() / (1 + zd.detach().abs())
+    derr = (dy.double() - zd.grad).abs()
+    assert err.max() < 2e-6, float(err.max())
+    assert derr.max() < 2e-6, float(derr.max())
+
+
 @pytest.mark.parametrize("rms", [False, True])
 def test_norm(ext, rms):
     x, w, b = _bf(513, 768, seed=1), _bf(768, seed=2), _bf(768, seed=3)

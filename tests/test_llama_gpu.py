@@ -342,3 +342,73 @@ def test_tma_decode_attention_matches_cp_async_kernel(ext, head_dim, run, mem_le
         s = torch.einsum("hd,khd->hk", q[b].float().view(H, head_dim), keys.repeat_interleave(g, 1)) / math.sqrt(head_dim)
         ref = torch.einsum("hk,khd->hd", torch.softmax(s, -1), vals.repeat_interleave(g, 1)).reshape(-1)
         assert torch.allclose(out_t[b].float(), ref, atol=2e-2, rtol=2e-2), (b, (out_t[b].float() - ref).abs().max())
+
+
+@pytest.mark.parametrize("tma", [True, False])
+def test_phase_split_decode_attention_equals_single_launch(ext, tma):
+    """Memory splits, local splits (launched first, on another stream, before the memory row
+    lists exist) and a separate merge give the single launch's output."""
+    torch.manual_seed(11)
+    B, H, Hkv, D, max_len, tc, chunks, sk = 4, 16, 4, 128, 600, 64, 30, 256
+    q = torch.randn(B, H * D, device="cuda").bfloat16()
+    pool = torch.randn(chunks * tc, 2 * Hkv * D, device="cuda").bfloat16()
+    mk, mv = pool[:, : Hkv * D], pool[:, Hkv * D:]
+    mem_max = 8 * tc
+    mem_idx = torch.zeros(B, mem_max, device="cuda", dtype=torch.int32)
+    for b in range(B):
+        picks = torch.randperm(chunks)[:8]
+        mem_idx[b] = torch.cat([c * tc + torch.arange(tc) for c in picks.tolist()]).to(torch.int32).cuda()
+    mem_len = torch.tensor([mem_max, 100, 0, 448], device="cuda", dtype=torch.int32)
+    cache = torch.randn(2, B, max_len, Hkv * D, device="cuda").bfloat16()
+    loc_len = torch.tensor([600, 1, 257, 64], device="cuda", dtype=torch.int32)
+    try:
+        ext.decode_set_tma(tma)
+        ref = ext.decode_attention(q, H, Hkv, D, mk, mv, mem_idx, mem_len, cache[0], cache[1], loc_len,
+                                   mem_max + max_len, sk, False)[0]
+        msk = 128  # finer memory splits than local ones
+        n_mem, n_loc = mem_max // msk, -(-max_len // sk)
+        part_o = torch.full((B, H, n_mem + n_loc, D), float("nan"), device="cuda")
+        part_ml = torch.full((B, H, n_mem + n_loc, 2), float("nan"), device="cuda")
+        common = dict(mem_splits=n_mem, mem_split_keys=msk, part_o=part_o, part_ml=part_ml)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            ext.decode_attention(q, H, Hkv, D, None, None, None, None, cache[0], cache[1], loc_len, 0, sk, False,
+                                 split_lo=n_mem, split_count=n_loc, phase=1, **common)
+        ext.decode_attention(q, H, Hkv, D, mk, mv, mem_idx, mem_len, cache[0], cache[1], loc_len, 0, sk, False,
+                             split_lo=0, split_count=n_mem, phase=1, **common)
+        torch.cuda.current_stream().wait_stream(side)
+        out = ext.decode_attention(q, H, Hkv, D, None, None, None, None, cache[0], cache[1], loc_len, 0, sk, False,
+                                   phase=2, **common)[0]
+    finally:
+        ext.decode_set_tma(True)
+    assert not torch.isnan(part_ml).any()
+    assert torch.allclose(out.float(), ref.float(), atol=1e-2, rtol=1e-2), (out.float() - ref.float()).abs().max()
+
+
+@pytest.mark.parametrize("graphed", [False, True])
+def test_overlapped_routing_decode_equals_serial(ext, graphed):
+    """Decode with routing on the side stream (local splits concurrent) matches the serial step
+    up to the summation order of the split layout, and repeats bit for bit (no race between the
+    streams)."""
+    from pdattention_b200.inference.llama_engine import LlamaWeights, PRALlamaEngine
+
+    cfg, model, chunks, lengths = _tiny_setup(5)
+    weights = LlamaWeights.from_reference(model, "cuda")
+    feed = torch.randint(0, cfg.vocab_size, (4, 2), generator=torch.Generator().manual_seed(9)).cuda()
+    outs = []
+    for overlap in (False, True, True):
+        engine = PRALlamaEngine(weights, "cuda", decode_split_keys=64, overlap_routing=overlap)
+        engine.build_memory(chunks, lengths)
+        engine.set_namespace(torch.tensor([0, 3], dtype=torch.int32), torch.tensor([12, 9], dtype=torch.int32))
+        engine.prefill(torch.arange(24).view(2, 12) % cfg.vocab_size, torch.tensor([12, 9]), 6)
+        engine.decode_step(feed[0])
+        step = engine.decode_step
+        if graphed:
+            engine.capture_decode()
+            step = engine.decode_step_graphed
+        outs.append(torch.stack([step(feed[i]).float().clone() for i in range(1, 4)]))
+    assert torch.equal(outs[1], outs[2])
+    cos = F.cosine_similarity(outs[0].flatten(0, 1), outs[1].flatten(0, 1), dim=-1)
+    assert cos.min() > 0.9999, cos
+    assert (outs[0] - outs[1]).abs().max() < 0.1
