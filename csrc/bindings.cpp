@@ -844,7 +844,7 @@ std::vector<torch::Tensor> decode_attention(torch::Tensor q, int64_t heads, int6
                                             int64_t mem_split_keys,
                                             int64_t split_lo, int64_t split_count, int64_t phase,
                                             c10::optional<torch::Tensor> part_o_in,
-                                            c10::optional<torch::Tensor> part_ml_in) {
+                                            c10::optional<torch::Tensor> part_ml_in, int64_t max_ctas) {
   c10::cuda::CUDAGuard guard(q.device());
   expect(q, at::kBFloat16, "q");
   TORCH_CHECK(q.dim() == 2 && q.stride(1) == 1 && q.size(1) == heads * head_dim, "q must be [B, H*Dh]");
@@ -892,6 +892,7 @@ std::vector<torch::Tensor> decode_attention(torch::Tensor q, int64_t heads, int6
   p.split_lo = split_lo;
   p.split_count = split_count;
   p.phase = phase;
+  p.max_ctas = (int)max_ctas;
   auto fo = q.options().dtype(at::kFloat);
   torch::Tensor part_o, part_ml;
   if (part_o_in.has_value()) {  // caller-owned partials (a launch split across streams shares them)
@@ -1557,7 +1558,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("head_dim"), py::arg("mem_k"), py::arg("mem_v"), py::arg("mem_idx"), py::arg("mem_len"),
         py::arg("loc_k"), py::arg("loc_v"), py::arg("loc_len"), py::arg("max_keys"), py::arg("split_keys"),
         py::arg("export_partials"), py::arg("mem_splits") = 0, py::arg("mem_split_keys") = 0, py::arg("split_lo") = 0, py::arg("split_count") = 0,
-        py::arg("phase") = 0, py::arg("part_o") = py::none(), py::arg("part_ml") = py::none());
+        py::arg("phase") = 0, py::arg("part_o") = py::none(), py::arg("part_ml") = py::none(),
+        py::arg("max_ctas") = 0);
   m.def("route_topk", &route_topk, py::arg("scores"), py::arg("query"), py::arg("gists"), py::arg("ns_start"),
         py::arg("ns_end"), py::arg("chunk_len"), py::arg("chunk_row0"), py::arg("k"), py::arg("k_cand"),
         py::arg("budget"), py::arg("mem_max"), py::arg("local"), py::arg("id_offset"), py::arg("gists_per_chunk"),
@@ -1571,8 +1573,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_set_tma", [](bool on) { pra_decode_set_tma(on ? 1 : 0); });
   m.def("set_pdl", [](bool on) { pra_set_pdl(on ? 1 : 0); });
   m.def("gelu_probe", &gelu_probe);
+  m.def("set_launch_priority", [](bool high) { pra_set_launch_priority(high ? 1 : 0); });
   m.def("pdl_enabled", []() { return pra_pdl_enabled() != 0; });
-  m.def("decode_gemm_configure", [](int64_t ctas, int64_t min_kb) { pra_decode_gemm_configure((int)ctas, (int)min_kb); });
+  m.def("decode_gemm_configure", [](int64_t ctas, int64_t min_kb, int64_t max_splits) {
+    pra_decode_gemm_configure((int)ctas, (int)min_kb, (int)max_splits);
+  }, py::arg("ctas"), py::arg("min_kb"), py::arg("max_splits") = 0);
   m.def("decode_set_stages", [](int64_t stages) { pra_decode_set_stages((int)stages); });
   m.def("bounds_check_enabled", &bounds_check_enabled);
   m.def("bounds_status", &bounds_status);
@@ -1583,6 +1588,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_qkv_rope", &decode_qkv_rope);
   m.def("decode_gemm_max_tiles", []() { return (int64_t)DG_MAX_TILES; });
   m.def("decode_gemm_flag_slots", []() { return (int64_t)DG_MAX_TILES * DG_MAX_SPLITS; });
+  m.def("decode_gemm_resident_clusters", [](int64_t splits) { return (int64_t)pra_decode_gemm_resident_clusters((int)splits); });
   m.def("plan_batch", &pra_plan_batch, "native cache-build planner (returns None when a batch needs the Python planner)");
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_open", &ipc_open);

@@ -259,6 +259,25 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 
 }  // namespace pra
 
+// The launch attributes every instrumented decode kernel gets: programmatic stream
+// serialization (when enabled) and the current launch priority (when set); returns how many
+// of `attr[0..1]` it filled.
+inline int pra_launch_attrs(cudaLaunchAttribute* attr) {
+  int n = 0;
+  if (pra_pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  const int prio = pra_launch_priority();
+  if (prio != 0) {
+    attr[n].id = cudaLaunchAttributePriority;
+    attr[n].val.priority = prio;
+    ++n;
+  }
+  return n;
+}
+
 // Launch `kernel` on `st`, with programmatic stream serialization when PDL is enabled.  Only
 // for kernels that follow the `pdl_wait` rules above.
 template <typename... Params, typename... Args>
@@ -269,10 +288,8 @@ inline cudaError_t pra_launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 blo
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
   cfg.attrs = attr;
-  cfg.numAttrs = pra_pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = pra_launch_attrs(attr);
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }

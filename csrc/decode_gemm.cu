@@ -30,6 +30,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <map>
 #include <mutex>
 #include <unordered_map>
 
@@ -431,15 +432,62 @@ const CUtensorMap* pra_tile_map_bf16(const void* ptr, int64_t cols, int64_t rows
 
 static int g_dg_ctas_per_sm = 2;
 static int g_dg_min_kb = 8;
-void pra_decode_gemm_configure(int ctas_per_sm, int min_blocks_per_split) {
+static int g_dg_max_splits = DG_MAX_SPLITS;
+void pra_decode_gemm_configure(int ctas_per_sm, int min_blocks_per_split, int max_splits) {
   if (ctas_per_sm == 1 || ctas_per_sm == 2) g_dg_ctas_per_sm = ctas_per_sm;
   if (min_blocks_per_split >= 1) g_dg_min_kb = min_blocks_per_split;
+  if (max_splits >= 1 && max_splits <= DG_MAX_SPLITS) g_dg_max_splits = max_splits;
 }
 int pra_decode_gemm_ctas_per_sm() { return g_dg_ctas_per_sm; }
 
 int pra_decode_gemm_splits(int tiles, int nkb, int sms) {
   const int slots = sms * g_dg_ctas_per_sm;
-  return std::max(1, std::min(std::min(nkb / g_dg_min_kb, slots / std::max(tiles, 1)), DG_MAX_SPLITS));
+  return std::max(1, std::min(std::min(nkb / g_dg_min_kb, slots / std::max(tiles, 1)), g_dg_max_splits));
+}
+
+// Whether `tiles` clusters of `splits` CTAs can all be resident at once (the fused all-reduce
+// waits for its peers inside the kernel, so its whole grid must run concurrently).  Queried with
+// the cluster shape alone; cached per (device, shape).
+template <int STAGES>
+static bool grid_fits(int tiles, int splits) {
+  using namespace pra::dg;
+  static std::mutex mu;
+  static std::map<std::pair<int, int>, int> cache;  // (device, splits) -> resident clusters
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find({dev, splits});
+  if (it == cache.end()) {
+    cudaLaunchConfig_t q = {};
+    q.gridDim = dim3(tiles, splits);
+    q.blockDim = dim3(NT);
+    q.dynamicSmemBytes = Ring<STAGES>::SMEM_BYTES;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = splits;
+    attr[0].val.clusterDim.z = 1;
+    q.attrs = attr;
+    q.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, decode_gemm_kernel<STAGES>, &q) != cudaSuccess) {
+      cudaGetLastError();  // clear; fall back to per-SM residency
+      int per_sm = 0, sms = 0;
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_gemm_kernel<STAGES>, NT, Ring<STAGES>::SMEM_BYTES);
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      clusters = per_sm * sms / splits;
+    }
+    it = cache.emplace(std::make_pair(dev, splits), clusters).first;
+  }
+  return it->second >= tiles;
+}
+
+int pra_decode_gemm_resident_clusters(int splits) {
+  const bool two = pra_decode_gemm_ctas_per_sm() == 2;
+  for (int t = 1;; t *= 2) {  // the largest power-of-two tile count that fits (cached per shape)
+    if (!(two ? grid_fits<4>(t, splits) : grid_fits<6>(t, splits))) return t / 2;
+    if (t > 4096) return t;
+  }
 }
 
 // Launch with the split-K cluster (1 x splits CTAs) and programmatic dependent launch.
@@ -452,7 +500,7 @@ static cudaError_t launch_dg(const CUtensorMap& map_w, const CUtensorMap& map_x,
   cfg.blockDim = dim3(NT);
   cfg.dynamicSmemBytes = Ring<STAGES>::SMEM_BYTES;
   cfg.stream = st;
-  cudaLaunchAttribute attr[2];
+  cudaLaunchAttribute attr[3];
   int n = 0;
   if (b.splits > 1) {
     attr[n].id = cudaLaunchAttributeClusterDimension;
@@ -461,18 +509,10 @@ static cudaError_t launch_dg(const CUtensorMap& map_w, const CUtensorMap& map_x,
     attr[n].val.clusterDim.z = 1;
     ++n;
   }
-  if (pra_pdl_enabled()) {
-    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[n].val.programmaticStreamSerializationAllowed = 1;
-    ++n;
-  }
+  n += pra_launch_attrs(attr + n);
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  if (b.world > 1) {  // every slice waits for its peers: the whole grid must be resident at once
-    int clusters = 0;
-    PRA_RETURN_IF_ERROR(cudaOccupancyMaxActiveClusters(&clusters, decode_gemm_kernel<STAGES>, &cfg));
-    if (b.splits > 1 ? clusters < tiles : clusters < tiles * b.splits) return cudaErrorInvalidConfiguration;
-  }
+  if (b.world > 1 && !grid_fits<STAGES>(tiles, b.splits)) return cudaErrorInvalidConfiguration;
   return cudaLaunchKernelEx(&cfg, decode_gemm_kernel<STAGES>, map_w, map_x, b);
 }
 
@@ -511,6 +551,14 @@ cudaError_t pra_decode_gemm(const DecodeGemmArgs& a, cudaStream_t st) {
   if (map_w == nullptr || map_x == nullptr) return cudaErrorInvalidValue;
   DecodeGemmArgs b = a;
   b.splits = splits;
+  if (a.world > 1) {  // the fused all-reduce's grid must be resident at once: fewer splits until it is
+    const bool two = pra_decode_gemm_ctas_per_sm() == 2;
+    while (b.splits > 1 && !(two ? grid_fits<4>(tiles, b.splits) : grid_fits<6>(tiles, b.splits))) {
+      const int per2 = (nkb + b.splits - 2) / (b.splits - 1);
+      b.splits = (nkb + per2 - 1) / per2;
+    }
+    if (!(two ? grid_fits<4>(tiles, b.splits) : grid_fits<6>(tiles, b.splits))) return cudaErrorInvalidConfiguration;
+  }
   if (a.out_f32 != nullptr) return launch_dg<2>(*map_w, *map_x, b, tiles, st);
   if (pra_decode_gemm_ctas_per_sm() == 2) return launch_dg<4>(*map_w, *map_x, b, tiles, st);
   return launch_dg<6>(*map_w, *map_x, b, tiles, st);

@@ -293,6 +293,7 @@ struct DecodeAttnParams {
   int mem_split_keys;          // keys per memory split when mem_splits > 0 (0: split_keys; <= split_keys)
   int split_lo, split_count;   // the splits this launch runs (split_count 0: all n_split)
   int phase;                   // 0: attention then merge; 1: attention only; 2: merge only
+  int max_ctas;                // > 0: a persistent grid of at most this many CTAs walks the work items
 };
 cudaError_t pra_decode_attention(const DecodeAttnParams& p, int head_dim, cudaStream_t stream);
 // 1 (default): eligible decode attention calls run the TMA-fed kernel; 0: the cp.async kernel.
@@ -301,6 +302,12 @@ void pra_decode_set_tma(int on);
 // attention and its merge) are launched with programmatic stream serialization (default on).
 void pra_set_pdl(int on);
 int pra_pdl_enabled();
+// Scheduling priority given to the instrumented decode kernels launched from now on (0: none,
+// else the device's highest stream priority): the routing chain that overlaps the decode
+// attention sets it so its CTAs are dispatched ahead of the attention's pending CTAs, also
+// inside a captured graph (the attribute is kept per kernel node).
+void pra_set_launch_priority(int high);
+int pra_launch_priority();
 // Pipeline stages of the TMA-fed decode kernel (2, 3 or 4; 2 by default).
 void pra_decode_set_stages(int stages);
 
@@ -455,7 +462,10 @@ struct DecodeGemmArgs {
 // decode-attention CTAs it runs concurrently with), and the
 // fewest 64-deep K blocks a split keeps; defaults 2 and 8.  pra_decode_gemm_splits picks the
 // K split of a launch from them (the grid fills the CTA slots once).
-void pra_decode_gemm_configure(int ctas_per_sm, int min_blocks_per_split);
+void pra_decode_gemm_configure(int ctas_per_sm, int min_blocks_per_split, int max_splits);
 int pra_decode_gemm_ctas_per_sm();
 int pra_decode_gemm_splits(int tiles, int nkb, int sms);
 cudaError_t pra_decode_gemm(const DecodeGemmArgs& a, cudaStream_t stream);
+// Clusters of `splits` decode-GEMM CTAs that can be resident at once (rounded down to a power of
+// two): the fused all-reduce needs tiles <= this.
+int pra_decode_gemm_resident_clusters(int splits);

@@ -15,6 +15,7 @@
 //  * route_topk     exact top-k routing per row: radix-select of the candidates from
 //                   tensor-core scores, fp32 cosine rescoring of the candidates, ties by
 //                   chunk id, greedy token budget, and the memory row list in chunk order.
+#include <algorithm>
 #include <climits>
 
 #include "common.cuh"
@@ -316,10 +317,6 @@ __global__ void __launch_bounds__(DT) decode_tma_kernel(const __grid_constant__ 
   float* red = reinterpret_cast<float*>(stages);  // [4][16][D + 2], after the key loop
 
   const int G = p.H / p.Hkv;
-  const int b = blockIdx.x / p.Hkv, kvh = blockIdx.x % p.Hkv;
-  const int split = p.split_lo + blockIdx.y;
-  const bool local_only = p.mem_splits > 0 && split >= p.mem_splits;
-  const bool mem_only = p.mem_splits > 0 && split < p.mem_splits;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < TST; ++s) mbar_init(full + s, 1);
@@ -330,6 +327,16 @@ __global__ void __launch_bounds__(DT) decode_tma_kernel(const __grid_constant__ 
   }
   pdl_launch_dependents();
   pdl_wait();  // q, the new cache row and the routed row lists come from the kernels before
+  uint32_t phase = 0;  // bit s: parity the next TMA completion of stage s shows (kept across items)
+  // Work items are (row, KV head, split).  The ordinary grid runs one item per CTA; a persistent
+  // grid (p.max_ctas) walks items with a stride, leaving the rest of each SM to other kernels.
+  const int n_items = p.B * p.Hkv * (p.split_count > 0 ? p.split_count : p.n_split);
+  for (int item = blockIdx.y * gridDim.x + blockIdx.x; item < n_items; item += gridDim.x * gridDim.y) {
+  const int bh = item % (p.B * p.Hkv);
+  const int b = bh / p.Hkv, kvh = bh % p.Hkv;
+  const int split = p.split_lo + item / (p.B * p.Hkv);
+  const bool local_only = p.mem_splits > 0 && split >= p.mem_splits;
+  const bool mem_only = p.mem_splits > 0 && split < p.mem_splits;
   const int mem_len = (!local_only && p.mem_len) ? p.mem_len[b] : 0;
   const int total = mem_len + ((!mem_only && p.loc_len) ? p.loc_len[b] : 0);
   const int keys = mem_only && p.mem_split_keys > 0 ? p.mem_split_keys : p.split_keys;
@@ -407,7 +414,6 @@ __global__ void __launch_bounds__(DT) decode_tma_kernel(const __grid_constant__ 
   for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
   const float sl2 = p.scale * LOG2E;
-  uint32_t phase = 0;  // bit s: parity the next TMA completion of stage s shows
 #pragma unroll
   for (int st = 0; st < TST - 1; ++st) {
     if (st < n_blocks) issue(st, st);
@@ -540,6 +546,8 @@ __global__ void __launch_bounds__(DT) decode_tma_kernel(const __grid_constant__ 
       p.part_ml[at * 2 + 1] = L;
     }
   }
+  __syncthreads();  // the merge buffer (staging area), q and the row list are the next item's
+  }  // work items
 }
 
 // Merge the splits of each (row, head): out = sum_s o_s e^{m_s - M} / sum_s l_s e^{m_s - M}.
@@ -1064,6 +1072,13 @@ static int g_decode_tma = 1;
 static int g_pdl = 1;
 void pra_set_pdl(int on) { g_pdl = on ? 1 : 0; }
 int pra_pdl_enabled() { return g_pdl; }
+static thread_local int g_launch_priority = 0;
+void pra_set_launch_priority(int high) {
+  int least = 0, greatest = 0;
+  if (high && cudaDeviceGetStreamPriorityRange(&least, &greatest) == cudaSuccess) g_launch_priority = greatest;
+  else g_launch_priority = 0;
+}
+int pra_launch_priority() { return g_launch_priority; }
 static int g_decode_stages = pra::llama::TST_DEFAULT;
 void pra_decode_set_tma(int on) { g_decode_tma = on; }
 void pra_decode_set_stages(int stages) { g_decode_stages = stages; }
@@ -1076,9 +1091,10 @@ static cudaError_t launch_decode_tma_stages(const DecodeAttnParams& p, const CUt
   const size_t smem = 1024 + (size_t)TST * Lay::STAGE + 16 * Lay::QLD * 2 + (size_t)(p.split_keys + 2 * TMAX_BLOCKS) * 4 +
                       TST * 8;
   PRA_RETURN_IF_ERROR(pra::set_max_dynamic_smem(reinterpret_cast<const void*>(decode_tma_kernel<D, TST>), (int)smem));
-  PRA_RETURN_IF_ERROR(pra_launch_pdl(decode_tma_kernel<D, TST>,
-                                     dim3(p.B * p.Hkv, p.split_count > 0 ? p.split_count : p.n_split), dim3(DT), smem,
-                                     st, *mk, *mv, *lk, *lv, p));
+  const int count = p.split_count > 0 ? p.split_count : p.n_split;
+  const int items = p.B * p.Hkv * count;
+  const dim3 grid = p.max_ctas > 0 ? dim3(std::min(items, p.max_ctas)) : dim3(p.B * p.Hkv, count);
+  PRA_RETURN_IF_ERROR(pra_launch_pdl(decode_tma_kernel<D, TST>, grid, dim3(DT), smem, st, *mk, *mv, *lk, *lv, p));
   return cudaGetLastError();
 }
 

@@ -193,6 +193,9 @@ class PRALlamaEngine:
         self._route_stream: torch.cuda.Stream | None = None
         self._parts: tuple[tuple[int, int], torch.Tensor, torch.Tensor] | None = None
         self._bounds_cache: tuple | None = None
+        # overlapped decode: the local-window splits run as a persistent grid of this many CTAs
+        # (default two per SM) so every SM keeps a slot for the routing chain and memory splits
+        self._local_ctas = int(os.environ.get("PRA_LOCAL_CTAS", "-1"))
         self.ext = _ext.require()
         self._rope_cache: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
         self.memory: ChunkMemory | None = None
@@ -652,12 +655,18 @@ class PRALlamaEngine:
             self._route_stream = torch.cuda.Stream(self.device, priority=-1)
         side = self._route_stream
         side.wait_stream(main)  # fork before the local splits: routing must not wait for them
+        if self._local_ctas < 0:
+            self._local_ctas = 2 * torch.cuda.get_device_properties(self.device).multi_processor_count
         ext.decode_attention(q, H, Hkv, D, None, None, None, None, kc, vc, new_len, 0, sk, False,
-                             split_lo=n_mem, split_count=n_loc, phase=1, **common)
+                             split_lo=n_mem, split_count=n_loc, phase=1, max_ctas=self._local_ctas, **common)
         with torch.cuda.stream(side):
-            mem_idx, mem_len = self._route(li, q_rows, B, route_query=rq)
-            ext.decode_attention(q, H, Hkv, D, self.memory.k(li), self.memory.v(li), mem_idx, mem_len, kc, vc,
-                                 new_len, 0, sk, False, split_lo=0, split_count=n_mem, phase=1, **common)
+            ext.set_launch_priority(True)  # also per kernel node when the step is captured
+            try:
+                mem_idx, mem_len = self._route(li, q_rows, B, route_query=rq)
+                ext.decode_attention(q, H, Hkv, D, self.memory.k(li), self.memory.v(li), mem_idx, mem_len, kc, vc,
+                                     new_len, 0, sk, False, split_lo=0, split_count=n_mem, phase=1, **common)
+            finally:
+                ext.set_launch_priority(False)
         main.wait_stream(side)
         return ext.decode_attention(q, H, Hkv, D, None, None, None, None, kc, vc, new_len, 0, sk, False, phase=2,
                                     **common)[0]

@@ -17,6 +17,7 @@ launch end quickly.  Numbers printed under a profiler are not benchmark values.
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 import tempfile
 import time
@@ -267,9 +268,99 @@ def decode_attention_sweep(iters: int = 20) -> None:
         us = 1000 * s.elapsed_time(e) / iters
         rows.append((name, us, nbytes / us / 1e6))
     ext.decode_set_tma(True)
-    ext.decode_set_stages(3)
+    ext.decode_set_stages(2)
     for name, us, tbs in rows:
         print(f"{name:20s} {us:8.1f} us  {tbs:5.2f} TB/s (attention + split merge, {nbytes / 1e9:.2f} GB of K/V)")
+
+
+def decode_overlap_probe(iters: int = 20) -> None:
+    """One Llama-3-8B layer's routing + decode attention (64 rows, 4,096 chunks of 1,024-wide gists,
+    top-16, 4,100 local keys per row; K/V > the L2), serial (scores, top-k, one attention launch)
+    against overlapped (local splits on the current stream while a high-priority side stream
+    scores, selects and attends over the memory splits; then the merge), and the attention
+    phases alone."""
+    import torch.nn.functional as F
+
+    from .ops import _ext
+
+    ext = _ext.require()
+    dev = torch.device("cuda", 0)
+    B, H, Hkv, D, max_len, chunks, W = 64, 32, 8, 128, 4352, 4096, 1024
+    gen = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn(B, H * D, device=dev, generator=gen).bfloat16()
+    pool = torch.randn(chunks * 64, 2 * Hkv * D, device=dev, generator=gen).bfloat16()
+    mk, mv = pool[:, : Hkv * D], pool[:, Hkv * D:]
+    cache = torch.randn(2, B, max_len, Hkv * D, device=dev, generator=gen).bfloat16()
+    loc_len = torch.full((B,), 4100, device=dev, dtype=torch.int32)
+    gists = F.normalize(torch.randn(chunks, W, device=dev, generator=gen), dim=-1)
+    gists_bf = gists.bfloat16().contiguous()
+    rq = torch.randn(B, W, device=dev, generator=gen).bfloat16()
+    lo = torch.zeros(B, dtype=torch.int32, device=dev)
+    hi = torch.full((B,), chunks, dtype=torch.int32, device=dev)
+    clen = torch.full((chunks,), 64, dtype=torch.int32, device=dev)
+    row0 = torch.arange(chunks, dtype=torch.int32, device=dev) * 64
+    scores = torch.empty(B, chunks, device=dev)
+    sk, msk = 1024, int(os.environ.get("PRA_PROBE_MEM_SPLIT", "256"))
+    n_mem, n_loc = 1024 // msk, -(-max_len // sk)
+    part_o = torch.empty(B, H, n_mem + n_loc, D, device=dev)
+    part_ml = torch.empty(B, H, n_mem + n_loc, 2, device=dev)
+    side = torch.cuda.Stream(dev, priority=-1)
+    common = dict(mem_splits=n_mem, mem_split_keys=msk, part_o=part_o, part_ml=part_ml)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    local_ctas = int(os.environ.get("PRA_PROBE_LOCAL_CTAS", str(2 * sms)))  # persistent local grid
+
+    def route():
+        ext.decode_gemm(rq, gists_bf, None, None, scores, None, 0, 0, [], [], 0, None, 0, None)
+        return ext.route_topk(scores, rq, gists, lo, hi, clen, row0, 16, 64, -1, 1024, False, 0, 1, 1)
+
+    def serial():
+        mem_idx, mem_len, _ = route()
+        ext.decode_attention(q, H, Hkv, D, mk, mv, mem_idx, mem_len, cache[0], cache[1], loc_len, 1024 + max_len,
+                             sk, False)
+
+    def overlapped():
+        main = torch.cuda.current_stream()
+        side.wait_stream(main)
+        ext.decode_attention(q, H, Hkv, D, None, None, None, None, cache[0], cache[1], loc_len, 0, sk, False,
+                             split_lo=n_mem, split_count=n_loc, phase=1, max_ctas=local_ctas, **common)
+        with torch.cuda.stream(side):
+            ext.set_launch_priority(True)
+            mem_idx, mem_len, _ = route()
+            ext.decode_attention(q, H, Hkv, D, mk, mv, mem_idx, mem_len, cache[0], cache[1], loc_len, 0, sk, False,
+                                 split_lo=0, split_count=n_mem, phase=1, **common)
+            ext.set_launch_priority(False)
+        main.wait_stream(side)
+        ext.decode_attention(q, H, Hkv, D, None, None, None, None, cache[0], cache[1], loc_len, 0, sk, False,
+                             phase=2, **common)
+
+    mem_idx0, mem_len0, _ = route()
+
+    def local_only():
+        ext.decode_attention(q, H, Hkv, D, None, None, None, None, cache[0], cache[1], loc_len, 0, sk, False,
+                             split_lo=n_mem, split_count=n_loc, phase=1, max_ctas=local_ctas, **common)
+
+    def memory_only():
+        ext.decode_attention(q, H, Hkv, D, mk, mv, mem_idx0, mem_len0, cache[0], cache[1], loc_len, 0, sk, False,
+                             split_lo=0, split_count=n_mem, phase=1, **common)
+
+    def single():
+        ext.decode_attention(q, H, Hkv, D, mk, mv, mem_idx0, mem_len0, cache[0], cache[1], loc_len, 1024 + max_len,
+                             sk, False)
+
+    for name, fn in (("routing only", route), ("single attention launch", single), ("local splits", local_only),
+                     ("memory splits", memory_only), ("serial routing + attention", serial),
+                     ("overlapped routing + attention", overlapped)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        print(f"{name:32s} {1000 * s.elapsed_time(e) / iters:8.1f} us (memory split {msk} keys, local grid "
+              f"{local_ctas or 'full'})")
 
 
 def route_topk_bench(iters: int = 50) -> None:
@@ -323,16 +414,16 @@ def decode_gemm_sweep(iters: int = 30) -> None:
     gen = torch.Generator(device=dev).manual_seed(0)
     shapes = {"qkv tp1": (7168, 4096), "o tp1": (4096, 4096), "gate_up tp1": (28672, 4096), "down tp1": (4096, 14336),
               "qkv tp8": (1792, 4096), "o tp8": (4096, 512), "gate_up tp8": (3584, 4096), "down tp8": (4096, 1792)}
-    configs = [(1, 8), (2, 8), (2, 4), (2, 2)]
-    print("shape            " + "  ".join(f"ctas{c}/minkb{k}" for c, k in configs))
+    configs = [(1, 8, 8), (2, 8, 8), (2, 8, 4), (2, 8, 2), (2, 4, 4)]
+    print("shape            " + "  ".join(f"ctas{c}/minkb{k}/max{m}" for c, k, m in configs))
     for name, (n, k) in shapes.items():
         copies = max(2, int(2 * 128e6 // (n * k * 2)) + 1)  # > L2 in total
         ws = [(torch.randn(n, k, device=dev, generator=gen) * 0.02).bfloat16() for _ in range(copies)]
         x = torch.randn(64, k, device=dev, generator=gen).bfloat16()
         out = torch.empty(64, n, device=dev, dtype=torch.bfloat16)
         cells = []
-        for ctas, min_kb in configs:
-            ext.decode_gemm_configure(ctas, min_kb)
+        for ctas, min_kb, max_splits in configs:
+            ext.decode_gemm_configure(ctas, min_kb, max_splits)
             for w in ws:
                 ext.decode_gemm(x, w, None, None, out, None, 0, 0, [], [], 0, None, 0, None)
             torch.cuda.synchronize()
@@ -345,7 +436,7 @@ def decode_gemm_sweep(iters: int = 30) -> None:
             us = 1000 * s.elapsed_time(e) / iters
             cells.append(f"{us:6.1f}us {n * k * 2 / us / 1e6:4.2f}TB/s")
         print(f"{name:16s} " + "  ".join(cells))
-    ext.decode_gemm_configure(2, 8)
+    ext.decode_gemm_configure(2, 8, 8)
 
 
 def decode_gemm_one(iters: int = 4) -> None:
@@ -455,7 +546,8 @@ def gemm_train_shapes(iters: int = 20) -> None:
     print(f"{'wgrad(sk) lm_head ' + f'{v}x{k}x{m}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
 
 
-CASES = {"attention-fwd": attention_fwd, "decode-gemm-one": decode_gemm_one, "gemm-train-shapes": gemm_train_shapes, "sweep-table": sweep_table, "train-small": train_small, "decode-small": decode_small, "train-table": train_table,
+CASES = {"attention-fwd": attention_fwd, "decode-gemm-one": decode_gemm_one, "gemm-train-shapes": gemm_train_shapes,
+         "decode-overlap-probe": decode_overlap_probe, "sweep-table": sweep_table, "train-small": train_small, "decode-small": decode_small, "train-table": train_table,
          "decode-table": decode_table, "decode-table-tp": decode_table_tp,
          "decode-attention-sweep": decode_attention_sweep, "route-topk-bench": route_topk_bench,
          "decode-gemm-sweep": decode_gemm_sweep}

@@ -98,3 +98,13 @@ def test_fp32_scores_output(ext, m, n, k):
     ext.decode_gemm(x, w, None, None, out, None, 0, 0, [], [], 0, None, 0, None)
     want = x.float() @ w.float().t()
     assert torch.allclose(out, want, atol=1e-3, rtol=1e-3), (out - want).abs().max()
+
+
+def test_resident_cluster_counts(ext):
+    """How many split-K clusters can be resident at once (the fused all-reduce lowers its split
+    count until its grid fits): an unsplit 32-tile row-parallel grid always fits, and wider
+    clusters never fit more."""
+    counts = [ext.decode_gemm_resident_clusters(s) for s in (1, 2, 4, 8)]
+    print("resident clusters for 1/2/4/8 splits:", counts)
+    assert counts[0] >= 32
+    assert all(a >= b for a, b in zip(counts, counts[1:])), counts

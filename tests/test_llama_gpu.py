@@ -372,9 +372,9 @@ def test_phase_split_decode_attention_equals_single_launch(ext, tma):
         common = dict(mem_splits=n_mem, mem_split_keys=msk, part_o=part_o, part_ml=part_ml)
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
+        with torch.cuda.stream(side):  # a persistent grid of 7 CTAs walks the local splits
             ext.decode_attention(q, H, Hkv, D, None, None, None, None, cache[0], cache[1], loc_len, 0, sk, False,
-                                 split_lo=n_mem, split_count=n_loc, phase=1, **common)
+                                 split_lo=n_mem, split_count=n_loc, phase=1, max_ctas=7, **common)
         ext.decode_attention(q, H, Hkv, D, mk, mv, mem_idx, mem_len, cache[0], cache[1], loc_len, 0, sk, False,
                              split_lo=0, split_count=n_mem, phase=1, **common)
         torch.cuda.current_stream().wait_stream(side)
