@@ -634,10 +634,16 @@ void tp_allgather(torch::Tensor src, std::vector<int64_t> dsts, std::vector<int6
 // out[M, N] (+ out2 for columns >= split_col) = x[M, K] w[N, K]^T (+ bias, + residual); with peer
 // addresses in recv / flags (one per rank) the result is summed over the ranks (row-parallel
 // projection) inside the same kernel.  splits <= 0 picks the K split from the SM count.
+static void set_folded_norm(DecodeGemmArgs& a, const c10::optional<torch::Tensor>& ss_out,
+                            const c10::optional<torch::Tensor>& ss_in, int64_t ss_tiles, int64_t ss_dim,
+                            double ss_eps);
+
 void decode_gemm(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
                  c10::optional<torch::Tensor> residual, torch::Tensor out, c10::optional<torch::Tensor> out2,
                  int64_t split_col, int64_t splits, std::vector<int64_t> recv, std::vector<int64_t> flags, int64_t rank,
-                 c10::optional<torch::Tensor> epochs, int64_t max_spins, c10::optional<torch::Tensor> error) {
+                 c10::optional<torch::Tensor> epochs, int64_t max_spins, c10::optional<torch::Tensor> error,
+                 bool swiglu, c10::optional<torch::Tensor> ss_out, c10::optional<torch::Tensor> ss_in, int64_t ss_tiles,
+                 int64_t ss_dim, double ss_eps) {
   c10::cuda::CUDAGuard guard(x.device());
   expect(x, at::kBFloat16, "x");
   expect(w, at::kBFloat16, "w");
@@ -674,7 +680,9 @@ void decode_gemm(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> 
     a.out2 = ptr<__nv_bfloat16>(*out2);
     a.ldo2 = out2->stride(0);
   }
-  TORCH_CHECK(out.size(1) >= a.split_col, "out narrower than its columns");
+  a.swiglu = swiglu ? 1 : 0;
+  set_folded_norm(a, ss_out, ss_in, ss_tiles, ss_dim, ss_eps);
+  TORCH_CHECK(swiglu ? out.size(1) >= a.N / 2 : out.size(1) >= a.split_col, "out narrower than its columns");
   const int tiles = (a.N + 127) / 128, nkb = a.K / 64;
   static int sm_cache[64] = {};
   int& sms = sm_cache[x.device().index() & 63];
@@ -709,7 +717,8 @@ void decode_gemm(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> 
 void decode_qkv_rope(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias, torch::Tensor q_out,
                      torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor cache_rows, torch::Tensor pos,
                      torch::Tensor cos_t, torch::Tensor sin_t, int64_t head_dim, int64_t q_end, int64_t k_end,
-                     int64_t v_end, c10::optional<torch::Tensor> route_out) {
+                     int64_t v_end, c10::optional<torch::Tensor> route_out, c10::optional<torch::Tensor> ss_in,
+                     int64_t ss_tiles, int64_t ss_dim, double ss_eps) {
   c10::cuda::CUDAGuard guard(x.device());
   expect(x, at::kBFloat16, "x");
   expect(w, at::kBFloat16, "w");
@@ -756,6 +765,7 @@ void decode_qkv_rope(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tens
   const int tiles = (a.N + 127) / 128, nkb = a.K / 64;
   a.splits = pra_decode_gemm_splits(tiles, nkb, sms);
   a.world = 1;
+  set_folded_norm(a, c10::nullopt, ss_in, ss_tiles, ss_dim, ss_eps);
   check(pra_decode_gemm(a, stream()), "decode_qkv_rope");
 }
 
@@ -785,13 +795,76 @@ void rope_copy(torch::Tensor src, torch::Tensor dst, c10::optional<torch::Tensor
   check(pra_rope_copy(a, stream()), "rope_copy");
 }
 
-void silu_mul(torch::Tensor gate_up, torch::Tensor out) {
+static BoundsStatus* bounds_word(const torch::Device& dev);
+
+// Folded-RMSNorm arguments of a decode GEMM (see DecodeGemmArgs::ss_out / ss_in).
+static void set_folded_norm(DecodeGemmArgs& a, const c10::optional<torch::Tensor>& ss_out,
+                            const c10::optional<torch::Tensor>& ss_in, int64_t ss_tiles, int64_t ss_dim,
+                            double ss_eps) {
+  if (ss_out.has_value()) {
+    TORCH_CHECK(ss_out->scalar_type() == at::kFloat && ss_out->is_cuda() && ss_out->is_contiguous() &&
+                    ss_out->numel() >= (int64_t)((a.N + 127) / 128) * 64,
+                "ss_out: fp32 [tiles, 64]");
+    a.ss_out = ptr<float>(*ss_out);
+  }
+  if (ss_in.has_value()) {
+    TORCH_CHECK(ss_in->scalar_type() == at::kFloat && ss_in->is_cuda() && ss_in->is_contiguous() &&
+                    ss_tiles > 0 && ss_in->numel() >= ss_tiles * 64 && ss_dim > 0,
+                "ss_in: fp32 [ss_tiles, 64] with ss_dim > 0");
+    a.ss_in = ptr<const float>(*ss_in);
+    a.ss_tiles = (int)ss_tiles;
+    a.ss_dim = (int)ss_dim;
+    a.ss_eps = (float)ss_eps;
+  }
+}
+
+// x [B, d], pos / rows / new_len [B] int32 for one decode step (see pra_decode_prologue).
+std::vector<torch::Tensor> decode_prologue(torch::Tensor ids, torch::Tensor cache_len,
+                                           c10::optional<torch::Tensor> pos_offset, torch::Tensor embed,
+                                           int64_t max_len, c10::optional<torch::Tensor> ss_out) {
+  c10::cuda::CUDAGuard guard(embed.device());
+  expect(embed, at::kBFloat16, "embed");
+  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_cuda() && ids.is_contiguous(), "ids: int64 CUDA [B]");
+  TORCH_CHECK(cache_len.scalar_type() == at::kInt && cache_len.is_contiguous() && cache_len.numel() == ids.numel(),
+              "cache_len: int32 [B]");
+  TORCH_CHECK(embed.is_contiguous() && embed.dim() == 2, "embed: [vocab, d] contiguous");
+  const int64_t B = ids.numel();
+  DecodePrologueArgs a{};
+  a.ids = ids.data_ptr<int64_t>();
+  a.cache_len = ptr<const int>(cache_len);
+  if (pos_offset.has_value()) {
+    TORCH_CHECK(pos_offset->scalar_type() == at::kInt && pos_offset->numel() == B && pos_offset->is_contiguous(),
+                "pos_offset: int32 [B]");
+    a.pos_offset = ptr<const int>(*pos_offset);
+  }
+  a.embed = ptr<const __nv_bfloat16>(embed);
+  a.vocab = embed.size(0);
+  a.d = embed.size(1);
+  a.B = (int)B;
+  a.max_len = (int)max_len;
+  auto x = torch::empty({B, a.d}, embed.options());
+  auto io = torch::empty({3, B}, cache_len.options());
+  a.x = ptr<__nv_bfloat16>(x);
+  a.pos = ptr<int>(io[0]);
+  a.rows = ptr<int>(io[1]);
+  a.new_len = ptr<int>(io[2]);
+  a.bounds = bounds_word(embed.device());
+  if (ss_out.has_value()) {
+    TORCH_CHECK(ss_out->scalar_type() == at::kFloat && ss_out->is_contiguous() && ss_out->numel() >= B,
+                "ss_out: fp32 [>= B]");
+    a.ss_out = ptr<float>(*ss_out);
+  }
+  check(pra_decode_prologue(a, stream()), "decode_prologue");
+  return {x, io[0], io[1], io[2]};
+}
+
+void silu_mul(torch::Tensor gate_up, torch::Tensor out, int64_t block) {
   c10::cuda::CUDAGuard guard(gate_up.device());
   expect(gate_up, at::kBFloat16, "gate_up");
   TORCH_CHECK(gate_up.is_contiguous() && out.is_contiguous() && gate_up.size(1) == 2 * out.size(1),
               "gate_up must be [M, 2F] and out [M, F]");
-  check(pra_silu_mul(ptr<const __nv_bfloat16>(gate_up), gate_up.size(0), out.size(1), ptr<__nv_bfloat16>(out),
-                     stream()),
+  check(pra_silu_mul(ptr<const __nv_bfloat16>(gate_up), gate_up.size(0), out.size(1), (int)block,
+                     ptr<__nv_bfloat16>(out), stream()),
         "silu_mul");
 }
 
@@ -1553,7 +1626,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_allreduce", &tp_allreduce);
   m.def("tp_allgather", &tp_allgather);
   m.def("tp_signal_words", [](int64_t world) { return (int64_t)TP_MAX_BLOCKS * world; });
-  m.def("silu_mul", &silu_mul);
+  m.def("silu_mul", &silu_mul, py::arg("gate_up"), py::arg("out"), py::arg("block") = 0);
+  m.def("decode_prologue", &decode_prologue, py::arg("ids"), py::arg("cache_len"), py::arg("pos_offset"),
+        py::arg("embed"), py::arg("max_len"), py::arg("ss_out") = py::none());
   m.def("decode_attention", &decode_attention, py::arg("q"), py::arg("heads"), py::arg("kv_heads"),
         py::arg("head_dim"), py::arg("mem_k"), py::arg("mem_v"), py::arg("mem_idx"), py::arg("mem_len"),
         py::arg("loc_k"), py::arg("loc_v"), py::arg("loc_len"), py::arg("max_keys"), py::arg("split_keys"),
@@ -1584,8 +1659,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("bounds_reset", &bounds_reset);
   m.def("embed_add", &embed_add);
   m.def("combine_partials", &combine_partials);
-  m.def("decode_gemm", &decode_gemm);
-  m.def("decode_qkv_rope", &decode_qkv_rope);
+  m.def("decode_gemm", &decode_gemm, py::arg("x"), py::arg("w"), py::arg("bias"), py::arg("residual"), py::arg("out"),
+        py::arg("out2"), py::arg("split_col"), py::arg("splits"), py::arg("recv"), py::arg("flags"), py::arg("rank"),
+        py::arg("epochs"), py::arg("max_spins"), py::arg("error"), py::arg("swiglu") = false,
+        py::arg("ss_out") = py::none(), py::arg("ss_in") = py::none(), py::arg("ss_tiles") = 0, py::arg("ss_dim") = 0,
+        py::arg("ss_eps") = 0.0);
+  m.def("decode_qkv_rope", &decode_qkv_rope, py::arg("x"), py::arg("w"), py::arg("bias"), py::arg("q_out"),
+        py::arg("k_cache"), py::arg("v_cache"), py::arg("cache_rows"), py::arg("pos"), py::arg("cos_t"),
+        py::arg("sin_t"), py::arg("head_dim"), py::arg("q_end"), py::arg("k_end"), py::arg("v_end"),
+        py::arg("route_out"), py::arg("ss_in") = py::none(), py::arg("ss_tiles") = 0, py::arg("ss_dim") = 0,
+        py::arg("ss_eps") = 0.0);
   m.def("decode_gemm_max_tiles", []() { return (int64_t)DG_MAX_TILES; });
   m.def("decode_gemm_flag_slots", []() { return (int64_t)DG_MAX_TILES * DG_MAX_SPLITS; });
   m.def("decode_gemm_resident_clusters", [](int64_t splits) { return (int64_t)pra_decode_gemm_resident_clusters((int)splits); });

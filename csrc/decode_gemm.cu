@@ -51,7 +51,8 @@ constexpr int B_BYTES = MT * BK * 2;  // 8 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 template <int STAGES>
 struct Ring {
-  static_assert(STAGES * STAGE_BYTES >= MT * BF * 4, "the epilogue stages the fp32 tile in the ring");
+  static_assert(STAGES * STAGE_BYTES >= (MT * BF + MT + MT * (BF / 8)) * 4,
+                "the epilogue stages the fp32 tile, the row scales and the chunk sums in the ring");
   static constexpr int OFF_BAR = STAGES * STAGE_BYTES;
   static constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;  // + barriers, + alignment slack for the 1024-byte atoms
   };
@@ -258,6 +259,39 @@ __global__ void __launch_bounds__(NT) decode_gemm_kernel(const __grid_constant__
     __syncthreads();
   }
   const int c_lo = m_lo * (BF / 8), c_hi = m_hi * (BF / 8);  // this CTA's 8-feature row chunks
+  float* s_rstd = tile_s + MT * BF;  // [MT] folded-norm row scales
+  float* s_part = s_rstd + MT;       // [MT][BF / 8] per-chunk sums of squares (producer)
+  if (a.ss_in != nullptr) {  // folded RMSNorm: scale this CTA's rows by their rsqrt(mean square)
+    for (int m = m_lo + tid; m < m_hi; m += NT) {
+      float t = 0.f;
+      for (int k = 0; k < a.ss_tiles; ++k) t += a.ss_in[k * MT + m];
+      s_rstd[m] = rsqrtf(t / (float)a.ss_dim + a.ss_eps);
+    }
+    __syncthreads();
+    for (int i = m_lo * BF + tid; i < m_hi * BF; i += NT) tile_s[i] *= s_rstd[i / BF];
+    __syncthreads();
+  }
+  // producer side: sum of squares of the bf16 values stored, per (row, chunk), then per row in order
+  auto ss_chunk = [&](int m, int c, const uint4& packed) {
+    if (a.ss_out == nullptr) return;
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&packed);
+    float t = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      t += f.x * f.x + f.y * f.y;
+    }
+    s_part[m * (BF / 8) + c] = t;
+  };
+  auto ss_finish = [&]() {
+    if (a.ss_out == nullptr) return;
+    __syncthreads();
+    for (int m = m_lo + tid; m < m_hi; m += NT) {
+      float t = 0.f;
+      for (int c = 0; c < BF / 8; ++c) t += s_part[m * (BF / 8) + c];
+      a.ss_out[tile * MT + m] = t;
+    }
+  };
 
   if (a.world <= 1 && a.pos != nullptr) {  // decode QKV: bias, rotary, scatter into q / caches / routing query
     const int half = a.head_dim / 2;
@@ -296,6 +330,19 @@ __global__ void __launch_bounds__(NT) decode_gemm_kernel(const __grid_constant__
     return;
   }
 
+  if (a.swiglu) {  // [64 gate | 64 up] features -> 64 SwiGLU outputs per row
+    for (int i = m_lo * 8 + tid; i < m_hi * 8; i += NT) {
+      const int m = i / 8, c = i % 8, n = tile * (BF / 2) + c * 8;
+      float g[8], u[8], v[8];
+      staged8(tile_s + m * BF + c * 8, g);
+      staged8(tile_s + m * BF + BF / 2 + c * 8, u);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = g[j] / (1.f + __expf(-g[j])) * u[j];
+      *reinterpret_cast<uint4*>(a.out + (int64_t)m * a.ldo + n) = pack8(v);
+    }
+    return;
+  }
+
   if (a.out_f32 != nullptr) {  // fp32 results (routing scores): 2 x 16-byte stores per chunk
     for (int i = c_lo + tid; i < c_hi; i += NT) {
       const int m = i / (BF / 8), c = i % (BF / 8), n = n0 + c * 8;
@@ -328,8 +375,11 @@ __global__ void __launch_bounds__(NT) decode_gemm_kernel(const __grid_constant__
       }
       const bool second = a.out2 != nullptr && n >= a.split_col;
       __nv_bfloat16* dst = second ? a.out2 + (int64_t)m * a.ldo2 + (n - a.split_col) : a.out + (int64_t)m * a.ldo + n;
-      *reinterpret_cast<uint4*>(dst) = pack8(v);
+      const uint4 packed = pack8(v);
+      *reinterpret_cast<uint4*>(dst) = packed;
+      ss_chunk(m, c, packed);
     }
+    ss_finish();
     return;
   }
 
@@ -383,8 +433,11 @@ __global__ void __launch_bounds__(NT) decode_gemm_kernel(const __grid_constant__
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[j] += part[j];
     }
-    *reinterpret_cast<uint4*>(a.out + (int64_t)m * a.ldo + n) = pack8(v);
+    const uint4 packed = pack8(v);
+    *reinterpret_cast<uint4*>(a.out + (int64_t)m * a.ldo + n) = packed;
+    ss_chunk(m, c, packed);
   }
+  ss_finish();
 }
 
 }  // namespace dg
@@ -533,6 +586,10 @@ cudaError_t pra_decode_gemm(const DecodeGemmArgs& a, cudaStream_t st) {
   splits = (nkb + per - 1) / per;  // no empty split
   if (a.world > 1 && (a.epochs == nullptr || a.error == nullptr)) return cudaErrorInvalidValue;
   if (a.out_f32 && (a.bias || a.residual || a.out2 || a.pos || a.world > 1 || a.ldo % 4)) return cudaErrorInvalidValue;
+  if (a.swiglu && (a.N % BF || a.bias || a.residual || a.out2 || a.pos || a.out_f32 || a.world > 1))
+    return cudaErrorInvalidValue;
+  if (a.ss_out && (a.N % BF || a.out2 || a.pos || a.out_f32 || a.swiglu)) return cudaErrorInvalidValue;
+  if (a.ss_in && (a.ss_tiles <= 0 || a.ss_dim <= 0 || a.out_f32)) return cudaErrorInvalidValue;
   static int configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);

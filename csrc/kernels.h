@@ -238,7 +238,11 @@ struct RopeCopyArgs {
   int M, heads, head_dim;
 };
 cudaError_t pra_rope_copy(const RopeCopyArgs& args, cudaStream_t stream);
-cudaError_t pra_silu_mul(const __nv_bfloat16* gate_up, int64_t M, int F, __nv_bfloat16* out, cudaStream_t stream);
+// act = silu(gate) * up.  block == 0: gate_up rows are [gate (F) | up (F)]; block > 0: they
+// alternate in runs of `block` features ([gate block j | up block j] ...), the layout the fused
+// decode GEMM epilogue reads.
+cudaError_t pra_silu_mul(const __nv_bfloat16* gate_up, int64_t M, int F, int block, __nv_bfloat16* out,
+                         cudaStream_t stream);
 
 // Bounds-checked kernel variants (``set_bounds_check(true)``): a checked kernel records the
 // first out-of-range index it meets here and skips that access (the key is masked, the row is
@@ -256,7 +260,25 @@ enum : int {
   PRA_BOUNDS_ROUTE_NAMESPACE = 4,  // routing: namespace range outside the chunk table
   PRA_BOUNDS_ROUTE_POOL_ROW = 5,   // routing: a selected chunk's rows run past the pool
   PRA_BOUNDS_ROUTE_CHUNK = 6,      // routing merge: candidate chunk id outside the chunk table
+  PRA_BOUNDS_DECODE_TOKEN = 7,     // decode prologue: token id outside the vocabulary (row 0 read)
 };
+
+// Decode step prologue (one launch): token embeddings, rotary positions, cache rows, new lengths.
+struct DecodePrologueArgs {
+  const int64_t* ids;          // [B] token ids
+  const int* cache_len;        // [B]
+  const int* pos_offset;       // [B] or null
+  const __nv_bfloat16* embed;  // [vocab, d]
+  int64_t vocab, d;
+  int B, max_len;
+  __nv_bfloat16* x;            // [B, d]
+  int* pos;                    // [B] cache_len + pos_offset
+  int* rows;                   // [B] b * max_len + cache_len
+  int* new_len;                // [B] cache_len + 1
+  BoundsStatus* bounds;        // non-null: report out-of-vocabulary ids
+  float* ss_out;               // [B] or null: sum of squares of each embedding row (first RMSNorm)
+};
+cudaError_t pra_decode_prologue(const DecodePrologueArgs& a, cudaStream_t stream);
 
 struct DecodeAttnParams {
   const __nv_bfloat16* q;      // [B, H * Dh] post-rotary queries of the decoded tokens
@@ -431,6 +453,16 @@ struct DecodeGemmArgs {
   const __nv_bfloat16* residual;  // [M, N] (row stride ldo) or null
   __nv_bfloat16* out;             // columns [0, split_col): out[m * ldo + n]
   float* out_f32;                 // instead of out: fp32 results (no bias / residual / out2; one GPU)
+  int swiglu;                     // each 128-row weight tile is [64 gate | 64 up] rows: out[m, tile * 64 + j] =
+                                  // silu(gate_j) * up_j (N / 2 output columns; no bias / residual; one GPU)
+  // RMSNorm folded into the GEMMs around it (the norm weight multiplied into this GEMM's weight
+  // columns): a producer writes, per 128-feature tile and token row, the sum of squares of its
+  // bf16 output (ss_out[tile * 64 + m]); a consumer scales its accumulator row m by
+  // rsqrt(sum_t ss_in[t * 64 + m] / ss_dim + ss_eps), the tiles summed in order.
+  float* ss_out;
+  const float* ss_in;
+  int ss_tiles, ss_dim;
+  float ss_eps;
   int64_t ldo;
   __nv_bfloat16* out2;            // columns [split_col, N): out2[m * ldo2 + n - split_col] (null: none)
   int64_t ldo2;

@@ -48,16 +48,65 @@ __global__ void rope_copy_kernel(RopeCopyArgs a) {
   }
 }
 
+// ---------------------------------------------------------------- decode step prologue
+// One CTA per batch row: the token's embedding row (16-byte copies), its rotary position
+// (cache length + position offset), the cache row it is written to (b * max_len + cache length)
+// and the row's new cache length.  Token ids outside the vocabulary read row 0 and are reported
+// through the bounds status when checking is on.
+__global__ void decode_prologue_kernel(DecodePrologueArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int b = blockIdx.x;
+  int64_t id = a.ids[b];
+  if (id < 0 || id >= a.vocab) {
+    if (threadIdx.x == 0 && a.bounds) bounds_fail(a.bounds, PRA_BOUNDS_DECODE_TOKEN, id, a.vocab);
+    id = 0;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(a.embed + id * a.d);
+  uint4* dst = reinterpret_cast<uint4*>(a.x + (int64_t)b * a.d);
+  float ss = 0.f;
+  for (int64_t c = threadIdx.x; c < a.d / 8; c += blockDim.x) {
+    const uint4 v = src[c];
+    dst[c] = v;
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      ss += f.x * f.x + f.y * f.y;
+    }
+  }
+  if (a.ss_out != nullptr) {  // the first folded RMSNorm's sum of squares (fixed summation order)
+    __shared__ float warp_ss[32];
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) warp_ss[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.f;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += warp_ss[w];
+      a.ss_out[b] = t;
+    }
+  }
+  if (threadIdx.x == 0) {
+    const int len = a.cache_len[b];
+    a.pos[b] = len + (a.pos_offset ? a.pos_offset[b] : 0);
+    a.rows[b] = b * a.max_len + len;
+    a.new_len[b] = len + 1;
+  }
+}
+
 // ---------------------------------------------------------------- swiglu
-__global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int64_t M, int F, __nv_bfloat16* __restrict__ out) {
+__global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int64_t M, int F, int block,
+                                __nv_bfloat16* __restrict__ out) {
   pdl_launch_dependents();
   pdl_wait();
   const int64_t pairs = M * (F / 2);
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < pairs; e += (int64_t)gridDim.x * blockDim.x) {
     const int64_t m = e / (F / 2);
     const int j = 2 * (int)(e - m * (F / 2));
-    const float2 g = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(gu + m * 2 * F + j));
-    const float2 u = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(gu + m * 2 * F + F + j));
+    const int gc = block > 0 ? (j / block) * 2 * block + j % block : j;  // gate column of feature j
+    const int uc = block > 0 ? gc + block : F + j;
+    const float2 g = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(gu + m * 2 * F + gc));
+    const float2 u = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(gu + m * 2 * F + uc));
     const float a = g.x / (1.f + __expf(-g.x)) * u.x;
     const float b = g.y / (1.f + __expf(-g.y)) * u.y;
     *reinterpret_cast<__nv_bfloat162*>(out + m * F + j) = __floats2bfloat162_rn(a, b);
@@ -1036,13 +1085,23 @@ cudaError_t pra_rope_copy(const RopeCopyArgs& a, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-cudaError_t pra_silu_mul(const __nv_bfloat16* gate_up, int64_t M, int F, __nv_bfloat16* out, cudaStream_t st) {
+cudaError_t pra_decode_prologue(const DecodePrologueArgs& a, cudaStream_t st) {
+  if (a.B == 0) return cudaSuccess;
+  if (a.d % 8 || (reinterpret_cast<uintptr_t>(a.embed) | reinterpret_cast<uintptr_t>(a.x)) & 15)
+    return cudaErrorInvalidValue;
+  return pra_launch_pdl(pra::llama::decode_prologue_kernel, dim3(a.B), dim3(128), 0, st, a);
+}
+
+cudaError_t pra_silu_mul(const __nv_bfloat16* gate_up, int64_t M, int F, int block, __nv_bfloat16* out,
+                         cudaStream_t st) {
   if (M == 0) return cudaSuccess;
   if (F % 2) return cudaErrorInvalidValue;
   const int64_t pairs = M * (F / 2);
   const int64_t want = (pairs + 255) / 256;
   const int blocks = (int)(want < 148 * 16 ? want : 148 * 16);
-  PRA_RETURN_IF_ERROR(pra_launch_pdl(pra::llama::silu_mul_kernel, dim3(blocks), dim3(256), 0, st, gate_up, M, F, out));
+  if (block < 0 || (block > 0 && (F % block || block % 2))) return cudaErrorInvalidValue;
+  PRA_RETURN_IF_ERROR(
+      pra_launch_pdl(pra::llama::silu_mul_kernel, dim3(blocks), dim3(256), 0, st, gate_up, M, F, block, out));
   return cudaGetLastError();
 }
 

@@ -61,6 +61,8 @@ class LlamaWeights:
                  head: torch.Tensor, tp_rank: int = 0, tp_size: int = 1):
         self.cfg, self.layers, self.embed, self.norm, self.head = cfg, layers, embed, norm, head
         self.tp_rank, self.tp_size = tp_rank, tp_size
+        self.mlp_block = 0  # > 0: gate / up rows interleaved in runs of this many (set by an engine)
+        self.norm_folded = False  # RMSNorm weights multiplied into qkv_route / gate_up (set by an engine)
 
     @staticmethod
     def _shard_rows(t: torch.Tensor, rank: int, size: int) -> torch.Tensor:
@@ -218,6 +220,9 @@ class PRALlamaEngine:
         # ones fused with their all-reduce; each layer's QKV weight gains the routing-query rows.
         self.native_decode = _DECODE_GEMM
         self.route_dim = cfg.num_key_value_heads * cfg.head_dim
+        self._ones = torch.ones(cfg.hidden_size, device=self.device, dtype=torch.bfloat16)
+        self._ss_tiles = cfg.hidden_size // 128
+        self._ss: torch.Tensor | None = None  # [2, hidden / 128, 64] folded-norm sums of squares
         if self.native_decode:
             self._attach_route_rows()
 
@@ -253,6 +258,40 @@ class PRALlamaEngine:
                 rb = gather(group_mean(lw.qkv_bias[:qd]).to(torch.bfloat16))
                 lw.qkv_route_bias = torch.cat([lw.qkv_bias, rb]).contiguous()
                 lw.qkv_bias = lw.qkv_route_bias[: qd + 2 * kd]
+        self._block_mlp_rows()
+        self._fold_norms()
+
+    def _fold_norms(self) -> None:
+        """Multiply each layer's RMSNorm weights into the columns of the projection after them
+        (``qkv_route`` <- ``ln_in``, ``gate_up`` <- ``ln_post``), once per weight set.  The decode
+        GEMMs then apply the norm as one row scale in their epilogue (the sums of squares come
+        from the GEMM that produced the residual stream), and every explicit RMSNorm (prefill,
+        chunk encoding, batches above 64 rows) normalises with unit weights."""
+        if getattr(self.w, "norm_folded", False) or self.cfg.hidden_size % 128:
+            return
+        qd, kd = self.q_dim, self.kv_dim
+        for lw in self.w.layers:
+            fused = (lw.qkv_route.float() * lw.ln_in.float()[None, :]).to(torch.bfloat16).contiguous()
+            lw.qkv_route = fused
+            lw.qkv = fused[: qd + 2 * kd]
+            lw.gate_up = (lw.gate_up.float() * lw.ln_post.float()[None, :]).to(torch.bfloat16).contiguous()
+        self.w.norm_folded = True
+
+    def _block_mlp_rows(self, block: int = 64) -> None:
+        """Interleave every layer's ``[gate | up]`` rows in runs of ``block`` (``[gate 0..63 |
+        up 0..63 | gate 64..127 | ...]``), once per weight set: a 128-row tile of the decode GEMM then
+        holds matching gate and up features and applies SwiGLU in its epilogue; larger batches
+        use the same layout through ``silu_mul(..., block)``."""
+        if getattr(self.w, "mlp_block", 0) or not self.native_decode:
+            return
+        f = self.w.layers[0].gate_up.shape[0] // 2
+        if f % block:
+            return
+        for lw in self.w.layers:
+            d = lw.gate_up.shape[1]
+            g, u = lw.gate_up[:f].view(f // block, block, d), lw.gate_up[f:].view(f // block, block, d)
+            lw.gate_up = torch.stack([g, u], 1).reshape(2 * f, d).contiguous()
+        self.w.mlp_block = block
 
     # -- helpers ----------------------------------------------------------------
     def rope_tables(self, max_pos: int) -> tuple[torch.Tensor, torch.Tensor]:
@@ -285,29 +324,54 @@ class PRALlamaEngine:
     def _decode_rows(self, x) -> bool:
         return self.native_decode and x.shape[0] <= _DECODE_ROWS
 
-    def _gemm(self, x, w, bias=None, residual=None) -> torch.Tensor:
+    def _gemm(self, x, w, bias=None, residual=None, ss_out=None) -> torch.Tensor:
         out = torch.empty((x.shape[0], w.shape[0]), device=x.device, dtype=torch.bfloat16)
         if self._decode_rows(x):
-            self.ext.decode_gemm(x, w, bias, residual, out, None, 0, 0, [], [], 0, None, 0, None)
+            self.ext.decode_gemm(x, w, bias, residual, out, None, 0, 0, [], [], 0, None, 0, None, ss_out=ss_out)
             return out
         self.ext.gemm("tn", x, w, residual, out, bias, None, 1.0, 1.0 if residual is not None else 0.0, None)
         return out
 
-    def _row_parallel(self, x, w, residual) -> torch.Tensor:
+    def _row_parallel(self, x, w, residual, ss_out=None) -> torch.Tensor:
         """out = residual + x @ w^T, summed over tensor-parallel ranks (decode rows: one fused
-        GEMM + all-reduce kernel)."""
+        GEMM + all-reduce kernel).  ``ss_out`` (decode rows): the output's per-tile row sums of
+        squares for the next, folded RMSNorm."""
         if self.tp is None:
-            return self._gemm(x, w, residual=residual)
+            return self._gemm(x, w, residual=residual, ss_out=ss_out)
         if self._decode_rows(x) and x.shape[0] <= self.tp.decode_rows and w.shape[0] <= self.tp.decode_width:
-            return self.tp.fused_gemm_allreduce(x, w, residual)
+            return self.tp.fused_gemm_allreduce(x, w, residual, ss_out=ss_out)
         return self.tp.gemm_allreduce(x, w, residual)
 
-    def _mlp(self, lw: LayerWeights, x: torch.Tensor) -> torch.Tensor:
-        h = self._norm(x, lw.ln_post)
-        gu = self._gemm(h, lw.gate_up)
-        act = torch.empty((x.shape[0], gu.shape[1] // 2), device=x.device, dtype=torch.bfloat16)
-        self.ext.silu_mul(gu, act)
+    def _mlp(self, lw: LayerWeights, x: torch.Tensor, ss=None) -> torch.Tensor:
+        """SwiGLU MLP with its residual.  ``ss`` (decode rows, folded norms): ``(ss_in, ss_out)``,
+        the per-tile sums of squares of ``x`` (its RMSNorm, folded into ``gate_up``) and where the
+        down projection leaves those of its output (the next layer's input norm)."""
+        blocked = getattr(self.w, "mlp_block", 0)
+        act = torch.empty((x.shape[0], lw.gate_up.shape[0] // 2), device=x.device, dtype=torch.bfloat16)
+        if ss is not None:
+            # one GEMM: the folded post-attention RMSNorm, SwiGLU in the epilogue
+            norm = dict(ss_in=ss[0], ss_tiles=self._ss_tiles, ss_dim=self.cfg.hidden_size, ss_eps=self.cfg.rms_norm_eps)
+            if blocked == 64 and lw.gate_up.shape[0] % 128 == 0:
+                self.ext.decode_gemm(x, lw.gate_up, None, None, act, None, 0, 0, [], [], 0, None, 0, None,
+                                     swiglu=True, **norm)
+            else:
+                gu = torch.empty((x.shape[0], lw.gate_up.shape[0]), device=x.device, dtype=torch.bfloat16)
+                self.ext.decode_gemm(x, lw.gate_up, None, None, gu, None, 0, 0, [], [], 0, None, 0, None, **norm)
+                self.ext.silu_mul(gu, act, blocked)
+            return self._row_parallel(act, lw.down, x, ss_out=ss[1])
+        h = self._norm(x, self._ln(lw.ln_post))
+        if blocked == 64 and self._decode_rows(h) and lw.gate_up.shape[0] % 128 == 0:
+            # one GEMM: SwiGLU in the epilogue of the [gate | up]-interleaved weight
+            self.ext.decode_gemm(h, lw.gate_up, None, None, act, None, 0, 0, [], [], 0, None, 0, None, swiglu=True)
+        else:
+            gu = self._gemm(h, lw.gate_up)
+            self.ext.silu_mul(gu, act, blocked)
         return self._row_parallel(act, lw.down, x)
+
+    def _ln(self, weight: torch.Tensor) -> torch.Tensor:
+        """The weight an explicit RMSNorm applies: ones once the norm weights are folded into
+        the projections after them."""
+        return self._ones if getattr(self.w, "norm_folded", False) else weight
 
     def _embed(self, ids: torch.Tensor) -> torch.Tensor:
         return self.w.embed[ids.reshape(-1)].contiguous()
@@ -440,7 +504,7 @@ class PRALlamaEngine:
         x = self._embed(ids)
         qd, kd = self.q_dim, self.kv_dim
         for li, lw in enumerate(self.w.layers):
-            h = self._norm(x, lw.ln_in)
+            h = self._norm(x, self._ln(lw.ln_in))
             qkv = self._gemm(h, lw.qkv, lw.qkv_bias)
             # gist: mean pre-rotary key of each chunk
             k_pre = qkv[:, qd: qd + kd]
@@ -491,7 +555,7 @@ class PRALlamaEngine:
         self.max_len = max_len
         # rotary position of cache slot t of row b: offset[b] + t (a long prompt's direct
         # tail continues the positions of its implicit head when they are natively legal)
-        self.pos_offset = (position_offset.to(self.device, torch.int32) if position_offset is not None
+        self.pos_offset = (position_offset.to(self.device, torch.int32).contiguous() if position_offset is not None
                            else torch.zeros(B, device=self.device, dtype=torch.int32))
         self._max_pos = int(self.pos_offset.max()) + max_len if B else max_len
         step = row_batch or B
@@ -518,7 +582,7 @@ class PRALlamaEngine:
             namespace = (self.namespace[0][r0: r0 + B].contiguous(), self.namespace[1][r0: r0 + B].contiguous())
             self._row0 = r0
         for li, lw in enumerate(self.w.layers):
-            h = self._norm(x, lw.ln_in)
+            h = self._norm(x, self._ln(lw.ln_in))
             qkv = self._gemm(h, lw.qkv, lw.qkv_bias)
             mem_args = (None, None, None, None)
             if use_memory and cfg.is_pra_layer(li):
@@ -580,23 +644,32 @@ class PRALlamaEngine:
         B = token_ids.shape[0]
         qd, kd = self.q_dim, self.kv_dim
         cos, sin = self.rope_tables(self._max_pos)
-        pos = self.cache_len + self.pos_offset
-        rows = torch.arange(B, device=self.device, dtype=torch.int32) * self.max_len + self.cache_len
-        new_len = self.cache_len + 1
-        x = self._embed(token_ids.to(self.device))
+        # one launch: embeddings, rotary positions, cache rows and new lengths of this step
+        # folded RMSNorms: buffer 0 holds the per-tile row sums of squares of each layer's input
+        # (from the prologue, then from the previous down projection), buffer 1 those of the
+        # attention block's output (from the O projection)
+        folded = getattr(self.w, "norm_folded", False) and self._decode_rows(token_ids.reshape(-1, 1))
+        if folded and (self._ss is None or self._ss.device != self.device):
+            self._ss = torch.zeros((2, self._ss_tiles, 64), device=self.device, dtype=torch.float32)
+        x, pos, rows, new_len = ext.decode_prologue(token_ids.to(self.device, torch.long).reshape(-1).contiguous(),
+                                                    self.cache_len, self.pos_offset, self.w.embed, self.max_len,
+                                                    ss_out=self._ss[0] if folded else None)
         use_memory = self.memory is not None and self.namespace is not None and cfg.top_k_chunks > 0
         max_keys = cfg.memory_tokens_per_row + self.max_len
         for li, lw in enumerate(self.w.layers):
-            h = self._norm(x, lw.ln_in)
+            h = x if folded else self._norm(x, self._ln(lw.ln_in))
             kc = self.cache[li, 0].view(B * self.max_len, kd)
             vc = self.cache[li, 1].view(B * self.max_len, kd)
             q = torch.empty((B, qd), device=self.device, dtype=torch.bfloat16)
             rq = qkv = None
             if self._decode_rows(h):
-                # one GEMM: rotated q, rotated k and v straight into their cache rows, routing query
+                # one GEMM: (folded input norm,) rotated q, rotated k and v straight into their
+                # cache rows, routing query
                 rq = torch.empty((B, self.route_dim), device=self.device, dtype=torch.bfloat16)
+                norm = dict(ss_in=self._ss[0], ss_tiles=1 if li == 0 else self._ss_tiles, ss_dim=cfg.hidden_size,
+                            ss_eps=cfg.rms_norm_eps) if folded else {}
                 ext.decode_qkv_rope(h, lw.qkv_route, lw.qkv_route_bias, q, kc, vc, rows, pos, cos, sin, cfg.head_dim,
-                                    qd, qd + kd, qd + 2 * kd, rq)
+                                    qd, qd + kd, qd + 2 * kd, rq, **norm)
             else:
                 qkv = self._gemm(h, lw.qkv, lw.qkv_bias)
                 ext.rope_copy(qkv[:, qd: qd + kd], kc, rows, pos, cos, sin, self.kv_heads, cfg.head_dim)
@@ -612,8 +685,12 @@ class PRALlamaEngine:
                     mem_args = (self.memory.k(li), self.memory.v(li), mem_idx, mem_len)
                 a = ext.decode_attention(q, self.heads, self.kv_heads, cfg.head_dim, *mem_args, self.cache[li, 0],
                                          self.cache[li, 1], new_len, max_keys, self._split_for(B, max_keys), False)[0]
-            x = self._row_parallel(a, lw.o, x)
-            x = self._mlp(lw, x)
+            if folded:
+                x = self._row_parallel(a, lw.o, x, ss_out=self._ss[1])
+                x = self._mlp(lw, x, ss=(self._ss[1], self._ss[0]))
+            else:
+                x = self._row_parallel(a, lw.o, x)
+                x = self._mlp(lw, x)
         self.cache_len.copy_(new_len)  # in place: a captured step replays on the same tensors
         return self._greedy(x) if sample else self._logits(x)
 

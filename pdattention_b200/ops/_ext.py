@@ -36,7 +36,7 @@ KERNELS_PER_CALL = {"attention_fwd": 1, "attention_bwd": 3, "gemm": 1, "norm_fwd
                     "gist_mean_into": 1, "gist_kmeans_into": 1,
                     "stack_forward": 0, "stack_train_forward": 0, "stack_train_backward": 0, "dp_allreduce": 1, "dp_signal_words": 0,
                     "ipc_alloc": 0, "ipc_open": 0, "ipc_close": 0,
-                    "rope_copy": 1, "silu_mul": 1, "decode_attention": 2, "route_topk": 1,
+                    "rope_copy": 1, "silu_mul": 1, "decode_prologue": 1, "decode_attention": 2, "route_topk": 1,
                     "tp_allreduce": 1, "tp_allgather": 1, "tp_signal_words": 0, "route_merge": 1, "embed_add": 1, "combine_partials": 1, "attention_status": 0, "plan_batch": 0, "decode_gemm": 1, "decode_qkv_rope": 1, "decode_gemm_max_tiles": 0, "decode_gemm_flag_slots": 0, "decode_gemm_resident_clusters": 0, "set_attention_impl": 0, "attention_impl": 0,
                     "dropout": 1, "dropout_add": 1, "decode_set_tma": 0, "set_pdl": 0, "pdl_enabled": 0, "gelu_probe": 1, "set_launch_priority": 0, "decode_set_stages": 0, "decode_gemm_configure": 0, "route_topk_exchange": 1, "set_bounds_check": 0, "bounds_check_enabled": 0, "bounds_status": 0, "bounds_reset": 0}  # stack_*: counted per layer by their callers
 

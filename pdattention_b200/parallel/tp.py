@@ -95,10 +95,11 @@ class TensorParallel:
         return out
 
     def fused_gemm_allreduce(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None,
-                             bias: torch.Tensor | None = None) -> torch.Tensor:
+                             bias: torch.Tensor | None = None, ss_out: torch.Tensor | None = None) -> torch.Tensor:
         """``residual + sum_ranks x @ w^T`` for at most ``decode_rows`` rows in ONE kernel: each
         128-feature tile's partial is pushed to every rank over NVLink as soon as it is computed
-        and summed where it lands (``decode_gemm``); the row-parallel projections of decode."""
+        and summed where it lands (``decode_gemm``); the row-parallel projections of decode.
+        ``ss_out``: per-tile row sums of squares of the result (a folded RMSNorm after it)."""
         m, n = x.shape[0], w.shape[0]
         if m > self.decode_rows or n > self.decode_width:
             raise ValueError("fused all-reduce sized for decode rows; use gemm_allreduce")
@@ -106,7 +107,7 @@ class TensorParallel:
         self.epoch_dg += 1
         out = torch.empty((m, n), device=x.device, dtype=torch.bfloat16)
         _ext.require().decode_gemm(x, w, bias, residual, out, None, 0, 0, self.dg_recv[half], self.dg_flags[half],
-                                   self.rank, self.dg_epochs, self.max_spins, self.error)
+                                   self.rank, self.dg_epochs, self.max_spins, self.error, ss_out=ss_out)
         return out
 
     def route_exchange(self, scores, query, gists, lo, hi, k: int, k_cand: int, budget: int, mem_max: int,

@@ -108,3 +108,50 @@ def test_resident_cluster_counts(ext):
     print("resident clusters for 1/2/4/8 splits:", counts)
     assert counts[0] >= 32
     assert all(a >= b for a, b in zip(counts, counts[1:])), counts
+
+
+@pytest.mark.parametrize("m,f,k", [(64, 1792, 4096), (5, 256, 128)])
+def test_swiglu_epilogue_matches_gemm_then_silu(ext, m, f, k):
+    """A [gate | up]-interleaved weight (runs of 64) with the SwiGLU epilogue equals fp32
+    silu(x G^T) * (x U^T); the blocked silu_mul on the GEMM's output agrees."""
+    gen = torch.Generator(device="cuda").manual_seed(f + k)
+    x = torch.randn(m, k, device="cuda", generator=gen).bfloat16()
+    gate = (torch.randn(f, k, device="cuda", generator=gen) * 0.05).bfloat16()
+    up = (torch.randn(f, k, device="cuda", generator=gen) * 0.05).bfloat16()
+    blocked = torch.stack([gate.view(f // 64, 64, k), up.view(f // 64, 64, k)], 1).reshape(2 * f, k).contiguous()
+    act = torch.empty(m, f, device="cuda", dtype=torch.bfloat16)
+    ext.decode_gemm(x, blocked, None, None, act, None, 0, 0, [], [], 0, None, 0, None, swiglu=True)
+    g, u = x.float() @ gate.float().t(), x.float() @ up.float().t()
+    want = torch.nn.functional.silu(g) * u
+    assert torch.allclose(act.float(), want, atol=2e-2 * want.abs().max().item(), rtol=2e-2)
+    gu = torch.empty(m, 2 * f, device="cuda", dtype=torch.bfloat16)
+    ext.decode_gemm(x, blocked, None, None, gu, None, 0, 0, [], [], 0, None, 0, None)
+    act2 = torch.empty_like(act)
+    ext.silu_mul(gu, act2, 64)
+    assert torch.allclose(act2.float(), want, atol=2e-2 * want.abs().max().item(), rtol=2e-2)
+
+
+def test_folded_rmsnorm_producer_and_consumer(ext):
+    """A producer GEMM (with residual) writes per-tile row sums of squares of its bf16 output; a
+    consumer GEMM whose weight carries the norm weight scales its rows by rsqrt(mean square + eps):
+    equal to RMSNorm then GEMM in fp32."""
+    gen = torch.Generator(device="cuda").manual_seed(21)
+    m, d, k, n, eps = 37, 1024, 512, 768, 1e-5
+    a = torch.randn(m, k, device="cuda", generator=gen).bfloat16()
+    wo = (torch.randn(d, k, device="cuda", generator=gen) * 0.05).bfloat16()
+    res = torch.randn(m, d, device="cuda", generator=gen).bfloat16()
+    x = torch.empty(m, d, device="cuda", dtype=torch.bfloat16)
+    ss = torch.full((d // 128, 64), float("nan"), device="cuda")
+    ext.decode_gemm(a, wo, None, res, x, None, 0, 0, [], [], 0, None, 0, None, ss_out=ss)
+    want_ss = (x.float() ** 2).view(m, d // 128, 128).sum(-1).t()
+    assert torch.allclose(ss[:, :m], want_ss, rtol=1e-5, atol=1e-3)
+    g = (1 + 0.1 * torch.randn(d, device="cuda", generator=gen)).bfloat16()
+    w = (torch.randn(n, d, device="cuda", generator=gen) * 0.05).bfloat16()
+    wg = (w.float() * g.float()[None]).bfloat16()
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    ext.decode_gemm(x, wg, None, None, out, None, 0, 0, [], [], 0, None, 0, None, ss_in=ss, ss_tiles=d // 128,
+                    ss_dim=d, ss_eps=eps)
+    xf = x.float()
+    h = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * g.float()
+    want = h @ w.float().t()
+    assert torch.allclose(out.float(), want, atol=2e-2 * want.abs().max().item(), rtol=2e-2)

@@ -9,7 +9,7 @@ host reads, and the context must stay usable.
 """
 
 import os
-import socket
+import tempfile
 from datetime import timedelta
 
 import pytest
@@ -20,16 +20,17 @@ import torch.multiprocessing as mp
 pytestmark = pytest.mark.gpu
 
 
-def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+def _rendezvous_file() -> str:
+    """A fresh path for a file-based process-group rendezvous: no TCP port for the ranks to race
+    other processes for (a port picked free can be taken before rank 0 listens on it)."""
+    return os.path.join(tempfile.mkdtemp(prefix="pra_pg_"), "store")
 
 
-def _worker(rank: int, world: int, port: int, queue, out_dtype: str = "bf16") -> None:
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+def _worker(rank: int, world: int, store: str, queue, out_dtype: str = "bf16") -> None:
+    os.environ.update(NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+    dist.init_process_group("nccl", init_method=f"file://{store}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     result = {"rank": rank}
     try:
@@ -132,8 +133,8 @@ def test_peer_gradient_allreduce_two_gpus(out_dtype):
     world = 2
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, queue, out_dtype)) for r in range(world)]
+    store = _rendezvous_file()
+    procs = [ctx.Process(target=_worker, args=(r, world, store, queue, out_dtype)) for r in range(world)]
     for p in procs:
         p.start()
     results = {}

@@ -6,7 +6,7 @@ peer's bounded wait runs out and reports an error status.
 """
 
 import os
-import socket
+import tempfile
 from datetime import timedelta
 
 import pytest
@@ -18,16 +18,17 @@ import torch.nn.functional as F
 pytestmark = pytest.mark.gpu
 
 
-def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+def _rendezvous_file() -> str:
+    """A fresh path for a file-based process-group rendezvous: no TCP port for the ranks to race
+    other processes for (a port picked free can be taken before rank 0 listens on it)."""
+    return os.path.join(tempfile.mkdtemp(prefix="pra_pg_"), "store")
 
 
 def _worker(rank, world, port, queue):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+    dist.init_process_group("nccl", init_method=f"file://{store}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     result = {"rank": rank}
     try:
@@ -151,8 +152,8 @@ def test_tensor_parallel_engine_two_gpus():
     world = 2
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, queue)) for r in range(world)]
+    store = _rendezvous_file()
+    procs = [ctx.Process(target=_worker, args=(r, world, store, queue)) for r in range(world)]
     for p in procs:
         p.start()
     results = {}
