@@ -70,6 +70,27 @@ def test_matches_fp32_sum_and_existing_colsum_on_consecutive_calls(lib):
 
 
 @pytest.mark.gpu
+def test_captured_in_a_cuda_graph_and_replayed_on_new_data(lib):
+    """The use it exists for: after one warm-up call (which looks up the scratch address), a call
+    made while a CUDA graph is being captured launches kernels only, and replays of that graph
+    sum whatever the input buffer holds at replay time."""
+    m, n = 2048, 1536
+    g = torch.randn(m, n, device="cuda").bfloat16()
+    out = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    assert _call(lib, g, out) == 0  # warm-up outside the capture
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        rc = _call(lib, g, out)
+    assert rc == 0
+    for seed in (1, 2):
+        g.copy_(torch.randn(m, n, device="cuda", generator=torch.Generator(device="cuda").manual_seed(seed)))
+        graph.replay()
+        torch.cuda.synchronize()
+        _check(out, g)
+
+
+@pytest.mark.gpu
 def test_accepts_a_shape_that_fills_the_scratch_exactly(lib):
     capacity = lib.pra_colsum_noalloc_capacity()
     m, n = 16384, 4096  # 256 partial rows x 4096 columns
