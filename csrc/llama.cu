@@ -705,13 +705,17 @@ __device__ void finish_selection(const float* cscore, const int* cand, int nc, i
     }
   }
   __syncthreads();
-  // greedy token budget in rank order (sequential by definition; shared-memory only)
+  // greedy token budget in rank order (sequential by definition; shared-memory only).  Without
+  // a budget every ranked candidate is kept, so the loop is skipped.
   __shared__ int s_keep[64], sel_len[64];
-  if (threadIdx.x == 0) {
+  if (budget < 0) {
+    if (threadIdx.x < kk) s_keep[threadIdx.x] = 1;
+    if (threadIdx.x == 0) *n_sel = kk;
+  } else if (threadIdx.x == 0) {
     int used = 0, chosen = 0;
     for (int r = 0; r < kk; ++r) {
       const int len = s_len[r];
-      const bool keep = !(budget >= 0 && used + len > budget);
+      const bool keep = used + len <= budget;
       if (keep) {
         used += len;
         ++chosen;
@@ -732,14 +736,25 @@ __device__ void finish_selection(const float* cscore, const int* cand, int nc, i
     sel_row0[pos] = s_row0[r];
   }
   __syncthreads();
-  if (threadIdx.x == 0) {  // row offsets (chunks held elsewhere, row0 < 0, add no rows here)
-    int written = 0;
-    for (int i = 0; i < chosen; ++i) {
-      sel_off[i] = written;
-      written += sel_row0[i] >= 0 ? sel_len[i] : 0;
+  if (threadIdx.x < 32) {  // row offsets by a warp prefix sum, two chunks per lane (chunks held
+                           // elsewhere, row0 < 0, add no rows here)
+    const int lane = threadIdx.x;
+    const int i0 = 2 * lane, i1 = 2 * lane + 1;
+    const int n0 = i0 < chosen && sel_row0[i0] >= 0 ? sel_len[i0] : 0;
+    const int n1 = i1 < chosen && sel_row0[i1] >= 0 ? sel_len[i1] : 0;
+    int incl = n0 + n1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
     }
-    sel_off[chosen] = written;
-    mem_len[b] = min(written, mem_max);
+    const int excl = incl - n0 - n1;
+    if (i0 <= chosen) sel_off[i0] = excl;
+    if (i1 <= chosen) sel_off[i1] = excl + n0;
+    if (lane == 31) {
+      sel_off[chosen] = incl;  // == the total once every lane is summed
+      mem_len[b] = min(incl, mem_max);
+    }
   }
   for (int i = threadIdx.x; i < k_req && sel_out; i += blockDim.x)
     sel_out[(int64_t)b * k_req + i] = i < chosen ? sel_chunk[i] : -1;

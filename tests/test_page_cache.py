@@ -118,7 +118,10 @@ def test_engine_over_page_tables_equals_contiguous_memory():
     cache.page_table([[e[0], e[1]], [e[2]]])
     got = paged.prefill(ids, plen, 3).float()
     got_step = paged.decode_step(got.argmax(-1)).float()
-    assert torch.allclose(got, want, atol=1e-3, rtol=1e-3), (got - want).abs().max()
-    assert torch.allclose(got_step, want_step, atol=1e-3, rtol=1e-3)
+    # same selections (below) and the same logits up to bf16 rounding: each reference encoded on its
+    # own takes the <= 64-row decode GEMM (SwiGLU in its epilogue) where the back-to-back encode
+    # of all nine chunks takes the large-batch GEMM and a separate SwiGLU pass
+    assert torch.allclose(got, want, atol=3e-2, rtol=1e-2), (got - want).abs().max()
+    assert torch.allclose(got_step, want_step, atol=3e-2, rtol=1e-2), (got_step - want_step).abs().max()
     for li in base.last_selection:
         assert torch.equal(paged.last_selection[li], base.last_selection[li])
