@@ -219,14 +219,6 @@ torch::Tensor& workspace(const torch::Tensor& like) {
   return per_device[dev];
 }
 
-// Long reductions into few 128 x 256 output tiles (the LM head's data gradient: K = vocabulary)
-// run under the stream-K scheduler; measured 0.76x vs 0.58x of cuBLAS for 8,192 x 768 x 50,304,
-// and slower than the data-parallel tiles for every d_model-sized reduction.
-static bool long_reduction(const GemmArgs& g) {
-  const int64_t tiles = (int64_t)((g.M + 127) / 128) * ((g.N + 255) / 256);
-  return g.K >= 16384 && tiles < 4 * 148;
-}
-
 void gemm(const std::string& kind, torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> C, torch::Tensor D,
           c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> aux, double alpha, double beta,
           c10::optional<torch::Tensor> alpha_ptr) {
@@ -248,13 +240,13 @@ void gemm(const std::string& kind, torch::Tensor A, torch::Tensor B, c10::option
   auto& ws = workspace(A);
   g.workspace = ws.data_ptr();
   g.workspace_bytes = ws.numel();
-  if (kind == "tn" || kind == "tn_gelu" || kind == "tn_f32") {  // D[M,N] = A[M,K] B[N,K]^T
+  if (kind == "tn" || kind == "tn_gelu" || kind == "tn_f32" || kind == "tn_2sm") {  // D[M,N] = A[M,K] B[N,K]^T
     g.M = A.size(0); g.K = A.size(1); g.N = B.size(0);
     TORCH_CHECK(B.size(1) == g.K && D.size(0) == g.M && D.size(1) == g.N, "tn shape mismatch");
-  } else if (kind == "nn" || kind == "nn_dgelu" || kind == "nn_sk") {  // D[M,N] = A[M,K] B[K,N]
+  } else if (kind == "nn" || kind == "nn_dgelu" || kind == "nn_sk" || kind == "nn_2sm") {  // D[M,N] = A[M,K] B[K,N]
     g.M = A.size(0); g.K = A.size(1); g.N = B.size(1);
     TORCH_CHECK(B.size(0) == g.K && D.size(0) == g.M && D.size(1) == g.N, "nn shape mismatch");
-  } else if (kind == "wgrad" || kind == "wgrad_sk") {  // D[M,N] = A[K,M]^T B[K,N]
+  } else if (kind == "wgrad" || kind == "wgrad_sk" || kind == "wgrad_2sm") {  // D[M,N] = A[K,M]^T B[K,N]
     g.K = A.size(0); g.M = A.size(1); g.N = B.size(1);
     TORCH_CHECK(B.size(0) == g.K && D.size(0) == g.M && D.size(1) == g.N, "wgrad shape mismatch");
   } else {
@@ -263,17 +255,17 @@ void gemm(const std::string& kind, torch::Tensor A, torch::Tensor B, c10::option
   if (C.has_value()) TORCH_CHECK(C->is_contiguous() && C->sizes() == D.sizes(), "C must match D");
   if (g.beta != 0.f) TORCH_CHECK(g.C != nullptr, "beta != 0 needs C");
   cudaError_t e;
-  if (kind == "tn")
-    e = g.M <= 128 ? pra_gemm_tn_bias_small(g, stream())
-                   : (g.N <= 1024 ? pra_gemm_tn_bias_narrow(g, stream()) : pra_gemm_tn_bias(g, stream()));
+  if (kind == "tn") e = pra_gemm_tn_auto(g, stream());
   else if (kind == "tn_f32") e = pra_gemm_tn_f32(g, stream());
   else if (kind == "tn_gelu") e = pra_gemm_tn_bias_gelu(g, stream());
-  else if (kind == "nn") e = long_reduction(g) ? pra_gemm_nn_sk(g, stream()) : pra_gemm_nn(g, stream());
+  else if (kind == "nn") e = pra_gemm_nn_auto(g, stream());
   else if (kind == "nn_dgelu") e = pra_gemm_nn_dgelu(g, stream());
   else if (kind == "nn_sk") e = pra_gemm_nn_sk(g, stream());
+  else if (kind == "tn_2sm") e = pra_gemm_tn_bias_2sm(g, stream());
+  else if (kind == "nn_2sm") e = pra_gemm_nn_2sm(g, stream());
+  else if (kind == "wgrad_2sm") e = pra_gemm_wgrad_2sm(g, stream());
   else if (kind == "wgrad_sk") e = pra_gemm_wgrad_sk(g, stream());
-  else  // large outputs (the LM head's weight gradient) on 128 x 256 stream-K tiles: 0.76x vs 0.72x of cuBLAS
-    e = (int64_t)g.M * g.N >= (16 << 20) ? pra_gemm_wgrad_sk(g, stream()) : pra_gemm_wgrad(g, stream());
+  else e = pra_gemm_wgrad_auto(g, stream());
   check(e, kind.c_str());
 }
 

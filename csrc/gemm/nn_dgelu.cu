@@ -40,7 +40,7 @@ cudaError_t pra_gemm_nn_dgelu(const GemmArgs& g, cudaStream_t st) {
     GemmArgs p = g;
     p.C = nullptr;
     p.beta = 0.f;
-    const cudaError_t e = pra_gemm_nn(p, st);
+    const cudaError_t e = pra_gemm_nn_auto(p, st);
     if (e != cudaSuccess) return e;
     const int64_t n = (int64_t)g.M * g.N;
     const int blocks = (int)std::min<int64_t>((n / 8 + 255) / 256 + 1, 148 * 16);

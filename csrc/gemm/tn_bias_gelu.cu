@@ -42,7 +42,7 @@ cudaError_t pra_gemm_tn_bias_gelu(const GemmArgs& g, cudaStream_t st) {
     z.D = g.aux;
     z.C = nullptr;
     z.beta = 0.f;
-    const cudaError_t e = pra_gemm_tn_bias(z, st);
+    const cudaError_t e = pra_gemm_tn_auto(z, st);
     if (e != cudaSuccess) return e;
     const int64_t n = (int64_t)g.M * g.N;
     const int blocks = (int)std::min<int64_t>((n / 8 + 255) / 256 + 1, 148 * 16);

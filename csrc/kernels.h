@@ -87,6 +87,14 @@ cudaError_t pra_gemm_nn(const GemmArgs& g, cudaStream_t stream);
 // Stream-K variants (128 x 256 tiles) for long reductions into few output tiles.
 cudaError_t pra_gemm_nn_sk(const GemmArgs& g, cudaStream_t stream);
 cudaError_t pra_gemm_wgrad_sk(const GemmArgs& g, cudaStream_t stream);
+// Shape-based choice among the instantiations (gemm/dispatch.cu): what ext.gemm runs.
+cudaError_t pra_gemm_tn_auto(const GemmArgs& g, cudaStream_t stream);
+cudaError_t pra_gemm_nn_auto(const GemmArgs& g, cudaStream_t stream);
+cudaError_t pra_gemm_wgrad_auto(const GemmArgs& g, cudaStream_t stream);
+// 2-SM variants (one tcgen05 MMA across an SM pair, 2 x 1 cluster, plain 2-SM TMA loads).
+cudaError_t pra_gemm_tn_bias_2sm(const GemmArgs& g, cudaStream_t stream);
+cudaError_t pra_gemm_nn_2sm(const GemmArgs& g, cudaStream_t stream);
+cudaError_t pra_gemm_wgrad_2sm(const GemmArgs& g, cudaStream_t stream);
 cudaError_t pra_gemm_nn_dgelu(const GemmArgs& g, cudaStream_t stream);
 cudaError_t pra_gemm_wgrad(const GemmArgs& g, cudaStream_t stream);
 
