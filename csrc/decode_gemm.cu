@@ -4,16 +4,23 @@
 // whole cost.  Each CTA owns 128 output features (one weight slab) and, with split-K, a range
 // of the reduction; the MMA is "swapped": A = the weight tile (128 features x 64 K, K-major),
 // B = the token rows (M x 64 K, K-major), so the fp32 accumulator in TMEM is D^T[feature][token]
-// with one TMEM lane per output feature.  Both operands stream through a 6-stage ring of 2-D
-// TMA tiles in the 128-byte swizzle layout (64 K elements per row): one thread issues the
-// copies against "full" mbarriers, one thread issues the MMAs and releases each stage through
-// its "empty" mbarrier (tcgen05.commit), so a CTA keeps up to six tiles in flight with two
-// instructions per tile instead of one 16-byte copy per thread per chunk.
+// with one TMEM lane per output feature.  Both operands stream through a ring of 2-D TMA tiles
+// in the 128-byte swizzle layout (64 K elements per row; 4 stages at two CTAs per SM, 6 at one,
+// 2 for the small-footprint fp32-score launches): one thread issues the copies against "full"
+// mbarriers, one thread issues the MMAs and releases each stage through its "empty" mbarrier
+// (tcgen05.commit).  Under programmatic dependent launch the weight tiles of the first stages
+// are requested before griddepcontrol.wait, while the previous kernel drains.
 //
 // Epilogues (the accumulator is staged through shared memory as fp32 [token][feature] so every
 // global access is a 16-byte row chunk):
 //  * plain: + bias, + residual, bf16 store; columns >= split_col go to a second output (the
 //    routing query rows appended to a QKV weight land in their own buffer);
+//  * rotary QKV: q / k rotated and scattered into the query buffer and the cache rows, v into
+//    its cache rows, the routing-query columns into their own buffer;
+//  * SwiGLU: a [64 gate | 64 up]-interleaved weight tile yields 64 silu(gate) * up outputs;
+//  * fp32 scores (routing);
+//  * folded RMSNorm: a consumer scales its rows by rsqrt(mean square + eps) from the per-tile
+//    sums of squares its producer (a residual-adding epilogue) wrote;
 //  * split-K: the splits of a tile run as one thread-block cluster; each stages its fp32
 //    partial in shared memory, and after a cluster barrier each CTA sums a slice of the token
 //    rows over all splits' partials through distributed shared memory and finishes those rows

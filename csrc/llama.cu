@@ -4,14 +4,19 @@
 //                   fp64 on the host) applied while copying head rows to a destination row
 //                   (in place for queries, into the KV cache / chunk pool for keys); with a
 //                   null position table it is a plain row copy (values).
-//  * silu_mul       SwiGLU activation over a fused [gate | up] GEMM output.
+//  * decode_prologue one launch per decode step: token embeddings (with the first folded
+//                   RMSNorm's sums of squares), rotary positions, cache rows, new lengths.
+//  * silu_mul       SwiGLU activation over a fused [gate | up] GEMM output (halves, or the
+//                   runs-of-64 interleave the decode GEMM's SwiGLU epilogue reads).
 //  * decode attention: split-K flash decoding for grouped-query heads.  One CTA per
 //                   (row, kv head, key split) computes the unnormalised partial
 //                   (max, sum, out) of the group's query heads over its keys; keys are
 //                   [selected memory rows (gathered through a row list) ; local cache
-//                   rows], all visible to the token being decoded.  A second kernel
-//                   merges the splits (and optionally exports the merged partial for a
-//                   cross-GPU combine).
+//                   rows], all visible to the token being decoded.  The splits can be laid
+//                   out as memory-only and local-only ranges launched separately (the local
+//                   ones before routing has run), and a persistent grid can walk them.  A
+//                   second kernel merges the splits (and optionally exports the merged
+//                   partial for a cross-GPU combine).
 //  * route_topk     exact top-k routing per row: radix-select of the candidates from
 //                   tensor-core scores, fp32 cosine rescoring of the candidates, ties by
 //                   chunk id, greedy token budget, and the memory row list in chunk order.
