@@ -1,7 +1,9 @@
 // tcgen05 (5th-generation tensor core) helpers for single-CTA sm_100a kernels: TMEM
 // allocation, shared-memory matrix descriptors for no-swizzle canonical layouts, bf16 MMAs
 // with fp32 accumulators in TMEM, commits to an mbarrier, and 32-column TMEM loads/stores.
-// No clusters and no multicast: every operand is this CTA's shared memory.
+// The MMAs are single-CTA (cta_group::1): every operand is this CTA's shared memory.  (Kernels
+// that use these helpers may still form clusters for other reasons, e.g. the decode GEMM's
+// split-K reduction through distributed shared memory; no operand load is shared.)
 //
 // Canonical no-swizzle layouts: an operand tile is a grid of "core matrices" of 8 rows x
 // 16 bytes (8 bf16), each stored as one contiguous 128-byte block (row i at byte 16 * i).
