@@ -63,6 +63,7 @@ class LlamaWeights:
         self.tp_rank, self.tp_size = tp_rank, tp_size
         self.mlp_block = 0  # > 0: gate / up rows interleaved in runs of this many (set by an engine)
         self.norm_folded = False  # RMSNorm weights multiplied into qkv_route / gate_up (set by an engine)
+        self.route_rows = False  # routing-query rows appended to every QKV weight (set by an engine)
 
     @staticmethod
     def _shard_rows(t: torch.Tensor, rank: int, size: int) -> torch.Tensor:
@@ -235,6 +236,10 @@ class PRALlamaEngine:
         cfg = self.cfg
         g, dh = cfg.group, cfg.head_dim
         qd, kd = self.q_dim, self.kv_dim
+        if getattr(self.w, "route_rows", False):  # once per weight set (engines may share one)
+            self._block_mlp_rows()
+            self._fold_norms()
+            return
 
         def group_mean(rows: torch.Tensor) -> torch.Tensor:  # [heads * dh, ...] -> [kv_heads * dh, ...]
             return rows.float().unflatten(0, (self.kv_heads, g, dh)).mean(1).flatten(0, 1)
@@ -258,6 +263,7 @@ class PRALlamaEngine:
                 rb = gather(group_mean(lw.qkv_bias[:qd]).to(torch.bfloat16))
                 lw.qkv_route_bias = torch.cat([lw.qkv_bias, rb]).contiguous()
                 lw.qkv_bias = lw.qkv_route_bias[: qd + 2 * kd]
+        self.w.route_rows = True
         self._block_mlp_rows()
         self._fold_norms()
 
