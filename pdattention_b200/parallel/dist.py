@@ -23,7 +23,8 @@ def env_world() -> tuple[int, int, int]:
 
 
 def maybe_init_distributed(backend: str | None = None, timeout_s: float | None = None) -> tuple[int, int]:
-    """Initialise the default group when launched with ``WORLD_SIZE > 1``; returns ``(rank, world)``."""
+    """Initialise the default group when launched with ``WORLD_SIZE > 1``; returns ``(rank, world)``.
+    Rendezvous through ``MASTER_ADDR`` / ``MASTER_PORT``, or ``PRA_INIT_METHOD`` when set."""
     rank, local_rank, world = env_world()
     if world <= 1:
         return 0, 1
@@ -38,6 +39,8 @@ def maybe_init_distributed(backend: str | None = None, timeout_s: float | None =
               "world_size": world}
     if use_cuda:
         kwargs["device_id"] = torch.device("cuda", local_rank)
+    if os.environ.get("PRA_INIT_METHOD"):  # e.g. file:///path: a rendezvous that needs no TCP port
+        kwargs["init_method"] = os.environ["PRA_INIT_METHOD"]
     dist.init_process_group(**kwargs)
     return rank, world
 

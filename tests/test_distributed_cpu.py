@@ -7,31 +7,30 @@ timeout / closed connection) instead of hanging.
 """
 
 import os
-import socket
+import tempfile
 
 import pytest
 import torch
 import torch.multiprocessing as mp
 
 
-def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+def _rendezvous_file() -> str:
+    """A fresh file-store path: no TCP port that a concurrently running test could take first."""
+    return os.path.join(tempfile.mkdtemp(prefix="pra_pg_"), "store")
 
 
-def _setup(rank, world, port, root):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+def _setup(rank, world, store, root):
+    os.environ.update(PRA_INIT_METHOD=f"file://{store}", RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
     from pdattention_b200.parallel.dist import maybe_init_distributed
 
     maybe_init_distributed(backend="gloo", timeout_s=20)
 
 
-def _train_worker(rank, world, port, root, queue):
+def _train_worker(rank, world, store, root, queue):
     result = {"rank": rank}
     try:
-        _setup(rank, world, port, root)
+        _setup(rank, world, store, root)
         import torch.distributed as dist
 
         from pdattention_b200.config import PRAConfig, TrainConfig
@@ -61,10 +60,10 @@ def _train_worker(rank, world, port, root, queue):
     queue.put(result)
 
 
-def _failing_worker(rank, world, port, root, queue):
+def _failing_worker(rank, world, store, root, queue):
     result = {"rank": rank}
     try:
-        _setup(rank, world, port, root)
+        _setup(rank, world, store, root)
         import torch.distributed as dist
 
         t = torch.ones(4)
@@ -84,8 +83,8 @@ def _failing_worker(rank, world, port, root, queue):
 def _run(target, root, world=2, timeout=120):
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=target, args=(r, world, port, root, queue)) for r in range(world)]
+    store = _rendezvous_file()
+    procs = [ctx.Process(target=target, args=(r, world, store, root, queue)) for r in range(world)]
     for p in procs:
         p.start()
     results = {}
