@@ -240,13 +240,13 @@ void gemm(const std::string& kind, torch::Tensor A, torch::Tensor B, c10::option
   auto& ws = workspace(A);
   g.workspace = ws.data_ptr();
   g.workspace_bytes = ws.numel();
-  if (kind == "tn" || kind == "tn_gelu" || kind == "tn_f32" || kind == "tn_2sm") {  // D[M,N] = A[M,K] B[N,K]^T
+  if (kind == "tn" || kind == "tn_gelu" || kind == "tn_f32") {  // D[M,N] = A[M,K] B[N,K]^T
     g.M = A.size(0); g.K = A.size(1); g.N = B.size(0);
     TORCH_CHECK(B.size(1) == g.K && D.size(0) == g.M && D.size(1) == g.N, "tn shape mismatch");
-  } else if (kind == "nn" || kind == "nn_dgelu" || kind == "nn_sk" || kind == "nn_2sm") {  // D[M,N] = A[M,K] B[K,N]
+  } else if (kind == "nn" || kind == "nn_dgelu" || kind == "nn_sk") {  // D[M,N] = A[M,K] B[K,N]
     g.M = A.size(0); g.K = A.size(1); g.N = B.size(1);
     TORCH_CHECK(B.size(0) == g.K && D.size(0) == g.M && D.size(1) == g.N, "nn shape mismatch");
-  } else if (kind == "wgrad" || kind == "wgrad_sk" || kind == "wgrad_2sm") {  // D[M,N] = A[K,M]^T B[K,N]
+  } else if (kind == "wgrad" || kind == "wgrad_sk") {  // D[M,N] = A[K,M]^T B[K,N]
     g.K = A.size(0); g.M = A.size(1); g.N = B.size(1);
     TORCH_CHECK(B.size(0) == g.K && D.size(0) == g.M && D.size(1) == g.N, "wgrad shape mismatch");
   } else {
@@ -261,9 +261,6 @@ void gemm(const std::string& kind, torch::Tensor A, torch::Tensor B, c10::option
   else if (kind == "nn") e = pra_gemm_nn_auto(g, stream());
   else if (kind == "nn_dgelu") e = pra_gemm_nn_dgelu(g, stream());
   else if (kind == "nn_sk") e = pra_gemm_nn_sk(g, stream());
-  else if (kind == "tn_2sm") e = pra_gemm_tn_bias_2sm(g, stream());
-  else if (kind == "nn_2sm") e = pra_gemm_nn_2sm(g, stream());
-  else if (kind == "wgrad_2sm") e = pra_gemm_wgrad_2sm(g, stream());
   else if (kind == "wgrad_sk") e = pra_gemm_wgrad_sk(g, stream());
   else e = pra_gemm_wgrad_auto(g, stream());
   check(e, kind.c_str());

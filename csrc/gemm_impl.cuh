@@ -10,7 +10,6 @@
 #pragma once
 
 #include <atomic>
-#include <type_traits>
 
 #include <cutlass/cutlass.h>
 #include <cute/tensor.hpp>
@@ -154,29 +153,22 @@ inline int sm_count() {
 
 // Scheduler: void (persistent data-parallel tiles) or cutlass::gemm::StreamKScheduler (the
 // K loop of the remaining tiles is split across idle SMs: skinny decode GEMMs).
-// TwoSm: one MMA spans a pair of SMs (tcgen05 cta_group::2, a 2 x 1 cluster): each SM of the pair
-// loads its half of A and half of B with plain (non-multicast) 2-SM TMA loads and the pair
-// computes a 256-row tile; TileShape is then the pair's tile.
 template <class LayoutA, class LayoutB, class ElementD, class FusionOp, class TileShape = Shape<_128, _256, _64>,
-          class Scheduler = void, bool TwoSm = false>
+          class Scheduler = void>
 struct Gemm {
-  using ClusterShape = std::conditional_t<TwoSm, Shape<_2, _1, _1>, Shape<_1, _1, _1>>;
-  using EpilogueSchedule =
-      std::conditional_t<TwoSm, cutlass::epilogue::TmaWarpSpecialized2Sm, cutlass::epilogue::TmaWarpSpecialized1Sm>;
-  using MainloopSchedule =
-      std::conditional_t<TwoSm, cutlass::gemm::KernelTmaWarpSpecialized2SmSm100, cutlass::gemm::KernelTmaWarpSpecialized1SmSm100>;
+  using ClusterShape = Shape<_1, _1, _1>;
   using LayoutD = cutlass::layout::RowMajor;
   static constexpr int AlignAB = 8;
   static constexpr int AlignD = 128 / cutlass::sizeof_bits<ElementD>::value;
   using Epilogue = typename cutlass::epilogue::collective::CollectiveBuilder<
       cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, TileShape, ClusterShape,
       cutlass::epilogue::collective::EpilogueTileAuto, float, float, ElementD, LayoutD, AlignD, ElementD, LayoutD,
-      AlignD, EpilogueSchedule, FusionOp>::CollectiveOp;
+      AlignD, cutlass::epilogue::TmaWarpSpecialized1Sm, FusionOp>::CollectiveOp;
   using Mainloop = typename cutlass::gemm::collective::CollectiveBuilder<
       cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, BF16, LayoutA, AlignAB, BF16, LayoutB, AlignAB, float,
       TileShape, ClusterShape,
       cutlass::gemm::collective::StageCountAutoCarveout<static_cast<int>(sizeof(typename Epilogue::SharedStorage))>,
-      MainloopSchedule>::CollectiveOp;
+      cutlass::gemm::KernelTmaWarpSpecialized1SmSm100>::CollectiveOp;
   using Kernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, Mainloop, Epilogue, Scheduler>;
   using Device = cutlass::gemm::device::GemmUniversalAdapter<Kernel>;
   using StrideA = typename Kernel::StrideA;

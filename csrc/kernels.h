@@ -91,10 +91,6 @@ cudaError_t pra_gemm_wgrad_sk(const GemmArgs& g, cudaStream_t stream);
 cudaError_t pra_gemm_tn_auto(const GemmArgs& g, cudaStream_t stream);
 cudaError_t pra_gemm_nn_auto(const GemmArgs& g, cudaStream_t stream);
 cudaError_t pra_gemm_wgrad_auto(const GemmArgs& g, cudaStream_t stream);
-// 2-SM variants (one tcgen05 MMA across an SM pair, 2 x 1 cluster, plain 2-SM TMA loads).
-cudaError_t pra_gemm_tn_bias_2sm(const GemmArgs& g, cudaStream_t stream);
-cudaError_t pra_gemm_nn_2sm(const GemmArgs& g, cudaStream_t stream);
-cudaError_t pra_gemm_wgrad_2sm(const GemmArgs& g, cudaStream_t stream);
 cudaError_t pra_gemm_nn_dgelu(const GemmArgs& g, cudaStream_t stream);
 cudaError_t pra_gemm_wgrad(const GemmArgs& g, cudaStream_t stream);
 

@@ -24,7 +24,7 @@ BUILD_DIR = Path(__file__).resolve().parent / "_build"
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 _SOURCES = ["bindings.cpp", "attention.cu", "attention_tc.cu", "norm.cu", "loss_optim.cu", "gist.cu", "routing.cu", "llama.cu",
-            "gemm/tn_bias.cu", "gemm/tn_bias_gelu.cu", "gemm/nn.cu", "gemm/nn_dgelu.cu", "gemm/wgrad.cu", "gemm/tn_f32.cu", "gemm/tn_bias_small.cu", "gemm/tn_bias_narrow.cu", "gemm/nn_sk.cu", "gemm/wgrad_sk.cu", "gemm/tn_bias_2sm.cu", "gemm/nn_2sm.cu", "gemm/wgrad_2sm.cu", "gemm/dispatch.cu",
+            "gemm/tn_bias.cu", "gemm/tn_bias_gelu.cu", "gemm/nn.cu", "gemm/nn_dgelu.cu", "gemm/wgrad.cu", "gemm/tn_f32.cu", "gemm/tn_bias_small.cu", "gemm/tn_bias_narrow.cu", "gemm/nn_sk.cu", "gemm/wgrad_sk.cu", "gemm/dispatch.cu",
             "planner.cpp", "decode_gemm.cu", "dropout.cu", "colsum_noalloc.cu", "dp_reduce.cu", "tp_comm.cu", "embed.cu", "driver_shim.cu"]
 
 _module = None

@@ -498,8 +498,6 @@ def gemm_train_shapes(iters: int = 20) -> None:
             ref = timed(lambda: torch.nn.functional.linear(a, w, bias))
             fl = 2 * m * n * k
             print(f"{'fwd ' + name + f' {m}x{n}x{k}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
-            ours = timed(lambda: ext.gemm("tn_2sm", a, w, None, d, bias, None, 1.0, 0.0, None))
-            print(f"{'fwd(2sm) ' + name + f' {m}x{n}x{k}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
             if name == "fc1":  # + GELU epilogue storing the pre-activation too, against linear + gelu
                 z = torch.empty_like(d)
                 ours = timed(lambda: ext.gemm("tn_gelu", a, w, None, d, bias, z, 1.0, 0.0, None))
@@ -519,14 +517,10 @@ def gemm_train_shapes(iters: int = 20) -> None:
                 ours = timed(lambda: ext.gemm("nn", dy, w, None, dx, None, None, 1.0, 0.0, None))
                 ref = timed(lambda: dy @ w)
                 print(f"{'dgrad ' + name + f' {m}x{k}x{n}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
-                ours = timed(lambda: ext.gemm("nn_2sm", dy, w, None, dx, None, None, 1.0, 0.0, None))
-                print(f"{'dgrad(2sm) ' + name + f' {m}x{k}x{n}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
                 dw = torch.empty(n, k, device=dev, dtype=torch.bfloat16)
                 ours = timed(lambda: ext.gemm("wgrad", dy, a, None, dw, None, None, 1.0, 0.0, None))
                 ref = timed(lambda: dy.t() @ a)
                 print(f"{'wgrad ' + name + f' {n}x{k}x{m}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
-                ours = timed(lambda: ext.gemm("wgrad_2sm", dy, a, None, dw, None, None, 1.0, 0.0, None))
-                print(f"{'wgrad(2sm) ' + name + f' {n}x{k}x{m}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
     m, v, k = 8192, 50304, 768
     a, w = rnd(m, k), rnd(v, k)
     d = torch.empty(m, v, device=dev, dtype=torch.bfloat16)
@@ -534,20 +528,14 @@ def gemm_train_shapes(iters: int = 20) -> None:
     ours = timed(lambda: ext.gemm("tn", a, w, None, d, None, None, 1.0, 0.0, None))
     ref = timed(lambda: a @ w.t())
     print(f"{'fwd lm_head ' + f'{m}x{v}x{k}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
-    ours = timed(lambda: ext.gemm("tn_2sm", a, w, None, d, None, None, 1.0, 0.0, None))
-    print(f"{'fwd(2sm) lm_head ' + f'{m}x{v}x{k}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
     dx = torch.empty(m, k, device=dev, dtype=torch.bfloat16)
     ours = timed(lambda: ext.gemm("nn", d, w, None, dx, None, None, 1.0, 0.0, None))
     ref = timed(lambda: d @ w)
     print(f"{'dgrad lm_head ' + f'{m}x{k}x{v}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
-    ours = timed(lambda: ext.gemm("nn_2sm", d, w, None, dx, None, None, 1.0, 0.0, None))
-    print(f"{'dgrad(2sm) lm_head ' + f'{m}x{k}x{v}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
     dw = torch.empty(v, k, device=dev, dtype=torch.bfloat16)
     ours = timed(lambda: ext.gemm("wgrad", d, a, None, dw, None, None, 1.0, 0.0, None))
     ref = timed(lambda: d.t() @ a)
     print(f"{'wgrad lm_head ' + f'{v}x{k}x{m}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
-    ours = timed(lambda: ext.gemm("wgrad_2sm", d, a, None, dw, None, None, 1.0, 0.0, None))
-    print(f"{'wgrad(2sm) lm_head ' + f'{v}x{k}x{m}':44s} {ours:8.1f} {ref:9.1f} {fl / ours / 1e6:9.0f} {ref / ours:6.2f}")
 
 
 CASES = {"attention-fwd": attention_fwd, "decode-gemm-one": decode_gemm_one, "gemm-train-shapes": gemm_train_shapes,
